@@ -1,0 +1,942 @@
+// Exported C ABI (include/hybridsplat_rasterizer_c_api.h).
+//
+// Argument validation order, status codes and message texts follow the
+// reference entry points (rasterizer/c_api.cpp:129-397 for the error
+// plumbing, :543-1134 for the renderer entry points, :1136-1910 for the
+// elementwise and math helpers), so callers observe the same behaviour for
+// invalid input. Every entry point catches C++ exceptions (guard).
+#include "hybridsplat_rasterizer_c_api.h"
+
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+#include <cusolverDn.h>
+
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <mutex>
+#include <new>
+#include <string>
+
+#include "context.h"
+#include "precise.h"
+
+namespace hs {
+void flashgs_prepare_host(uint64_t count, const float* opacity_raw, const float* scaling_raw,
+                          const float* rotation_raw, const float* specular_raw,
+                          const float* roughness_raw, float* opacity, float* scaling,
+                          float* rotation, float* covariance, float* specular, float* roughness);
+}
+
+namespace {
+
+constexpr uint64_t kMathWorkspaceBytes = 2ull * 1024ull * 1024ull;
+constexpr uint64_t kMathCameraOffset = 0;
+constexpr uint64_t kMathIdentity3Offset = 256;
+constexpr uint64_t kMathIdentity4Offset = 384;
+constexpr uint64_t kMathFactorOffset = 512;
+constexpr uint64_t kMathRhsOffset = 768;
+constexpr uint64_t kMathPivotsOffset = 1024;
+constexpr uint64_t kMathInfoOffset = 1280;
+constexpr uint64_t kMathFactorArrayOffset = 1536;
+constexpr uint64_t kMathRhsArrayOffset = 1792;
+constexpr uint64_t kMathSolverWorkspaceOffset = 2048;
+
+unsigned char* math_at(HsRasterizerContext* c, uint64_t offset) {
+    return static_cast<unsigned char*>(c->math_workspace) + offset;
+}
+
+void write_text(char* destination, uint64_t capacity, const char* text) noexcept {
+    if (destination == nullptr || capacity == 0) return;
+    const char* source = text == nullptr ? "" : text;
+    const size_t n = std::min(std::strlen(source), static_cast<size_t>(capacity - 1));
+    if (n != 0) std::memcpy(destination, source, n);
+    destination[n] = '\0';
+}
+
+int32_t ok(char* error_text, uint64_t error_capacity) noexcept {
+    write_text(error_text, error_capacity, "");
+    return HS_STATUS_OK;
+}
+
+int32_t fail(HsStatus status, const std::string& message, char* error_text,
+             uint64_t error_capacity) noexcept {
+    write_text(error_text, error_capacity, message.c_str());
+    return static_cast<int32_t>(status);
+}
+
+int32_t cuda_failure(cudaError_t error, const char* operation, char* error_text,
+                     uint64_t error_capacity) noexcept {
+    const HsStatus status =
+        error == cudaErrorMemoryAllocation ? HS_STATUS_OUT_OF_MEMORY : HS_STATUS_CUDA_ERROR;
+    std::string message(operation);
+    message += ": ";
+    message += cudaGetErrorString(error);
+    return fail(status, message, error_text, error_capacity);
+}
+
+int32_t cublas_failure(cublasStatus_t status, const char* operation, char* error_text,
+                       uint64_t error_capacity) noexcept {
+    std::string message(operation);
+    message += ": ";
+    message += cublasGetStatusString(status);
+    return fail(HS_STATUS_CUDA_ERROR, message, error_text, error_capacity);
+}
+
+int32_t cusolver_failure(cusolverStatus_t status, const char* operation, char* error_text,
+                         uint64_t error_capacity) noexcept {
+    char message[256] = {};
+    std::snprintf(message, sizeof(message), "%s: cuSOLVER status %d", operation,
+                  static_cast<int>(status));
+    return fail(status == CUSOLVER_STATUS_ALLOC_FAILED ? HS_STATUS_OUT_OF_MEMORY
+                                                       : HS_STATUS_CUDA_ERROR,
+                message, error_text, error_capacity);
+}
+
+int32_t select_device(HsRasterizerHandle handle, char* error_text,
+                      uint64_t error_capacity) noexcept {
+    if (handle == nullptr) {
+        return fail(HS_STATUS_INVALID_ARGUMENT, "handle is null", error_text, error_capacity);
+    }
+    const cudaError_t error = cudaSetDevice(handle->device);
+    if (error != cudaSuccess) return cuda_failure(error, "cudaSetDevice", error_text, error_capacity);
+    return HS_STATUS_OK;
+}
+
+template <typename Function>
+int32_t guard(char* error_text, uint64_t error_capacity, Function&& function) noexcept {
+    if (error_capacity != 0 && error_text == nullptr) return HS_STATUS_INVALID_ARGUMENT;
+    try {
+        return function();
+    } catch (const std::bad_alloc& e) {
+        return fail(HS_STATUS_OUT_OF_MEMORY, e.what(), error_text, error_capacity);
+    } catch (const std::exception& e) {
+        return fail(HS_STATUS_INTERNAL_ERROR, e.what(), error_text, error_capacity);
+    } catch (...) {
+        return fail(HS_STATUS_INTERNAL_ERROR, "unknown native exception", error_text,
+                    error_capacity);
+    }
+}
+
+cudaError_t release_math(HsRasterizerContext* c) noexcept {
+    cudaError_t first = cudaSuccess;
+    if (c->math_workspace != nullptr) {
+        const cudaError_t e = cudaFree(c->math_workspace);
+        if (first == cudaSuccess) first = e;
+        c->math_workspace = nullptr;
+    }
+    for (cublasHandle_t* h : {&c->math_tf32_blas, &c->math_default_blas}) {
+        if (*h != nullptr) {
+            if (cublasDestroy(*h) != CUBLAS_STATUS_SUCCESS && first == cudaSuccess)
+                first = cudaErrorUnknown;
+            *h = nullptr;
+        }
+    }
+    if (c->math_solver != nullptr) {
+        if (cusolverDnDestroy(c->math_solver) != CUSOLVER_STATUS_SUCCESS && first == cudaSuccess)
+            first = cudaErrorUnknown;
+        c->math_solver = nullptr;
+    }
+    c->math_workspace_bytes = 0;
+    return first;
+}
+
+// Persistent cuBLAS/cuSOLVER resources for the camera helpers
+// (reference c_api.cpp:234-364).
+int32_t initialize_math(HsRasterizerContext* c, char* error_text, uint64_t error_capacity) {
+    cublasStatus_t bs = cublasCreate(&c->math_tf32_blas);
+    if (bs != CUBLAS_STATUS_SUCCESS)
+        return cublas_failure(bs, "math TF32 cublasCreate", error_text, error_capacity);
+    ++c->math_handle_create_count;
+    bs = cublasSetStream(c->math_tf32_blas, nullptr);
+    if (bs == CUBLAS_STATUS_SUCCESS) bs = cublasSetPointerMode(c->math_tf32_blas, CUBLAS_POINTER_MODE_HOST);
+    if (bs == CUBLAS_STATUS_SUCCESS) bs = cublasSetMathMode(c->math_tf32_blas, CUBLAS_TF32_TENSOR_OP_MATH);
+    if (bs != CUBLAS_STATUS_SUCCESS)
+        return cublas_failure(bs, "math TF32 handle setup", error_text, error_capacity);
+    bs = cublasCreate(&c->math_default_blas);
+    if (bs != CUBLAS_STATUS_SUCCESS)
+        return cublas_failure(bs, "math FP32 cublasCreate", error_text, error_capacity);
+    ++c->math_handle_create_count;
+    bs = cublasSetStream(c->math_default_blas, nullptr);
+    if (bs == CUBLAS_STATUS_SUCCESS) bs = cublasSetPointerMode(c->math_default_blas, CUBLAS_POINTER_MODE_HOST);
+    if (bs == CUBLAS_STATUS_SUCCESS) bs = cublasSetMathMode(c->math_default_blas, CUBLAS_DEFAULT_MATH);
+    if (bs != CUBLAS_STATUS_SUCCESS)
+        return cublas_failure(bs, "math FP32 handle setup", error_text, error_capacity);
+    cusolverStatus_t ss = cusolverDnCreate(&c->math_solver);
+    if (ss != CUSOLVER_STATUS_SUCCESS)
+        return cusolver_failure(ss, "math cusolverDnCreate", error_text, error_capacity);
+    ++c->math_handle_create_count;
+    ss = cusolverDnSetStream(c->math_solver, nullptr);
+    if (ss != CUSOLVER_STATUS_SUCCESS)
+        return cusolver_failure(ss, "math cusolverDnSetStream", error_text, error_capacity);
+    cudaError_t cs = cudaMalloc(&c->math_workspace, kMathWorkspaceBytes);
+    if (cs != cudaSuccess)
+        return cuda_failure(cs, "math workspace cudaMalloc", error_text, error_capacity);
+    c->math_workspace_bytes = kMathWorkspaceBytes;
+    c->math_peak_bytes = kMathWorkspaceBytes;
+    ++c->math_growth_count;
+    float identity3[9] = {}, identity4[16] = {};
+    for (int i = 0; i < 3; ++i) identity3[4 * i] = 1.0f;
+    for (int i = 0; i < 4; ++i) identity4[5 * i] = 1.0f;
+    float* factor = reinterpret_cast<float*>(math_at(c, kMathFactorOffset));
+    float* rhs = reinterpret_cast<float*>(math_at(c, kMathRhsOffset));
+    cs = cudaMemcpy(math_at(c, kMathIdentity3Offset), identity3, sizeof(identity3), cudaMemcpyHostToDevice);
+    if (cs == cudaSuccess)
+        cs = cudaMemcpy(math_at(c, kMathIdentity4Offset), identity4, sizeof(identity4), cudaMemcpyHostToDevice);
+    if (cs == cudaSuccess)
+        cs = cudaMemcpy(math_at(c, kMathFactorArrayOffset), &factor, sizeof(factor), cudaMemcpyHostToDevice);
+    if (cs == cudaSuccess)
+        cs = cudaMemcpy(math_at(c, kMathRhsArrayOffset), &rhs, sizeof(rhs), cudaMemcpyHostToDevice);
+    if (cs != cudaSuccess)
+        return cuda_failure(cs, "math workspace initialization", error_text, error_capacity);
+    ss = cusolverDnSgetrf_bufferSize(c->math_solver, 4, 4, factor, 4, &c->math_inverse_workspace_count);
+    if (ss != CUSOLVER_STATUS_SUCCESS)
+        return cusolver_failure(ss, "math inverse workspace query", error_text, error_capacity);
+    if (kMathSolverWorkspaceOffset + uint64_t(c->math_inverse_workspace_count) * sizeof(float) >
+        kMathWorkspaceBytes) {
+        return fail(HS_STATUS_RANGE_ERROR, "math inverse workspace exceeds persistent allocation",
+                    error_text, error_capacity);
+    }
+    return HS_STATUS_OK;
+}
+
+bool finite3(const float* v) {
+    return std::isfinite(v[0]) && std::isfinite(v[1]) && std::isfinite(v[2]);
+}
+
+// Guards the elementwise entry points: count == 0 succeeds with NULL buffers.
+template <class Launch>
+int32_t elementwise(const char* name, uint64_t count, bool buffers_present, char* error_text,
+                    uint64_t error_capacity, Launch&& launch) {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (count == 0) return ok(error_text, error_capacity);
+        if (!buffers_present) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        std::string(name) + " received a null non-empty buffer", error_text,
+                        error_capacity);
+        }
+        const cudaError_t e = launch();
+        if (e != cudaSuccess)
+            return cuda_failure(e, (std::string(name) + " launch").c_str(), error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+}  // namespace
+
+extern "C" {
+
+uint32_t hs_rasterizer_abi_version(void) noexcept { return HS_RASTERIZER_ABI_VERSION; }
+
+int32_t hs_rasterizer_build_info(char* output_text, uint64_t output_capacity) noexcept {
+    if (output_text == nullptr || output_capacity == 0) return HS_STATUS_INVALID_ARGUMENT;
+    const char* info =
+        "{\"abi\":2,\"build_id\":\"hybridsplat-b200\",\"cuda\":\"12.9\",\"sm\":100,"
+        "\"arch\":\"sm_100a\",\"cxx_standard\":17,\"cuda_standard\":17,"
+        "\"fast_math\":false,\"stream\":0,"
+        "\"flashgs_forward\":\"deterministic_depth_then_tile_sort_v1\","
+        "\"flashgs_preprocess_invisible_slots\":\"zero\","
+        "\"five_channel_rasterizer\":\"forward_v1\","
+        "\"optix_reflection_tracer\":\"unavailable\","
+        "\"workspace_growth\":\"1.25x_align_2mib\"}";
+    write_text(output_text, output_capacity, info);
+    return std::strlen(info) + 1 > output_capacity ? HS_STATUS_RANGE_ERROR : HS_STATUS_OK;
+}
+
+int32_t hs_rasterizer_create(int32_t device, HsRasterizerHandle* handle, char* error_text,
+                             uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "handle output is null", error_text, error_capacity);
+        }
+        *handle = nullptr;
+        int device_count = 0;
+        cudaError_t e = cudaGetDeviceCount(&device_count);
+        if (e != cudaSuccess) return cuda_failure(e, "cudaGetDeviceCount", error_text, error_capacity);
+        if (device < 0 || device >= device_count) {
+            return fail(HS_STATUS_RANGE_ERROR, "device is outside the visible CUDA device range",
+                        error_text, error_capacity);
+        }
+        e = cudaSetDevice(device);
+        if (e != cudaSuccess) return cuda_failure(e, "cudaSetDevice", error_text, error_capacity);
+        *handle = new HsRasterizerContext(device);
+        const int32_t status = initialize_math(*handle, error_text, error_capacity);
+        if (status != HS_STATUS_OK) {
+            release_math(*handle);
+            delete *handle;
+            *handle = nullptr;
+            return status;
+        }
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_synchronize(HsRasterizerHandle handle, char* error_text,
+                                  uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        const cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_failure(e, "cudaDeviceSynchronize", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_workspace_stats(HsRasterizerHandle handle,
+                                      HsRasterizerWorkspaceStatsV1* stats, char* error_text,
+                                      uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || stats == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "handle or stats is null", error_text, error_capacity);
+        }
+        if (stats->struct_size != sizeof(HsRasterizerWorkspaceStatsV1) ||
+            stats->abi_version != HS_RASTERIZER_ABI_VERSION) {
+            return fail(HS_STATUS_ABI_MISMATCH, "workspace stats ABI does not match", error_text,
+                        error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        stats->device = handle->device;
+        stats->reserved = 0;
+        stats->geometry_bytes = handle->std_geometry.bytes;
+        stats->binning_bytes = handle->std_binning.bytes;
+        stats->image_bytes = handle->std_image.bytes;
+        stats->current_bytes = hs::standard_current_bytes(handle);
+        stats->peak_bytes = handle->std_peak_bytes;
+        stats->growth_count = handle->std_growth_count;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_release_workspace(HsRasterizerHandle handle, char* error_text,
+                                        uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_failure(e, "cudaDeviceSynchronize", error_text, error_capacity);
+        e = hs::standard_release(handle);
+        if (e != cudaSuccess) return cuda_failure(e, "release rasterizer workspace", error_text, error_capacity);
+        e = hs::flashgs_release(handle);
+        if (e != cudaSuccess) return cuda_failure(e, "release FlashGS workspace", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_math_workspace_stats_v2(HsRasterizerHandle handle,
+                                              HsMathWorkspaceStatsV2* stats, char* error_text,
+                                              uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || stats == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "handle or math stats is null", error_text,
+                        error_capacity);
+        }
+        if (stats->struct_size != sizeof(HsMathWorkspaceStatsV2) ||
+            stats->abi_version != HS_RASTERIZER_ABI_VERSION) {
+            return fail(HS_STATUS_ABI_MISMATCH, "math workspace stats ABI does not match",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        stats->device = handle->device;
+        stats->handles_ready = handle->math_tf32_blas != nullptr &&
+                                       handle->math_default_blas != nullptr &&
+                                       handle->math_solver != nullptr
+                                   ? 1u
+                                   : 0u;
+        stats->workspace_bytes = handle->math_workspace_bytes;
+        stats->current_bytes = handle->math_workspace_bytes;
+        stats->peak_bytes = handle->math_peak_bytes;
+        stats->growth_count = handle->math_growth_count;
+        stats->handle_create_count = handle->math_handle_create_count;
+        stats->camera_center_calls = handle->math_camera_center_calls;
+        stats->general_inverse_calls = handle->math_general_inverse_calls;
+        stats->matmul_calls = handle->math_matmul_calls;
+        stats->pixel_world_calls = handle->math_pixel_world_calls;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_destroy(HsRasterizerHandle handle, char* error_text,
+                              uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "handle is null", error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        {
+            std::lock_guard<std::mutex> lock(handle->mutex);
+            cudaError_t e = cudaDeviceSynchronize();
+            if (e != cudaSuccess) return cuda_failure(e, "cudaDeviceSynchronize", error_text, error_capacity);
+            e = hs::standard_release(handle);
+            if (e != cudaSuccess) return cuda_failure(e, "release rasterizer workspace", error_text, error_capacity);
+            e = hs::flashgs_release(handle);
+            if (e != cudaSuccess) return cuda_failure(e, "release FlashGS context", error_text, error_capacity);
+            e = release_math(handle);
+            if (e != cudaSuccess) return cuda_failure(e, "release math context", error_text, error_capacity);
+        }
+        delete handle;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_flashgs_forward_f32_v1(
+    HsRasterizerHandle handle, uint64_t point_count, int32_t width, int32_t height,
+    const float* positions3, const float* shs48, const float* colors3, int32_t use_sh,
+    const float* opacities1, const float* covariance6, const float* scales2, float scale_modifier,
+    const float* rotations4, const float* specular1, const float* roughness1,
+    const float* camera_position3, const float* camera_rotation9, float focal_x, float focal_y,
+    float z_far, float z_near, const float* background3, uint64_t initial_pair_capacity,
+    float* output_color3, float* output_other2, float* output_depth1, float* output_alpha1,
+    float* output_normal3, float* output_median_depth1, float* output_distortion1,
+    int32_t* output_num_rendered, char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || camera_position3 == nullptr || camera_rotation9 == nullptr ||
+            background3 == nullptr || output_color3 == nullptr || output_other2 == nullptr ||
+            output_depth1 == nullptr || output_alpha1 == nullptr || output_normal3 == nullptr ||
+            output_median_depth1 == nullptr || output_distortion1 == nullptr ||
+            output_num_rendered == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "FlashGS received a null required handle or buffer", error_text,
+                        error_capacity);
+        }
+        if (point_count > static_cast<uint64_t>(INT_MAX) || width <= 0 || height <= 0 ||
+            (use_sh != 0 && use_sh != 1) || initial_pair_capacity == 0 ||
+            initial_pair_capacity > static_cast<uint64_t>(INT_MAX) ||
+            !std::isfinite(scale_modifier) || scale_modifier <= 0.0f || !std::isfinite(focal_x) ||
+            focal_x <= 0.0f || !std::isfinite(focal_y) || focal_y <= 0.0f ||
+            !std::isfinite(z_near) || z_near <= 0.0f || !std::isfinite(z_far) || z_far <= z_near) {
+            return fail(HS_STATUS_RANGE_ERROR, "FlashGS dimensions or scalar arguments are invalid",
+                        error_text, error_capacity);
+        }
+        if (!finite3(camera_position3) || !finite3(background3)) {
+            return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera position or background is not finite",
+                        error_text, error_capacity);
+        }
+        for (int i = 0; i < 9; ++i) {
+            if (!std::isfinite(camera_rotation9[i])) {
+                return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera rotation is not finite",
+                            error_text, error_capacity);
+            }
+        }
+        if (point_count != 0 &&
+            (positions3 == nullptr || opacities1 == nullptr || covariance6 == nullptr ||
+             scales2 == nullptr || rotations4 == nullptr || specular1 == nullptr ||
+             roughness1 == nullptr || (use_sh != 0 && shs48 == nullptr) ||
+             (use_sh == 0 && colors3 == nullptr))) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "non-empty FlashGS input contains a null buffer",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        const cudaError_t e = hs::flashgs_forward(
+            handle, static_cast<int32_t>(point_count), width, height, positions3, shs48, colors3,
+            use_sh != 0, opacities1, covariance6, scales2, scale_modifier, rotations4, specular1,
+            roughness1, camera_position3, camera_rotation9, focal_x, focal_y, z_far, z_near,
+            background3, initial_pair_capacity, output_color3, output_other2, output_depth1,
+            output_alpha1, output_normal3, output_median_depth1, output_distortion1,
+            output_num_rendered, nullptr);
+        if (e != cudaSuccess)
+            return cuda_failure(e, "deterministic FlashGS forward", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_flashgs_workspace_stats_v1(HsRasterizerHandle handle,
+                                      HsFlashgsWorkspaceStatsV1* stats, char* error_text,
+                                      uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || stats == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "handle or FlashGS stats is null", error_text,
+                        error_capacity);
+        }
+        if (stats->struct_size != sizeof(HsFlashgsWorkspaceStatsV1) ||
+            stats->abi_version != HS_RASTERIZER_ABI_VERSION) {
+            return fail(HS_STATUS_ABI_MISMATCH, "FlashGS workspace stats ABI does not match",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        stats->device = handle->device;
+        stats->initialized = handle->fg_pairs.ptr != nullptr ? 1u : 0u;
+        stats->gaussian_capacity = handle->fg_gaussian_capacity;
+        stats->pair_capacity = handle->fg_pair_capacity;
+        stats->range_capacity = handle->fg_range_capacity;
+        stats->output_pixel_capacity = 0;
+        stats->gaussian_bytes = handle->fg_gaussian.bytes;
+        stats->pair_bytes = handle->fg_pairs.bytes;
+        stats->cub_bytes = handle->fg_sort.bytes;
+        stats->ranges_bytes = handle->fg_ranges.bytes;
+        stats->output_bytes = 0;
+        stats->current_bytes = hs::flashgs_current_bytes(handle);
+        stats->peak_bytes = handle->fg_peak_bytes;
+        stats->growth_count = handle->fg_growth_count;
+        stats->overflow_retry_count = handle->fg_overflow_retry_count;
+        stats->forward_calls = handle->fg_forward_calls;
+        stats->last_point_count = handle->fg_last_point_count;
+        stats->last_num_rendered = handle->fg_last_num_rendered;
+        stats->last_tile_count = handle->fg_last_tile_count;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_flashgs_prepare_npz_host_f32_v1(uint64_t point_count, const float* opacity_raw1,
+                                           const float* scaling_raw2, const float* rotation_raw4,
+                                           const float* specular_raw1,
+                                           const float* roughness_raw1, float* opacity1,
+                                           float* scaling2, float* rotation4, float* covariance6,
+                                           float* specular1, float* roughness1, char* error_text,
+                                           uint64_t error_capacity) noexcept {
+    // Validation order of flashgs_prepare.cpp:46-56: the error buffer is
+    // cleared first, then checked.
+    write_text(error_text, error_capacity, "");
+    if (error_capacity != 0 && error_text == nullptr) return HS_STATUS_INVALID_ARGUMENT;
+    if (point_count == 0) return HS_STATUS_OK;
+    if (opacity_raw1 == nullptr || scaling_raw2 == nullptr || rotation_raw4 == nullptr ||
+        specular_raw1 == nullptr || roughness_raw1 == nullptr || opacity1 == nullptr ||
+        scaling2 == nullptr || rotation4 == nullptr || covariance6 == nullptr ||
+        specular1 == nullptr || roughness1 == nullptr) {
+        write_text(error_text, error_capacity, "FlashGS NPZ preparation received a null host buffer");
+        return HS_STATUS_INVALID_ARGUMENT;
+    }
+    try {
+        hs::flashgs_prepare_host(point_count, opacity_raw1, scaling_raw2, rotation_raw4,
+                                 specular_raw1, roughness_raw1, opacity1, scaling2, rotation4,
+                                 covariance6, specular1, roughness1);
+        return HS_STATUS_OK;
+    } catch (const std::exception& e) {
+        write_text(error_text, error_capacity, e.what());
+        return HS_STATUS_INTERNAL_ERROR;
+    } catch (...) {
+        write_text(error_text, error_capacity, "unknown FlashGS NPZ preparation error");
+        return HS_STATUS_INTERNAL_ERROR;
+    }
+}
+
+int32_t hs_flashgs_debug_copy_v1(HsRasterizerHandle handle, uint64_t point_capacity,
+                                 uint64_t pair_capacity, uint64_t tile_capacity,
+                                 float* points_xy2, float* rgb3, float* other2,
+                                 float* conic_opacity4, float* normal_opacity4, float* tu3,
+                                 float* tv3, float* tw3, uint64_t* sorted_keys,
+                                 uint32_t* sorted_values, int32_t* tile_ranges2,
+                                 char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "FlashGS debug copy received a null context",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        const cudaError_t e = hs::flashgs_debug_copy(
+            handle, point_capacity, pair_capacity, tile_capacity, points_xy2, rgb3, other2,
+            conic_opacity4, normal_opacity4, tu3, tv3, tw3, sorted_keys, sorted_values,
+            tile_ranges2);
+        if (e != cudaSuccess) return cuda_failure(e, "FlashGS debug copy", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_forward_f32_v1(
+    HsRasterizerHandle handle, uint64_t point_count, const float* background5, int32_t width,
+    int32_t height, const float* means3d, const float* colors5, const float* opacities,
+    const float* scales2, float scale_modifier, const float* rotations4,
+    const float* viewmatrix4x4, const float* projmatrix4x4, const float* camera_position3,
+    float tan_fovx, float tan_fovy, int32_t prefiltered, float* output_color5, float* output_aux7,
+    float* output_weight, int32_t* output_radii, int32_t* output_rendered, char* error_text,
+    uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || background5 == nullptr || output_color5 == nullptr ||
+            output_aux7 == nullptr || output_rendered == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "rasterizer received a null required handle or buffer", error_text,
+                        error_capacity);
+        }
+        if (point_count > static_cast<uint64_t>(INT_MAX) || width <= 0 || height <= 0 ||
+            !std::isfinite(scale_modifier) || !std::isfinite(tan_fovx) ||
+            !std::isfinite(tan_fovy) || tan_fovx <= 0.0f || tan_fovy <= 0.0f ||
+            (prefiltered != 0 && prefiltered != 1)) {
+            return fail(HS_STATUS_RANGE_ERROR, "rasterizer dimensions or scalar arguments are invalid",
+                        error_text, error_capacity);
+        }
+        if (point_count != 0 &&
+            (means3d == nullptr || colors5 == nullptr || opacities == nullptr ||
+             scales2 == nullptr || rotations4 == nullptr || viewmatrix4x4 == nullptr ||
+             projmatrix4x4 == nullptr || camera_position3 == nullptr ||
+             output_weight == nullptr || output_radii == nullptr)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "non-empty rasterizer input contains a null buffer", error_text,
+                        error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        const cudaError_t e = hs::standard_forward(
+            handle, static_cast<int32_t>(point_count), background5, width, height, means3d,
+            colors5, opacities, scales2, scale_modifier, rotations4, viewmatrix4x4,
+            projmatrix4x4, camera_position3, tan_fovx, tan_fovy, prefiltered != 0, output_color5,
+            output_aux7, output_weight, output_radii, output_rendered, nullptr);
+        if (e != cudaSuccess)
+            return cuda_failure(e, "five-channel rasterizer forward", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+// OptiX entry points: the OptiX SDK is not part of this build.
+static const char* kNoOptix =
+    "OptiX reflection tracing is not available in this build: the OptiX SDK is not part of it";
+
+int32_t hs_optix_build_scene_v1(HsRasterizerHandle, const float*, uint64_t, const int32_t*,
+                                uint64_t, uint64_t, int32_t, int32_t*, char* error_text,
+                                uint64_t error_capacity) noexcept {
+    if (error_capacity != 0 && error_text == nullptr) return HS_STATUS_INVALID_ARGUMENT;
+    return fail(HS_STATUS_INTERNAL_ERROR, kNoOptix, error_text, error_capacity);
+}
+
+int32_t hs_optix_trace_f32_v1(HsRasterizerHandle, uint64_t, const float*, const float*,
+                              const float*, const float*, const float*, uint32_t, uint32_t,
+                              const float*, const float*, const float*, float, const float*,
+                              const float*, const float*, const float*, int32_t, int32_t, float,
+                              int32_t, float*, float*, float*, float*, float*, float*, float*,
+                              float*, char* error_text, uint64_t error_capacity) noexcept {
+    if (error_capacity != 0 && error_text == nullptr) return HS_STATUS_INVALID_ARGUMENT;
+    return fail(HS_STATUS_INTERNAL_ERROR, kNoOptix, error_text, error_capacity);
+}
+
+int32_t hs_optix_workspace_stats_v1(HsRasterizerHandle handle, HsOptixWorkspaceStatsV1* stats,
+                                    char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || stats == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "handle or OptiX stats is null", error_text,
+                        error_capacity);
+        }
+        if (stats->struct_size != sizeof(HsOptixWorkspaceStatsV1) ||
+            stats->abi_version != HS_RASTERIZER_ABI_VERSION) {
+            return fail(HS_STATUS_ABI_MISMATCH, "OptiX workspace stats ABI does not match",
+                        error_text, error_capacity);
+        }
+        const uint32_t size = stats->struct_size, abi = stats->abi_version;
+        std::memset(stats, 0, sizeof(*stats));
+        stats->struct_size = size;
+        stats->abi_version = abi;
+        stats->device = handle->device;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_optix_release_scene_v1(HsRasterizerHandle handle, char* error_text,
+                                  uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "handle is null", error_text, error_capacity);
+        }
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_precise_exp_f32_v1(const float* input, float* output, uint64_t count,
+                                         char* error_text, uint64_t error_capacity) noexcept {
+    return elementwise("precise_exp", count, input != nullptr && output != nullptr, error_text,
+                       error_capacity, [&] { return hs::precise::exp(input, output, count, nullptr); });
+}
+
+int32_t hs_rasterizer_precise_sigmoid_f32_v1(const float* input, float* output, uint64_t count,
+                                             char* error_text, uint64_t error_capacity) noexcept {
+    return elementwise("precise_sigmoid", count, input != nullptr && output != nullptr, error_text,
+                       error_capacity,
+                       [&] { return hs::precise::sigmoid(input, output, count, nullptr); });
+}
+
+int32_t hs_rasterizer_precise_normalize4_f32_v1(const float* input4, float* output4,
+                                                uint64_t count, char* error_text,
+                                                uint64_t error_capacity) noexcept {
+    return elementwise("precise_normalize4", count, input4 != nullptr && output4 != nullptr,
+                       error_text, error_capacity,
+                       [&] { return hs::precise::normalize4(input4, output4, count, nullptr); });
+}
+
+int32_t hs_rasterizer_precise_fuse_maps_f32_v1(const float* base_rgb, const float* reflection_rgb,
+                                               const float* specular, float* diffuse,
+                                               float* final_rgb, float* stored_reflection,
+                                               uint64_t pixel_count, char* error_text,
+                                               uint64_t error_capacity) noexcept {
+    const bool present = base_rgb != nullptr && reflection_rgb != nullptr &&
+                         specular != nullptr && diffuse != nullptr && final_rgb != nullptr &&
+                         stored_reflection != nullptr;
+    return elementwise("precise_fuse_maps", pixel_count, present, error_text, error_capacity, [&] {
+        return hs::precise::fuse_maps(base_rgb, reflection_rgb, specular, diffuse, final_rgb,
+                                      stored_reflection, pixel_count, nullptr);
+    });
+}
+
+int32_t hs_rasterizer_precise_sh_to_rgb_f32_v1(const float* sh, const float* directions,
+                                               uint64_t count, uint32_t coefficient_count,
+                                               uint32_t degree, float* output, char* error_text,
+                                               uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (degree > 3) {
+            return fail(HS_STATUS_RANGE_ERROR, "precise_sh_to_rgb supports degrees 0 through 3",
+                        error_text, error_capacity);
+        }
+        if (coefficient_count < (degree + 1) * (degree + 1)) {
+            return fail(HS_STATUS_RANGE_ERROR, "precise_sh_to_rgb coefficient count is too small",
+                        error_text, error_capacity);
+        }
+        if (count == 0) return ok(error_text, error_capacity);
+        if (sh == nullptr || directions == nullptr || output == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "precise_sh_to_rgb received a null non-empty buffer",
+                        error_text, error_capacity);
+        }
+        const cudaError_t e = hs::precise::sh_to_rgb(sh, directions, count, coefficient_count,
+                                                     degree, output, nullptr);
+        if (e != cudaSuccess) return cuda_failure(e, "precise_sh_to_rgb launch", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_precise_direction_f32_v1(const float* points, const float* center,
+                                               uint64_t count, float* output, char* error_text,
+                                               uint64_t error_capacity) noexcept {
+    return elementwise("precise_direction", count,
+                       points != nullptr && center != nullptr && output != nullptr, error_text,
+                       error_capacity,
+                       [&] { return hs::precise::direction(points, center, count, output, nullptr); });
+}
+
+int32_t hs_rasterizer_precise_camera_center_f32_v2(HsRasterizerHandle handle,
+                                                   const float* rotation3x3,
+                                                   const float* translation3x1, float* output3,
+                                                   char* error_text,
+                                                   uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || rotation3x3 == nullptr || translation3x1 == nullptr ||
+            output3 == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "precise_camera_center received a null buffer",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        if (handle->math_workspace == nullptr || handle->math_tf32_blas == nullptr) {
+            return fail(HS_STATUS_INTERNAL_ERROR, "precise_camera_center math context is not initialized",
+                        error_text, error_capacity);
+        }
+        float* negative = reinterpret_cast<float*>(math_at(handle, kMathCameraOffset));
+        const cudaError_t ce = hs::precise::negate9(rotation3x3, negative, nullptr);
+        if (ce != cudaSuccess)
+            return cuda_failure(ce, "precise_camera_center negative-R", error_text, error_capacity);
+        // output[1x3] = t[1x3] * (-R)^T as in reference c_api.cpp:1390-1407.
+        const float alpha = 1.0f, beta = 0.0f;
+        const cublasStatus_t bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_N, CUBLAS_OP_T, 1,
+                                              3, 3, &alpha, translation3x1, 1, negative, 3, &beta,
+                                              output3, 1);
+        if (bs != CUBLAS_STATUS_SUCCESS)
+            return cublas_failure(bs, "precise_camera_center SGEMM", error_text, error_capacity);
+        ++handle->math_camera_center_calls;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_precise_general_inverse_f32_v2(HsRasterizerHandle handle,
+                                                     const float* input, uint32_t dimension,
+                                                     float* output, char* error_text,
+                                                     uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (dimension != 3 && dimension != 4) {
+            return fail(HS_STATUS_RANGE_ERROR, "precise_general_inverse dimension must be 3 or 4",
+                        error_text, error_capacity);
+        }
+        if (handle == nullptr || input == nullptr || output == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "precise_general_inverse received a null buffer",
+                        error_text, error_capacity);
+        }
+        const cudaError_t prior = cudaGetLastError();
+        if (prior != cudaSuccess) {
+            return cuda_failure(prior, "precise_general_inverse preexisting CUDA error", error_text,
+                                error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        if (handle->math_workspace == nullptr || handle->math_solver == nullptr ||
+            handle->math_tf32_blas == nullptr) {
+            return fail(HS_STATUS_INTERNAL_ERROR,
+                        "precise_general_inverse math context is not initialized", error_text,
+                        error_capacity);
+        }
+        // linalg_inv_ex as in reference c_api.cpp:1493-1600: identity RHS, LU of
+        // the row-major input read as column-major A^T, getrs with OP_T.
+        const int n = static_cast<int>(dimension);
+        float* factor = reinterpret_cast<float*>(math_at(handle, kMathFactorOffset));
+        float* rhs = reinterpret_cast<float*>(math_at(handle, kMathRhsOffset));
+        float* work = reinterpret_cast<float*>(math_at(handle, kMathSolverWorkspaceOffset));
+        int* pivots = reinterpret_cast<int*>(math_at(handle, kMathPivotsOffset));
+        int* info = reinterpret_cast<int*>(math_at(handle, kMathInfoOffset));
+        float** factor_array = reinterpret_cast<float**>(math_at(handle, kMathFactorArrayOffset));
+        float** rhs_array = reinterpret_cast<float**>(math_at(handle, kMathRhsArrayOffset));
+        const size_t bytes = static_cast<size_t>(n) * n * sizeof(float);
+        cudaError_t ce = cudaMemcpyAsync(
+            rhs, math_at(handle, n == 3 ? kMathIdentity3Offset : kMathIdentity4Offset), bytes,
+            cudaMemcpyDeviceToDevice, nullptr);
+        if (ce == cudaSuccess) ce = cudaMemcpyAsync(factor, input, bytes, cudaMemcpyDeviceToDevice, nullptr);
+        if (ce != cudaSuccess)
+            return cuda_failure(ce, "precise_general_inverse identity/input copy", error_text, error_capacity);
+        int work_count = 0;
+        cusolverStatus_t ss = cusolverDnSgetrf_bufferSize(handle->math_solver, n, n, factor, n, &work_count);
+        if (ss != CUSOLVER_STATUS_SUCCESS)
+            return cusolver_failure(ss, "precise_general_inverse cusolverDnSgetrf_bufferSize",
+                                    error_text, error_capacity);
+        if (work_count > handle->math_inverse_workspace_count) {
+            return fail(HS_STATUS_RANGE_ERROR, "precise_general_inverse persistent workspace is too small",
+                        error_text, error_capacity);
+        }
+        ss = cusolverDnSgetrf(handle->math_solver, n, n, factor, n, work, pivots, info);
+        if (ss != CUSOLVER_STATUS_SUCCESS)
+            return cusolver_failure(ss, "precise_general_inverse cusolverDnSgetrf", error_text, error_capacity);
+        int32_t* solve_info = &handle->math_solve_info[handle->math_general_inverse_calls % 16];
+        *solve_info = 0;
+        const cublasStatus_t bs = cublasSgetrsBatched(handle->math_tf32_blas, CUBLAS_OP_T, n, n,
+                                                      factor_array, n, pivots, rhs_array, n,
+                                                      solve_info, 1);
+        if (bs != CUBLAS_STATUS_SUCCESS)
+            return cublas_failure(bs, "precise_general_inverse cublasSgetrsBatched", error_text,
+                                  error_capacity);
+        ce = hs::precise::column_to_row_major(rhs, dimension, output, nullptr);
+        if (ce != cudaSuccess)
+            return cuda_failure(ce, "precise_general_inverse output transpose", error_text, error_capacity);
+        const cudaError_t trailing = cudaGetLastError();
+        if (trailing != cudaSuccess)
+            return cuda_failure(trailing, "precise_general_inverse trailing CUDA error", error_text,
+                                error_capacity);
+        ++handle->math_general_inverse_calls;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_precise_matmul_nt_n3k3_f32_v2(HsRasterizerHandle handle,
+                                                    const float* left_n3, const float* right3x3,
+                                                    uint64_t count, float* output_n3,
+                                                    char* error_text,
+                                                    uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (count == 0) return ok(error_text, error_capacity);
+        if (count > static_cast<uint64_t>(INT_MAX)) {
+            return fail(HS_STATUS_RANGE_ERROR, "precise_matmul_nt_n3k3 count exceeds cuBLAS int range",
+                        error_text, error_capacity);
+        }
+        if (handle == nullptr || left_n3 == nullptr || right3x3 == nullptr || output_n3 == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "precise_matmul_nt_n3k3 received a null non-empty buffer", error_text,
+                        error_capacity);
+        }
+        const cudaError_t prior = cudaGetLastError();
+        if (prior != cudaSuccess) {
+            return cuda_failure(prior, "precise_matmul_nt_n3k3 preexisting CUDA error", error_text,
+                                error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        if (handle->math_tf32_blas == nullptr) {
+            return fail(HS_STATUS_INTERNAL_ERROR, "precise_matmul_nt_n3k3 math context is not initialized",
+                        error_text, error_capacity);
+        }
+        const float alpha = 1.0f, beta = 0.0f;
+        const cublasStatus_t bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3,
+                                              static_cast<int>(count), 3, &alpha, right3x3, 3,
+                                              left_n3, 3, &beta, output_n3, 3);
+        if (bs != CUBLAS_STATUS_SUCCESS)
+            return cublas_failure(bs, "precise_matmul_nt_n3k3 cublasSgemm", error_text, error_capacity);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess)
+            return cuda_failure(e, "precise_matmul_nt_n3k3 execution", error_text, error_capacity);
+        ++handle->math_matmul_calls;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_precise_pixel_world_f32_v2(HsRasterizerHandle handle,
+                                                 const float* rotation3x3,
+                                                 const float* vectors_n3, uint64_t count,
+                                                 float* output_n3, char* error_text,
+                                                 uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (count == 0) return ok(error_text, error_capacity);
+        if (count > static_cast<uint64_t>(INT_MAX)) {
+            return fail(HS_STATUS_RANGE_ERROR, "precise_pixel_world count exceeds cuBLAS int range",
+                        error_text, error_capacity);
+        }
+        if (handle == nullptr || rotation3x3 == nullptr || vectors_n3 == nullptr ||
+            output_n3 == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "precise_pixel_world received a null non-empty buffer",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        if (handle->math_default_blas == nullptr) {
+            return fail(HS_STATUS_INTERNAL_ERROR, "precise_pixel_world math context is not initialized",
+                        error_text, error_capacity);
+        }
+        const float alpha = 1.0f, beta = 0.0f;
+        const cublasStatus_t bs = cublasGemmStridedBatchedEx(
+            handle->math_default_blas, CUBLAS_OP_N, CUBLAS_OP_N, 3, 1, 3, &alpha, rotation3x3,
+            CUDA_R_32F, 3, 0, vectors_n3, CUDA_R_32F, 3, 3, &beta, output_n3, CUDA_R_32F, 3, 3,
+            static_cast<int>(count), CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+        if (bs != CUBLAS_STATUS_SUCCESS)
+            return cublas_failure(bs, "precise_pixel_world batched GEMM", error_text, error_capacity);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_failure(e, "precise_pixel_world execution", error_text, error_capacity);
+        ++handle->math_pixel_world_calls;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_rasterizer_precise_disk_rotation_f32_v1(const float* rotation_wxyz, uint64_t count,
+                                                   float* rotation_matrix9, char* error_text,
+                                                   uint64_t error_capacity) noexcept {
+    return elementwise("precise_disk_rotation", count,
+                       rotation_wxyz != nullptr && rotation_matrix9 != nullptr, error_text,
+                       error_capacity, [&] {
+                           return hs::precise::disk_rotation(rotation_wxyz, count, rotation_matrix9,
+                                                             nullptr);
+                       });
+}
+
+int32_t hs_rasterizer_precise_reflection_prefix_f32_v1(const float* rotation_wxyz,
+                                                       uint64_t count, float* rotation_matrix9,
+                                                       char* error_text,
+                                                       uint64_t error_capacity) noexcept {
+    return elementwise("precise_reflection_prefix", count,
+                       rotation_wxyz != nullptr && rotation_matrix9 != nullptr, error_text,
+                       error_capacity, [&] {
+                           return hs::precise::reflection_prefix(rotation_wxyz, count,
+                                                                 rotation_matrix9, nullptr);
+                       });
+}
+
+int32_t hs_rasterizer_precise_reflection_suffix_f32_v1(const float* xyz,
+                                                       const float* camera_center,
+                                                       const float* normal_raw3, uint64_t count,
+                                                       float* output36, char* error_text,
+                                                       uint64_t error_capacity) noexcept {
+    return elementwise("precise_reflection_suffix", count,
+                       xyz != nullptr && camera_center != nullptr && normal_raw3 != nullptr &&
+                           output36 != nullptr,
+                       error_text, error_capacity, [&] {
+                           return hs::precise::reflection_suffix(xyz, camera_center, normal_raw3,
+                                                                 count, output36, nullptr);
+                       });
+}
+
+}  // extern "C"

@@ -1,0 +1,289 @@
+// FlashGS kernels (templates over the rounding policy). Instantiated by
+// flashgs.cu with the pinned policy; see flashgs.cu for the pipeline.
+#pragma once
+
+#include <climits>
+
+#include "flashgs_math.cuh"
+
+namespace hs {
+namespace fg {
+
+
+constexpr int kPreThreads = 128;
+constexpr int kRenderThreads = 128;  // 4 warps, 2 pixels per thread
+constexpr int kBatch = 32;           // Gaussians staged per shared-memory batch
+constexpr int kRecordQuads = 6;      // 96-byte record: 5 blend quads + conic/opacity
+constexpr int kEmitQuads = 2;        // 32-byte emit record
+
+struct Camera {
+    float view[16];
+    float proj[16];
+    float campos[3];
+    float tan_fovx, tan_fovy;
+    float focal_x, focal_y;
+    int width, height, grid_x, grid_y;
+};
+
+__device__ __forceinline__ float4 f4(float a, float b, float c, float d) {
+    return make_float4(a, b, c, d);
+}
+
+template <class R>
+__global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
+    int point_count, Camera cam, const float* __restrict__ positions,
+    const float* __restrict__ shs, const float* __restrict__ colors, int use_sh,
+    const float* __restrict__ opacities, const float* __restrict__ cov6,
+    const float* __restrict__ scales, float scale_modifier, const float* __restrict__ rotations,
+    const float* __restrict__ specular, const float* __restrict__ roughness,
+    float4* __restrict__ records, float4* __restrict__ emit, uint32_t* __restrict__ depth_keys,
+    uint32_t* __restrict__ order, uint32_t* __restrict__ pair_counts) {
+    const int idx = blockIdx.x * kPreThreads + threadIdx.x;
+    if (idx >= point_count) return;
+    const R r;
+    const float3 p = make_float3(positions[3 * idx], positions[3 * idx + 1], positions[3 * idx + 2]);
+    const float opacity = opacities[idx];
+    float cov[6];
+#pragma unroll
+    for (int k = 0; k < 6; ++k) cov[k] = cov6[6 * idx + k];
+    const float2 scale = make_float2(scales[2 * idx], scales[2 * idx + 1]);
+    const float4 rot = make_float4(rotations[4 * idx], rotations[4 * idx + 1],
+                                   rotations[4 * idx + 2], rotations[4 * idx + 3]);
+    const Projected g = project_gaussian(r, cam.view, cam.proj, p, opacity, cov, scale,
+                                         scale_modifier, rot, cam.width, cam.height, cam.focal_x,
+                                         cam.focal_y, cam.tan_fovx, cam.tan_fovy, cam.grid_x,
+                                         cam.grid_y);
+    uint32_t hits = 0;
+    bool write = false;
+    if (g.in_front && g.touches) {
+        const int area = (g.rect_max.x - g.rect_min.x) * (g.rect_max.y - g.rect_min.y);
+        if (area == 1) {
+            // Single-tile Gaussians always keep their record (preprocess.cu:482-506).
+            write = true;
+            hits = tile_hit(r, g.rect_min.x, g.rect_min.y, g.xy, g.conic, g.power) ? 1u : 0u;
+        } else {
+            for (int ty = g.rect_min.y; ty < g.rect_max.y; ++ty) {
+                for (int tx = g.rect_min.x; tx < g.rect_max.x; ++tx) {
+                    hits += tile_hit(r, tx, ty, g.xy, g.conic, g.power) ? 1u : 0u;
+                }
+            }
+            write = hits > 0;
+        }
+    }
+    float4* rec = records + static_cast<size_t>(idx) * kRecordQuads;
+    if (write) {
+        float3 rgb;
+        if (use_sh) {
+            rgb = sh_color(r, p, make_float3(cam.campos[0], cam.campos[1], cam.campos[2]),
+                           shs + static_cast<size_t>(idx) * 48);
+        } else {
+            rgb = make_float3(colors[3 * idx], colors[3 * idx + 1], colors[3 * idx + 2]);
+        }
+        const float sp = specular[idx], ro = roughness[idx];
+        rec[0] = f4(g.xy.x, g.xy.y, g.normal.x, g.normal.y);
+        rec[1] = f4(g.normal.z, opacity, rgb.x, rgb.y);
+        rec[2] = f4(rgb.z, sp, ro, g.tu.x);
+        rec[3] = f4(g.tu.y, g.tu.z, g.tv.x, g.tv.y);
+        rec[4] = f4(g.tv.z, g.tw.x, g.tw.y, g.tw.z);
+        rec[5] = f4(mul(-0.5f * kLog2e, g.conic.x), mul(-kLog2e, g.conic.y),
+                    mul(-0.5f * kLog2e, g.conic.z), g.log2_opacity);
+    } else {
+        const float4 z = f4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int q = 0; q < kRecordQuads; ++q) rec[q] = z;
+    }
+    float4* em = emit + static_cast<size_t>(idx) * kEmitQuads;
+    em[0] = f4(g.xy.x, g.xy.y, g.conic.x, g.conic.y);
+    const uint32_t lo = static_cast<uint32_t>(g.rect_min.x) | (static_cast<uint32_t>(g.rect_min.y) << 16);
+    const uint32_t hi = static_cast<uint32_t>(g.rect_max.x) | (static_cast<uint32_t>(g.rect_max.y) << 16);
+    em[1] = f4(g.conic.z, g.power, __uint_as_float(lo), __uint_as_float(hi));
+    depth_keys[idx] = hits > 0 ? __float_as_uint(g.depth) : 0xffffffffu;
+    order[idx] = static_cast<uint32_t>(idx);
+    pair_counts[idx] = hits;
+}
+
+template <class R>
+__global__ void __launch_bounds__(kPreThreads) emit_kernel(
+    int point_count, int grid_x, const uint32_t* __restrict__ order,
+    const uint32_t* __restrict__ pair_counts, const uint32_t* __restrict__ offsets,
+    const float4* __restrict__ emit, uint32_t* __restrict__ tile_ids,
+    uint32_t* __restrict__ gaussian_ids) {
+    const int s = blockIdx.x * kPreThreads + threadIdx.x;
+    if (s >= point_count) return;
+    const uint32_t gid = order[s];
+    if (pair_counts[gid] == 0) return;
+    const R r;
+    const float4 e0 = emit[static_cast<size_t>(gid) * kEmitQuads];
+    const float4 e1 = emit[static_cast<size_t>(gid) * kEmitQuads + 1];
+    const float2 xy = make_float2(e0.x, e0.y);
+    const float3 conic = make_float3(e0.z, e0.w, e1.x);
+    const float power = e1.y;
+    const uint32_t lo = __float_as_uint(e1.z), hi = __float_as_uint(e1.w);
+    const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff, y1 = hi >> 16;
+    uint32_t out = offsets[s];
+    for (int ty = y0; ty < y1; ++ty) {
+        for (int tx = x0; tx < x1; ++tx) {
+            if (tile_hit(r, tx, ty, xy, conic, power)) {
+                tile_ids[out] = static_cast<uint32_t>(ty * grid_x + tx);
+                gaussian_ids[out] = gid;
+                ++out;
+            }
+        }
+    }
+}
+
+__global__ void ranges_kernel(uint32_t pair_count, const uint32_t* __restrict__ tile_ids,
+                              int2* __restrict__ ranges) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= pair_count) return;
+    const uint32_t t = tile_ids[i];
+    if (i == 0) {
+        ranges[t].x = 0;
+    } else {
+        const uint32_t prev = tile_ids[i - 1];
+        if (t != prev) {
+            ranges[prev].y = static_cast<int>(i);
+            ranges[t].x = static_cast<int>(i);
+        }
+    }
+    if (i == pair_count - 1) ranges[t].y = static_cast<int>(pair_count);
+}
+
+__device__ __forceinline__ BlendRecord load_record(const float4* q) {
+    const float4 a = q[0], b = q[1], c = q[2], d = q[3], e = q[4];
+    BlendRecord g;
+    g.x = a.x; g.y = a.y; g.nx = a.z; g.ny = a.w;
+    g.nz = b.x; g.op = b.y; g.r = b.z; g.g = b.w;
+    g.b = c.x; g.spec = c.y; g.rough = c.z; g.tux = c.w;
+    g.tuy = d.x; g.tuz = d.y; g.tvx = d.z; g.tvy = d.w;
+    g.tvz = e.x; g.twx = e.y; g.twy = e.z; g.twz = e.w;
+    return g;
+}
+
+struct Outputs {
+    float* color;
+    float* other;
+    float* depth;
+    float* alpha;
+    float* normal;
+    float* median;
+    float* distortion;
+};
+
+template <class R>
+__device__ __forceinline__ void store_pixel(const R& r, const PixelState& s, float3 bg,
+                                            const Outputs& o, size_t plane, size_t pix) {
+    float v[12];
+    finish_pixel(r, s, bg, v);
+    o.color[pix] = v[0];
+    o.color[plane + pix] = v[1];
+    o.color[2 * plane + pix] = v[2];
+    o.other[pix] = v[3];
+    o.other[plane + pix] = v[4];
+    o.depth[pix] = v[5];
+    o.alpha[pix] = v[6];
+    o.normal[pix] = v[7];
+    o.normal[plane + pix] = v[8];
+    o.normal[2 * plane + pix] = v[9];
+    o.median[pix] = v[10];
+    o.distortion[pix] = v[11];
+}
+
+__device__ __forceinline__ void store_empty(float3 bg_encoded, const Outputs& o, size_t plane,
+                                            size_t pix) {
+    o.color[pix] = bg_encoded.x;
+    o.color[plane + pix] = bg_encoded.y;
+    o.color[2 * plane + pix] = bg_encoded.z;
+    o.other[pix] = 0.0f;
+    o.other[plane + pix] = 0.0f;
+    o.depth[pix] = 0.0f;
+    o.alpha[pix] = 0.0f;
+    o.normal[pix] = 0.0f;
+    o.normal[plane + pix] = 0.0f;
+    o.normal[2 * plane + pix] = 0.0f;
+    o.median[pix] = 0.0f;
+    o.distortion[pix] = 0.0f;
+}
+
+// Tile-wide termination. The reference warp stops after Gaussian j when all
+// 256 pixels of the tile (including pixels outside the image) have T < 1e-4,
+// so the tile consumes n_tile = (first such j) + 1 Gaussians and every pixel
+// blends exactly those. T never increases, so "warp w is done after j" is
+// monotone and n_tile - 1 = max over warps of each warp's first done index.
+// Per batch: phase A - every warp that is not yet done blends until it is
+// done (recording the index) or the batch ends; barrier; if all warps are
+// done the tile end is the maximum index, otherwise the batch end; phase B -
+// warps that stopped early blend the remaining Gaussians up to that end.
+template <class R>
+__global__ void __launch_bounds__(kRenderThreads) render_kernel(
+    const int2* __restrict__ ranges, const uint32_t* __restrict__ gaussian_ids,
+    const float4* __restrict__ records, int width, int height, int grid_x, float3 bg,
+    float3 bg_encoded, Outputs out) {
+    __shared__ float4 batch[kBatch * 5];
+    __shared__ int done_at[kRenderThreads / 32];
+    const R r;
+    const int tile = blockIdx.x;
+    const int tx = tile % grid_x, ty = tile / grid_x;
+    const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4;
+    const int px = tx * 16 + lx, py0 = ty * 16 + ly, py1 = py0 + 8;
+    const size_t plane = static_cast<size_t>(width) * height;
+    const bool in0 = px < width && py0 < height;
+    const bool in1 = px < width && py1 < height;
+    const int2 range = ranges[tile];
+    if (range.x >= range.y) {
+        if (in0) store_empty(bg_encoded, out, plane, static_cast<size_t>(py0) * width + px);
+        if (in1) store_empty(bg_encoded, out, plane, static_cast<size_t>(py1) * width + px);
+        return;
+    }
+    const float fx = static_cast<float>(px);
+    const float fy0 = static_cast<float>(py0), fy1 = static_cast<float>(py1);
+    PixelState s0, s1;
+    pixel_init(s0);
+    pixel_init(s1);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int n = range.y - range.x;
+    bool warp_done = false;
+    int warp_done_at = 0;
+    for (int base = 0; base < n; base += kBatch) {
+        const int nb = min(kBatch, n - base);
+        __syncthreads();
+        for (int i = threadIdx.x; i < nb * 5; i += kRenderThreads) {
+            const int j = i / 5, q = i - j * 5;
+            const uint32_t gid = gaussian_ids[range.x + base + j];
+            batch[i] = records[static_cast<size_t>(gid) * kRecordQuads + q];
+        }
+        __syncthreads();
+        int cursor = 0;
+        if (!warp_done) {
+            cursor = nb;
+            for (int j = 0; j < nb; ++j) {
+                const BlendRecord g = load_record(batch + j * 5);
+                blend(r, s0, fx, fy0, g);
+                blend(r, s1, fx, fy1, g);
+                if (__all_sync(0xffffffffu, s0.t < 0.0001f && s1.t < 0.0001f)) {
+                    warp_done = true;
+                    warp_done_at = base + j;
+                    cursor = j + 1;
+                    break;
+                }
+            }
+        }
+        if (lane == 0) done_at[warp] = warp_done ? warp_done_at : INT_MAX;
+        __syncthreads();
+        int tile_end = done_at[0];
+#pragma unroll
+        for (int w = 1; w < kRenderThreads / 32; ++w) tile_end = max(tile_end, done_at[w]);
+        const int stop = tile_end == INT_MAX ? nb : tile_end - base + 1;
+        for (int j = cursor; j < stop; ++j) {
+            const BlendRecord g = load_record(batch + j * 5);
+            blend(r, s0, fx, fy0, g);
+            blend(r, s1, fx, fy1, g);
+        }
+        if (tile_end != INT_MAX) break;
+    }
+    if (in0) store_pixel(r, s0, bg, out, plane, static_cast<size_t>(py0) * width + px);
+    if (in1) store_pixel(r, s1, bg, out, plane, static_cast<size_t>(py1) * width + px);
+}
+
+}  // namespace fg
+}  // namespace hs

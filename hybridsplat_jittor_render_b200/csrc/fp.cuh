@@ -1,0 +1,79 @@
+// Explicitly rounded FP32 arithmetic used by every kernel whose results must
+// be bit-identical to the reference backend.
+//
+// The reference kernels are plain C++ expressions compiled by nvcc with
+// --fmad=true, so the compiler decided where a product and a following
+// add/sub became one fused multiply-add. Results are reproduced bit-exactly
+// here by writing each such expression with explicit __fmul_rn / __fadd_rn /
+// __fmaf_rn operations; the fused/unfused form of every expression is a
+// "rounding site" with a small numbered choice, pinned by a Rounding policy
+// (see flashgs_math.cuh). Explicit *_rn operations are never re-contracted
+// by the compiler, whatever --fmad says.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hs {
+
+__device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float sub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fma(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+__device__ __forceinline__ float div(float a, float b) { return __fdiv_rn(a, b); }
+
+// Approximate special-function unit instructions, the same PTX instructions
+// the reference issues through inline asm (flashgs preprocess.cu:36-62).
+__device__ __forceinline__ float approx_sqrt(float x) {
+    float y;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float approx_rsqrt(float x) {
+    float y;
+    asm("rsqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float approx_lg2(float x) {
+    float y;
+    asm("lg2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float ptx_max(float a, float b) {
+    float d;
+    asm("max.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+
+// a*b + c with rounding choice: 0 fused, 1 product rounded first.
+__device__ __forceinline__ float mad(int v, float a, float b, float c) {
+    return v == 0 ? fma(a, b, c) : add(mul(a, b), c);
+}
+// a*b - c: 0 fma(a, b, -c), 1 product rounded first.
+__device__ __forceinline__ float msub(int v, float a, float b, float c) {
+    return v == 0 ? fma(a, b, -c) : sub(mul(a, b), c);
+}
+// x - a*b: 0 fma(-a, b, x), 1 product rounded first.
+__device__ __forceinline__ float nmad(int v, float x, float a, float b) {
+    return v == 0 ? fma(-a, b, x) : sub(x, mul(a, b));
+}
+// a*b + c*d: 0 fma(a, b, c*d), 1 fma(c, d, a*b), 2 both products rounded.
+__device__ __forceinline__ float dot2(int v, float a, float b, float c, float d) {
+    if (v == 0) return fma(a, b, mul(c, d));
+    if (v == 1) return fma(c, d, mul(a, b));
+    return add(mul(a, b), mul(c, d));
+}
+// a*b - c*d: 0 fma(a, b, -(c*d)), 1 fma(-c, d, a*b), 2 both rounded.
+__device__ __forceinline__ float diff2(int v, float a, float b, float c, float d) {
+    if (v == 0) return fma(a, b, -mul(c, d));
+    if (v == 1) return fma(-c, d, mul(a, b));
+    return sub(mul(a, b), mul(c, d));
+}
+// (a*b + c*d) + e*f: pair choice as dot2, tail 0 fused, 1 rounded.
+__device__ __forceinline__ float dot3(int vp, int vt, float a, float b, float c, float d,
+                                      float e, float f) {
+    const float s = dot2(vp, a, b, c, d);
+    return mad(vt, e, f, s);
+}
+
+}  // namespace hs

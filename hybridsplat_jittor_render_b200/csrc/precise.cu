@@ -1,0 +1,330 @@
+// Elementwise kernels with fixed FP32 rounding: activations, SH colour, view
+// direction, reflection-ray generation (prefix/suffix), disk rotation and the
+// two-branch fusion.
+//
+// Each kernel restates the rounding steps of the reference kernel named in
+// its comment. This file is compiled with --fmad=false (as the reference
+// compiles rasterizer/precise_{activation,direction,disk_rotation,
+// reflection_trace,sh}.cu, CMakeLists.txt:109-120), and every step is an
+// explicit *_rn operation, so the results are bit-identical. The kernels are
+// HBM-bound grid-stride loops sized to the SM count.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "fp.cuh"
+#include "precise.h"
+
+namespace hs {
+namespace precise {
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float norm3_torch(float x, float y, float z) {
+    // PyTorch's length-3 inner reduction adds (x^2 + z^2) + y^2
+    // (precise_reflection_trace.cu:35-42).
+    return __fsqrt_rn(add(add(mul(x, x), mul(z, z)), mul(y, y)));
+}
+
+__device__ __forceinline__ float norm4_torch(float a, float b, float c, float d) {
+    // (a^2 + b^2) + (c^2 + d^2) (precise_reflection_trace.cu:44-55).
+    return __fsqrt_rn(add(add(mul(a, a), mul(b, b)), add(mul(c, c), mul(d, d))));
+}
+
+__device__ __forceinline__ void normalize4_clamp(float& a, float& b, float& c, float& d,
+                                                 float eps) {
+    const float n = norm4_torch(a, b, c, d);
+    const float den = n < eps ? eps : n;
+    a = div(a, den);
+    b = div(b, den);
+    c = div(c, den);
+    d = div(d, den);
+}
+
+// Two F.normalize-style passes of build_rotation (precise_reflection_trace.cu:
+// 129-151, precise_disk_rotation.cu:68-92).
+__device__ __forceinline__ void twice_normalized(const float* q, float& w, float& x, float& y,
+                                                 float& z) {
+    w = q[0];
+    x = q[1];
+    y = q[2];
+    z = q[3];
+    normalize4_clamp(w, x, y, z, 1.0e-12f);
+    const float n = norm4_torch(w, x, y, z);
+    w = div(w, n);
+    x = div(x, n);
+    y = div(y, n);
+    z = div(z, n);
+}
+
+__global__ void sigmoid_kernel(const float* __restrict__ in, float* __restrict__ out,
+                               uint64_t count) {
+    // precise_activation.cu:11-17
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        out[i] = div(1.0f, add(1.0f, expf(sub(0.0f, in[i]))));
+    }
+}
+
+__global__ void normalize4_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                  uint64_t count) {
+    // precise_activation.cu:19-34
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        float a = in[4 * i], b = in[4 * i + 1], c = in[4 * i + 2], d = in[4 * i + 3];
+        normalize4_clamp(a, b, c, d, 1.0e-12f);
+        out[4 * i] = a;
+        out[4 * i + 1] = b;
+        out[4 * i + 2] = c;
+        out[4 * i + 3] = d;
+    }
+}
+
+__global__ void fuse_maps_kernel(const float* __restrict__ base, const float* __restrict__ refl,
+                                 const float* __restrict__ specular, float* __restrict__ diffuse,
+                                 float* __restrict__ final_rgb, float* __restrict__ stored,
+                                 uint64_t values) {
+    // precise_activation.cu:36-55
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < values;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        const float s = specular[i / 3];
+        const float dv = mul(base[i], sub(1.0f, s));
+        const float rv = mul(mul(refl[i], s), 2.0f);
+        diffuse[i] = dv;
+        stored[i] = rv;
+        final_rgb[i] = add(dv, mul(0.5f, rv));
+    }
+}
+
+__global__ void direction_kernel(const float* __restrict__ points,
+                                 const float* __restrict__ center, uint64_t count,
+                                 float* __restrict__ out) {
+    // precise_direction.cu:11-35
+    const float cx = center[0], cy = center[1], cz = center[2];
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        const float x = sub(points[3 * i], cx);
+        const float y = sub(points[3 * i + 1], cy);
+        const float z = sub(points[3 * i + 2], cz);
+        const float n = norm3_torch(x, y, z);
+        out[3 * i] = div(x, n);
+        out[3 * i + 1] = div(y, n);
+        out[3 * i + 2] = div(z, n);
+    }
+}
+
+__global__ void sh_to_rgb_kernel(const float* __restrict__ sh, const float* __restrict__ dirs,
+                                 uint64_t count, uint32_t coefficients, uint32_t degree,
+                                 float* __restrict__ out) {
+    // precise_sh.cu:11-138: every product and sum rounded in source order.
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        const float x = dirs[3 * i], y = dirs[3 * i + 1], z = dirs[3 * i + 2];
+        const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
+        const float xy = mul(x, y), yz = mul(y, z), xz = mul(x, z);
+        for (uint32_t ch = 0; ch < 3; ++ch) {
+            const float* c = sh + (i * 3 + ch) * coefficients;
+            float r = mul(0.28209479177387814f, c[0]);
+            if (degree > 0) {
+                const float c1 = 0.4886025119029199f;
+                r = sub(r, mul(mul(c1, y), c[1]));
+                r = add(r, mul(mul(c1, z), c[2]));
+                r = sub(r, mul(mul(c1, x), c[3]));
+            }
+            if (degree > 1) {
+                r = add(r, mul(mul(1.0925484305920792f, xy), c[4]));
+                r = add(r, mul(mul(-1.0925484305920792f, yz), c[5]));
+                const float p6 = sub(sub(mul(2.0f, zz), xx), yy);
+                r = add(r, mul(mul(0.31539156525252005f, p6), c[6]));
+                r = add(r, mul(mul(-1.0925484305920792f, xz), c[7]));
+                r = add(r, mul(mul(0.5462742152960396f, sub(xx, yy)), c[8]));
+            }
+            if (degree > 2) {
+                const float p9 = sub(mul(3.0f, xx), yy);
+                r = add(r, mul(mul(mul(-0.5900435899266435f, y), p9), c[9]));
+                r = add(r, mul(mul(mul(2.890611442640554f, xy), z), c[10]));
+                const float p11 = sub(sub(mul(4.0f, zz), xx), yy);
+                r = add(r, mul(mul(mul(-0.4570457994644658f, y), p11), c[11]));
+                const float p12 = sub(sub(mul(2.0f, zz), mul(3.0f, xx)), mul(3.0f, yy));
+                r = add(r, mul(mul(mul(0.3731763325901154f, z), p12), c[12]));
+                r = add(r, mul(mul(mul(-0.4570457994644658f, x), p11), c[13]));
+                r = add(r, mul(mul(mul(1.445305721320277f, z), sub(xx, yy)), c[14]));
+                const float p15 = sub(xx, mul(3.0f, yy));
+                r = add(r, mul(mul(mul(-0.5900435899266435f, x), p15), c[15]));
+            }
+            r = add(r, 0.5f);
+            out[3 * i + ch] = fmaxf(r, 0.0f);
+        }
+    }
+}
+
+__global__ void reflection_prefix_kernel(const float* __restrict__ rot, uint64_t count,
+                                         float* __restrict__ out) {
+    // precise_reflection_trace.cu:119-183: the matrix entries contract the
+    // leading product with the following add/sub (one fma each).
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        float w, x, y, z;
+        twice_normalized(rot + 4 * i, w, x, y, z);
+        const float wz = mul(w, z), wy = mul(w, y), wx = mul(w, x);
+        const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
+        float* o = out + 9 * i;
+        o[0] = sub(1.0f, mul(2.0f, fma(y, y, zz)));
+        o[1] = mul(2.0f, fma(x, y, sub(0.0f, wz)));
+        o[2] = mul(2.0f, fma(x, z, wy));
+        o[3] = mul(2.0f, fma(x, y, wz));
+        o[4] = sub(1.0f, mul(2.0f, fma(x, x, zz)));
+        o[5] = mul(2.0f, fma(y, z, sub(0.0f, wx)));
+        o[6] = mul(2.0f, fma(x, z, sub(0.0f, wy)));
+        o[7] = mul(2.0f, fma(y, z, wx));
+        o[8] = sub(1.0f, mul(2.0f, fma(x, x, yy)));
+    }
+}
+
+__global__ void disk_rotation_kernel(const float* __restrict__ rot, uint64_t count,
+                                     float* __restrict__ out) {
+    // precise_disk_rotation.cu:58-125: every stage rounded separately.
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        float w, x, y, z;
+        twice_normalized(rot + 4 * i, w, x, y, z);
+        const float xy = mul(x, y), xz = mul(x, z), yz = mul(y, z);
+        const float wz = mul(w, z), wy = mul(w, y), wx = mul(w, x);
+        const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
+        float* o = out + 9 * i;
+        o[0] = sub(1.0f, mul(2.0f, add(yy, zz)));
+        o[1] = mul(2.0f, sub(xy, wz));
+        o[2] = mul(2.0f, add(xz, wy));
+        o[3] = mul(2.0f, add(xy, wz));
+        o[4] = sub(1.0f, mul(2.0f, add(xx, zz)));
+        o[5] = mul(2.0f, sub(yz, wx));
+        o[6] = mul(2.0f, sub(xz, wy));
+        o[7] = mul(2.0f, add(yz, wx));
+        o[8] = sub(1.0f, mul(2.0f, add(xx, yy)));
+    }
+}
+
+// normalize with "+ eps" in the denominator (math_utils normalize).
+__device__ __forceinline__ float normalize3_add(float& x, float& y, float& z) {
+    const float den = add(norm3_torch(x, y, z), 1.0e-8f);
+    x = div(x, den);
+    y = div(y, den);
+    z = div(z, den);
+    return den;
+}
+
+__global__ void reflection_suffix_kernel(const float* __restrict__ xyz,
+                                         const float* __restrict__ center,
+                                         const float* __restrict__ normal_raw, uint64_t count,
+                                         float* __restrict__ out36) {
+    // precise_reflection_trace.cu:185-330
+    const float cx = center[0], cy = center[1], cz = center[2];
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        const float px = xyz[3 * i], py = xyz[3 * i + 1], pz = xyz[3 * i + 2];
+        float vx = sub(cx, px), vy = sub(cy, py), vz = sub(cz, pz);
+        normalize3_add(vx, vy, vz);
+        const float inx = normal_raw[3 * i], iny = normal_raw[3 * i + 1], inz = normal_raw[3 * i + 2];
+        // Facing flip against -(p - c), dot reduced as (x + z) + y.
+        const float tx = sub(0.0f, sub(px, cx));
+        const float ty = sub(0.0f, sub(py, cy));
+        const float tz = sub(0.0f, sub(pz, cz));
+        const float flip_dot = add(add(mul(inx, tx), mul(inz, tz)), mul(iny, ty));
+        const bool positive = flip_dot >= 0.0f;
+        const float sign = positive ? 1.0f : -1.0f;
+        const float nrx = mul(inx, sign), nry = mul(iny, sign), nrz = mul(inz, sign);
+        const float nn = norm3_torch(nrx, nry, nrz);
+        const float nden = nn < 1.0e-20f ? 1.0e-20f : nn;
+        const float nx = div(nrx, nden), ny = div(nry, nden), nz = div(nrz, nden);
+        const float rpx = mul(nx, vx), rpy = mul(ny, vy), rpz = mul(nz, vz);
+        const float dot_nv = add(add(rpx, rpz), rpy);
+        const float two_dot = mul(2.0f, dot_nv);
+        const float snx = mul(two_dot, nx), sny = mul(two_dot, ny), snz = mul(two_dot, nz);
+        const float rx = sub(snx, vx), ry = sub(sny, vy), rz = sub(snz, vz);
+        float dx = rx, dy = ry, dz = rz;
+        const float ray_den = normalize3_add(dx, dy, dz);
+        const float ox = mul(0.05f, dx), oy = mul(0.05f, dy), oz = mul(0.05f, dz);
+        float* o = out36 + 36 * i;
+        const float values[36] = {vx,  vy,  vz,  nx,  ny,  nz,  rx,  ry,  rz,
+                                  dx,  dy,  dz,  add(px, ox), add(py, oy), add(pz, oz),
+                                  positive ? 1.0f : 0.0f,
+                                  inx, iny, inz, nrx, nry, nrz, nden, rpx, rpy, rpz,
+                                  dot_nv, two_dot, snx, sny, snz, ray_den, ox, oy, oz,
+                                  flip_dot};
+#pragma unroll
+        for (int k = 0; k < 36; ++k) o[k] = values[k];
+    }
+}
+
+unsigned grid_for(uint64_t count) {
+    int device = 0, sms = 148;
+    if (cudaGetDevice(&device) == cudaSuccess) {
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    }
+    const uint64_t needed = (count + kThreads - 1) / kThreads;
+    const uint64_t cap = static_cast<uint64_t>(sms) * 8;
+    return static_cast<unsigned>(needed < cap ? (needed > 0 ? needed : 1) : cap);
+}
+
+}  // namespace
+
+cudaError_t sigmoid(const float* in, float* out, uint64_t count, cudaStream_t s) {
+    if (count == 0) return cudaSuccess;
+    sigmoid_kernel<<<grid_for(count), kThreads, 0, s>>>(in, out, count);
+    return cudaGetLastError();
+}
+
+cudaError_t normalize4(const float* in, float* out, uint64_t count, cudaStream_t s) {
+    if (count == 0) return cudaSuccess;
+    normalize4_kernel<<<grid_for(count), kThreads, 0, s>>>(in, out, count);
+    return cudaGetLastError();
+}
+
+cudaError_t fuse_maps(const float* base, const float* refl, const float* specular,
+                      float* diffuse, float* final_rgb, float* stored, uint64_t pixels,
+                      cudaStream_t s) {
+    if (pixels == 0) return cudaSuccess;
+    if (pixels > UINT64_MAX / 3) return cudaErrorInvalidValue;
+    fuse_maps_kernel<<<grid_for(pixels * 3), kThreads, 0, s>>>(base, refl, specular, diffuse,
+                                                                final_rgb, stored, pixels * 3);
+    return cudaGetLastError();
+}
+
+cudaError_t direction(const float* points, const float* center, uint64_t count, float* out,
+                      cudaStream_t s) {
+    if (count == 0) return cudaSuccess;
+    direction_kernel<<<grid_for(count), kThreads, 0, s>>>(points, center, count, out);
+    return cudaGetLastError();
+}
+
+cudaError_t sh_to_rgb(const float* sh, const float* dirs, uint64_t count, uint32_t coefficients,
+                      uint32_t degree, float* out, cudaStream_t s) {
+    if (count == 0) return cudaSuccess;
+    sh_to_rgb_kernel<<<grid_for(count), kThreads, 0, s>>>(sh, dirs, count, coefficients, degree,
+                                                           out);
+    return cudaGetLastError();
+}
+
+cudaError_t reflection_prefix(const float* rot, uint64_t count, float* out, cudaStream_t s) {
+    if (count == 0) return cudaSuccess;
+    reflection_prefix_kernel<<<grid_for(count), kThreads, 0, s>>>(rot, count, out);
+    return cudaGetLastError();
+}
+
+cudaError_t disk_rotation(const float* rot, uint64_t count, float* out, cudaStream_t s) {
+    if (count == 0) return cudaSuccess;
+    disk_rotation_kernel<<<grid_for(count), kThreads, 0, s>>>(rot, count, out);
+    return cudaGetLastError();
+}
+
+cudaError_t reflection_suffix(const float* xyz, const float* center, const float* normal_raw,
+                              uint64_t count, float* out36, cudaStream_t s) {
+    if (count == 0) return cudaSuccess;
+    reflection_suffix_kernel<<<grid_for(count), kThreads, 0, s>>>(xyz, center, normal_raw, count,
+                                                                   out36);
+    return cudaGetLastError();
+}
+
+}  // namespace precise
+}  // namespace hs

@@ -1,0 +1,31 @@
+// Launchers for the fixed-rounding elementwise kernels (precise.cu,
+// precise_exp.cu). All pointers are device pointers; count == 0 is a no-op.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace hs {
+namespace precise {
+
+cudaError_t exp(const float* in, float* out, uint64_t count, cudaStream_t s);
+cudaError_t sigmoid(const float* in, float* out, uint64_t count, cudaStream_t s);
+cudaError_t normalize4(const float* in, float* out, uint64_t count, cudaStream_t s);
+cudaError_t fuse_maps(const float* base, const float* refl, const float* specular, float* diffuse,
+                      float* final_rgb, float* stored, uint64_t pixels, cudaStream_t s);
+cudaError_t direction(const float* points, const float* center, uint64_t count, float* out,
+                      cudaStream_t s);
+cudaError_t sh_to_rgb(const float* sh, const float* dirs, uint64_t count, uint32_t coefficients,
+                      uint32_t degree, float* out, cudaStream_t s);
+cudaError_t reflection_prefix(const float* rot, uint64_t count, float* out, cudaStream_t s);
+cudaError_t reflection_suffix(const float* xyz, const float* center, const float* normal_raw,
+                              uint64_t count, float* out36, cudaStream_t s);
+cudaError_t disk_rotation(const float* rot, uint64_t count, float* out, cudaStream_t s);
+
+// Tiny kernels used around the cuBLAS / cuSOLVER camera helpers.
+cudaError_t negate9(const float* in, float* out, cudaStream_t s);
+cudaError_t column_to_row_major(const float* in, uint32_t dimension, float* out, cudaStream_t s);
+
+}  // namespace precise
+}  // namespace hs

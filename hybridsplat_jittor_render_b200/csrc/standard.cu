@@ -1,0 +1,211 @@
+// Standard five-channel 2DGS forward for sm_100a.
+//
+// Pipeline (reference full_rasterizer.cu:203-394):
+//   preprocess  one thread per Gaussian: near cull, 2DGS transform, facing
+//               flip, screen-space AABB and tile rectangle; writes an 80-byte
+//               blend record (centre, normal, opacity, 5 colours, Tu/Tv/Tw),
+//               the depth key, the rectangle and radii[P].
+//   depth sort  stable radix sort by the depth bits (ties keep index order).
+//   offsets     exclusive scan of rectangle areas in depth order; the total is
+//               `rendered` (read back once, like the reference's D2H copy at
+//               full_rasterizer.cu:309-320).
+//   emit        every tile of each rectangle, in depth order.
+//   tile sort   stable radix sort by tile id: the result is the reference's
+//               (tile|depth key, index) order (full_rasterizer.cu:127-153,
+//               345-355).
+//   ranges      per-tile [start, end).
+//   render      128 threads per 16x16 tile, 2 pixels per thread, per-pixel
+//               termination as in forward.cu:323-422; the per-Gaussian blend
+//               weights are summed across each warp before one atomicAdd.
+#include <algorithm>
+#include <climits>
+
+#include "context.h"
+
+// Rounding policy of the kernels: the pinned forms that reproduce the
+// reference build. Diagnostic builds may define this to a runtime table.
+#ifndef HS_STANDARD_ROUNDING
+#define HS_STANDARD_ROUNDING PinnedRounding
+#endif
+#include "sort.cuh"
+#include "standard_kernels.cuh"
+
+namespace hs {
+namespace st {
+namespace {
+
+uint64_t geometry_bytes(uint64_t count) {
+    Carver c(nullptr);
+    c.take<float4>(count * kRecordQuads);
+    c.take<uint2>(count);
+    for (int k = 0; k < 6; ++k) c.take<uint32_t>(count);
+    c.take<uint32_t>(64);
+    return c.offset;
+}
+
+struct GeometryViews {
+    float4* records;
+    uint2* rects;
+    uint32_t* keys;
+    uint32_t* order;
+    uint32_t* counts;
+    uint32_t* alt_keys;
+    uint32_t* alt_order;
+    uint32_t* offsets;
+    uint32_t* total;  // [0] pair total, [1] error flag
+};
+
+GeometryViews geometry_views(void* base, uint64_t count) {
+    Carver c(base);
+    GeometryViews v;
+    v.records = c.take<float4>(count * kRecordQuads);
+    v.rects = c.take<uint2>(count);
+    v.keys = c.take<uint32_t>(count);
+    v.order = c.take<uint32_t>(count);
+    v.counts = c.take<uint32_t>(count);
+    v.alt_keys = c.take<uint32_t>(count);
+    v.alt_order = c.take<uint32_t>(count);
+    v.offsets = c.take<uint32_t>(count);
+    v.total = c.take<uint32_t>(64);
+    return v;
+}
+
+uint64_t binning_bytes(uint64_t pairs) {
+    Carver c(nullptr);
+    for (int k = 0; k < 4; ++k) c.take<uint32_t>(pairs);
+    c.offset += sort::sort_scratch_bytes(static_cast<uint32_t>(pairs > 0 ? pairs : 1)) + 256;
+    return c.offset;
+}
+
+}  // namespace
+}  // namespace st
+
+uint64_t standard_current_bytes(const HsRasterizerContext* ctx) {
+    return ctx->std_geometry.bytes + ctx->std_binning.bytes + ctx->std_image.bytes;
+}
+
+// Returned when prefiltered is set and a Gaussian fails the near cull; the
+// reference traps the device in that case (auxiliary.h:218-224), this
+// library reports the violation instead.
+constexpr cudaError_t kPrefilteredViolation = cudaErrorInvalidValue;
+
+cudaError_t standard_release(HsRasterizerContext* ctx) {
+    cudaError_t first = cudaSuccess;
+    for (DeviceBuffer* b : {&ctx->std_geometry, &ctx->std_binning, &ctx->std_image}) {
+        const cudaError_t e = release_buffer(*b);
+        if (first == cudaSuccess) first = e;
+    }
+    if (ctx->std_total_host != nullptr) {
+        const cudaError_t e = cudaFreeHost(ctx->std_total_host);
+        if (first == cudaSuccess) first = e;
+        ctx->std_total_host = nullptr;
+    }
+    return first;
+}
+
+cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
+                             const float* background5, int32_t width, int32_t height,
+                             const float* means3d, const float* colors5, const float* opacities,
+                             const float* scales2, float scale_modifier, const float* rotations4,
+                             const float* viewmatrix4x4, const float* projmatrix4x4,
+                             const float* camera_position3, float tan_fovx, float tan_fovy,
+                             bool prefiltered, float* output_color5, float* output_aux7,
+                             float* output_weight, int32_t* output_radii,
+                             int32_t* output_rendered, cudaStream_t stream) {
+    using namespace st;
+    // Only the matrices drive the 2DGS projection; the camera position and
+    // field of view are accepted for ABI compatibility (the reference passes
+    // them through without using them when colours are precomputed).
+    (void)camera_position3;
+    (void)tan_fovx;
+    (void)tan_fovy;
+    const uint64_t pixels = static_cast<uint64_t>(width) * static_cast<uint64_t>(height);
+    if (point_count == 0) {
+        // zero_outputs (full_rasterizer.cu:178-199) and nothing else.
+        cudaError_t st = cudaMemsetAsync(output_color5, 0, 5 * pixels * sizeof(float), stream);
+        if (st == cudaSuccess) st = cudaMemsetAsync(output_aux7, 0, 7 * pixels * sizeof(float), stream);
+        if (st == cudaSuccess) st = cudaMemsetAsync(output_rendered, 0, sizeof(int32_t), stream);
+        return st;
+    }
+    const uint32_t grid_x = static_cast<uint32_t>((width + 15) / 16);
+    const uint32_t grid_y = static_cast<uint32_t>((height + 15) / 16);
+    const uint64_t tiles = static_cast<uint64_t>(grid_x) * grid_y;
+    const uint64_t count = static_cast<uint64_t>(point_count);
+
+    // Geometry: per-Gaussian views followed by the depth-sort / scan scratch.
+    const uint64_t geometry_used = geometry_bytes(count);
+    const uint64_t geometry_scratch_bytes =
+        std::max(sort::sort_scratch_bytes(point_count), sort::scan_scratch_bytes(point_count));
+    cudaError_t st = ensure_buffer(ctx->std_geometry, geometry_used + geometry_scratch_bytes,
+                                   &ctx->std_growth_count);
+    if (st != cudaSuccess) return st;
+    st = ensure_buffer(ctx->std_image, tiles * sizeof(uint2), &ctx->std_growth_count);
+    if (st != cudaSuccess) return st;
+    if (ctx->std_total_host == nullptr) {
+        st = cudaHostAlloc(reinterpret_cast<void**>(&ctx->std_total_host), 2 * sizeof(uint32_t),
+                           cudaHostAllocPortable);
+        if (st != cudaSuccess) return st;
+    }
+    ctx->std_peak_bytes = std::max(ctx->std_peak_bytes, standard_current_bytes(ctx));
+    const GeometryViews gv = geometry_views(ctx->std_geometry.ptr, count);
+    void* geometry_scratch = static_cast<unsigned char*>(ctx->std_geometry.ptr) + geometry_used;
+    uint2* ranges = static_cast<uint2*>(ctx->std_image.ptr);
+
+    st = cudaMemsetAsync(output_weight, 0, count * sizeof(float), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(gv.total, 0, 2 * sizeof(uint32_t), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(ranges, 0, tiles * sizeof(uint2), stream);
+    if (st != cudaSuccess) return st;
+    const int blocks = (point_count + kPreThreads - 1) / kPreThreads;
+    preprocess_kernel<HS_STANDARD_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
+        point_count, viewmatrix4x4, projmatrix4x4, width, height, grid_x, grid_y, means3d,
+        colors5, opacities, scales2, scale_modifier, rotations4, prefiltered ? 1 : 0, gv.records,
+        gv.rects, gv.keys, gv.order, gv.counts, output_radii, gv.total + 1);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+    st = sort::sort_pairs(gv.keys, gv.order, gv.alt_keys, gv.alt_order, point_count, 0, 32,
+                          geometry_scratch, stream);
+    if (st != cudaSuccess) return st;
+    st = sort::exclusive_scan(gv.counts, gv.order, gv.offsets, gv.total, point_count,
+                              geometry_scratch, stream);
+    if (st != cudaSuccess) return st;
+    st = cudaMemcpyAsync(ctx->std_total_host, gv.total, 2 * sizeof(uint32_t),
+                         cudaMemcpyDeviceToHost, stream);
+    if (st != cudaSuccess) return st;
+    st = cudaStreamSynchronize(stream);
+    if (st != cudaSuccess) return st;
+    const uint32_t rendered = ctx->std_total_host[0];
+    if (ctx->std_total_host[1] != 0) return kPrefilteredViolation;
+    if (rendered > static_cast<uint32_t>(INT_MAX)) return cudaErrorInvalidValue;
+    st = cudaMemcpyAsync(output_rendered, gv.total, sizeof(int32_t), cudaMemcpyDeviceToDevice,
+                         stream);
+    if (st != cudaSuccess) return st;
+
+    uint32_t* ids = nullptr;
+    if (rendered > 0) {
+        st = ensure_buffer(ctx->std_binning, binning_bytes(rendered), &ctx->std_growth_count);
+        if (st != cudaSuccess) return st;
+        ctx->std_peak_bytes = std::max(ctx->std_peak_bytes, standard_current_bytes(ctx));
+        Carver c(ctx->std_binning.ptr);
+        uint32_t* tile_ids = c.take<uint32_t>(rendered);
+        ids = c.take<uint32_t>(rendered);
+        uint32_t* alt_tiles = c.take<uint32_t>(rendered);
+        uint32_t* alt_ids = c.take<uint32_t>(rendered);
+        void* scratch = c.take<unsigned char>(sort::sort_scratch_bytes(rendered));
+        emit_kernel<<<blocks, kPreThreads, 0, stream>>>(point_count, grid_x, gv.order, gv.counts,
+                                                        gv.offsets, gv.rects, tile_ids, ids);
+        st = cudaGetLastError();
+        if (st != cudaSuccess) return st;
+        st = sort::sort_pairs(tile_ids, ids, alt_tiles, alt_ids, rendered, 0,
+                              sort::bits_for_tiles(static_cast<uint32_t>(tiles)), scratch, stream);
+        if (st != cudaSuccess) return st;
+        ranges_kernel<<<(rendered + 255) / 256, 256, 0, stream>>>(rendered, tile_ids, ranges);
+        st = cudaGetLastError();
+        if (st != cudaSuccess) return st;
+    }
+    render_kernel<HS_STANDARD_ROUNDING><<<static_cast<unsigned>(tiles), kRenderThreads, 0, stream>>>(
+        ranges, ids, gv.records, width, height, grid_x, background5, output_color5, output_aux7,
+        output_weight);
+    return cudaGetLastError();
+}
+
+}  // namespace hs

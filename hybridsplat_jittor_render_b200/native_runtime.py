@@ -1,0 +1,377 @@
+"""ctypes binding of the HybridSplat rasterizer C ABI.
+
+Mirrors the reference runtime ``jittor_hybridsplat/ops/native_runtime.py``
+(`load_native_library` :164-423, `NativeRendererContext` :515-705): the same
+struct layouts, ABI check (version 2), status handling and context methods.
+Device synchronisation uses ``torch.cuda`` instead of Jittor, since PyTorch
+owns device memory on this side of the boundary.
+
+`bind_library(path)` applies the ABI signatures to any library that exports
+them, so the same binding drives this package's sm_100a library and, in
+tests, the reference build used as the parity oracle.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+from typing import Any
+
+HS_STATUS_OK = 0
+HS_RASTERIZER_ABI_VERSION = 2
+_ERROR_CAPACITY = 4096
+_BUILD_INFO_CAPACITY = 8192
+
+PACKAGE_DIR = Path(__file__).resolve().parent
+LIBRARY_PATH = PACKAGE_DIR / "lib" / "libhybridsplat_rasterizer.so"
+
+
+class NativeRasterizerError(RuntimeError):
+    """Raised when a native entry point returns a non-OK HsStatus."""
+
+    def __init__(self, message: str, status: int = -1):
+        super().__init__(message)
+        self.status = status
+
+
+class _StatsBase(ctypes.Structure):
+    def as_dict(self) -> dict[str, int]:
+        return {name: int(getattr(self, name)) for name, _ in self._fields_}
+
+
+class WorkspaceStatsV1(_StatsBase):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("abi_version", ctypes.c_uint32),
+        ("device", ctypes.c_int32),
+        ("reserved", ctypes.c_uint32),
+        ("geometry_bytes", ctypes.c_uint64),
+        ("binning_bytes", ctypes.c_uint64),
+        ("image_bytes", ctypes.c_uint64),
+        ("current_bytes", ctypes.c_uint64),
+        ("peak_bytes", ctypes.c_uint64),
+        ("growth_count", ctypes.c_uint64),
+    ]
+
+
+class OptixWorkspaceStatsV1(_StatsBase):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("abi_version", ctypes.c_uint32),
+        ("device", ctypes.c_int32),
+        ("scene_ready", ctypes.c_uint32),
+        ("params_bytes", ctypes.c_uint64),
+        ("gas_output_bytes", ctypes.c_uint64),
+        ("gas_scratch_bytes", ctypes.c_uint64),
+        ("dist3_bytes", ctypes.c_uint64),
+        ("current_bytes", ctypes.c_uint64),
+        ("peak_bytes", ctypes.c_uint64),
+        ("growth_count", ctypes.c_uint64),
+        ("scene_signature", ctypes.c_uint64),
+        ("gas_build_count", ctypes.c_uint64),
+        ("pipeline_create_count", ctypes.c_uint64),
+    ]
+
+
+class MathWorkspaceStatsV2(_StatsBase):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("abi_version", ctypes.c_uint32),
+        ("device", ctypes.c_int32),
+        ("handles_ready", ctypes.c_uint32),
+        ("workspace_bytes", ctypes.c_uint64),
+        ("current_bytes", ctypes.c_uint64),
+        ("peak_bytes", ctypes.c_uint64),
+        ("growth_count", ctypes.c_uint64),
+        ("handle_create_count", ctypes.c_uint64),
+        ("camera_center_calls", ctypes.c_uint64),
+        ("general_inverse_calls", ctypes.c_uint64),
+        ("matmul_calls", ctypes.c_uint64),
+        ("pixel_world_calls", ctypes.c_uint64),
+    ]
+
+
+class FlashgsWorkspaceStatsV1(_StatsBase):
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("abi_version", ctypes.c_uint32),
+        ("device", ctypes.c_int32),
+        ("initialized", ctypes.c_uint32),
+        ("gaussian_capacity", ctypes.c_uint64),
+        ("pair_capacity", ctypes.c_uint64),
+        ("range_capacity", ctypes.c_uint64),
+        ("output_pixel_capacity", ctypes.c_uint64),
+        ("gaussian_bytes", ctypes.c_uint64),
+        ("pair_bytes", ctypes.c_uint64),
+        ("cub_bytes", ctypes.c_uint64),
+        ("ranges_bytes", ctypes.c_uint64),
+        ("output_bytes", ctypes.c_uint64),
+        ("current_bytes", ctypes.c_uint64),
+        ("peak_bytes", ctypes.c_uint64),
+        ("growth_count", ctypes.c_uint64),
+        ("overflow_retry_count", ctypes.c_uint64),
+        ("forward_calls", ctypes.c_uint64),
+        ("last_point_count", ctypes.c_uint64),
+        ("last_num_rendered", ctypes.c_uint64),
+        ("last_tile_count", ctypes.c_uint64),
+    ]
+
+
+_V = ctypes.c_void_p
+_U64 = ctypes.c_uint64
+_U32 = ctypes.c_uint32
+_I32 = ctypes.c_int32
+_F = ctypes.c_float
+_ERR = [ctypes.c_char_p, _U64]
+
+# Argument lists of every exported symbol (include/hybridsplat_rasterizer_c_api.h).
+# Device and host tensors are passed as raw addresses (c_void_p).
+SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
+    "hs_rasterizer_abi_version": (_U32, []),
+    "hs_rasterizer_build_info": (_I32, [ctypes.c_char_p, _U64]),
+    "hs_rasterizer_create": (_I32, [_I32, ctypes.POINTER(ctypes.c_void_p), *_ERR]),
+    "hs_rasterizer_synchronize": (_I32, [_V, *_ERR]),
+    "hs_rasterizer_workspace_stats": (_I32, [_V, ctypes.POINTER(WorkspaceStatsV1), *_ERR]),
+    "hs_rasterizer_release_workspace": (_I32, [_V, *_ERR]),
+    "hs_rasterizer_math_workspace_stats_v2": (_I32, [_V, ctypes.POINTER(MathWorkspaceStatsV2), *_ERR]),
+    "hs_rasterizer_destroy": (_I32, [_V, *_ERR]),
+    "hs_flashgs_forward_f32_v1": (
+        _I32,
+        [_V, _U64, _I32, _I32, _V, _V, _V, _I32, _V, _V, _V, _F, _V, _V, _V, _V, _V, _F, _F, _F,
+         _F, _V, _U64, _V, _V, _V, _V, _V, _V, _V, _V, *_ERR],
+    ),
+    "hs_flashgs_workspace_stats_v1": (_I32, [_V, ctypes.POINTER(FlashgsWorkspaceStatsV1), *_ERR]),
+    "hs_flashgs_prepare_npz_host_f32_v1": (_I32, [_U64, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, *_ERR]),
+    "hs_flashgs_debug_copy_v1": (_I32, [_V, _U64, _U64, _U64, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, _V, *_ERR]),
+    "hs_rasterizer_forward_f32_v1": (
+        _I32,
+        [_V, _U64, _V, _I32, _I32, _V, _V, _V, _V, _F, _V, _V, _V, _V, _F, _F, _I32, _V, _V, _V, _V,
+         _V, *_ERR],
+    ),
+    "hs_optix_build_scene_v1": (_I32, [_V, _V, _U64, _V, _U64, _U64, _I32, _V, *_ERR]),
+    "hs_optix_trace_f32_v1": (
+        _I32,
+        [_V, _U64, _V, _V, _V, _V, _V, _U32, _U32, _V, _V, _V, _F, _V, _V, _V, _V, _I32, _I32, _F,
+         _I32, _V, _V, _V, _V, _V, _V, _V, _V, *_ERR],
+    ),
+    "hs_optix_workspace_stats_v1": (_I32, [_V, ctypes.POINTER(OptixWorkspaceStatsV1), *_ERR]),
+    "hs_optix_release_scene_v1": (_I32, [_V, *_ERR]),
+    "hs_rasterizer_precise_exp_f32_v1": (_I32, [_V, _V, _U64, *_ERR]),
+    "hs_rasterizer_precise_sigmoid_f32_v1": (_I32, [_V, _V, _U64, *_ERR]),
+    "hs_rasterizer_precise_normalize4_f32_v1": (_I32, [_V, _V, _U64, *_ERR]),
+    "hs_rasterizer_precise_fuse_maps_f32_v1": (_I32, [_V, _V, _V, _V, _V, _V, _U64, *_ERR]),
+    "hs_rasterizer_precise_sh_to_rgb_f32_v1": (_I32, [_V, _V, _U64, _U32, _U32, _V, *_ERR]),
+    "hs_rasterizer_precise_direction_f32_v1": (_I32, [_V, _V, _U64, _V, *_ERR]),
+    "hs_rasterizer_precise_camera_center_f32_v2": (_I32, [_V, _V, _V, _V, *_ERR]),
+    "hs_rasterizer_precise_general_inverse_f32_v2": (_I32, [_V, _V, _U32, _V, *_ERR]),
+    "hs_rasterizer_precise_matmul_nt_n3k3_f32_v2": (_I32, [_V, _V, _V, _U64, _V, *_ERR]),
+    "hs_rasterizer_precise_pixel_world_f32_v2": (_I32, [_V, _V, _V, _U64, _V, *_ERR]),
+    "hs_rasterizer_precise_disk_rotation_f32_v1": (_I32, [_V, _U64, _V, *_ERR]),
+    "hs_rasterizer_precise_reflection_prefix_f32_v1": (_I32, [_V, _U64, _V, *_ERR]),
+    "hs_rasterizer_precise_reflection_suffix_f32_v1": (_I32, [_V, _V, _V, _U64, _V, *_ERR]),
+}
+
+# Entry points that the reference's OptiX-free oracle build does not export.
+OPTIX_SYMBOLS = {
+    "hs_optix_build_scene_v1",
+    "hs_optix_trace_f32_v1",
+    "hs_optix_workspace_stats_v1",
+    "hs_optix_release_scene_v1",
+}
+
+
+def error_buffer() -> ctypes.Array[ctypes.c_char]:
+    return ctypes.create_string_buffer(_ERROR_CAPACITY)
+
+
+def check_status(status: int, operation: str, error: ctypes.Array[ctypes.c_char]) -> None:
+    if status != HS_STATUS_OK:
+        detail = error.value.decode("utf-8", errors="replace")
+        raise NativeRasterizerError(f"{operation} failed with native status {status}: {detail}", status)
+
+
+def bind_library(path: Path | str, *, require_optix: bool = True) -> ctypes.CDLL:
+    """Loads a library exporting the C ABI and sets every signature.
+
+    Raises NativeRasterizerError if the file is missing, a symbol is absent
+    or the ABI version differs from 2.
+    """
+    path = Path(path)
+    if not path.is_file():
+        raise NativeRasterizerError(
+            f"native rasterizer library not found at {path}; build it with "
+            "`python -m hybridsplat_jittor_render_b200.build`"
+        )
+    library = ctypes.CDLL(str(path), mode=os.RTLD_LOCAL | os.RTLD_NOW)
+    for name, (restype, argtypes) in SIGNATURES.items():
+        if not require_optix and name in OPTIX_SYMBOLS:
+            continue
+        try:
+            function = getattr(library, name)
+        except AttributeError as exc:
+            raise NativeRasterizerError(f"{path} does not export {name}") from exc
+        function.restype = restype
+        function.argtypes = argtypes
+    version = int(library.hs_rasterizer_abi_version())
+    if version != HS_RASTERIZER_ABI_VERSION:
+        raise NativeRasterizerError(
+            f"{path} has ABI version {version}, expected {HS_RASTERIZER_ABI_VERSION}"
+        )
+    return library
+
+
+_LIBRARY: ctypes.CDLL | None = None
+_LOAD_LOCK = threading.Lock()
+
+
+def load_native_library() -> ctypes.CDLL:
+    """The sm_100a library of this package (loaded once, never a fallback)."""
+    global _LIBRARY
+    with _LOAD_LOCK:
+        if _LIBRARY is None:
+            _LIBRARY = bind_library(LIBRARY_PATH)
+        return _LIBRARY
+
+
+def _torch_synchronize(device: int) -> None:
+    try:
+        import torch
+    except ImportError:  # pragma: no cover - torch is a hard dependency on GPU hosts
+        return
+    if torch.cuda.is_available():
+        torch.cuda.synchronize(device)
+
+
+class NativeRendererContext:
+    """Owns one native context (HsRasterizerHandle) on one CUDA device.
+
+    Same surface as the reference NativeRendererContext
+    (native_runtime.py:515-705). `library` selects the shared library; the
+    default is this package's sm_100a build.
+    """
+
+    def __init__(self, device: int = 0, *, library: ctypes.CDLL | None = None):
+        self._library = library if library is not None else load_native_library()
+        self._device = int(device)
+        self._handle = ctypes.c_void_p()
+        error = error_buffer()
+        status = self._library.hs_rasterizer_create(self._device, ctypes.byref(self._handle), error, len(error))
+        check_status(status, "hs_rasterizer_create", error)
+
+    @property
+    def library(self) -> ctypes.CDLL:
+        return self._library
+
+    @property
+    def device(self) -> int:
+        return self._device
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if self._handle.value is None:
+            raise NativeRasterizerError("native rasterizer context is closed")
+        return self._handle
+
+    @property
+    def handle_value(self) -> int:
+        return int(self.handle.value)
+
+    @property
+    def build_info(self) -> str:
+        output = ctypes.create_string_buffer(_BUILD_INFO_CAPACITY)
+        status = self._library.hs_rasterizer_build_info(output, len(output))
+        check_status(status, "hs_rasterizer_build_info", output)
+        return output.value.decode("utf-8")
+
+    def synchronize(self) -> None:
+        _torch_synchronize(self._device)
+        error = error_buffer()
+        status = self._library.hs_rasterizer_synchronize(self.handle, error, len(error))
+        check_status(status, "hs_rasterizer_synchronize", error)
+
+    def _stats(self, symbol: str, struct_type: type[_StatsBase]) -> dict[str, int]:
+        stats = struct_type()
+        stats.struct_size = ctypes.sizeof(struct_type)
+        stats.abi_version = HS_RASTERIZER_ABI_VERSION
+        error = error_buffer()
+        status = getattr(self._library, symbol)(self.handle, ctypes.byref(stats), error, len(error))
+        check_status(status, symbol, error)
+        return stats.as_dict()
+
+    def workspace_stats(self) -> dict[str, int]:
+        return self._stats("hs_rasterizer_workspace_stats", WorkspaceStatsV1)
+
+    def math_workspace_stats(self) -> dict[str, int]:
+        return self._stats("hs_rasterizer_math_workspace_stats_v2", MathWorkspaceStatsV2)
+
+    def optix_workspace_stats(self) -> dict[str, int]:
+        return self._stats("hs_optix_workspace_stats_v1", OptixWorkspaceStatsV1)
+
+    def flashgs_workspace_stats(self) -> dict[str, int]:
+        return self._stats("hs_flashgs_workspace_stats_v1", FlashgsWorkspaceStatsV1)
+
+    def release_workspace(self) -> None:
+        _torch_synchronize(self._device)
+        error = error_buffer()
+        status = self._library.hs_rasterizer_release_workspace(self.handle, error, len(error))
+        check_status(status, "hs_rasterizer_release_workspace", error)
+
+    def release_optix_scene(self) -> None:
+        error = error_buffer()
+        status = self._library.hs_optix_release_scene_v1(self.handle, error, len(error))
+        check_status(status, "hs_optix_release_scene_v1", error)
+
+    def flashgs_debug_snapshot(self) -> dict[str, Any]:
+        """Host copies of the last FlashGS preprocess, sorted pairs and ranges."""
+        import numpy as np
+
+        _torch_synchronize(self._device)
+        stats = self.flashgs_workspace_stats()
+        points, pairs, tiles = stats["last_point_count"], stats["last_num_rendered"], stats["last_tile_count"]
+        arrays = {
+            "points_xy": np.empty((points, 2), np.float32),
+            "rgb": np.empty((points, 3), np.float32),
+            "other_features": np.empty((points, 2), np.float32),
+            "conic_opacity": np.empty((points, 4), np.float32),
+            "normal_opacity": np.empty((points, 4), np.float32),
+            "Tu": np.empty((points, 3), np.float32),
+            "Tv": np.empty((points, 3), np.float32),
+            "Tw": np.empty((points, 3), np.float32),
+            "sorted_keys": np.empty(pairs, np.uint64),
+            "sorted_values": np.empty(pairs, np.uint32),
+            "tile_ranges": np.empty((tiles, 2), np.int32),
+        }
+        error = error_buffer()
+        names = ("points_xy", "rgb", "other_features", "conic_opacity", "normal_opacity", "Tu", "Tv", "Tw",
+                 "sorted_keys", "sorted_values", "tile_ranges")
+        status = self._library.hs_flashgs_debug_copy_v1(
+            self.handle, points, pairs, tiles, *[arrays[n].ctypes.data for n in names], error, len(error)
+        )
+        check_status(status, "hs_flashgs_debug_copy_v1", error)
+        return arrays
+
+    def close(self) -> None:
+        if self._handle.value is None:
+            return
+        _torch_synchronize(self._device)
+        error = error_buffer()
+        status = self._library.hs_rasterizer_destroy(self._handle, error, len(error))
+        check_status(status, "hs_rasterizer_destroy", error)
+        self._handle = ctypes.c_void_p()
+
+    def __enter__(self) -> "NativeRendererContext":
+        return self
+
+    def __exit__(self, *exc: Any) -> None:
+        self.close()
+
+    def __del__(self) -> None:  # pragma: no cover - best effort at interpreter exit
+        try:
+            if self._handle.value is not None:
+                error = error_buffer()
+                self._library.hs_rasterizer_destroy(self._handle, error, len(error))
+                self._handle = ctypes.c_void_p()
+        except Exception:
+            pass

@@ -1,0 +1,344 @@
+"""Tensor-level operators over the C ABI (the Jittor op layer's counterpart).
+
+Names, argument order and validation follow the reference operators:
+``flashgs_forward`` (jittor_hybridsplat/ops/flashgs.py:54-136),
+``rasterize_forward`` (ops/rasterizer.py:40-97) and the precise_* helpers
+(ops/precise_*.py). Inputs are contiguous float32 CUDA ``torch.Tensor``s on
+the context's device; outputs are newly allocated tensors with the
+reference's shapes. Every call goes to the native library; there is no
+fallback implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from collections.abc import Sequence
+from typing import Any, NamedTuple
+
+import torch
+
+from .native_runtime import (
+    NativeRendererContext,
+    check_status,
+    error_buffer,
+    load_native_library,
+)
+
+
+class FlashgsOutputs(NamedTuple):
+    color: torch.Tensor
+    other: torch.Tensor
+    depth: torch.Tensor
+    alpha: torch.Tensor
+    normal: torch.Tensor
+    median_depth: torch.Tensor
+    distortion: torch.Tensor
+    rendered: torch.Tensor
+
+
+class RasterizerOutputs(NamedTuple):
+    color: torch.Tensor
+    auxiliary: torch.Tensor
+    weight: torch.Tensor
+    radii: torch.Tensor
+    rendered: torch.Tensor
+
+
+def _check_tensor(name: str, value: torch.Tensor, shape: tuple[int, ...], dtype=torch.float32) -> None:
+    if not isinstance(value, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if tuple(value.shape) != shape:
+        raise ValueError(f"{name} must have shape {shape}, got {tuple(value.shape)}")
+    if value.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {value.dtype}")
+    if not value.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _finite(name: str, value: float, *, positive: bool = False) -> float:
+    if isinstance(value, bool) or not isinstance(value, (int, float)):
+        raise TypeError(f"{name} must be a CPU real scalar")
+    result = float(value)
+    if not math.isfinite(result) or (positive and result <= 0.0):
+        raise ValueError(f"{name} must be {'finite and positive' if positive else 'finite'}")
+    return result
+
+
+def _vector(name: str, value: Sequence[float], count: int) -> tuple[float, ...]:
+    if isinstance(value, torch.Tensor):
+        value = value.detach().reshape(-1).cpu().tolist()
+    flat: list[Any] = []
+    for item in value:
+        if isinstance(item, Sequence) and not isinstance(item, (str, bytes)):
+            flat.extend(item)
+        else:
+            flat.append(item)
+    if len(flat) != count:
+        raise ValueError(f"{name} must contain {count} values")
+    return tuple(_finite(f"{name}[{i}]", v) for i, v in enumerate(flat))
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def flashgs_forward(
+    positions: torch.Tensor,
+    shs: torch.Tensor,
+    colors: torch.Tensor,
+    opacities: torch.Tensor,
+    covariance: torch.Tensor,
+    scales: torch.Tensor,
+    rotations: torch.Tensor,
+    specular: torch.Tensor,
+    roughness: torch.Tensor,
+    *,
+    width: int,
+    height: int,
+    use_sh: bool,
+    camera_position: Sequence[float],
+    camera_rotation: Sequence[float],
+    focal_x: float,
+    focal_y: float,
+    z_far: float = 100.0,
+    z_near: float = 0.01,
+    background: Sequence[float] = (0.0, 0.0, 0.0),
+    scale_modifier: float = 1.0,
+    initial_pair_capacity: int = 1 << 20,
+    context: NativeRendererContext,
+    out: FlashgsOutputs | None = None,
+) -> FlashgsOutputs:
+    """Deterministic FlashGS 16x16 forward; outputs are channel-first maps."""
+    if isinstance(width, bool) or not isinstance(width, int) or width <= 0:
+        raise ValueError("width must be a positive CPU integer")
+    if isinstance(height, bool) or not isinstance(height, int) or height <= 0:
+        raise ValueError("height must be a positive CPU integer")
+    if not isinstance(use_sh, bool):
+        raise TypeError("use_sh must be bool")
+    if isinstance(initial_pair_capacity, bool) or not isinstance(initial_pair_capacity, int) or initial_pair_capacity <= 0:
+        raise ValueError("initial_pair_capacity must be a positive CPU integer")
+    count = int(positions.shape[0])
+    for name, value, shape in (
+        ("positions", positions, (count, 3)),
+        ("shs", shs, (count, 48)),
+        ("colors", colors, (count, 3)),
+        ("opacities", opacities, (count, 1)),
+        ("covariance", covariance, (count, 6)),
+        ("scales", scales, (count, 2)),
+        ("rotations", rotations, (count, 4)),
+        ("specular", specular, (count, 1)),
+        ("roughness", roughness, (count, 1)),
+    ):
+        _check_tensor(name, value, shape)
+    position = _vector("camera_position", camera_position, 3)
+    rotation = _vector("camera_rotation", camera_rotation, 9)
+    bg = _vector("background", background, 3)
+    scale = _finite("scale_modifier", scale_modifier, positive=True)
+    fx = _finite("focal_x", focal_x, positive=True)
+    fy = _finite("focal_y", focal_y, positive=True)
+    far = _finite("z_far", z_far, positive=True)
+    near = _finite("z_near", z_near, positive=True)
+    if far <= near:
+        raise ValueError("z_far must be greater than z_near")
+    device = positions.device
+    if out is None:
+        f = dict(dtype=torch.float32, device=device)
+        out = FlashgsOutputs(
+            torch.empty((3, height, width), **f),
+            torch.empty((2, height, width), **f),
+            torch.empty((1, height, width), **f),
+            torch.empty((1, height, width), **f),
+            torch.empty((3, height, width), **f),
+            torch.empty((1, height, width), **f),
+            torch.empty((1, height, width), **f),
+            torch.empty((1,), dtype=torch.int32, device=device),
+        )
+    position_host = (ctypes.c_float * 3)(*position)
+    rotation_host = (ctypes.c_float * 9)(*rotation)
+    bg_host = (ctypes.c_float * 3)(*bg)
+    error = error_buffer()
+    status = context.library.hs_flashgs_forward_f32_v1(
+        context.handle, count, width, height,
+        _ptr(positions), _ptr(shs), _ptr(colors), int(use_sh), _ptr(opacities), _ptr(covariance),
+        _ptr(scales), scale, _ptr(rotations), _ptr(specular), _ptr(roughness),
+        ctypes.addressof(position_host), ctypes.addressof(rotation_host), fx, fy, far, near,
+        ctypes.addressof(bg_host), initial_pair_capacity,
+        *[t.data_ptr() for t in out], error, len(error),
+    )
+    check_status(status, "hs_flashgs_forward_f32_v1", error)
+    return out
+
+
+def rasterize_forward(
+    background: torch.Tensor,
+    means3d: torch.Tensor,
+    colors: torch.Tensor,
+    opacities: torch.Tensor,
+    scales: torch.Tensor,
+    rotations: torch.Tensor,
+    viewmatrix: torch.Tensor,
+    projmatrix: torch.Tensor,
+    camera_position: torch.Tensor,
+    *,
+    width: int,
+    height: int,
+    scale_modifier: float,
+    tan_fovx: float,
+    tan_fovy: float,
+    prefiltered: bool = False,
+    context: NativeRendererContext,
+    out: RasterizerOutputs | None = None,
+) -> RasterizerOutputs:
+    """Standard five-channel 2DGS forward (color[5,H,W], aux[7,H,W], ...)."""
+    if isinstance(width, bool) or not isinstance(width, int) or width <= 0:
+        raise ValueError("width must be a positive CPU integer")
+    if isinstance(height, bool) or not isinstance(height, int) or height <= 0:
+        raise ValueError("height must be a positive CPU integer")
+    if not isinstance(prefiltered, bool):
+        raise TypeError("prefiltered must be bool")
+    count = int(means3d.shape[0])
+    for name, value, shape in (
+        ("background", background, (5,)),
+        ("means3d", means3d, (count, 3)),
+        ("colors", colors, (count, 5)),
+        ("opacities", opacities, (count, 1)),
+        ("scales", scales, (count, 2)),
+        ("rotations", rotations, (count, 4)),
+        ("viewmatrix", viewmatrix, (4, 4)),
+        ("projmatrix", projmatrix, (4, 4)),
+        ("camera_position", camera_position, (3,)),
+    ):
+        _check_tensor(name, value, shape)
+    scale = _finite("scale_modifier", scale_modifier, positive=True)
+    fovx = _finite("tan_fovx", tan_fovx, positive=True)
+    fovy = _finite("tan_fovy", tan_fovy, positive=True)
+    device = means3d.device
+    if out is None:
+        f = dict(dtype=torch.float32, device=device)
+        out = RasterizerOutputs(
+            torch.empty((5, height, width), **f),
+            torch.empty((7, height, width), **f),
+            torch.empty((count, 1), **f),
+            torch.empty((count,), dtype=torch.int32, device=device),
+            torch.empty((1,), dtype=torch.int32, device=device),
+        )
+    error = error_buffer()
+    status = context.library.hs_rasterizer_forward_f32_v1(
+        context.handle, count, _ptr(background), width, height, _ptr(means3d), _ptr(colors),
+        _ptr(opacities), _ptr(scales), scale, _ptr(rotations), _ptr(viewmatrix), _ptr(projmatrix),
+        _ptr(camera_position), fovx, fovy, int(prefiltered),
+        *[t.data_ptr() for t in out], error, len(error),
+    )
+    check_status(status, "hs_rasterizer_forward_f32_v1", error)
+    return out
+
+
+def flashgs_prepare_host(
+    opacity_raw, scaling_raw, rotation_raw, specular_raw, roughness_raw, *, library: ctypes.CDLL | None = None
+) -> dict[str, Any]:
+    """Host FlashGS activation of raw NPZ arrays (numpy float32 in and out)."""
+    import numpy as np
+
+    lib = library if library is not None else load_native_library()
+    arrays = [np.ascontiguousarray(a, dtype=np.float32) for a in
+              (opacity_raw, scaling_raw, rotation_raw, specular_raw, roughness_raw)]
+    count = int(arrays[0].shape[0])
+    shapes = [(count, 1), (count, 2), (count, 4), (count, 1), (count, 1)]
+    for a, shape in zip(arrays, shapes):
+        if a.shape != shape:
+            raise ValueError(f"expected shape {shape}, got {a.shape}")
+    out = {
+        "opacity": np.empty((count, 1), np.float32),
+        "scaling": np.empty((count, 2), np.float32),
+        "rotation": np.empty((count, 4), np.float32),
+        "covariance": np.empty((count, 6), np.float32),
+        "specular": np.empty((count, 1), np.float32),
+        "roughness": np.empty((count, 1), np.float32),
+    }
+    error = error_buffer()
+    status = lib.hs_flashgs_prepare_npz_host_f32_v1(
+        count, *[a.ctypes.data for a in arrays], *[v.ctypes.data for v in out.values()], error, len(error)
+    )
+    check_status(status, "hs_flashgs_prepare_npz_host_f32_v1", error)
+    return out
+
+
+def _elementwise(symbol: str, library: ctypes.CDLL | None, *args: Any) -> None:
+    lib = library if library is not None else load_native_library()
+    error = error_buffer()
+    status = getattr(lib, symbol)(*args, error, len(error))
+    check_status(status, symbol, error)
+
+
+def precise_exp(x: torch.Tensor, *, library: ctypes.CDLL | None = None) -> torch.Tensor:
+    out = torch.empty_like(x)
+    _elementwise("hs_rasterizer_precise_exp_f32_v1", library, _ptr(x), _ptr(out), x.numel())
+    return out
+
+
+def precise_sigmoid(x: torch.Tensor, *, library: ctypes.CDLL | None = None) -> torch.Tensor:
+    out = torch.empty_like(x)
+    _elementwise("hs_rasterizer_precise_sigmoid_f32_v1", library, _ptr(x), _ptr(out), x.numel())
+    return out
+
+
+def precise_normalize4(x: torch.Tensor, *, library: ctypes.CDLL | None = None) -> torch.Tensor:
+    _check_tensor("input", x, (int(x.shape[0]), 4))
+    out = torch.empty_like(x)
+    _elementwise("hs_rasterizer_precise_normalize4_f32_v1", library, _ptr(x), _ptr(out), x.shape[0])
+    return out
+
+
+def precise_fuse_maps(base_rgb: torch.Tensor, reflection_rgb: torch.Tensor, specular: torch.Tensor, *,
+                      library: ctypes.CDLL | None = None) -> dict[str, torch.Tensor]:
+    """dif = base*(1-s), ref = (refl*s)*2, rgb = dif + 0.5*ref (math.py:301-311)."""
+    pixels = base_rgb.numel() // 3
+    diffuse = torch.empty_like(base_rgb)
+    final = torch.empty_like(base_rgb)
+    stored = torch.empty_like(base_rgb)
+    _elementwise("hs_rasterizer_precise_fuse_maps_f32_v1", library, _ptr(base_rgb), _ptr(reflection_rgb),
+                 _ptr(specular), _ptr(diffuse), _ptr(final), _ptr(stored), pixels)
+    return {"rgb_map": final, "dif_rgb_map": diffuse, "ref_rgb_map": stored}
+
+
+def precise_sh_to_rgb(sh: torch.Tensor, directions: torch.Tensor, degree: int, *,
+                      library: ctypes.CDLL | None = None) -> torch.Tensor:
+    """sh is [P,3,C] (channel-major), directions [P,3]; returns [P,3]."""
+    sh = sh.contiguous()
+    count = int(directions.shape[0])
+    out = torch.empty((count, 3), dtype=torch.float32, device=directions.device)
+    _elementwise("hs_rasterizer_precise_sh_to_rgb_f32_v1", library, _ptr(sh), _ptr(directions), count,
+                 int(sh.shape[-1]), int(degree), _ptr(out))
+    return out
+
+
+def precise_direction(points: torch.Tensor, center: torch.Tensor, *,
+                      library: ctypes.CDLL | None = None) -> torch.Tensor:
+    out = torch.empty_like(points)
+    _elementwise("hs_rasterizer_precise_direction_f32_v1", library, _ptr(points), _ptr(center),
+                 points.shape[0], _ptr(out))
+    return out
+
+
+def precise_reflection_prefix(rotation_wxyz: torch.Tensor, *, library: ctypes.CDLL | None = None) -> torch.Tensor:
+    count = int(rotation_wxyz.shape[0])
+    out = torch.empty((count, 3, 3), dtype=torch.float32, device=rotation_wxyz.device)
+    _elementwise("hs_rasterizer_precise_reflection_prefix_f32_v1", library, _ptr(rotation_wxyz), count, _ptr(out))
+    return out
+
+
+def precise_reflection_suffix(xyz: torch.Tensor, camera_center: torch.Tensor, normal_raw: torch.Tensor, *,
+                              library: ctypes.CDLL | None = None) -> torch.Tensor:
+    count = int(xyz.shape[0])
+    out = torch.empty((count, 36), dtype=torch.float32, device=xyz.device)
+    _elementwise("hs_rasterizer_precise_reflection_suffix_f32_v1", library, _ptr(xyz), _ptr(camera_center),
+                 _ptr(normal_raw), count, _ptr(out))
+    return out
+
+
+def precise_disk_rotation(rotation_wxyz: torch.Tensor, *, library: ctypes.CDLL | None = None) -> torch.Tensor:
+    count = int(rotation_wxyz.shape[0])
+    out = torch.empty((count, 3, 3), dtype=torch.float32, device=rotation_wxyz.device)
+    _elementwise("hs_rasterizer_precise_disk_rotation_f32_v1", library, _ptr(rotation_wxyz), count, _ptr(out))
+    return out
