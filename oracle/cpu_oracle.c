@@ -340,7 +340,9 @@ static float encode_bg(float v) {
  * rec24 is non-NULL it receives the per-Gaussian debug state in the layout
  * xy2, normal_opacity4, rgb3, other2, tu3, tv3, tw3, conic_opacity4.
  * keys/values receive the sorted pairs when non-NULL and *pairs fits.
- * Returns the pair count, or -1 on allocation failure.
+ * Only tile rows with ty % row_stride == 0 are binned and rendered (1 =
+ * the whole frame; larger strides give a bounded sample for CPU timing).
+ * Returns the number of pairs emitted, or -1 on allocation failure.
  */
 API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const float* shs,
                                    const float* colors, int use_sh, const float* opac,
@@ -351,7 +353,8 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
                                    float* out_other, float* out_depth, float* out_alpha,
                                    float* out_normal, float* out_median, float* out_dist,
                                    float* rec24, uint64_t* keys, uint32_t* values,
-                                   int64_t pair_capacity, int32_t* ranges_out, int threads) {
+                                   int64_t pair_capacity, int32_t* ranges_out, int threads,
+                                   int row_stride) {
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);
 #else
@@ -397,6 +400,7 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
             }
         }
     }
+    if (row_stride < 1) row_stride = 1;
     int64_t total = 0;
     for (int i = 0; i < P; ++i) total += gs[i].hits;
     Pair* pairs = (Pair*)malloc((size_t)(total > 0 ? total : 1) * sizeof(Pair));
@@ -413,12 +417,13 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
         memcpy(&depth_bits, &g->depth, 4);
         for (int y = g->rmin[1]; y < g->rmax[1]; ++y)
             for (int x = g->rmin[0]; x < g->rmax[0]; ++x)
-                if (tile_hit(x, y, g->xy, g->conic, g->power)) {
+                if (y % row_stride == 0 && tile_hit(x, y, g->xy, g->conic, g->power)) {
                     pairs[at].key = ((uint64_t)(y * gx + x) << 32) | depth_bits;
                     pairs[at].value = (uint32_t)i;
                     ++at;
                 }
     }
+    total = at;
     qsort(pairs, (size_t)total, sizeof(Pair), pair_less);
     int32_t* ranges = (int32_t*)calloc((size_t)tiles * 2, sizeof(int32_t));
     for (int64_t i = 0; i < total; ++i) {
@@ -444,6 +449,7 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
 #pragma omp parallel for schedule(dynamic, 1)
     for (int tile = 0; tile < tiles; ++tile) {
         const int tx = tile % gx, ty = tile / gx;
+        if (ty % row_stride != 0) continue;
         const int start = ranges[2 * tile], end = ranges[2 * tile + 1];
         FgPixel px[256];
         for (int k = 0; k < 256; ++k) {
@@ -604,12 +610,14 @@ static float st_blend(StPixel* s, float px, float py, const float* g) {
 }
 
 /* Full standard forward (full_rasterizer.cu:203-394); matrices column-major
- * as stored by the caller. Returns the pair count or -1. */
+ * as stored by the caller. row_stride samples tile rows as in
+ * oracle_flashgs_forward. Returns the full-frame pair count or -1. */
 API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const float* means,
                                     const float* colors5, const float* opac, const float* scales,
                                     float mod, const float* rot, const float* view,
                                     const float* proj, float* out_color5, float* out_aux7,
-                                    float* out_weight, int32_t* out_radii, int threads) {
+                                    float* out_weight, int32_t* out_radii, int threads,
+                                    int row_stride) {
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);
 #else
@@ -630,6 +638,7 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
         out_radii[i] = gs[i].valid ? gs[i].radius : 0;
         out_weight[i] = 0.0f;
     }
+    if (row_stride < 1) row_stride = 1;
     int64_t total = 0;
     for (int i = 0; i < P; ++i)
         if (gs[i].valid) total += (int64_t)(gs[i].rmax[0] - gs[i].rmin[0]) * (gs[i].rmax[1] - gs[i].rmin[1]);
@@ -643,13 +652,17 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
         if (!gs[i].valid) continue;
         uint32_t depth_bits;
         memcpy(&depth_bits, &gs[i].depth, 4);
-        for (int y = gs[i].rmin[1]; y < gs[i].rmax[1]; ++y)
+        for (int y = gs[i].rmin[1]; y < gs[i].rmax[1]; ++y) {
+            if (y % row_stride != 0) continue;
             for (int x = gs[i].rmin[0]; x < gs[i].rmax[0]; ++x) {
                 pairs[at].key = ((uint64_t)(y * gx + x) << 32) | depth_bits;
                 pairs[at].value = (uint32_t)i;
                 ++at;
             }
+        }
     }
+    const int64_t all_pairs = total;
+    total = at;
     qsort(pairs, (size_t)total, sizeof(Pair), pair_less);
     int64_t* ranges = (int64_t*)calloc((size_t)tiles * 2, sizeof(int64_t));
     for (int64_t i = 0; i < total; ++i) {
@@ -667,6 +680,7 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
 #pragma omp parallel for schedule(dynamic, 1)
     for (int tile = 0; tile < tiles; ++tile) {
         const int tx = tile % gx, ty = tile / gx;
+        if (ty % row_stride != 0) continue;
         StPixel px[256];
         for (int k = 0; k < 256; ++k) {
             memset(&px[k], 0, sizeof(StPixel));
@@ -702,5 +716,5 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
     free(ranges);
     free(pairs);
     free(gs);
-    return total;
+    return all_pairs;
 }
