@@ -31,9 +31,16 @@
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 #ifdef _OPENMP
 #include <omp.h>
 #endif
+
+static double now_ms(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return ts.tv_sec * 1e3 + ts.tv_nsec * 1e-6;
+}
 
 #define API __attribute__((visibility("default")))
 
@@ -342,6 +349,9 @@ static float encode_bg(float v) {
  * keys/values receive the sorted pairs when non-NULL and *pairs fits.
  * Only tile rows with ty % row_stride == 0 are binned and rendered (1 =
  * the whole frame; larger strides give a bounded sample for CPU timing).
+ * stage_ms, when non-NULL, receives 4 doubles: the wall times (ms) of
+ * preprocess, binning (pair emission, sort, ranges) and blending, and the
+ * number of pixel x Gaussian blend evaluations.
  * Returns the number of pairs emitted, or -1 on allocation failure.
  */
 API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const float* shs,
@@ -354,7 +364,8 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
                                    float* out_normal, float* out_median, float* out_dist,
                                    float* rec24, uint64_t* keys, uint32_t* values,
                                    int64_t pair_capacity, int32_t* ranges_out, int threads,
-                                   int row_stride) {
+                                   int row_stride, double* stage_ms) {
+    const double t0 = now_ms();
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);
 #else
@@ -401,6 +412,7 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
         }
     }
     if (row_stride < 1) row_stride = 1;
+    const double t1 = now_ms();
     int64_t total = 0;
     for (int i = 0; i < P; ++i) total += gs[i].hits;
     Pair* pairs = (Pair*)malloc((size_t)(total > 0 ? total : 1) * sizeof(Pair));
@@ -445,8 +457,10 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
         }
     }
     if (ranges_out != NULL) memcpy(ranges_out, ranges, (size_t)tiles * 2 * sizeof(int32_t));
+    const double t2 = now_ms();
     const size_t plane = (size_t)W * H;
-#pragma omp parallel for schedule(dynamic, 1)
+    int64_t evaluations = 0;
+#pragma omp parallel for schedule(dynamic, 1) reduction(+ : evaluations)
     for (int tile = 0; tile < tiles; ++tile) {
         const int tx = tile % gx, ty = tile / gx;
         if (ty % row_stride != 0) continue;
@@ -462,6 +476,7 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
              * (render.cu:499-698). */
             for (int j = start; j < end; ++j) {
                 const float* g = rec + 20 * (size_t)pairs[j].value;
+                evaluations += 256;
                 int done = 1;
                 for (int k = 0; k < 256; ++k) {
                     fg_blend(&px[k], (float)(tx * 16 + (k & 15)), (float)(ty * 16 + (k >> 4)), g);
@@ -499,6 +514,12 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
             out_median[pid] = s->median;
             out_dist[pid] = s->dist;
         }
+    }
+    if (stage_ms != NULL) {
+        stage_ms[0] = t1 - t0;
+        stage_ms[1] = t2 - t1;
+        stage_ms[2] = now_ms() - t2;
+        stage_ms[3] = (double)evaluations;
     }
     free(ranges);
     free(pairs);
@@ -617,7 +638,8 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
                                     float mod, const float* rot, const float* view,
                                     const float* proj, float* out_color5, float* out_aux7,
                                     float* out_weight, int32_t* out_radii, int threads,
-                                    int row_stride) {
+                                    int row_stride, double* stage_ms) {
+    const double t0 = now_ms();
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);
 #else
@@ -639,6 +661,7 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
         out_weight[i] = 0.0f;
     }
     if (row_stride < 1) row_stride = 1;
+    const double t1 = now_ms();
     int64_t total = 0;
     for (int i = 0; i < P; ++i)
         if (gs[i].valid) total += (int64_t)(gs[i].rmax[0] - gs[i].rmin[0]) * (gs[i].rmax[1] - gs[i].rmin[1]);
@@ -677,7 +700,9 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
         }
         if (i == total - 1) ranges[2 * t + 1] = total;
     }
-#pragma omp parallel for schedule(dynamic, 1)
+    const double t2 = now_ms();
+    int64_t evaluations = 0;
+#pragma omp parallel for schedule(dynamic, 1) reduction(+ : evaluations)
     for (int tile = 0; tile < tiles; ++tile) {
         const int tx = tile % gx, ty = tile / gx;
         if (ty % row_stride != 0) continue;
@@ -691,6 +716,7 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
             const StGauss* g = &gs[pairs[j].value];
             int all_done = 1;
             for (int k = 0; k < 256; ++k) {
+                evaluations += px[k].done ? 0 : 1;
                 const float w = st_blend(&px[k], (float)(tx * 16 + (k & 15)), (float)(ty * 16 + (k >> 4)), g->rec);
                 if (w != 0.0f) {
 #pragma omp atomic
@@ -712,6 +738,12 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
             out_aux7[5 * plane + pid] = s->median;
             out_aux7[6 * plane + pid] = s->dist;
         }
+    }
+    if (stage_ms != NULL) {
+        stage_ms[0] = t1 - t0;
+        stage_ms[1] = t2 - t1;
+        stage_ms[2] = now_ms() - t2;
+        stage_ms[3] = (double)evaluations;
     }
     free(ranges);
     free(pairs);

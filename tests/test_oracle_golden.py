@@ -1,0 +1,81 @@
+"""Pins the CPU oracle against golden vectors from the reference library.
+
+The C restatement uses correctly rounded sqrt/rsqrt/log2 and the C library
+expf where the GPU uses approximate hardware instructions and CUDA's expf,
+so agreement is statistical: the pair lists must agree to within a few
+entries and almost every pixel to 1e-4. The numpy restatements of the
+fixed-rounding elementwise kernels must be bit-identical except where expf
+is involved.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from cases import CASES
+from helpers import FLASHGS_OUT, camera_args, fixture_inputs
+from oracle import oracle
+
+CASE_NAMES = [c.name for c in CASES]
+PIXEL_TOL = 1e-4
+
+
+def close_fraction(a: np.ndarray, b: np.ndarray, tol: float = PIXEL_TOL) -> float:
+    if a.size == 0:
+        return 1.0
+    d = np.abs(a.astype(np.float64) - b.astype(np.float64))
+    return float(np.mean(d <= tol + tol * np.abs(b)))
+
+
+def test_oracle_library_loads():
+    lib = oracle.library()
+    assert hasattr(lib, "oracle_flashgs_forward") and hasattr(lib, "oracle_standard_forward")
+
+
+@pytest.mark.parametrize("case", CASE_NAMES)
+@pytest.mark.parametrize("group", ["base", "reflection"])
+def test_flashgs_oracle_matches_reference(golden, case, group):
+    data = golden(case)
+    out = oracle.flashgs_forward(fixture_inputs(data, "flashgs", group), use_sh=group == "base",
+                                 **camera_args(data))
+    ref_pairs = int(data[f"flashgs_{group}_out_rendered"][0])
+    assert abs(out["rendered"] - ref_pairs) <= max(2, ref_pairs // 200)
+    for name in FLASHGS_OUT:
+        assert close_fraction(out[name], data[f"flashgs_{group}_out_{name}"]) >= 0.99, name
+
+
+@pytest.mark.parametrize("case", CASE_NAMES)
+@pytest.mark.parametrize("group", ["base", "reflection"])
+def test_standard_oracle_matches_reference(golden, case, group):
+    data = golden(case)
+    w, h = (int(v) for v in data["camera_size"])
+    out = oracle.standard_forward(fixture_inputs(data, "standard", group), width=w, height=h)
+    assert out["rendered"] == int(data[f"standard_{group}_out_rendered"][0])
+    assert np.array_equal(out["radii"], data[f"standard_{group}_out_radii"])
+    for name in ("color", "auxiliary"):
+        assert close_fraction(out[name], data[f"standard_{group}_out_{name}"]) >= 0.99, name
+
+
+def test_precise_restatements_match_reference(golden):
+    d = golden("precise")
+    assert np.array_equal(oracle.precise_normalize4(d["in_q"]), d["out_normalize4"])
+    direction = oracle.precise_direction(d["in_points"], d["in_center"])
+    assert np.array_equal(direction, d["out_direction"])
+    for deg in range(4):
+        assert np.array_equal(oracle.precise_sh_to_rgb(d["in_sh"], d["out_direction"], deg), d[f"out_sh{deg}"])
+    fused = oracle.precise_fuse_maps(d["in_base"], d["in_refl"], d["in_spec"])
+    for k, v in fused.items():
+        assert np.array_equal(v, d[f"out_{k}"]), k
+    # expf-based kernels: within one ulp
+    np.testing.assert_array_max_ulp(oracle.precise_exp(d["in_x"]), d["out_exp"], maxulp=1)
+    np.testing.assert_array_max_ulp(oracle.precise_sigmoid(d["in_x"]), d["out_sigmoid"], maxulp=2)
+
+
+def test_oracle_detects_a_planted_error(golden):
+    """A wrong opacity (planted in the oracle's input) must fail the comparison."""
+    data = golden("small")
+    inputs = fixture_inputs(data, "flashgs", "base")
+    inputs["opacities"] = inputs["opacities"] * np.float32(0.5)
+    out = oracle.flashgs_forward(inputs, use_sh=True, **camera_args(data))
+    assert close_fraction(out["color"], data["flashgs_base_out_color"]) < 0.99
