@@ -6,6 +6,7 @@
 // elementwise and math helpers), so callers observe the same behaviour for
 // invalid input. Every entry point catches C++ exceptions (guard).
 #include "hybridsplat_rasterizer_c_api.h"
+#include "hybridsplat_b200_ext.h"
 
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
@@ -382,6 +383,7 @@ int32_t hs_rasterizer_destroy(HsRasterizerHandle handle, char* error_text,
             if (e != cudaSuccess) return cuda_failure(e, "release FlashGS context", error_text, error_capacity);
             e = release_math(handle);
             if (e != cudaSuccess) return cuda_failure(e, "release math context", error_text, error_capacity);
+            hs::stage_timing_destroy(handle->timer);
         }
         delete handle;
         return ok(error_text, error_capacity);
@@ -937,6 +939,35 @@ int32_t hs_rasterizer_precise_reflection_suffix_f32_v1(const float* xyz,
                            return hs::precise::reflection_suffix(xyz, camera_center, normal_raw3,
                                                                  count, output36, nullptr);
                        });
+}
+
+// ---- extensions of this library (no counterpart in the reference ABI) ----
+
+int32_t hs_b200_stage_timing_enable_v1(HsRasterizerHandle handle, int32_t enable, char* error_text,
+                                       uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        handle->timer.enabled = enable != 0;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_b200_stage_timing_read_v1(HsRasterizerHandle handle, double* stage_ms3,
+                                     uint64_t* raster_calls, char* error_text,
+                                     uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (stage_ms3 == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "stage_ms3 is null", error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        const cudaError_t e = hs::stage_timing_read(handle->timer, stage_ms3, raster_calls);
+        if (e != cudaSuccess) return cuda_failure(e, "stage timing", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
 }
 
 }  // extern "C"

@@ -11,8 +11,10 @@
 #include <cuda_runtime.h>
 #include <cusolverDn.h>
 
+#include <array>
 #include <cstdint>
 #include <mutex>
+#include <vector>
 
 namespace hs {
 
@@ -39,6 +41,38 @@ struct Carver {
         return p;
     }
 };
+
+// Optional device timing of the raster calls, split into the three stages
+// of the hot path: preprocess (projection, culling, colour), binning (depth
+// sort, pair emission, tile sort, tile ranges) and blending (the tile
+// renderer). Events are recorded on the launching stream only while enabled;
+// stage_timing_read drains them. Not part of the reference ABI.
+struct StageTimer {
+    static constexpr size_t kMaxPending = 4096;
+    bool enabled = false;
+    std::vector<std::array<cudaEvent_t, 4>> pool;
+    size_t used = 0;
+    uint64_t dropped = 0;
+    double total_ms[3] = {0.0, 0.0, 0.0};
+    uint64_t calls = 0;
+};
+
+// Marks the stage boundaries of one raster call. Boundaries a call does not
+// reach (early exits) are recorded when the marker goes out of scope, so
+// every drained event set is complete.
+class StageMarks {
+public:
+    StageMarks(StageTimer& timer, cudaStream_t stream);
+    ~StageMarks();
+    void mark(int boundary);  // 0 = start, 1 = after preprocess, 2 = before blend, 3 = end
+private:
+    std::array<cudaEvent_t, 4>* set_ = nullptr;
+    cudaStream_t stream_;
+    int next_ = 0;
+};
+
+cudaError_t stage_timing_read(StageTimer& timer, double out_ms[3], uint64_t* calls);
+void stage_timing_destroy(StageTimer& timer);
 
 }  // namespace hs
 
@@ -90,6 +124,8 @@ struct HsRasterizerContext {
     uint64_t math_general_inverse_calls = 0;
     uint64_t math_matmul_calls = 0;
     uint64_t math_pixel_world_calls = 0;
+
+    hs::StageTimer timer;
 };
 
 namespace hs {

@@ -160,6 +160,7 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
     cam.grid_x = grid_x;
     cam.grid_y = grid_y;
 
+    StageMarks marks(ctx->timer, stream);
     cudaError_t st = ensure_buffer(ctx->fg_ranges, tiles * sizeof(int2), &ctx->fg_growth_count);
     if (st != cudaSuccess) return st;
     ctx->fg_range_capacity = std::max<uint64_t>(ctx->fg_range_capacity, tiles);
@@ -195,6 +196,7 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
             gv.emit, gv.keys, gv.order, gv.counts);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
+        marks.mark(1);
         st = sort::sort_pairs(gv.keys, gv.order, gv.alt_keys, gv.alt_order, point_count, 0, 32,
                               ctx->fg_sort.ptr, stream);
         if (st != cudaSuccess) return st;
@@ -254,10 +256,12 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
     const float3 bg_encoded = make_float3(encode(bg.x), encode(bg.y), encode(bg.z));
     const uint32_t* ids = nullptr;
     if (num_rendered > 0) ids = pair_views(ctx->fg_pairs.ptr, ctx->fg_pair_capacity).ids;
+    marks.mark(2);
     render_kernel<HS_FLASHGS_ROUNDING><<<static_cast<unsigned>(tiles), kRenderThreads, 0, stream>>>(
         ranges, ids, gv.records, width, height, grid_x, bg, bg_encoded, out);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
+    marks.mark(3);
     if (num_rendered > 0) {
         st = cudaMemcpyAsync(output_num_rendered, gv.total, sizeof(int32_t),
                              cudaMemcpyDeviceToDevice, stream);

@@ -131,6 +131,7 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
     const uint32_t grid_y = static_cast<uint32_t>((height + 15) / 16);
     const uint64_t tiles = static_cast<uint64_t>(grid_x) * grid_y;
     const uint64_t count = static_cast<uint64_t>(point_count);
+    StageMarks marks(ctx->timer, stream);
 
     // Geometry: per-Gaussian views followed by the depth-sort / scan scratch.
     const uint64_t geometry_used = geometry_bytes(count);
@@ -162,6 +163,7 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
         gv.rects, gv.keys, gv.order, gv.counts, output_radii, gv.total + 1);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
+    marks.mark(1);
     st = sort::sort_pairs(gv.keys, gv.order, gv.alt_keys, gv.alt_order, point_count, 0, 32,
                           geometry_scratch, stream);
     if (st != cudaSuccess) return st;
@@ -202,6 +204,7 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
     }
+    marks.mark(2);
     render_kernel<HS_STANDARD_ROUNDING><<<static_cast<unsigned>(tiles), kRenderThreads, 0, stream>>>(
         ranges, ids, gv.records, width, height, grid_x, background5, output_color5, output_aux7,
         output_weight);

@@ -38,4 +38,59 @@ cudaError_t release_buffer(DeviceBuffer& buffer) {
     return status;
 }
 
+StageMarks::StageMarks(StageTimer& timer, cudaStream_t stream) : stream_(stream) {
+    if (!timer.enabled) return;
+    if (timer.used >= StageTimer::kMaxPending) {
+        ++timer.dropped;
+        return;
+    }
+    if (timer.used == timer.pool.size()) {
+        std::array<cudaEvent_t, 4> set{};
+        for (auto& e : set) {
+            if (cudaEventCreate(&e) != cudaSuccess) {
+                ++timer.dropped;
+                return;
+            }
+        }
+        timer.pool.push_back(set);
+    }
+    set_ = &timer.pool[timer.used++];
+    mark(0);
+}
+
+void StageMarks::mark(int boundary) {
+    if (set_ == nullptr) return;
+    while (next_ <= boundary && next_ < 4) cudaEventRecord((*set_)[next_++], stream_);
+}
+
+StageMarks::~StageMarks() { mark(3); }
+
+cudaError_t stage_timing_read(StageTimer& timer, double out_ms[3], uint64_t* calls) {
+    for (size_t i = 0; i < timer.used; ++i) {
+        auto& set = timer.pool[i];
+        cudaError_t st = cudaEventSynchronize(set[3]);
+        if (st != cudaSuccess) return st;
+        for (int k = 0; k < 3; ++k) {
+            float ms = 0.0f;
+            st = cudaEventElapsedTime(&ms, set[k], set[k + 1]);
+            if (st != cudaSuccess) return st;
+            timer.total_ms[k] += ms;
+        }
+        ++timer.calls;
+    }
+    timer.used = 0;
+    for (int k = 0; k < 3; ++k) out_ms[k] = timer.total_ms[k];
+    if (calls != nullptr) *calls = timer.calls;
+    timer.total_ms[0] = timer.total_ms[1] = timer.total_ms[2] = 0.0;
+    timer.calls = 0;
+    return cudaSuccess;
+}
+
+void stage_timing_destroy(StageTimer& timer) {
+    for (auto& set : timer.pool)
+        for (auto& e : set) cudaEventDestroy(e);
+    timer.pool.clear();
+    timer.used = 0;
+}
+
 }  // namespace hs

@@ -173,6 +173,13 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "hs_rasterizer_precise_reflection_suffix_f32_v1": (_I32, [_V, _V, _V, _U64, _V, *_ERR]),
 }
 
+# Extensions of this library (include/hybridsplat_b200_ext.h); the reference
+# library does not export them, so they are bound only where present.
+EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
+    "hs_b200_stage_timing_enable_v1": (_I32, [_V, _I32, *_ERR]),
+    "hs_b200_stage_timing_read_v1": (_I32, [_V, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_U64), *_ERR]),
+}
+
 # Entry points that the reference's OptiX-free oracle build does not export.
 OPTIX_SYMBOLS = {
     "hs_optix_build_scene_v1",
@@ -214,6 +221,10 @@ def bind_library(path: Path | str, *, require_optix: bool = True) -> ctypes.CDLL
             raise NativeRasterizerError(f"{path} does not export {name}") from exc
         function.restype = restype
         function.argtypes = argtypes
+    for name, (restype, argtypes) in EXTENSION_SIGNATURES.items():
+        if hasattr(library, name):
+            getattr(library, name).restype = restype
+            getattr(library, name).argtypes = argtypes
     version = int(library.hs_rasterizer_abi_version())
     if version != HS_RASTERIZER_ABI_VERSION:
         raise NativeRasterizerError(
@@ -311,6 +322,24 @@ class NativeRendererContext:
 
     def flashgs_workspace_stats(self) -> dict[str, int]:
         return self._stats("hs_flashgs_workspace_stats_v1", FlashgsWorkspaceStatsV1)
+
+    def stage_timing(self, enable: bool) -> None:
+        """Turns per-stage device timing of the raster calls on or off
+        (library extension; absent from the reference library)."""
+        error = error_buffer()
+        status = self._library.hs_b200_stage_timing_enable_v1(self.handle, int(bool(enable)), error, len(error))
+        check_status(status, "hs_b200_stage_timing_enable_v1", error)
+
+    def read_stage_timing(self) -> dict[str, float]:
+        """Summed preprocess / binning / blending ms of the raster calls
+        timed since the previous read, and their count."""
+        ms = (ctypes.c_double * 3)()
+        calls = _U64(0)
+        error = error_buffer()
+        status = self._library.hs_b200_stage_timing_read_v1(self.handle, ms, ctypes.byref(calls), error,
+                                                            len(error))
+        check_status(status, "hs_b200_stage_timing_read_v1", error)
+        return {"preprocess_ms": ms[0], "binning_ms": ms[1], "blend_ms": ms[2], "calls": int(calls.value)}
 
     def release_workspace(self) -> None:
         _torch_synchronize(self._device)

@@ -24,9 +24,13 @@ from hybridsplat_jittor_render_b200 import ops
 HEADER = REPO / "include" / "hybridsplat_rasterizer_c_api.h"
 
 
-def declared_symbols() -> list[str]:
-    text = HEADER.read_text()
-    return re.findall(r"HS_API\s+[a-z0-9_]+\s+(hs_[a-z0-9_]+)\s*\(", text)
+def declared_symbols(header=None) -> list[str]:
+    """Entry points declared by one header, or by every header in include/."""
+    files = [header] if header is not None else sorted((REPO / "include").glob("*.h"))
+    names = []
+    for f in files:
+        names += re.findall(r"HS_API\s+[a-z0-9_]+\s+(hs_[a-z0-9_]+)\s*\(", f.read_text())
+    return names
 
 
 @pytest.fixture(scope="module")
@@ -43,10 +47,11 @@ def ref():
 
 def test_exports_every_declared_symbol(lib):
     symbols = declared_symbols()
-    assert len(symbols) >= 30
+    assert len(declared_symbols(HEADER)) >= 30
     for name in symbols:
         assert hasattr(lib, name), name
-    assert set(nr.SIGNATURES) <= set(symbols)
+    assert set(nr.SIGNATURES) == set(declared_symbols(HEADER))
+    assert set(nr.SIGNATURES) | set(nr.EXTENSION_SIGNATURES) == set(symbols)
 
 
 def test_abi_version_and_build_info(lib):

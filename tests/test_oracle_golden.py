@@ -2,8 +2,10 @@
 
 The C restatement uses correctly rounded sqrt/rsqrt/log2 and the C library
 expf where the GPU uses approximate hardware instructions and CUDA's expf,
-so agreement is statistical: the pair lists must agree to within a few
-entries and almost every pixel to 1e-4. The numpy restatements of the
+so agreement is statistical: on the fixture scenes the pair counts agree
+exactly and at least 99.9% of the values agree to 1e-4 (absolute plus
+relative; all of them do at the time of writing, with a largest difference
+of 1.4e-5). The numpy restatements of the
 fixed-rounding elementwise kernels must be bit-identical except where expf
 is involved.
 """
@@ -19,6 +21,7 @@ from oracle import oracle
 
 CASE_NAMES = [c.name for c in CASES]
 PIXEL_TOL = 1e-4
+AGREEMENT = 0.999
 
 
 def close_fraction(a: np.ndarray, b: np.ndarray, tol: float = PIXEL_TOL) -> float:
@@ -40,9 +43,9 @@ def test_flashgs_oracle_matches_reference(golden, case, group):
     out = oracle.flashgs_forward(fixture_inputs(data, "flashgs", group), use_sh=group == "base",
                                  **camera_args(data))
     ref_pairs = int(data[f"flashgs_{group}_out_rendered"][0])
-    assert abs(out["rendered"] - ref_pairs) <= max(2, ref_pairs // 200)
+    assert out["rendered"] == ref_pairs
     for name in FLASHGS_OUT:
-        assert close_fraction(out[name], data[f"flashgs_{group}_out_{name}"]) >= 0.99, name
+        assert close_fraction(out[name], data[f"flashgs_{group}_out_{name}"]) >= AGREEMENT, name
 
 
 @pytest.mark.parametrize("case", CASE_NAMES)
@@ -54,7 +57,7 @@ def test_standard_oracle_matches_reference(golden, case, group):
     assert out["rendered"] == int(data[f"standard_{group}_out_rendered"][0])
     assert np.array_equal(out["radii"], data[f"standard_{group}_out_radii"])
     for name in ("color", "auxiliary"):
-        assert close_fraction(out[name], data[f"standard_{group}_out_{name}"]) >= 0.99, name
+        assert close_fraction(out[name], data[f"standard_{group}_out_{name}"]) >= AGREEMENT, name
 
 
 def test_precise_restatements_match_reference(golden):
@@ -67,9 +70,11 @@ def test_precise_restatements_match_reference(golden):
     fused = oracle.precise_fuse_maps(d["in_base"], d["in_refl"], d["in_spec"])
     for k, v in fused.items():
         assert np.array_equal(v, d[f"out_{k}"]), k
-    # expf-based kernels: within one ulp
-    np.testing.assert_array_max_ulp(oracle.precise_exp(d["in_x"]), d["out_exp"], maxulp=1)
-    np.testing.assert_array_max_ulp(oracle.precise_sigmoid(d["in_x"]), d["out_sigmoid"], maxulp=2)
+    # expf-based kernels: CUDA documents expf to within 2 ulp and numpy's
+    # float32 exp is within 1 ulp, so the two may differ by 3; the sigmoid's
+    # add and divide can carry that to 4.
+    np.testing.assert_array_max_ulp(oracle.precise_exp(d["in_x"]), d["out_exp"], maxulp=3)
+    np.testing.assert_array_max_ulp(oracle.precise_sigmoid(d["in_x"]), d["out_sigmoid"], maxulp=4)
 
 
 def test_oracle_detects_a_planted_error(golden):
@@ -78,4 +83,4 @@ def test_oracle_detects_a_planted_error(golden):
     inputs = fixture_inputs(data, "flashgs", "base")
     inputs["opacities"] = inputs["opacities"] * np.float32(0.5)
     out = oracle.flashgs_forward(inputs, use_sh=True, **camera_args(data))
-    assert close_fraction(out["color"], data["flashgs_base_out_color"]) < 0.99
+    assert close_fraction(out["color"], data["flashgs_base_out_color"]) < AGREEMENT
