@@ -1,0 +1,156 @@
+// Pair emission and tile ranges shared by both backends.
+//
+// After the depth sort, `order` lists the Gaussians by (depth bits, index).
+// offsets_kernel scans the per-Gaussian pair counts in that order (a
+// single-pass exclusive scan with decoupled look-back across blocks) and
+// stores each Gaussian's first pair slot by Gaussian index. emit_kernel then
+// writes the pairs, walking the Gaussians in index order so that the large
+// screen-space footprints of the nearest Gaussians (adjacent in depth order)
+// spread over all blocks. Pairs of one Gaussian may be written in any order
+// among themselves: each names a different tile, and the following stable
+// sort by tile id keeps, for every tile, the depth order of the Gaussians.
+// The result is the reference's lexicographic (tile | depth key, index)
+// order (vendor/flashgs/cuda_rasterizer/sort.cu:160-189,
+// rasterizer/full_rasterizer.cu:127-153).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "sort.cuh"
+
+namespace hs {
+namespace bin {
+
+constexpr int kScanThreads = 256;
+constexpr int kScanItems = 8;                          // sorted positions per thread
+constexpr int kScanTile = kScanThreads * kScanItems;   // 2048 Gaussians per block
+constexpr int kEmitThreads = 256;
+
+inline uint32_t scan_tiles(uint32_t count) { return (count + kScanTile - 1) / kScanTile; }
+// Scratch words of offsets_kernel (counter + one status word per block);
+// zeroed before the launch.
+inline uint64_t scan_scratch_bytes(uint32_t count) {
+    return (static_cast<uint64_t>(scan_tiles(count > 0 ? count : 1)) + 64) * sizeof(uint32_t);
+}
+
+__device__ __forceinline__ uint32_t warp_sum(uint32_t v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+// first_pair[order[i]] = sum(counts[order[j]] for j < i).
+static __global__ void __launch_bounds__(kScanThreads) offsets_kernel(
+    uint32_t count, const uint32_t* __restrict__ order, const uint32_t* __restrict__ counts,
+    uint32_t* __restrict__ control, uint32_t* __restrict__ error,
+    uint32_t* __restrict__ first_pair) {
+    __shared__ uint32_t warp_sums[kScanThreads / 32];
+    __shared__ uint32_t tile_slot, tile_prefix;
+    uint32_t* counter = control;
+    uint32_t* status = control + 64;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) tile_slot = atomicAdd(counter, 1u);
+    __syncthreads();
+    const uint32_t tile = tile_slot;
+    const uint64_t base = static_cast<uint64_t>(tile) * kScanTile +
+                          static_cast<uint64_t>(threadIdx.x) * kScanItems;
+    uint32_t gid[kScanItems], cnt[kScanItems];
+    uint32_t local = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) {
+        const uint64_t i = base + k;
+        gid[k] = i < count ? order[i] : 0u;
+        cnt[k] = i < count ? counts[gid[k]] : 0u;
+        local += cnt[k];
+    }
+    uint32_t incl = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t sum = 0;
+        for (int w = 0; w < kScanThreads / 32; ++w) sum += warp_sums[w];
+        uint32_t earlier = 0;
+        if (tile == 0) {
+            sort::store_status(status, sort::kFlagInclusive | (sum & sort::kValueMask));
+        } else {
+            sort::store_status(status + tile, sort::kFlagAggregate | (sum & sort::kValueMask));
+            earlier = sort::look_back(status, tile, 1, error);
+            sort::store_status(status + tile,
+                               sort::kFlagInclusive | ((earlier + sum) & sort::kValueMask));
+        }
+        tile_prefix = earlier;
+    }
+    __syncthreads();
+    uint32_t run = tile_prefix;
+    for (int w = 0; w < warp; ++w) run += warp_sums[w];
+    run += incl - local;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) {
+        if (cnt[k] != 0u) first_pair[gid[k]] = run;
+        run += cnt[k];
+    }
+}
+
+// Emitter interface:
+//   struct E {
+//     struct Shape {...};                                   // per-Gaussian emission data
+//     __device__ Shape load(uint32_t gid) const;            // read by the owning lane
+//     __device__ bool small(const Shape&) const;            // emit on the owning lane alone?
+//     __device__ void emit_serial(const Shape&, uint32_t gid, uint32_t offset, uint32_t count,
+//                                 uint32_t* tiles, uint32_t* values) const;  // one lane
+//     __device__ Shape shfl(const Shape&, int src) const;   // broadcast from lane src
+//     __device__ void emit(const Shape&, uint32_t gid, uint32_t offset, uint32_t count,
+//                          int lane, uint32_t* tiles, uint32_t* values) const;  // all 32 lanes
+//   };
+// Gaussians with small tile rectangles are emitted by their own lane, the
+// others by the whole warp, one Gaussian at a time.
+template <class Emitter>
+__global__ void __launch_bounds__(kEmitThreads) emit_kernel(
+    uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
+    Emitter em, uint32_t* __restrict__ tile_ids, uint32_t* __restrict__ values) {
+    const uint32_t gid = blockIdx.x * kEmitThreads + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const uint32_t cnt = gid < count ? counts[gid] : 0u;
+    const uint32_t off = cnt != 0u ? first_pair[gid] : 0u;
+    const typename Emitter::Shape mine = em.load(cnt != 0u ? gid : 0u);
+    const bool serial = cnt != 0u && em.small(mine);
+    if (serial) em.emit_serial(mine, gid, off, cnt, tile_ids, values);
+    uint32_t pending = __ballot_sync(0xffffffffu, cnt != 0u && !serial);
+    while (pending != 0u) {
+        const int src = __ffs(pending) - 1;
+        pending &= pending - 1u;
+        const typename Emitter::Shape s = em.shfl(mine, src);
+        const uint32_t g = __shfl_sync(0xffffffffu, gid, src);
+        const uint32_t o = __shfl_sync(0xffffffffu, off, src);
+        const uint32_t c = __shfl_sync(0xffffffffu, cnt, src);
+        em.emit(s, g, o, c, lane, tile_ids, values);
+    }
+}
+
+// Per-tile [start, end) of the sorted pair list. Entries of tiles without
+// pairs keep the zeros written before the launch. Tile ids >= tile_count are
+// padding and are ignored.
+template <class Range>
+__global__ void ranges_kernel(uint32_t pair_count, uint32_t tile_count,
+                              const uint32_t* __restrict__ tile_ids, Range* __restrict__ ranges) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= pair_count) return;
+    const uint32_t t = tile_ids[i];
+    const uint32_t prev = i == 0 ? 0xffffffffu : tile_ids[i - 1];
+    if (t != prev) {
+        if (t < tile_count) ranges[t].x = static_cast<decltype(ranges[t].x)>(i);
+        if (prev < tile_count) ranges[prev].y = static_cast<decltype(ranges[prev].y)>(i);
+    }
+    if (i == pair_count - 1 && t < tile_count) {
+        ranges[t].y = static_cast<decltype(ranges[t].y)>(pair_count);
+    }
+}
+
+}  // namespace bin
+}  // namespace hs

@@ -384,6 +384,9 @@ int32_t hs_rasterizer_destroy(HsRasterizerHandle handle, char* error_text,
             e = release_math(handle);
             if (e != cudaSuccess) return cuda_failure(e, "release math context", error_text, error_capacity);
             hs::stage_timing_destroy(handle->timer);
+            if (handle->std_count_event != nullptr) cudaEventDestroy(handle->std_count_event);
+            if (handle->fg_count_event != nullptr) cudaEventDestroy(handle->fg_count_event);
+            if (handle->device_error != nullptr) cudaFree(handle->device_error);
         }
         delete handle;
         return ok(error_text, error_capacity);

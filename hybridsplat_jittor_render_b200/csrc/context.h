@@ -16,6 +16,8 @@
 #include <mutex>
 #include <vector>
 
+struct HsRasterizerContext;
+
 namespace hs {
 
 struct DeviceBuffer {
@@ -23,9 +25,11 @@ struct DeviceBuffer {
     uint64_t bytes = 0;
 };
 
-// Grow-only device allocation: 2 MiB granularity; the old buffer is freed
-// after cudaDeviceSynchronize (reference flashgs_backend.cu:56-86).
-cudaError_t ensure_buffer(DeviceBuffer& buffer, uint64_t required, uint64_t* growth_count);
+// Grow-only device allocation with 2 MiB granularity; `geometric` grows to at
+// least 1.25x the previous size. The old buffer is freed after
+// cudaDeviceSynchronize (reference c_api.cpp:85-127, flashgs_backend.cu:56-86).
+cudaError_t ensure_buffer(DeviceBuffer& buffer, uint64_t required, uint64_t* growth_count,
+                          bool geometric = false);
 cudaError_t release_buffer(DeviceBuffer& buffer);
 
 // Carves aligned sub-ranges out of one workspace allocation.
@@ -72,6 +76,9 @@ private:
 };
 
 cudaError_t stage_timing_read(StageTimer& timer, double out_ms[3], uint64_t* calls);
+
+// Allocates and zeroes context->device_error on first use.
+cudaError_t ensure_device_error(HsRasterizerContext* context);
 void stage_timing_destroy(StageTimer& timer);
 
 }  // namespace hs
@@ -126,6 +133,12 @@ struct HsRasterizerContext {
     uint64_t math_pixel_world_calls = 0;
 
     hs::StageTimer timer;
+
+    // Device status word shared by the look-back waits of every sort and scan
+    // of this context (bit 0: a wait gave up). Allocated and zeroed once.
+    uint32_t* device_error = nullptr;
+    cudaEvent_t std_count_event = nullptr;  // marks the standard totals readback
+    cudaEvent_t fg_count_event = nullptr;   // marks the FlashGS totals readback
 };
 
 namespace hs {

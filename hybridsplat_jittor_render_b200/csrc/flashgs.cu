@@ -172,10 +172,16 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
     GaussianViews gv{};
     if (point_count > 0) {
         if (ctx->fg_total_host == nullptr) {
-            st = cudaHostAlloc(reinterpret_cast<void**>(&ctx->fg_total_host), sizeof(uint32_t),
+            st = cudaHostAlloc(reinterpret_cast<void**>(&ctx->fg_total_host), 4 * sizeof(uint32_t),
                                cudaHostAllocPortable);
             if (st != cudaSuccess) return st;
             ++ctx->fg_growth_count;
+        }
+        st = ensure_device_error(ctx);
+        if (st != cudaSuccess) return st;
+        if (ctx->fg_count_event == nullptr) {
+            st = cudaEventCreateWithFlags(&ctx->fg_count_event, cudaEventDisableTiming);
+            if (st != cudaSuccess) return st;
         }
         const uint64_t count = static_cast<uint64_t>(point_count);
         if (count > ctx->fg_gaussian_capacity || ctx->fg_gaussian.ptr == nullptr) {
@@ -185,31 +191,37 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
         }
         gv = gaussian_views(ctx->fg_gaussian.ptr, ctx->fg_gaussian_capacity);
         const uint64_t sort_need = std::max(sort::sort_scratch_bytes(point_count),
-                                            sort::scan_scratch_bytes(point_count));
+                                            bin::scan_scratch_bytes(point_count));
         st = ensure_buffer(ctx->fg_sort, sort_need, &ctx->fg_growth_count);
+        if (st != cudaSuccess) return st;
+        st = cudaMemsetAsync(gv.total, 0, 4 * sizeof(uint32_t), stream);
         if (st != cudaSuccess) return st;
 
         const int blocks = (point_count + kPreThreads - 1) / kPreThreads;
         preprocess_kernel<HS_FLASHGS_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
             point_count, cam, positions3, shs48, colors3, use_sh ? 1 : 0, opacities1,
             covariance6, scales2, scale_modifier, rotations4, specular1, roughness1, gv.records,
-            gv.emit, gv.keys, gv.order, gv.counts);
+            gv.emit, gv.keys, gv.order, gv.counts, gv.total, ctx->device_error);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
-        marks.mark(1);
-        st = sort::sort_pairs(gv.keys, gv.order, gv.alt_keys, gv.alt_order, point_count, 0, 32,
-                              ctx->fg_sort.ptr, stream);
-        if (st != cudaSuccess) return st;
-        st = sort::exclusive_scan(gv.counts, gv.order, gv.offsets, gv.total, point_count,
-                                  ctx->fg_sort.ptr, stream);
-        if (st != cudaSuccess) return st;
-        st = cudaMemcpyAsync(ctx->fg_total_host, gv.total, sizeof(uint32_t),
+        st = cudaMemcpyAsync(ctx->fg_total_host, gv.total, 4 * sizeof(uint32_t),
                              cudaMemcpyDeviceToHost, stream);
+        if (st == cudaSuccess) st = cudaEventRecord(ctx->fg_count_event, stream);
         if (st != cudaSuccess) return st;
-        st = cudaStreamSynchronize(stream);
+        marks.mark(1);
+        // The depth sort does not depend on the pair count: queue it, then
+        // wait for the count (the reference reads its counter back here,
+        // flashgs_backend.cu:480-488).
+        st = sort::sort_pairs(gv.keys, gv.order, gv.alt_keys, gv.alt_order, point_count, 0, 32,
+                              ctx->fg_sort.ptr, stream, ctx->device_error);
         if (st != cudaSuccess) return st;
-        num_rendered = *ctx->fg_total_host;
-        if (num_rendered > static_cast<uint32_t>(INT_MAX)) return cudaErrorInvalidValue;
+        st = cudaEventSynchronize(ctx->fg_count_event);
+        if (st != cudaSuccess) return st;
+        num_rendered = ctx->fg_total_host[0];
+        if (ctx->fg_total_host[1] != 0) return cudaErrorLaunchTimeout;  // a look-back wait gave up
+        if (num_rendered > static_cast<uint32_t>(INT_MAX) || num_rendered > sort::kMaxItems) {
+            return cudaErrorInvalidValue;
+        }
 
         // Pair capacity follows the reference's growth rule: start at the
         // caller's initial capacity and, whenever the pair count reaches it,
@@ -227,20 +239,37 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
         st = ensure_buffer(ctx->fg_pairs, pair_bytes(ctx->fg_pair_capacity), &ctx->fg_growth_count);
         if (st != cudaSuccess) return st;
         if (num_rendered > 0) {
-            st = ensure_buffer(ctx->fg_sort, sort::sort_scratch_bytes(num_rendered),
+            // sized by the pair capacity, so it grows only when the capacity does
+            st = ensure_buffer(ctx->fg_sort,
+                               std::max(sort_need, sort::sort_scratch_bytes(static_cast<uint32_t>(
+                                                       ctx->fg_pair_capacity))),
                                &ctx->fg_growth_count);
             if (st != cudaSuccess) return st;
             const PairViews pv = pair_views(ctx->fg_pairs.ptr, ctx->fg_pair_capacity);
-            emit_kernel<HS_FLASHGS_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
-                point_count, grid_x, gv.order, gv.counts, gv.offsets, gv.emit, pv.tiles, pv.ids);
+            st = cudaMemsetAsync(ctx->fg_sort.ptr, 0, bin::scan_scratch_bytes(point_count),
+                                 stream);
+            if (st != cudaSuccess) return st;
+            // alt_keys is free once the depth sort has finished: it receives
+            // the first pair slot of every Gaussian.
+            uint32_t* first_pair = gv.alt_keys;
+            bin::offsets_kernel<<<bin::scan_tiles(point_count), bin::kScanThreads, 0, stream>>>(
+                static_cast<uint32_t>(point_count), gv.order, gv.counts,
+                static_cast<uint32_t*>(ctx->fg_sort.ptr), ctx->device_error, first_pair);
+            st = cudaGetLastError();
+            if (st != cudaSuccess) return st;
+            const Emitter<HS_FLASHGS_ROUNDING> em{gv.emit, grid_x};
+            bin::emit_kernel<Emitter<HS_FLASHGS_ROUNDING>>
+                <<<(point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
+                   stream>>>(static_cast<uint32_t>(point_count), gv.counts, first_pair, em,
+                             pv.tiles, pv.ids);
             st = cudaGetLastError();
             if (st != cudaSuccess) return st;
             st = sort::sort_pairs(pv.tiles, pv.ids, pv.alt_tiles, pv.alt_ids, num_rendered, 0,
                                   sort::bits_for_tiles(static_cast<uint32_t>(tiles)),
-                                  ctx->fg_sort.ptr, stream);
+                                  ctx->fg_sort.ptr, stream, ctx->device_error);
             if (st != cudaSuccess) return st;
-            ranges_kernel<<<(num_rendered + 255) / 256, 256, 0, stream>>>(num_rendered, pv.tiles,
-                                                                          ranges);
+            bin::ranges_kernel<int2><<<(num_rendered + 255) / 256, 256, 0, stream>>>(
+                num_rendered, static_cast<uint32_t>(tiles), pv.tiles, ranges);
             st = cudaGetLastError();
             if (st != cudaSuccess) return st;
         }

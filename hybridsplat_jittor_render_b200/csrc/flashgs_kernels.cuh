@@ -4,6 +4,7 @@
 
 #include <climits>
 
+#include "binning.cuh"
 #include "flashgs_math.cuh"
 
 namespace hs {
@@ -29,6 +30,10 @@ __device__ __forceinline__ float4 f4(float a, float b, float c, float d) {
     return make_float4(a, b, c, d);
 }
 
+// Rectangles up to this many tiles are tested by their own lane; larger ones
+// by the whole warp, 32 tiles per step.
+constexpr int kSerialTiles = 4;
+
 template <class R>
 __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     int point_count, Camera cam, const float* __restrict__ positions,
@@ -37,39 +42,69 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     const float* __restrict__ scales, float scale_modifier, const float* __restrict__ rotations,
     const float* __restrict__ specular, const float* __restrict__ roughness,
     float4* __restrict__ records, float4* __restrict__ emit, uint32_t* __restrict__ depth_keys,
-    uint32_t* __restrict__ order, uint32_t* __restrict__ pair_counts) {
+    uint32_t* __restrict__ order, uint32_t* __restrict__ pair_counts,
+    uint32_t* __restrict__ totals, const uint32_t* __restrict__ error) {
     const int idx = blockIdx.x * kPreThreads + threadIdx.x;
-    if (idx >= point_count) return;
+    const bool active = idx < point_count;
+    const int lane = threadIdx.x & 31;
     const R r;
-    const float3 p = make_float3(positions[3 * idx], positions[3 * idx + 1], positions[3 * idx + 2]);
-    const float opacity = opacities[idx];
-    float cov[6];
+    if (blockIdx.x == 0 && threadIdx.x == 0) totals[1] = *error;
+    Projected g;
+    g.in_front = false;
+    g.touches = false;
+    float3 p = make_float3(0.0f, 0.0f, 0.0f);
+    float opacity = 0.0f;
+    if (active) {
+        p = make_float3(positions[3 * idx], positions[3 * idx + 1], positions[3 * idx + 2]);
+        opacity = opacities[idx];
+        float cov[6];
 #pragma unroll
-    for (int k = 0; k < 6; ++k) cov[k] = cov6[6 * idx + k];
-    const float2 scale = make_float2(scales[2 * idx], scales[2 * idx + 1]);
-    const float4 rot = make_float4(rotations[4 * idx], rotations[4 * idx + 1],
-                                   rotations[4 * idx + 2], rotations[4 * idx + 3]);
-    const Projected g = project_gaussian(r, cam.view, cam.proj, p, opacity, cov, scale,
-                                         scale_modifier, rot, cam.width, cam.height, cam.focal_x,
-                                         cam.focal_y, cam.tan_fovx, cam.tan_fovy, cam.grid_x,
-                                         cam.grid_y);
+        for (int k = 0; k < 6; ++k) cov[k] = cov6[6 * idx + k];
+        const float2 scale = make_float2(scales[2 * idx], scales[2 * idx + 1]);
+        const float4 rot = make_float4(rotations[4 * idx], rotations[4 * idx + 1],
+                                       rotations[4 * idx + 2], rotations[4 * idx + 3]);
+        g = project_gaussian(r, cam.view, cam.proj, p, opacity, cov, scale, scale_modifier, rot,
+                             cam.width, cam.height, cam.focal_x, cam.focal_y, cam.tan_fovx,
+                             cam.tan_fovy, cam.grid_x, cam.grid_y);
+    }
+    // Exact tile/ellipse count (preprocess.cu:482-506).
+    const bool candidate = g.in_front && g.touches;
+    const int gw = candidate ? g.rect_max.x - g.rect_min.x : 0;
+    const int area = candidate ? gw * (g.rect_max.y - g.rect_min.y) : 0;
     uint32_t hits = 0;
-    bool write = false;
-    if (g.in_front && g.touches) {
-        const int area = (g.rect_max.x - g.rect_min.x) * (g.rect_max.y - g.rect_min.y);
-        if (area == 1) {
-            // Single-tile Gaussians always keep their record (preprocess.cu:482-506).
-            write = true;
-            hits = tile_hit(r, g.rect_min.x, g.rect_min.y, g.xy, g.conic, g.power) ? 1u : 0u;
-        } else {
-            for (int ty = g.rect_min.y; ty < g.rect_max.y; ++ty) {
-                for (int tx = g.rect_min.x; tx < g.rect_max.x; ++tx) {
-                    hits += tile_hit(r, tx, ty, g.xy, g.conic, g.power) ? 1u : 0u;
-                }
+    if (candidate && area <= kSerialTiles) {
+        for (int ty = g.rect_min.y; ty < g.rect_max.y; ++ty) {
+            for (int tx = g.rect_min.x; tx < g.rect_max.x; ++tx) {
+                hits += tile_hit(r, tx, ty, g.xy, g.conic, g.power) ? 1u : 0u;
             }
-            write = hits > 0;
         }
     }
+    uint32_t pending = __ballot_sync(0xffffffffu, area > kSerialTiles);
+    while (pending != 0u) {
+        const int src = __ffs(pending) - 1;
+        pending &= pending - 1u;
+        const float2 xy = make_float2(__shfl_sync(0xffffffffu, g.xy.x, src),
+                                      __shfl_sync(0xffffffffu, g.xy.y, src));
+        const float3 conic = make_float3(__shfl_sync(0xffffffffu, g.conic.x, src),
+                                         __shfl_sync(0xffffffffu, g.conic.y, src),
+                                         __shfl_sync(0xffffffffu, g.conic.z, src));
+        const float power = __shfl_sync(0xffffffffu, g.power, src);
+        const int x0 = __shfl_sync(0xffffffffu, g.rect_min.x, src);
+        const int y0 = __shfl_sync(0xffffffffu, g.rect_min.y, src);
+        const int w = __shfl_sync(0xffffffffu, gw, src);
+        const int n = __shfl_sync(0xffffffffu, area, src);
+        uint32_t c = 0;
+        for (int t = lane; t < n; t += 32) {
+            c += tile_hit(r, x0 + t % w, y0 + t / w, xy, conic, power) ? 1u : 0u;
+        }
+        c = bin::warp_sum(c);
+        if (lane == src) hits = c;
+    }
+    const uint32_t total_hits = bin::warp_sum(hits);
+    if (lane == 0 && total_hits != 0u) atomicAdd(totals, total_hits);
+    if (!active) return;
+    // Single-tile Gaussians always keep their record (preprocess.cu:482-506).
+    const bool write = candidate && (area == 1 || hits > 0);
     float4* rec = records + static_cast<size_t>(idx) * kRecordQuads;
     if (write) {
         float3 rgb;
@@ -102,52 +137,79 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     pair_counts[idx] = hits;
 }
 
+// Emits the (tile, index) pairs of one Gaussian: the tiles of its rectangle
+// that pass the exact tile/ellipse test, compacted with a warp ballot.
 template <class R>
-__global__ void __launch_bounds__(kPreThreads) emit_kernel(
-    int point_count, int grid_x, const uint32_t* __restrict__ order,
-    const uint32_t* __restrict__ pair_counts, const uint32_t* __restrict__ offsets,
-    const float4* __restrict__ emit, uint32_t* __restrict__ tile_ids,
-    uint32_t* __restrict__ gaussian_ids) {
-    const int s = blockIdx.x * kPreThreads + threadIdx.x;
-    if (s >= point_count) return;
-    const uint32_t gid = order[s];
-    if (pair_counts[gid] == 0) return;
-    const R r;
-    const float4 e0 = emit[static_cast<size_t>(gid) * kEmitQuads];
-    const float4 e1 = emit[static_cast<size_t>(gid) * kEmitQuads + 1];
-    const float2 xy = make_float2(e0.x, e0.y);
-    const float3 conic = make_float3(e0.z, e0.w, e1.x);
-    const float power = e1.y;
-    const uint32_t lo = __float_as_uint(e1.z), hi = __float_as_uint(e1.w);
-    const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff, y1 = hi >> 16;
-    uint32_t out = offsets[s];
-    for (int ty = y0; ty < y1; ++ty) {
-        for (int tx = x0; tx < x1; ++tx) {
-            if (tile_hit(r, tx, ty, xy, conic, power)) {
-                tile_ids[out] = static_cast<uint32_t>(ty * grid_x + tx);
-                gaussian_ids[out] = gid;
-                ++out;
+struct Emitter {
+    const float4* emit_records;
+    int grid_x;
+
+    struct Shape {
+        float4 a, b;
+    };
+    __device__ __forceinline__ Shape load(uint32_t gid) const {
+        const float4* q = emit_records + static_cast<size_t>(gid) * kEmitQuads;
+        return Shape{q[0], q[1]};
+    }
+    __device__ __forceinline__ static float4 shfl4(float4 v, int src) {
+        return make_float4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
+                           __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
+    }
+    __device__ __forceinline__ Shape shfl(const Shape& s, int src) const {
+        return Shape{shfl4(s.a, src), shfl4(s.b, src)};
+    }
+    __device__ __forceinline__ bool small(const Shape& s) const {
+        const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
+        return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16)) <=
+               static_cast<uint32_t>(2 * kSerialTiles);
+    }
+    __device__ __forceinline__ void emit_serial(const Shape& s, uint32_t gid, uint32_t offset,
+                                                uint32_t count, uint32_t* tiles,
+                                                uint32_t* values) const {
+        const R r;
+        const float2 xy = make_float2(s.a.x, s.a.y);
+        const float3 conic = make_float3(s.a.z, s.a.w, s.b.x);
+        const float power = s.b.y;
+        const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
+        const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff, y1 = hi >> 16;
+        uint32_t at = offset;
+        const uint32_t end = offset + count;
+        for (int ty = y0; ty < y1 && at < end; ++ty) {
+            for (int tx = x0; tx < x1 && at < end; ++tx) {
+                if (tile_hit(r, tx, ty, xy, conic, power)) {
+                    tiles[at] = static_cast<uint32_t>(ty * grid_x + tx);
+                    values[at] = gid;
+                    ++at;
+                }
             }
         }
     }
-}
-
-__global__ void ranges_kernel(uint32_t pair_count, const uint32_t* __restrict__ tile_ids,
-                              int2* __restrict__ ranges) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= pair_count) return;
-    const uint32_t t = tile_ids[i];
-    if (i == 0) {
-        ranges[t].x = 0;
-    } else {
-        const uint32_t prev = tile_ids[i - 1];
-        if (t != prev) {
-            ranges[prev].y = static_cast<int>(i);
-            ranges[t].x = static_cast<int>(i);
+    __device__ __forceinline__ void emit(const Shape& s, uint32_t gid, uint32_t offset,
+                                         uint32_t count, int lane, uint32_t* tiles,
+                                         uint32_t* values) const {
+        const R r;
+        const float2 xy = make_float2(s.a.x, s.a.y);
+        const float3 conic = make_float3(s.a.z, s.a.w, s.b.x);
+        const float power = s.b.y;
+        const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
+        const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff, y1 = hi >> 16;
+        const int w = x1 - x0, n = w * (y1 - y0);
+        const uint32_t lt = (1u << lane) - 1u;
+        uint32_t written = 0;
+        for (int base = 0; base < n && written < count; base += 32) {
+            const int t = base + lane;
+            const int tx = x0 + t % w, ty = y0 + t / w;
+            const bool hit = t < n && tile_hit(r, tx, ty, xy, conic, power);
+            const uint32_t m = __ballot_sync(0xffffffffu, hit);
+            if (hit) {
+                const uint32_t at = offset + written + __popc(m & lt);
+                tiles[at] = static_cast<uint32_t>(ty * grid_x + tx);
+                values[at] = gid;
+            }
+            written += __popc(m);
         }
     }
-    if (i == pair_count - 1) ranges[t].y = static_cast<int>(pair_count);
-}
+};
 
 __device__ __forceinline__ BlendRecord load_record(const float4* q) {
     const float4 a = q[0], b = q[1], c = q[2], d = q[3], e = q[4];

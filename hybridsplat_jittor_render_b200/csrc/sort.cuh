@@ -1,10 +1,17 @@
-// Device-wide stable LSD radix sort of (uint32 key, uint32 value) pairs and
-// an exclusive scan of uint32 counts.
+// Device-wide stable LSD radix sort of (uint32 key, uint32 value) pairs, a
+// single-pass exclusive scan, and the decoupled look-back primitive they
+// share.
 //
 // These replace the reference's CUB calls (vendor/flashgs/cuda_rasterizer/
 // sort.cu:29-58, rasterizer/full_rasterizer.cu:301-355). Only the ordering
 // contract matters for parity: the sort is stable, so equal keys keep their
 // input order, and the scan is exact integer arithmetic.
+//
+// The sort is a "onesweep" LSD radix sort (Adinets and Merrill, 2022): one
+// histogram kernel computes the digit counts of every pass in a single read
+// of the keys, then each 8-bit pass is ONE kernel in which every block ranks
+// its tile in shared memory, obtains the counts of all earlier tiles by
+// decoupled look-back and scatters its items digit-run by digit-run.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -18,25 +25,43 @@ constexpr int kItemsPerThread = 8;
 constexpr int kTile = kThreads * kItemsPerThread;    // 2048 items per block
 constexpr int kRadixBits = 8;
 constexpr int kBins = 1 << kRadixBits;
+constexpr int kMaxPasses = 4;                        // 32-bit keys
+
+// Look-back status words: two flag bits over a 30-bit count.
+constexpr uint32_t kFlagAggregate = 1u << 30;
+constexpr uint32_t kFlagInclusive = 2u << 30;
+constexpr uint32_t kValueMask = (1u << 30) - 1u;
+constexpr uint32_t kMaxItems = kValueMask;           // counts must fit 30 bits
+
+// Bound on the spin iterations of one look-back step. A predecessor tile is
+// always resident (tiles are numbered in the order blocks start), so the
+// bound is never reached in a correct launch; reaching it sets bit 0 of the
+// error word and the wait gives up.
+constexpr uint32_t kSpinLimit = 1u << 24;
 
 inline uint32_t tiles_for(uint32_t count) { return (count + kTile - 1) / kTile; }
 
-// Scratch bytes needed by sort_pairs / exclusive_scan for `count` items.
+// Scratch bytes needed by sort_pairs for `count` items.
 uint64_t sort_scratch_bytes(uint32_t count);
+// Scratch bytes needed by exclusive_scan for `count` items.
 uint64_t scan_scratch_bytes(uint32_t count);
 
 // Stable sort of keys[0, count) by bits [begin_bit, end_bit) of the key.
 // keys/vals hold the input and receive the output; alt_keys/alt_vals are
-// ping-pong buffers of the same size. scratch holds sort_scratch_bytes(count).
+// ping-pong buffers of the same size. scratch holds sort_scratch_bytes(count)
+// bytes; error (may be null) receives bit 0 if a look-back wait gave up.
+// Launches: one memset, one histogram kernel, one kernel per 8-bit pass
+// (plus two copies when the pass count is odd).
 cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals,
                        uint32_t count, int begin_bit, int end_bit, void* scratch,
-                       cudaStream_t stream);
+                       cudaStream_t stream, uint32_t* error = nullptr);
 
 // out[i] = sum(in[gather[j]] for j < i) when gather != nullptr, else
 // sum(in[j] for j < i); *total = the full sum. out may alias in when
-// gather == nullptr (each thread reads its items before writing them).
+// gather == nullptr. One memset and one kernel.
 cudaError_t exclusive_scan(const uint32_t* in, const uint32_t* gather, uint32_t* out,
-                           uint32_t* total, uint32_t count, void* scratch, cudaStream_t stream);
+                           uint32_t* total, uint32_t count, void* scratch, cudaStream_t stream,
+                           uint32_t* error = nullptr);
 
 // Number of bits needed to hold values in [0, n): the reference's
 // getHigherMsb(n) for the tile count (sort.cu:141-156).
@@ -44,6 +69,56 @@ inline int bits_for_tiles(uint32_t n) {
     int bits = 0;
     while (bits < 32 && (n >> bits) != 0u) ++bits;
     return bits;
+}
+
+// ---- device helpers shared with the fused scan-and-emit kernels ----
+
+__device__ __forceinline__ uint32_t load_status(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void store_status(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Exclusive prefix of `status[tile * stride]` over all earlier tiles, by
+// decoupled look-back. The caller has already published its own aggregate.
+// Eight predecessors are read per step, so a chain of tiles that have only
+// published aggregates costs one memory round trip per eight tiles.
+constexpr int kLookBackWindow = 8;
+
+__device__ __forceinline__ uint32_t look_back(const uint32_t* status, uint32_t tile,
+                                              uint32_t stride, uint32_t* error) {
+    uint32_t prefix = 0;
+    int64_t t = static_cast<int64_t>(tile) - 1;
+    uint32_t spins = 0;
+    while (t >= 0) {
+        uint32_t s[kLookBackWindow];
+#pragma unroll
+        for (int k = 0; k < kLookBackWindow; ++k) {
+            s[k] = t - k >= 0 ? load_status(status + static_cast<uint64_t>(t - k) * stride)
+                              : kFlagInclusive;
+        }
+        int k = 0;
+#pragma unroll
+        for (int i = 0; i < kLookBackWindow; ++i) {
+            if (k != i || (s[i] & ~kValueMask) == 0u) continue;  // stopped, or not published yet
+            prefix += s[i] & kValueMask;
+            if ((s[i] & kFlagInclusive) != 0u) return prefix;
+            k = i + 1;
+        }
+        if (k == 0) {
+            if (++spins > kSpinLimit) {
+                if (error != nullptr) atomicOr(error, 1u);
+                return prefix;
+            }
+            __nanosleep(32);
+        }
+        t -= k;
+    }
+    return prefix;
 }
 
 }  // namespace sort

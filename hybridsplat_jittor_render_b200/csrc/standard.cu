@@ -2,21 +2,26 @@
 //
 // Pipeline (reference full_rasterizer.cu:203-394):
 //   preprocess  one thread per Gaussian: near cull, 2DGS transform, facing
-//               flip, screen-space AABB and tile rectangle; writes an 80-byte
-//               blend record (centre, normal, opacity, 5 colours, Tu/Tv/Tw),
-//               the depth key, the rectangle and radii[P].
-//   depth sort  stable radix sort by the depth bits (ties keep index order).
-//   offsets     exclusive scan of rectangle areas in depth order; the total is
-//               `rendered` (read back once, like the reference's D2H copy at
-//               full_rasterizer.cu:309-320).
-//   emit        every tile of each rectangle, in depth order.
-//   tile sort   stable radix sort by tile id: the result is the reference's
-//               (tile|depth key, index) order (full_rasterizer.cu:127-153,
-//               345-355).
+//               flip, screen-space AABB and tile rectangle (radii[P]); writes
+//               an 80-byte blend record and a 48-byte cull shape (the region
+//               where the Gaussian can reach alpha >= 1/255); counts the
+//               reference's pairs (`rendered`) and the pairs it will emit.
+//               One 12-byte readback of those totals replaces the reference's
+//               D2H copy of num_rendered (full_rasterizer.cu:309-320); the
+//               host waits for it while the depth sort runs.
+//   depth sort  stable onesweep radix sort by the depth bits (ties keep
+//               index order).
+//   scan+emit   one kernel: exclusive scan of the emitted counts in depth
+//               order and warp-cooperative emission of (tile, index | quadrant
+//               mask) pairs.
+//   tile sort   stable radix sort by tile id: per tile, the Gaussians keep the
+//               reference's (depth key, index) order (full_rasterizer.cu:
+//               127-153, 345-355).
 //   ranges      per-tile [start, end).
-//   render      128 threads per 16x16 tile, 2 pixels per thread, per-pixel
-//               termination as in forward.cu:323-422; the per-Gaussian blend
-//               weights are summed across each warp before one atomicAdd.
+//   render      128 threads per 16x16 tile, one warp per 8x8 quadrant, two
+//               pixels per lane, per-pixel termination as in
+//               forward.cu:323-422; pairs whose quadrant bit is clear are
+//               skipped (they cannot reach alpha >= 1/255 there).
 #include <algorithm>
 #include <climits>
 
@@ -37,36 +42,34 @@ namespace {
 uint64_t geometry_bytes(uint64_t count) {
     Carver c(nullptr);
     c.take<float4>(count * kRecordQuads);
-    c.take<uint2>(count);
-    for (int k = 0; k < 6; ++k) c.take<uint32_t>(count);
+    c.take<float4>(count * kCullQuads);
+    for (int k = 0; k < 5; ++k) c.take<uint32_t>(count);
     c.take<uint32_t>(64);
     return c.offset;
 }
 
 struct GeometryViews {
     float4* records;
-    uint2* rects;
+    float4* cull;
     uint32_t* keys;
     uint32_t* order;
     uint32_t* counts;
     uint32_t* alt_keys;
     uint32_t* alt_order;
-    uint32_t* offsets;
-    uint32_t* total;  // [0] pair total, [1] error flag
+    uint32_t* totals;  // [0] reference pairs, [1] prefiltered violation, [2] emitted pairs, [3] errors
 };
 
 GeometryViews geometry_views(void* base, uint64_t count) {
     Carver c(base);
     GeometryViews v;
     v.records = c.take<float4>(count * kRecordQuads);
-    v.rects = c.take<uint2>(count);
+    v.cull = c.take<float4>(count * kCullQuads);
     v.keys = c.take<uint32_t>(count);
     v.order = c.take<uint32_t>(count);
     v.counts = c.take<uint32_t>(count);
     v.alt_keys = c.take<uint32_t>(count);
     v.alt_order = c.take<uint32_t>(count);
-    v.offsets = c.take<uint32_t>(count);
-    v.total = c.take<uint32_t>(64);
+    v.totals = c.take<uint32_t>(64);
     return v;
 }
 
@@ -136,15 +139,21 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
     // Geometry: per-Gaussian views followed by the depth-sort / scan scratch.
     const uint64_t geometry_used = geometry_bytes(count);
     const uint64_t geometry_scratch_bytes =
-        std::max(sort::sort_scratch_bytes(point_count), sort::scan_scratch_bytes(point_count));
+        std::max(sort::sort_scratch_bytes(point_count), bin::scan_scratch_bytes(point_count));
     cudaError_t st = ensure_buffer(ctx->std_geometry, geometry_used + geometry_scratch_bytes,
-                                   &ctx->std_growth_count);
+                                   &ctx->std_growth_count, true);
     if (st != cudaSuccess) return st;
-    st = ensure_buffer(ctx->std_image, tiles * sizeof(uint2), &ctx->std_growth_count);
+    st = ensure_buffer(ctx->std_image, tiles * sizeof(uint2), &ctx->std_growth_count, true);
     if (st != cudaSuccess) return st;
     if (ctx->std_total_host == nullptr) {
-        st = cudaHostAlloc(reinterpret_cast<void**>(&ctx->std_total_host), 2 * sizeof(uint32_t),
+        st = cudaHostAlloc(reinterpret_cast<void**>(&ctx->std_total_host), 4 * sizeof(uint32_t),
                            cudaHostAllocPortable);
+        if (st != cudaSuccess) return st;
+    }
+    st = ensure_device_error(ctx);
+    if (st != cudaSuccess) return st;
+    if (ctx->std_count_event == nullptr) {
+        st = cudaEventCreateWithFlags(&ctx->std_count_event, cudaEventDisableTiming);
         if (st != cudaSuccess) return st;
     }
     ctx->std_peak_bytes = std::max(ctx->std_peak_bytes, standard_current_bytes(ctx));
@@ -153,61 +162,89 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
     uint2* ranges = static_cast<uint2*>(ctx->std_image.ptr);
 
     st = cudaMemsetAsync(output_weight, 0, count * sizeof(float), stream);
-    if (st == cudaSuccess) st = cudaMemsetAsync(gv.total, 0, 2 * sizeof(uint32_t), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(gv.totals, 0, 4 * sizeof(uint32_t), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(ranges, 0, tiles * sizeof(uint2), stream);
     if (st != cudaSuccess) return st;
     const int blocks = (point_count + kPreThreads - 1) / kPreThreads;
+    PreprocessOut po{gv.records, gv.cull, gv.keys, gv.order, gv.counts, output_radii, gv.totals,
+                     ctx->device_error};
     preprocess_kernel<HS_STANDARD_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
         point_count, viewmatrix4x4, projmatrix4x4, width, height, grid_x, grid_y, means3d,
-        colors5, opacities, scales2, scale_modifier, rotations4, prefiltered ? 1 : 0, gv.records,
-        gv.rects, gv.keys, gv.order, gv.counts, output_radii, gv.total + 1);
+        colors5, opacities, scales2, scale_modifier, rotations4, prefiltered ? 1 : 0, po);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
-    marks.mark(1);
-    st = sort::sort_pairs(gv.keys, gv.order, gv.alt_keys, gv.alt_order, point_count, 0, 32,
-                          geometry_scratch, stream);
-    if (st != cudaSuccess) return st;
-    st = sort::exclusive_scan(gv.counts, gv.order, gv.offsets, gv.total, point_count,
-                              geometry_scratch, stream);
-    if (st != cudaSuccess) return st;
-    st = cudaMemcpyAsync(ctx->std_total_host, gv.total, 2 * sizeof(uint32_t),
+    st = cudaMemcpyAsync(ctx->std_total_host, gv.totals, 4 * sizeof(uint32_t),
                          cudaMemcpyDeviceToHost, stream);
+    if (st == cudaSuccess) st = cudaEventRecord(ctx->std_count_event, stream);
     if (st != cudaSuccess) return st;
-    st = cudaStreamSynchronize(stream);
+    marks.mark(1);
+    // The depth sort does not depend on the totals: queue it before waiting.
+    st = sort::sort_pairs(gv.keys, gv.order, gv.alt_keys, gv.alt_order, point_count, 0, 32,
+                          geometry_scratch, stream, ctx->device_error);
+    if (st != cudaSuccess) return st;
+    st = cudaEventSynchronize(ctx->std_count_event);
     if (st != cudaSuccess) return st;
     const uint32_t rendered = ctx->std_total_host[0];
+    const uint32_t emitted = ctx->std_total_host[2];
+    if (ctx->std_total_host[3] != 0) return cudaErrorLaunchTimeout;  // a look-back wait gave up
     if (ctx->std_total_host[1] != 0) return kPrefilteredViolation;
-    if (rendered > static_cast<uint32_t>(INT_MAX)) return cudaErrorInvalidValue;
-    st = cudaMemcpyAsync(output_rendered, gv.total, sizeof(int32_t), cudaMemcpyDeviceToDevice,
+    if (rendered > static_cast<uint32_t>(INT_MAX) || emitted > sort::kMaxItems) {
+        return cudaErrorInvalidValue;
+    }
+    st = cudaMemcpyAsync(output_rendered, gv.totals, sizeof(int32_t), cudaMemcpyDeviceToDevice,
                          stream);
     if (st != cudaSuccess) return st;
 
-    uint32_t* ids = nullptr;
-    if (rendered > 0) {
-        st = ensure_buffer(ctx->std_binning, binning_bytes(rendered), &ctx->std_growth_count);
+    const bool masked = count <= static_cast<uint64_t>(kIndexMask) + 1u;
+    uint32_t* values = nullptr;
+    if (emitted > 0) {
+        st = ensure_buffer(ctx->std_binning, binning_bytes(emitted), &ctx->std_growth_count, true);
         if (st != cudaSuccess) return st;
         ctx->std_peak_bytes = std::max(ctx->std_peak_bytes, standard_current_bytes(ctx));
         Carver c(ctx->std_binning.ptr);
-        uint32_t* tile_ids = c.take<uint32_t>(rendered);
-        ids = c.take<uint32_t>(rendered);
-        uint32_t* alt_tiles = c.take<uint32_t>(rendered);
-        uint32_t* alt_ids = c.take<uint32_t>(rendered);
-        void* scratch = c.take<unsigned char>(sort::sort_scratch_bytes(rendered));
-        emit_kernel<<<blocks, kPreThreads, 0, stream>>>(point_count, grid_x, gv.order, gv.counts,
-                                                        gv.offsets, gv.rects, tile_ids, ids);
+        uint32_t* tile_ids = c.take<uint32_t>(emitted);
+        values = c.take<uint32_t>(emitted);
+        uint32_t* alt_tiles = c.take<uint32_t>(emitted);
+        uint32_t* alt_values = c.take<uint32_t>(emitted);
+        void* scratch = c.take<unsigned char>(sort::sort_scratch_bytes(emitted));
+        st = cudaMemsetAsync(geometry_scratch, 0, bin::scan_scratch_bytes(point_count), stream);
+        if (st != cudaSuccess) return st;
+        // alt_keys is free once the depth sort has finished: it receives the
+        // first pair slot of every Gaussian.
+        uint32_t* first_pair = gv.alt_keys;
+        bin::offsets_kernel<<<bin::scan_tiles(point_count), bin::kScanThreads, 0, stream>>>(
+            static_cast<uint32_t>(point_count), gv.order, gv.counts,
+            static_cast<uint32_t*>(geometry_scratch), ctx->device_error, first_pair);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
-        st = sort::sort_pairs(tile_ids, ids, alt_tiles, alt_ids, rendered, 0,
-                              sort::bits_for_tiles(static_cast<uint32_t>(tiles)), scratch, stream);
+        const Emitter em{gv.cull, grid_x, masked};
+        bin::emit_kernel<Emitter>
+            <<<(point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
+               stream>>>(static_cast<uint32_t>(point_count), gv.counts, first_pair, em, tile_ids,
+                         values);
+        st = cudaGetLastError();
         if (st != cudaSuccess) return st;
-        ranges_kernel<<<(rendered + 255) / 256, 256, 0, stream>>>(rendered, tile_ids, ranges);
+        st = sort::sort_pairs(tile_ids, values, alt_tiles, alt_values, emitted, 0,
+                              sort::bits_for_tiles(static_cast<uint32_t>(tiles)), scratch, stream,
+                              ctx->device_error);
+        if (st != cudaSuccess) return st;
+        bin::ranges_kernel<uint2><<<(emitted + 255) / 256, 256, 0, stream>>>(
+            emitted, static_cast<uint32_t>(tiles), tile_ids, ranges);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
     }
     marks.mark(2);
-    render_kernel<HS_STANDARD_ROUNDING><<<static_cast<unsigned>(tiles), kRenderThreads, 0, stream>>>(
-        ranges, ids, gv.records, width, height, grid_x, background5, output_color5, output_aux7,
-        output_weight);
+    if (masked) {
+        render_kernel<HS_STANDARD_ROUNDING, true>
+            <<<static_cast<unsigned>(tiles), kRenderThreads, 0, stream>>>(
+                ranges, values, gv.records, width, height, grid_x, background5, output_color5,
+                output_aux7, output_weight);
+    } else {
+        render_kernel<HS_STANDARD_ROUNDING, false>
+            <<<static_cast<unsigned>(tiles), kRenderThreads, 0, stream>>>(
+                ranges, values, gv.records, width, height, grid_x, background5, output_color5,
+                output_aux7, output_weight);
+    }
     return cudaGetLastError();
 }
 

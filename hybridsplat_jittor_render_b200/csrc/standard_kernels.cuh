@@ -2,101 +2,183 @@
 // by standard.cu with the pinned policy; see standard.cu for the pipeline.
 #pragma once
 
+#include "binning.cuh"
 #include "standard_math.cuh"
 
 namespace hs {
 namespace st {
 
-
 constexpr int kPreThreads = 128;
-constexpr int kRenderThreads = 128;
-constexpr int kBatch = 32;
-constexpr int kRecordQuads = 5;
+constexpr int kRenderThreads = 128;  // 4 warps, one 8x8 quadrant each
+constexpr int kRecordQuads = 5;      // 80-byte blend record
+constexpr int kCullQuads = 4;        // 64-byte cull shape + clipped rectangle
+// Pair values carry the Gaussian index in the low 28 bits and the quadrant
+// mask in the top 4 when the point count allows it.
+constexpr uint32_t kIndexBits = 28;
+constexpr uint32_t kIndexMask = (1u << kIndexBits) - 1u;
 
+struct PreprocessOut {
+    float4* records;
+    float4* cull;            // kCullQuads per Gaussian
+    uint32_t* depth_keys;
+    uint32_t* order;
+    uint32_t* counts;        // pairs emitted per Gaussian
+    int32_t* radii;
+    uint32_t* totals;        // [0] reference pair count, [1] prefiltered violation, [2] emitted,
+                             // [3] copy of the context's look-back error word
+    const uint32_t* error;   // the context's look-back error word
+};
+
+__device__ __forceinline__ void warp_add(uint32_t* dst, uint32_t v) {
+    v = bin::warp_sum(v);
+    if ((threadIdx.x & 31) == 0 && v != 0u) atomicAdd(dst, v);
+}
+
+// preprocessCUDA<5> (forward.cu:148-251) plus the cull shape. A Gaussian
+// emits the tiles of its reference rectangle (getRect) that also lie in the
+// bounding box of its live region; `rendered` still counts the whole
+// rectangle, as the reference does.
 template <class R>
 __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     int point_count, const float* __restrict__ viewmatrix, const float* __restrict__ projmatrix,
     int width, int height, uint32_t grid_x, uint32_t grid_y, const float* __restrict__ means,
     const float* __restrict__ colors5, const float* __restrict__ opacities,
     const float* __restrict__ scales, float scale_modifier, const float* __restrict__ rotations,
-    int prefiltered, float4* __restrict__ records, uint2* __restrict__ rects,
-    uint32_t* __restrict__ depth_keys, uint32_t* __restrict__ order,
-    uint32_t* __restrict__ pair_counts, int32_t* __restrict__ radii,
-    uint32_t* __restrict__ error_flag) {
+    int prefiltered, PreprocessOut out) {
     const int idx = blockIdx.x * kPreThreads + threadIdx.x;
-    if (idx >= point_count) return;
+    const bool active = idx < point_count;
     const R r;
+    __shared__ float m[32];
+    if (threadIdx.x < 16) m[threadIdx.x] = viewmatrix[threadIdx.x];
+    else if (threadIdx.x < 32) m[threadIdx.x] = projmatrix[threadIdx.x - 16];
+    __syncthreads();
     float view[16], proj[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) {
-        view[k] = viewmatrix[k];
-        proj[k] = projmatrix[k];
+        view[k] = m[k];
+        proj[k] = m[16 + k];
     }
-    const float3 p = make_float3(means[3 * idx], means[3 * idx + 1], means[3 * idx + 2]);
-    const float2 scale = make_float2(scales[2 * idx], scales[2 * idx + 1]);
-    const float4 rot = make_float4(rotations[4 * idx], rotations[4 * idx + 1],
-                                   rotations[4 * idx + 2], rotations[4 * idx + 3]);
-    const Projected g =
-        project_gaussian(r, view, proj, p, scale, scale_modifier, rot, width, height, grid_x, grid_y);
-    if (g.behind && prefiltered) atomicOr(error_flag, 1u);
-    order[idx] = static_cast<uint32_t>(idx);
-    if (!g.valid) {
-        radii[idx] = 0;
-        pair_counts[idx] = 0;
-        depth_keys[idx] = 0xffffffffu;
-        return;
-    }
-    const float op = opacities[idx];
-    const float* c = colors5 + 5 * static_cast<size_t>(idx);
-    float4* rec = records + static_cast<size_t>(idx) * kRecordQuads;
-    rec[0] = make_float4(g.xy.x, g.xy.y, g.normal.x, g.normal.y);
-    rec[1] = make_float4(g.normal.z, op, c[0], c[1]);
-    rec[2] = make_float4(c[2], c[3], c[4], g.tu.x);
-    rec[3] = make_float4(g.tu.y, g.tu.z, g.tv.x, g.tv.y);
-    rec[4] = make_float4(g.tv.z, g.tw.x, g.tw.y, g.tw.z);
-    rects[idx] = make_uint2(g.rect_min.x | (g.rect_min.y << 16), g.rect_max.x | (g.rect_max.y << 16));
-    radii[idx] = static_cast<int32_t>(g.radius);
-    pair_counts[idx] = (g.rect_max.x - g.rect_min.x) * (g.rect_max.y - g.rect_min.y);
-    depth_keys[idx] = __float_as_uint(g.depth);
-}
-
-__global__ void __launch_bounds__(kPreThreads) emit_kernel(
-    int point_count, uint32_t grid_x, const uint32_t* __restrict__ order,
-    const uint32_t* __restrict__ pair_counts, const uint32_t* __restrict__ offsets,
-    const uint2* __restrict__ rects, uint32_t* __restrict__ tile_ids,
-    uint32_t* __restrict__ gaussian_ids) {
-    const int s = blockIdx.x * kPreThreads + threadIdx.x;
-    if (s >= point_count) return;
-    const uint32_t gid = order[s];
-    if (pair_counts[gid] == 0) return;
-    const uint2 rc = rects[gid];
-    const uint32_t x0 = rc.x & 0xffff, y0 = rc.x >> 16, x1 = rc.y & 0xffff, y1 = rc.y >> 16;
-    uint32_t out = offsets[s];
-    for (uint32_t y = y0; y < y1; ++y) {
-        for (uint32_t x = x0; x < x1; ++x) {
-            tile_ids[out] = y * grid_x + x;
-            gaussian_ids[out] = gid;
-            ++out;
+    if (blockIdx.x == 0 && threadIdx.x == 0) out.totals[3] = *out.error;
+    uint32_t area = 0, emitted = 0, violation = 0;
+    if (active) {
+        const float3 p = make_float3(means[3 * idx], means[3 * idx + 1], means[3 * idx + 2]);
+        const float2 scale = make_float2(scales[2 * idx], scales[2 * idx + 1]);
+        const float4 rot = make_float4(rotations[4 * idx], rotations[4 * idx + 1],
+                                       rotations[4 * idx + 2], rotations[4 * idx + 3]);
+        const Projected g = project_gaussian(r, view, proj, p, scale, scale_modifier, rot, width,
+                                             height, grid_x, grid_y);
+        violation = (g.behind && prefiltered) ? 1u : 0u;
+        out.order[idx] = static_cast<uint32_t>(idx);
+        if (!g.valid) {
+            out.radii[idx] = 0;
+            out.counts[idx] = 0;
+            out.depth_keys[idx] = 0xffffffffu;
+        } else {
+            const float op = opacities[idx];
+            const float* c = colors5 + 5 * static_cast<size_t>(idx);
+            float4* rec = out.records + static_cast<size_t>(idx) * kRecordQuads;
+            rec[0] = make_float4(g.xy.x, g.xy.y, g.normal.x, g.normal.y);
+            rec[1] = make_float4(g.normal.z, op, c[0], c[1]);
+            rec[2] = make_float4(c[2], c[3], c[4], g.tu.x);
+            rec[3] = make_float4(g.tu.y, g.tu.z, g.tv.x, g.tv.y);
+            rec[4] = make_float4(g.tv.z, g.tw.x, g.tw.y, g.tw.z);
+            area = (g.rect_max.x - g.rect_min.x) * (g.rect_max.y - g.rect_min.y);
+            const CullShape cs = cull_shape(op, g.xy.x, g.xy.y, g.tu, g.tv, g.tw);
+            int bx0, by0, bx1, by1;
+            int x0 = 0, y0 = 0, x1 = 0, y1 = 0;
+            if (cull_tile_box(cs, bx0, by0, bx1, by1)) {
+                x0 = max(static_cast<int>(g.rect_min.x), bx0);
+                y0 = max(static_cast<int>(g.rect_min.y), by0);
+                x1 = min(static_cast<int>(g.rect_max.x), bx1 + 1);
+                y1 = min(static_cast<int>(g.rect_max.y), by1 + 1);
+                if (x1 <= x0 || y1 <= y0) x0 = y0 = x1 = y1 = 0;
+            }
+            emitted = static_cast<uint32_t>((x1 - x0) * (y1 - y0));
+            float4* cu = out.cull + static_cast<size_t>(idx) * kCullQuads;
+            cu[0] = make_float4(cs.mx, cs.my, cs.cs, cs.sn);
+            cu[1] = make_float4(cs.ia, cs.ib, cs.ryx, cs.rxy);
+            cu[2] = make_float4(cs.gx, cs.gy, cs.r2, __int_as_float(cs.mode));
+            cu[3] = make_float4(__uint_as_float(static_cast<uint32_t>(x0) | (static_cast<uint32_t>(y0) << 16)),
+                                __uint_as_float(static_cast<uint32_t>(x1) | (static_cast<uint32_t>(y1) << 16)),
+                                0.0f, 0.0f);
+            out.radii[idx] = static_cast<int32_t>(g.radius);
+            out.counts[idx] = emitted;
+            out.depth_keys[idx] = emitted != 0 ? __float_as_uint(g.depth) : 0xffffffffu;
         }
     }
+    warp_add(out.totals + 0, area);
+    warp_add(out.totals + 1, violation);
+    warp_add(out.totals + 2, emitted);
 }
 
-__global__ void ranges_kernel(uint32_t pair_count, const uint32_t* __restrict__ tile_ids,
-                              uint2* __restrict__ ranges) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= pair_count) return;
-    const uint32_t t = tile_ids[i];
-    if (i == 0) {
-        ranges[t].x = 0;
-    } else {
-        const uint32_t prev = tile_ids[i - 1];
-        if (t != prev) {
-            ranges[prev].y = i;
-            ranges[t].x = i;
+// Emits, for one Gaussian, every tile of its clipped rectangle with the mask
+// of the 8x8 quadrants that may hold a live pixel.
+struct Emitter {
+    const float4* cull;
+    uint32_t grid_x;
+    bool masked;
+
+    struct Shape {
+        float4 a, b, c;
+        float2 d;
+    };
+    __device__ __forceinline__ Shape load(uint32_t gid) const {
+        const float4* p = cull + static_cast<size_t>(gid) * kCullQuads;
+        const float4 d = p[3];
+        return Shape{p[0], p[1], p[2], make_float2(d.x, d.y)};
+    }
+    __device__ __forceinline__ static float4 shfl4(float4 v, int src) {
+        return make_float4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
+                           __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
+    }
+    __device__ __forceinline__ Shape shfl(const Shape& s, int src) const {
+        return Shape{shfl4(s.a, src), shfl4(s.b, src), shfl4(s.c, src),
+                     make_float2(__shfl_sync(0xffffffffu, s.d.x, src),
+                                 __shfl_sync(0xffffffffu, s.d.y, src))};
+    }
+    __device__ __forceinline__ static CullShape unpack(const Shape& s) {
+        CullShape c;
+        c.mx = s.a.x; c.my = s.a.y; c.cs = s.a.z; c.sn = s.a.w;
+        c.ia = s.b.x; c.ib = s.b.y; c.ryx = s.b.z; c.rxy = s.b.w;
+        c.gx = s.c.x; c.gy = s.c.y; c.r2 = s.c.z; c.mode = __float_as_int(s.c.w);
+        return c;
+    }
+    __device__ __forceinline__ bool small(const Shape& s) const {
+        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
+        return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16)) <= 8u;
+    }
+    __device__ __forceinline__ void emit_serial(const Shape& s, uint32_t gid, uint32_t offset,
+                                                uint32_t count, uint32_t* tiles,
+                                                uint32_t* values) const {
+        const CullShape c = unpack(s);
+        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
+        const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff, y1 = hi >> 16;
+        uint32_t at = offset;
+        for (int ty = y0; ty < y1; ++ty) {
+            for (int tx = x0; tx < x1; ++tx, ++at) {
+                tiles[at] = static_cast<uint32_t>(ty) * grid_x + static_cast<uint32_t>(tx);
+                values[at] = masked ? (gid | (cull_quadrants(c, tx, ty) << kIndexBits)) : gid;
+            }
+        }
+        (void)count;
+    }
+    __device__ __forceinline__ void emit(const Shape& s, uint32_t gid, uint32_t offset,
+                                         uint32_t count, int lane, uint32_t* tiles,
+                                         uint32_t* values) const {
+        CullShape c;
+        c.mx = s.a.x; c.my = s.a.y; c.cs = s.a.z; c.sn = s.a.w;
+        c.ia = s.b.x; c.ib = s.b.y; c.ryx = s.b.z; c.rxy = s.b.w;
+        c.gx = s.c.x; c.gy = s.c.y; c.r2 = s.c.z; c.mode = __float_as_int(s.c.w);
+        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
+        const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff;
+        const int w = x1 - x0;
+        for (uint32_t t = lane; t < count; t += 32) {
+            const int ty = y0 + static_cast<int>(t) / w, tx = x0 + static_cast<int>(t) % w;
+            tiles[offset + t] = static_cast<uint32_t>(ty) * grid_x + static_cast<uint32_t>(tx);
+            values[offset + t] = masked ? (gid | (cull_quadrants(c, tx, ty) << kIndexBits)) : gid;
         }
     }
-    if (i == pair_count - 1) ranges[t].y = pair_count;
-}
+};
 
 __device__ __forceinline__ BlendRecord load_record(const float4* q) {
     const float4 a = q[0], b = q[1], c = q[2], d = q[3], e = q[4];
@@ -125,55 +207,74 @@ __device__ __forceinline__ void store_pixel(const R& r, const PixelState& s,
     aux[6 * plane + pix] = s.dist;
 }
 
-template <class R>
+// renderCUDA<5> (forward.cu:256-445). Every pixel blends its tile's list in
+// order and stops on its own (forward.cu:323-328, 398-402), so each warp can
+// run on its own: warp q owns the 8x8 quadrant q of the tile (two pixels per
+// lane, rows ly and ly + 4) and walks the tile's list 32 pairs at a time,
+// keeping the pairs whose quadrant bit is set. Their records are staged in
+// the warp's shared-memory slots, then blended in list order. The warp stops
+// when its 64 pixels are done. Blend weights are summed across the warp
+// before one atomicAdd per Gaussian.
+template <class R, bool kMasked>
 __global__ void __launch_bounds__(kRenderThreads) render_kernel(
-    const uint2* __restrict__ ranges, const uint32_t* __restrict__ gaussian_ids,
+    const uint2* __restrict__ ranges, const uint32_t* __restrict__ pair_values,
     const float4* __restrict__ records, int width, int height, uint32_t grid_x,
     const float* __restrict__ background5, float* __restrict__ color, float* __restrict__ aux,
     float* __restrict__ weight) {
-    __shared__ float4 batch[kBatch * kRecordQuads];
-    __shared__ uint32_t batch_ids[kBatch];
+    __shared__ float4 slots[kRenderThreads / 32][32 * kRecordQuads];
+    __shared__ uint32_t slot_ids[kRenderThreads / 32][32];
     const R r;
     const uint32_t tile = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int tx = tile % grid_x, ty = tile / grid_x;
-    const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4;
-    const int px = tx * 16 + lx, py0 = ty * 16 + ly, py1 = py0 + 8;
+    const int px = tx * 16 + (warp & 1) * 8 + (lane & 7);
+    const int py0 = ty * 16 + (warp >> 1) * 8 + (lane >> 3), py1 = py0 + 4;
     const bool in0 = px < width && py0 < height;
     const bool in1 = px < width && py1 < height;
     const float fx = static_cast<float>(px);
     const float fy0 = static_cast<float>(py0), fy1 = static_cast<float>(py1);
-    float bg[5];
-#pragma unroll
-    for (int k = 0; k < 5; ++k) bg[k] = background5[k];
     PixelState s0, s1;
     pixel_init(s0, in0);
     pixel_init(s1, in1);
     const uint2 range = ranges[tile];
-    const int n = static_cast<int>(range.y - range.x);
-    const int lane = threadIdx.x & 31;
-    for (int base = 0; base < n; base += kBatch) {
-        // Stop once every pixel of the tile is done (forward.cu:326-328).
-        if (__syncthreads_and(s0.done && s1.done)) break;
-        const int nb = min(kBatch, n - base);
-        for (int i = threadIdx.x; i < nb * kRecordQuads; i += kRenderThreads) {
-            const int j = i / kRecordQuads, q = i - j * kRecordQuads;
-            const uint32_t gid = gaussian_ids[range.x + base + j];
-            if (q == 0) batch_ids[j] = gid;
-            batch[i] = records[static_cast<size_t>(gid) * kRecordQuads + q];
-        }
-        __syncthreads();
-        if (!__all_sync(0xffffffffu, s0.done && s1.done)) {
-            for (int j = 0; j < nb; ++j) {
-                const BlendRecord g = load_record(batch + j * kRecordQuads);
-                float w = blend(r, s0, fx, fy0, g);
-                w += blend(r, s1, fx, fy1, g);
+    const uint32_t n = range.y - range.x;
+    const uint32_t lt = (1u << lane) - 1u;
+    float4* my_slots = slots[warp];
+    uint32_t* my_ids = slot_ids[warp];
+    for (uint32_t base = 0; base < n; base += 32) {
+        if (__all_sync(0xffffffffu, s0.done && s1.done)) break;
+        const uint32_t j = base + lane;
+        const uint32_t v = j < n ? pair_values[range.x + j] : 0u;
+        const bool live = j < n && (!kMasked || ((v >> (kIndexBits + warp)) & 1u) != 0u);
+        const uint32_t mask = __ballot_sync(0xffffffffu, live);
+        if (live) {
+            const uint32_t gid = kMasked ? (v & kIndexMask) : v;
+            const uint32_t slot = __popc(mask & lt);
+            const float4* src = records + static_cast<size_t>(gid) * kRecordQuads;
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) w += __shfl_xor_sync(0xffffffffu, w, off);
-                if (lane == 0 && w != 0.0f) atomicAdd(weight + batch_ids[j], w);
+            for (int q = 0; q < kRecordQuads; ++q) my_slots[slot * kRecordQuads + q] = src[q];
+            my_ids[slot] = gid;
+        }
+        __syncwarp();
+        const int live_count = __popc(mask);
+        for (int k = 0; k < live_count; ++k) {
+            const BlendRecord g = load_record(my_slots + k * kRecordQuads);
+            float w = blend(r, s0, fx, fy0, g);
+            w += blend(r, s1, fx, fy1, g);
+            if (__any_sync(0xffffffffu, w != 0.0f)) {
+                w = w + __shfl_xor_sync(0xffffffffu, w, 16);
+                w = w + __shfl_xor_sync(0xffffffffu, w, 8);
+                w = w + __shfl_xor_sync(0xffffffffu, w, 4);
+                w = w + __shfl_xor_sync(0xffffffffu, w, 2);
+                w = w + __shfl_xor_sync(0xffffffffu, w, 1);
+                if (lane == 0 && w != 0.0f) atomicAdd(weight + my_ids[k], w);
             }
         }
-        __syncthreads();
+        __syncwarp();
     }
+    float bg[5];
+#pragma unroll
+    for (int k = 0; k < 5; ++k) bg[k] = background5[k];
     const size_t plane = static_cast<size_t>(width) * height;
     if (in0) store_pixel(r, s0, bg, color, aux, plane, static_cast<size_t>(py0) * width + px);
     if (in1) store_pixel(r, s1, bg, color, aux, plane, static_cast<size_t>(py1) * width + px);

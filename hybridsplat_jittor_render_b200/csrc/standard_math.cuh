@@ -10,6 +10,8 @@
 // it has its own pinned rounding policy.
 #pragma once
 
+#include <climits>
+
 #include "splat_math.cuh"
 
 namespace hs {
@@ -194,6 +196,151 @@ __device__ __forceinline__ float blend(const R& r, PixelState& s, float px, floa
     for (int k = 0; k < 5; ++k) s.c[k] = mad(va, g.c[k], w, s.c[k]);
     s.t = test_t;
     return w;
+}
+
+// ---------------------------------------------------------------- culling
+//
+// A pixel x Gaussian evaluation changes the pixel state only when
+// alpha = min(0.99, op * expf(-rho / 2)) >= 1/255 (forward.cu:392-393; the
+// median, depth, normal and colour updates all follow that test). Since
+// 0.99 > 1/255 this needs rho <= c = 2 ln(255 op), and rho = min(rho3d, rho2d)
+// with rho3d = s.s (the ray-splat intersection in splat units) and
+// rho2d = 2 |xy - pixel|^2. So the pixels that can change are inside
+//   * the image of the disc s.s <= c under the splat's homography: an ellipse
+//     with centre m and matrix S, (p - m)^T S^-1 (p - m) <= 1, whenever the
+//     splat plane's horizon stays off the disc (otherwise: no culling); and
+//   * the disc |p - xy|^2 <= c / 2.
+// m and S come from the dual conic of the disc, the same construction the
+// reference uses for its cutoff-3 AABB (forward.cu:119-145) with the cutoff
+// replaced by sqrt(c). The shape is computed in double precision with c
+// widened to 1.02 c + 0.05, and quadrant rectangles are widened by one pixel,
+// so rounding in the per-pixel arithmetic cannot make a culled evaluation
+// live. Culling therefore never changes an output value; it only skips
+// evaluations that would have returned early.
+enum CullMode : int { kCullEllipse = 0, kCullNever = 1, kCullAlways = 2 };
+
+// The ellipse is stored in its axis frame: with X, Y relative to the centre,
+// (u, v) = (cs X + sn Y, cs Y - sn X) and u^2 ia + v^2 ib <= 1. Evaluating
+// squares in the axis frame keeps thin (edge-on) ellipses well conditioned in
+// single precision: rounding moves the boundary by about 1e-7 of the
+// distance to the centre, far below the one-pixel widening of the tested
+// rectangles. ryx and rxy locate the minimum of the form along a vertical or
+// horizontal edge (Y = ryx X, X = rxy Y).
+struct CullShape {
+    float mx, my;     // ellipse centre (pixels)
+    float cs, sn;     // major-axis direction
+    float ia, ib;     // inverse squared semi-axes
+    float ryx, rxy;   // edge minimisers
+    float gx, gy, r2; // disc centre and squared radius
+    int mode;         // kCullEllipse: test; kCullNever: every pixel may be live; kCullAlways: none
+    float hx, hy;     // half extents of the ellipse's bounding box
+};
+
+__device__ __forceinline__ CullShape cull_shape(float op, float x, float y, float3 tu, float3 tv,
+                                                float3 tw) {
+    CullShape c;
+    c.mx = c.my = c.sn = c.ia = c.ib = c.ryx = c.rxy = c.hx = c.hy = 0.0f;
+    c.cs = 1.0f;
+    c.gx = x;
+    c.gy = y;
+    c.r2 = 0.0f;
+    if (!(op > 1.0f / 255.0f)) {  // op * expf(.) < 1/255 everywhere (NaN opacity included)
+        c.mode = kCullAlways;
+        return c;
+    }
+    const double lc = 2.0 * log(255.0 * static_cast<double>(op));
+    const double cw = 1.02 * lc + 0.05;
+    c.r2 = static_cast<float>(0.5 * cw * 1.0001);
+    const double twx = tw.x, twy = tw.y, twz = tw.z;
+    const double d = cw * (twx * twx + twy * twy) - twz * twz;
+    c.mode = kCullNever;
+    if (!(d < -1e-6 * twz * twz)) return c;  // unbounded image of the disc
+    const double fxy = cw / d, fz = -1.0 / d;
+    const double mx = fxy * (double(tu.x) * twx + double(tu.y) * twy) + fz * double(tu.z) * twz;
+    const double my = fxy * (double(tv.x) * twx + double(tv.y) * twy) + fz * double(tv.z) * twz;
+    const double quu = fxy * (double(tu.x) * tu.x + double(tu.y) * tu.y) + fz * double(tu.z) * tu.z;
+    const double qvv = fxy * (double(tv.x) * tv.x + double(tv.y) * tv.y) + fz * double(tv.z) * tv.z;
+    const double quv = fxy * (double(tu.x) * tv.x + double(tu.y) * tv.y) + fz * double(tu.z) * tv.z;
+    const double sxx = mx * mx - quu, syy = my * my - qvv, sxy = mx * my - quv;
+    const double det = sxx * syy - sxy * sxy;
+    if (!(sxx > 0.0 && syy > 0.0 && det > 0.0) || !(fabs(mx) < 1e7 && fabs(my) < 1e7)) return c;
+    const double la = 0.5 * (sxx + syy) + sqrt(0.25 * (sxx - syy) * (sxx - syy) + sxy * sxy);
+    const double lb = det / la;
+    const double th = 0.5 * atan2(2.0 * sxy, sxx - syy);
+    const double cs = cos(th), sn = sin(th);
+    // widen the axes slightly to absorb the rounding of the stored direction
+    const double ia = 1.0 / (la * 1.0002), ib = 1.0 / (lb * 1.0002 + 1e-8 * la);
+    const double axx = cs * cs * ia + sn * sn * ib, ayy = sn * sn * ia + cs * cs * ib;
+    const double axy = cs * sn * (ia - ib);
+    c.mx = static_cast<float>(mx);
+    c.my = static_cast<float>(my);
+    c.cs = static_cast<float>(cs);
+    c.sn = static_cast<float>(sn);
+    c.ia = static_cast<float>(ia);
+    c.ib = static_cast<float>(ib);
+    c.ryx = static_cast<float>(-axy / ayy);
+    c.rxy = static_cast<float>(-axy / axx);
+    c.hx = static_cast<float>(sqrt(sxx) * 1.0003);
+    c.hy = static_cast<float>(sqrt(syy) * 1.0003);
+    c.mode = kCullEllipse;
+    return c;
+}
+
+__device__ __forceinline__ float cull_form(const CullShape& c, float X, float Y) {
+    const float u = c.cs * X + c.sn * Y, v = c.cs * Y - c.sn * X;
+    return u * u * c.ia + v * v * c.ib;
+}
+
+// Can any pixel of [x0, x1] x [y0, y1] (already widened) be live?
+__device__ __forceinline__ bool cull_rect_live(const CullShape& c, float x0, float y0, float x1,
+                                               float y1) {
+    if (c.mode == kCullAlways) return false;
+    if (c.mode == kCullNever) return true;
+    const float cx = fminf(fmaxf(c.gx, x0), x1), cy = fminf(fmaxf(c.gy, y0), y1);
+    const float ddx = cx - c.gx, ddy = cy - c.gy;
+    if (ddx * ddx + ddy * ddy <= c.r2) return true;
+    const float X0 = x0 - c.mx, X1 = x1 - c.mx, Y0 = y0 - c.my, Y1 = y1 - c.my;
+    if (X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f) return true;
+    // Minimum of the form along each edge of the rectangle.
+    const float fa = cull_form(c, X0, fminf(fmaxf(c.ryx * X0, Y0), Y1));
+    const float fb = cull_form(c, X1, fminf(fmaxf(c.ryx * X1, Y0), Y1));
+    const float fc = cull_form(c, fminf(fmaxf(c.rxy * Y0, X0), X1), Y0);
+    const float fd = cull_form(c, fminf(fmaxf(c.rxy * Y1, X0), X1), Y1);
+    return fminf(fminf(fa, fb), fminf(fc, fd)) <= 1.0f;
+}
+
+// Tiles (16 px) that may hold a live pixel: the bounding box of the ellipse
+// and the disc, widened by one pixel. Returns false when there are none.
+__device__ __forceinline__ bool cull_tile_box(const CullShape& c, int& tx0, int& ty0, int& tx1,
+                                              int& ty1) {
+    if (c.mode == kCullAlways) return false;
+    if (c.mode == kCullNever) {
+        tx0 = ty0 = INT_MIN / 2;
+        tx1 = ty1 = INT_MAX / 2;
+        return true;
+    }
+    const float rd = sqrtf(c.r2) + 1.0f;
+    const float ex = c.hx + 1.0f, ey = c.hy + 1.0f;
+    const float bx0 = fminf(c.gx - rd, c.mx - ex), bx1 = fmaxf(c.gx + rd, c.mx + ex);
+    const float by0 = fminf(c.gy - rd, c.my - ey), by1 = fmaxf(c.gy + rd, c.my + ey);
+    tx0 = static_cast<int>(floorf(fmaxf(bx0, -1e6f) * (1.0f / 16.0f)));
+    ty0 = static_cast<int>(floorf(fmaxf(by0, -1e6f) * (1.0f / 16.0f)));
+    tx1 = static_cast<int>(floorf(fminf(bx1, 1e6f) * (1.0f / 16.0f)));
+    ty1 = static_cast<int>(floorf(fminf(by1, 1e6f) * (1.0f / 16.0f)));
+    return true;
+}
+
+// 4-bit mask of the 8x8 quadrants of tile (tx, ty) that may hold a live
+// pixel; bit (qy * 2 + qx).
+__device__ __forceinline__ uint32_t cull_quadrants(const CullShape& c, int tx, int ty) {
+    uint32_t mask = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float x0 = static_cast<float>(tx * 16 + (q & 1) * 8) - 1.0f;
+        const float y0 = static_cast<float>(ty * 16 + (q >> 1) * 8) - 1.0f;
+        if (cull_rect_live(c, x0, y0, x0 + 9.0f, y0 + 9.0f)) mask |= 1u << q;
+    }
+    return mask;
 }
 
 }  // namespace st

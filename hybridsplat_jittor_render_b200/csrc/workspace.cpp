@@ -1,4 +1,5 @@
-// Grow-only device buffers owned by a context (context.h).
+// Grow-only device buffers owned by a context (context.h) and the optional
+// stage timer.
 #include <algorithm>
 
 #include "context.h"
@@ -9,9 +10,17 @@ namespace {
 constexpr uint64_t kGranule = 2ull * 1024ull * 1024ull;
 }
 
-cudaError_t ensure_buffer(DeviceBuffer& buffer, uint64_t required, uint64_t* growth_count) {
-    const uint64_t target = (std::max<uint64_t>(required, 1) + kGranule - 1) & ~(kGranule - 1);
-    if (buffer.ptr != nullptr && buffer.bytes >= target) return cudaSuccess;
+cudaError_t ensure_buffer(DeviceBuffer& buffer, uint64_t required, uint64_t* growth_count,
+                          bool geometric) {
+    if (buffer.ptr != nullptr && buffer.bytes >= required) return cudaSuccess;
+    // Growth rules of the reference workspaces: the standard backend grows to
+    // at least 1.25x the previous capacity (rasterizer/c_api.cpp:85-127), the
+    // FlashGS buffers to the requirement (flashgs_backend.cu:56-86); both
+    // round up to 2 MiB.
+    const uint64_t grown = (!geometric || buffer.bytes == 0)
+                               ? required
+                               : std::max(required, buffer.bytes + buffer.bytes / 4);
+    const uint64_t target = (std::max<uint64_t>(grown, 1) + kGranule - 1) & ~(kGranule - 1);
     void* replacement = nullptr;
     cudaError_t status = cudaMalloc(&replacement, target);
     if (status != cudaSuccess) return status;
@@ -83,6 +92,20 @@ cudaError_t stage_timing_read(StageTimer& timer, double out_ms[3], uint64_t* cal
     if (calls != nullptr) *calls = timer.calls;
     timer.total_ms[0] = timer.total_ms[1] = timer.total_ms[2] = 0.0;
     timer.calls = 0;
+    return cudaSuccess;
+}
+
+cudaError_t ensure_device_error(HsRasterizerContext* context) {
+    if (context->device_error != nullptr) return cudaSuccess;
+    void* p = nullptr;
+    cudaError_t st = cudaMalloc(&p, 256);
+    if (st != cudaSuccess) return st;
+    st = cudaMemset(p, 0, 256);
+    if (st != cudaSuccess) {
+        cudaFree(p);
+        return st;
+    }
+    context->device_error = static_cast<uint32_t*>(p);
     return cudaSuccess;
 }
 
