@@ -161,10 +161,14 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
     cam.grid_y = grid_y;
 
     StageMarks marks(ctx->timer, stream);
-    cudaError_t st = ensure_buffer(ctx->fg_ranges, tiles * sizeof(int2), &ctx->fg_growth_count);
+    // ranges, rasterisation order of the tiles, work counter
+    cudaError_t st = ensure_buffer(ctx->fg_ranges, tiles * (sizeof(int2) + sizeof(uint32_t)) + 256,
+                                   &ctx->fg_growth_count);
     if (st != cudaSuccess) return st;
     ctx->fg_range_capacity = std::max<uint64_t>(ctx->fg_range_capacity, tiles);
     int2* ranges = static_cast<int2*>(ctx->fg_ranges.ptr);
+    uint32_t* tile_order = reinterpret_cast<uint32_t*>(ranges + tiles);
+    uint32_t* work_counter = tile_order + tiles;
     st = cudaMemsetAsync(ranges, 0, tiles * sizeof(int2), stream);
     if (st != cudaSuccess) return st;
 
@@ -285,9 +289,22 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
     const float3 bg_encoded = make_float3(encode(bg.x), encode(bg.y), encode(bg.z));
     const uint32_t* ids = nullptr;
     if (num_rendered > 0) ids = pair_views(ctx->fg_pairs.ptr, ctx->fg_pair_capacity).ids;
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+    bin::tile_order_kernel<int2><<<1, bin::kOrderThreads, 0, stream>>>(
+        static_cast<uint32_t>(tiles), ranges, tile_order, work_counter);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
     marks.mark(2);
-    render_kernel<HS_FLASHGS_ROUNDING><<<static_cast<unsigned>(tiles), kRenderThreads, 0, stream>>>(
-        ranges, ids, gv.records, width, height, grid_x, bg, bg_encoded, out);
+    int sms = 148, per_sm = 1;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, render_kernel<HS_FLASHGS_ROUNDING>,
+                                                  kRenderThreads, 0);
+    const uint32_t render_blocks = static_cast<uint32_t>(
+        std::min<uint64_t>(tiles, static_cast<uint64_t>(sms) * std::max(per_sm, 1)));
+    render_kernel<HS_FLASHGS_ROUNDING><<<render_blocks, kRenderThreads, 0, stream>>>(
+        ranges, tile_order, static_cast<uint32_t>(tiles), work_counter, ids, gv.records, width,
+        height, grid_x, bg, bg_encoded, out);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     marks.mark(3);

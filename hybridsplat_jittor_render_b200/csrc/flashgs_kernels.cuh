@@ -278,73 +278,84 @@ __device__ __forceinline__ void store_empty(float3 bg_encoded, const Outputs& o,
 // warps that stopped early blend the remaining Gaussians up to that end.
 template <class R>
 __global__ void __launch_bounds__(kRenderThreads) render_kernel(
-    const int2* __restrict__ ranges, const uint32_t* __restrict__ gaussian_ids,
+    const int2* __restrict__ ranges, const uint32_t* __restrict__ tile_order, uint32_t tile_count,
+    uint32_t* __restrict__ work_counter, const uint32_t* __restrict__ gaussian_ids,
     const float4* __restrict__ records, int width, int height, int grid_x, float3 bg,
     float3 bg_encoded, Outputs out) {
     __shared__ float4 batch[kBatch * 5];
     __shared__ int done_at[kRenderThreads / 32];
+    __shared__ uint32_t next_tile;
     const R r;
-    const int tile = blockIdx.x;
-    const int tx = tile % grid_x, ty = tile / grid_x;
-    const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4;
-    const int px = tx * 16 + lx, py0 = ty * 16 + ly, py1 = py0 + 8;
-    const size_t plane = static_cast<size_t>(width) * height;
-    const bool in0 = px < width && py0 < height;
-    const bool in1 = px < width && py1 < height;
-    const int2 range = ranges[tile];
-    if (range.x >= range.y) {
-        if (in0) store_empty(bg_encoded, out, plane, static_cast<size_t>(py0) * width + px);
-        if (in1) store_empty(bg_encoded, out, plane, static_cast<size_t>(py1) * width + px);
-        return;
-    }
-    const float fx = static_cast<float>(px);
-    const float fy0 = static_cast<float>(py0), fy1 = static_cast<float>(py1);
-    PixelState s0, s1;
-    pixel_init(s0);
-    pixel_init(s1);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int n = range.y - range.x;
-    bool warp_done = false;
-    int warp_done_at = 0;
-    for (int base = 0; base < n; base += kBatch) {
-        const int nb = min(kBatch, n - base);
+    const int lx = threadIdx.x & 15, ly = threadIdx.x >> 4;
+    const size_t plane = static_cast<size_t>(width) * height;
+    // Persistent: each block takes tiles from the global counter, in the
+    // longest-first order of tile_order.
+    for (;;) {
+        __syncthreads();  // the previous tile's readers of next_tile/done_at are finished
+        if (threadIdx.x == 0) next_tile = atomicAdd(work_counter, 1u);
         __syncthreads();
-        for (int i = threadIdx.x; i < nb * 5; i += kRenderThreads) {
-            const int j = i / 5, q = i - j * 5;
-            const uint32_t gid = gaussian_ids[range.x + base + j];
-            batch[i] = records[static_cast<size_t>(gid) * kRecordQuads + q];
+        const uint32_t slot = next_tile;
+        if (slot >= tile_count) break;
+        const int tile = static_cast<int>(tile_order[slot]);
+        const int tx = tile % grid_x, ty = tile / grid_x;
+        const int px = tx * 16 + lx, py0 = ty * 16 + ly, py1 = py0 + 8;
+        const bool in0 = px < width && py0 < height;
+        const bool in1 = px < width && py1 < height;
+        const int2 range = ranges[tile];
+        if (range.x >= range.y) {
+            if (in0) store_empty(bg_encoded, out, plane, static_cast<size_t>(py0) * width + px);
+            if (in1) store_empty(bg_encoded, out, plane, static_cast<size_t>(py1) * width + px);
+            continue;
         }
-        __syncthreads();
-        int cursor = 0;
-        if (!warp_done) {
-            cursor = nb;
-            for (int j = 0; j < nb; ++j) {
+        const float fx = static_cast<float>(px);
+        const float fy0 = static_cast<float>(py0), fy1 = static_cast<float>(py1);
+        PixelState s0, s1;
+        pixel_init(s0);
+        pixel_init(s1);
+        const int n = range.y - range.x;
+        bool warp_done = false;
+        int warp_done_at = 0;
+        for (int base = 0; base < n; base += kBatch) {
+            const int nb = min(kBatch, n - base);
+            __syncthreads();
+            for (int i = threadIdx.x; i < nb * 5; i += kRenderThreads) {
+                const int j = i / 5, q = i - j * 5;
+                const uint32_t gid = gaussian_ids[range.x + base + j];
+                batch[i] = records[static_cast<size_t>(gid) * kRecordQuads + q];
+            }
+            __syncthreads();
+            int cursor = 0;
+            if (!warp_done) {
+                cursor = nb;
+                for (int j = 0; j < nb; ++j) {
+                    const BlendRecord g = load_record(batch + j * 5);
+                    blend(r, s0, fx, fy0, g);
+                    blend(r, s1, fx, fy1, g);
+                    if (__all_sync(0xffffffffu, s0.t < 0.0001f && s1.t < 0.0001f)) {
+                        warp_done = true;
+                        warp_done_at = base + j;
+                        cursor = j + 1;
+                        break;
+                    }
+                }
+            }
+            if (lane == 0) done_at[warp] = warp_done ? warp_done_at : INT_MAX;
+            __syncthreads();
+            int tile_end = done_at[0];
+#pragma unroll
+            for (int w = 1; w < kRenderThreads / 32; ++w) tile_end = max(tile_end, done_at[w]);
+            const int stop = tile_end == INT_MAX ? nb : tile_end - base + 1;
+            for (int j = cursor; j < stop; ++j) {
                 const BlendRecord g = load_record(batch + j * 5);
                 blend(r, s0, fx, fy0, g);
                 blend(r, s1, fx, fy1, g);
-                if (__all_sync(0xffffffffu, s0.t < 0.0001f && s1.t < 0.0001f)) {
-                    warp_done = true;
-                    warp_done_at = base + j;
-                    cursor = j + 1;
-                    break;
-                }
             }
+            if (tile_end != INT_MAX) break;
         }
-        if (lane == 0) done_at[warp] = warp_done ? warp_done_at : INT_MAX;
-        __syncthreads();
-        int tile_end = done_at[0];
-#pragma unroll
-        for (int w = 1; w < kRenderThreads / 32; ++w) tile_end = max(tile_end, done_at[w]);
-        const int stop = tile_end == INT_MAX ? nb : tile_end - base + 1;
-        for (int j = cursor; j < stop; ++j) {
-            const BlendRecord g = load_record(batch + j * 5);
-            blend(r, s0, fx, fy0, g);
-            blend(r, s1, fx, fy1, g);
-        }
-        if (tile_end != INT_MAX) break;
+        if (in0) store_pixel(r, s0, bg, out, plane, static_cast<size_t>(py0) * width + px);
+        if (in1) store_pixel(r, s1, bg, out, plane, static_cast<size_t>(py1) * width + px);
     }
-    if (in0) store_pixel(r, s0, bg, out, plane, static_cast<size_t>(py0) * width + px);
-    if (in1) store_pixel(r, s1, bg, out, plane, static_cast<size_t>(py1) * width + px);
 }
 
 }  // namespace fg

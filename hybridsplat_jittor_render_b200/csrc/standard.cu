@@ -143,7 +143,9 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
     cudaError_t st = ensure_buffer(ctx->std_geometry, geometry_used + geometry_scratch_bytes,
                                    &ctx->std_growth_count, true);
     if (st != cudaSuccess) return st;
-    st = ensure_buffer(ctx->std_image, tiles * sizeof(uint2), &ctx->std_growth_count, true);
+    // image buffer: ranges, rasterisation order of the tiles, work counter
+    st = ensure_buffer(ctx->std_image, tiles * (sizeof(uint2) + sizeof(uint32_t)) + 256,
+                       &ctx->std_growth_count, true);
     if (st != cudaSuccess) return st;
     if (ctx->std_total_host == nullptr) {
         st = cudaHostAlloc(reinterpret_cast<void**>(&ctx->std_total_host), 4 * sizeof(uint32_t),
@@ -160,6 +162,8 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
     const GeometryViews gv = geometry_views(ctx->std_geometry.ptr, count);
     void* geometry_scratch = static_cast<unsigned char*>(ctx->std_geometry.ptr) + geometry_used;
     uint2* ranges = static_cast<uint2*>(ctx->std_image.ptr);
+    uint32_t* tile_order = reinterpret_cast<uint32_t*>(ranges + tiles);
+    uint32_t* work_counter = tile_order + tiles;
 
     st = cudaMemsetAsync(output_weight, 0, count * sizeof(float), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(gv.totals, 0, 4 * sizeof(uint32_t), stream);
@@ -233,17 +237,32 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
     }
+    bin::tile_order_kernel<uint2><<<1, bin::kOrderThreads, 0, stream>>>(
+        static_cast<uint32_t>(tiles), ranges, tile_order, work_counter);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
     marks.mark(2);
+    const uint32_t items = static_cast<uint32_t>(tiles) * 4u;
+    int sms = 148, per_sm = 1;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
     if (masked) {
-        render_kernel<HS_STANDARD_ROUNDING, true>
-            <<<static_cast<unsigned>(tiles), kRenderThreads, 0, stream>>>(
-                ranges, values, gv.records, width, height, grid_x, background5, output_color5,
-                output_aux7, output_weight);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, render_kernel<HS_STANDARD_ROUNDING, true>, kRenderThreads, 0);
     } else {
-        render_kernel<HS_STANDARD_ROUNDING, false>
-            <<<static_cast<unsigned>(tiles), kRenderThreads, 0, stream>>>(
-                ranges, values, gv.records, width, height, grid_x, background5, output_color5,
-                output_aux7, output_weight);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, render_kernel<HS_STANDARD_ROUNDING, false>, kRenderThreads, 0);
+    }
+    const uint32_t wanted = (items + kRenderThreads / 32 - 1) / (kRenderThreads / 32);
+    const uint32_t render_blocks =
+        std::min<uint32_t>(wanted, static_cast<uint32_t>(sms * std::max(per_sm, 1)));
+    if (masked) {
+        render_kernel<HS_STANDARD_ROUNDING, true><<<render_blocks, kRenderThreads, 0, stream>>>(
+            ranges, tile_order, items, work_counter, values, gv.records, width, height, grid_x,
+            background5, output_color5, output_aux7, output_weight);
+    } else {
+        render_kernel<HS_STANDARD_ROUNDING, false><<<render_blocks, kRenderThreads, 0, stream>>>(
+            ranges, tile_order, items, work_counter, values, gv.records, width, height, grid_x,
+            background5, output_color5, output_aux7, output_weight);
     }
     return cudaGetLastError();
 }

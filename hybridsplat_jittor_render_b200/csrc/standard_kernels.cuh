@@ -208,76 +208,85 @@ __device__ __forceinline__ void store_pixel(const R& r, const PixelState& s,
 }
 
 // renderCUDA<5> (forward.cu:256-445). Every pixel blends its tile's list in
-// order and stops on its own (forward.cu:323-328, 398-402), so each warp can
-// run on its own: warp q owns the 8x8 quadrant q of the tile (two pixels per
-// lane, rows ly and ly + 4) and walks the tile's list 32 pairs at a time,
-// keeping the pairs whose quadrant bit is set. Their records are staged in
-// the warp's shared-memory slots, then blended in list order. The warp stops
-// when its 64 pixels are done. Blend weights are summed across the warp
-// before one atomicAdd per Gaussian.
+// order and stops on its own (forward.cu:323-328, 398-402), so each 8x8
+// quadrant of a tile is an independent work item. The kernel is persistent:
+// each warp takes items (tile order[i / 4], quadrant i % 4) from a global
+// counter, longest tiles first, two pixels per lane (rows ly and ly + 4). A
+// warp walks its tile's list 32 pairs at a time, keeps the pairs whose
+// quadrant bit is set, stages their records in its shared-memory slots and
+// blends them in list order; it stops when its 64 pixels are done. Blend
+// weights are summed across the warp before one atomicAdd per Gaussian.
 template <class R, bool kMasked>
 __global__ void __launch_bounds__(kRenderThreads) render_kernel(
-    const uint2* __restrict__ ranges, const uint32_t* __restrict__ pair_values,
+    const uint2* __restrict__ ranges, const uint32_t* __restrict__ tile_order, uint32_t items,
+    uint32_t* __restrict__ work_counter, const uint32_t* __restrict__ pair_values,
     const float4* __restrict__ records, int width, int height, uint32_t grid_x,
     const float* __restrict__ background5, float* __restrict__ color, float* __restrict__ aux,
     float* __restrict__ weight) {
     __shared__ float4 slots[kRenderThreads / 32][32 * kRecordQuads];
     __shared__ uint32_t slot_ids[kRenderThreads / 32][32];
     const R r;
-    const uint32_t tile = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int tx = tile % grid_x, ty = tile / grid_x;
-    const int px = tx * 16 + (warp & 1) * 8 + (lane & 7);
-    const int py0 = ty * 16 + (warp >> 1) * 8 + (lane >> 3), py1 = py0 + 4;
-    const bool in0 = px < width && py0 < height;
-    const bool in1 = px < width && py1 < height;
-    const float fx = static_cast<float>(px);
-    const float fy0 = static_cast<float>(py0), fy1 = static_cast<float>(py1);
-    PixelState s0, s1;
-    pixel_init(s0, in0);
-    pixel_init(s1, in1);
-    const uint2 range = ranges[tile];
-    const uint32_t n = range.y - range.x;
     const uint32_t lt = (1u << lane) - 1u;
     float4* my_slots = slots[warp];
     uint32_t* my_ids = slot_ids[warp];
-    for (uint32_t base = 0; base < n; base += 32) {
-        if (__all_sync(0xffffffffu, s0.done && s1.done)) break;
-        const uint32_t j = base + lane;
-        const uint32_t v = j < n ? pair_values[range.x + j] : 0u;
-        const bool live = j < n && (!kMasked || ((v >> (kIndexBits + warp)) & 1u) != 0u);
-        const uint32_t mask = __ballot_sync(0xffffffffu, live);
-        if (live) {
-            const uint32_t gid = kMasked ? (v & kIndexMask) : v;
-            const uint32_t slot = __popc(mask & lt);
-            const float4* src = records + static_cast<size_t>(gid) * kRecordQuads;
-#pragma unroll
-            for (int q = 0; q < kRecordQuads; ++q) my_slots[slot * kRecordQuads + q] = src[q];
-            my_ids[slot] = gid;
-        }
-        __syncwarp();
-        const int live_count = __popc(mask);
-        for (int k = 0; k < live_count; ++k) {
-            const BlendRecord g = load_record(my_slots + k * kRecordQuads);
-            float w = blend(r, s0, fx, fy0, g);
-            w += blend(r, s1, fx, fy1, g);
-            if (__any_sync(0xffffffffu, w != 0.0f)) {
-                w = w + __shfl_xor_sync(0xffffffffu, w, 16);
-                w = w + __shfl_xor_sync(0xffffffffu, w, 8);
-                w = w + __shfl_xor_sync(0xffffffffu, w, 4);
-                w = w + __shfl_xor_sync(0xffffffffu, w, 2);
-                w = w + __shfl_xor_sync(0xffffffffu, w, 1);
-                if (lane == 0 && w != 0.0f) atomicAdd(weight + my_ids[k], w);
-            }
-        }
-        __syncwarp();
-    }
     float bg[5];
 #pragma unroll
     for (int k = 0; k < 5; ++k) bg[k] = background5[k];
     const size_t plane = static_cast<size_t>(width) * height;
-    if (in0) store_pixel(r, s0, bg, color, aux, plane, static_cast<size_t>(py0) * width + px);
-    if (in1) store_pixel(r, s1, bg, color, aux, plane, static_cast<size_t>(py1) * width + px);
+    for (;;) {
+        uint32_t item = 0;
+        if (lane == 0) item = atomicAdd(work_counter, 1u);
+        item = __shfl_sync(0xffffffffu, item, 0);
+        if (item >= items) break;
+        const uint32_t tile = tile_order[item >> 2];
+        const int quad = static_cast<int>(item & 3u);
+        const int tx = tile % grid_x, ty = tile / grid_x;
+        const int px = tx * 16 + (quad & 1) * 8 + (lane & 7);
+        const int py0 = ty * 16 + (quad >> 1) * 8 + (lane >> 3), py1 = py0 + 4;
+        const bool in0 = px < width && py0 < height;
+        const bool in1 = px < width && py1 < height;
+        const float fx = static_cast<float>(px);
+        const float fy0 = static_cast<float>(py0), fy1 = static_cast<float>(py1);
+        PixelState s0, s1;
+        pixel_init(s0, in0);
+        pixel_init(s1, in1);
+        const uint2 range = ranges[tile];
+        const uint32_t n = range.y - range.x;
+        for (uint32_t base = 0; base < n; base += 32) {
+            if (__all_sync(0xffffffffu, s0.done && s1.done)) break;
+            const uint32_t j = base + lane;
+            const uint32_t v = j < n ? pair_values[range.x + j] : 0u;
+            const bool live = j < n && (!kMasked || ((v >> (kIndexBits + quad)) & 1u) != 0u);
+            const uint32_t mask = __ballot_sync(0xffffffffu, live);
+            if (live) {
+                const uint32_t gid = kMasked ? (v & kIndexMask) : v;
+                const uint32_t slot = __popc(mask & lt);
+                const float4* src = records + static_cast<size_t>(gid) * kRecordQuads;
+#pragma unroll
+                for (int q = 0; q < kRecordQuads; ++q) my_slots[slot * kRecordQuads + q] = src[q];
+                my_ids[slot] = gid;
+            }
+            __syncwarp();
+            const int live_count = __popc(mask);
+            for (int k = 0; k < live_count; ++k) {
+                const BlendRecord g = load_record(my_slots + k * kRecordQuads);
+                float w = blend(r, s0, fx, fy0, g);
+                w += blend(r, s1, fx, fy1, g);
+                if (__any_sync(0xffffffffu, w != 0.0f)) {
+                    w = w + __shfl_xor_sync(0xffffffffu, w, 16);
+                    w = w + __shfl_xor_sync(0xffffffffu, w, 8);
+                    w = w + __shfl_xor_sync(0xffffffffu, w, 4);
+                    w = w + __shfl_xor_sync(0xffffffffu, w, 2);
+                    w = w + __shfl_xor_sync(0xffffffffu, w, 1);
+                    if (lane == 0 && w != 0.0f) atomicAdd(weight + my_ids[k], w);
+                }
+            }
+            __syncwarp();
+        }
+        if (in0) store_pixel(r, s0, bg, color, aux, plane, static_cast<size_t>(py0) * width + px);
+        if (in1) store_pixel(r, s1, bg, color, aux, plane, static_cast<size_t>(py1) * width + px);
+    }
 }
 
 }  // namespace st
