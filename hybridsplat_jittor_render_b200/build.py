@@ -61,6 +61,7 @@ CXX_COMMON = [
 SOURCES = [
     ("flashgs.cu", "cuda", []),
     ("standard.cu", "cuda", []),
+    ("standard_noalloc.cu", "cuda", []),
     ("sort.cu", "cuda", []),
     ("precise.cu", "cuda", ["--fmad=false"]),
     ("precise_exp.cu", "cuda", []),

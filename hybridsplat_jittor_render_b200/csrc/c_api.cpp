@@ -26,6 +26,16 @@
 #include "precise.h"
 
 namespace hs {
+cudaError_t standard_forward_noalloc(int32_t device, int32_t point_count,
+                                    const float* background5, int32_t width, int32_t height,
+                                    const float* means3d, const float* colors5,
+                                    const float* opacities, const float* scales2,
+                                    float scale_modifier, const float* rotations4,
+                                    const float* viewmatrix4x4, const float* projmatrix4x4,
+                                    bool prefiltered, float* output_color5, float* output_aux7,
+                                    float* output_weight, int32_t* output_radii,
+                                    int32_t* output_rendered, char* limit_text,
+                                    uint64_t limit_capacity);
 void flashgs_prepare_host(uint64_t count, const float* opacity_raw, const float* scaling_raw,
                           const float* rotation_raw, const float* specular_raw,
                           const float* roughness_raw, float* opacity, float* scaling,
@@ -969,6 +979,63 @@ int32_t hs_b200_stage_timing_read_v1(HsRasterizerHandle handle, double* stage_ms
         std::lock_guard<std::mutex> lock(handle->mutex);
         const cudaError_t e = hs::stage_timing_read(handle->timer, stage_ms3, raster_calls);
         if (e != cudaSuccess) return cuda_failure(e, "stage timing", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_b200_rasterizer_forward_noalloc_f32_v1(
+    int32_t device, uint64_t point_count, const float* background5, int32_t width,
+    int32_t height, const float* means3d, const float* colors5, const float* opacities,
+    const float* scales2, float scale_modifier, const float* rotations4,
+    const float* viewmatrix4x4, const float* projmatrix4x4, const float* camera_position3,
+    float tan_fovx, float tan_fovy, int32_t prefiltered, float* output_color5, float* output_aux7,
+    float* output_weight, int32_t* output_radii, int32_t* output_rendered, char* error_text,
+    uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        // Same argument checks as hs_rasterizer_forward_f32_v1, with a device
+        // ordinal in place of the context handle.
+        if (background5 == nullptr || output_color5 == nullptr || output_aux7 == nullptr ||
+            output_rendered == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "rasterizer received a null required handle or buffer", error_text,
+                        error_capacity);
+        }
+        if (point_count > static_cast<uint64_t>(INT_MAX) || width <= 0 || height <= 0 ||
+            !std::isfinite(scale_modifier) || !std::isfinite(tan_fovx) ||
+            !std::isfinite(tan_fovy) || tan_fovx <= 0.0f || tan_fovy <= 0.0f ||
+            (prefiltered != 0 && prefiltered != 1)) {
+            return fail(HS_STATUS_RANGE_ERROR, "rasterizer dimensions or scalar arguments are invalid",
+                        error_text, error_capacity);
+        }
+        if (point_count != 0 &&
+            (means3d == nullptr || colors5 == nullptr || opacities == nullptr ||
+             scales2 == nullptr || rotations4 == nullptr || viewmatrix4x4 == nullptr ||
+             projmatrix4x4 == nullptr || camera_position3 == nullptr ||
+             output_weight == nullptr || output_radii == nullptr)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "non-empty rasterizer input contains a null buffer", error_text,
+                        error_capacity);
+        }
+        int device_count = 0;
+        cudaError_t e = cudaGetDeviceCount(&device_count);
+        if (e != cudaSuccess) return cuda_failure(e, "cudaGetDeviceCount", error_text, error_capacity);
+        if (device < 0 || device >= device_count) {
+            return fail(HS_STATUS_RANGE_ERROR, "device is outside the visible CUDA device range",
+                        error_text, error_capacity);
+        }
+        e = cudaSetDevice(device);
+        if (e != cudaSuccess) return cuda_failure(e, "cudaSetDevice", error_text, error_capacity);
+        char limit[256] = {};
+        e = hs::standard_forward_noalloc(
+            device, static_cast<int32_t>(point_count), background5, width, height, means3d,
+            colors5, opacities, scales2, scale_modifier, rotations4, viewmatrix4x4,
+            projmatrix4x4, prefiltered != 0, output_color5, output_aux7, output_weight,
+            output_radii, output_rendered, limit, sizeof(limit));
+        if (limit[0] != '\0') return fail(HS_STATUS_RANGE_ERROR, limit, error_text, error_capacity);
+        if (e != cudaSuccess) {
+            return cuda_failure(e, "no-alloc five-channel rasterizer forward", error_text,
+                                error_capacity);
+        }
         return ok(error_text, error_capacity);
     });
 }

@@ -30,6 +30,29 @@ HS_API int32_t hs_b200_stage_timing_read_v1(
     HsRasterizerHandle handle, double* stage_ms3, uint64_t* raster_calls,
     char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
 
+/* The standard five-channel forward of hs_rasterizer_forward_f32_v1 without
+ * any allocation: no context, no cudaMalloc/cudaFree/cudaHostAlloc. Every
+ * scratch buffer comes from one 8 MiB device array inside the library (its
+ * address is looked up with cudaGetSymbolAddress on the first call on each
+ * device, so make one call before any phase where the runtime must not load
+ * modules). No counterpart in the reference library. Same arguments as
+ * hs_rasterizer_forward_f32_v1 with a device ordinal in place of the handle,
+ * same outputs. Limits: point_count <= 16384, ceil(W/16)*ceil(H/16) <= 4096
+ * tiles, <= 262144 emitted (tile, Gaussian) pairs; beyond them the call
+ * returns HS_STATUS_RANGE_ERROR naming the limit (the pair limit is known only
+ * after preprocessing, so outputs are then incomplete). All calls on a device
+ * share the array: they are serialised by a process-wide lock and run on the
+ * legacy default stream. The call reads the pair count back with a blocking
+ * copy into host stack memory. */
+HS_API int32_t hs_b200_rasterizer_forward_noalloc_f32_v1(
+    int32_t device, uint64_t point_count, const float* background5, int32_t width,
+    int32_t height, const float* means3d, const float* colors5, const float* opacities,
+    const float* scales2, float scale_modifier, const float* rotations4,
+    const float* viewmatrix4x4, const float* projmatrix4x4, const float* camera_position3,
+    float tan_fovx, float tan_fovy, int32_t prefiltered, float* output_color5, float* output_aux7,
+    float* output_weight, int32_t* output_radii, int32_t* output_rendered, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,84 @@
+"""The allocation-free standard forward against the context entry point.
+
+hs_b200_rasterizer_forward_noalloc_f32_v1 runs the kernels of
+hs_rasterizer_forward_f32_v1 with its scratch in a fixed device array; on the
+same inputs its outputs must agree with the context path within the standard
+backend's tolerance (they are expected to be identical), on two calls in a
+row. Kept in its own file, collected last, so it also runs after every other
+GPU test in the same process.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import STANDARD_MAX_ABS, fixture_inputs, within_standard_tolerance
+from hybridsplat_jittor_render_b200 import NativeRendererContext, ops
+from hybridsplat_jittor_render_b200 import native_runtime as nr
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def noalloc_forward(lib, inputs, w, h, point_count=None):
+    f = dict(dtype=torch.float32, device="cuda")
+    n = int(inputs["means3d"].shape[0])
+    color = torch.empty((5, h, w), **f)
+    aux = torch.empty((7, h, w), **f)
+    weight = torch.empty((n, 1), **f)
+    radii = torch.empty((n,), dtype=torch.int32, device="cuda")
+    rendered = torch.empty((1,), dtype=torch.int32, device="cuda")
+    t = {k: dev(v) for k, v in inputs.items()}
+    err = nr.error_buffer()
+    status = lib.hs_b200_rasterizer_forward_noalloc_f32_v1(
+        torch.cuda.current_device(), n if point_count is None else point_count,
+        t["background"].data_ptr(), w, h, t["means3d"].data_ptr(), t["colors"].data_ptr(),
+        t["opacities"].data_ptr(), t["scales"].data_ptr(), 1.0, t["rotations"].data_ptr(),
+        t["viewmatrix"].data_ptr(), t["projmatrix"].data_ptr(), t["camera_position"].data_ptr(), 0.5,
+        0.5, 0,
+        color.data_ptr(), aux.data_ptr(), weight.data_ptr(), radii.data_ptr(), rendered.data_ptr(),
+        err, len(err))
+    torch.cuda.synchronize()
+    return status, err.value.decode(), (color, aux, weight, radii, rendered)
+
+
+@pytest.mark.parametrize("case", ["small", "ragged", "background"])
+@pytest.mark.parametrize("group", ["base", "reflection"])
+def test_noalloc_matches_context_path_twice(golden, case, group):
+    data = golden(case)
+    inputs = fixture_inputs(data, "standard", group)
+    w, h = (int(v) for v in data["camera_size"])
+    lib = nr.load_native_library()
+    with NativeRendererContext(0) as ctx:
+        ref = ops.rasterize_forward(*[dev(v) for v in inputs.values()], width=w, height=h,
+                                    scale_modifier=1.0, tan_fovx=0.5, tan_fovy=0.5, context=ctx)
+        torch.cuda.synchronize()
+    for _ in range(2):
+        status, message, (color, aux, weight, radii, rendered) = noalloc_forward(lib, inputs, w, h)
+        assert status == 0, message
+        assert int(rendered.item()) == int(ref.rendered.item())
+        assert torch.equal(radii, ref.radii)
+        assert within_standard_tolerance(color.cpu().numpy(), ref.color.cpu().numpy())
+        assert within_standard_tolerance(aux.cpu().numpy(), ref.auxiliary.cpu().numpy())
+        np.testing.assert_allclose(weight.cpu().numpy(), ref.weight.cpu().numpy(), rtol=1e-5,
+                                   atol=STANDARD_MAX_ABS)
+
+
+def test_noalloc_rejects_sizes_beyond_its_limits(golden):
+    data = golden("small")
+    inputs = fixture_inputs(data, "standard", "base")
+    lib = nr.load_native_library()
+    status, message, _ = noalloc_forward(lib, inputs, 4096, 2048)  # 32768 tiles > 4096
+    assert status == 3 and "tile count" in message and "4096" in message
+    big = {k: v for k, v in inputs.items()}
+    for key in ("means3d", "colors", "opacities", "scales", "rotations"):
+        big[key] = np.concatenate([inputs[key]] * 9, axis=0)  # 18000 Gaussians > 16384
+    status, message, _ = noalloc_forward(lib, big, 96, 72)
+    assert status == 3 and "point_count" in message and "16384" in message
