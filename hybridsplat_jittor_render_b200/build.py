@@ -86,7 +86,7 @@ def _run(job: tuple[list[str], str]) -> str:
 def _inputs() -> list[Path]:
     files = [CSRC / name for name, _, _ in SOURCES]
     files += sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h"))
-    files += [INCLUDE / "hybridsplat_rasterizer_c_api.h", Path(__file__)]
+    files += sorted(INCLUDE.glob("*.h")) + [Path(__file__)]
     return files
 
 

@@ -152,6 +152,48 @@ __global__ void ranges_kernel(uint32_t pair_count, uint32_t tile_count,
     }
 }
 
+// Emission for emitters whose k-th pair of a Gaussian is a fixed function of
+// k (every tile of a rectangle): the pairs of a warp's 32 Gaussians are
+// numbered 0..total-1 and dealt to the lanes round-robin, so every lane does
+// the same amount of work whatever the rectangle sizes. A lane finds the
+// Gaussian of pair f by binary search over the warp's inclusive pair counts.
+// Emitter interface: Shape, load(gid), and
+//   __device__ void emit_one(const Shape&, uint32_t gid, uint32_t offset, uint32_t k,
+//                            uint32_t* tiles, uint32_t* values) const;
+template <class Emitter>
+__global__ void __launch_bounds__(kEmitThreads) emit_flat_kernel(
+    uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
+    Emitter em, uint32_t* __restrict__ tile_ids, uint32_t* __restrict__ values) {
+    __shared__ typename Emitter::Shape shapes[kEmitThreads];
+    __shared__ uint32_t gids[kEmitThreads], offsets[kEmitThreads], inclusive[kEmitThreads];
+    const uint32_t gid = blockIdx.x * kEmitThreads + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const uint32_t base = threadIdx.x & ~31u;
+    const uint32_t cnt = gid < count ? counts[gid] : 0u;
+    shapes[threadIdx.x] = em.load(cnt != 0u ? gid : 0u);
+    gids[threadIdx.x] = gid;
+    offsets[threadIdx.x] = cnt != 0u ? first_pair[gid] : 0u;
+    uint32_t incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+    }
+    inclusive[threadIdx.x] = incl;
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();
+    for (uint32_t f = lane; f < total; f += 32) {
+        uint32_t j = 0;
+#pragma unroll
+        for (uint32_t step = 16; step >= 1; step >>= 1) {
+            if (inclusive[base + j + step - 1] <= f) j += step;
+        }
+        const uint32_t owner = base + j;
+        const uint32_t k = f - (j == 0 ? 0u : inclusive[owner - 1]);
+        em.emit_one(shapes[owner], gids[owner], offsets[owner], k, tile_ids, values);
+    }
+}
+
 // Rasterisation order of the tiles: longest pair lists first (buckets by
 // the bit length of the list length; any order inside a bucket), so that the
 // persistent rasterisers take the expensive tiles before the cheap ones.

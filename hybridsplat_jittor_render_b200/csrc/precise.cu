@@ -114,48 +114,91 @@ __global__ void direction_kernel(const float* __restrict__ points,
     }
 }
 
+// One colour channel of precise_sh.cu:11-138: every product and sum rounded
+// in source order. c points at the channel's coefficients.
+__device__ __forceinline__ float sh_channel(const float* c, float x, float y, float z, float xx,
+                                            float yy, float zz, float xy, float yz, float xz,
+                                            uint32_t degree) {
+    float r = mul(0.28209479177387814f, c[0]);
+    if (degree > 0) {
+        const float c1 = 0.4886025119029199f;
+        r = sub(r, mul(mul(c1, y), c[1]));
+        r = add(r, mul(mul(c1, z), c[2]));
+        r = sub(r, mul(mul(c1, x), c[3]));
+    }
+    if (degree > 1) {
+        r = add(r, mul(mul(1.0925484305920792f, xy), c[4]));
+        r = add(r, mul(mul(-1.0925484305920792f, yz), c[5]));
+        const float p6 = sub(sub(mul(2.0f, zz), xx), yy);
+        r = add(r, mul(mul(0.31539156525252005f, p6), c[6]));
+        r = add(r, mul(mul(-1.0925484305920792f, xz), c[7]));
+        r = add(r, mul(mul(0.5462742152960396f, sub(xx, yy)), c[8]));
+    }
+    if (degree > 2) {
+        const float p9 = sub(mul(3.0f, xx), yy);
+        r = add(r, mul(mul(mul(-0.5900435899266435f, y), p9), c[9]));
+        r = add(r, mul(mul(mul(2.890611442640554f, xy), z), c[10]));
+        const float p11 = sub(sub(mul(4.0f, zz), xx), yy);
+        r = add(r, mul(mul(mul(-0.4570457994644658f, y), p11), c[11]));
+        const float p12 = sub(sub(mul(2.0f, zz), mul(3.0f, xx)), mul(3.0f, yy));
+        r = add(r, mul(mul(mul(0.3731763325901154f, z), p12), c[12]));
+        r = add(r, mul(mul(mul(-0.4570457994644658f, x), p11), c[13]));
+        r = add(r, mul(mul(mul(1.445305721320277f, z), sub(xx, yy)), c[14]));
+        const float p15 = sub(xx, mul(3.0f, yy));
+        r = add(r, mul(mul(mul(-0.5900435899266435f, x), p15), c[15]));
+    }
+    return fmaxf(add(r, 0.5f), 0.0f);
+}
+
+// Any coefficient count and alignment.
 __global__ void sh_to_rgb_kernel(const float* __restrict__ sh, const float* __restrict__ dirs,
                                  uint64_t count, uint32_t coefficients, uint32_t degree,
                                  float* __restrict__ out) {
-    // precise_sh.cu:11-138: every product and sum rounded in source order.
     for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
          i += uint64_t(gridDim.x) * blockDim.x) {
         const float x = dirs[3 * i], y = dirs[3 * i + 1], z = dirs[3 * i + 2];
         const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
         const float xy = mul(x, y), yz = mul(y, z), xz = mul(x, z);
         for (uint32_t ch = 0; ch < 3; ++ch) {
-            const float* c = sh + (i * 3 + ch) * coefficients;
-            float r = mul(0.28209479177387814f, c[0]);
-            if (degree > 0) {
-                const float c1 = 0.4886025119029199f;
-                r = sub(r, mul(mul(c1, y), c[1]));
-                r = add(r, mul(mul(c1, z), c[2]));
-                r = sub(r, mul(mul(c1, x), c[3]));
-            }
-            if (degree > 1) {
-                r = add(r, mul(mul(1.0925484305920792f, xy), c[4]));
-                r = add(r, mul(mul(-1.0925484305920792f, yz), c[5]));
-                const float p6 = sub(sub(mul(2.0f, zz), xx), yy);
-                r = add(r, mul(mul(0.31539156525252005f, p6), c[6]));
-                r = add(r, mul(mul(-1.0925484305920792f, xz), c[7]));
-                r = add(r, mul(mul(0.5462742152960396f, sub(xx, yy)), c[8]));
-            }
-            if (degree > 2) {
-                const float p9 = sub(mul(3.0f, xx), yy);
-                r = add(r, mul(mul(mul(-0.5900435899266435f, y), p9), c[9]));
-                r = add(r, mul(mul(mul(2.890611442640554f, xy), z), c[10]));
-                const float p11 = sub(sub(mul(4.0f, zz), xx), yy);
-                r = add(r, mul(mul(mul(-0.4570457994644658f, y), p11), c[11]));
-                const float p12 = sub(sub(mul(2.0f, zz), mul(3.0f, xx)), mul(3.0f, yy));
-                r = add(r, mul(mul(mul(0.3731763325901154f, z), p12), c[12]));
-                r = add(r, mul(mul(mul(-0.4570457994644658f, x), p11), c[13]));
-                r = add(r, mul(mul(mul(1.445305721320277f, z), sub(xx, yy)), c[14]));
-                const float p15 = sub(xx, mul(3.0f, yy));
-                r = add(r, mul(mul(mul(-0.5900435899266435f, x), p15), c[15]));
-            }
-            r = add(r, 0.5f);
-            out[3 * i + ch] = fmaxf(r, 0.0f);
+            out[3 * i + ch] = sh_channel(sh + (i * 3 + ch) * coefficients, x, y, z, xx, yy, zz,
+                                         xy, yz, xz, degree);
         }
+    }
+}
+
+// 16 coefficients per channel, 16-byte aligned rows. A block stages the
+// 192-byte rows of its 128 Gaussians in shared memory with coalesced 128-bit
+// loads (rows padded to 49 words so the per-thread reads do not conflict),
+// then each thread evaluates its own Gaussian.
+constexpr int kShThreads = 128;
+constexpr int kShStride = 49;
+
+template <uint32_t kDegree>
+__global__ void __launch_bounds__(kShThreads) sh16_to_rgb_kernel(
+    const float4* __restrict__ sh, const float* __restrict__ dirs, uint64_t count,
+    float* __restrict__ out) {
+    __shared__ float rows[kShThreads * kShStride];
+    const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kShThreads;
+    const uint64_t left = count - first;
+    const uint32_t n = left < kShThreads ? static_cast<uint32_t>(left) : kShThreads;
+    for (uint32_t f = threadIdx.x; f < n * 12; f += kShThreads) {
+        const float4 v = sh[first * 12 + f];
+        float* d = rows + (f / 12) * kShStride + (f % 12) * 4;
+        d[0] = v.x;
+        d[1] = v.y;
+        d[2] = v.z;
+        d[3] = v.w;
+    }
+    __syncthreads();
+    if (threadIdx.x >= n) return;
+    const uint64_t i = first + threadIdx.x;
+    const float* c = rows + threadIdx.x * kShStride;
+    const float x = dirs[3 * i], y = dirs[3 * i + 1], z = dirs[3 * i + 2];
+    const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
+    const float xy = mul(x, y), yz = mul(y, z), xz = mul(x, z);
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+        out[3 * i + ch] = sh_channel(c + 16 * ch, x, y, z, xx, yy, zz, xy, yz, xz, kDegree);
     }
 }
 
@@ -214,14 +257,23 @@ __device__ __forceinline__ float normalize3_add(float& x, float& y, float& z) {
     return den;
 }
 
-__global__ void reflection_suffix_kernel(const float* __restrict__ xyz,
-                                         const float* __restrict__ center,
-                                         const float* __restrict__ normal_raw, uint64_t count,
-                                         float* __restrict__ out36) {
+// One thread per reflective Gaussian; the block's 36-float output rows are
+// staged in shared memory (padded to 37 words) and written with coalesced
+// stores.
+constexpr int kSuffixThreads = 128;
+constexpr int kSuffixStride = 37;
+
+__global__ void __launch_bounds__(kSuffixThreads) reflection_suffix_kernel(
+    const float* __restrict__ xyz, const float* __restrict__ center,
+    const float* __restrict__ normal_raw, uint64_t count, float* __restrict__ out36) {
     // precise_reflection_trace.cu:185-330
-    const float cx = center[0], cy = center[1], cz = center[2];
-    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
-         i += uint64_t(gridDim.x) * blockDim.x) {
+    __shared__ float rows[kSuffixThreads * kSuffixStride];
+    const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kSuffixThreads;
+    const uint64_t left = count - first;
+    const uint32_t n = left < kSuffixThreads ? static_cast<uint32_t>(left) : kSuffixThreads;
+    if (threadIdx.x < n) {
+        const uint64_t i = first + threadIdx.x;
+        const float cx = center[0], cy = center[1], cz = center[2];
         const float px = xyz[3 * i], py = xyz[3 * i + 1], pz = xyz[3 * i + 2];
         float vx = sub(cx, px), vy = sub(cy, py), vz = sub(cz, pz);
         normalize3_add(vx, vy, vz);
@@ -245,15 +297,20 @@ __global__ void reflection_suffix_kernel(const float* __restrict__ xyz,
         float dx = rx, dy = ry, dz = rz;
         const float ray_den = normalize3_add(dx, dy, dz);
         const float ox = mul(0.05f, dx), oy = mul(0.05f, dy), oz = mul(0.05f, dz);
-        float* o = out36 + 36 * i;
         const float values[36] = {vx,  vy,  vz,  nx,  ny,  nz,  rx,  ry,  rz,
                                   dx,  dy,  dz,  add(px, ox), add(py, oy), add(pz, oz),
                                   positive ? 1.0f : 0.0f,
                                   inx, iny, inz, nrx, nry, nrz, nden, rpx, rpy, rpz,
                                   dot_nv, two_dot, snx, sny, snz, ray_den, ox, oy, oz,
                                   flip_dot};
+        float* row = rows + threadIdx.x * kSuffixStride;
 #pragma unroll
-        for (int k = 0; k < 36; ++k) o[k] = values[k];
+        for (int k = 0; k < 36; ++k) row[k] = values[k];
+    }
+    __syncthreads();
+    float* dst = out36 + first * 36;
+    for (uint32_t f = threadIdx.x; f < n * 36; f += kSuffixThreads) {
+        dst[f] = rows[(f / 36) * kSuffixStride + f % 36];
     }
 }
 
@@ -301,6 +358,17 @@ cudaError_t direction(const float* points, const float* center, uint64_t count, 
 cudaError_t sh_to_rgb(const float* sh, const float* dirs, uint64_t count, uint32_t coefficients,
                       uint32_t degree, float* out, cudaStream_t s) {
     if (count == 0) return cudaSuccess;
+    if (coefficients == 16 && (reinterpret_cast<uintptr_t>(sh) & 15u) == 0 && degree <= 3) {
+        const unsigned blocks = static_cast<unsigned>((count + kShThreads - 1) / kShThreads);
+        const float4* sh4 = reinterpret_cast<const float4*>(sh);
+        switch (degree) {
+            case 0: sh16_to_rgb_kernel<0><<<blocks, kShThreads, 0, s>>>(sh4, dirs, count, out); break;
+            case 1: sh16_to_rgb_kernel<1><<<blocks, kShThreads, 0, s>>>(sh4, dirs, count, out); break;
+            case 2: sh16_to_rgb_kernel<2><<<blocks, kShThreads, 0, s>>>(sh4, dirs, count, out); break;
+            default: sh16_to_rgb_kernel<3><<<blocks, kShThreads, 0, s>>>(sh4, dirs, count, out); break;
+        }
+        return cudaGetLastError();
+    }
     sh_to_rgb_kernel<<<grid_for(count), kThreads, 0, s>>>(sh, dirs, count, coefficients, degree,
                                                            out);
     return cudaGetLastError();
@@ -321,8 +389,8 @@ cudaError_t disk_rotation(const float* rot, uint64_t count, float* out, cudaStre
 cudaError_t reflection_suffix(const float* xyz, const float* center, const float* normal_raw,
                               uint64_t count, float* out36, cudaStream_t s) {
     if (count == 0) return cudaSuccess;
-    reflection_suffix_kernel<<<grid_for(count), kThreads, 0, s>>>(xyz, center, normal_raw, count,
-                                                                   out36);
+    reflection_suffix_kernel<<<static_cast<unsigned>((count + kSuffixThreads - 1) / kSuffixThreads),
+                               kSuffixThreads, 0, s>>>(xyz, center, normal_raw, count, out36);
     return cudaGetLastError();
 }
 

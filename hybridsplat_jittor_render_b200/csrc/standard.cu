@@ -222,7 +222,7 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
         const Emitter em{gv.cull, grid_x, masked};
-        bin::emit_kernel<Emitter>
+        bin::emit_flat_kernel<Emitter>
             <<<(point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
                stream>>>(static_cast<uint32_t>(point_count), gv.counts, first_pair, em, tile_ids,
                          values);

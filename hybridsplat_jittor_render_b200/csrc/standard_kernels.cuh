@@ -143,6 +143,15 @@ struct Emitter {
         c.gx = s.c.x; c.gy = s.c.y; c.r2 = s.c.z; c.mode = __float_as_int(s.c.w);
         return c;
     }
+    __device__ __forceinline__ void emit_one(const Shape& s, uint32_t gid, uint32_t offset,
+                                             uint32_t k, uint32_t* tiles, uint32_t* values) const {
+        const CullShape c = unpack(s);
+        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
+        const int x0 = lo & 0xffff, y0 = lo >> 16, w = static_cast<int>(hi & 0xffff) - x0;
+        const int ty = y0 + static_cast<int>(k) / w, tx = x0 + static_cast<int>(k) % w;
+        tiles[offset + k] = static_cast<uint32_t>(ty) * grid_x + static_cast<uint32_t>(tx);
+        values[offset + k] = masked ? (gid | (cull_quadrants(c, tx, ty) << kIndexBits)) : gid;
+    }
     __device__ __forceinline__ bool small(const Shape& s) const {
         const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
         return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16)) <= 8u;
@@ -217,7 +226,7 @@ __device__ __forceinline__ void store_pixel(const R& r, const PixelState& s,
 // blends them in list order; it stops when its 64 pixels are done. Blend
 // weights are summed across the warp before one atomicAdd per Gaussian.
 template <class R, bool kMasked>
-__global__ void __launch_bounds__(kRenderThreads) render_kernel(
+__global__ void __launch_bounds__(kRenderThreads, 7) render_kernel(
     const uint2* __restrict__ ranges, const uint32_t* __restrict__ tile_order, uint32_t items,
     uint32_t* __restrict__ work_counter, const uint32_t* __restrict__ pair_values,
     const float4* __restrict__ records, int width, int height, uint32_t grid_x,

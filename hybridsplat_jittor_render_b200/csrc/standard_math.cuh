@@ -291,22 +291,24 @@ __device__ __forceinline__ float cull_form(const CullShape& c, float X, float Y)
     return u * u * c.ia + v * v * c.ib;
 }
 
-// Can any pixel of [x0, x1] x [y0, y1] (already widened) be live?
+// Can any pixel of [x0, x1] x [y0, y1] (already widened) be live? Written
+// without early exits so that the lanes of a warp, each testing a different
+// Gaussian, stay converged.
 __device__ __forceinline__ bool cull_rect_live(const CullShape& c, float x0, float y0, float x1,
                                                float y1) {
-    if (c.mode == kCullAlways) return false;
-    if (c.mode == kCullNever) return true;
     const float cx = fminf(fmaxf(c.gx, x0), x1), cy = fminf(fmaxf(c.gy, y0), y1);
     const float ddx = cx - c.gx, ddy = cy - c.gy;
-    if (ddx * ddx + ddy * ddy <= c.r2) return true;
+    const bool disc = ddx * ddx + ddy * ddy <= c.r2;
     const float X0 = x0 - c.mx, X1 = x1 - c.mx, Y0 = y0 - c.my, Y1 = y1 - c.my;
-    if (X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f) return true;
+    const bool centre = X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f;
     // Minimum of the form along each edge of the rectangle.
     const float fa = cull_form(c, X0, fminf(fmaxf(c.ryx * X0, Y0), Y1));
     const float fb = cull_form(c, X1, fminf(fmaxf(c.ryx * X1, Y0), Y1));
     const float fc = cull_form(c, fminf(fmaxf(c.rxy * Y0, X0), X1), Y0);
     const float fd = cull_form(c, fminf(fmaxf(c.rxy * Y1, X0), X1), Y1);
-    return fminf(fminf(fa, fb), fminf(fc, fd)) <= 1.0f;
+    const bool edge = fminf(fminf(fa, fb), fminf(fc, fd)) <= 1.0f;
+    const bool tested = disc || centre || edge;
+    return c.mode == kCullNever || (c.mode == kCullEllipse && tested);
 }
 
 // Tiles (16 px) that may hold a live pixel: the bounding box of the ellipse

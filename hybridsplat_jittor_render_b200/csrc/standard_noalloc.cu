@@ -189,7 +189,7 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
         st = cudaGetLastError();
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
         const Emitter em{l.cull, grid_x, true};
-        bin::emit_kernel<Emitter>
+        bin::emit_flat_kernel<Emitter>
             <<<(point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
                stream>>>(static_cast<uint32_t>(point_count), l.counts, first_pair, em, l.tile_ids,
                          l.values);
