@@ -66,6 +66,8 @@ def parse_args():
     p.add_argument("--scale", type=float, default=1.0, help="Gaussian-count scale (profiling runs only)")
     p.add_argument("--profile-frames", type=int, default=0,
                    help="render this many frames untimed and exit (a short, fixed launch sequence for ncu)")
+    p.add_argument("--profile-reference", action="store_true",
+                   help="with --profile-frames: render with the reference CUDA rebuild (oracle/_ref)")
     return p.parse_args()
 
 
@@ -195,14 +197,17 @@ class Frame:
         return [fused["rgb_map"], acc, depth, normal, spec, fused["dif_rgb_map"], fused["ref_rgb_map"]]
 
     def launches_per_step(self) -> int:
-        """Kernels of this library launched by one render() call."""
+        """Kernels of this library launched by one render() call (memsets and
+        copies excluded): per raster call preprocess, depth-sort histogram +
+        4 passes, pair offsets, emission, tile-sort histogram + passes, ranges,
+        tile order and the rasteriser; plus the elementwise kernels of the view."""
         from hybridsplat_jittor_render_b200.scenes import SCENES
         spec = SCENES[SCENE]
         tiles = ((spec.width + 15) // 16) * ((spec.height + 15) // 16)
-        tile_passes = math.ceil(max(1, int(tiles - 1).bit_length()) / 8)
-        per_raster = 1 + 4 * 5 + 3 + 1 + tile_passes * 5 + 1 + 1  # preprocess, depth sort, scan, emit, tile sort, ranges, render
+        tile_passes = math.ceil(max(1, int(tiles).bit_length()) / 8)
+        per_raster = 1 + (1 + 4) + 1 + 1 + (1 + tile_passes) + 1 + 1 + 1
         extra = 2 if self.backend == "standard" else 0  # direction + SH
-        return 2 * per_raster + extra + 3  # + prefix, suffix, fuse
+        return 2 * per_raster + extra + 3  # + reflection prefix, suffix, fusion
 
 
 # --------------------------------------------------------------------------- clocks
@@ -359,7 +364,11 @@ def run_ours(args):
         for key, v in rep.items():
             g, k = key.split("/")
             scene_np[g][k] = v.cpu().numpy()
-    frame = Frame(scene_np, args.backend, device)
+    library = None
+    if args.profile_frames > 0 and args.profile_reference:
+        from hybridsplat_jittor_render_b200.native_runtime import bind_library
+        library = bind_library(REPO / "oracle" / "_ref" / "libref_hybridsplat.so", require_optix=False)
+    frame = Frame(scene_np, args.backend, device, library=library)
     views = [(info.rank + world * s) % 20 for s in range(args.warmup + args.steps)]
     cams = [scenes.orbit_camera(SCENE, v) for v in views]
     if args.profile_frames > 0:

@@ -248,13 +248,15 @@ __device__ __forceinline__ CullShape cull_shape(float op, float x, float y, floa
         c.mode = kCullAlways;
         return c;
     }
-    const double lc = 2.0 * log(255.0 * static_cast<double>(op));
-    const double cw = 1.02 * lc + 0.05;
+    // The widening (2% + 0.05) dwarfs the error of logf here.
+    const float cwf = 1.02f * (2.0f * logf(255.0f * op)) + 0.05f;
+    const double cw = static_cast<double>(cwf) * 1.0001;
     c.r2 = static_cast<float>(0.5 * cw * 1.0001);
     const double twx = tw.x, twy = tw.y, twz = tw.z;
     const double d = cw * (twx * twx + twy * twy) - twz * twz;
     c.mode = kCullNever;
     if (!(d < -1e-6 * twz * twz)) return c;  // unbounded image of the disc
+    // Dual-conic moments in double: m^2 - q cancels to the ellipse size.
     const double fxy = cw / d, fz = -1.0 / d;
     const double mx = fxy * (double(tu.x) * twx + double(tu.y) * twy) + fz * double(tu.z) * twz;
     const double my = fxy * (double(tv.x) * twx + double(tv.y) * twy) + fz * double(tv.z) * twz;
@@ -264,10 +266,24 @@ __device__ __forceinline__ CullShape cull_shape(float op, float x, float y, floa
     const double sxx = mx * mx - quu, syy = my * my - qvv, sxy = mx * my - quv;
     const double det = sxx * syy - sxy * sxy;
     if (!(sxx > 0.0 && syy > 0.0 && det > 0.0) || !(fabs(mx) < 1e7 && fabs(my) < 1e7)) return c;
-    const double la = 0.5 * (sxx + syy) + sqrt(0.25 * (sxx - syy) * (sxx - syy) + sxy * sxy);
+    // Eigen-decomposition of [[sxx, sxy], [sxy, syy]] without trigonometry:
+    // r = la - lb, (cos 2t, sin 2t) = (sxx - syy, 2 sxy) / r, and the
+    // half-angle formulas taken on the side that avoids cancellation.
+    const double dxy = sxx - syy;
+    const double r = sqrt(dxy * dxy + 4.0 * sxy * sxy);
+    const double la = 0.5 * (sxx + syy + r);
     const double lb = det / la;
-    const double th = 0.5 * atan2(2.0 * sxy, sxx - syy);
-    const double cs = cos(th), sn = sin(th);
+    double cs = 1.0, sn = 0.0;
+    if (r > 0.0) {
+        if (dxy >= 0.0) {
+            cs = sqrt(0.5 * (1.0 + dxy / r));
+            sn = sxy / (r * cs);
+        } else {
+            sn = sqrt(0.5 * (1.0 - dxy / r));
+            if (sxy < 0.0) sn = -sn;
+            cs = sxy / (r * sn);
+        }
+    }
     // widen the axes slightly to absorb the rounding of the stored direction
     const double ia = 1.0 / (la * 1.0002), ib = 1.0 / (lb * 1.0002 + 1e-8 * la);
     const double axx = cs * cs * ia + sn * sn * ib, ayy = sn * sn * ia + cs * cs * ib;
