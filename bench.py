@@ -46,12 +46,14 @@ sys.path.insert(0, str(REPO))
 METRIC = "FPS @1292x839, 1M base+200k refl Gaussians, 1/2/4/8 B200; per-stage ms"
 SCENE = "standard_1m"
 SM_COUNT = 148
-# Algorithmic FP32 work of one pixel x Gaussian blend evaluation, counted from
-# csrc/standard_math.cuh blend(): 51 FP32 add/mul/fma (fma = 2 flop) = 80
-# flop, plus 3 IEEE divisions and one expf (counted as 1 flop each here).
-FLOP_PER_EVAL_STANDARD = 84
-# csrc/flashgs_math.cuh blend(): 48 add/mul/fma (76 flop) + 3 div + 1 exp.
-FLOP_PER_EVAL_FLASHGS = 80
+# Algorithmic FP32 work of one pixel x Gaussian blend evaluation, counted
+# from the blend functions (FMA = 2 flop; each IEEE division and expf = 1):
+# standard (csrc/standard_math.cuh blend): 39 flop up to the alpha < 1/255
+# exit, 76 for an evaluation that blends; FlashGS (csrc/flashgs_math.cuh
+# blend) always blends: 75.
+FLOP_STANDARD_DEAD = 39
+FLOP_STANDARD_LIVE = 76
+FLOP_FLASHGS = 75
 
 
 def parse_args():
@@ -127,6 +129,7 @@ class Frame:
             self.r_in = prep(r)
             self.r_in[2] = self.trace_rgb
         self.cam = None
+        self.split = None  # list: per raster call stage timings (instrumented pass)
 
     def set_camera(self, cam, upload_from=None):
         """Per-view camera state. For the standard backend the matrices are
@@ -156,6 +159,8 @@ class Frame:
                                          scale_modifier=1.0, tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy,
                                          context=self.ctx)
             rec(1)
+            if self.split is not None:
+                self.split.append(("base", self.ctx.read_stage_timing()))
             center = self.center
         else:
             base = ops.flashgs_forward(*self.b_in, width=cam.width, height=cam.height, use_sh=True,
@@ -163,6 +168,8 @@ class Frame:
                                        focal_x=cam.fx, focal_y=cam.fy, initial_pair_capacity=2_000_000,
                                        context=self.ctx)
             rec(1)
+            if self.split is not None:
+                self.split.append(("base", self.ctx.read_stage_timing()))
             center = torch.from_numpy(self.scenes.standard_camera_center(cam)).to(self.device, non_blocking=True)
         rot = ops.precise_reflection_prefix(self.r_rot_raw, library=lib)
         normal_raw = rot[:, :, 2].contiguous()
@@ -180,6 +187,8 @@ class Frame:
                                        focal_x=cam.fx, focal_y=cam.fy, initial_pair_capacity=2_000_000,
                                        context=self.ctx)
             base_rgb, spec = base.color, base.other[0:1]
+        if self.split is not None:
+            self.split.append(("reflection", self.ctx.read_stage_timing()))
         rec(3)
         fused = ops.precise_fuse_maps(base_rgb.permute(1, 2, 0).contiguous(),
                                       refl.color[:3].permute(1, 2, 0).contiguous(),
@@ -266,19 +275,21 @@ class ClockSampler:
 # --------------------------------------------------------------------------- CPU oracle
 
 def cpu_oracle_frame(scene, backend: str, row_stride: int, threads: int) -> dict:
-    """Times the CPU oracle on the benchmark frame, sampling every
-    `row_stride`-th tile row; returns the extrapolated full-frame time and
-    the blend-evaluation count."""
+    """Times the CPU oracle on the benchmark frame (view 0), sampling every
+    `row_stride`-th tile row; returns the extrapolated full-frame time and,
+    per Gaussian group, the blend evaluations by the reference's rule and
+    those that changed a pixel."""
     from hybridsplat_jittor_render_b200 import scenes
     from oracle import oracle
     cam = scenes.orbit_camera(SCENE, 0)
     b, r = scene["base"], scene["reflection"]
-    total_ms, evals = 0.0, 0.0
+    total_ms = 0.0
+    evals, live = {}, {}
     t0 = time.perf_counter()
     for gname in ("base", "reflection"):
         g = scene[gname]
         n = g["xyz"].shape[0]
-        stats = np.zeros(4, np.float64)
+        stats = np.zeros(5, np.float64)
         if backend == "standard":
             center = scenes.standard_camera_center(cam)
             if gname == "base":
@@ -306,9 +317,10 @@ def cpu_oracle_frame(scene, backend: str, row_stride: int, threads: int) -> dict
                                    stage_ms=stats)
         # preprocess covers every Gaussian; binning and blending cover 1/row_stride of the tile rows
         total_ms += stats[0] + row_stride * (stats[1] + stats[2])
-        evals += row_stride * stats[3]
+        evals[gname] = row_stride * stats[3]
+        live[gname] = row_stride * stats[4]
     wall = time.perf_counter() - t0
-    return {"frame_ms": total_ms, "evaluations": evals, "wall_s": wall}
+    return {"frame_ms": total_ms, "evaluations": evals, "live": live, "wall_s": wall}
 
 
 # --------------------------------------------------------------------------- arms
@@ -411,24 +423,28 @@ def run_ours(args):
         ms = float(t.item())
     fps_total = world * 1000.0 / ms
 
-    # per-stage ms (instrumented pass, not the headline): CUDA events between
-    # the frame stages plus the library's own stage events inside each raster call
+    # per-stage ms (instrumented pass, not the headline): the view the CPU
+    # oracle counts evaluations on (view 0), CUDA events between the frame
+    # stages plus the library's own stage events inside each raster call
     stage_names = ("base_raster", "reflection_prepare", "reflection_raster", "fusion")
     sums = np.zeros(4)
+    view0 = scenes.orbit_camera(SCENE, 0)
     frame.ctx.stage_timing(True)
     frame.ctx.read_stage_timing()
+    frame.split = []
     for s in range(args.steps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-        frame.set_camera(cams[args.warmup + s])
+        frame.set_camera(view0)
         frame.render(ev)
         torch.cuda.synchronize()
         sums += [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
-    raster = frame.ctx.read_stage_timing()
     frame.ctx.stage_timing(False)
+    split, frame.split = frame.split, None
     stages = {k: float(v / args.steps) for k, v in zip(stage_names, sums)}
-    for k in ("preprocess_ms", "binning_ms", "blend_ms"):
-        stages["raster_" + k] = raster[k] / args.steps  # both raster calls of a frame
-    stages["raster_calls_per_frame"] = raster["calls"] / args.steps
+    for group in ("base", "reflection"):
+        runs = [t for g, t in split if g == group]
+        for k in ("preprocess_ms", "binning_ms", "blend_ms"):
+            stages[f"{group}_{k}"] = float(np.mean([t[k] for t in runs]))
 
     # end-to-end through the public API with host buffers
     pinned_cam = [torch.from_numpy(np.concatenate([c.world_view().reshape(-1), c.full_proj().reshape(-1),
@@ -497,29 +513,33 @@ def roofline_and_baselines(args, frame, cams, stages, scene_np, clocks: dict) ->
                                "kind": "port",
                                "sample": f"one full {args.backend} frame (base + reflection) of the benchmark "
                                          f"scene by the CPU oracle, {threads} threads, {cpu['wall_s']:.1f} s"}
-    # Roofline of the dominant kernel (the tile blender of both raster calls):
-    # FP32-pipe bound. Work = pixel x Gaussian evaluations counted by the CPU
-    # oracle on the same frame; time = the blend stage's CUDA events.
-    blend_ms = stages["raster_blend_ms"]
-    evals_base = None
-    if cpu is not None:
-        evals_base = cpu["evaluations"]
-    flop_per_eval = FLOP_PER_EVAL_STANDARD if args.backend == "standard" else FLOP_PER_EVAL_FLASHGS
+    # Roofline of the dominant kernel: the rasteriser's launch for the base
+    # group of view 0 (FP32-pipe bound). Work = the reference-rule
+    # evaluations counted by the CPU oracle on the same view, split into
+    # those that exit at the alpha test and those that blend; time = that
+    # launch's CUDA events inside the library.
+    blend_ms = stages["base_blend_ms"]
     sm_mhz = clocks.get("sm_mhz") or peaks.get("sm_max_mhz") or 1965.0
     peak_tflops = SM_COUNT * 128 * 2 * sm_mhz * 1e6 / 1e12
     traffic = None
     tpath = REPO / "profiles" / "traffic.json"
     if tpath.exists():
-        traffic = json.loads(tpath.read_text()).get(f"{args.backend}_render_bytes_per_launch")
-    if evals_base is not None:
-        achieved = evals_base * flop_per_eval / (blend_ms * 1e-3) / 1e12
-        out["roofline"] = {"bound": "fp32", "kernel": f"{args.backend} render_kernel (base + reflection launch of one frame)",
-                           "kernel_ms": blend_ms,
-                           "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
+        traffic = json.loads(tpath.read_text()).get(f"{args.backend}_render_base_bytes_per_launch")
+    if cpu is not None:
+        evals = cpu["evaluations"]["base"]
+        live = cpu["live"]["base"]
+        if args.backend == "standard":
+            flop = live * FLOP_STANDARD_LIVE + (evals - live) * FLOP_STANDARD_DEAD
+        else:
+            flop = evals * FLOP_FLASHGS
+        achieved = flop / (blend_ms * 1e-3) / 1e12
+        out["roofline"] = {"bound": "fp32", "kernel": f"{args.backend} render_kernel, base-group launch of view 0",
+                           "kernel_ms": blend_ms, "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
                            "frac": achieved / peak_tflops, "traffic": traffic,
-                           "work": f"{evals_base:.4g} pixel x Gaussian evaluations x {flop_per_eval} flop",
+                           "work": f"{evals:.4g} reference-rule evaluations ({live:.4g} blend), {flop:.4g} flop",
                            "peak_source": f"nominal FP32 FMA rate, {SM_COUNT} SMs x 128 lanes x 2 flop at "
-                                          f"{sm_mhz:.0f} MHz (measured median SM clock under load)"}
+                                          f"{sm_mhz:.0f} MHz (measured median SM clock under load); "
+                                          "MEASURED_PEAKS.json has no FP32 figure"}
     if not args.no_reference_gpu:
         ref_path = REPO / "oracle" / "_ref" / "libref_hybridsplat.so"
         if ref_path.exists():

@@ -349,9 +349,10 @@ static float encode_bg(float v) {
  * keys/values receive the sorted pairs when non-NULL and *pairs fits.
  * Only tile rows with ty % row_stride == 0 are binned and rendered (1 =
  * the whole frame; larger strides give a bounded sample for CPU timing).
- * stage_ms, when non-NULL, receives 4 doubles: the wall times (ms) of
- * preprocess, binning (pair emission, sort, ranges) and blending, and the
- * number of pixel x Gaussian blend evaluations.
+ * stage_ms, when non-NULL, receives 5 doubles: the wall times (ms) of
+ * preprocess, binning (pair emission, sort, ranges) and blending, the
+ * number of pixel x Gaussian blend evaluations and the number of those that
+ * changed the pixel (FlashGS blends on every evaluation, so both are equal).
  * Returns the number of pairs emitted, or -1 on allocation failure.
  */
 API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const float* shs,
@@ -520,6 +521,7 @@ API int64_t oracle_flashgs_forward(int P, int W, int H, const float* pos, const 
         stage_ms[1] = t2 - t1;
         stage_ms[2] = now_ms() - t2;
         stage_ms[3] = (double)evaluations;
+        stage_ms[4] = (double)evaluations;
     }
     free(ranges);
     free(pairs);
@@ -701,8 +703,8 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
         if (i == total - 1) ranges[2 * t + 1] = total;
     }
     const double t2 = now_ms();
-    int64_t evaluations = 0;
-#pragma omp parallel for schedule(dynamic, 1) reduction(+ : evaluations)
+    int64_t evaluations = 0, live = 0;
+#pragma omp parallel for schedule(dynamic, 1) reduction(+ : evaluations, live)
     for (int tile = 0; tile < tiles; ++tile) {
         const int tx = tile % gx, ty = tile / gx;
         if (ty % row_stride != 0) continue;
@@ -716,8 +718,10 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
             const StGauss* g = &gs[pairs[j].value];
             int all_done = 1;
             for (int k = 0; k < 256; ++k) {
-                evaluations += px[k].done ? 0 : 1;
+                const int was_done = px[k].done;
+                evaluations += was_done ? 0 : 1;
                 const float w = st_blend(&px[k], (float)(tx * 16 + (k & 15)), (float)(ty * 16 + (k >> 4)), g->rec);
+                live += (!was_done && (w != 0.0f || px[k].done)) ? 1 : 0;
                 if (w != 0.0f) {
 #pragma omp atomic
                     out_weight[pairs[j].value] += w;
@@ -744,6 +748,7 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
         stage_ms[1] = t2 - t1;
         stage_ms[2] = now_ms() - t2;
         stage_ms[3] = (double)evaluations;
+        stage_ms[4] = (double)live;
     }
     free(ranges);
     free(pairs);
