@@ -194,6 +194,55 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_kernel(
     }
 }
 
+// Flattened emission for emitters that keep a subset of a rectangle (the
+// FlashGS tile/ellipse test): the rectangle tiles of a warp's 32 Gaussians
+// are dealt to the lanes round-robin, and a kept tile takes the next slot of
+// its Gaussian from a shared-memory cursor. Slots of one Gaussian are thus
+// filled in no particular order, which the following stable sort by tile id
+// makes irrelevant (each tile appears once per Gaussian).
+// Emitter interface: Shape, load(gid), and
+//   __device__ uint32_t slots(const Shape&) const;             // rectangle size
+//   __device__ bool pair_at(const Shape&, uint32_t k, uint32_t& tile) const;
+template <class Emitter>
+__global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
+    uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
+    Emitter em, uint32_t* __restrict__ tile_ids, uint32_t* __restrict__ values) {
+    __shared__ typename Emitter::Shape shapes[kEmitThreads];
+    __shared__ uint32_t offsets[kEmitThreads], inclusive[kEmitThreads], cursor[kEmitThreads];
+    const uint32_t gid = blockIdx.x * kEmitThreads + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const uint32_t base = threadIdx.x & ~31u;
+    const uint32_t cnt = gid < count ? counts[gid] : 0u;
+    const typename Emitter::Shape mine = em.load(cnt != 0u ? gid : 0u);
+    shapes[threadIdx.x] = mine;
+    offsets[threadIdx.x] = cnt != 0u ? first_pair[gid] : 0u;
+    cursor[threadIdx.x] = 0;
+    uint32_t incl = cnt != 0u ? em.slots(mine) : 0u;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+    }
+    inclusive[threadIdx.x] = incl;
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();
+    for (uint32_t f = lane; f < total; f += 32) {
+        uint32_t j = 0;
+#pragma unroll
+        for (uint32_t step = 16; step >= 1; step >>= 1) {
+            if (inclusive[base + j + step - 1] <= f) j += step;
+        }
+        const uint32_t owner = base + j;
+        const uint32_t k = f - (j == 0 ? 0u : inclusive[owner - 1]);
+        uint32_t tile;
+        if (em.pair_at(shapes[owner], k, tile)) {
+            const uint32_t at = offsets[owner] + atomicAdd(&cursor[owner], 1u);
+            tile_ids[at] = tile;
+            values[at] = blockIdx.x * kEmitThreads + owner;
+        }
+    }
+}
+
 // Rasterisation order of the tiles: longest pair lists first (buckets by
 // the bit length of the list length; any order inside a bucket), so that the
 // persistent rasterisers take the expensive tiles before the cheap ones.

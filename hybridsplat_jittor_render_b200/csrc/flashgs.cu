@@ -262,7 +262,7 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
             st = cudaGetLastError();
             if (st != cudaSuccess) return st;
             const Emitter<HS_FLASHGS_ROUNDING> em{gv.emit, grid_x};
-            bin::emit_kernel<Emitter<HS_FLASHGS_ROUNDING>>
+            bin::emit_flat_compact_kernel<Emitter<HS_FLASHGS_ROUNDING>>
                 <<<(point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
                    stream>>>(static_cast<uint32_t>(point_count), gv.counts, first_pair, em,
                              pv.tiles, pv.ids);

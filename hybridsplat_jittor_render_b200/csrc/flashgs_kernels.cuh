@@ -30,8 +30,8 @@ __device__ __forceinline__ float4 f4(float a, float b, float c, float d) {
     return make_float4(a, b, c, d);
 }
 
-// Rectangles up to this many tiles are tested by their own lane; larger ones
-// by the whole warp, 32 tiles per step.
+// Rectangles up to 2 * kSerialTiles tiles are emitted by their own lane,
+// larger ones by the whole warp, 32 tiles per step.
 constexpr int kSerialTiles = 4;
 
 template <class R>
@@ -67,44 +67,60 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
                              cam.width, cam.height, cam.focal_x, cam.focal_y, cam.tan_fovx,
                              cam.tan_fovy, cam.grid_x, cam.grid_y);
     }
-    // Exact tile/ellipse count (preprocess.cu:482-506).
+    // Exact tile/ellipse count (preprocess.cu:482-506). The rectangle tiles
+    // of the warp's 32 Gaussians are numbered 0..total-1 and dealt to the
+    // lanes round-robin; each lane finds the owning Gaussian by binary search
+    // over the warp's inclusive tile counts and adds its hit to the owner's
+    // shared-memory counter, so every lane does the same number of tests.
+    __shared__ float s_shape[kPreThreads][6];      // xy, conic, power
+    __shared__ int s_rect[kPreThreads][3];         // x0, y0, width
+    __shared__ uint32_t s_incl[kPreThreads];
+    __shared__ uint32_t s_hits[kPreThreads];
     const bool candidate = g.in_front && g.touches;
     const int gw = candidate ? g.rect_max.x - g.rect_min.x : 0;
-    const int area = candidate ? gw * (g.rect_max.y - g.rect_min.y) : 0;
-    uint32_t hits = 0;
-    if (candidate && area <= kSerialTiles) {
-        for (int ty = g.rect_min.y; ty < g.rect_max.y; ++ty) {
-            for (int tx = g.rect_min.x; tx < g.rect_max.x; ++tx) {
-                hits += tile_hit(r, tx, ty, g.xy, g.conic, g.power) ? 1u : 0u;
-            }
-        }
+    const uint32_t area = candidate ? static_cast<uint32_t>(gw * (g.rect_max.y - g.rect_min.y)) : 0u;
+    s_shape[threadIdx.x][0] = g.xy.x;
+    s_shape[threadIdx.x][1] = g.xy.y;
+    s_shape[threadIdx.x][2] = g.conic.x;
+    s_shape[threadIdx.x][3] = g.conic.y;
+    s_shape[threadIdx.x][4] = g.conic.z;
+    s_shape[threadIdx.x][5] = g.power;
+    s_rect[threadIdx.x][0] = g.rect_min.x;
+    s_rect[threadIdx.x][1] = g.rect_min.y;
+    s_rect[threadIdx.x][2] = gw;
+    s_hits[threadIdx.x] = 0;
+    uint32_t incl = area;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
     }
-    uint32_t pending = __ballot_sync(0xffffffffu, area > kSerialTiles);
-    while (pending != 0u) {
-        const int src = __ffs(pending) - 1;
-        pending &= pending - 1u;
-        const float2 xy = make_float2(__shfl_sync(0xffffffffu, g.xy.x, src),
-                                      __shfl_sync(0xffffffffu, g.xy.y, src));
-        const float3 conic = make_float3(__shfl_sync(0xffffffffu, g.conic.x, src),
-                                         __shfl_sync(0xffffffffu, g.conic.y, src),
-                                         __shfl_sync(0xffffffffu, g.conic.z, src));
-        const float power = __shfl_sync(0xffffffffu, g.power, src);
-        const int x0 = __shfl_sync(0xffffffffu, g.rect_min.x, src);
-        const int y0 = __shfl_sync(0xffffffffu, g.rect_min.y, src);
-        const int w = __shfl_sync(0xffffffffu, gw, src);
-        const int n = __shfl_sync(0xffffffffu, area, src);
-        uint32_t c = 0;
-        for (int t = lane; t < n; t += 32) {
-            c += tile_hit(r, x0 + t % w, y0 + t / w, xy, conic, power) ? 1u : 0u;
+    s_incl[threadIdx.x] = incl;
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    const uint32_t wbase = threadIdx.x & ~31u;
+    __syncwarp();
+    for (uint32_t f = lane; f < total; f += 32) {
+        uint32_t j = 0;
+#pragma unroll
+        for (uint32_t step = 16; step >= 1; step >>= 1) {
+            if (s_incl[wbase + j + step - 1] <= f) j += step;
         }
-        c = bin::warp_sum(c);
-        if (lane == src) hits = c;
+        const uint32_t o = wbase + j;
+        const uint32_t k = f - (j == 0 ? 0u : s_incl[o - 1]);
+        const int w = s_rect[o][2];
+        const int tx = s_rect[o][0] + static_cast<int>(k) % w;
+        const int ty = s_rect[o][1] + static_cast<int>(k) / w;
+        const float2 cxy = make_float2(s_shape[o][0], s_shape[o][1]);
+        const float3 cc = make_float3(s_shape[o][2], s_shape[o][3], s_shape[o][4]);
+        if (tile_hit(r, tx, ty, cxy, cc, s_shape[o][5])) atomicAdd(&s_hits[o], 1u);
     }
+    __syncwarp();
+    const uint32_t hits = s_hits[threadIdx.x];
     const uint32_t total_hits = bin::warp_sum(hits);
     if (lane == 0 && total_hits != 0u) atomicAdd(totals, total_hits);
     if (!active) return;
     // Single-tile Gaussians always keep their record (preprocess.cu:482-506).
-    const bool write = candidate && (area == 1 || hits > 0);
+    const bool write = candidate && (area == 1u || hits > 0);
     float4* rec = records + static_cast<size_t>(idx) * kRecordQuads;
     if (write) {
         float3 rgb;
@@ -162,6 +178,18 @@ struct Emitter {
         const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
         return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16)) <=
                static_cast<uint32_t>(2 * kSerialTiles);
+    }
+    __device__ __forceinline__ uint32_t slots(const Shape& s) const {
+        const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
+        return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16));
+    }
+    __device__ __forceinline__ bool pair_at(const Shape& s, uint32_t k, uint32_t& tile) const {
+        const R r;
+        const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
+        const int x0 = lo & 0xffff, y0 = lo >> 16, w = static_cast<int>(hi & 0xffff) - x0;
+        const int tx = x0 + static_cast<int>(k) % w, ty = y0 + static_cast<int>(k) / w;
+        tile = static_cast<uint32_t>(ty * grid_x + tx);
+        return tile_hit(r, tx, ty, make_float2(s.a.x, s.a.y), make_float3(s.a.z, s.a.w, s.b.x), s.b.y);
     }
     __device__ __forceinline__ void emit_serial(const Shape& s, uint32_t gid, uint32_t offset,
                                                 uint32_t count, uint32_t* tiles,

@@ -61,10 +61,20 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     if (blockIdx.x == 0 && threadIdx.x == 0) out.totals[3] = *out.error;
     uint32_t area = 0, emitted = 0, violation = 0;
     if (active) {
+        // All inputs are requested before any arithmetic; scales and
+        // rotations use 64/128-bit loads when their rows are aligned.
         const float3 p = make_float3(means[3 * idx], means[3 * idx + 1], means[3 * idx + 2]);
-        const float2 scale = make_float2(scales[2 * idx], scales[2 * idx + 1]);
-        const float4 rot = make_float4(rotations[4 * idx], rotations[4 * idx + 1],
-                                       rotations[4 * idx + 2], rotations[4 * idx + 3]);
+        const float2 scale = (reinterpret_cast<uintptr_t>(scales) & 7u) == 0
+                                 ? reinterpret_cast<const float2*>(scales)[idx]
+                                 : make_float2(scales[2 * idx], scales[2 * idx + 1]);
+        const float4 rot = (reinterpret_cast<uintptr_t>(rotations) & 15u) == 0
+                               ? reinterpret_cast<const float4*>(rotations)[idx]
+                               : make_float4(rotations[4 * idx], rotations[4 * idx + 1],
+                                             rotations[4 * idx + 2], rotations[4 * idx + 3]);
+        const float op_in = opacities[idx];
+        float col[5];
+#pragma unroll
+        for (int k = 0; k < 5; ++k) col[k] = colors5[5 * static_cast<size_t>(idx) + k];
         const Projected g = project_gaussian(r, view, proj, p, scale, scale_modifier, rot, width,
                                              height, grid_x, grid_y);
         violation = (g.behind && prefiltered) ? 1u : 0u;
@@ -74,8 +84,8 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
             out.counts[idx] = 0;
             out.depth_keys[idx] = 0xffffffffu;
         } else {
-            const float op = opacities[idx];
-            const float* c = colors5 + 5 * static_cast<size_t>(idx);
+            const float op = op_in;
+            const float* c = col;
             float4* rec = out.records + static_cast<size_t>(idx) * kRecordQuads;
             rec[0] = make_float4(g.xy.x, g.xy.y, g.normal.x, g.normal.y);
             rec[1] = make_float4(g.normal.z, op, c[0], c[1]);
