@@ -45,6 +45,14 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "FPS @1292x839, 1M base+200k refl Gaussians, 1/2/4/8 B200; per-stage ms"
 SCENE = "standard_1m"
+# Further workloads (--workload): the large view-sharded scene and the 4K
+# stress frame sharded by tile strips; the default is the benchmark view above.
+WORKLOADS = {
+    "view": ("standard_1m", METRIC, "view-sharded"),
+    "large_6m": ("large_6m", "FPS @1920x1080, 6M base+1M refl Gaussians, 160-view orbit, view-sharded", "view-sharded"),
+    "stress_4k": ("stress_4k", "frames/s of one 3840x2160 frame, 3M base+500k refl (inflated scales), tile-strip sharded",
+                  "tile-strip"),
+}
 SM_COUNT = 148
 # Algorithmic FP32 work of one pixel x Gaussian blend evaluation, counted
 # from the blend functions (FMA = 2 flop; each IEEE division and expf = 1):
@@ -63,6 +71,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--backend", choices=("standard", "flashgs"), default="standard")
+    p.add_argument("--workload", choices=tuple(WORKLOADS), default="view")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU oracle leg")
     p.add_argument("--no-reference-gpu", action="store_true", help="skip timing the reference CUDA rebuild")
     p.add_argument("--scale", type=float, default=1.0, help="Gaussian-count scale (profiling runs only)")
@@ -130,6 +139,7 @@ class Frame:
             self.r_in[2] = self.trace_rgb
         self.cam = None
         self.split = None  # list: per raster call stage timings (instrumented pass)
+        self.tile_rows = None  # (begin, end): render only this strip of tile rows
 
     def set_camera(self, cam, upload_from=None):
         """Per-view camera state. For the standard backend the matrices are
@@ -157,7 +167,7 @@ class Frame:
             base = ops.rasterize_forward(self.bg5, self.b_xyz, colors, self.b_op, self.b_scale, self.b_rot,
                                          self.view, self.proj, self.center, width=cam.width, height=cam.height,
                                          scale_modifier=1.0, tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy,
-                                         context=self.ctx)
+                                         context=self.ctx, tile_rows=self.tile_rows)
             rec(1)
             if self.split is not None:
                 self.split.append(("base", self.ctx.read_stage_timing()))
@@ -166,7 +176,7 @@ class Frame:
             base = ops.flashgs_forward(*self.b_in, width=cam.width, height=cam.height, use_sh=True,
                                        camera_position=cam.flashgs_position, camera_rotation=cam.flashgs_rotation9,
                                        focal_x=cam.fx, focal_y=cam.fy, initial_pair_capacity=2_000_000,
-                                       context=self.ctx)
+                                       context=self.ctx, tile_rows=self.tile_rows)
             rec(1)
             if self.split is not None:
                 self.split.append(("base", self.ctx.read_stage_timing()))
@@ -179,13 +189,13 @@ class Frame:
             refl = ops.rasterize_forward(self.bg5, self.r_xyz, self.r_colors, self.r_op, self.r_scale, self.r_rot,
                                          self.view, self.proj, self.center, width=cam.width, height=cam.height,
                                          scale_modifier=1.0, tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy,
-                                         context=self.ctx)
+                                         context=self.ctx, tile_rows=self.tile_rows)
             base_rgb, spec = base.color[:3], base.color[3:4]
         else:
             refl = ops.flashgs_forward(*self.r_in, width=cam.width, height=cam.height, use_sh=False,
                                        camera_position=cam.flashgs_position, camera_rotation=cam.flashgs_rotation9,
                                        focal_x=cam.fx, focal_y=cam.fy, initial_pair_capacity=2_000_000,
-                                       context=self.ctx)
+                                       context=self.ctx, tile_rows=self.tile_rows)
             base_rgb, spec = base.color, base.other[0:1]
         if self.split is not None:
             self.split.append(("reflection", self.ctx.read_stage_timing()))
@@ -381,7 +391,16 @@ def run_ours(args):
         from hybridsplat_jittor_render_b200.native_runtime import bind_library
         library = bind_library(REPO / "oracle" / "_ref" / "libref_hybridsplat.so", require_optix=False)
     frame = Frame(scene_np, args.backend, device, library=library)
-    views = [(info.rank + world * s) % 20 for s in range(args.warmup + args.steps)]
+    spec = scenes.SCENES[SCENE]
+    strips = WORKLOADS[args.workload][2] == "tile-strip"
+    if strips:
+        # one frame, rows of 16x16 tiles split across the ranks (strong scaling)
+        grid_y = (spec.height + 15) // 16
+        frame.tile_rows = multigpu.tile_strips(grid_y, world)[info.rank]
+        views = [0] * (args.warmup + args.steps)
+    else:
+        n_views = max(spec.views, 20)
+        views = [(info.rank + world * s) % n_views for s in range(args.warmup + args.steps)]
     cams = [scenes.orbit_camera(SCENE, v) for v in views]
     if args.profile_frames > 0:
         for s in range(args.profile_frames):
@@ -421,7 +440,7 @@ def run_ours(args):
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    fps_total = world * 1000.0 / ms
+    fps_total = (1 if strips else world) * 1000.0 / ms
 
     # per-stage ms (instrumented pass, not the headline): the view the CPU
     # oracle counts evaluations on (view 0), CUDA events between the frame
@@ -472,17 +491,22 @@ def run_ours(args):
 
     line = None
     if info.is_root:
+        what = (f"one {spec.width}x{spec.height} frame per step, tile rows split across the GPUs" if strips else
+                f"one {spec.width}x{spec.height} orbit view per step per GPU")
         line = {"metric": METRIC, "value": fps_total, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong" if strips else "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene with the benchmark "
                 "configuration's sizes and distributions; fixed synthetic trace colours)",
-                "config": {"workload": f"{args.backend} backend, 1M base + 200k reflection Gaussians, 1292x839, "
-                                       "one orbit view per step per GPU",
-                           "backend": args.backend, "gaussians": [frame.nb, frame.nr], "l2": "inputs larger than L2",
+                "config": {"workload": f"{args.backend} backend, {frame.nb} base + {frame.nr} reflection Gaussians, "
+                                       f"{what}",
+                           "scene": SCENE, "backend": args.backend, "gaussians": [frame.nb, frame.nr],
+                           "l2": "inputs larger than L2",
                            "priming": "one untimed render of each timed view before the warm-up steps",
-                           "parallelism": f"view-sharded x{world}"},
+                           "parallelism": f"{WORKLOADS[args.workload][2]} x{world}"},
                 "stages_ms": stages, "clocks": clocks.summary(),
-                "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "frames/s", "h2d_bytes_per_step": h2d,
+                "e2e": {"value": (1 if strips else world) * 1000.0 / e2e_ms, "unit": "frames/s",
+                        "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": frame.launches_per_step() * args.steps}
     if world > 1:
@@ -566,7 +590,11 @@ def roofline_and_baselines(args, frame, cams, stages, scene_np, clocks: dict) ->
 
 
 def main() -> int:
+    global SCENE, METRIC
     args = parse_args()
+    SCENE, METRIC, _ = WORKLOADS[args.workload]
+    if args.workload != "view":
+        args.no_cpu_baseline = True  # the CPU oracle would take minutes at these sizes
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_ours(args)

@@ -246,20 +246,20 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
 // Rasterisation order of the tiles: longest pair lists first (buckets by
 // the bit length of the list length; any order inside a bucket), so that the
 // persistent rasterisers take the expensive tiles before the cheap ones.
-// One block of kOrderThreads threads; `counter` (the rasteriser's work
-// counter) is reset here.
+// One block of kOrderThreads threads over tiles [tile_first, tile_first +
+// tile_count); `counter` (the rasteriser's work counter) is reset here.
 constexpr int kOrderThreads = 1024;
 
 template <class Range>
 __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
-    uint32_t tile_count, const Range* __restrict__ ranges, uint32_t* __restrict__ order,
-    uint32_t* __restrict__ counter) {
+    uint32_t tile_first, uint32_t tile_count, const Range* __restrict__ ranges,
+    uint32_t* __restrict__ order, uint32_t* __restrict__ counter) {
     __shared__ uint32_t hist[33];
     __shared__ uint32_t next[33];
     if (threadIdx.x < 33) hist[threadIdx.x] = 0;
     if (threadIdx.x == 0) *counter = 0;
     __syncthreads();
-    for (uint32_t t = threadIdx.x; t < tile_count; t += kOrderThreads) {
+    for (uint32_t t = tile_first + threadIdx.x; t < tile_first + tile_count; t += kOrderThreads) {
         const uint32_t len = static_cast<uint32_t>(ranges[t].y - ranges[t].x);
         atomicAdd(&hist[__clz(len)], 1u);
     }
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
         }
     }
     __syncthreads();
-    for (uint32_t t = threadIdx.x; t < tile_count; t += kOrderThreads) {
+    for (uint32_t t = tile_first + threadIdx.x; t < tile_first + tile_count; t += kOrderThreads) {
         const uint32_t len = static_cast<uint32_t>(ranges[t].y - ranges[t].x);
         order[atomicAdd(&next[__clz(len)], 1u)] = t;
     }

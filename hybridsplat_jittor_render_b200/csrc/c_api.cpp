@@ -238,6 +238,124 @@ int32_t elementwise(const char* name, uint64_t count, bool buffers_present, char
 
 }  // namespace
 
+static int32_t flashgs_entry(
+    uint32_t row_begin, uint32_t row_end, HsRasterizerHandle handle, uint64_t point_count, int32_t width, int32_t height,
+    const float* positions3, const float* shs48, const float* colors3, int32_t use_sh,
+    const float* opacities1, const float* covariance6, const float* scales2, float scale_modifier,
+    const float* rotations4, const float* specular1, const float* roughness1,
+    const float* camera_position3, const float* camera_rotation9, float focal_x, float focal_y,
+    float z_far, float z_near, const float* background3, uint64_t initial_pair_capacity,
+    float* output_color3, float* output_other2, float* output_depth1, float* output_alpha1,
+    float* output_normal3, float* output_median_depth1, float* output_distortion1,
+    int32_t* output_num_rendered, char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || camera_position3 == nullptr || camera_rotation9 == nullptr ||
+            background3 == nullptr || output_color3 == nullptr || output_other2 == nullptr ||
+            output_depth1 == nullptr || output_alpha1 == nullptr || output_normal3 == nullptr ||
+            output_median_depth1 == nullptr || output_distortion1 == nullptr ||
+            output_num_rendered == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "FlashGS received a null required handle or buffer", error_text,
+                        error_capacity);
+        }
+        if (point_count > static_cast<uint64_t>(INT_MAX) || width <= 0 || height <= 0 ||
+            (use_sh != 0 && use_sh != 1) || initial_pair_capacity == 0 ||
+            initial_pair_capacity > static_cast<uint64_t>(INT_MAX) ||
+            !std::isfinite(scale_modifier) || scale_modifier <= 0.0f || !std::isfinite(focal_x) ||
+            focal_x <= 0.0f || !std::isfinite(focal_y) || focal_y <= 0.0f ||
+            !std::isfinite(z_near) || z_near <= 0.0f || !std::isfinite(z_far) || z_far <= z_near) {
+            return fail(HS_STATUS_RANGE_ERROR, "FlashGS dimensions or scalar arguments are invalid",
+                        error_text, error_capacity);
+        }
+        if (!finite3(camera_position3) || !finite3(background3)) {
+            return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera position or background is not finite",
+                        error_text, error_capacity);
+        }
+        for (int i = 0; i < 9; ++i) {
+            if (!std::isfinite(camera_rotation9[i])) {
+                return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera rotation is not finite",
+                            error_text, error_capacity);
+            }
+        }
+        if (point_count != 0 &&
+            (positions3 == nullptr || opacities1 == nullptr || covariance6 == nullptr ||
+             scales2 == nullptr || rotations4 == nullptr || specular1 == nullptr ||
+             roughness1 == nullptr || (use_sh != 0 && shs48 == nullptr) ||
+             (use_sh == 0 && colors3 == nullptr))) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "non-empty FlashGS input contains a null buffer",
+                        error_text, error_capacity);
+        }
+        const uint32_t grid_y = static_cast<uint32_t>((height + 15) / 16);
+        if (row_begin >= row_end || (row_end != UINT32_MAX && row_end > grid_y)) {
+            return fail(HS_STATUS_RANGE_ERROR, "tile rows must satisfy 0 <= begin < end <= tile rows",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        const cudaError_t e = hs::flashgs_forward(
+            handle, static_cast<int32_t>(point_count), width, height, positions3, shs48, colors3,
+            use_sh != 0, opacities1, covariance6, scales2, scale_modifier, rotations4, specular1,
+            roughness1, camera_position3, camera_rotation9, focal_x, focal_y, z_far, z_near,
+            background3, initial_pair_capacity, output_color3, output_other2, output_depth1,
+            output_alpha1, output_normal3, output_median_depth1, output_distortion1,
+            output_num_rendered, nullptr, row_begin, row_end);
+        if (e != cudaSuccess)
+            return cuda_failure(e, "deterministic FlashGS forward", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+static int32_t rasterizer_entry(
+    uint32_t row_begin, uint32_t row_end, HsRasterizerHandle handle, uint64_t point_count, const float* background5, int32_t width,
+    int32_t height, const float* means3d, const float* colors5, const float* opacities,
+    const float* scales2, float scale_modifier, const float* rotations4,
+    const float* viewmatrix4x4, const float* projmatrix4x4, const float* camera_position3,
+    float tan_fovx, float tan_fovy, int32_t prefiltered, float* output_color5, float* output_aux7,
+    float* output_weight, int32_t* output_radii, int32_t* output_rendered, char* error_text,
+    uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || background5 == nullptr || output_color5 == nullptr ||
+            output_aux7 == nullptr || output_rendered == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "rasterizer received a null required handle or buffer", error_text,
+                        error_capacity);
+        }
+        if (point_count > static_cast<uint64_t>(INT_MAX) || width <= 0 || height <= 0 ||
+            !std::isfinite(scale_modifier) || !std::isfinite(tan_fovx) ||
+            !std::isfinite(tan_fovy) || tan_fovx <= 0.0f || tan_fovy <= 0.0f ||
+            (prefiltered != 0 && prefiltered != 1)) {
+            return fail(HS_STATUS_RANGE_ERROR, "rasterizer dimensions or scalar arguments are invalid",
+                        error_text, error_capacity);
+        }
+        if (point_count != 0 &&
+            (means3d == nullptr || colors5 == nullptr || opacities == nullptr ||
+             scales2 == nullptr || rotations4 == nullptr || viewmatrix4x4 == nullptr ||
+             projmatrix4x4 == nullptr || camera_position3 == nullptr ||
+             output_weight == nullptr || output_radii == nullptr)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "non-empty rasterizer input contains a null buffer", error_text,
+                        error_capacity);
+        }
+        const uint32_t grid_y = static_cast<uint32_t>((height + 15) / 16);
+        if (row_begin >= row_end || (row_end != UINT32_MAX && row_end > grid_y)) {
+            return fail(HS_STATUS_RANGE_ERROR, "tile rows must satisfy 0 <= begin < end <= tile rows",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        const cudaError_t e = hs::standard_forward(
+            handle, static_cast<int32_t>(point_count), background5, width, height, means3d,
+            colors5, opacities, scales2, scale_modifier, rotations4, viewmatrix4x4,
+            projmatrix4x4, camera_position3, tan_fovx, tan_fovy, prefiltered != 0, output_color5,
+            output_aux7, output_weight, output_radii, output_rendered, nullptr, row_begin, row_end);
+        if (e != cudaSuccess)
+            return cuda_failure(e, "five-channel rasterizer forward", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
 extern "C" {
 
 uint32_t hs_rasterizer_abi_version(void) noexcept { return HS_RASTERIZER_ABI_VERSION; }
@@ -413,57 +531,13 @@ int32_t hs_flashgs_forward_f32_v1(
     float* output_color3, float* output_other2, float* output_depth1, float* output_alpha1,
     float* output_normal3, float* output_median_depth1, float* output_distortion1,
     int32_t* output_num_rendered, char* error_text, uint64_t error_capacity) noexcept {
-    return guard(error_text, error_capacity, [&]() -> int32_t {
-        if (handle == nullptr || camera_position3 == nullptr || camera_rotation9 == nullptr ||
-            background3 == nullptr || output_color3 == nullptr || output_other2 == nullptr ||
-            output_depth1 == nullptr || output_alpha1 == nullptr || output_normal3 == nullptr ||
-            output_median_depth1 == nullptr || output_distortion1 == nullptr ||
-            output_num_rendered == nullptr) {
-            return fail(HS_STATUS_INVALID_ARGUMENT,
-                        "FlashGS received a null required handle or buffer", error_text,
-                        error_capacity);
-        }
-        if (point_count > static_cast<uint64_t>(INT_MAX) || width <= 0 || height <= 0 ||
-            (use_sh != 0 && use_sh != 1) || initial_pair_capacity == 0 ||
-            initial_pair_capacity > static_cast<uint64_t>(INT_MAX) ||
-            !std::isfinite(scale_modifier) || scale_modifier <= 0.0f || !std::isfinite(focal_x) ||
-            focal_x <= 0.0f || !std::isfinite(focal_y) || focal_y <= 0.0f ||
-            !std::isfinite(z_near) || z_near <= 0.0f || !std::isfinite(z_far) || z_far <= z_near) {
-            return fail(HS_STATUS_RANGE_ERROR, "FlashGS dimensions or scalar arguments are invalid",
-                        error_text, error_capacity);
-        }
-        if (!finite3(camera_position3) || !finite3(background3)) {
-            return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera position or background is not finite",
-                        error_text, error_capacity);
-        }
-        for (int i = 0; i < 9; ++i) {
-            if (!std::isfinite(camera_rotation9[i])) {
-                return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera rotation is not finite",
-                            error_text, error_capacity);
-            }
-        }
-        if (point_count != 0 &&
-            (positions3 == nullptr || opacities1 == nullptr || covariance6 == nullptr ||
-             scales2 == nullptr || rotations4 == nullptr || specular1 == nullptr ||
-             roughness1 == nullptr || (use_sh != 0 && shs48 == nullptr) ||
-             (use_sh == 0 && colors3 == nullptr))) {
-            return fail(HS_STATUS_INVALID_ARGUMENT, "non-empty FlashGS input contains a null buffer",
-                        error_text, error_capacity);
-        }
-        const int32_t ds = select_device(handle, error_text, error_capacity);
-        if (ds != HS_STATUS_OK) return ds;
-        std::lock_guard<std::mutex> lock(handle->mutex);
-        const cudaError_t e = hs::flashgs_forward(
-            handle, static_cast<int32_t>(point_count), width, height, positions3, shs48, colors3,
-            use_sh != 0, opacities1, covariance6, scales2, scale_modifier, rotations4, specular1,
-            roughness1, camera_position3, camera_rotation9, focal_x, focal_y, z_far, z_near,
-            background3, initial_pair_capacity, output_color3, output_other2, output_depth1,
-            output_alpha1, output_normal3, output_median_depth1, output_distortion1,
-            output_num_rendered, nullptr);
-        if (e != cudaSuccess)
-            return cuda_failure(e, "deterministic FlashGS forward", error_text, error_capacity);
-        return ok(error_text, error_capacity);
-    });
+    return flashgs_entry(
+        0u, UINT32_MAX, handle, point_count, width, height, positions3, shs48, colors3,
+        use_sh, opacities1, covariance6, scales2, scale_modifier, rotations4, specular1,
+        roughness1, camera_position3, camera_rotation9, focal_x, focal_y, z_far, z_near,
+        background3, initial_pair_capacity, output_color3, output_other2, output_depth1,
+        output_alpha1, output_normal3, output_median_depth1, output_distortion1,
+        output_num_rendered, error_text, error_capacity);
 }
 
 int32_t hs_flashgs_workspace_stats_v1(HsRasterizerHandle handle,
@@ -570,41 +644,11 @@ int32_t hs_rasterizer_forward_f32_v1(
     float tan_fovx, float tan_fovy, int32_t prefiltered, float* output_color5, float* output_aux7,
     float* output_weight, int32_t* output_radii, int32_t* output_rendered, char* error_text,
     uint64_t error_capacity) noexcept {
-    return guard(error_text, error_capacity, [&]() -> int32_t {
-        if (handle == nullptr || background5 == nullptr || output_color5 == nullptr ||
-            output_aux7 == nullptr || output_rendered == nullptr) {
-            return fail(HS_STATUS_INVALID_ARGUMENT,
-                        "rasterizer received a null required handle or buffer", error_text,
-                        error_capacity);
-        }
-        if (point_count > static_cast<uint64_t>(INT_MAX) || width <= 0 || height <= 0 ||
-            !std::isfinite(scale_modifier) || !std::isfinite(tan_fovx) ||
-            !std::isfinite(tan_fovy) || tan_fovx <= 0.0f || tan_fovy <= 0.0f ||
-            (prefiltered != 0 && prefiltered != 1)) {
-            return fail(HS_STATUS_RANGE_ERROR, "rasterizer dimensions or scalar arguments are invalid",
-                        error_text, error_capacity);
-        }
-        if (point_count != 0 &&
-            (means3d == nullptr || colors5 == nullptr || opacities == nullptr ||
-             scales2 == nullptr || rotations4 == nullptr || viewmatrix4x4 == nullptr ||
-             projmatrix4x4 == nullptr || camera_position3 == nullptr ||
-             output_weight == nullptr || output_radii == nullptr)) {
-            return fail(HS_STATUS_INVALID_ARGUMENT,
-                        "non-empty rasterizer input contains a null buffer", error_text,
-                        error_capacity);
-        }
-        const int32_t ds = select_device(handle, error_text, error_capacity);
-        if (ds != HS_STATUS_OK) return ds;
-        std::lock_guard<std::mutex> lock(handle->mutex);
-        const cudaError_t e = hs::standard_forward(
-            handle, static_cast<int32_t>(point_count), background5, width, height, means3d,
-            colors5, opacities, scales2, scale_modifier, rotations4, viewmatrix4x4,
-            projmatrix4x4, camera_position3, tan_fovx, tan_fovy, prefiltered != 0, output_color5,
-            output_aux7, output_weight, output_radii, output_rendered, nullptr);
-        if (e != cudaSuccess)
-            return cuda_failure(e, "five-channel rasterizer forward", error_text, error_capacity);
-        return ok(error_text, error_capacity);
-    });
+    return rasterizer_entry(
+        0u, UINT32_MAX, handle, point_count, background5, width, height, means3d, colors5,
+        opacities, scales2, scale_modifier, rotations4, viewmatrix4x4, projmatrix4x4,
+        camera_position3, tan_fovx, tan_fovy, prefiltered, output_color5, output_aux7,
+        output_weight, output_radii, output_rendered, error_text, error_capacity);
 }
 
 // OptiX entry points: the OptiX SDK is not part of this build.
@@ -1038,6 +1082,44 @@ int32_t hs_b200_rasterizer_forward_noalloc_f32_v1(
         }
         return ok(error_text, error_capacity);
     });
+}
+
+int32_t hs_b200_flashgs_forward_rows_f32_v1(
+    HsRasterizerHandle handle, uint32_t tile_row_begin, uint32_t tile_row_end,
+    uint64_t point_count, int32_t width, int32_t height, const float* positions3,
+    const float* shs48, const float* colors3, int32_t use_sh, const float* opacities1,
+    const float* covariance6, const float* scales2, float scale_modifier, const float* rotations4,
+    const float* specular1, const float* roughness1, const float* camera_position3,
+    const float* camera_rotation9, float focal_x, float focal_y, float z_far, float z_near,
+    const float* background3, uint64_t initial_pair_capacity, float* output_color3,
+    float* output_other2, float* output_depth1, float* output_alpha1, float* output_normal3,
+    float* output_median_depth1, float* output_distortion1, int32_t* output_num_rendered,
+    char* error_text, uint64_t error_capacity) noexcept {
+    if (tile_row_end == UINT32_MAX) tile_row_end = UINT32_MAX - 1;  // an explicit strip
+    return flashgs_entry(
+        tile_row_begin, tile_row_end, handle, point_count, width, height, positions3, shs48,
+        colors3, use_sh, opacities1, covariance6, scales2, scale_modifier, rotations4, specular1,
+        roughness1, camera_position3, camera_rotation9, focal_x, focal_y, z_far, z_near,
+        background3, initial_pair_capacity, output_color3, output_other2, output_depth1,
+        output_alpha1, output_normal3, output_median_depth1, output_distortion1,
+        output_num_rendered, error_text, error_capacity);
+}
+
+int32_t hs_b200_rasterizer_forward_rows_f32_v1(
+    HsRasterizerHandle handle, uint32_t tile_row_begin, uint32_t tile_row_end,
+    uint64_t point_count, const float* background5, int32_t width, int32_t height,
+    const float* means3d, const float* colors5, const float* opacities, const float* scales2,
+    float scale_modifier, const float* rotations4, const float* viewmatrix4x4,
+    const float* projmatrix4x4, const float* camera_position3, float tan_fovx, float tan_fovy,
+    int32_t prefiltered, float* output_color5, float* output_aux7, float* output_weight,
+    int32_t* output_radii, int32_t* output_rendered, char* error_text,
+    uint64_t error_capacity) noexcept {
+    if (tile_row_end == UINT32_MAX) tile_row_end = UINT32_MAX - 1;  // an explicit strip
+    return rasterizer_entry(
+        tile_row_begin, tile_row_end, handle, point_count, background5, width, height, means3d,
+        colors5, opacities, scales2, scale_modifier, rotations4, viewmatrix4x4, projmatrix4x4,
+        camera_position3, tan_fovx, tan_fovy, prefiltered, output_color5, output_aux7,
+        output_weight, output_radii, output_rendered, error_text, error_capacity);
 }
 
 }  // extern "C"

@@ -66,12 +66,16 @@ struct StageTimer {
 // every drained event set is complete.
 class StageMarks {
 public:
-    StageMarks(StageTimer& timer, cudaStream_t stream);
+    StageMarks() = default;
+    StageMarks(StageTimer& timer, cudaStream_t stream) { start(timer, stream); }
+    StageMarks(const StageMarks&) = delete;
+    StageMarks& operator=(const StageMarks&) = delete;
     ~StageMarks();
+    void start(StageTimer& timer, cudaStream_t stream);  // records boundary 0
     void mark(int boundary);  // 0 = start, 1 = after preprocess, 2 = before blend, 3 = end
 private:
     std::array<cudaEvent_t, 4>* set_ = nullptr;
-    cudaStream_t stream_;
+    cudaStream_t stream_ = nullptr;
     int next_ = 0;
 };
 
@@ -148,7 +152,9 @@ uint64_t standard_current_bytes(const HsRasterizerContext* context);
 cudaError_t flashgs_release(HsRasterizerContext* context);
 cudaError_t standard_release(HsRasterizerContext* context);
 
-// FlashGS forward (flashgs.cu). Arguments as in hs_flashgs_forward_f32_v1.
+// FlashGS forward (flashgs.cu). Arguments as in hs_flashgs_forward_f32_v1;
+// only 16x16 tile rows [row_begin, row_end) (clamped to the frame) are
+// binned and rendered, other output rows are left untouched.
 cudaError_t flashgs_forward(HsRasterizerContext* context, int32_t point_count, int32_t width,
                             int32_t height, const float* positions3, const float* shs48,
                             const float* colors3, bool use_sh, const float* opacities1,
@@ -161,7 +167,8 @@ cudaError_t flashgs_forward(HsRasterizerContext* context, int32_t point_count, i
                             float* output_other2, float* output_depth1, float* output_alpha1,
                             float* output_normal3, float* output_median_depth1,
                             float* output_distortion1, int32_t* output_num_rendered,
-                            cudaStream_t stream);
+                            cudaStream_t stream, uint32_t row_begin = 0,
+                            uint32_t row_end = UINT32_MAX);
 
 cudaError_t flashgs_debug_copy(HsRasterizerContext* context, uint64_t point_capacity,
                                uint64_t pair_capacity, uint64_t tile_capacity,
@@ -170,7 +177,8 @@ cudaError_t flashgs_debug_copy(HsRasterizerContext* context, uint64_t point_capa
                                float* tv3, float* tw3, uint64_t* sorted_keys,
                                uint32_t* sorted_values, int32_t* tile_ranges2);
 
-// Standard five-channel forward (standard.cu).
+// Standard five-channel forward (standard.cu); row_begin/row_end as for
+// flashgs_forward.
 cudaError_t standard_forward(HsRasterizerContext* context, int32_t point_count,
                              const float* background5, int32_t width, int32_t height,
                              const float* means3d, const float* colors5, const float* opacities,
@@ -179,7 +187,8 @@ cudaError_t standard_forward(HsRasterizerContext* context, int32_t point_count,
                              const float* camera_position3, float tan_fovx, float tan_fovy,
                              bool prefiltered, float* output_color5, float* output_aux7,
                              float* output_weight, int32_t* output_radii,
-                             int32_t* output_rendered, cudaStream_t stream);
+                             int32_t* output_rendered, cudaStream_t stream,
+                             uint32_t row_begin = 0, uint32_t row_end = UINT32_MAX);
 
 // FlashGS host-side camera matrices (preprocess.cu:599-627), column-major.
 void flashgs_camera_matrices(const float position[3], const float rotation9[9], int width,

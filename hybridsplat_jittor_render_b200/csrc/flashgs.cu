@@ -142,10 +142,12 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
                             float* output_other2, float* output_depth1, float* output_alpha1,
                             float* output_normal3, float* output_median_depth1,
                             float* output_distortion1, int32_t* output_num_rendered,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, uint32_t row_begin, uint32_t row_end) {
     using namespace fg;
     const int grid_x = (width + 15) / 16, grid_y = (height + 15) / 16;
     const uint64_t tiles = static_cast<uint64_t>(grid_x) * grid_y;
+    row_end = std::min(row_end, static_cast<uint32_t>(grid_y));
+    if (row_begin >= row_end) return cudaErrorInvalidValue;
 
     Camera cam;
     flashgs_camera_matrices(camera_position3, camera_rotation9, width, height, focal_x, focal_y,
@@ -205,7 +207,8 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
         preprocess_kernel<HS_FLASHGS_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
             point_count, cam, positions3, shs48, colors3, use_sh ? 1 : 0, opacities1,
             covariance6, scales2, scale_modifier, rotations4, specular1, roughness1, gv.records,
-            gv.emit, gv.keys, gv.order, gv.counts, gv.total, ctx->device_error);
+            gv.emit, gv.keys, gv.order, gv.counts, gv.total, ctx->device_error,
+            static_cast<int>(row_begin), static_cast<int>(row_end));
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
         st = cudaMemcpyAsync(ctx->fg_total_host, gv.total, 4 * sizeof(uint32_t),
@@ -291,8 +294,9 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
     if (num_rendered > 0) ids = pair_views(ctx->fg_pairs.ptr, ctx->fg_pair_capacity).ids;
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
+    const uint32_t strip_tiles = (row_end - row_begin) * static_cast<uint32_t>(grid_x);
     bin::tile_order_kernel<int2><<<1, bin::kOrderThreads, 0, stream>>>(
-        static_cast<uint32_t>(tiles), ranges, tile_order, work_counter);
+        row_begin * static_cast<uint32_t>(grid_x), strip_tiles, ranges, tile_order, work_counter);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     marks.mark(2);
@@ -301,10 +305,10 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, render_kernel<HS_FLASHGS_ROUNDING>,
                                                   kRenderThreads, 0);
     const uint32_t render_blocks = static_cast<uint32_t>(
-        std::min<uint64_t>(tiles, static_cast<uint64_t>(sms) * std::max(per_sm, 1)));
+        std::min<uint64_t>(strip_tiles, static_cast<uint64_t>(sms) * std::max(per_sm, 1)));
     render_kernel<HS_FLASHGS_ROUNDING><<<render_blocks, kRenderThreads, 0, stream>>>(
-        ranges, tile_order, static_cast<uint32_t>(tiles), work_counter, ids, gv.records, width,
-        height, grid_x, bg, bg_encoded, out);
+        ranges, tile_order, strip_tiles, work_counter, ids, gv.records, width, height, grid_x, bg,
+        bg_encoded, out);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     marks.mark(3);

@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     const float* __restrict__ specular, const float* __restrict__ roughness,
     float4* __restrict__ records, float4* __restrict__ emit, uint32_t* __restrict__ depth_keys,
     uint32_t* __restrict__ order, uint32_t* __restrict__ pair_counts,
-    uint32_t* __restrict__ totals, const uint32_t* __restrict__ error) {
+    uint32_t* __restrict__ totals, const uint32_t* __restrict__ error, int row_begin, int row_end) {
     const int idx = blockIdx.x * kPreThreads + threadIdx.x;
     const bool active = idx < point_count;
     const int lane = threadIdx.x & 31;
@@ -78,7 +78,11 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     __shared__ uint32_t s_hits[kPreThreads];
     const bool candidate = g.in_front && g.touches;
     const int gw = candidate ? g.rect_max.x - g.rect_min.x : 0;
-    const uint32_t area = candidate ? static_cast<uint32_t>(gw * (g.rect_max.y - g.rect_min.y)) : 0u;
+    const uint32_t full_area =
+        candidate ? static_cast<uint32_t>(gw * (g.rect_max.y - g.rect_min.y)) : 0u;
+    // rows of the rectangle inside the rendered tile rows
+    const int ry0 = max(g.rect_min.y, row_begin), ry1 = min(g.rect_max.y, row_end);
+    const uint32_t area = candidate && ry1 > ry0 ? static_cast<uint32_t>(gw * (ry1 - ry0)) : 0u;
     s_shape[threadIdx.x][0] = g.xy.x;
     s_shape[threadIdx.x][1] = g.xy.y;
     s_shape[threadIdx.x][2] = g.conic.x;
@@ -86,7 +90,7 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     s_shape[threadIdx.x][4] = g.conic.z;
     s_shape[threadIdx.x][5] = g.power;
     s_rect[threadIdx.x][0] = g.rect_min.x;
-    s_rect[threadIdx.x][1] = g.rect_min.y;
+    s_rect[threadIdx.x][1] = ry0;
     s_rect[threadIdx.x][2] = gw;
     s_hits[threadIdx.x] = 0;
     uint32_t incl = area;
@@ -120,7 +124,7 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     if (lane == 0 && total_hits != 0u) atomicAdd(totals, total_hits);
     if (!active) return;
     // Single-tile Gaussians always keep their record (preprocess.cu:482-506).
-    const bool write = candidate && (area == 1u || hits > 0);
+    const bool write = candidate && (full_area == 1u || hits > 0);
     float4* rec = records + static_cast<size_t>(idx) * kRecordQuads;
     if (write) {
         float3 rgb;
@@ -145,8 +149,8 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     }
     float4* em = emit + static_cast<size_t>(idx) * kEmitQuads;
     em[0] = f4(g.xy.x, g.xy.y, g.conic.x, g.conic.y);
-    const uint32_t lo = static_cast<uint32_t>(g.rect_min.x) | (static_cast<uint32_t>(g.rect_min.y) << 16);
-    const uint32_t hi = static_cast<uint32_t>(g.rect_max.x) | (static_cast<uint32_t>(g.rect_max.y) << 16);
+    const uint32_t lo = static_cast<uint32_t>(g.rect_min.x) | (static_cast<uint32_t>(area != 0u ? ry0 : 0) << 16);
+    const uint32_t hi = static_cast<uint32_t>(g.rect_max.x) | (static_cast<uint32_t>(area != 0u ? ry1 : 0) << 16);
     em[1] = f4(g.conic.z, g.power, __uint_as_float(lo), __uint_as_float(hi));
     depth_keys[idx] = hits > 0 ? __float_as_uint(g.depth) : 0xffffffffu;
     order[idx] = static_cast<uint32_t>(idx);

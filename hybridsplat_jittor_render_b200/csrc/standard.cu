@@ -114,7 +114,8 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
                              const float* camera_position3, float tan_fovx, float tan_fovy,
                              bool prefiltered, float* output_color5, float* output_aux7,
                              float* output_weight, int32_t* output_radii,
-                             int32_t* output_rendered, cudaStream_t stream) {
+                             int32_t* output_rendered, cudaStream_t stream, uint32_t row_begin,
+                             uint32_t row_end) {
     using namespace st;
     // Only the matrices drive the 2DGS projection; the camera position and
     // field of view are accepted for ABI compatibility (the reference passes
@@ -123,15 +124,26 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
     (void)tan_fovx;
     (void)tan_fovy;
     const uint64_t pixels = static_cast<uint64_t>(width) * static_cast<uint64_t>(height);
-    if (point_count == 0) {
-        // zero_outputs (full_rasterizer.cu:178-199) and nothing else.
-        cudaError_t st = cudaMemsetAsync(output_color5, 0, 5 * pixels * sizeof(float), stream);
-        if (st == cudaSuccess) st = cudaMemsetAsync(output_aux7, 0, 7 * pixels * sizeof(float), stream);
-        if (st == cudaSuccess) st = cudaMemsetAsync(output_rendered, 0, sizeof(int32_t), stream);
-        return st;
-    }
     const uint32_t grid_x = static_cast<uint32_t>((width + 15) / 16);
     const uint32_t grid_y = static_cast<uint32_t>((height + 15) / 16);
+    row_end = std::min(row_end, grid_y);
+    if (row_begin >= row_end) return cudaErrorInvalidValue;
+    const bool full_frame = row_begin == 0 && row_end == grid_y;
+    if (point_count == 0) {
+        // zero_outputs (full_rasterizer.cu:178-199) and nothing else.
+        cudaError_t st = cudaMemsetAsync(output_rendered, 0, sizeof(int32_t), stream);
+        if (full_frame) {
+            if (st == cudaSuccess) st = cudaMemsetAsync(output_color5, 0, 5 * pixels * sizeof(float), stream);
+            if (st == cudaSuccess) st = cudaMemsetAsync(output_aux7, 0, 7 * pixels * sizeof(float), stream);
+            return st;
+        }
+        const uint64_t y0 = uint64_t(row_begin) * 16, y1 = std::min<uint64_t>(uint64_t(row_end) * 16, height);
+        for (int c = 0; c < 12 && st == cudaSuccess; ++c) {
+            float* plane = c < 5 ? output_color5 + c * pixels : output_aux7 + (c - 5) * pixels;
+            st = cudaMemsetAsync(plane + y0 * width, 0, (y1 - y0) * width * sizeof(float), stream);
+        }
+        return st;
+    }
     const uint64_t tiles = static_cast<uint64_t>(grid_x) * grid_y;
     const uint64_t count = static_cast<uint64_t>(point_count);
     StageMarks marks(ctx->timer, stream);
@@ -174,7 +186,8 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
                      ctx->device_error};
     preprocess_kernel<HS_STANDARD_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
         point_count, viewmatrix4x4, projmatrix4x4, width, height, grid_x, grid_y, means3d,
-        colors5, opacities, scales2, scale_modifier, rotations4, prefiltered ? 1 : 0, po);
+        colors5, opacities, scales2, scale_modifier, rotations4, prefiltered ? 1 : 0, row_begin,
+        row_end, po);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     st = cudaMemcpyAsync(ctx->std_total_host, gv.totals, 4 * sizeof(uint32_t),
@@ -237,12 +250,13 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
     }
+    const uint32_t strip_tiles = (row_end - row_begin) * grid_x;
     bin::tile_order_kernel<uint2><<<1, bin::kOrderThreads, 0, stream>>>(
-        static_cast<uint32_t>(tiles), ranges, tile_order, work_counter);
+        row_begin * grid_x, strip_tiles, ranges, tile_order, work_counter);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     marks.mark(2);
-    const uint32_t items = static_cast<uint32_t>(tiles) * 4u;
+    const uint32_t items = strip_tiles * 4u;
     int sms = 148, per_sm = 1;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
     if (masked) {

@@ -37,14 +37,15 @@ __device__ __forceinline__ void warp_add(uint32_t* dst, uint32_t v) {
 // preprocessCUDA<5> (forward.cu:148-251) plus the cull shape. A Gaussian
 // emits the tiles of its reference rectangle (getRect) that also lie in the
 // bounding box of its live region; `rendered` still counts the whole
-// rectangle, as the reference does.
+// rectangle, as the reference does. Only tile rows [row_begin, row_end) are
+// rendered (the whole frame unless a caller renders a strip of it).
 template <class R>
 __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     int point_count, const float* __restrict__ viewmatrix, const float* __restrict__ projmatrix,
     int width, int height, uint32_t grid_x, uint32_t grid_y, const float* __restrict__ means,
     const float* __restrict__ colors5, const float* __restrict__ opacities,
     const float* __restrict__ scales, float scale_modifier, const float* __restrict__ rotations,
-    int prefiltered, PreprocessOut out) {
+    int prefiltered, uint32_t row_begin, uint32_t row_end, PreprocessOut out) {
     const int idx = blockIdx.x * kPreThreads + threadIdx.x;
     const bool active = idx < point_count;
     const R r;
@@ -92,15 +93,17 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
             rec[2] = make_float4(c[2], c[3], c[4], g.tu.x);
             rec[3] = make_float4(g.tu.y, g.tu.z, g.tv.x, g.tv.y);
             rec[4] = make_float4(g.tv.z, g.tw.x, g.tw.y, g.tw.z);
-            area = (g.rect_max.x - g.rect_min.x) * (g.rect_max.y - g.rect_min.y);
+            // pairs of the reference rectangle inside the rendered tile rows
+            const uint32_t ry0 = max(g.rect_min.y, row_begin), ry1 = min(g.rect_max.y, row_end);
+            area = ry1 > ry0 ? (g.rect_max.x - g.rect_min.x) * (ry1 - ry0) : 0u;
             const CullShape cs = cull_shape(op, g.xy.x, g.xy.y, g.tu, g.tv, g.tw);
             int bx0, by0, bx1, by1;
             int x0 = 0, y0 = 0, x1 = 0, y1 = 0;
             if (cull_tile_box(cs, bx0, by0, bx1, by1)) {
                 x0 = max(static_cast<int>(g.rect_min.x), bx0);
-                y0 = max(static_cast<int>(g.rect_min.y), by0);
+                y0 = max(static_cast<int>(max(g.rect_min.y, row_begin)), by0);
                 x1 = min(static_cast<int>(g.rect_max.x), bx1 + 1);
-                y1 = min(static_cast<int>(g.rect_max.y), by1 + 1);
+                y1 = min(static_cast<int>(min(g.rect_max.y, row_end)), by1 + 1);
                 if (x1 <= x0 || y1 <= y0) x0 = y0 = x1 = y1 = 0;
             }
             emitted = static_cast<uint32_t>((x1 - x0) * (y1 - y0));

@@ -160,7 +160,8 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
     PreprocessOut po{l.records, l.cull, l.keys, l.order, l.counts, output_radii, l.totals, l.error};
     preprocess_kernel<HS_STANDARD_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
         point_count, viewmatrix4x4, projmatrix4x4, width, height, grid_x, grid_y, means3d,
-        colors5, opacities, scales2, scale_modifier, rotations4, prefiltered ? 1 : 0, po);
+        colors5, opacities, scales2, scale_modifier, rotations4, prefiltered ? 1 : 0, 0u, grid_y,
+        po);
     st = cudaGetLastError();
     if (st != cudaSuccess) return {st, nullptr, 0, 0};
     st = sort::sort_pairs(l.keys, l.order, l.alt_keys, l.alt_order, point_count, 0, 32,
@@ -205,7 +206,7 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
     }
     bin::tile_order_kernel<uint2><<<1, bin::kOrderThreads, 0, stream>>>(
-        static_cast<uint32_t>(tiles), l.ranges, l.tile_order, l.work_counter);
+        0u, static_cast<uint32_t>(tiles), l.ranges, l.tile_order, l.work_counter);
     st = cudaGetLastError();
     if (st != cudaSuccess) return {st, nullptr, 0, 0};
     const uint32_t items = static_cast<uint32_t>(tiles) * 4u;

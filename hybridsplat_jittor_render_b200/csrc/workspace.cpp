@@ -47,7 +47,8 @@ cudaError_t release_buffer(DeviceBuffer& buffer) {
     return status;
 }
 
-StageMarks::StageMarks(StageTimer& timer, cudaStream_t stream) : stream_(stream) {
+void StageMarks::start(StageTimer& timer, cudaStream_t stream) {
+    stream_ = stream;
     if (!timer.enabled) return;
     if (timer.used >= StageTimer::kMaxPending) {
         ++timer.dropped;

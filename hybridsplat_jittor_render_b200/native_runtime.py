@@ -178,6 +178,16 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
 EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "hs_b200_stage_timing_enable_v1": (_I32, [_V, _I32, *_ERR]),
     "hs_b200_stage_timing_read_v1": (_I32, [_V, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_U64), *_ERR]),
+    "hs_b200_flashgs_forward_rows_f32_v1": (
+        _I32,
+        [_V, _U32, _U32, _U64, _I32, _I32, _V, _V, _V, _I32, _V, _V, _V, _F, _V, _V, _V, _V, _V, _F, _F, _F,
+         _F, _V, _U64, _V, _V, _V, _V, _V, _V, _V, _V, *_ERR],
+    ),
+    "hs_b200_rasterizer_forward_rows_f32_v1": (
+        _I32,
+        [_V, _U32, _U32, _U64, _V, _I32, _I32, _V, _V, _V, _V, _F, _V, _V, _V, _V, _F, _F, _I32, _V, _V, _V,
+         _V, _V, *_ERR],
+    ),
     "hs_b200_rasterizer_forward_noalloc_f32_v1": (
         _I32,
         [_I32, _U64, _V, _I32, _I32, _V, _V, _V, _V, _F, _V, _V, _V, _V, _F, _F, _I32, _V, _V, _V, _V,

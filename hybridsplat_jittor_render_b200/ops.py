@@ -108,8 +108,14 @@ def flashgs_forward(
     initial_pair_capacity: int = 1 << 20,
     context: NativeRendererContext,
     out: FlashgsOutputs | None = None,
+    tile_rows: tuple[int, int] | None = None,
 ) -> FlashgsOutputs:
-    """Deterministic FlashGS 16x16 forward; outputs are channel-first maps."""
+    """Deterministic FlashGS 16x16 forward; outputs are channel-first maps.
+
+    tile_rows=(begin, end) renders only 16x16 tile rows [begin, end) (library
+    extension for sharding one frame by strips): those rows are identical to a
+    full-frame call, the other output rows are left untouched.
+    """
     if isinstance(width, bool) or not isinstance(width, int) or width <= 0:
         raise ValueError("width must be a positive CPU integer")
     if isinstance(height, bool) or not isinstance(height, int) or height <= 0:
@@ -158,15 +164,22 @@ def flashgs_forward(
     rotation_host = (ctypes.c_float * 9)(*rotation)
     bg_host = (ctypes.c_float * 3)(*bg)
     error = error_buffer()
-    status = context.library.hs_flashgs_forward_f32_v1(
-        context.handle, count, width, height,
+    if tile_rows is not None:
+        call = context.library.hs_b200_flashgs_forward_rows_f32_v1
+        prefix = (context.handle, int(tile_rows[0]), int(tile_rows[1]))
+    else:
+        call = context.library.hs_flashgs_forward_f32_v1
+        prefix = (context.handle,)
+    status = call(
+        *prefix, count, width, height,
         _ptr(positions), _ptr(shs), _ptr(colors), int(use_sh), _ptr(opacities), _ptr(covariance),
         _ptr(scales), scale, _ptr(rotations), _ptr(specular), _ptr(roughness),
         ctypes.addressof(position_host), ctypes.addressof(rotation_host), fx, fy, far, near,
         ctypes.addressof(bg_host), initial_pair_capacity,
         *[t.data_ptr() for t in out], error, len(error),
     )
-    check_status(status, "hs_flashgs_forward_f32_v1", error)
+    check_status(status, "hs_b200_flashgs_forward_rows_f32_v1" if tile_rows is not None else
+                 "hs_flashgs_forward_f32_v1", error)
     return out
 
 
@@ -189,8 +202,13 @@ def rasterize_forward(
     prefiltered: bool = False,
     context: NativeRendererContext,
     out: RasterizerOutputs | None = None,
+    tile_rows: tuple[int, int] | None = None,
 ) -> RasterizerOutputs:
-    """Standard five-channel 2DGS forward (color[5,H,W], aux[7,H,W], ...)."""
+    """Standard five-channel 2DGS forward (color[5,H,W], aux[7,H,W], ...).
+
+    tile_rows=(begin, end): render only those 16x16 tile rows, as in
+    flashgs_forward (library extension).
+    """
     if isinstance(width, bool) or not isinstance(width, int) or width <= 0:
         raise ValueError("width must be a positive CPU integer")
     if isinstance(height, bool) or not isinstance(height, int) or height <= 0:
@@ -224,13 +242,20 @@ def rasterize_forward(
             torch.empty((1,), dtype=torch.int32, device=device),
         )
     error = error_buffer()
-    status = context.library.hs_rasterizer_forward_f32_v1(
-        context.handle, count, _ptr(background), width, height, _ptr(means3d), _ptr(colors),
+    if tile_rows is not None:
+        call = context.library.hs_b200_rasterizer_forward_rows_f32_v1
+        prefix = (context.handle, int(tile_rows[0]), int(tile_rows[1]))
+    else:
+        call = context.library.hs_rasterizer_forward_f32_v1
+        prefix = (context.handle,)
+    status = call(
+        *prefix, count, _ptr(background), width, height, _ptr(means3d), _ptr(colors),
         _ptr(opacities), _ptr(scales), scale, _ptr(rotations), _ptr(viewmatrix), _ptr(projmatrix),
         _ptr(camera_position), fovx, fovy, int(prefiltered),
         *[t.data_ptr() for t in out], error, len(error),
     )
-    check_status(status, "hs_rasterizer_forward_f32_v1", error)
+    check_status(status, "hs_b200_rasterizer_forward_rows_f32_v1" if tile_rows is not None else
+                 "hs_rasterizer_forward_f32_v1", error)
     return out
 
 

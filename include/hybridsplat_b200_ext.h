@@ -30,6 +30,38 @@ HS_API int32_t hs_b200_stage_timing_read_v1(
     HsRasterizerHandle handle, double* stage_ms3, uint64_t* raster_calls,
     char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
 
+/* Tile-strip variants of the two raster entry points, for sharding one frame
+ * across GPUs by rows of 16x16 tiles. Arguments are those of
+ * hs_flashgs_forward_f32_v1 / hs_rasterizer_forward_f32_v1 with the strip
+ * [tile_row_begin, tile_row_end) inserted after the handle (0 <= begin < end
+ * <= ceil(height / 16), else HS_STATUS_RANGE_ERROR). Every Gaussian is
+ * preprocessed, but pairs are emitted, sorted and rendered only for tiles of
+ * the strip: each tile's list is the full-frame list, so the strip's pixels are
+ * identical to those of a full-frame call. Only the strip's output rows are
+ * written; *num_rendered / *rendered count the strip's pairs. No counterpart
+ * in the reference library. */
+HS_API int32_t hs_b200_flashgs_forward_rows_f32_v1(
+    HsRasterizerHandle handle, uint32_t tile_row_begin, uint32_t tile_row_end,
+    uint64_t point_count, int32_t width, int32_t height, const float* positions3,
+    const float* shs48, const float* colors3, int32_t use_sh, const float* opacities1,
+    const float* covariance6, const float* scales2, float scale_modifier, const float* rotations4,
+    const float* specular1, const float* roughness1, const float* camera_position3,
+    const float* camera_rotation9, float focal_x, float focal_y, float z_far, float z_near,
+    const float* background3, uint64_t initial_pair_capacity, float* output_color3,
+    float* output_other2, float* output_depth1, float* output_alpha1, float* output_normal3,
+    float* output_median_depth1, float* output_distortion1, int32_t* output_num_rendered,
+    char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
+HS_API int32_t hs_b200_rasterizer_forward_rows_f32_v1(
+    HsRasterizerHandle handle, uint32_t tile_row_begin, uint32_t tile_row_end,
+    uint64_t point_count, const float* background5, int32_t width, int32_t height,
+    const float* means3d, const float* colors5, const float* opacities, const float* scales2,
+    float scale_modifier, const float* rotations4, const float* viewmatrix4x4,
+    const float* projmatrix4x4, const float* camera_position3, float tan_fovx, float tan_fovy,
+    int32_t prefiltered, float* output_color5, float* output_aux7, float* output_weight,
+    int32_t* output_radii, int32_t* output_rendered, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+
 /* The standard five-channel forward of hs_rasterizer_forward_f32_v1 without
  * any allocation: no context, no cudaMalloc/cudaFree/cudaHostAlloc. Every
  * scratch buffer comes from one 8 MiB device array inside the library (its
