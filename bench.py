@@ -69,6 +69,8 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--sequential", action="store_true",
+                   help="render the two raster branches one after the other (v1 calls) instead of concurrently")
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--backend", choices=("standard", "flashgs"), default="standard")
     p.add_argument("--workload", choices=tuple(WORKLOADS), default="view")
@@ -98,12 +100,16 @@ def reflection_trace_rgb(group) -> np.ndarray:
 class Frame:
     """Device-resident state and the per-view render sequence."""
 
-    def __init__(self, scene, backend: str, device, library=None):
+    def __init__(self, scene, backend: str, device, library=None, concurrent: bool = True):
         import torch
         from hybridsplat_jittor_render_b200 import NativeRendererContext, ops, scenes
         self.torch, self.ops, self.scenes = torch, ops, scenes
         self.backend, self.device, self.library = backend, device, library
         self.ctx = NativeRendererContext(device.index or 0, library=library)
+        # Concurrent branches (hs_b200_*_forward_many_v2) need a context each;
+        # sequential ones share one, as the reference session does.
+        self.concurrent = concurrent
+        self.ctx_r = NativeRendererContext(device.index or 0, library=library) if concurrent else self.ctx
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
         b, r = scene["base"], scene["reflection"]
         self.nb, self.nr = b["xyz"].shape[0], r["xyz"].shape[0]
@@ -156,49 +162,56 @@ class Frame:
 
     def render(self, events=None):
         """One view. `events`, when given, is a list of 5 CUDA events recorded
-        between the stages (base, reflection prepare, reflection, fusion)."""
+        between the stages (base, reflection prepare, reflection, fusion); the
+        branches then run one after the other so that each stage is timed
+        alone. Otherwise, with self.concurrent, both raster branches go to the
+        library in one concurrent call."""
         ops, torch, cam, lib = self.ops, self.torch, self.cam, self.library
+        sequential = events is not None or not self.concurrent
         rec = (lambda i: events[i].record()) if events else (lambda i: None)
         rec(0)
         if self.backend == "standard":
             d = ops.precise_direction(self.b_xyz, self.center, library=lib)
             rgb = ops.precise_sh_to_rgb(self.b_sh, d, 3, library=lib)
             colors = torch.cat([rgb, self.b_spec, self.b_rough], 1)
-            base = ops.rasterize_forward(self.bg5, self.b_xyz, colors, self.b_op, self.b_scale, self.b_rot,
-                                         self.view, self.proj, self.center, width=cam.width, height=cam.height,
-                                         scale_modifier=1.0, tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy,
-                                         context=self.ctx, tile_rows=self.tile_rows)
-            rec(1)
-            if self.split is not None:
-                self.split.append(("base", self.ctx.read_stage_timing()))
+            common = dict(viewmatrix=self.view, projmatrix=self.proj, camera_position=self.center, width=cam.width,
+                          height=cam.height, scale_modifier=1.0, tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy,
+                          tile_rows=self.tile_rows)
+            base_call = dict(background=self.bg5, means3d=self.b_xyz, colors=colors, opacities=self.b_op,
+                             scales=self.b_scale, rotations=self.b_rot, context=self.ctx, **common)
+            refl_call = dict(background=self.bg5, means3d=self.r_xyz, colors=self.r_colors, opacities=self.r_op,
+                             scales=self.r_scale, rotations=self.r_rot, context=self.ctx_r, **common)
+            single, many = ops.rasterize_forward, ops.rasterize_forward_many
             center = self.center
         else:
-            base = ops.flashgs_forward(*self.b_in, width=cam.width, height=cam.height, use_sh=True,
-                                       camera_position=cam.flashgs_position, camera_rotation=cam.flashgs_rotation9,
-                                       focal_x=cam.fx, focal_y=cam.fy, initial_pair_capacity=2_000_000,
-                                       context=self.ctx, tile_rows=self.tile_rows)
+            common = dict(width=cam.width, height=cam.height, camera_position=cam.flashgs_position,
+                          camera_rotation=cam.flashgs_rotation9, focal_x=cam.fx, focal_y=cam.fy,
+                          initial_pair_capacity=2_000_000, tile_rows=self.tile_rows)
+            names = ("positions", "shs", "colors", "opacities", "covariance", "scales", "rotations", "specular",
+                     "roughness")
+            base_call = dict(zip(names, self.b_in), use_sh=True, context=self.ctx, **common)
+            refl_call = dict(zip(names, self.r_in), use_sh=False, context=self.ctx_r, **common)
+            single, many = ops.flashgs_forward, ops.flashgs_forward_many
+            center = torch.from_numpy(self.scenes.standard_camera_center(cam)).to(self.device, non_blocking=True)
+        if sequential:
+            base = single(**base_call)
             rec(1)
             if self.split is not None:
                 self.split.append(("base", self.ctx.read_stage_timing()))
-            center = torch.from_numpy(self.scenes.standard_camera_center(cam)).to(self.device, non_blocking=True)
         rot = ops.precise_reflection_prefix(self.r_rot_raw, library=lib)
         normal_raw = rot[:, :, 2].contiguous()
         rays = ops.precise_reflection_suffix(self.r_xyz, center, normal_raw, library=lib)
         rec(2)
+        if sequential:
+            refl = single(**refl_call)
+            if self.split is not None:
+                self.split.append(("reflection", self.ctx_r.read_stage_timing()))
+        else:
+            base, refl = many([base_call, refl_call], stream=torch.cuda.current_stream(self.device).cuda_stream)
         if self.backend == "standard":
-            refl = ops.rasterize_forward(self.bg5, self.r_xyz, self.r_colors, self.r_op, self.r_scale, self.r_rot,
-                                         self.view, self.proj, self.center, width=cam.width, height=cam.height,
-                                         scale_modifier=1.0, tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy,
-                                         context=self.ctx, tile_rows=self.tile_rows)
             base_rgb, spec = base.color[:3], base.color[3:4]
         else:
-            refl = ops.flashgs_forward(*self.r_in, width=cam.width, height=cam.height, use_sh=False,
-                                       camera_position=cam.flashgs_position, camera_rotation=cam.flashgs_rotation9,
-                                       focal_x=cam.fx, focal_y=cam.fy, initial_pair_capacity=2_000_000,
-                                       context=self.ctx, tile_rows=self.tile_rows)
             base_rgb, spec = base.color, base.other[0:1]
-        if self.split is not None:
-            self.split.append(("reflection", self.ctx.read_stage_timing()))
         rec(3)
         fused = ops.precise_fuse_maps(base_rgb.permute(1, 2, 0).contiguous(),
                                       refl.color[:3].permute(1, 2, 0).contiguous(),
@@ -390,7 +403,7 @@ def run_ours(args):
     if args.profile_frames > 0 and args.profile_reference:
         from hybridsplat_jittor_render_b200.native_runtime import bind_library
         library = bind_library(REPO / "oracle" / "_ref" / "libref_hybridsplat.so", require_optix=False)
-    frame = Frame(scene_np, args.backend, device, library=library)
+    frame = Frame(scene_np, args.backend, device, library=library, concurrent=not args.sequential)
     spec = scenes.SCENES[SCENE]
     strips = WORKLOADS[args.workload][2] == "tile-strip"
     if strips:
@@ -448,8 +461,9 @@ def run_ours(args):
     stage_names = ("base_raster", "reflection_prepare", "reflection_raster", "fusion")
     sums = np.zeros(4)
     view0 = scenes.orbit_camera(SCENE, 0)
-    frame.ctx.stage_timing(True)
-    frame.ctx.read_stage_timing()
+    for c in {id(c): c for c in (frame.ctx, frame.ctx_r)}.values():
+        c.stage_timing(True)
+        c.read_stage_timing()
     frame.split = []
     for s in range(args.steps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
@@ -457,7 +471,8 @@ def run_ours(args):
         frame.render(ev)
         torch.cuda.synchronize()
         sums += [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
-    frame.ctx.stage_timing(False)
+    for c in {id(c): c for c in (frame.ctx, frame.ctx_r)}.values():
+        c.stage_timing(False)
     split, frame.split = frame.split, None
     stages = {k: float(v / args.steps) for k, v in zip(stage_names, sums)}
     for group in ("base", "reflection"):
@@ -469,21 +484,42 @@ def run_ours(args):
     pinned_cam = [torch.from_numpy(np.concatenate([c.world_view().reshape(-1), c.full_proj().reshape(-1),
                                                    scenes.standard_camera_center(c)]).astype(np.float32)).pin_memory()
                   for c in cams]
+    # Each frame's maps go back to pinned host memory on a copy stream, so the
+    # read-back of frame s overlaps the render of frame s + 1 (two host slots,
+    # as a streaming session would double-buffer them).
     res = frame.render()
-    host_maps = [torch.empty(m.shape, dtype=m.dtype, pin_memory=True) for m in frame.maps_for_host(res)]
-    d2h = sum(m.numel() * m.element_size() for m in host_maps)
+    host_maps = [[torch.empty(m.shape, dtype=m.dtype, pin_memory=True) for m in frame.maps_for_host(res)]
+                 for _ in range(2)]
+    d2h = sum(m.numel() * m.element_size() for m in host_maps[0])
     h2d = pinned_cam[0].numel() * 4 if args.backend == "standard" else 0
+    copy_stream = torch.cuda.Stream(device=device)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for s in range(args.steps):
         frame.set_camera(cams[args.warmup + s], upload_from=pinned_cam[args.warmup + s])
         res = frame.render()
-        for dst, src in zip(host_maps, frame.maps_for_host(res)):
-            dst.copy_(src, non_blocking=True)
+        copy_stream.wait_stream(stream)
+        with torch.cuda.stream(copy_stream):
+            for dst, src in zip(host_maps[s % 2], frame.maps_for_host(res)):
+                dst.copy_(src, non_blocking=True)
+                src.record_stream(copy_stream)
+    stream.wait_stream(copy_stream)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    # The same read-back alone (last frame's maps, same pinned slots): the
+    # host link bounds the end-to-end rate when it is slower than the render.
+    maps = frame.maps_for_host(res)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(copy_stream):
+        c0.record(copy_stream)
+        for s in range(args.steps):
+            for dst, src in zip(host_maps[s % 2], maps):
+                dst.copy_(src, non_blocking=True)
+        c1.record(copy_stream)
+    torch.cuda.synchronize()
+    d2h_ms = c0.elapsed_time(c1) / args.steps
     if world > 1:
         t = torch.tensor([e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -503,11 +539,18 @@ def run_ours(args):
                            "scene": SCENE, "backend": args.backend, "gaussians": [frame.nb, frame.nr],
                            "l2": "inputs larger than L2",
                            "priming": "one untimed render of each timed view before the warm-up steps",
-                           "parallelism": f"{WORKLOADS[args.workload][2]} x{world}"},
+                           "parallelism": f"{WORKLOADS[args.workload][2]} x{world}",
+                           "branches": "sequential v1 calls" if args.sequential else
+                                       "base and reflection rasters in one concurrent call "
+                                       "(hs_b200_*_forward_many_v2)",
+                           "stages_ms": "from a separate pass with the branches sequential, each stage alone"},
                 "stages_ms": stages, "clocks": clocks.summary(),
                 "e2e": {"value": (1 if strips else world) * 1000.0 / e2e_ms, "unit": "frames/s",
                         "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h},
+                        "d2h_bytes_per_step": d2h,
+                        "overlap": "maps of each frame copied to pinned host memory on a copy stream while "
+                                   "the next frame renders",
+                        "d2h_ms_alone": d2h_ms, "d2h_gbs_alone": d2h / (d2h_ms * 1e6)},
                 "gpu_launches": frame.launches_per_step() * args.steps}
     if world > 1:
         dist.barrier()
@@ -569,7 +612,7 @@ def roofline_and_baselines(args, frame, cams, stages, scene_np, clocks: dict) ->
         if ref_path.exists():
             from hybridsplat_jittor_render_b200.native_runtime import bind_library
             ref = bind_library(ref_path, require_optix=False)
-            rframe = Frame(scene_np, args.backend, frame.device, library=ref)
+            rframe = Frame(scene_np, args.backend, frame.device, library=ref, concurrent=False)
             for s in range(args.warmup):
                 rframe.set_camera(cams[s])
                 rframe.render()

@@ -21,6 +21,7 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "context.h"
 #include "precise.h"
@@ -238,8 +239,151 @@ int32_t elementwise(const char* name, uint64_t count, bool buffers_present, char
 
 }  // namespace
 
-static int32_t flashgs_entry(
-    uint32_t row_begin, uint32_t row_end, HsRasterizerHandle handle, uint64_t point_count, int32_t width, int32_t height,
+namespace {
+
+// Checks one FlashGS call as hs_flashgs_forward_f32_v1 does and converts it
+// (the host camera and background are copied).
+int32_t check_flashgs(const HsB200FlashgsCallV2& a, hs::FlashgsCall* call, char* error_text,
+                      uint64_t error_capacity) {
+    if (a.handle == nullptr || a.camera_position3 == nullptr || a.camera_rotation9 == nullptr ||
+        a.background3 == nullptr || a.output_color3 == nullptr || a.output_other2 == nullptr ||
+        a.output_depth1 == nullptr || a.output_alpha1 == nullptr || a.output_normal3 == nullptr ||
+        a.output_median_depth1 == nullptr || a.output_distortion1 == nullptr ||
+        a.output_num_rendered == nullptr) {
+        return fail(HS_STATUS_INVALID_ARGUMENT, "FlashGS received a null required handle or buffer",
+                    error_text, error_capacity);
+    }
+    if (a.point_count > static_cast<uint64_t>(INT_MAX) || a.width <= 0 || a.height <= 0 ||
+        (a.use_sh != 0 && a.use_sh != 1) || a.initial_pair_capacity == 0 ||
+        a.initial_pair_capacity > static_cast<uint64_t>(INT_MAX) ||
+        !std::isfinite(a.scale_modifier) || a.scale_modifier <= 0.0f ||
+        !std::isfinite(a.focal_x) || a.focal_x <= 0.0f || !std::isfinite(a.focal_y) ||
+        a.focal_y <= 0.0f || !std::isfinite(a.z_near) || a.z_near <= 0.0f ||
+        !std::isfinite(a.z_far) || a.z_far <= a.z_near) {
+        return fail(HS_STATUS_RANGE_ERROR, "FlashGS dimensions or scalar arguments are invalid",
+                    error_text, error_capacity);
+    }
+    if (!finite3(a.camera_position3) || !finite3(a.background3)) {
+        return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera position or background is not finite",
+                    error_text, error_capacity);
+    }
+    for (int i = 0; i < 9; ++i) {
+        if (!std::isfinite(a.camera_rotation9[i])) {
+            return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera rotation is not finite", error_text,
+                        error_capacity);
+        }
+    }
+    if (a.point_count != 0 &&
+        (a.positions3 == nullptr || a.opacities1 == nullptr || a.covariance6 == nullptr ||
+         a.scales2 == nullptr || a.rotations4 == nullptr || a.specular1 == nullptr ||
+         a.roughness1 == nullptr || (a.use_sh != 0 && a.shs48 == nullptr) ||
+         (a.use_sh == 0 && a.colors3 == nullptr))) {
+        return fail(HS_STATUS_INVALID_ARGUMENT, "non-empty FlashGS input contains a null buffer",
+                    error_text, error_capacity);
+    }
+    const uint32_t grid_y = static_cast<uint32_t>((a.height + 15) / 16);
+    if (a.tile_row_begin >= a.tile_row_end ||
+        (a.tile_row_end != UINT32_MAX && a.tile_row_end > grid_y)) {
+        return fail(HS_STATUS_RANGE_ERROR, "tile rows must satisfy 0 <= begin < end <= tile rows",
+                    error_text, error_capacity);
+    }
+    hs::FlashgsCall& c = *call;
+    c.point_count = static_cast<int32_t>(a.point_count);
+    c.width = a.width;
+    c.height = a.height;
+    c.positions3 = a.positions3;
+    c.shs48 = a.shs48;
+    c.colors3 = a.colors3;
+    c.use_sh = a.use_sh != 0;
+    c.opacities1 = a.opacities1;
+    c.covariance6 = a.covariance6;
+    c.scales2 = a.scales2;
+    c.scale_modifier = a.scale_modifier;
+    c.rotations4 = a.rotations4;
+    c.specular1 = a.specular1;
+    c.roughness1 = a.roughness1;
+    std::memcpy(c.camera_position3, a.camera_position3, sizeof(c.camera_position3));
+    std::memcpy(c.camera_rotation9, a.camera_rotation9, sizeof(c.camera_rotation9));
+    c.focal_x = a.focal_x;
+    c.focal_y = a.focal_y;
+    c.z_far = a.z_far;
+    c.z_near = a.z_near;
+    std::memcpy(c.background3, a.background3, sizeof(c.background3));
+    c.initial_pair_capacity = a.initial_pair_capacity;
+    c.output_color3 = a.output_color3;
+    c.output_other2 = a.output_other2;
+    c.output_depth1 = a.output_depth1;
+    c.output_alpha1 = a.output_alpha1;
+    c.output_normal3 = a.output_normal3;
+    c.output_median_depth1 = a.output_median_depth1;
+    c.output_distortion1 = a.output_distortion1;
+    c.output_num_rendered = a.output_num_rendered;
+    c.stream = nullptr;
+    c.row_begin = a.tile_row_begin;
+    c.row_end = a.tile_row_end;
+    return HS_STATUS_OK;
+}
+
+// Checks one standard call as hs_rasterizer_forward_f32_v1 does and converts it.
+int32_t check_rasterizer(const HsB200RasterizerCallV2& a, hs::StandardCall* call,
+                         char* error_text, uint64_t error_capacity) {
+    if (a.handle == nullptr || a.background5 == nullptr || a.output_color5 == nullptr ||
+        a.output_aux7 == nullptr || a.output_rendered == nullptr) {
+        return fail(HS_STATUS_INVALID_ARGUMENT,
+                    "rasterizer received a null required handle or buffer", error_text,
+                    error_capacity);
+    }
+    if (a.point_count > static_cast<uint64_t>(INT_MAX) || a.width <= 0 || a.height <= 0 ||
+        !std::isfinite(a.scale_modifier) || !std::isfinite(a.tan_fovx) ||
+        !std::isfinite(a.tan_fovy) || a.tan_fovx <= 0.0f || a.tan_fovy <= 0.0f ||
+        (a.prefiltered != 0 && a.prefiltered != 1)) {
+        return fail(HS_STATUS_RANGE_ERROR, "rasterizer dimensions or scalar arguments are invalid",
+                    error_text, error_capacity);
+    }
+    if (a.point_count != 0 &&
+        (a.means3d == nullptr || a.colors5 == nullptr || a.opacities == nullptr ||
+         a.scales2 == nullptr || a.rotations4 == nullptr || a.viewmatrix4x4 == nullptr ||
+         a.projmatrix4x4 == nullptr || a.camera_position3 == nullptr ||
+         a.output_weight == nullptr || a.output_radii == nullptr)) {
+        return fail(HS_STATUS_INVALID_ARGUMENT, "non-empty rasterizer input contains a null buffer",
+                    error_text, error_capacity);
+    }
+    const uint32_t grid_y = static_cast<uint32_t>((a.height + 15) / 16);
+    if (a.tile_row_begin >= a.tile_row_end ||
+        (a.tile_row_end != UINT32_MAX && a.tile_row_end > grid_y)) {
+        return fail(HS_STATUS_RANGE_ERROR, "tile rows must satisfy 0 <= begin < end <= tile rows",
+                    error_text, error_capacity);
+    }
+    hs::StandardCall& c = *call;
+    c.point_count = static_cast<int32_t>(a.point_count);
+    c.background5 = a.background5;
+    c.width = a.width;
+    c.height = a.height;
+    c.means3d = a.means3d;
+    c.colors5 = a.colors5;
+    c.opacities = a.opacities;
+    c.scales2 = a.scales2;
+    c.scale_modifier = a.scale_modifier;
+    c.rotations4 = a.rotations4;
+    c.viewmatrix4x4 = a.viewmatrix4x4;
+    c.projmatrix4x4 = a.projmatrix4x4;
+    c.camera_position3 = a.camera_position3;
+    c.tan_fovx = a.tan_fovx;
+    c.tan_fovy = a.tan_fovy;
+    c.prefiltered = a.prefiltered != 0;
+    c.output_color5 = a.output_color5;
+    c.output_aux7 = a.output_aux7;
+    c.output_weight = a.output_weight;
+    c.output_radii = a.output_radii;
+    c.output_rendered = a.output_rendered;
+    c.stream = nullptr;
+    c.row_begin = a.tile_row_begin;
+    c.row_end = a.tile_row_end;
+    return HS_STATUS_OK;
+}
+
+HsB200FlashgsCallV2 flashgs_args(
+    HsRasterizerHandle handle, uint64_t point_count, int32_t width, int32_t height,
     const float* positions3, const float* shs48, const float* colors3, int32_t use_sh,
     const float* opacities1, const float* covariance6, const float* scales2, float scale_modifier,
     const float* rotations4, const float* specular1, const float* roughness1,
@@ -247,114 +391,154 @@ static int32_t flashgs_entry(
     float z_far, float z_near, const float* background3, uint64_t initial_pair_capacity,
     float* output_color3, float* output_other2, float* output_depth1, float* output_alpha1,
     float* output_normal3, float* output_median_depth1, float* output_distortion1,
-    int32_t* output_num_rendered, char* error_text, uint64_t error_capacity) noexcept {
+    int32_t* output_num_rendered) {
+    HsB200FlashgsCallV2 a{};
+    a.handle = handle;
+    a.point_count = point_count;
+    a.width = width;
+    a.height = height;
+    a.positions3 = positions3;
+    a.shs48 = shs48;
+    a.colors3 = colors3;
+    a.use_sh = use_sh;
+    a.scale_modifier = scale_modifier;
+    a.opacities1 = opacities1;
+    a.covariance6 = covariance6;
+    a.scales2 = scales2;
+    a.rotations4 = rotations4;
+    a.specular1 = specular1;
+    a.roughness1 = roughness1;
+    a.camera_position3 = camera_position3;
+    a.camera_rotation9 = camera_rotation9;
+    a.focal_x = focal_x;
+    a.focal_y = focal_y;
+    a.z_far = z_far;
+    a.z_near = z_near;
+    a.background3 = background3;
+    a.initial_pair_capacity = initial_pair_capacity;
+    a.output_color3 = output_color3;
+    a.output_other2 = output_other2;
+    a.output_depth1 = output_depth1;
+    a.output_alpha1 = output_alpha1;
+    a.output_normal3 = output_normal3;
+    a.output_median_depth1 = output_median_depth1;
+    a.output_distortion1 = output_distortion1;
+    a.output_num_rendered = output_num_rendered;
+    a.tile_row_begin = 0;
+    a.tile_row_end = UINT32_MAX;
+    return a;
+}
+
+HsB200RasterizerCallV2 rasterizer_args(
+    HsRasterizerHandle handle, uint64_t point_count, const float* background5, int32_t width,
+    int32_t height, const float* means3d, const float* colors5, const float* opacities,
+    const float* scales2, float scale_modifier, const float* rotations4,
+    const float* viewmatrix4x4, const float* projmatrix4x4, const float* camera_position3,
+    float tan_fovx, float tan_fovy, int32_t prefiltered, float* output_color5, float* output_aux7,
+    float* output_weight, int32_t* output_radii, int32_t* output_rendered) {
+    HsB200RasterizerCallV2 a{};
+    a.handle = handle;
+    a.point_count = point_count;
+    a.background5 = background5;
+    a.width = width;
+    a.height = height;
+    a.means3d = means3d;
+    a.colors5 = colors5;
+    a.opacities = opacities;
+    a.scales2 = scales2;
+    a.scale_modifier = scale_modifier;
+    a.prefiltered = prefiltered;
+    a.rotations4 = rotations4;
+    a.viewmatrix4x4 = viewmatrix4x4;
+    a.projmatrix4x4 = projmatrix4x4;
+    a.camera_position3 = camera_position3;
+    a.tan_fovx = tan_fovx;
+    a.tan_fovy = tan_fovy;
+    a.output_color5 = output_color5;
+    a.output_aux7 = output_aux7;
+    a.output_weight = output_weight;
+    a.output_radii = output_radii;
+    a.output_rendered = output_rendered;
+    a.tile_row_begin = 0;
+    a.tile_row_end = UINT32_MAX;
+    return a;
+}
+
+int32_t flashgs_entry(const HsB200FlashgsCallV2& a, char* error_text,
+                      uint64_t error_capacity) noexcept {
     return guard(error_text, error_capacity, [&]() -> int32_t {
-        if (handle == nullptr || camera_position3 == nullptr || camera_rotation9 == nullptr ||
-            background3 == nullptr || output_color3 == nullptr || output_other2 == nullptr ||
-            output_depth1 == nullptr || output_alpha1 == nullptr || output_normal3 == nullptr ||
-            output_median_depth1 == nullptr || output_distortion1 == nullptr ||
-            output_num_rendered == nullptr) {
-            return fail(HS_STATUS_INVALID_ARGUMENT,
-                        "FlashGS received a null required handle or buffer", error_text,
-                        error_capacity);
-        }
-        if (point_count > static_cast<uint64_t>(INT_MAX) || width <= 0 || height <= 0 ||
-            (use_sh != 0 && use_sh != 1) || initial_pair_capacity == 0 ||
-            initial_pair_capacity > static_cast<uint64_t>(INT_MAX) ||
-            !std::isfinite(scale_modifier) || scale_modifier <= 0.0f || !std::isfinite(focal_x) ||
-            focal_x <= 0.0f || !std::isfinite(focal_y) || focal_y <= 0.0f ||
-            !std::isfinite(z_near) || z_near <= 0.0f || !std::isfinite(z_far) || z_far <= z_near) {
-            return fail(HS_STATUS_RANGE_ERROR, "FlashGS dimensions or scalar arguments are invalid",
-                        error_text, error_capacity);
-        }
-        if (!finite3(camera_position3) || !finite3(background3)) {
-            return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera position or background is not finite",
-                        error_text, error_capacity);
-        }
-        for (int i = 0; i < 9; ++i) {
-            if (!std::isfinite(camera_rotation9[i])) {
-                return fail(HS_STATUS_RANGE_ERROR, "FlashGS camera rotation is not finite",
-                            error_text, error_capacity);
-            }
-        }
-        if (point_count != 0 &&
-            (positions3 == nullptr || opacities1 == nullptr || covariance6 == nullptr ||
-             scales2 == nullptr || rotations4 == nullptr || specular1 == nullptr ||
-             roughness1 == nullptr || (use_sh != 0 && shs48 == nullptr) ||
-             (use_sh == 0 && colors3 == nullptr))) {
-            return fail(HS_STATUS_INVALID_ARGUMENT, "non-empty FlashGS input contains a null buffer",
-                        error_text, error_capacity);
-        }
-        const uint32_t grid_y = static_cast<uint32_t>((height + 15) / 16);
-        if (row_begin >= row_end || (row_end != UINT32_MAX && row_end > grid_y)) {
-            return fail(HS_STATUS_RANGE_ERROR, "tile rows must satisfy 0 <= begin < end <= tile rows",
-                        error_text, error_capacity);
-        }
-        const int32_t ds = select_device(handle, error_text, error_capacity);
+        hs::FlashgsCall call;
+        const int32_t cs = check_flashgs(a, &call, error_text, error_capacity);
+        if (cs != HS_STATUS_OK) return cs;
+        const int32_t ds = select_device(a.handle, error_text, error_capacity);
         if (ds != HS_STATUS_OK) return ds;
-        std::lock_guard<std::mutex> lock(handle->mutex);
-        const cudaError_t e = hs::flashgs_forward(
-            handle, static_cast<int32_t>(point_count), width, height, positions3, shs48, colors3,
-            use_sh != 0, opacities1, covariance6, scales2, scale_modifier, rotations4, specular1,
-            roughness1, camera_position3, camera_rotation9, focal_x, focal_y, z_far, z_near,
-            background3, initial_pair_capacity, output_color3, output_other2, output_depth1,
-            output_alpha1, output_normal3, output_median_depth1, output_distortion1,
-            output_num_rendered, nullptr, row_begin, row_end);
+        std::lock_guard<std::mutex> lock(a.handle->mutex);
+        const cudaError_t e = hs::flashgs_forward(a.handle, call);
         if (e != cudaSuccess)
             return cuda_failure(e, "deterministic FlashGS forward", error_text, error_capacity);
         return ok(error_text, error_capacity);
     });
 }
 
-static int32_t rasterizer_entry(
-    uint32_t row_begin, uint32_t row_end, HsRasterizerHandle handle, uint64_t point_count, const float* background5, int32_t width,
-    int32_t height, const float* means3d, const float* colors5, const float* opacities,
-    const float* scales2, float scale_modifier, const float* rotations4,
-    const float* viewmatrix4x4, const float* projmatrix4x4, const float* camera_position3,
-    float tan_fovx, float tan_fovy, int32_t prefiltered, float* output_color5, float* output_aux7,
-    float* output_weight, int32_t* output_radii, int32_t* output_rendered, char* error_text,
-    uint64_t error_capacity) noexcept {
+int32_t rasterizer_entry(const HsB200RasterizerCallV2& a, char* error_text,
+                         uint64_t error_capacity) noexcept {
     return guard(error_text, error_capacity, [&]() -> int32_t {
-        if (handle == nullptr || background5 == nullptr || output_color5 == nullptr ||
-            output_aux7 == nullptr || output_rendered == nullptr) {
-            return fail(HS_STATUS_INVALID_ARGUMENT,
-                        "rasterizer received a null required handle or buffer", error_text,
-                        error_capacity);
-        }
-        if (point_count > static_cast<uint64_t>(INT_MAX) || width <= 0 || height <= 0 ||
-            !std::isfinite(scale_modifier) || !std::isfinite(tan_fovx) ||
-            !std::isfinite(tan_fovy) || tan_fovx <= 0.0f || tan_fovy <= 0.0f ||
-            (prefiltered != 0 && prefiltered != 1)) {
-            return fail(HS_STATUS_RANGE_ERROR, "rasterizer dimensions or scalar arguments are invalid",
-                        error_text, error_capacity);
-        }
-        if (point_count != 0 &&
-            (means3d == nullptr || colors5 == nullptr || opacities == nullptr ||
-             scales2 == nullptr || rotations4 == nullptr || viewmatrix4x4 == nullptr ||
-             projmatrix4x4 == nullptr || camera_position3 == nullptr ||
-             output_weight == nullptr || output_radii == nullptr)) {
-            return fail(HS_STATUS_INVALID_ARGUMENT,
-                        "non-empty rasterizer input contains a null buffer", error_text,
-                        error_capacity);
-        }
-        const uint32_t grid_y = static_cast<uint32_t>((height + 15) / 16);
-        if (row_begin >= row_end || (row_end != UINT32_MAX && row_end > grid_y)) {
-            return fail(HS_STATUS_RANGE_ERROR, "tile rows must satisfy 0 <= begin < end <= tile rows",
-                        error_text, error_capacity);
-        }
-        const int32_t ds = select_device(handle, error_text, error_capacity);
+        hs::StandardCall call;
+        const int32_t cs = check_rasterizer(a, &call, error_text, error_capacity);
+        if (cs != HS_STATUS_OK) return cs;
+        const int32_t ds = select_device(a.handle, error_text, error_capacity);
         if (ds != HS_STATUS_OK) return ds;
-        std::lock_guard<std::mutex> lock(handle->mutex);
-        const cudaError_t e = hs::standard_forward(
-            handle, static_cast<int32_t>(point_count), background5, width, height, means3d,
-            colors5, opacities, scales2, scale_modifier, rotations4, viewmatrix4x4,
-            projmatrix4x4, camera_position3, tan_fovx, tan_fovy, prefiltered != 0, output_color5,
-            output_aux7, output_weight, output_radii, output_rendered, nullptr, row_begin, row_end);
+        std::lock_guard<std::mutex> lock(a.handle->mutex);
+        const cudaError_t e = hs::standard_forward(a.handle, call);
         if (e != cudaSuccess)
             return cuda_failure(e, "five-channel rasterizer forward", error_text, error_capacity);
         return ok(error_text, error_capacity);
     });
 }
+
+// Shared body of the forward_many entry points: checks every call before
+// anything is queued, requires distinct handles on one device, locks the
+// handles in address order and runs the calls concurrently.
+template <class Args, class Call, class Check, class Run>
+int32_t many_entry(const Args* calls, uint32_t call_count, void* stream, const char* what,
+                   Check&& check, Run&& run, char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (calls == nullptr && call_count != 0) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "calls is null", error_text, error_capacity);
+        }
+        if (call_count == 0) return ok(error_text, error_capacity);
+        std::vector<Call> converted(call_count);
+        std::vector<HsRasterizerContext*> contexts(call_count);
+        for (uint32_t i = 0; i < call_count; ++i) {
+            const int32_t cs = check(calls[i], &converted[i], error_text, error_capacity);
+            if (cs != HS_STATUS_OK) return cs;
+            contexts[i] = calls[i].handle;
+        }
+        for (uint32_t i = 0; i < call_count; ++i) {
+            if (contexts[i]->device != contexts[0]->device) {
+                return fail(HS_STATUS_INVALID_ARGUMENT, "all calls must use handles of one device",
+                            error_text, error_capacity);
+            }
+        }
+        std::vector<HsRasterizerContext*> lock_order = contexts;
+        std::sort(lock_order.begin(), lock_order.end());
+        if (std::adjacent_find(lock_order.begin(), lock_order.end()) != lock_order.end()) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "each call needs its own handle", error_text,
+                        error_capacity);
+        }
+        const int32_t ds = select_device(contexts[0], error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::vector<std::unique_lock<std::mutex>> locks;
+        locks.reserve(call_count);
+        for (HsRasterizerContext* c : lock_order) locks.emplace_back(c->mutex);
+        const cudaError_t e = run(contexts.data(), converted.data(), call_count,
+                                  static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_failure(e, what, error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -515,6 +699,7 @@ int32_t hs_rasterizer_destroy(HsRasterizerHandle handle, char* error_text,
             if (handle->std_count_event != nullptr) cudaEventDestroy(handle->std_count_event);
             if (handle->fg_count_event != nullptr) cudaEventDestroy(handle->fg_count_event);
             if (handle->device_error != nullptr) cudaFree(handle->device_error);
+            hs::destroy_side_stream(handle);
         }
         delete handle;
         return ok(error_text, error_capacity);
@@ -532,12 +717,13 @@ int32_t hs_flashgs_forward_f32_v1(
     float* output_normal3, float* output_median_depth1, float* output_distortion1,
     int32_t* output_num_rendered, char* error_text, uint64_t error_capacity) noexcept {
     return flashgs_entry(
-        0u, UINT32_MAX, handle, point_count, width, height, positions3, shs48, colors3,
-        use_sh, opacities1, covariance6, scales2, scale_modifier, rotations4, specular1,
-        roughness1, camera_position3, camera_rotation9, focal_x, focal_y, z_far, z_near,
-        background3, initial_pair_capacity, output_color3, output_other2, output_depth1,
-        output_alpha1, output_normal3, output_median_depth1, output_distortion1,
-        output_num_rendered, error_text, error_capacity);
+        flashgs_args(handle, point_count, width, height, positions3, shs48, colors3, use_sh,
+                     opacities1, covariance6, scales2, scale_modifier, rotations4, specular1,
+                     roughness1, camera_position3, camera_rotation9, focal_x, focal_y, z_far,
+                     z_near, background3, initial_pair_capacity, output_color3, output_other2,
+                     output_depth1, output_alpha1, output_normal3, output_median_depth1,
+                     output_distortion1, output_num_rendered),
+        error_text, error_capacity);
 }
 
 int32_t hs_flashgs_workspace_stats_v1(HsRasterizerHandle handle,
@@ -645,10 +831,11 @@ int32_t hs_rasterizer_forward_f32_v1(
     float* output_weight, int32_t* output_radii, int32_t* output_rendered, char* error_text,
     uint64_t error_capacity) noexcept {
     return rasterizer_entry(
-        0u, UINT32_MAX, handle, point_count, background5, width, height, means3d, colors5,
-        opacities, scales2, scale_modifier, rotations4, viewmatrix4x4, projmatrix4x4,
-        camera_position3, tan_fovx, tan_fovy, prefiltered, output_color5, output_aux7,
-        output_weight, output_radii, output_rendered, error_text, error_capacity);
+        rasterizer_args(handle, point_count, background5, width, height, means3d, colors5,
+                        opacities, scales2, scale_modifier, rotations4, viewmatrix4x4,
+                        projmatrix4x4, camera_position3, tan_fovx, tan_fovy, prefiltered,
+                        output_color5, output_aux7, output_weight, output_radii, output_rendered),
+        error_text, error_capacity);
 }
 
 // OptiX entry points: the OptiX SDK is not part of this build.
@@ -1095,14 +1282,16 @@ int32_t hs_b200_flashgs_forward_rows_f32_v1(
     float* output_other2, float* output_depth1, float* output_alpha1, float* output_normal3,
     float* output_median_depth1, float* output_distortion1, int32_t* output_num_rendered,
     char* error_text, uint64_t error_capacity) noexcept {
-    if (tile_row_end == UINT32_MAX) tile_row_end = UINT32_MAX - 1;  // an explicit strip
-    return flashgs_entry(
-        tile_row_begin, tile_row_end, handle, point_count, width, height, positions3, shs48,
-        colors3, use_sh, opacities1, covariance6, scales2, scale_modifier, rotations4, specular1,
-        roughness1, camera_position3, camera_rotation9, focal_x, focal_y, z_far, z_near,
-        background3, initial_pair_capacity, output_color3, output_other2, output_depth1,
-        output_alpha1, output_normal3, output_median_depth1, output_distortion1,
-        output_num_rendered, error_text, error_capacity);
+    HsB200FlashgsCallV2 a = flashgs_args(
+        handle, point_count, width, height, positions3, shs48, colors3, use_sh, opacities1,
+        covariance6, scales2, scale_modifier, rotations4, specular1, roughness1, camera_position3,
+        camera_rotation9, focal_x, focal_y, z_far, z_near, background3, initial_pair_capacity,
+        output_color3, output_other2, output_depth1, output_alpha1, output_normal3,
+        output_median_depth1, output_distortion1, output_num_rendered);
+    a.tile_row_begin = tile_row_begin;
+    // an explicit strip: UINT32_MAX is out of range here, not "whole frame"
+    a.tile_row_end = tile_row_end == UINT32_MAX ? UINT32_MAX - 1 : tile_row_end;
+    return flashgs_entry(a, error_text, error_capacity);
 }
 
 int32_t hs_b200_rasterizer_forward_rows_f32_v1(
@@ -1114,12 +1303,30 @@ int32_t hs_b200_rasterizer_forward_rows_f32_v1(
     int32_t prefiltered, float* output_color5, float* output_aux7, float* output_weight,
     int32_t* output_radii, int32_t* output_rendered, char* error_text,
     uint64_t error_capacity) noexcept {
-    if (tile_row_end == UINT32_MAX) tile_row_end = UINT32_MAX - 1;  // an explicit strip
-    return rasterizer_entry(
-        tile_row_begin, tile_row_end, handle, point_count, background5, width, height, means3d,
-        colors5, opacities, scales2, scale_modifier, rotations4, viewmatrix4x4, projmatrix4x4,
-        camera_position3, tan_fovx, tan_fovy, prefiltered, output_color5, output_aux7,
-        output_weight, output_radii, output_rendered, error_text, error_capacity);
+    HsB200RasterizerCallV2 a = rasterizer_args(
+        handle, point_count, background5, width, height, means3d, colors5, opacities, scales2,
+        scale_modifier, rotations4, viewmatrix4x4, projmatrix4x4, camera_position3, tan_fovx,
+        tan_fovy, prefiltered, output_color5, output_aux7, output_weight, output_radii,
+        output_rendered);
+    a.tile_row_begin = tile_row_begin;
+    a.tile_row_end = tile_row_end == UINT32_MAX ? UINT32_MAX - 1 : tile_row_end;
+    return rasterizer_entry(a, error_text, error_capacity);
+}
+
+int32_t hs_b200_flashgs_forward_many_v2(const HsB200FlashgsCallV2* calls, uint32_t call_count,
+                                        void* stream, char* error_text,
+                                        uint64_t error_capacity) noexcept {
+    return many_entry<HsB200FlashgsCallV2, hs::FlashgsCall>(
+        calls, call_count, stream, "concurrent FlashGS forward", check_flashgs,
+        hs::flashgs_forward_many, error_text, error_capacity);
+}
+
+int32_t hs_b200_rasterizer_forward_many_v2(const HsB200RasterizerCallV2* calls,
+                                           uint32_t call_count, void* stream, char* error_text,
+                                           uint64_t error_capacity) noexcept {
+    return many_entry<HsB200RasterizerCallV2, hs::StandardCall>(
+        calls, call_count, stream, "concurrent five-channel rasterizer forward", check_rasterizer,
+        hs::standard_forward_many, error_text, error_capacity);
 }
 
 }  // extern "C"

@@ -83,6 +83,9 @@ cudaError_t stage_timing_read(StageTimer& timer, double out_ms[3], uint64_t* cal
 
 // Allocates and zeroes context->device_error on first use.
 cudaError_t ensure_device_error(HsRasterizerContext* context);
+// Creates context->side_stream, side_event and fork_event on first use.
+cudaError_t ensure_side_stream(HsRasterizerContext* context);
+void destroy_side_stream(HsRasterizerContext* context);
 void stage_timing_destroy(StageTimer& timer);
 
 }  // namespace hs
@@ -143,6 +146,12 @@ struct HsRasterizerContext {
     uint32_t* device_error = nullptr;
     cudaEvent_t std_count_event = nullptr;  // marks the standard totals readback
     cudaEvent_t fg_count_event = nullptr;   // marks the FlashGS totals readback
+
+    // Concurrent calls (forward_many): this context's calls run on its own
+    // non-blocking stream, ordered against the caller's stream by events.
+    cudaStream_t side_stream = nullptr;
+    cudaEvent_t side_event = nullptr;  // phase marks on side_stream
+    cudaEvent_t fork_event = nullptr;  // recorded on the caller's stream
 };
 
 namespace hs {
@@ -152,23 +161,77 @@ uint64_t standard_current_bytes(const HsRasterizerContext* context);
 cudaError_t flashgs_release(HsRasterizerContext* context);
 cudaError_t standard_release(HsRasterizerContext* context);
 
-// FlashGS forward (flashgs.cu). Arguments as in hs_flashgs_forward_f32_v1;
-// only 16x16 tile rows [row_begin, row_end) (clamped to the frame) are
-// binned and rendered, other output rows are left untouched.
-cudaError_t flashgs_forward(HsRasterizerContext* context, int32_t point_count, int32_t width,
-                            int32_t height, const float* positions3, const float* shs48,
-                            const float* colors3, bool use_sh, const float* opacities1,
-                            const float* covariance6, const float* scales2, float scale_modifier,
-                            const float* rotations4, const float* specular1,
-                            const float* roughness1, const float camera_position3[3],
-                            const float camera_rotation9[9], float focal_x, float focal_y,
-                            float z_far, float z_near, const float background3[3],
-                            uint64_t initial_pair_capacity, float* output_color3,
-                            float* output_other2, float* output_depth1, float* output_alpha1,
-                            float* output_normal3, float* output_median_depth1,
-                            float* output_distortion1, int32_t* output_num_rendered,
-                            cudaStream_t stream, uint32_t row_begin = 0,
-                            uint32_t row_end = UINT32_MAX);
+// Arguments of one FlashGS raster call, as in hs_flashgs_forward_f32_v1
+// (host camera position, rotation and background are copied in). Only the
+// 16x16 tile rows [row_begin, row_end) (clamped to the frame) are binned and
+// rendered; other output rows are left untouched.
+struct FlashgsCall {
+    int32_t point_count = 0;
+    int32_t width = 0, height = 0;
+    const float* positions3 = nullptr;
+    const float* shs48 = nullptr;
+    const float* colors3 = nullptr;
+    bool use_sh = false;
+    const float* opacities1 = nullptr;
+    const float* covariance6 = nullptr;
+    const float* scales2 = nullptr;
+    float scale_modifier = 1.0f;
+    const float* rotations4 = nullptr;
+    const float* specular1 = nullptr;
+    const float* roughness1 = nullptr;
+    float camera_position3[3] = {};
+    float camera_rotation9[9] = {};
+    float focal_x = 0.0f, focal_y = 0.0f, z_far = 0.0f, z_near = 0.0f;
+    float background3[3] = {};
+    uint64_t initial_pair_capacity = 1;
+    float* output_color3 = nullptr;
+    float* output_other2 = nullptr;
+    float* output_depth1 = nullptr;
+    float* output_alpha1 = nullptr;
+    float* output_normal3 = nullptr;
+    float* output_median_depth1 = nullptr;
+    float* output_distortion1 = nullptr;
+    int32_t* output_num_rendered = nullptr;
+    cudaStream_t stream = nullptr;
+    uint32_t row_begin = 0, row_end = UINT32_MAX;
+};
+
+// Arguments of one standard raster call, as in hs_rasterizer_forward_f32_v1,
+// with the same tile-row restriction.
+struct StandardCall {
+    int32_t point_count = 0;
+    const float* background5 = nullptr;
+    int32_t width = 0, height = 0;
+    const float* means3d = nullptr;
+    const float* colors5 = nullptr;
+    const float* opacities = nullptr;
+    const float* scales2 = nullptr;
+    float scale_modifier = 1.0f;
+    const float* rotations4 = nullptr;
+    const float* viewmatrix4x4 = nullptr;
+    const float* projmatrix4x4 = nullptr;
+    const float* camera_position3 = nullptr;
+    float tan_fovx = 0.0f, tan_fovy = 0.0f;
+    bool prefiltered = false;
+    float* output_color5 = nullptr;
+    float* output_aux7 = nullptr;
+    float* output_weight = nullptr;
+    int32_t* output_radii = nullptr;
+    int32_t* output_rendered = nullptr;
+    cudaStream_t stream = nullptr;
+    uint32_t row_begin = 0, row_end = UINT32_MAX;
+};
+
+// FlashGS forward (flashgs.cu) on call.stream.
+cudaError_t flashgs_forward(HsRasterizerContext* context, const FlashgsCall& call);
+
+// Independent FlashGS calls, one context each (distinct contexts), run
+// concurrently on the contexts' side streams: all preprocess and binning
+// stages are queued before any tile renderer, and `stream` (the caller's)
+// is ordered before and after all of them. Each call's stream field is
+// ignored. Outputs are identical to flashgs_forward of each call.
+cudaError_t flashgs_forward_many(HsRasterizerContext* const* contexts, const FlashgsCall* calls,
+                                 uint32_t count, cudaStream_t stream);
 
 cudaError_t flashgs_debug_copy(HsRasterizerContext* context, uint64_t point_capacity,
                                uint64_t pair_capacity, uint64_t tile_capacity,
@@ -177,18 +240,13 @@ cudaError_t flashgs_debug_copy(HsRasterizerContext* context, uint64_t point_capa
                                float* tv3, float* tw3, uint64_t* sorted_keys,
                                uint32_t* sorted_values, int32_t* tile_ranges2);
 
-// Standard five-channel forward (standard.cu); row_begin/row_end as for
-// flashgs_forward.
-cudaError_t standard_forward(HsRasterizerContext* context, int32_t point_count,
-                             const float* background5, int32_t width, int32_t height,
-                             const float* means3d, const float* colors5, const float* opacities,
-                             const float* scales2, float scale_modifier, const float* rotations4,
-                             const float* viewmatrix4x4, const float* projmatrix4x4,
-                             const float* camera_position3, float tan_fovx, float tan_fovy,
-                             bool prefiltered, float* output_color5, float* output_aux7,
-                             float* output_weight, int32_t* output_radii,
-                             int32_t* output_rendered, cudaStream_t stream,
-                             uint32_t row_begin = 0, uint32_t row_end = UINT32_MAX);
+// Standard five-channel forward (standard.cu) on call.stream.
+cudaError_t standard_forward(HsRasterizerContext* context, const StandardCall& call);
+
+// Independent standard calls run as flashgs_forward_many runs FlashGS calls.
+cudaError_t standard_forward_many(HsRasterizerContext* const* contexts,
+                                  const StandardCall* calls, uint32_t count,
+                                  cudaStream_t stream);
 
 // FlashGS host-side camera matrices (preprocess.cu:599-627), column-major.
 void flashgs_camera_matrices(const float position[3], const float rotation9[9], int width,

@@ -28,6 +28,7 @@
 #include <cstring>
 #include <vector>
 
+#include "concurrent.h"
 #include "context.h"
 
 // Rounding policy of the kernels: the pinned forms that reproduce the
@@ -130,204 +131,241 @@ cudaError_t flashgs_release(HsRasterizerContext* ctx) {
     return first;
 }
 
-cudaError_t flashgs_forward(HsRasterizerContext* ctx, int32_t point_count, int32_t width,
-                            int32_t height, const float* positions3, const float* shs48,
-                            const float* colors3, bool use_sh, const float* opacities1,
-                            const float* covariance6, const float* scales2, float scale_modifier,
-                            const float* rotations4, const float* specular1,
-                            const float* roughness1, const float camera_position3[3],
-                            const float camera_rotation9[9], float focal_x, float focal_y,
-                            float z_far, float z_near, const float background3[3],
-                            uint64_t initial_pair_capacity, float* output_color3,
-                            float* output_other2, float* output_depth1, float* output_alpha1,
-                            float* output_normal3, float* output_median_depth1,
-                            float* output_distortion1, int32_t* output_num_rendered,
-                            cudaStream_t stream, uint32_t row_begin, uint32_t row_end) {
-    using namespace fg;
-    const int grid_x = (width + 15) / 16, grid_y = (height + 15) / 16;
-    const uint64_t tiles = static_cast<uint64_t>(grid_x) * grid_y;
-    row_end = std::min(row_end, static_cast<uint32_t>(grid_y));
-    if (row_begin >= row_end) return cudaErrorInvalidValue;
+namespace fg {
+namespace {
 
-    Camera cam;
-    flashgs_camera_matrices(camera_position3, camera_rotation9, width, height, focal_x, focal_y,
-                            z_far, z_near, cam.view, cam.proj);
-    for (int k = 0; k < 3; ++k) cam.campos[k] = camera_position3[k];
-    cam.tan_fovx = static_cast<float>(width) / (2.0f * focal_x);
-    cam.tan_fovy = static_cast<float>(height) / (2.0f * focal_y);
-    cam.focal_x = focal_x;
-    cam.focal_y = focal_y;
-    cam.width = width;
-    cam.height = height;
-    cam.grid_x = grid_x;
-    cam.grid_y = grid_y;
+// One FlashGS raster call in the three phases of run_many (concurrent.h).
+class FlashgsPass {
+public:
+    FlashgsPass(HsRasterizerContext* ctx, const FlashgsCall& call) : ctx_(ctx), c_(call) {}
+    cudaError_t begin();
+    cudaError_t bin();
+    cudaError_t render();
 
-    StageMarks marks(ctx->timer, stream);
+private:
+    HsRasterizerContext* ctx_;
+    FlashgsCall c_;
+    StageMarks marks_;
+    Camera cam_{};
+    int grid_x_ = 0, grid_y_ = 0;
+    uint64_t tiles_ = 0;
+    int2* ranges_ = nullptr;
+    uint32_t* tile_order_ = nullptr;
+    uint32_t* work_counter_ = nullptr;
+    uint32_t num_rendered_ = 0;
+    GaussianViews gv_{};
+    uint64_t sort_need_ = 0;
+};
+
+cudaError_t FlashgsPass::begin() {
+    const cudaStream_t stream = c_.stream;
+    grid_x_ = (c_.width + 15) / 16;
+    grid_y_ = (c_.height + 15) / 16;
+    tiles_ = static_cast<uint64_t>(grid_x_) * grid_y_;
+    c_.row_end = std::min(c_.row_end, static_cast<uint32_t>(grid_y_));
+    if (c_.row_begin >= c_.row_end) return cudaErrorInvalidValue;
+
+    flashgs_camera_matrices(c_.camera_position3, c_.camera_rotation9, c_.width, c_.height,
+                            c_.focal_x, c_.focal_y, c_.z_far, c_.z_near, cam_.view, cam_.proj);
+    for (int k = 0; k < 3; ++k) cam_.campos[k] = c_.camera_position3[k];
+    cam_.tan_fovx = static_cast<float>(c_.width) / (2.0f * c_.focal_x);
+    cam_.tan_fovy = static_cast<float>(c_.height) / (2.0f * c_.focal_y);
+    cam_.focal_x = c_.focal_x;
+    cam_.focal_y = c_.focal_y;
+    cam_.width = c_.width;
+    cam_.height = c_.height;
+    cam_.grid_x = grid_x_;
+    cam_.grid_y = grid_y_;
+
+    marks_.start(ctx_->timer, stream);
     // ranges, rasterisation order of the tiles, work counter
-    cudaError_t st = ensure_buffer(ctx->fg_ranges, tiles * (sizeof(int2) + sizeof(uint32_t)) + 256,
-                                   &ctx->fg_growth_count);
+    cudaError_t st = ensure_buffer(ctx_->fg_ranges, tiles_ * (sizeof(int2) + sizeof(uint32_t)) + 256,
+                                   &ctx_->fg_growth_count);
     if (st != cudaSuccess) return st;
-    ctx->fg_range_capacity = std::max<uint64_t>(ctx->fg_range_capacity, tiles);
-    int2* ranges = static_cast<int2*>(ctx->fg_ranges.ptr);
-    uint32_t* tile_order = reinterpret_cast<uint32_t*>(ranges + tiles);
-    uint32_t* work_counter = tile_order + tiles;
-    st = cudaMemsetAsync(ranges, 0, tiles * sizeof(int2), stream);
+    ctx_->fg_range_capacity = std::max<uint64_t>(ctx_->fg_range_capacity, tiles_);
+    ranges_ = static_cast<int2*>(ctx_->fg_ranges.ptr);
+    tile_order_ = reinterpret_cast<uint32_t*>(ranges_ + tiles_);
+    work_counter_ = tile_order_ + tiles_;
+    st = cudaMemsetAsync(ranges_, 0, tiles_ * sizeof(int2), stream);
+    if (st != cudaSuccess || c_.point_count == 0) return st;
+
+    if (ctx_->fg_total_host == nullptr) {
+        st = cudaHostAlloc(reinterpret_cast<void**>(&ctx_->fg_total_host), 4 * sizeof(uint32_t),
+                           cudaHostAllocPortable);
+        if (st != cudaSuccess) return st;
+        ++ctx_->fg_growth_count;
+    }
+    st = ensure_device_error(ctx_);
+    if (st != cudaSuccess) return st;
+    if (ctx_->fg_count_event == nullptr) {
+        st = cudaEventCreateWithFlags(&ctx_->fg_count_event, cudaEventDisableTiming);
+        if (st != cudaSuccess) return st;
+    }
+    const uint64_t count = static_cast<uint64_t>(c_.point_count);
+    if (count > ctx_->fg_gaussian_capacity || ctx_->fg_gaussian.ptr == nullptr) {
+        st = ensure_buffer(ctx_->fg_gaussian, gaussian_bytes(count), &ctx_->fg_growth_count);
+        if (st != cudaSuccess) return st;
+        ctx_->fg_gaussian_capacity = count;
+    }
+    gv_ = gaussian_views(ctx_->fg_gaussian.ptr, ctx_->fg_gaussian_capacity);
+    sort_need_ = std::max(sort::sort_scratch_bytes(c_.point_count),
+                          bin::scan_scratch_bytes(c_.point_count));
+    st = ensure_buffer(ctx_->fg_sort, sort_need_, &ctx_->fg_growth_count);
+    if (st != cudaSuccess) return st;
+    st = cudaMemsetAsync(gv_.total, 0, 4 * sizeof(uint32_t), stream);
     if (st != cudaSuccess) return st;
 
-    uint32_t num_rendered = 0;
-    GaussianViews gv{};
-    if (point_count > 0) {
-        if (ctx->fg_total_host == nullptr) {
-            st = cudaHostAlloc(reinterpret_cast<void**>(&ctx->fg_total_host), 4 * sizeof(uint32_t),
-                               cudaHostAllocPortable);
-            if (st != cudaSuccess) return st;
-            ++ctx->fg_growth_count;
-        }
-        st = ensure_device_error(ctx);
-        if (st != cudaSuccess) return st;
-        if (ctx->fg_count_event == nullptr) {
-            st = cudaEventCreateWithFlags(&ctx->fg_count_event, cudaEventDisableTiming);
-            if (st != cudaSuccess) return st;
-        }
-        const uint64_t count = static_cast<uint64_t>(point_count);
-        if (count > ctx->fg_gaussian_capacity || ctx->fg_gaussian.ptr == nullptr) {
-            st = ensure_buffer(ctx->fg_gaussian, gaussian_bytes(count), &ctx->fg_growth_count);
-            if (st != cudaSuccess) return st;
-            ctx->fg_gaussian_capacity = count;
-        }
-        gv = gaussian_views(ctx->fg_gaussian.ptr, ctx->fg_gaussian_capacity);
-        const uint64_t sort_need = std::max(sort::sort_scratch_bytes(point_count),
-                                            bin::scan_scratch_bytes(point_count));
-        st = ensure_buffer(ctx->fg_sort, sort_need, &ctx->fg_growth_count);
-        if (st != cudaSuccess) return st;
-        st = cudaMemsetAsync(gv.total, 0, 4 * sizeof(uint32_t), stream);
-        if (st != cudaSuccess) return st;
+    const int blocks = (c_.point_count + kPreThreads - 1) / kPreThreads;
+    preprocess_kernel<HS_FLASHGS_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
+        c_.point_count, cam_, c_.positions3, c_.shs48, c_.colors3, c_.use_sh ? 1 : 0,
+        c_.opacities1, c_.covariance6, c_.scales2, c_.scale_modifier, c_.rotations4, c_.specular1,
+        c_.roughness1, gv_.records, gv_.emit, gv_.keys, gv_.order, gv_.counts, gv_.total,
+        ctx_->device_error, static_cast<int>(c_.row_begin), static_cast<int>(c_.row_end));
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+    st = cudaMemcpyAsync(ctx_->fg_total_host, gv_.total, 4 * sizeof(uint32_t),
+                         cudaMemcpyDeviceToHost, stream);
+    if (st == cudaSuccess) st = cudaEventRecord(ctx_->fg_count_event, stream);
+    if (st != cudaSuccess) return st;
+    marks_.mark(1);
+    // The depth sort does not depend on the pair count: queue it, then wait
+    // for the count in bin() (the reference reads its counter back at this
+    // point, flashgs_backend.cu:480-488).
+    return sort::sort_pairs(gv_.keys, gv_.order, gv_.alt_keys, gv_.alt_order, c_.point_count, 0,
+                            32, ctx_->fg_sort.ptr, stream, ctx_->device_error);
+}
 
-        const int blocks = (point_count + kPreThreads - 1) / kPreThreads;
-        preprocess_kernel<HS_FLASHGS_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
-            point_count, cam, positions3, shs48, colors3, use_sh ? 1 : 0, opacities1,
-            covariance6, scales2, scale_modifier, rotations4, specular1, roughness1, gv.records,
-            gv.emit, gv.keys, gv.order, gv.counts, gv.total, ctx->device_error,
-            static_cast<int>(row_begin), static_cast<int>(row_end));
-        st = cudaGetLastError();
+cudaError_t FlashgsPass::bin() {
+    const cudaStream_t stream = c_.stream;
+    cudaError_t st = cudaSuccess;
+    if (c_.point_count > 0) {
+        st = cudaEventSynchronize(ctx_->fg_count_event);
         if (st != cudaSuccess) return st;
-        st = cudaMemcpyAsync(ctx->fg_total_host, gv.total, 4 * sizeof(uint32_t),
-                             cudaMemcpyDeviceToHost, stream);
-        if (st == cudaSuccess) st = cudaEventRecord(ctx->fg_count_event, stream);
-        if (st != cudaSuccess) return st;
-        marks.mark(1);
-        // The depth sort does not depend on the pair count: queue it, then
-        // wait for the count (the reference reads its counter back here,
-        // flashgs_backend.cu:480-488).
-        st = sort::sort_pairs(gv.keys, gv.order, gv.alt_keys, gv.alt_order, point_count, 0, 32,
-                              ctx->fg_sort.ptr, stream, ctx->device_error);
-        if (st != cudaSuccess) return st;
-        st = cudaEventSynchronize(ctx->fg_count_event);
-        if (st != cudaSuccess) return st;
-        num_rendered = ctx->fg_total_host[0];
-        if (ctx->fg_total_host[1] != 0) return cudaErrorLaunchTimeout;  // a look-back wait gave up
-        if (num_rendered > static_cast<uint32_t>(INT_MAX) || num_rendered > sort::kMaxItems) {
+        num_rendered_ = ctx_->fg_total_host[0];
+        if (ctx_->fg_total_host[1] != 0) return cudaErrorLaunchTimeout;  // a look-back wait gave up
+        if (num_rendered_ > static_cast<uint32_t>(INT_MAX) || num_rendered_ > sort::kMaxItems) {
             return cudaErrorInvalidValue;
         }
 
         // Pair capacity follows the reference's growth rule: start at the
         // caller's initial capacity and, whenever the pair count reaches it,
         // grow to max(count + 1, 1.25 x capacity) (flashgs_backend.cu:415-500).
-        if (ctx->fg_pair_capacity == 0) {
-            ctx->fg_pair_capacity = std::max<uint64_t>(initial_pair_capacity, 1);
+        if (ctx_->fg_pair_capacity == 0) {
+            ctx_->fg_pair_capacity = std::max<uint64_t>(c_.initial_pair_capacity, 1);
         }
-        if (num_rendered >= ctx->fg_pair_capacity) {
-            ctx->fg_pair_capacity = std::max<uint64_t>(
-                static_cast<uint64_t>(num_rendered) + 1,
-                ctx->fg_pair_capacity + ctx->fg_pair_capacity / 4);
-            ++ctx->fg_overflow_retry_count;
+        if (num_rendered_ >= ctx_->fg_pair_capacity) {
+            ctx_->fg_pair_capacity = std::max<uint64_t>(
+                static_cast<uint64_t>(num_rendered_) + 1,
+                ctx_->fg_pair_capacity + ctx_->fg_pair_capacity / 4);
+            ++ctx_->fg_overflow_retry_count;
         }
-        if (ctx->fg_pair_capacity > static_cast<uint64_t>(INT_MAX)) return cudaErrorInvalidValue;
-        st = ensure_buffer(ctx->fg_pairs, pair_bytes(ctx->fg_pair_capacity), &ctx->fg_growth_count);
+        if (ctx_->fg_pair_capacity > static_cast<uint64_t>(INT_MAX)) return cudaErrorInvalidValue;
+        st = ensure_buffer(ctx_->fg_pairs, pair_bytes(ctx_->fg_pair_capacity),
+                           &ctx_->fg_growth_count);
         if (st != cudaSuccess) return st;
-        if (num_rendered > 0) {
+        if (num_rendered_ > 0) {
             // sized by the pair capacity, so it grows only when the capacity does
-            st = ensure_buffer(ctx->fg_sort,
-                               std::max(sort_need, sort::sort_scratch_bytes(static_cast<uint32_t>(
-                                                       ctx->fg_pair_capacity))),
-                               &ctx->fg_growth_count);
+            st = ensure_buffer(ctx_->fg_sort,
+                               std::max(sort_need_, sort::sort_scratch_bytes(static_cast<uint32_t>(
+                                                        ctx_->fg_pair_capacity))),
+                               &ctx_->fg_growth_count);
             if (st != cudaSuccess) return st;
-            const PairViews pv = pair_views(ctx->fg_pairs.ptr, ctx->fg_pair_capacity);
-            st = cudaMemsetAsync(ctx->fg_sort.ptr, 0, bin::scan_scratch_bytes(point_count),
+            const PairViews pv = pair_views(ctx_->fg_pairs.ptr, ctx_->fg_pair_capacity);
+            st = cudaMemsetAsync(ctx_->fg_sort.ptr, 0, bin::scan_scratch_bytes(c_.point_count),
                                  stream);
             if (st != cudaSuccess) return st;
             // alt_keys is free once the depth sort has finished: it receives
             // the first pair slot of every Gaussian.
-            uint32_t* first_pair = gv.alt_keys;
-            bin::offsets_kernel<<<bin::scan_tiles(point_count), bin::kScanThreads, 0, stream>>>(
-                static_cast<uint32_t>(point_count), gv.order, gv.counts,
-                static_cast<uint32_t*>(ctx->fg_sort.ptr), ctx->device_error, first_pair);
+            uint32_t* first_pair = gv_.alt_keys;
+            bin::offsets_kernel<<<bin::scan_tiles(c_.point_count), bin::kScanThreads, 0, stream>>>(
+                static_cast<uint32_t>(c_.point_count), gv_.order, gv_.counts,
+                static_cast<uint32_t*>(ctx_->fg_sort.ptr), ctx_->device_error, first_pair);
             st = cudaGetLastError();
             if (st != cudaSuccess) return st;
-            const Emitter<HS_FLASHGS_ROUNDING> em{gv.emit, grid_x};
+            const Emitter<HS_FLASHGS_ROUNDING> em{gv_.emit, grid_x_};
             bin::emit_flat_compact_kernel<Emitter<HS_FLASHGS_ROUNDING>>
-                <<<(point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
-                   stream>>>(static_cast<uint32_t>(point_count), gv.counts, first_pair, em,
-                             pv.tiles, pv.ids);
+                <<<(c_.point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads,
+                   0, stream>>>(static_cast<uint32_t>(c_.point_count), gv_.counts, first_pair, em,
+                                pv.tiles, pv.ids);
             st = cudaGetLastError();
             if (st != cudaSuccess) return st;
-            st = sort::sort_pairs(pv.tiles, pv.ids, pv.alt_tiles, pv.alt_ids, num_rendered, 0,
-                                  sort::bits_for_tiles(static_cast<uint32_t>(tiles)),
-                                  ctx->fg_sort.ptr, stream, ctx->device_error);
+            st = sort::sort_pairs(pv.tiles, pv.ids, pv.alt_tiles, pv.alt_ids, num_rendered_, 0,
+                                  sort::bits_for_tiles(static_cast<uint32_t>(tiles_)),
+                                  ctx_->fg_sort.ptr, stream, ctx_->device_error);
             if (st != cudaSuccess) return st;
-            bin::ranges_kernel<int2><<<(num_rendered + 255) / 256, 256, 0, stream>>>(
-                num_rendered, static_cast<uint32_t>(tiles), pv.tiles, ranges);
+            bin::ranges_kernel<int2><<<(num_rendered_ + 255) / 256, 256, 0, stream>>>(
+                num_rendered_, static_cast<uint32_t>(tiles_), pv.tiles, ranges_);
             st = cudaGetLastError();
             if (st != cudaSuccess) return st;
         }
     }
+    const uint32_t strip_tiles = (c_.row_end - c_.row_begin) * static_cast<uint32_t>(grid_x_);
+    bin::tile_order_kernel<int2><<<1, bin::kOrderThreads, 0, stream>>>(
+        c_.row_begin * static_cast<uint32_t>(grid_x_), strip_tiles, ranges_, tile_order_,
+        work_counter_);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return st;
+    marks_.mark(2);
+    return cudaSuccess;
+}
 
-    Outputs out{output_color3, output_other2, output_depth1, output_alpha1,
-                output_normal3, output_median_depth1, output_distortion1};
-    const float3 bg = make_float3(background3[0], background3[1], background3[2]);
+cudaError_t FlashgsPass::render() {
+    const cudaStream_t stream = c_.stream;
+    Outputs out{c_.output_color3, c_.output_other2, c_.output_depth1, c_.output_alpha1,
+                c_.output_normal3, c_.output_median_depth1, c_.output_distortion1};
+    const float3 bg = make_float3(c_.background3[0], c_.background3[1], c_.background3[2]);
     auto encode = [](float v) {
         const float c = std::min(std::max(0.0f, v * 255.0f), 255.0f);
         return static_cast<float>(static_cast<unsigned char>(c));
     };
     const float3 bg_encoded = make_float3(encode(bg.x), encode(bg.y), encode(bg.z));
     const uint32_t* ids = nullptr;
-    if (num_rendered > 0) ids = pair_views(ctx->fg_pairs.ptr, ctx->fg_pair_capacity).ids;
-    st = cudaGetLastError();
-    if (st != cudaSuccess) return st;
-    const uint32_t strip_tiles = (row_end - row_begin) * static_cast<uint32_t>(grid_x);
-    bin::tile_order_kernel<int2><<<1, bin::kOrderThreads, 0, stream>>>(
-        row_begin * static_cast<uint32_t>(grid_x), strip_tiles, ranges, tile_order, work_counter);
-    st = cudaGetLastError();
-    if (st != cudaSuccess) return st;
-    marks.mark(2);
+    if (num_rendered_ > 0) ids = pair_views(ctx_->fg_pairs.ptr, ctx_->fg_pair_capacity).ids;
+    const uint32_t strip_tiles = (c_.row_end - c_.row_begin) * static_cast<uint32_t>(grid_x_);
     int sms = 148, per_sm = 1;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx_->device);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, render_kernel<HS_FLASHGS_ROUNDING>,
                                                   kRenderThreads, 0);
     const uint32_t render_blocks = static_cast<uint32_t>(
         std::min<uint64_t>(strip_tiles, static_cast<uint64_t>(sms) * std::max(per_sm, 1)));
     render_kernel<HS_FLASHGS_ROUNDING><<<render_blocks, kRenderThreads, 0, stream>>>(
-        ranges, tile_order, strip_tiles, work_counter, ids, gv.records, width, height, grid_x, bg,
-        bg_encoded, out);
-    st = cudaGetLastError();
+        ranges_, tile_order_, strip_tiles, work_counter_, ids, gv_.records, c_.width, c_.height,
+        grid_x_, bg, bg_encoded, out);
+    cudaError_t st = cudaGetLastError();
     if (st != cudaSuccess) return st;
-    marks.mark(3);
-    if (num_rendered > 0) {
-        st = cudaMemcpyAsync(output_num_rendered, gv.total, sizeof(int32_t),
+    marks_.mark(3);
+    if (num_rendered_ > 0) {
+        st = cudaMemcpyAsync(c_.output_num_rendered, gv_.total, sizeof(int32_t),
                              cudaMemcpyDeviceToDevice, stream);
     } else {
-        st = cudaMemsetAsync(output_num_rendered, 0, sizeof(int32_t), stream);
+        st = cudaMemsetAsync(c_.output_num_rendered, 0, sizeof(int32_t), stream);
     }
     if (st != cudaSuccess) return st;
 
-    ++ctx->fg_forward_calls;
-    ctx->fg_last_point_count = static_cast<uint64_t>(point_count);
-    ctx->fg_last_num_rendered = num_rendered;
-    ctx->fg_last_tile_count = tiles;
-    ctx->fg_last_width = width;
-    ctx->fg_last_height = height;
-    update_peak(ctx);
+    ++ctx_->fg_forward_calls;
+    ctx_->fg_last_point_count = static_cast<uint64_t>(c_.point_count);
+    ctx_->fg_last_num_rendered = num_rendered_;
+    ctx_->fg_last_tile_count = tiles_;
+    ctx_->fg_last_width = c_.width;
+    ctx_->fg_last_height = c_.height;
+    update_peak(ctx_);
     return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace fg
+
+cudaError_t flashgs_forward(HsRasterizerContext* ctx, const FlashgsCall& call) {
+    fg::FlashgsPass pass(ctx, call);
+    cudaError_t e = pass.begin();
+    if (e == cudaSuccess) e = pass.bin();
+    if (e == cudaSuccess) e = pass.render();
+    return e;
+}
+
+cudaError_t flashgs_forward_many(HsRasterizerContext* const* contexts, const FlashgsCall* calls,
+                                 uint32_t count, cudaStream_t stream) {
+    return run_many<fg::FlashgsPass>(contexts, calls, count, stream);
 }
 
 cudaError_t flashgs_debug_copy(HsRasterizerContext* ctx, uint64_t point_capacity,

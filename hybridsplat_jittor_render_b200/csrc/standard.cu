@@ -25,6 +25,7 @@
 #include <algorithm>
 #include <climits>
 
+#include "concurrent.h"
 #include "context.h"
 
 // Rounding policy of the kernels: the pinned forms that reproduce the
@@ -106,160 +107,187 @@ cudaError_t standard_release(HsRasterizerContext* ctx) {
     return first;
 }
 
-cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
-                             const float* background5, int32_t width, int32_t height,
-                             const float* means3d, const float* colors5, const float* opacities,
-                             const float* scales2, float scale_modifier, const float* rotations4,
-                             const float* viewmatrix4x4, const float* projmatrix4x4,
-                             const float* camera_position3, float tan_fovx, float tan_fovy,
-                             bool prefiltered, float* output_color5, float* output_aux7,
-                             float* output_weight, int32_t* output_radii,
-                             int32_t* output_rendered, cudaStream_t stream, uint32_t row_begin,
-                             uint32_t row_end) {
-    using namespace st;
+namespace st {
+namespace {
+
+// One standard raster call in the three phases of run_many (concurrent.h).
+class StandardPass {
+public:
+    StandardPass(HsRasterizerContext* ctx, const StandardCall& call) : ctx_(ctx), c_(call) {}
+    cudaError_t begin();
+    cudaError_t bin();
+    cudaError_t render();
+
+private:
+    HsRasterizerContext* ctx_;
+    StandardCall c_;
+    StageMarks marks_;
+    bool done_ = false;  // empty input: begin() wrote the outputs
+    uint32_t grid_x_ = 0, grid_y_ = 0;
+    uint64_t tiles_ = 0, count_ = 0;
+    GeometryViews gv_{};
+    void* geometry_scratch_ = nullptr;
+    uint2* ranges_ = nullptr;
+    uint32_t* tile_order_ = nullptr;
+    uint32_t* work_counter_ = nullptr;
+    uint32_t* values_ = nullptr;
+    bool masked_ = false;
+};
+
+cudaError_t StandardPass::begin() {
     // Only the matrices drive the 2DGS projection; the camera position and
     // field of view are accepted for ABI compatibility (the reference passes
     // them through without using them when colours are precomputed).
-    (void)camera_position3;
-    (void)tan_fovx;
-    (void)tan_fovy;
-    const uint64_t pixels = static_cast<uint64_t>(width) * static_cast<uint64_t>(height);
-    const uint32_t grid_x = static_cast<uint32_t>((width + 15) / 16);
-    const uint32_t grid_y = static_cast<uint32_t>((height + 15) / 16);
-    row_end = std::min(row_end, grid_y);
-    if (row_begin >= row_end) return cudaErrorInvalidValue;
-    const bool full_frame = row_begin == 0 && row_end == grid_y;
-    if (point_count == 0) {
+    const cudaStream_t stream = c_.stream;
+    const uint64_t pixels = static_cast<uint64_t>(c_.width) * static_cast<uint64_t>(c_.height);
+    grid_x_ = static_cast<uint32_t>((c_.width + 15) / 16);
+    grid_y_ = static_cast<uint32_t>((c_.height + 15) / 16);
+    c_.row_end = std::min(c_.row_end, grid_y_);
+    if (c_.row_begin >= c_.row_end) return cudaErrorInvalidValue;
+    const bool full_frame = c_.row_begin == 0 && c_.row_end == grid_y_;
+    if (c_.point_count == 0) {
         // zero_outputs (full_rasterizer.cu:178-199) and nothing else.
-        cudaError_t st = cudaMemsetAsync(output_rendered, 0, sizeof(int32_t), stream);
+        done_ = true;
+        cudaError_t st = cudaMemsetAsync(c_.output_rendered, 0, sizeof(int32_t), stream);
         if (full_frame) {
-            if (st == cudaSuccess) st = cudaMemsetAsync(output_color5, 0, 5 * pixels * sizeof(float), stream);
-            if (st == cudaSuccess) st = cudaMemsetAsync(output_aux7, 0, 7 * pixels * sizeof(float), stream);
+            if (st == cudaSuccess)
+                st = cudaMemsetAsync(c_.output_color5, 0, 5 * pixels * sizeof(float), stream);
+            if (st == cudaSuccess)
+                st = cudaMemsetAsync(c_.output_aux7, 0, 7 * pixels * sizeof(float), stream);
             return st;
         }
-        const uint64_t y0 = uint64_t(row_begin) * 16, y1 = std::min<uint64_t>(uint64_t(row_end) * 16, height);
+        const uint64_t y0 = uint64_t(c_.row_begin) * 16;
+        const uint64_t y1 = std::min<uint64_t>(uint64_t(c_.row_end) * 16, c_.height);
         for (int c = 0; c < 12 && st == cudaSuccess; ++c) {
-            float* plane = c < 5 ? output_color5 + c * pixels : output_aux7 + (c - 5) * pixels;
-            st = cudaMemsetAsync(plane + y0 * width, 0, (y1 - y0) * width * sizeof(float), stream);
+            float* plane = c < 5 ? c_.output_color5 + c * pixels : c_.output_aux7 + (c - 5) * pixels;
+            st = cudaMemsetAsync(plane + y0 * c_.width, 0, (y1 - y0) * c_.width * sizeof(float), stream);
         }
         return st;
     }
-    const uint64_t tiles = static_cast<uint64_t>(grid_x) * grid_y;
-    const uint64_t count = static_cast<uint64_t>(point_count);
-    StageMarks marks(ctx->timer, stream);
+    tiles_ = static_cast<uint64_t>(grid_x_) * grid_y_;
+    count_ = static_cast<uint64_t>(c_.point_count);
+    marks_.start(ctx_->timer, stream);
 
     // Geometry: per-Gaussian views followed by the depth-sort / scan scratch.
-    const uint64_t geometry_used = geometry_bytes(count);
+    const uint64_t geometry_used = geometry_bytes(count_);
     const uint64_t geometry_scratch_bytes =
-        std::max(sort::sort_scratch_bytes(point_count), bin::scan_scratch_bytes(point_count));
-    cudaError_t st = ensure_buffer(ctx->std_geometry, geometry_used + geometry_scratch_bytes,
-                                   &ctx->std_growth_count, true);
+        std::max(sort::sort_scratch_bytes(c_.point_count), bin::scan_scratch_bytes(c_.point_count));
+    cudaError_t st = ensure_buffer(ctx_->std_geometry, geometry_used + geometry_scratch_bytes,
+                                   &ctx_->std_growth_count, true);
     if (st != cudaSuccess) return st;
     // image buffer: ranges, rasterisation order of the tiles, work counter
-    st = ensure_buffer(ctx->std_image, tiles * (sizeof(uint2) + sizeof(uint32_t)) + 256,
-                       &ctx->std_growth_count, true);
+    st = ensure_buffer(ctx_->std_image, tiles_ * (sizeof(uint2) + sizeof(uint32_t)) + 256,
+                       &ctx_->std_growth_count, true);
     if (st != cudaSuccess) return st;
-    if (ctx->std_total_host == nullptr) {
-        st = cudaHostAlloc(reinterpret_cast<void**>(&ctx->std_total_host), 4 * sizeof(uint32_t),
+    if (ctx_->std_total_host == nullptr) {
+        st = cudaHostAlloc(reinterpret_cast<void**>(&ctx_->std_total_host), 4 * sizeof(uint32_t),
                            cudaHostAllocPortable);
         if (st != cudaSuccess) return st;
     }
-    st = ensure_device_error(ctx);
+    st = ensure_device_error(ctx_);
     if (st != cudaSuccess) return st;
-    if (ctx->std_count_event == nullptr) {
-        st = cudaEventCreateWithFlags(&ctx->std_count_event, cudaEventDisableTiming);
+    if (ctx_->std_count_event == nullptr) {
+        st = cudaEventCreateWithFlags(&ctx_->std_count_event, cudaEventDisableTiming);
         if (st != cudaSuccess) return st;
     }
-    ctx->std_peak_bytes = std::max(ctx->std_peak_bytes, standard_current_bytes(ctx));
-    const GeometryViews gv = geometry_views(ctx->std_geometry.ptr, count);
-    void* geometry_scratch = static_cast<unsigned char*>(ctx->std_geometry.ptr) + geometry_used;
-    uint2* ranges = static_cast<uint2*>(ctx->std_image.ptr);
-    uint32_t* tile_order = reinterpret_cast<uint32_t*>(ranges + tiles);
-    uint32_t* work_counter = tile_order + tiles;
+    ctx_->std_peak_bytes = std::max(ctx_->std_peak_bytes, standard_current_bytes(ctx_));
+    gv_ = geometry_views(ctx_->std_geometry.ptr, count_);
+    geometry_scratch_ = static_cast<unsigned char*>(ctx_->std_geometry.ptr) + geometry_used;
+    ranges_ = static_cast<uint2*>(ctx_->std_image.ptr);
+    tile_order_ = reinterpret_cast<uint32_t*>(ranges_ + tiles_);
+    work_counter_ = tile_order_ + tiles_;
 
-    st = cudaMemsetAsync(output_weight, 0, count * sizeof(float), stream);
-    if (st == cudaSuccess) st = cudaMemsetAsync(gv.totals, 0, 4 * sizeof(uint32_t), stream);
-    if (st == cudaSuccess) st = cudaMemsetAsync(ranges, 0, tiles * sizeof(uint2), stream);
+    st = cudaMemsetAsync(c_.output_weight, 0, count_ * sizeof(float), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(gv_.totals, 0, 4 * sizeof(uint32_t), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(ranges_, 0, tiles_ * sizeof(uint2), stream);
     if (st != cudaSuccess) return st;
-    const int blocks = (point_count + kPreThreads - 1) / kPreThreads;
-    PreprocessOut po{gv.records, gv.cull, gv.keys, gv.order, gv.counts, output_radii, gv.totals,
-                     ctx->device_error};
+    const int blocks = (c_.point_count + kPreThreads - 1) / kPreThreads;
+    PreprocessOut po{gv_.records, gv_.cull, gv_.keys, gv_.order, gv_.counts, c_.output_radii,
+                     gv_.totals, ctx_->device_error};
     preprocess_kernel<HS_STANDARD_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
-        point_count, viewmatrix4x4, projmatrix4x4, width, height, grid_x, grid_y, means3d,
-        colors5, opacities, scales2, scale_modifier, rotations4, prefiltered ? 1 : 0, row_begin,
-        row_end, po);
+        c_.point_count, c_.viewmatrix4x4, c_.projmatrix4x4, c_.width, c_.height, grid_x_, grid_y_,
+        c_.means3d, c_.colors5, c_.opacities, c_.scales2, c_.scale_modifier, c_.rotations4,
+        c_.prefiltered ? 1 : 0, c_.row_begin, c_.row_end, po);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
-    st = cudaMemcpyAsync(ctx->std_total_host, gv.totals, 4 * sizeof(uint32_t),
+    st = cudaMemcpyAsync(ctx_->std_total_host, gv_.totals, 4 * sizeof(uint32_t),
                          cudaMemcpyDeviceToHost, stream);
-    if (st == cudaSuccess) st = cudaEventRecord(ctx->std_count_event, stream);
+    if (st == cudaSuccess) st = cudaEventRecord(ctx_->std_count_event, stream);
     if (st != cudaSuccess) return st;
-    marks.mark(1);
+    marks_.mark(1);
     // The depth sort does not depend on the totals: queue it before waiting.
-    st = sort::sort_pairs(gv.keys, gv.order, gv.alt_keys, gv.alt_order, point_count, 0, 32,
-                          geometry_scratch, stream, ctx->device_error);
+    return sort::sort_pairs(gv_.keys, gv_.order, gv_.alt_keys, gv_.alt_order, c_.point_count, 0, 32,
+                            geometry_scratch_, stream, ctx_->device_error);
+}
+
+cudaError_t StandardPass::bin() {
+    if (done_) return cudaSuccess;
+    const cudaStream_t stream = c_.stream;
+    cudaError_t st = cudaEventSynchronize(ctx_->std_count_event);
     if (st != cudaSuccess) return st;
-    st = cudaEventSynchronize(ctx->std_count_event);
-    if (st != cudaSuccess) return st;
-    const uint32_t rendered = ctx->std_total_host[0];
-    const uint32_t emitted = ctx->std_total_host[2];
-    if (ctx->std_total_host[3] != 0) return cudaErrorLaunchTimeout;  // a look-back wait gave up
-    if (ctx->std_total_host[1] != 0) return kPrefilteredViolation;
+    const uint32_t rendered = ctx_->std_total_host[0];
+    const uint32_t emitted = ctx_->std_total_host[2];
+    if (ctx_->std_total_host[3] != 0) return cudaErrorLaunchTimeout;  // a look-back wait gave up
+    if (ctx_->std_total_host[1] != 0) return kPrefilteredViolation;
     if (rendered > static_cast<uint32_t>(INT_MAX) || emitted > sort::kMaxItems) {
         return cudaErrorInvalidValue;
     }
-    st = cudaMemcpyAsync(output_rendered, gv.totals, sizeof(int32_t), cudaMemcpyDeviceToDevice,
+    st = cudaMemcpyAsync(c_.output_rendered, gv_.totals, sizeof(int32_t), cudaMemcpyDeviceToDevice,
                          stream);
     if (st != cudaSuccess) return st;
 
-    const bool masked = count <= static_cast<uint64_t>(kIndexMask) + 1u;
-    uint32_t* values = nullptr;
+    masked_ = count_ <= static_cast<uint64_t>(kIndexMask) + 1u;
     if (emitted > 0) {
-        st = ensure_buffer(ctx->std_binning, binning_bytes(emitted), &ctx->std_growth_count, true);
+        st = ensure_buffer(ctx_->std_binning, binning_bytes(emitted), &ctx_->std_growth_count, true);
         if (st != cudaSuccess) return st;
-        ctx->std_peak_bytes = std::max(ctx->std_peak_bytes, standard_current_bytes(ctx));
-        Carver c(ctx->std_binning.ptr);
+        ctx_->std_peak_bytes = std::max(ctx_->std_peak_bytes, standard_current_bytes(ctx_));
+        Carver c(ctx_->std_binning.ptr);
         uint32_t* tile_ids = c.take<uint32_t>(emitted);
-        values = c.take<uint32_t>(emitted);
+        values_ = c.take<uint32_t>(emitted);
         uint32_t* alt_tiles = c.take<uint32_t>(emitted);
         uint32_t* alt_values = c.take<uint32_t>(emitted);
         void* scratch = c.take<unsigned char>(sort::sort_scratch_bytes(emitted));
-        st = cudaMemsetAsync(geometry_scratch, 0, bin::scan_scratch_bytes(point_count), stream);
+        st = cudaMemsetAsync(geometry_scratch_, 0, bin::scan_scratch_bytes(c_.point_count), stream);
         if (st != cudaSuccess) return st;
         // alt_keys is free once the depth sort has finished: it receives the
         // first pair slot of every Gaussian.
-        uint32_t* first_pair = gv.alt_keys;
-        bin::offsets_kernel<<<bin::scan_tiles(point_count), bin::kScanThreads, 0, stream>>>(
-            static_cast<uint32_t>(point_count), gv.order, gv.counts,
-            static_cast<uint32_t*>(geometry_scratch), ctx->device_error, first_pair);
+        uint32_t* first_pair = gv_.alt_keys;
+        bin::offsets_kernel<<<bin::scan_tiles(c_.point_count), bin::kScanThreads, 0, stream>>>(
+            static_cast<uint32_t>(c_.point_count), gv_.order, gv_.counts,
+            static_cast<uint32_t*>(geometry_scratch_), ctx_->device_error, first_pair);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
-        const Emitter em{gv.cull, grid_x, masked};
+        const Emitter em{gv_.cull, grid_x_, masked_};
         bin::emit_flat_kernel<Emitter>
-            <<<(point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
-               stream>>>(static_cast<uint32_t>(point_count), gv.counts, first_pair, em, tile_ids,
-                         values);
+            <<<(c_.point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
+               stream>>>(static_cast<uint32_t>(c_.point_count), gv_.counts, first_pair, em,
+                         tile_ids, values_);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
-        st = sort::sort_pairs(tile_ids, values, alt_tiles, alt_values, emitted, 0,
-                              sort::bits_for_tiles(static_cast<uint32_t>(tiles)), scratch, stream,
-                              ctx->device_error);
+        st = sort::sort_pairs(tile_ids, values_, alt_tiles, alt_values, emitted, 0,
+                              sort::bits_for_tiles(static_cast<uint32_t>(tiles_)), scratch, stream,
+                              ctx_->device_error);
         if (st != cudaSuccess) return st;
         bin::ranges_kernel<uint2><<<(emitted + 255) / 256, 256, 0, stream>>>(
-            emitted, static_cast<uint32_t>(tiles), tile_ids, ranges);
+            emitted, static_cast<uint32_t>(tiles_), tile_ids, ranges_);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
     }
-    const uint32_t strip_tiles = (row_end - row_begin) * grid_x;
+    const uint32_t strip_tiles = (c_.row_end - c_.row_begin) * grid_x_;
     bin::tile_order_kernel<uint2><<<1, bin::kOrderThreads, 0, stream>>>(
-        row_begin * grid_x, strip_tiles, ranges, tile_order, work_counter);
+        c_.row_begin * grid_x_, strip_tiles, ranges_, tile_order_, work_counter_);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
-    marks.mark(2);
-    const uint32_t items = strip_tiles * 4u;
+    marks_.mark(2);
+    return cudaSuccess;
+}
+
+cudaError_t StandardPass::render() {
+    if (done_) return cudaSuccess;
+    const uint32_t items = (c_.row_end - c_.row_begin) * grid_x_ * 4u;
     int sms = 148, per_sm = 1;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
-    if (masked) {
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx_->device);
+    if (masked_) {
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(
             &per_sm, render_kernel<HS_STANDARD_ROUNDING, true>, kRenderThreads, 0);
     } else {
@@ -269,16 +297,34 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, int32_t point_count,
     const uint32_t wanted = (items + kRenderThreads / 32 - 1) / (kRenderThreads / 32);
     const uint32_t render_blocks =
         std::min<uint32_t>(wanted, static_cast<uint32_t>(sms * std::max(per_sm, 1)));
-    if (masked) {
-        render_kernel<HS_STANDARD_ROUNDING, true><<<render_blocks, kRenderThreads, 0, stream>>>(
-            ranges, tile_order, items, work_counter, values, gv.records, width, height, grid_x,
-            background5, output_color5, output_aux7, output_weight);
+    if (masked_) {
+        render_kernel<HS_STANDARD_ROUNDING, true><<<render_blocks, kRenderThreads, 0, c_.stream>>>(
+            ranges_, tile_order_, items, work_counter_, values_, gv_.records, c_.width, c_.height,
+            grid_x_, c_.background5, c_.output_color5, c_.output_aux7, c_.output_weight);
     } else {
-        render_kernel<HS_STANDARD_ROUNDING, false><<<render_blocks, kRenderThreads, 0, stream>>>(
-            ranges, tile_order, items, work_counter, values, gv.records, width, height, grid_x,
-            background5, output_color5, output_aux7, output_weight);
+        render_kernel<HS_STANDARD_ROUNDING, false><<<render_blocks, kRenderThreads, 0, c_.stream>>>(
+            ranges_, tile_order_, items, work_counter_, values_, gv_.records, c_.width, c_.height,
+            grid_x_, c_.background5, c_.output_color5, c_.output_aux7, c_.output_weight);
     }
-    return cudaGetLastError();
+    const cudaError_t st = cudaGetLastError();
+    marks_.mark(3);
+    return st;
+}
+
+}  // namespace
+}  // namespace st
+
+cudaError_t standard_forward(HsRasterizerContext* ctx, const StandardCall& call) {
+    st::StandardPass pass(ctx, call);
+    cudaError_t e = pass.begin();
+    if (e == cudaSuccess) e = pass.bin();
+    if (e == cudaSuccess) e = pass.render();
+    return e;
+}
+
+cudaError_t standard_forward_many(HsRasterizerContext* const* contexts, const StandardCall* calls,
+                                  uint32_t count, cudaStream_t stream) {
+    return run_many<st::StandardPass>(contexts, calls, count, stream);
 }
 
 }  // namespace hs

@@ -110,6 +110,26 @@ cudaError_t ensure_device_error(HsRasterizerContext* context) {
     return cudaSuccess;
 }
 
+cudaError_t ensure_side_stream(HsRasterizerContext* context) {
+    cudaError_t st = cudaSuccess;
+    if (context->side_stream == nullptr)
+        st = cudaStreamCreateWithFlags(&context->side_stream, cudaStreamNonBlocking);
+    if (st == cudaSuccess && context->side_event == nullptr)
+        st = cudaEventCreateWithFlags(&context->side_event, cudaEventDisableTiming);
+    if (st == cudaSuccess && context->fork_event == nullptr)
+        st = cudaEventCreateWithFlags(&context->fork_event, cudaEventDisableTiming);
+    return st;
+}
+
+void destroy_side_stream(HsRasterizerContext* context) {
+    if (context->side_stream != nullptr) cudaStreamDestroy(context->side_stream);
+    if (context->side_event != nullptr) cudaEventDestroy(context->side_event);
+    if (context->fork_event != nullptr) cudaEventDestroy(context->fork_event);
+    context->side_stream = nullptr;
+    context->side_event = nullptr;
+    context->fork_event = nullptr;
+}
+
 void stage_timing_destroy(StageTimer& timer) {
     for (auto& set : timer.pool)
         for (auto& e : set) cudaEventDestroy(e);

@@ -175,7 +175,43 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
 
 # Extensions of this library (include/hybridsplat_b200_ext.h); the reference
 # library does not export them, so they are bound only where present.
+class FlashgsCallV2(ctypes.Structure):
+    """HsB200FlashgsCallV2 (include/hybridsplat_b200_ext.h)."""
+    _fields_ = [
+        ("handle", ctypes.c_void_p), ("point_count", ctypes.c_uint64), ("width", ctypes.c_int32),
+        ("height", ctypes.c_int32), ("positions3", ctypes.c_void_p), ("shs48", ctypes.c_void_p),
+        ("colors3", ctypes.c_void_p), ("use_sh", ctypes.c_int32), ("scale_modifier", ctypes.c_float),
+        ("opacities1", ctypes.c_void_p), ("covariance6", ctypes.c_void_p), ("scales2", ctypes.c_void_p),
+        ("rotations4", ctypes.c_void_p), ("specular1", ctypes.c_void_p), ("roughness1", ctypes.c_void_p),
+        ("camera_position3", ctypes.c_void_p), ("camera_rotation9", ctypes.c_void_p),
+        ("focal_x", ctypes.c_float), ("focal_y", ctypes.c_float), ("z_far", ctypes.c_float),
+        ("z_near", ctypes.c_float), ("background3", ctypes.c_void_p), ("initial_pair_capacity", ctypes.c_uint64),
+        ("output_color3", ctypes.c_void_p), ("output_other2", ctypes.c_void_p), ("output_depth1", ctypes.c_void_p),
+        ("output_alpha1", ctypes.c_void_p), ("output_normal3", ctypes.c_void_p),
+        ("output_median_depth1", ctypes.c_void_p), ("output_distortion1", ctypes.c_void_p),
+        ("output_num_rendered", ctypes.c_void_p), ("tile_row_begin", ctypes.c_uint32),
+        ("tile_row_end", ctypes.c_uint32),
+    ]
+
+
+class RasterizerCallV2(ctypes.Structure):
+    """HsB200RasterizerCallV2 (include/hybridsplat_b200_ext.h)."""
+    _fields_ = [
+        ("handle", ctypes.c_void_p), ("point_count", ctypes.c_uint64), ("background5", ctypes.c_void_p),
+        ("width", ctypes.c_int32), ("height", ctypes.c_int32), ("means3d", ctypes.c_void_p),
+        ("colors5", ctypes.c_void_p), ("opacities", ctypes.c_void_p), ("scales2", ctypes.c_void_p),
+        ("scale_modifier", ctypes.c_float), ("prefiltered", ctypes.c_int32), ("rotations4", ctypes.c_void_p),
+        ("viewmatrix4x4", ctypes.c_void_p), ("projmatrix4x4", ctypes.c_void_p),
+        ("camera_position3", ctypes.c_void_p), ("tan_fovx", ctypes.c_float), ("tan_fovy", ctypes.c_float),
+        ("output_color5", ctypes.c_void_p), ("output_aux7", ctypes.c_void_p), ("output_weight", ctypes.c_void_p),
+        ("output_radii", ctypes.c_void_p), ("output_rendered", ctypes.c_void_p),
+        ("tile_row_begin", ctypes.c_uint32), ("tile_row_end", ctypes.c_uint32),
+    ]
+
+
 EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
+    "hs_b200_flashgs_forward_many_v2": (_I32, [ctypes.POINTER(FlashgsCallV2), _U32, _V, *_ERR]),
+    "hs_b200_rasterizer_forward_many_v2": (_I32, [ctypes.POINTER(RasterizerCallV2), _U32, _V, *_ERR]),
     "hs_b200_stage_timing_enable_v1": (_I32, [_V, _I32, *_ERR]),
     "hs_b200_stage_timing_read_v1": (_I32, [_V, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_U64), *_ERR]),
     "hs_b200_flashgs_forward_rows_f32_v1": (

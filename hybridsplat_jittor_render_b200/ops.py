@@ -18,6 +18,7 @@ from typing import Any, NamedTuple
 
 import torch
 
+from . import native_runtime
 from .native_runtime import (
     NativeRendererContext,
     check_status,
@@ -83,7 +84,25 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-def flashgs_forward(
+# Argument names of hs_flashgs_forward_f32_v1 after the handle, in ABI order
+# (also the field names of HsB200FlashgsCallV2).
+_FLASHGS_ORDER = (
+    "point_count", "width", "height", "positions3", "shs48", "colors3", "use_sh", "opacities1",
+    "covariance6", "scales2", "scale_modifier", "rotations4", "specular1", "roughness1",
+    "camera_position3", "camera_rotation9", "focal_x", "focal_y", "z_far", "z_near", "background3",
+    "initial_pair_capacity", "output_color3", "output_other2", "output_depth1", "output_alpha1",
+    "output_normal3", "output_median_depth1", "output_distortion1", "output_num_rendered",
+)
+# The same for hs_rasterizer_forward_f32_v1 (fields of HsB200RasterizerCallV2).
+_RASTERIZER_ORDER = (
+    "point_count", "background5", "width", "height", "means3d", "colors5", "opacities", "scales2",
+    "scale_modifier", "rotations4", "viewmatrix4x4", "projmatrix4x4", "camera_position3", "tan_fovx",
+    "tan_fovy", "prefiltered", "output_color5", "output_aux7", "output_weight", "output_radii",
+    "output_rendered",
+)
+
+
+def _flashgs_arguments(
     positions: torch.Tensor,
     shs: torch.Tensor,
     colors: torch.Tensor,
@@ -106,16 +125,10 @@ def flashgs_forward(
     background: Sequence[float] = (0.0, 0.0, 0.0),
     scale_modifier: float = 1.0,
     initial_pair_capacity: int = 1 << 20,
-    context: NativeRendererContext,
     out: FlashgsOutputs | None = None,
-    tile_rows: tuple[int, int] | None = None,
-) -> FlashgsOutputs:
-    """Deterministic FlashGS 16x16 forward; outputs are channel-first maps.
-
-    tile_rows=(begin, end) renders only 16x16 tile rows [begin, end) (library
-    extension for sharding one frame by strips): those rows are identical to a
-    full-frame call, the other output rows are left untouched.
-    """
+) -> tuple[dict[str, Any], FlashgsOutputs, list[Any]]:
+    """Checks one FlashGS call; returns its named ABI arguments, the outputs
+    and the host arrays that must outlive the call."""
     if isinstance(width, bool) or not isinstance(width, int) or width <= 0:
         raise ValueError("width must be a positive CPU integer")
     if isinstance(height, bool) or not isinstance(height, int) or height <= 0:
@@ -163,6 +176,51 @@ def flashgs_forward(
     position_host = (ctypes.c_float * 3)(*position)
     rotation_host = (ctypes.c_float * 9)(*rotation)
     bg_host = (ctypes.c_float * 3)(*bg)
+    values = [count, width, height, _ptr(positions), _ptr(shs), _ptr(colors), int(use_sh), _ptr(opacities),
+              _ptr(covariance), _ptr(scales), scale, _ptr(rotations), _ptr(specular), _ptr(roughness),
+              ctypes.addressof(position_host), ctypes.addressof(rotation_host), fx, fy, far, near,
+              ctypes.addressof(bg_host), initial_pair_capacity, *[t.data_ptr() for t in out]]
+    return dict(zip(_FLASHGS_ORDER, values)), out, [position_host, rotation_host, bg_host]
+
+
+def flashgs_forward(
+    positions: torch.Tensor,
+    shs: torch.Tensor,
+    colors: torch.Tensor,
+    opacities: torch.Tensor,
+    covariance: torch.Tensor,
+    scales: torch.Tensor,
+    rotations: torch.Tensor,
+    specular: torch.Tensor,
+    roughness: torch.Tensor,
+    *,
+    width: int,
+    height: int,
+    use_sh: bool,
+    camera_position: Sequence[float],
+    camera_rotation: Sequence[float],
+    focal_x: float,
+    focal_y: float,
+    z_far: float = 100.0,
+    z_near: float = 0.01,
+    background: Sequence[float] = (0.0, 0.0, 0.0),
+    scale_modifier: float = 1.0,
+    initial_pair_capacity: int = 1 << 20,
+    context: NativeRendererContext,
+    out: FlashgsOutputs | None = None,
+    tile_rows: tuple[int, int] | None = None,
+) -> FlashgsOutputs:
+    """Deterministic FlashGS 16x16 forward; outputs are channel-first maps.
+
+    tile_rows=(begin, end) renders only 16x16 tile rows [begin, end) (library
+    extension for sharding one frame by strips): those rows are identical to a
+    full-frame call, the other output rows are left untouched.
+    """
+    named, out, keep = _flashgs_arguments(
+        positions, shs, colors, opacities, covariance, scales, rotations, specular, roughness, width=width,
+        height=height, use_sh=use_sh, camera_position=camera_position, camera_rotation=camera_rotation,
+        focal_x=focal_x, focal_y=focal_y, z_far=z_far, z_near=z_near, background=background,
+        scale_modifier=scale_modifier, initial_pair_capacity=initial_pair_capacity, out=out)
     error = error_buffer()
     if tile_rows is not None:
         call = context.library.hs_b200_flashgs_forward_rows_f32_v1
@@ -170,20 +228,53 @@ def flashgs_forward(
     else:
         call = context.library.hs_flashgs_forward_f32_v1
         prefix = (context.handle,)
-    status = call(
-        *prefix, count, width, height,
-        _ptr(positions), _ptr(shs), _ptr(colors), int(use_sh), _ptr(opacities), _ptr(covariance),
-        _ptr(scales), scale, _ptr(rotations), _ptr(specular), _ptr(roughness),
-        ctypes.addressof(position_host), ctypes.addressof(rotation_host), fx, fy, far, near,
-        ctypes.addressof(bg_host), initial_pair_capacity,
-        *[t.data_ptr() for t in out], error, len(error),
-    )
+    status = call(*prefix, *[named[k] for k in _FLASHGS_ORDER], error, len(error))
+    del keep
     check_status(status, "hs_b200_flashgs_forward_rows_f32_v1" if tile_rows is not None else
                  "hs_flashgs_forward_f32_v1", error)
     return out
 
 
-def rasterize_forward(
+def flashgs_forward_many(calls: Sequence[dict[str, Any]], *, stream: int | None = None) -> list[FlashgsOutputs]:
+    """Independent FlashGS calls run concurrently (hs_b200_flashgs_forward_many_v2).
+
+    Each item holds the arguments of one flashgs_forward call by name (the
+    nine input tensors as ``positions`` ... ``roughness``, the keywords, and
+    ``context``, distinct per item; ``tile_rows`` optional). ``stream`` is a
+    raw cudaStream_t (default: the legacy default stream, like the v1 calls).
+    Outputs are identical to calling flashgs_forward item by item.
+    """
+    structs, outs, keep = [], [], []
+    library = None
+    for item in calls:
+        item = dict(item)
+        context = item.pop("context")
+        rows = item.pop("tile_rows", None)
+        named, out, hold = _flashgs_arguments(**item)
+        keep.append(hold)
+        library = context.library
+        structs.append(native_runtime.FlashgsCallV2(handle=context.handle, **named,
+                                                    **_rows_fields(rows)))
+        outs.append(out)
+    if not structs:
+        return []
+    array = (native_runtime.FlashgsCallV2 * len(structs))(*structs)
+    error = error_buffer()
+    status = library.hs_b200_flashgs_forward_many_v2(array, len(structs), stream, error, len(error))
+    del keep
+    check_status(status, "hs_b200_flashgs_forward_many_v2", error)
+    return outs
+
+
+def _rows_fields(rows: tuple[int, int] | None) -> dict[str, int]:
+    if rows is None:
+        return {"tile_row_begin": 0, "tile_row_end": 0xFFFFFFFF}
+    begin, end = int(rows[0]), int(rows[1])
+    # an explicit strip end of UINT32_MAX is out of range, as in the rows entries
+    return {"tile_row_begin": begin, "tile_row_end": 0xFFFFFFFE if end == 0xFFFFFFFF else end}
+
+
+def _rasterizer_arguments(
     background: torch.Tensor,
     means3d: torch.Tensor,
     colors: torch.Tensor,
@@ -200,15 +291,9 @@ def rasterize_forward(
     tan_fovx: float,
     tan_fovy: float,
     prefiltered: bool = False,
-    context: NativeRendererContext,
     out: RasterizerOutputs | None = None,
-    tile_rows: tuple[int, int] | None = None,
-) -> RasterizerOutputs:
-    """Standard five-channel 2DGS forward (color[5,H,W], aux[7,H,W], ...).
-
-    tile_rows=(begin, end): render only those 16x16 tile rows, as in
-    flashgs_forward (library extension).
-    """
+) -> tuple[dict[str, Any], RasterizerOutputs]:
+    """Checks one standard call; returns its named ABI arguments and outputs."""
     if isinstance(width, bool) or not isinstance(width, int) or width <= 0:
         raise ValueError("width must be a positive CPU integer")
     if isinstance(height, bool) or not isinstance(height, int) or height <= 0:
@@ -241,6 +326,42 @@ def rasterize_forward(
             torch.empty((count,), dtype=torch.int32, device=device),
             torch.empty((1,), dtype=torch.int32, device=device),
         )
+    values = [count, _ptr(background), width, height, _ptr(means3d), _ptr(colors), _ptr(opacities),
+              _ptr(scales), scale, _ptr(rotations), _ptr(viewmatrix), _ptr(projmatrix), _ptr(camera_position),
+              fovx, fovy, int(prefiltered), *[t.data_ptr() for t in out]]
+    return dict(zip(_RASTERIZER_ORDER, values)), out
+
+
+def rasterize_forward(
+    background: torch.Tensor,
+    means3d: torch.Tensor,
+    colors: torch.Tensor,
+    opacities: torch.Tensor,
+    scales: torch.Tensor,
+    rotations: torch.Tensor,
+    viewmatrix: torch.Tensor,
+    projmatrix: torch.Tensor,
+    camera_position: torch.Tensor,
+    *,
+    width: int,
+    height: int,
+    scale_modifier: float,
+    tan_fovx: float,
+    tan_fovy: float,
+    prefiltered: bool = False,
+    context: NativeRendererContext,
+    out: RasterizerOutputs | None = None,
+    tile_rows: tuple[int, int] | None = None,
+) -> RasterizerOutputs:
+    """Standard five-channel 2DGS forward (color[5,H,W], aux[7,H,W], ...).
+
+    tile_rows=(begin, end): render only those 16x16 tile rows, as in
+    flashgs_forward (library extension).
+    """
+    named, out = _rasterizer_arguments(
+        background, means3d, colors, opacities, scales, rotations, viewmatrix, projmatrix, camera_position,
+        width=width, height=height, scale_modifier=scale_modifier, tan_fovx=tan_fovx, tan_fovy=tan_fovy,
+        prefiltered=prefiltered, out=out)
     error = error_buffer()
     if tile_rows is not None:
         call = context.library.hs_b200_rasterizer_forward_rows_f32_v1
@@ -248,15 +369,39 @@ def rasterize_forward(
     else:
         call = context.library.hs_rasterizer_forward_f32_v1
         prefix = (context.handle,)
-    status = call(
-        *prefix, count, _ptr(background), width, height, _ptr(means3d), _ptr(colors),
-        _ptr(opacities), _ptr(scales), scale, _ptr(rotations), _ptr(viewmatrix), _ptr(projmatrix),
-        _ptr(camera_position), fovx, fovy, int(prefiltered),
-        *[t.data_ptr() for t in out], error, len(error),
-    )
+    status = call(*prefix, *[named[k] for k in _RASTERIZER_ORDER], error, len(error))
     check_status(status, "hs_b200_rasterizer_forward_rows_f32_v1" if tile_rows is not None else
                  "hs_rasterizer_forward_f32_v1", error)
     return out
+
+
+def rasterize_forward_many(calls: Sequence[dict[str, Any]], *,
+                           stream: int | None = None) -> list[RasterizerOutputs]:
+    """Independent standard calls run concurrently (hs_b200_rasterizer_forward_many_v2).
+
+    Each item holds the arguments of one rasterize_forward call by name (the
+    nine tensors ``background`` ... ``camera_position``, the keywords and a
+    distinct ``context``; ``tile_rows`` optional). ``stream`` as in
+    flashgs_forward_many. Outputs are identical to calling rasterize_forward
+    item by item.
+    """
+    structs, outs = [], []
+    library = None
+    for item in calls:
+        item = dict(item)
+        context = item.pop("context")
+        rows = item.pop("tile_rows", None)
+        named, out = _rasterizer_arguments(**item)
+        library = context.library
+        structs.append(native_runtime.RasterizerCallV2(handle=context.handle, **named, **_rows_fields(rows)))
+        outs.append(out)
+    if not structs:
+        return []
+    array = (native_runtime.RasterizerCallV2 * len(structs))(*structs)
+    error = error_buffer()
+    status = library.hs_b200_rasterizer_forward_many_v2(array, len(structs), stream, error, len(error))
+    check_status(status, "hs_b200_rasterizer_forward_many_v2", error)
+    return outs
 
 
 def flashgs_prepare_host(

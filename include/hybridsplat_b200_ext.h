@@ -85,6 +85,96 @@ HS_API int32_t hs_b200_rasterizer_forward_noalloc_f32_v1(
     float* output_weight, int32_t* output_radii, int32_t* output_rendered, char* error_text,
     uint64_t error_capacity) HS_NOEXCEPT;
 
+/* Arguments of one hs_flashgs_forward_f32_v1 call (same names, meaning and
+ * checks) plus a strip of 16x16 tile rows as in
+ * hs_b200_flashgs_forward_rows_f32_v1 (tile_row_end = UINT32_MAX: the whole
+ * frame). camera_position3, camera_rotation9 and background3 are host
+ * pointers, read before the call returns. */
+typedef struct HsB200FlashgsCallV2 {
+    HsRasterizerHandle handle;
+    uint64_t point_count;
+    int32_t width;
+    int32_t height;
+    const float* positions3;
+    const float* shs48;
+    const float* colors3;
+    int32_t use_sh;
+    float scale_modifier;
+    const float* opacities1;
+    const float* covariance6;
+    const float* scales2;
+    const float* rotations4;
+    const float* specular1;
+    const float* roughness1;
+    const float* camera_position3;
+    const float* camera_rotation9;
+    float focal_x;
+    float focal_y;
+    float z_far;
+    float z_near;
+    const float* background3;
+    uint64_t initial_pair_capacity;
+    float* output_color3;
+    float* output_other2;
+    float* output_depth1;
+    float* output_alpha1;
+    float* output_normal3;
+    float* output_median_depth1;
+    float* output_distortion1;
+    int32_t* output_num_rendered;
+    uint32_t tile_row_begin;
+    uint32_t tile_row_end;
+} HsB200FlashgsCallV2;
+
+/* Arguments of one hs_rasterizer_forward_f32_v1 call plus a tile-row strip,
+ * as above. */
+typedef struct HsB200RasterizerCallV2 {
+    HsRasterizerHandle handle;
+    uint64_t point_count;
+    const float* background5;
+    int32_t width;
+    int32_t height;
+    const float* means3d;
+    const float* colors5;
+    const float* opacities;
+    const float* scales2;
+    float scale_modifier;
+    int32_t prefiltered;
+    const float* rotations4;
+    const float* viewmatrix4x4;
+    const float* projmatrix4x4;
+    const float* camera_position3;
+    float tan_fovx;
+    float tan_fovy;
+    float* output_color5;
+    float* output_aux7;
+    float* output_weight;
+    int32_t* output_radii;
+    int32_t* output_rendered;
+    uint32_t tile_row_begin;
+    uint32_t tile_row_end;
+} HsB200RasterizerCallV2;
+
+/* Runs call_count independent raster calls concurrently, for example the
+ * base and reflection branches of one view. Each call needs its own handle
+ * (distinct handles, all on one device); each handle's workspaces, counters
+ * and stage timing are used as by a single call. The calls run on per-handle
+ * streams ordered after the work queued on `stream` (a cudaStream_t; NULL is
+ * the legacy default stream the v1 entry points use), and `stream` is ordered
+ * after all of them, so outputs are ready for work queued there next. Every
+ * preprocess and binning stage is queued before any tile renderer, so the
+ * latency-bound stages of the calls overlap. Outputs are identical to those
+ * of the calls made one by one. As in the v1 calls, the host waits once per
+ * call for its pair count. All arguments are checked before any work is
+ * queued; after an error during execution the outputs are unspecified. No
+ * counterpart in the reference library. */
+HS_API int32_t hs_b200_flashgs_forward_many_v2(
+    const HsB200FlashgsCallV2* calls, uint32_t call_count, void* stream, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+HS_API int32_t hs_b200_rasterizer_forward_many_v2(
+    const HsB200RasterizerCallV2* calls, uint32_t call_count, void* stream, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+
 #ifdef __cplusplus
 }
 #endif

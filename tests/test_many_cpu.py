@@ -1,0 +1,124 @@
+"""Host side of the concurrent raster entry points (hs_b200_*_forward_many_v2).
+
+The call structs of include/hybridsplat_b200_ext.h must match their ctypes
+mirrors field by field, and every call is checked, with the messages of the
+single-call entry points, before any handle is used.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import REPO
+from hybridsplat_jittor_render_b200 import native_runtime as nr
+from hybridsplat_jittor_render_b200 import ops
+
+EXT_HEADER = REPO / "include" / "hybridsplat_b200_ext.h"
+C_TYPES = {
+    "HsRasterizerHandle": ctypes.c_void_p, "uint64_t": ctypes.c_uint64, "int32_t": ctypes.c_int32,
+    "uint32_t": ctypes.c_uint32, "float": ctypes.c_float,
+}
+
+
+def header_struct(name: str) -> list[tuple[str, object]]:
+    body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), EXT_HEADER.read_text(), re.S).group(1)
+    fields = []
+    for decl in filter(None, (d.strip() for d in body.split(";"))):
+        decl = re.sub(r"/\*.*?\*/", "", decl, flags=re.S).strip()
+        ctype, field = decl.rsplit(None, 1)
+        if field.startswith("*") or ctype.endswith("*"):
+            fields.append((field.lstrip("*"), ctypes.c_void_p))
+        else:
+            fields.append((field, C_TYPES[ctype.replace("const ", "")]))
+    return fields
+
+
+@pytest.mark.parametrize("name,mirror", [("HsB200FlashgsCallV2", nr.FlashgsCallV2),
+                                         ("HsB200RasterizerCallV2", nr.RasterizerCallV2)])
+def test_call_structs_match_header(name, mirror):
+    assert [(f, t) for f, t in mirror._fields_] == header_struct(name)
+
+
+def test_struct_fields_cover_the_single_call_arguments():
+    flashgs = {f for f, _ in nr.FlashgsCallV2._fields_}
+    raster = {f for f, _ in nr.RasterizerCallV2._fields_}
+    assert flashgs == set(ops._FLASHGS_ORDER) | {"handle", "tile_row_begin", "tile_row_end"}
+    assert raster == set(ops._RASTERIZER_ORDER) | {"handle", "tile_row_begin", "tile_row_end"}
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return nr.load_native_library()
+
+
+def _flashgs_struct(**over):
+    position, rotation, bg = (ctypes.c_float * 3)(), (ctypes.c_float * 9)(1, 0, 0, 0, 1, 0, 0, 0, 1), \
+        (ctypes.c_float * 3)()
+    dummy = 16
+    s = nr.FlashgsCallV2(handle=dummy, point_count=0, width=64, height=48, use_sh=1, scale_modifier=1.0,
+                         camera_position3=ctypes.addressof(position), camera_rotation9=ctypes.addressof(rotation),
+                         focal_x=50.0, focal_y=50.0, z_far=100.0, z_near=0.01, background3=ctypes.addressof(bg),
+                         initial_pair_capacity=1024, output_color3=dummy, output_other2=dummy, output_depth1=dummy,
+                         output_alpha1=dummy, output_normal3=dummy, output_median_depth1=dummy,
+                         output_distortion1=dummy, output_num_rendered=dummy, tile_row_begin=0,
+                         tile_row_end=0xFFFFFFFF)
+    for k, v in over.items():
+        setattr(s, k, v)
+    return s, (position, rotation, bg)
+
+
+def _raster_struct(**over):
+    dummy = 16
+    s = nr.RasterizerCallV2(handle=dummy, point_count=0, background5=dummy, width=64, height=48,
+                            scale_modifier=1.0, tan_fovx=0.5, tan_fovy=0.5, output_color5=dummy,
+                            output_aux7=dummy, output_rendered=dummy, tile_row_begin=0, tile_row_end=0xFFFFFFFF)
+    for k, v in over.items():
+        setattr(s, k, v)
+    return s
+
+
+def _many(lib, symbol, structs, count=None):
+    array = (type(structs[0]) * len(structs))(*structs) if structs else None
+    err = ctypes.create_string_buffer(512)
+    status = getattr(lib, symbol)(array, len(structs) if count is None else count, None, err, len(err))
+    return status, err.value.decode()
+
+
+def test_empty_and_null_batches(lib):
+    for symbol in ("hs_b200_flashgs_forward_many_v2", "hs_b200_rasterizer_forward_many_v2"):
+        assert _many(lib, symbol, []) == (0, "")
+        assert _many(lib, symbol, [], count=2) == (1, "calls is null")
+
+
+@pytest.mark.parametrize("over,expected", [
+    (dict(handle=None), (1, "FlashGS received a null required handle or buffer")),
+    (dict(width=0), (3, "FlashGS dimensions or scalar arguments are invalid")),
+    (dict(tile_row_begin=2, tile_row_end=2), (3, "tile rows must satisfy 0 <= begin < end <= tile rows")),
+    (dict(tile_row_end=4), (3, "tile rows must satisfy 0 <= begin < end <= tile rows")),
+    (dict(point_count=5), (1, "non-empty FlashGS input contains a null buffer")),
+])
+def test_flashgs_batch_checks_every_call_first(lib, over, expected):
+    good, keep_a = _flashgs_struct()
+    bad, keep_b = _flashgs_struct(**over)
+    # the bad call is second: the first (fake) handle must not be touched
+    assert _many(lib, "hs_b200_flashgs_forward_many_v2", [good, bad]) == expected
+
+
+@pytest.mark.parametrize("over,expected", [
+    (dict(handle=None), (1, "rasterizer received a null required handle or buffer")),
+    (dict(tan_fovx=0.0), (3, "rasterizer dimensions or scalar arguments are invalid")),
+    (dict(prefiltered=2), (3, "rasterizer dimensions or scalar arguments are invalid")),
+    (dict(tile_row_begin=1, tile_row_end=0), (3, "tile rows must satisfy 0 <= begin < end <= tile rows")),
+    (dict(point_count=3), (1, "non-empty rasterizer input contains a null buffer")),
+])
+def test_rasterizer_batch_checks_every_call_first(lib, over, expected):
+    assert _many(lib, "hs_b200_rasterizer_forward_many_v2", [_raster_struct(), _raster_struct(**over)]) == expected
+
+
+def test_ops_rows_fields():
+    assert ops._rows_fields(None) == {"tile_row_begin": 0, "tile_row_end": 0xFFFFFFFF}
+    assert ops._rows_fields((1, 3)) == {"tile_row_begin": 1, "tile_row_end": 3}
+    assert ops._rows_fields((0, 0xFFFFFFFF))["tile_row_end"] == 0xFFFFFFFE
