@@ -230,14 +230,14 @@ class Frame:
 
     def launches_per_step(self) -> int:
         """Kernels of this library launched by one render() call (memsets and
-        copies excluded): per raster call preprocess, depth-sort histogram +
+        copies excluded): per raster call preprocess, totals publication, depth-sort histogram +
         4 passes, pair offsets, emission, tile-sort histogram + passes, ranges,
         tile order and the rasteriser; plus the elementwise kernels of the view."""
         from hybridsplat_jittor_render_b200.scenes import SCENES
         spec = SCENES[SCENE]
         tiles = ((spec.width + 15) // 16) * ((spec.height + 15) // 16)
         tile_passes = math.ceil(max(1, int(tiles).bit_length()) / 8)
-        per_raster = 1 + (1 + 4) + 1 + 1 + (1 + tile_passes) + 1 + 1 + 1
+        per_raster = 1 + 1 + (1 + 4) + 1 + 1 + (1 + tile_passes) + 1 + 1 + 1
         extra = 2 if self.backend == "standard" else 0  # direction + SH
         return 2 * per_raster + extra + 3  # + reflection prefix, suffix, fusion
 

@@ -28,6 +28,31 @@ constexpr int kScanTile = kScanThreads * kScanItems;   // 2048 Gaussians per blo
 constexpr int kEmitThreads = 256;
 
 inline uint32_t scan_tiles(uint32_t count) { return (count + kScanTile - 1) / kScanTile; }
+
+// Publishes the four totals words of a raster call to mapped pinned host
+// memory from the SMs. A cudaMemcpyAsync of them would queue on the
+// device-to-host copy engine behind any bulk read-back the caller has in
+// flight (a previous frame's maps), delaying the host's wait for the pair
+// count by the whole transfer; stores from a kernel do not.
+static __global__ void publish_totals_kernel(const uint32_t* __restrict__ totals,
+                                             volatile uint32_t* host) {
+    if (threadIdx.x < 4) host[threadIdx.x] = totals[threadIdx.x];
+    __threadfence_system();
+}
+
+// Allocates the mapped pinned totals block of a context: *host for the host,
+// *device for kernels.
+inline cudaError_t alloc_mapped_totals(uint32_t** host, uint32_t** device) {
+    cudaError_t st = cudaHostAlloc(reinterpret_cast<void**>(host), 4 * sizeof(uint32_t),
+                                   cudaHostAllocPortable | cudaHostAllocMapped);
+    if (st != cudaSuccess) return st;
+    st = cudaHostGetDevicePointer(reinterpret_cast<void**>(device), *host, 0);
+    if (st != cudaSuccess) {
+        cudaFreeHost(*host);
+        *host = nullptr;
+    }
+    return st;
+}
 // Scratch words of offsets_kernel (counter + one status word per block);
 // zeroed before the launch.
 inline uint64_t scan_scratch_bytes(uint32_t count) {

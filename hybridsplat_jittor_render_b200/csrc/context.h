@@ -102,14 +102,16 @@ struct HsRasterizerContext {
     hs::DeviceBuffer std_image;     // tile ranges
     uint64_t std_peak_bytes = 0;
     uint64_t std_growth_count = 0;
-    uint32_t* std_total_host = nullptr;  // pinned readback of the pair count
+    uint32_t* std_total_host = nullptr;    // mapped pinned readback of the pair totals
+    uint32_t* std_total_mapped = nullptr;  // its device address
 
     // deterministic FlashGS backend
     hs::DeviceBuffer fg_gaussian;   // records, keys, counts, depth order
     hs::DeviceBuffer fg_pairs;      // tile ids / Gaussian ids (+ ping-pong)
     hs::DeviceBuffer fg_sort;       // radix-sort and scan scratch
     hs::DeviceBuffer fg_ranges;     // int2 per tile
-    uint32_t* fg_total_host = nullptr;
+    uint32_t* fg_total_host = nullptr;    // mapped pinned readback of the pair count
+    uint32_t* fg_total_mapped = nullptr;  // its device address
     uint64_t fg_gaussian_capacity = 0;
     uint64_t fg_pair_capacity = 0;
     uint64_t fg_range_capacity = 0;

@@ -124,6 +124,7 @@ cudaError_t flashgs_release(HsRasterizerContext* ctx) {
         const cudaError_t e = cudaFreeHost(ctx->fg_total_host);
         if (first == cudaSuccess) first = e;
         ctx->fg_total_host = nullptr;
+        ctx->fg_total_mapped = nullptr;
     }
     ctx->fg_gaussian_capacity = 0;
     ctx->fg_pair_capacity = 0;
@@ -190,8 +191,7 @@ cudaError_t FlashgsPass::begin() {
     if (st != cudaSuccess || c_.point_count == 0) return st;
 
     if (ctx_->fg_total_host == nullptr) {
-        st = cudaHostAlloc(reinterpret_cast<void**>(&ctx_->fg_total_host), 4 * sizeof(uint32_t),
-                           cudaHostAllocPortable);
+        st = bin::alloc_mapped_totals(&ctx_->fg_total_host, &ctx_->fg_total_mapped);
         if (st != cudaSuccess) return st;
         ++ctx_->fg_growth_count;
     }
@@ -223,8 +223,8 @@ cudaError_t FlashgsPass::begin() {
         ctx_->device_error, static_cast<int>(c_.row_begin), static_cast<int>(c_.row_end));
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
-    st = cudaMemcpyAsync(ctx_->fg_total_host, gv_.total, 4 * sizeof(uint32_t),
-                         cudaMemcpyDeviceToHost, stream);
+    bin::publish_totals_kernel<<<1, 32, 0, stream>>>(gv_.total, ctx_->fg_total_mapped);
+    st = cudaGetLastError();
     if (st == cudaSuccess) st = cudaEventRecord(ctx_->fg_count_event, stream);
     if (st != cudaSuccess) return st;
     marks_.mark(1);

@@ -6,15 +6,20 @@
 //   status[kMaxPasses][tiles][kBins] look-back words
 // Each pass kernel block:
 //   1. takes the next tile number (so every earlier tile's block has
-//      already started and will publish without waiting on this one);
+//      already started and will publish without waiting on this one) and
+//      copies the tile's keys and values into shared memory with two bulk
+//      asynchronous copies (the TMA engine; a ragged tail of < 4 items with
+//      plain loads), so no thread holds the items in registers while ranking;
 //   2. ranks its 2048 items stably: warp w owns the contiguous segment
 //      [256w, 256w + 256) and walks it 32 items at a time with
 //      __match_any_sync on the digit; per-warp digit counts are prefixed
 //      across warps;
 //   3. publishes its per-digit counts, looks back for the counts of all
 //      earlier tiles, publishes the inclusive sums;
-//   4. stages the tile in shared memory in digit order and writes each digit
-//      run to consecutive global positions (coalesced).
+//   4. permutes the tile in shared memory into digit order and writes each
+//      digit run to consecutive global positions (coalesced).
+// Keeping the tile in shared memory instead of registers lets six blocks
+// share an SM, which hides the latency of the look-back.
 #include "sort.cuh"
 
 namespace hs {
@@ -22,7 +27,16 @@ namespace sort {
 namespace {
 
 constexpr int kWarps = kThreads / 32;
-constexpr int kWarpItems = kTile / kWarps;  // 256 contiguous items per warp
+
+// Pass kernels come in two tile sizes: 2048 items (8 per thread) while the
+// whole sort fits in about two waves of resident blocks, 4096 items (16 per
+// thread) above that. Larger tiles halve the rate at which tiles start, and
+// with it the number of predecessors a new tile finds holding only an
+// aggregate; the look-back of the large variant also reads more of them per
+// round trip.
+constexpr int kLargeItems = 16;
+constexpr int kLargeWindow = 16;
+constexpr uint32_t kLargeSortItems = 1u << 23;
 
 struct SortScratch {
     uint32_t* hist;       // [kMaxPasses][kBins]
@@ -46,6 +60,8 @@ __device__ __forceinline__ uint32_t digit_of(uint32_t key, int shift, uint32_t m
     return (key >> shift) & mask;
 }
 
+// Digit counts of every pass in one read of the keys: 16-byte loads (the key
+// arrays are 16-byte aligned), per-block shared-memory counts.
 __global__ void __launch_bounds__(kThreads) histogram_kernel(const uint32_t* __restrict__ keys,
                                                              uint32_t count, int begin_bit,
                                                              int end_bit,
@@ -54,21 +70,64 @@ __global__ void __launch_bounds__(kThreads) histogram_kernel(const uint32_t* __r
     const int passes = (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
     for (int p = 0; p < passes; ++p) bins[p][threadIdx.x] = 0;
     __syncthreads();
-    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kThreads;
-    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x; i < count;
-         i += stride) {
-        const uint32_t key = keys[i];
+    auto count_key = [&](uint32_t key) {
         for (int p = 0; p < passes; ++p) {
             const int shift = begin_bit + p * kRadixBits;
             const int bits = min(kRadixBits, end_bit - shift);
             atomicAdd(&bins[p][digit_of(key, shift, (1u << bits) - 1u)], 1u);
         }
+    };
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * kThreads;
+    const uint64_t quads = count / 4u;
+    const uint4* keys4 = reinterpret_cast<const uint4*>(keys);
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x; i < quads;
+         i += stride) {
+        const uint4 q = keys4[i];
+        count_key(q.x);
+        count_key(q.y);
+        count_key(q.z);
+        count_key(q.w);
     }
+    if (blockIdx.x == 0 && threadIdx.x < count - quads * 4u) count_key(keys[quads * 4u + threadIdx.x]);
     __syncthreads();
     for (int p = 0; p < passes; ++p) {
         const uint32_t v = bins[p][threadIdx.x];
         if (v != 0u) atomicAdd(&hist[p * kBins + threadIdx.x], v);
     }
+}
+
+__device__ __forceinline__ uint32_t shared_address(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Bulk asynchronous copy global -> shared, completing on an mbarrier. Both
+// addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* barrier) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(shared_address(dst)), "l"(src), "r"(bytes), "r"(shared_address(barrier))
+        : "memory");
+}
+
+__device__ __forceinline__ bool barrier_try_wait(uint64_t* barrier, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(shared_address(barrier)), "r"(parity)
+        : "memory");
+    return done != 0u;
+}
+
+// Bounded wait for phase 0 of the tile barrier; false when it gave up.
+__device__ __forceinline__ bool wait_tile(uint64_t* barrier) {
+    for (uint32_t spins = 0; spins < kSpinLimit; ++spins) {
+        if (barrier_try_wait(barrier, 0u)) return true;
+    }
+    return false;
 }
 
 // Exclusive scan of 256 values held one per thread (all kThreads threads).
@@ -88,48 +147,99 @@ __device__ __forceinline__ uint32_t block_exclusive_256(uint32_t v, uint32_t* wa
     return base + incl - v;
 }
 
-__global__ void __launch_bounds__(kThreads) onesweep_kernel(
+template <int kItems, int kWindow>
+__global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel(
     const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, uint32_t count, int shift,
     int bits, uint32_t tiles, const uint32_t* __restrict__ hist, uint32_t* __restrict__ counter,
     uint32_t* __restrict__ status, uint32_t* __restrict__ error) {
+    constexpr uint32_t kTileItems = kThreads * kItems;
+    constexpr uint32_t kWarpItems = kTileItems / kWarps;  // contiguous items per warp
+    // The tile, in input order until step 4 permutes it into digit order.
+    __shared__ alignas(16) uint32_t tile_keys[kTileItems];
+    __shared__ alignas(16) uint32_t tile_vals[kTileItems];
     __shared__ uint32_t warp_count[kWarps][kBins];
     __shared__ uint32_t digit_start[kBins];   // first local position of each digit
     __shared__ uint32_t global_base[kBins];   // destination of the digit run's first item
     __shared__ uint32_t warp_sums[kWarps];
-    __shared__ uint32_t stage_keys[kTile];
-    __shared__ uint32_t stage_vals[kTile];
     __shared__ uint32_t tile_slot;
+    __shared__ alignas(8) uint64_t loaded;    // completes when the bulk copies land
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t mask = (1u << bits) - 1u;
-    if (threadIdx.x == 0) tile_slot = atomicAdd(counter, 1u);
+    if (threadIdx.x == 0) {
+        tile_slot = atomicAdd(counter, 1u);
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(shared_address(&loaded))
+                     : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     for (int b = lane; b < kBins; b += 32) warp_count[warp][b] = 0;
     __syncthreads();
     const uint32_t tile = tile_slot;
+    const uint64_t tile_begin = static_cast<uint64_t>(tile) * kTileItems;
+    const uint64_t left = count - tile_begin;
+    const uint32_t n = left < static_cast<uint64_t>(kTileItems) ? static_cast<uint32_t>(left)
+                                                                : kTileItems;
+    const uint32_t bulk = n & ~3u;  // whole 16-byte groups go through the copy engine
+
+    // 1. load the tile
+    if (threadIdx.x == 0) {
+        if (bulk != 0u) {
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                         ::"r"(shared_address(&loaded)), "r"(2u * bulk * 4u) : "memory");
+            bulk_load(tile_keys, keys_in + tile_begin, bulk * 4u, &loaded);
+            bulk_load(tile_vals, vals_in + tile_begin, bulk * 4u, &loaded);
+        } else {
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];"
+                         ::"r"(shared_address(&loaded)) : "memory");
+        }
+    }
+    if (threadIdx.x < n - bulk) {
+        tile_keys[bulk + threadIdx.x] = keys_in[tile_begin + bulk + threadIdx.x];
+        tile_vals[bulk + threadIdx.x] = vals_in[tile_begin + bulk + threadIdx.x];
+    }
+    const bool landed = wait_tile(&loaded);
+    if (!__syncthreads_and(landed)) {
+        // The copies did not complete within the bound: report, wait once more
+        // (bounded) so that no copy is left writing this block's shared memory.
+        if (threadIdx.x == 0) {
+            if (error != nullptr) atomicOr(error, 1u);
+            wait_tile(&loaded);
+        }
+        return;
+    }
 
     // 2. stable ranking within the tile
-    const uint64_t seg = static_cast<uint64_t>(tile) * kTile +
-                         static_cast<uint64_t>(warp) * kWarpItems;
+    const uint32_t seg = static_cast<uint32_t>(warp) * kWarpItems;
     const uint32_t lt_mask = (1u << lane) - 1u;
-    uint32_t key[kItemsPerThread], val[kItemsPerThread], rank[kItemsPerThread];
-    int dig[kItemsPerThread];
+    uint32_t rank[kItems];
 #pragma unroll
-    for (int k = 0; k < kItemsPerThread; ++k) {
-        const uint64_t i = seg + static_cast<uint64_t>(k) * 32 + lane;
-        const bool valid = i < count;
-        key[k] = valid ? keys_in[i] : 0u;
-        val[k] = valid ? vals_in[i] : 0u;
-        dig[k] = valid ? static_cast<int>(digit_of(key[k], shift, mask)) : -1;
-    }
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t i = seg + static_cast<uint32_t>(k) * 32u + lane;
+        const bool valid = i < n;
+        const uint32_t dg = valid ? digit_of(tile_keys[i], shift, mask) : 0u;
+        uint32_t peers;
+        if (kItems == kLargeItems) {
+            // lanes holding the same digit, one ballot per digit bit (cheaper
+            // than __match_any_sync when many blocks share an SM)
+            peers = __ballot_sync(0xffffffffu, valid);
 #pragma unroll
-    for (int k = 0; k < kItemsPerThread; ++k) {
-        const uint32_t peers = __match_any_sync(0xffffffffu, dig[k]);
-        const uint32_t before = dig[k] >= 0 ? warp_count[warp][dig[k]] : 0u;
+            for (int bit = 0; bit < kRadixBits; ++bit) {
+                if (bit < bits) {
+                    const uint32_t set = (dg >> bit) & 1u;
+                    const uint32_t vote = __ballot_sync(0xffffffffu, set != 0u);
+                    peers &= set != 0u ? vote : ~vote;
+                }
+            }
+        } else {
+            peers = __match_any_sync(0xffffffffu, valid ? static_cast<int>(dg) : -1);
+        }
+        const int dig = valid ? static_cast<int>(dg) : -1;
+        const uint32_t before = dig >= 0 ? warp_count[warp][dig] : 0u;
         __syncwarp();
         rank[k] = before + __popc(peers & lt_mask);
         const int leader = __ffs(peers) - 1;
-        if (dig[k] >= 0 && lane == leader) warp_count[warp][dig[k]] = before + __popc(peers);
+        if (dig >= 0 && lane == leader) warp_count[warp][dig] = before + __popc(peers);
         __syncwarp();
     }
     __syncthreads();
@@ -150,7 +260,8 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(
     } else {
         store_status(my_status, kFlagAggregate | total);
     }
-    const uint32_t earlier = tile == 0 ? 0u : look_back(status + b, tile, kBins, error);
+    const uint32_t earlier =
+        tile == 0 ? 0u : look_back<kWindow>(status + b, tile, kBins, error);
     if (tile != 0) store_status(my_status, kFlagInclusive | ((earlier + total) & kValueMask));
 
     // global start of each digit: exclusive scan of the pass histogram
@@ -158,26 +269,39 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(
     const uint32_t local_start = block_exclusive_256(total, warp_sums);
     digit_start[b] = local_start;
     global_base[b] = digit_global + earlier;
-    __syncthreads();
 
-    // 4. stage in digit order, then write digit runs
+    // 4. permute the tile into digit order in place (keys, then values), then
+    //    write digit runs
+    uint32_t item[kItems];
+    __syncthreads();  // digit_start / global_base
 #pragma unroll
-    for (int k = 0; k < kItemsPerThread; ++k) {
-        if (dig[k] < 0) continue;
-        const uint32_t pos = digit_start[dig[k]] + warp_count[warp][dig[k]] + rank[k];
-        stage_keys[pos] = key[k];
-        stage_vals[pos] = val[k];
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t i = seg + static_cast<uint32_t>(k) * 32u + lane;
+        item[k] = tile_keys[i];
+        if (i < n) {
+            const uint32_t d = digit_of(item[k], shift, mask);
+            rank[k] += digit_start[d] + warp_count[warp][d];  // final position in the tile
+        }
     }
     __syncthreads();
-    const uint64_t tile_begin = static_cast<uint64_t>(tile) * kTile;
-    const uint64_t left = count - tile_begin;
-    const uint32_t n = left < static_cast<uint64_t>(kTile) ? static_cast<uint32_t>(left) : kTile;
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        if (seg + static_cast<uint32_t>(k) * 32u + lane < n) tile_keys[rank[k]] = item[k];
+    }
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) item[k] = tile_vals[seg + static_cast<uint32_t>(k) * 32u + lane];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        if (seg + static_cast<uint32_t>(k) * 32u + lane < n) tile_vals[rank[k]] = item[k];
+    }
+    __syncthreads();
     for (uint32_t i = threadIdx.x; i < n; i += kThreads) {
-        const uint32_t k = stage_keys[i];
+        const uint32_t k = tile_keys[i];
         const uint32_t d = digit_of(k, shift, mask);
         const uint32_t dst = global_base[d] + (i - digit_start[d]);
         keys_out[dst] = k;
-        vals_out[dst] = stage_vals[i];
+        vals_out[dst] = tile_vals[i];
     }
 }
 
@@ -262,7 +386,12 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
         return cudaErrorInvalidValue;
     }
     const uint32_t tiles = tiles_for(count);
+    const bool large = count >= kLargeSortItems;
+    const uint32_t large_tiles =
+        static_cast<uint32_t>((static_cast<uint64_t>(count) + kThreads * kLargeItems - 1) /
+                              (kThreads * kLargeItems));
     const int passes = (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
+    // status words are laid out for 2048-item tiles, enough for either size
     const SortScratch s = sort_scratch(scratch, tiles, passes);
     cudaError_t st = cudaMemsetAsync(scratch, 0, s.zero_bytes, stream);
     if (st != cudaSuccess) return st;
@@ -270,7 +399,7 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
     if (cudaGetDevice(&device) == cudaSuccess) {
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
     }
-    const uint32_t hist_cap = static_cast<uint32_t>(sms) * 4u;
+    const uint32_t hist_cap = static_cast<uint32_t>(sms) * 8u;
     const uint32_t hist_blocks = tiles < hist_cap ? tiles : hist_cap;
     histogram_kernel<<<hist_blocks, kThreads, 0, stream>>>(keys, count, begin_bit, end_bit,
                                                            s.hist);
@@ -281,9 +410,16 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
     int pass = 0;
     for (int shift = begin_bit; shift < end_bit; shift += kRadixBits, ++pass) {
         const int bits = min(kRadixBits, end_bit - shift);
-        onesweep_kernel<<<tiles, kThreads, 0, stream>>>(
-            src_k, src_v, dst_k, dst_v, count, shift, bits, tiles, s.hist + pass * kBins,
-            s.counters + pass, s.status + static_cast<uint64_t>(pass) * tiles * kBins, error);
+        uint32_t* pass_status = s.status + static_cast<uint64_t>(pass) * tiles * kBins;
+        if (large) {
+            onesweep_kernel<kLargeItems, kLargeWindow><<<large_tiles, kThreads, 0, stream>>>(
+                src_k, src_v, dst_k, dst_v, count, shift, bits, large_tiles,
+                s.hist + pass * kBins, s.counters + pass, pass_status, error);
+        } else {
+            onesweep_kernel<kItemsPerThread, kLookBackWindow><<<tiles, kThreads, 0, stream>>>(
+                src_k, src_v, dst_k, dst_v, count, shift, bits, tiles, s.hist + pass * kBins,
+                s.counters + pass, pass_status, error);
+        }
         uint32_t* tk = src_k;
         uint32_t* tv = src_v;
         src_k = dst_k;

@@ -85,25 +85,26 @@ __device__ __forceinline__ void store_status(uint32_t* p, uint32_t v) {
 
 // Exclusive prefix of `status[tile * stride]` over all earlier tiles, by
 // decoupled look-back. The caller has already published its own aggregate.
-// Eight predecessors are read per step, so a chain of tiles that have only
-// published aggregates costs one memory round trip per eight tiles.
+// kWindow predecessors are read per step, so a chain of tiles that have only
+// published aggregates costs one memory round trip per kWindow tiles.
 constexpr int kLookBackWindow = 8;
 
+template <int kWindow = kLookBackWindow>
 __device__ __forceinline__ uint32_t look_back(const uint32_t* status, uint32_t tile,
                                               uint32_t stride, uint32_t* error) {
     uint32_t prefix = 0;
     int64_t t = static_cast<int64_t>(tile) - 1;
     uint32_t spins = 0;
     while (t >= 0) {
-        uint32_t s[kLookBackWindow];
+        uint32_t s[kWindow];
 #pragma unroll
-        for (int k = 0; k < kLookBackWindow; ++k) {
+        for (int k = 0; k < kWindow; ++k) {
             s[k] = t - k >= 0 ? load_status(status + static_cast<uint64_t>(t - k) * stride)
                               : kFlagInclusive;
         }
         int k = 0;
 #pragma unroll
-        for (int i = 0; i < kLookBackWindow; ++i) {
+        for (int i = 0; i < kWindow; ++i) {
             if (k != i || (s[i] & ~kValueMask) == 0u) continue;  // stopped, or not published yet
             prefix += s[i] & kValueMask;
             if ((s[i] & kFlagInclusive) != 0u) return prefix;

@@ -103,6 +103,7 @@ cudaError_t standard_release(HsRasterizerContext* ctx) {
         const cudaError_t e = cudaFreeHost(ctx->std_total_host);
         if (first == cudaSuccess) first = e;
         ctx->std_total_host = nullptr;
+        ctx->std_total_mapped = nullptr;
     }
     return first;
 }
@@ -180,8 +181,7 @@ cudaError_t StandardPass::begin() {
                        &ctx_->std_growth_count, true);
     if (st != cudaSuccess) return st;
     if (ctx_->std_total_host == nullptr) {
-        st = cudaHostAlloc(reinterpret_cast<void**>(&ctx_->std_total_host), 4 * sizeof(uint32_t),
-                           cudaHostAllocPortable);
+        st = bin::alloc_mapped_totals(&ctx_->std_total_host, &ctx_->std_total_mapped);
         if (st != cudaSuccess) return st;
     }
     st = ensure_device_error(ctx_);
@@ -210,8 +210,8 @@ cudaError_t StandardPass::begin() {
         c_.prefiltered ? 1 : 0, c_.row_begin, c_.row_end, po);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
-    st = cudaMemcpyAsync(ctx_->std_total_host, gv_.totals, 4 * sizeof(uint32_t),
-                         cudaMemcpyDeviceToHost, stream);
+    bin::publish_totals_kernel<<<1, 32, 0, stream>>>(gv_.totals, ctx_->std_total_mapped);
+    st = cudaGetLastError();
     if (st == cudaSuccess) st = cudaEventRecord(ctx_->std_count_event, stream);
     if (st != cudaSuccess) return st;
     marks_.mark(1);
