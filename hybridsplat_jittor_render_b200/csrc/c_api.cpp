@@ -950,6 +950,55 @@ int32_t hs_rasterizer_precise_sh_to_rgb_f32_v1(const float* sh, const float* dir
     });
 }
 
+int32_t hs_b200_precise_sh_colors5_f32_v1(const float* sh, uint32_t coefficient_count,
+                                          uint32_t degree, const float* points,
+                                          const float* center3, const float* specular,
+                                          const float* roughness, uint64_t count,
+                                          float* colors5, char* error_text,
+                                          uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (degree > 3) {
+            return fail(HS_STATUS_RANGE_ERROR, "precise_sh_to_rgb supports degrees 0 through 3",
+                        error_text, error_capacity);
+        }
+        if (coefficient_count < (degree + 1) * (degree + 1)) {
+            return fail(HS_STATUS_RANGE_ERROR, "precise_sh_to_rgb coefficient count is too small",
+                        error_text, error_capacity);
+        }
+        if (count == 0) return ok(error_text, error_capacity);
+        if (sh == nullptr || points == nullptr || center3 == nullptr || specular == nullptr ||
+            roughness == nullptr || colors5 == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "precise_sh_colors5 received a null non-empty buffer", error_text,
+                        error_capacity);
+        }
+        const cudaError_t e = hs::precise::sh_colors5(sh, coefficient_count, degree, points,
+                                                      center3, specular, roughness, count,
+                                                      colors5, nullptr);
+        if (e != cudaSuccess)
+            return cuda_failure(e, "precise_sh_colors5 launch", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_b200_precise_fuse_maps_planar_f32_v1(const float* base_rgb,
+                                                const float* reflection_rgb,
+                                                const float* specular, float* diffuse,
+                                                float* final_rgb, float* stored_reflection,
+                                                uint64_t pixel_count, char* error_text,
+                                                uint64_t error_capacity) noexcept {
+    const bool present = base_rgb != nullptr && reflection_rgb != nullptr &&
+                         specular != nullptr && diffuse != nullptr && final_rgb != nullptr &&
+                         stored_reflection != nullptr;
+    return elementwise("precise_fuse_maps_planar", pixel_count, present, error_text,
+                       error_capacity, [&] {
+                           return hs::precise::fuse_maps_planar(base_rgb, reflection_rgb, specular,
+                                                                diffuse, final_rgb,
+                                                                stored_reflection, pixel_count,
+                                                                nullptr);
+                       });
+}
+
 int32_t hs_rasterizer_precise_direction_f32_v1(const float* points, const float* center,
                                                uint64_t count, float* output, char* error_text,
                                                uint64_t error_capacity) noexcept {

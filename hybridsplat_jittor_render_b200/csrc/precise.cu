@@ -202,6 +202,101 @@ __global__ void __launch_bounds__(kShThreads) sh16_to_rgb_kernel(
     }
 }
 
+// View direction of one Gaussian, as direction_kernel computes it.
+__device__ __forceinline__ void view_direction(const float* p, float cx, float cy, float cz,
+                                               float& x, float& y, float& z) {
+    const float dx = sub(p[0], cx), dy = sub(p[1], cy), dz = sub(p[2], cz);
+    const float n = norm3_torch(dx, dy, dz);
+    x = div(dx, n);
+    y = div(dy, n);
+    z = div(dz, n);
+}
+
+// The standard branch's colours in one pass: view direction (direction_kernel),
+// SH colour (sh_to_rgb_kernel) and the [rgb, specular, roughness] concatenation
+// that the reference performs in Jittor (renderer.py:260-266). Same rounding
+// as the three steps, so colours5 is bit-identical to them.
+__global__ void sh_colors5_kernel(const float* __restrict__ sh, uint32_t coefficients,
+                                  uint32_t degree, const float* __restrict__ points,
+                                  const float* __restrict__ center,
+                                  const float* __restrict__ specular,
+                                  const float* __restrict__ roughness, uint64_t count,
+                                  float* __restrict__ out5) {
+    const float cx = center[0], cy = center[1], cz = center[2];
+    for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
+         i += uint64_t(gridDim.x) * blockDim.x) {
+        float x, y, z;
+        view_direction(points + 3 * i, cx, cy, cz, x, y, z);
+        const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
+        const float xy = mul(x, y), yz = mul(y, z), xz = mul(x, z);
+        for (uint32_t ch = 0; ch < 3; ++ch) {
+            out5[5 * i + ch] = sh_channel(sh + (i * 3 + ch) * coefficients, x, y, z, xx, yy, zz,
+                                          xy, yz, xz, degree);
+        }
+        out5[5 * i + 3] = specular[i];
+        out5[5 * i + 4] = roughness[i];
+    }
+}
+
+// sh_colors5_kernel for 16 coefficients per channel in 16-byte aligned rows,
+// staged through shared memory as in sh16_to_rgb_kernel.
+template <uint32_t kDegree>
+__global__ void __launch_bounds__(kShThreads) sh16_colors5_kernel(
+    const float4* __restrict__ sh, const float* __restrict__ points,
+    const float* __restrict__ center, const float* __restrict__ specular,
+    const float* __restrict__ roughness, uint64_t count, float* __restrict__ out5) {
+    __shared__ float rows[kShThreads * kShStride];
+    const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kShThreads;
+    const uint64_t left = count - first;
+    const uint32_t n = left < kShThreads ? static_cast<uint32_t>(left) : kShThreads;
+    for (uint32_t f = threadIdx.x; f < n * 12; f += kShThreads) {
+        const float4 v = sh[first * 12 + f];
+        float* d = rows + (f / 12) * kShStride + (f % 12) * 4;
+        d[0] = v.x;
+        d[1] = v.y;
+        d[2] = v.z;
+        d[3] = v.w;
+    }
+    __syncthreads();
+    if (threadIdx.x >= n) return;
+    const uint64_t i = first + threadIdx.x;
+    const float* c = rows + threadIdx.x * kShStride;
+    float x, y, z;
+    view_direction(points + 3 * i, center[0], center[1], center[2], x, y, z);
+    const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
+    const float xy = mul(x, y), yz = mul(y, z), xz = mul(x, z);
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+        out5[5 * i + ch] = sh_channel(c + 16 * ch, x, y, z, xx, yy, zz, xy, yz, xz, kDegree);
+    }
+    out5[5 * i + 3] = specular[i];
+    out5[5 * i + 4] = roughness[i];
+}
+
+// fuse_maps_kernel with channel-first inputs: base and reflection colours as
+// three planes of `pixels` values each, the specular plane; the outputs are
+// interleaved [pixels, 3] exactly as fuse_maps_kernel writes them. This
+// replaces the three HWC transposes that precede fuse_maps in the reference
+// session (renderer.py, math.py:301-311).
+__global__ void fuse_maps_planar_kernel(const float* __restrict__ base,
+                                        const float* __restrict__ refl,
+                                        const float* __restrict__ specular,
+                                        float* __restrict__ diffuse, float* __restrict__ final_rgb,
+                                        float* __restrict__ stored, uint64_t pixels) {
+    for (uint64_t p = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; p < pixels;
+         p += uint64_t(gridDim.x) * blockDim.x) {
+        const float s = specular[p];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const float dv = mul(base[c * pixels + p], sub(1.0f, s));
+            const float rv = mul(mul(refl[c * pixels + p], s), 2.0f);
+            diffuse[3 * p + c] = dv;
+            stored[3 * p + c] = rv;
+            final_rgb[3 * p + c] = add(dv, mul(0.5f, rv));
+        }
+    }
+}
+
 __global__ void reflection_prefix_kernel(const float* __restrict__ rot, uint64_t count,
                                          float* __restrict__ out) {
     // precise_reflection_trace.cu:119-183: the matrix entries contract the
@@ -371,6 +466,36 @@ cudaError_t sh_to_rgb(const float* sh, const float* dirs, uint64_t count, uint32
     }
     sh_to_rgb_kernel<<<grid_for(count), kThreads, 0, s>>>(sh, dirs, count, coefficients, degree,
                                                            out);
+    return cudaGetLastError();
+}
+
+cudaError_t sh_colors5(const float* sh, uint32_t coefficients, uint32_t degree,
+                      const float* points, const float* center, const float* specular,
+                      const float* roughness, uint64_t count, float* out5, cudaStream_t s) {
+    if (count == 0) return cudaSuccess;
+    if (coefficients == 16 && (reinterpret_cast<uintptr_t>(sh) & 15u) == 0 && degree <= 3) {
+        const unsigned blocks = static_cast<unsigned>((count + kShThreads - 1) / kShThreads);
+        const float4* sh4 = reinterpret_cast<const float4*>(sh);
+        switch (degree) {
+            case 0: sh16_colors5_kernel<0><<<blocks, kShThreads, 0, s>>>(sh4, points, center, specular, roughness, count, out5); break;
+            case 1: sh16_colors5_kernel<1><<<blocks, kShThreads, 0, s>>>(sh4, points, center, specular, roughness, count, out5); break;
+            case 2: sh16_colors5_kernel<2><<<blocks, kShThreads, 0, s>>>(sh4, points, center, specular, roughness, count, out5); break;
+            default: sh16_colors5_kernel<3><<<blocks, kShThreads, 0, s>>>(sh4, points, center, specular, roughness, count, out5); break;
+        }
+        return cudaGetLastError();
+    }
+    sh_colors5_kernel<<<grid_for(count), kThreads, 0, s>>>(sh, coefficients, degree, points, center,
+                                                            specular, roughness, count, out5);
+    return cudaGetLastError();
+}
+
+cudaError_t fuse_maps_planar(const float* base, const float* refl, const float* specular,
+                             float* diffuse, float* final_rgb, float* stored, uint64_t pixels,
+                             cudaStream_t s) {
+    if (pixels == 0) return cudaSuccess;
+    if (pixels > UINT64_MAX / 3) return cudaErrorInvalidValue;
+    fuse_maps_planar_kernel<<<grid_for(pixels), kThreads, 0, s>>>(base, refl, specular, diffuse,
+                                                                    final_rgb, stored, pixels);
     return cudaGetLastError();
 }
 

@@ -18,6 +18,14 @@ cudaError_t direction(const float* points, const float* center, uint64_t count, 
                       cudaStream_t s);
 cudaError_t sh_to_rgb(const float* sh, const float* dirs, uint64_t count, uint32_t coefficients,
                       uint32_t degree, float* out, cudaStream_t s);
+// direction + sh_to_rgb + [rgb, specular, roughness] concatenation in one pass.
+cudaError_t sh_colors5(const float* sh, uint32_t coefficients, uint32_t degree,
+                      const float* points, const float* center, const float* specular,
+                      const float* roughness, uint64_t count, float* out5, cudaStream_t s);
+// fuse_maps reading channel-first colour planes.
+cudaError_t fuse_maps_planar(const float* base, const float* refl, const float* specular,
+                             float* diffuse, float* final_rgb, float* stored, uint64_t pixels,
+                             cudaStream_t s);
 cudaError_t reflection_prefix(const float* rot, uint64_t count, float* out, cudaStream_t s);
 cudaError_t reflection_suffix(const float* xyz, const float* center, const float* normal_raw,
                               uint64_t count, float* out36, cudaStream_t s);

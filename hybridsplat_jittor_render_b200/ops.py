@@ -472,6 +472,39 @@ def precise_fuse_maps(base_rgb: torch.Tensor, reflection_rgb: torch.Tensor, spec
     return {"rgb_map": final, "dif_rgb_map": diffuse, "ref_rgb_map": stored}
 
 
+def precise_fuse_maps_planar(base_rgb: torch.Tensor, reflection_rgb: torch.Tensor, specular: torch.Tensor, *,
+                             library: ctypes.CDLL | None = None) -> dict[str, torch.Tensor]:
+    """precise_fuse_maps of channel-first inputs: base_rgb and reflection_rgb
+    [3,H,W] (views of a raster call's colour planes), specular [1,H,W] or
+    [H,W]; returns the same [H,W,3] maps as precise_fuse_maps of their
+    HWC transposes (hs_b200_precise_fuse_maps_planar_f32_v1)."""
+    if base_rgb.shape[0] != 3 or reflection_rgb.shape != base_rgb.shape:
+        raise ValueError("base_rgb and reflection_rgb must be [3,H,W]")
+    for name, t in (("base_rgb", base_rgb), ("reflection_rgb", reflection_rgb), ("specular", specular)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    h, w = int(base_rgb.shape[1]), int(base_rgb.shape[2])
+    if specular.numel() != h * w:
+        raise ValueError("specular must hold one value per pixel")
+    f = dict(dtype=torch.float32, device=base_rgb.device)
+    diffuse, final, stored = (torch.empty((h, w, 3), **f) for _ in range(3))
+    _elementwise("hs_b200_precise_fuse_maps_planar_f32_v1", library, _ptr(base_rgb), _ptr(reflection_rgb),
+                 _ptr(specular), _ptr(diffuse), _ptr(final), _ptr(stored), h * w)
+    return {"rgb_map": final, "dif_rgb_map": diffuse, "ref_rgb_map": stored}
+
+
+def precise_sh_colors5(sh: torch.Tensor, points: torch.Tensor, center: torch.Tensor, specular: torch.Tensor,
+                       roughness: torch.Tensor, degree: int, *, library: ctypes.CDLL | None = None) -> torch.Tensor:
+    """[P,5] = [precise_sh_to_rgb(sh, precise_direction(points, center), degree),
+    specular, roughness] in one pass (hs_b200_precise_sh_colors5_f32_v1)."""
+    sh = sh.contiguous()
+    count = int(points.shape[0])
+    out = torch.empty((count, 5), dtype=torch.float32, device=points.device)
+    _elementwise("hs_b200_precise_sh_colors5_f32_v1", library, _ptr(sh), int(sh.shape[-1]), int(degree),
+                 _ptr(points), _ptr(center), _ptr(specular), _ptr(roughness), count, _ptr(out))
+    return out
+
+
 def precise_sh_to_rgb(sh: torch.Tensor, directions: torch.Tensor, degree: int, *,
                       library: ctypes.CDLL | None = None) -> torch.Tensor:
     """sh is [P,3,C] (channel-major), directions [P,3]; returns [P,3]."""

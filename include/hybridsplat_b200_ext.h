@@ -175,6 +175,30 @@ HS_API int32_t hs_b200_rasterizer_forward_many_v2(
     const HsB200RasterizerCallV2* calls, uint32_t call_count, void* stream, char* error_text,
     uint64_t error_capacity) HS_NOEXCEPT;
 
+/* The standard branch's colours in one pass: hs_rasterizer_precise_direction_f32_v1
+ * of points[count,3] from center3, hs_rasterizer_precise_sh_to_rgb_f32_v1 of
+ * sh[count,3,coefficient_count] (channel-major, as the reference passes its
+ * transposed features) at that direction, and the concatenation
+ * [rgb, specular, roughness] into colors5[count,5] that the reference session
+ * performs in Jittor (renderer.py:260-266). Bit-identical to the three steps;
+ * same argument checks as the SH entry point. All pointers are device
+ * pointers; legacy default stream. No counterpart in the reference library. */
+HS_API int32_t hs_b200_precise_sh_colors5_f32_v1(
+    const float* sh, uint32_t coefficient_count, uint32_t degree, const float* points,
+    const float* center3, const float* specular, const float* roughness, uint64_t count,
+    float* colors5, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
+/* hs_rasterizer_precise_fuse_maps_f32_v1 with channel-first inputs: base_rgb and
+ * reflection_rgb are three planes of pixel_count values each (the first three
+ * planes of a raster call's colour output), specular one plane. Outputs are
+ * the interleaved [pixel_count, 3] maps of the v1 entry point, bit-identical
+ * to transposing the inputs and calling it. No counterpart in the reference
+ * library. */
+HS_API int32_t hs_b200_precise_fuse_maps_planar_f32_v1(
+    const float* base_rgb, const float* reflection_rgb, const float* specular, float* diffuse,
+    float* final_rgb, float* stored_reflection, uint64_t pixel_count, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+
 #ifdef __cplusplus
 }
 #endif

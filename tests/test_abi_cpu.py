@@ -191,3 +191,20 @@ def test_prepare_host_empty_and_null(lib):
     assert lib.hs_flashgs_prepare_npz_host_f32_v1(0, *([None] * 11), err, len(err)) == 0
     assert lib.hs_flashgs_prepare_npz_host_f32_v1(3, *([None] * 11), err, len(err)) == 1
     assert err.value == b"FlashGS NPZ preparation received a null host buffer"
+
+
+@pytest.mark.parametrize("symbol,args,expected", [
+    ("hs_b200_precise_sh_colors5_f32_v1", (None, 16, 3, None, None, None, None, 0, None), 0),
+    ("hs_b200_precise_sh_colors5_f32_v1", (None, 16, 3, None, None, None, None, 10, None), 1),
+    ("hs_b200_precise_sh_colors5_f32_v1", (None, 16, 4, None, None, None, None, 10, None), 3),
+    ("hs_b200_precise_sh_colors5_f32_v1", (None, 8, 3, None, None, None, None, 10, None), 3),
+    ("hs_b200_precise_fuse_maps_planar_f32_v1", (None, None, None, None, None, None, 0), 0),
+    ("hs_b200_precise_fuse_maps_planar_f32_v1", (None, None, None, None, None, None, 10), 1),
+])
+def test_fused_glue_validation(lib, symbol, args, expected):
+    """Argument checks of the fused view-glue entry points, before any launch;
+    the SH checks use the messages of hs_rasterizer_precise_sh_to_rgb_f32_v1."""
+    err = ctypes.create_string_buffer(256)
+    assert getattr(lib, symbol)(*args, err, len(err)) == expected
+    if expected == 3:
+        assert err.value.decode().startswith("precise_sh_to_rgb")

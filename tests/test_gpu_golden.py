@@ -88,3 +88,31 @@ def test_precise_kernels_bit_exact(golden):
     fused = ops.precise_fuse_maps(dev(d["in_base"]), dev(d["in_refl"]), dev(d["in_spec"]))
     for k, v in fused.items():
         assert bits_equal(v.cpu().numpy(), d[f"out_{k}"]), k
+
+
+def test_fused_view_glue_matches_reference_vectors(golden):
+    """hs_b200_precise_sh_colors5 (direction + SH + concatenation) and
+    hs_b200_precise_fuse_maps_planar (channel-first fusion) reproduce the
+    reference build's outputs of the separate steps bit for bit."""
+    d = golden("precise")
+    points, center = dev(d["in_points"]), dev(d["in_center"])
+    spec, rough = dev(d["in_x"][:, None]), dev(d["in_x"][::-1].copy()[:, None])
+    sh = dev(d["in_sh"])
+    for deg in range(4):
+        for variant in ("aligned", "offset", "trimmed"):
+            if variant == "aligned":
+                coeffs = sh
+            elif variant == "offset":  # not 16-byte aligned: the generic kernel
+                store = torch.empty(sh.numel() + 1, device="cuda")
+                store[1:] = sh.reshape(-1)
+                coeffs = store[1:].view(sh.shape)
+            else:  # fewer coefficients than 16 per channel
+                coeffs = sh[:, :, : (deg + 1) ** 2].contiguous()
+            out = ops.precise_sh_colors5(coeffs, points, center, spec, rough, deg).cpu().numpy()
+            assert bits_equal(out[:, :3], d[f"out_sh{deg}"]), (deg, variant)
+            assert bits_equal(out[:, 3], d["in_x"]) and bits_equal(out[:, 4], d["in_x"][::-1]), (deg, variant)
+    planes = lambda a: dev(np.ascontiguousarray(a.T.reshape(a.shape[1], 64, 64)))
+    fused = ops.precise_fuse_maps_planar(planes(d["in_base"]), planes(d["in_refl"]), planes(d["in_spec"]))
+    for k, v in fused.items():
+        assert v.shape == (64, 64, 3)
+        assert bits_equal(v.reshape(-1, 3).cpu().numpy(), d[f"out_{k}"]), k
