@@ -160,20 +160,49 @@ __global__ void __launch_bounds__(kEmitThreads) emit_kernel(
 
 // Per-tile [start, end) of the sorted pair list. Entries of tiles without
 // pairs keep the zeros written before the launch. Tile ids >= tile_count are
-// padding and are ignored.
+// padding and are ignored. Each thread reads four consecutive tile ids with
+// one 16-byte load (the arrays are 16-byte aligned) plus the id before them;
+// the grid strides over the list (ranges_grid blocks of kRangeThreads).
+constexpr int kRangeThreads = 256;
+
+inline unsigned ranges_grid(uint32_t pair_count) {
+    const uint64_t quads = (static_cast<uint64_t>(pair_count) + 3) / 4;
+    const uint64_t blocks = (quads + kRangeThreads - 1) / kRangeThreads;
+    return static_cast<unsigned>(blocks < 148 * 8 ? (blocks > 0 ? blocks : 1) : 148 * 8);
+}
+
 template <class Range>
-__global__ void ranges_kernel(uint32_t pair_count, uint32_t tile_count,
-                              const uint32_t* __restrict__ tile_ids, Range* __restrict__ ranges) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= pair_count) return;
-    const uint32_t t = tile_ids[i];
-    const uint32_t prev = i == 0 ? 0xffffffffu : tile_ids[i - 1];
-    if (t != prev) {
-        if (t < tile_count) ranges[t].x = static_cast<decltype(ranges[t].x)>(i);
-        if (prev < tile_count) ranges[prev].y = static_cast<decltype(ranges[prev].y)>(i);
-    }
-    if (i == pair_count - 1 && t < tile_count) {
-        ranges[t].y = static_cast<decltype(ranges[t].y)>(pair_count);
+__global__ void __launch_bounds__(kRangeThreads) ranges_kernel(
+    uint32_t pair_count, uint32_t tile_count, const uint32_t* __restrict__ tile_ids,
+    Range* __restrict__ ranges) {
+    using Index = decltype(ranges[0].x);
+    const uint32_t quads = (pair_count + 3u) / 4u;
+    for (uint32_t q = blockIdx.x * kRangeThreads + threadIdx.x; q < quads;
+         q += gridDim.x * kRangeThreads) {
+        const uint32_t base = q * 4u;
+        uint32_t t[4];
+        if (base + 4u <= pair_count) {
+            const uint4 v = reinterpret_cast<const uint4*>(tile_ids)[q];
+            t[0] = v.x;
+            t[1] = v.y;
+            t[2] = v.z;
+            t[3] = v.w;
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) t[k] = base + k < pair_count ? tile_ids[base + k] : 0u;
+        }
+        uint32_t prev = base == 0u ? 0xffffffffu : tile_ids[base - 1u];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t i = base + k;
+            if (i >= pair_count) break;
+            if (t[k] != prev) {
+                if (t[k] < tile_count) ranges[t[k]].x = static_cast<Index>(i);
+                if (prev < tile_count) ranges[prev].y = static_cast<Index>(i);
+            }
+            if (i == pair_count - 1u && t[k] < tile_count) ranges[t[k]].y = static_cast<Index>(pair_count);
+            prev = t[k];
+        }
     }
 }
 
@@ -227,13 +256,17 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_kernel(
 // makes irrelevant (each tile appears once per Gaussian).
 // Emitter interface: Shape, load(gid), and
 //   __device__ uint32_t slots(const Shape&) const;             // rectangle size
-//   __device__ bool pair_at(const Shape&, uint32_t k, uint32_t& tile) const;
+//   __device__ bool pair_at(const Shape&, uint32_t k, uint32_t& tile,
+//                           uint32_t& tag) const;                // kept? tile, value bits
+// The value of a kept pair is the Gaussian index | tag. A Gaussian never
+// writes more than its counted pairs.
 template <class Emitter>
 __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
     uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
     Emitter em, uint32_t* __restrict__ tile_ids, uint32_t* __restrict__ values) {
     __shared__ typename Emitter::Shape shapes[kEmitThreads];
-    __shared__ uint32_t offsets[kEmitThreads], inclusive[kEmitThreads], cursor[kEmitThreads];
+    __shared__ uint32_t offsets[kEmitThreads], inclusive[kEmitThreads], cursor[kEmitThreads],
+        counted[kEmitThreads];
     const uint32_t gid = blockIdx.x * kEmitThreads + threadIdx.x;
     const int lane = threadIdx.x & 31;
     const uint32_t base = threadIdx.x & ~31u;
@@ -242,6 +275,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
     shapes[threadIdx.x] = mine;
     offsets[threadIdx.x] = cnt != 0u ? first_pair[gid] : 0u;
     cursor[threadIdx.x] = 0;
+    counted[threadIdx.x] = cnt;
     uint32_t incl = cnt != 0u ? em.slots(mine) : 0u;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
@@ -259,11 +293,13 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
         }
         const uint32_t owner = base + j;
         const uint32_t k = f - (j == 0 ? 0u : inclusive[owner - 1]);
-        uint32_t tile;
-        if (em.pair_at(shapes[owner], k, tile)) {
-            const uint32_t at = offsets[owner] + atomicAdd(&cursor[owner], 1u);
-            tile_ids[at] = tile;
-            values[at] = blockIdx.x * kEmitThreads + owner;
+        uint32_t tile, tag = 0;
+        if (em.pair_at(shapes[owner], k, tile, tag)) {
+            const uint32_t slot = atomicAdd(&cursor[owner], 1u);
+            if (slot < counted[owner]) {
+                tile_ids[offsets[owner] + slot] = tile;
+                values[offsets[owner] + slot] = (blockIdx.x * kEmitThreads + owner) | tag;
+            }
         }
     }
 }

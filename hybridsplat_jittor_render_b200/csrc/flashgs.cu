@@ -293,7 +293,7 @@ cudaError_t FlashgsPass::bin() {
                                   sort::bits_for_tiles(static_cast<uint32_t>(tiles_)),
                                   ctx_->fg_sort.ptr, stream, ctx_->device_error);
             if (st != cudaSuccess) return st;
-            bin::ranges_kernel<int2><<<(num_rendered_ + 255) / 256, 256, 0, stream>>>(
+            bin::ranges_kernel<int2><<<bin::ranges_grid(num_rendered_), bin::kRangeThreads, 0, stream>>>(
                 num_rendered_, static_cast<uint32_t>(tiles_), pv.tiles, ranges_);
             st = cudaGetLastError();
             if (st != cudaSuccess) return st;

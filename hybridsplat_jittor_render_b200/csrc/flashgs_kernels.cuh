@@ -187,7 +187,9 @@ struct Emitter {
         const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
         return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16));
     }
-    __device__ __forceinline__ bool pair_at(const Shape& s, uint32_t k, uint32_t& tile) const {
+    __device__ __forceinline__ bool pair_at(const Shape& s, uint32_t k, uint32_t& tile,
+                                            uint32_t& tag) const {
+        tag = 0u;
         const R r;
         const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
         const int x0 = lo & 0xffff, y0 = lo >> 16, w = static_cast<int>(hi & 0xffff) - x0;

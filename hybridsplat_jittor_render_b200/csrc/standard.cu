@@ -258,7 +258,7 @@ cudaError_t StandardPass::bin() {
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
         const Emitter em{gv_.cull, grid_x_, masked_};
-        bin::emit_flat_kernel<Emitter>
+        bin::emit_flat_compact_kernel<Emitter>
             <<<(c_.point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
                stream>>>(static_cast<uint32_t>(c_.point_count), gv_.counts, first_pair, em,
                          tile_ids, values_);
@@ -268,7 +268,7 @@ cudaError_t StandardPass::bin() {
                               sort::bits_for_tiles(static_cast<uint32_t>(tiles_)), scratch, stream,
                               ctx_->device_error);
         if (st != cudaSuccess) return st;
-        bin::ranges_kernel<uint2><<<(emitted + 255) / 256, 256, 0, stream>>>(
+        bin::ranges_kernel<uint2><<<bin::ranges_grid(emitted), bin::kRangeThreads, 0, stream>>>(
             emitted, static_cast<uint32_t>(tiles_), tile_ids, ranges_);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;

@@ -106,11 +106,18 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
                 y1 = min(static_cast<int>(min(g.rect_max.y, row_end)), by1 + 1);
                 if (x1 <= x0 || y1 <= y0) x0 = y0 = x1 = y1 = 0;
             }
-            emitted = static_cast<uint32_t>((x1 - x0) * (y1 - y0));
+            // pairs to emit: the live tiles of the clipped box, row by row
+            // (the emission makes the same per-tile decisions)
+            if (cs.mode == kCullNever) {
+                emitted = static_cast<uint32_t>((x1 - x0) * (y1 - y0));
+            } else {
+                for (int ty = y0; ty < y1; ++ty)
+                    emitted += static_cast<uint32_t>(live_tiles(tile_row_spans(cs, ty), x0, x1));
+            }
             float4* cu = out.cull + static_cast<size_t>(idx) * kCullQuads;
-            cu[0] = make_float4(cs.mx, cs.my, cs.cs, cs.sn);
-            cu[1] = make_float4(cs.ia, cs.ib, cs.ryx, cs.rxy);
-            cu[2] = make_float4(cs.gx, cs.gy, cs.r2, __int_as_float(cs.mode));
+            cu[0] = make_float4(cs.mx, cs.my, cs.k, cs.w0);
+            cu[1] = make_float4(cs.hx, cs.hy, cs.yr, cs.gx);
+            cu[2] = make_float4(cs.gy, cs.r2, __int_as_float(cs.mode), 0.0f);
             cu[3] = make_float4(__uint_as_float(static_cast<uint32_t>(x0) | (static_cast<uint32_t>(y0) << 16)),
                                 __uint_as_float(static_cast<uint32_t>(x1) | (static_cast<uint32_t>(y1) << 16)),
                                 0.0f, 0.0f);
@@ -124,8 +131,9 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     warp_add(out.totals + 2, emitted);
 }
 
-// Emits, for one Gaussian, every tile of its clipped rectangle with the mask
-// of the 8x8 quadrants that may hold a live pixel.
+// Emits, for one Gaussian, the live tiles of its clipped rectangle (those the
+// preprocess counted) with the mask of the 8x8 quadrants that may hold a live
+// pixel (emit_flat_compact_kernel interface).
 struct Emitter {
     const float4* cull;
     uint32_t grid_x;
@@ -140,65 +148,31 @@ struct Emitter {
         const float4 d = p[3];
         return Shape{p[0], p[1], p[2], make_float2(d.x, d.y)};
     }
-    __device__ __forceinline__ static float4 shfl4(float4 v, int src) {
-        return make_float4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
-                           __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
-    }
-    __device__ __forceinline__ Shape shfl(const Shape& s, int src) const {
-        return Shape{shfl4(s.a, src), shfl4(s.b, src), shfl4(s.c, src),
-                     make_float2(__shfl_sync(0xffffffffu, s.d.x, src),
-                                 __shfl_sync(0xffffffffu, s.d.y, src))};
-    }
     __device__ __forceinline__ static CullShape unpack(const Shape& s) {
         CullShape c;
-        c.mx = s.a.x; c.my = s.a.y; c.cs = s.a.z; c.sn = s.a.w;
-        c.ia = s.b.x; c.ib = s.b.y; c.ryx = s.b.z; c.rxy = s.b.w;
-        c.gx = s.c.x; c.gy = s.c.y; c.r2 = s.c.z; c.mode = __float_as_int(s.c.w);
+        c.mx = s.a.x; c.my = s.a.y; c.k = s.a.z; c.w0 = s.a.w;
+        c.hx = s.b.x; c.hy = s.b.y; c.yr = s.b.z; c.gx = s.b.w;
+        c.gy = s.c.x; c.r2 = s.c.y; c.mode = __float_as_int(s.c.z);
         return c;
     }
-    __device__ __forceinline__ void emit_one(const Shape& s, uint32_t gid, uint32_t offset,
-                                             uint32_t k, uint32_t* tiles, uint32_t* values) const {
+    __device__ __forceinline__ uint32_t slots(const Shape& s) const {
+        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
+        return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16));
+    }
+    __device__ __forceinline__ bool pair_at(const Shape& s, uint32_t k, uint32_t& tile,
+                                            uint32_t& tag) const {
         const CullShape c = unpack(s);
         const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
         const int x0 = lo & 0xffff, y0 = lo >> 16, w = static_cast<int>(hi & 0xffff) - x0;
         const int ty = y0 + static_cast<int>(k) / w, tx = x0 + static_cast<int>(k) % w;
-        tiles[offset + k] = static_cast<uint32_t>(ty) * grid_x + static_cast<uint32_t>(tx);
-        values[offset + k] = masked ? (gid | (cull_quadrants(c, tx, ty) << kIndexBits)) : gid;
-    }
-    __device__ __forceinline__ bool small(const Shape& s) const {
-        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
-        return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16)) <= 8u;
-    }
-    __device__ __forceinline__ void emit_serial(const Shape& s, uint32_t gid, uint32_t offset,
-                                                uint32_t count, uint32_t* tiles,
-                                                uint32_t* values) const {
-        const CullShape c = unpack(s);
-        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
-        const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff, y1 = hi >> 16;
-        uint32_t at = offset;
-        for (int ty = y0; ty < y1; ++ty) {
-            for (int tx = x0; tx < x1; ++tx, ++at) {
-                tiles[at] = static_cast<uint32_t>(ty) * grid_x + static_cast<uint32_t>(tx);
-                values[at] = masked ? (gid | (cull_quadrants(c, tx, ty) << kIndexBits)) : gid;
-            }
+        tile = static_cast<uint32_t>(ty) * grid_x + static_cast<uint32_t>(tx);
+        if (c.mode == kCullNever) {
+            tag = masked ? (0xfu << kIndexBits) : 0u;
+            return true;
         }
-        (void)count;
-    }
-    __device__ __forceinline__ void emit(const Shape& s, uint32_t gid, uint32_t offset,
-                                         uint32_t count, int lane, uint32_t* tiles,
-                                         uint32_t* values) const {
-        CullShape c;
-        c.mx = s.a.x; c.my = s.a.y; c.cs = s.a.z; c.sn = s.a.w;
-        c.ia = s.b.x; c.ib = s.b.y; c.ryx = s.b.z; c.rxy = s.b.w;
-        c.gx = s.c.x; c.gy = s.c.y; c.r2 = s.c.z; c.mode = __float_as_int(s.c.w);
-        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
-        const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff;
-        const int w = x1 - x0;
-        for (uint32_t t = lane; t < count; t += 32) {
-            const int ty = y0 + static_cast<int>(t) / w, tx = x0 + static_cast<int>(t) % w;
-            tiles[offset + t] = static_cast<uint32_t>(ty) * grid_x + static_cast<uint32_t>(tx);
-            values[offset + t] = masked ? (gid | (cull_quadrants(c, tx, ty) << kIndexBits)) : gid;
-        }
+        if (!tile_live(tile_row_spans(c, ty), tx)) return false;
+        tag = masked ? (quadrant_mask(c, tx, ty) << kIndexBits) : 0u;
+        return true;
     }
 };
 

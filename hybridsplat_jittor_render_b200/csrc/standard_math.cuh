@@ -219,28 +219,32 @@ __device__ __forceinline__ float blend(const R& r, PixelState& s, float px, floa
 // evaluations that would have returned early.
 enum CullMode : int { kCullEllipse = 0, kCullNever = 1, kCullAlways = 2 };
 
-// The ellipse is stored in its axis frame: with X, Y relative to the centre,
-// (u, v) = (cs X + sn Y, cs Y - sn X) and u^2 ia + v^2 ib <= 1. Evaluating
-// squares in the axis frame keeps thin (edge-on) ellipses well conditioned in
-// single precision: rounding moves the boundary by about 1e-7 of the
-// distance to the centre, far below the one-pixel widening of the tested
-// rectangles. ryx and rxy locate the minimum of the form along a vertical or
-// horizontal edge (Y = ryx X, X = rxy Y).
+// The ellipse is stored by its horizontal chords: with Y the height above
+// the centre, the chord at Y is centred at mx + k Y and has half-width
+// w0 sqrt(1 - (Y / hy)^2) for |Y| <= hy; its extreme points are x = mx +- hx
+// at heights +-yr. These parameters are computed in double from the dual
+// conic and scaled together by 1.0003 about the centre (a uniform widening
+// that dwarfs their float rounding). The x-extent of the ellipse over a band
+// of rows then costs two square roots (the chord ends at the band's edges, or
+// the extreme point when its height is inside the band), so each band of a
+// Gaussian is reduced to two x-intervals (ellipse, disc) and a tile or
+// quadrant is live when its widened x-range meets one of them. Every step is
+// an explicitly rounded operation, so the preprocess (which counts the live
+// tiles) and the emission (which writes them) take identical decisions.
 struct CullShape {
     float mx, my;     // ellipse centre (pixels)
-    float cs, sn;     // major-axis direction
-    float ia, ib;     // inverse squared semi-axes
-    float ryx, rxy;   // edge minimisers
+    float k;          // chord-centre slope
+    float w0;         // chord half-width at the centre height
+    float hx, hy;     // half extents of the ellipse's bounding box
+    float yr;         // height of the rightmost point (the leftmost is at -yr)
     float gx, gy, r2; // disc centre and squared radius
     int mode;         // kCullEllipse: test; kCullNever: every pixel may be live; kCullAlways: none
-    float hx, hy;     // half extents of the ellipse's bounding box
 };
 
 __device__ __forceinline__ CullShape cull_shape(float op, float x, float y, float3 tu, float3 tv,
                                                 float3 tw) {
     CullShape c;
-    c.mx = c.my = c.sn = c.ia = c.ib = c.ryx = c.rxy = c.hx = c.hy = 0.0f;
-    c.cs = 1.0f;
+    c.mx = c.my = c.k = c.w0 = c.hx = c.hy = c.yr = 0.0f;
     c.gx = x;
     c.gy = y;
     c.r2 = 0.0f;
@@ -263,68 +267,132 @@ __device__ __forceinline__ CullShape cull_shape(float op, float x, float y, floa
     const double quu = fxy * (double(tu.x) * tu.x + double(tu.y) * tu.y) + fz * double(tu.z) * tu.z;
     const double qvv = fxy * (double(tv.x) * tv.x + double(tv.y) * tv.y) + fz * double(tv.z) * tv.z;
     const double quv = fxy * (double(tu.x) * tv.x + double(tu.y) * tv.y) + fz * double(tu.z) * tv.z;
+    // (p - m)^T S^-1 (p - m) <= 1 with S = [[sxx, sxy], [sxy, syy]]
     const double sxx = mx * mx - quu, syy = my * my - qvv, sxy = mx * my - quv;
     const double det = sxx * syy - sxy * sxy;
     if (!(sxx > 0.0 && syy > 0.0 && det > 0.0) || !(fabs(mx) < 1e7 && fabs(my) < 1e7)) return c;
-    // Eigen-decomposition of [[sxx, sxy], [sxy, syy]] without trigonometry:
-    // r = la - lb, (cos 2t, sin 2t) = (sxx - syy, 2 sxy) / r, and the
-    // half-angle formulas taken on the side that avoids cancellation.
-    const double dxy = sxx - syy;
-    const double r = sqrt(dxy * dxy + 4.0 * sxy * sxy);
-    const double la = 0.5 * (sxx + syy + r);
-    const double lb = det / la;
-    double cs = 1.0, sn = 0.0;
-    if (r > 0.0) {
-        if (dxy >= 0.0) {
-            cs = sqrt(0.5 * (1.0 + dxy / r));
-            sn = sxy / (r * cs);
-        } else {
-            sn = sqrt(0.5 * (1.0 - dxy / r));
-            if (sxy < 0.0) sn = -sn;
-            cs = sxy / (r * sn);
-        }
-    }
-    // widen the axes slightly to absorb the rounding of the stored direction
-    const double ia = 1.0 / (la * 1.0002), ib = 1.0 / (lb * 1.0002 + 1e-8 * la);
-    const double axx = cs * cs * ia + sn * sn * ib, ayy = sn * sn * ia + cs * cs * ib;
-    const double axy = cs * sn * (ia - ib);
+    constexpr double kWiden = 1.0003;
     c.mx = static_cast<float>(mx);
     c.my = static_cast<float>(my);
-    c.cs = static_cast<float>(cs);
-    c.sn = static_cast<float>(sn);
-    c.ia = static_cast<float>(ia);
-    c.ib = static_cast<float>(ib);
-    c.ryx = static_cast<float>(-axy / ayy);
-    c.rxy = static_cast<float>(-axy / axx);
-    c.hx = static_cast<float>(sqrt(sxx) * 1.0003);
-    c.hy = static_cast<float>(sqrt(syy) * 1.0003);
+    c.k = static_cast<float>(sxy / syy);
+    c.w0 = static_cast<float>(sqrt(det / syy) * kWiden);
+    c.hx = static_cast<float>(sqrt(sxx) * kWiden);
+    c.hy = static_cast<float>(sqrt(syy) * kWiden);
+    c.yr = static_cast<float>(sxy / sqrt(sxx) * kWiden);
     c.mode = kCullEllipse;
     return c;
 }
 
-__device__ __forceinline__ float cull_form(const CullShape& c, float X, float Y) {
-    const float u = c.cs * X + c.sn * Y, v = c.cs * Y - c.sn * X;
-    return u * u * c.ia + v * v * c.ib;
+// x-interval [l, r] (pixels) of the ellipse within rows [ya, yb]; empty
+// (l > r) when the band misses it.
+__device__ __forceinline__ void ellipse_span(const CullShape& c, float ya, float yb, float& l,
+                                             float& r) {
+    const float y0 = fmaxf(sub(ya, c.my), -c.hy), y1 = fminf(sub(yb, c.my), c.hy);
+    if (!(y0 <= y1)) {
+        l = 1.0f;
+        r = 0.0f;
+        return;
+    }
+    const float t0 = div(y0, c.hy), t1 = div(y1, c.hy);  // in [-1, 1]
+    const float h0 = mul(c.w0, __fsqrt_rn(mul(sub(1.0f, t0), add(1.0f, t0))));
+    const float h1 = mul(c.w0, __fsqrt_rn(mul(sub(1.0f, t1), add(1.0f, t1))));
+    const float c0 = mul(c.k, y0), c1 = mul(c.k, y1);
+    float xl = fminf(sub(c0, h0), sub(c1, h1));
+    float xr = fmaxf(add(c0, h0), add(c1, h1));
+    if (y0 <= -c.yr && -c.yr <= y1) xl = fminf(xl, -c.hx);
+    if (y0 <= c.yr && c.yr <= y1) xr = fmaxf(xr, c.hx);
+    l = add(c.mx, xl);
+    r = add(c.mx, xr);
 }
 
-// Can any pixel of [x0, x1] x [y0, y1] (already widened) be live? Written
-// without early exits so that the lanes of a warp, each testing a different
-// Gaussian, stay converged.
-__device__ __forceinline__ bool cull_rect_live(const CullShape& c, float x0, float y0, float x1,
-                                               float y1) {
-    const float cx = fminf(fmaxf(c.gx, x0), x1), cy = fminf(fmaxf(c.gy, y0), y1);
-    const float ddx = cx - c.gx, ddy = cy - c.gy;
-    const bool disc = ddx * ddx + ddy * ddy <= c.r2;
-    const float X0 = x0 - c.mx, X1 = x1 - c.mx, Y0 = y0 - c.my, Y1 = y1 - c.my;
-    const bool centre = X0 <= 0.0f && X1 >= 0.0f && Y0 <= 0.0f && Y1 >= 0.0f;
-    // Minimum of the form along each edge of the rectangle.
-    const float fa = cull_form(c, X0, fminf(fmaxf(c.ryx * X0, Y0), Y1));
-    const float fb = cull_form(c, X1, fminf(fmaxf(c.ryx * X1, Y0), Y1));
-    const float fc = cull_form(c, fminf(fmaxf(c.rxy * Y0, X0), X1), Y0);
-    const float fd = cull_form(c, fminf(fmaxf(c.rxy * Y1, X0), X1), Y1);
-    const bool edge = fminf(fminf(fa, fb), fminf(fc, fd)) <= 1.0f;
-    const bool tested = disc || centre || edge;
-    return c.mode == kCullNever || (c.mode == kCullEllipse && tested);
+// x-interval of the disc within rows [ya, yb].
+__device__ __forceinline__ void disc_span(const CullShape& c, float ya, float yb, float& l,
+                                          float& r) {
+    const float dy = fmaxf(fmaxf(sub(ya, c.gy), sub(c.gy, yb)), 0.0f);
+    const float q = sub(c.r2, mul(dy, dy));
+    if (!(q >= 0.0f)) {
+        l = 1.0f;
+        r = 0.0f;
+        return;
+    }
+    const float w = __fsqrt_rn(q);
+    l = sub(c.gx, w);
+    r = add(c.gx, w);
+}
+
+// Does [x0, x1] meet [l, r]? (False for an empty or NaN interval.)
+__device__ __forceinline__ bool meets(float l, float r, float x0, float x1) {
+    return x0 <= r && x1 >= l && l <= r;
+}
+
+// Culling intervals of one band of rows: ellipse and disc.
+struct BandSpans {
+    float el, er, dl, dr;
+};
+
+__device__ __forceinline__ BandSpans band_spans(const CullShape& c, float ya, float yb) {
+    BandSpans s;
+    ellipse_span(c, ya, yb, s.el, s.er);
+    disc_span(c, ya, yb, s.dl, s.dr);
+    return s;
+}
+
+// Tile row ty, widened by one pixel: rows [16 ty - 1, 16 ty + 16]; tile tx
+// of it is live when [16 tx - 1, 16 tx + 16] meets one of the spans.
+__device__ __forceinline__ BandSpans tile_row_spans(const CullShape& c, int ty) {
+    return band_spans(c, static_cast<float>(ty * 16 - 1), static_cast<float>(ty * 16 + 16));
+}
+
+__device__ __forceinline__ bool tile_live(const BandSpans& s, int tx) {
+    const float x0 = static_cast<float>(tx * 16 - 1), x1 = static_cast<float>(tx * 16 + 16);
+    return meets(s.el, s.er, x0, x1) || meets(s.dl, s.dr, x0, x1);
+}
+
+// Tile columns [lo, hi] whose widened range meets [l, r]: the first column
+// with 16 lo + 16 >= l and the last with 16 hi - 1 <= r, found from the
+// quotients and corrected with the same comparisons tile_live makes.
+__device__ __forceinline__ void span_columns(float l, float r, int& lo, int& hi) {
+    const float lc = fminf(fmaxf(l, -4.0e6f), 4.0e6f), rc = fminf(fmaxf(r, -4.0e6f), 4.0e6f);
+    lo = static_cast<int>(ceilf(mul(sub(lc, 16.0f), 0.0625f)));
+    hi = static_cast<int>(floorf(mul(add(rc, 1.0f), 0.0625f)));
+    if (!(static_cast<float>(lo * 16 + 16) >= l)) ++lo;
+    if (static_cast<float>((lo - 1) * 16 + 16) >= l) --lo;
+    if (!(static_cast<float>(hi * 16 - 1) <= r)) --hi;
+    if (static_cast<float>((hi + 1) * 16 - 1) <= r) ++hi;
+}
+
+// Number of tiles tx in [x0, x1) with tile_live(s, tx).
+__device__ __forceinline__ int live_tiles(const BandSpans& s, int x0, int x1) {
+    int elo = 1, ehi = 0, dlo = 1, dhi = 0;
+    if (s.el <= s.er) span_columns(s.el, s.er, elo, ehi);
+    if (s.dl <= s.dr) span_columns(s.dl, s.dr, dlo, dhi);
+    elo = max(elo, x0);
+    ehi = min(ehi, x1 - 1);
+    dlo = max(dlo, x0);
+    dhi = min(dhi, x1 - 1);
+    const int ne = max(ehi - elo + 1, 0), nd = max(dhi - dlo + 1, 0);
+    const int both = max(min(ehi, dhi) - max(elo, dlo) + 1, 0);
+    return ne + nd - (ne > 0 && nd > 0 ? both : 0);
+}
+
+// 4-bit mask of the 8x8 quadrants of live tile (tx, ty) that may hold a live
+// pixel; bit (qy * 2 + qx). Quadrants are widened by one pixel like tiles.
+// Never empty for a live tile: a rounding disagreement between the tile and
+// quadrant tests falls back to all four quadrants.
+__device__ __forceinline__ uint32_t quadrant_mask(const CullShape& c, int tx, int ty) {
+    uint32_t mask = 0;
+#pragma unroll
+    for (int qy = 0; qy < 2; ++qy) {
+        const float ya = static_cast<float>(ty * 16 + qy * 8 - 1);
+        const BandSpans s = band_spans(c, ya, ya + 9.0f);
+#pragma unroll
+        for (int qx = 0; qx < 2; ++qx) {
+            const float x0 = static_cast<float>(tx * 16 + qx * 8 - 1);
+            if (meets(s.el, s.er, x0, x0 + 9.0f) || meets(s.dl, s.dr, x0, x0 + 9.0f))
+                mask |= 1u << (qy * 2 + qx);
+        }
+    }
+    return mask != 0u ? mask : 0xfu;
 }
 
 // Tiles (16 px) that may hold a live pixel: the bounding box of the ellipse
@@ -346,19 +414,6 @@ __device__ __forceinline__ bool cull_tile_box(const CullShape& c, int& tx0, int&
     tx1 = static_cast<int>(floorf(fminf(bx1, 1e6f) * (1.0f / 16.0f)));
     ty1 = static_cast<int>(floorf(fminf(by1, 1e6f) * (1.0f / 16.0f)));
     return true;
-}
-
-// 4-bit mask of the 8x8 quadrants of tile (tx, ty) that may hold a live
-// pixel; bit (qy * 2 + qx).
-__device__ __forceinline__ uint32_t cull_quadrants(const CullShape& c, int tx, int ty) {
-    uint32_t mask = 0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const float x0 = static_cast<float>(tx * 16 + (q & 1) * 8) - 1.0f;
-        const float y0 = static_cast<float>(ty * 16 + (q >> 1) * 8) - 1.0f;
-        if (cull_rect_live(c, x0, y0, x0 + 9.0f, y0 + 9.0f)) mask |= 1u << q;
-    }
-    return mask;
 }
 
 }  // namespace st

@@ -190,7 +190,7 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
         st = cudaGetLastError();
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
         const Emitter em{l.cull, grid_x, true};
-        bin::emit_flat_kernel<Emitter>
+        bin::emit_flat_compact_kernel<Emitter>
             <<<(point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
                stream>>>(static_cast<uint32_t>(point_count), l.counts, first_pair, em, l.tile_ids,
                          l.values);
@@ -200,7 +200,7 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
                               sort::bits_for_tiles(static_cast<uint32_t>(tiles)), l.pair_scratch,
                               stream, l.error);
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
-        bin::ranges_kernel<uint2><<<(emitted + 255) / 256, 256, 0, stream>>>(
+        bin::ranges_kernel<uint2><<<bin::ranges_grid(emitted), bin::kRangeThreads, 0, stream>>>(
             emitted, static_cast<uint32_t>(tiles), l.tile_ids, l.ranges);
         st = cudaGetLastError();
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
