@@ -3,8 +3,9 @@
 // After the depth sort, `order` lists the Gaussians by (depth bits, index).
 // offsets_kernel scans the per-Gaussian pair counts in that order (a
 // single-pass exclusive scan with decoupled look-back across blocks) and
-// stores each Gaussian's first pair slot by Gaussian index. emit_kernel then
-// writes the pairs, walking the Gaussians in index order so that the large
+// stores each Gaussian's first pair slot by Gaussian index.
+// emit_flat_compact_kernel then writes the pairs, walking the Gaussians in
+// index order so that the large
 // screen-space footprints of the nearest Gaussians (adjacent in depth order)
 // spread over all blocks. Pairs of one Gaussian may be written in any order
 // among themselves: each names a different tile, and the following stable
@@ -122,42 +123,6 @@ static __global__ void __launch_bounds__(kScanThreads) offsets_kernel(
     }
 }
 
-// Emitter interface:
-//   struct E {
-//     struct Shape {...};                                   // per-Gaussian emission data
-//     __device__ Shape load(uint32_t gid) const;            // read by the owning lane
-//     __device__ bool small(const Shape&) const;            // emit on the owning lane alone?
-//     __device__ void emit_serial(const Shape&, uint32_t gid, uint32_t offset, uint32_t count,
-//                                 uint32_t* tiles, uint32_t* values) const;  // one lane
-//     __device__ Shape shfl(const Shape&, int src) const;   // broadcast from lane src
-//     __device__ void emit(const Shape&, uint32_t gid, uint32_t offset, uint32_t count,
-//                          int lane, uint32_t* tiles, uint32_t* values) const;  // all 32 lanes
-//   };
-// Gaussians with small tile rectangles are emitted by their own lane, the
-// others by the whole warp, one Gaussian at a time.
-template <class Emitter>
-__global__ void __launch_bounds__(kEmitThreads) emit_kernel(
-    uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
-    Emitter em, uint32_t* __restrict__ tile_ids, uint32_t* __restrict__ values) {
-    const uint32_t gid = blockIdx.x * kEmitThreads + threadIdx.x;
-    const int lane = threadIdx.x & 31;
-    const uint32_t cnt = gid < count ? counts[gid] : 0u;
-    const uint32_t off = cnt != 0u ? first_pair[gid] : 0u;
-    const typename Emitter::Shape mine = em.load(cnt != 0u ? gid : 0u);
-    const bool serial = cnt != 0u && em.small(mine);
-    if (serial) em.emit_serial(mine, gid, off, cnt, tile_ids, values);
-    uint32_t pending = __ballot_sync(0xffffffffu, cnt != 0u && !serial);
-    while (pending != 0u) {
-        const int src = __ffs(pending) - 1;
-        pending &= pending - 1u;
-        const typename Emitter::Shape s = em.shfl(mine, src);
-        const uint32_t g = __shfl_sync(0xffffffffu, gid, src);
-        const uint32_t o = __shfl_sync(0xffffffffu, off, src);
-        const uint32_t c = __shfl_sync(0xffffffffu, cnt, src);
-        em.emit(s, g, o, c, lane, tile_ids, values);
-    }
-}
-
 // Per-tile [start, end) of the sorted pair list. Entries of tiles without
 // pairs keep the zeros written before the launch. Tile ids >= tile_count are
 // padding and are ignored. Each thread reads four consecutive tile ids with
@@ -206,48 +171,6 @@ __global__ void __launch_bounds__(kRangeThreads) ranges_kernel(
     }
 }
 
-// Emission for emitters whose k-th pair of a Gaussian is a fixed function of
-// k (every tile of a rectangle): the pairs of a warp's 32 Gaussians are
-// numbered 0..total-1 and dealt to the lanes round-robin, so every lane does
-// the same amount of work whatever the rectangle sizes. A lane finds the
-// Gaussian of pair f by binary search over the warp's inclusive pair counts.
-// Emitter interface: Shape, load(gid), and
-//   __device__ void emit_one(const Shape&, uint32_t gid, uint32_t offset, uint32_t k,
-//                            uint32_t* tiles, uint32_t* values) const;
-template <class Emitter>
-__global__ void __launch_bounds__(kEmitThreads) emit_flat_kernel(
-    uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
-    Emitter em, uint32_t* __restrict__ tile_ids, uint32_t* __restrict__ values) {
-    __shared__ typename Emitter::Shape shapes[kEmitThreads];
-    __shared__ uint32_t gids[kEmitThreads], offsets[kEmitThreads], inclusive[kEmitThreads];
-    const uint32_t gid = blockIdx.x * kEmitThreads + threadIdx.x;
-    const int lane = threadIdx.x & 31;
-    const uint32_t base = threadIdx.x & ~31u;
-    const uint32_t cnt = gid < count ? counts[gid] : 0u;
-    shapes[threadIdx.x] = em.load(cnt != 0u ? gid : 0u);
-    gids[threadIdx.x] = gid;
-    offsets[threadIdx.x] = cnt != 0u ? first_pair[gid] : 0u;
-    uint32_t incl = cnt;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += t;
-    }
-    inclusive[threadIdx.x] = incl;
-    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-    __syncwarp();
-    for (uint32_t f = lane; f < total; f += 32) {
-        uint32_t j = 0;
-#pragma unroll
-        for (uint32_t step = 16; step >= 1; step >>= 1) {
-            if (inclusive[base + j + step - 1] <= f) j += step;
-        }
-        const uint32_t owner = base + j;
-        const uint32_t k = f - (j == 0 ? 0u : inclusive[owner - 1]);
-        em.emit_one(shapes[owner], gids[owner], offsets[owner], k, tile_ids, values);
-    }
-}
-
 // Flattened emission for emitters that keep a subset of a rectangle (the
 // FlashGS tile/ellipse test): the rectangle tiles of a warp's 32 Gaussians
 // are dealt to the lanes round-robin, and a kept tile takes the next slot of
@@ -256,8 +179,11 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_kernel(
 // makes irrelevant (each tile appears once per Gaussian).
 // Emitter interface: Shape, load(gid), and
 //   __device__ uint32_t slots(const Shape&) const;             // rectangle size
-//   __device__ bool pair_at(const Shape&, uint32_t k, uint32_t& tile,
-//                           uint32_t& tag) const;                // kept? tile, value bits
+//   struct Cache;                                               // per-lane scratch, value-initialised
+//   __device__ bool pair_at(const Shape&, uint32_t owner, uint32_t k, uint32_t& tile,
+//                           uint32_t& tag, Cache&) const;        // kept? tile, value bits
+// `owner` names the Gaussian within the block, so an emitter may keep work
+// shared by consecutive pairs of one Gaussian in its Cache.
 // The value of a kept pair is the Gaussian index | tag. A Gaussian never
 // writes more than its counted pairs.
 template <class Emitter>
@@ -285,6 +211,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
     inclusive[threadIdx.x] = incl;
     const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
     __syncwarp();
+    typename Emitter::Cache cache{};
     for (uint32_t f = lane; f < total; f += 32) {
         uint32_t j = 0;
 #pragma unroll
@@ -294,7 +221,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
         const uint32_t owner = base + j;
         const uint32_t k = f - (j == 0 ? 0u : inclusive[owner - 1]);
         uint32_t tile, tag = 0;
-        if (em.pair_at(shapes[owner], k, tile, tag)) {
+        if (em.pair_at(shapes[owner], owner, k, tile, tag, cache)) {
             const uint32_t slot = atomicAdd(&cursor[owner], 1u);
             if (slot < counted[owner]) {
                 tile_ids[offsets[owner] + slot] = tile;

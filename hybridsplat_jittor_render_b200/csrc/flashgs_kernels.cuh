@@ -171,24 +171,13 @@ struct Emitter {
         const float4* q = emit_records + static_cast<size_t>(gid) * kEmitQuads;
         return Shape{q[0], q[1]};
     }
-    __device__ __forceinline__ static float4 shfl4(float4 v, int src) {
-        return make_float4(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src),
-                           __shfl_sync(0xffffffffu, v.z, src), __shfl_sync(0xffffffffu, v.w, src));
-    }
-    __device__ __forceinline__ Shape shfl(const Shape& s, int src) const {
-        return Shape{shfl4(s.a, src), shfl4(s.b, src)};
-    }
-    __device__ __forceinline__ bool small(const Shape& s) const {
-        const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
-        return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16)) <=
-               static_cast<uint32_t>(2 * kSerialTiles);
-    }
     __device__ __forceinline__ uint32_t slots(const Shape& s) const {
         const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
         return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16));
     }
-    __device__ __forceinline__ bool pair_at(const Shape& s, uint32_t k, uint32_t& tile,
-                                            uint32_t& tag) const {
+    struct Cache {};
+    __device__ __forceinline__ bool pair_at(const Shape& s, uint32_t, uint32_t k, uint32_t& tile,
+                                            uint32_t& tag, Cache&) const {
         tag = 0u;
         const R r;
         const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
@@ -196,52 +185,6 @@ struct Emitter {
         const int tx = x0 + static_cast<int>(k) % w, ty = y0 + static_cast<int>(k) / w;
         tile = static_cast<uint32_t>(ty * grid_x + tx);
         return tile_hit(r, tx, ty, make_float2(s.a.x, s.a.y), make_float3(s.a.z, s.a.w, s.b.x), s.b.y);
-    }
-    __device__ __forceinline__ void emit_serial(const Shape& s, uint32_t gid, uint32_t offset,
-                                                uint32_t count, uint32_t* tiles,
-                                                uint32_t* values) const {
-        const R r;
-        const float2 xy = make_float2(s.a.x, s.a.y);
-        const float3 conic = make_float3(s.a.z, s.a.w, s.b.x);
-        const float power = s.b.y;
-        const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
-        const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff, y1 = hi >> 16;
-        uint32_t at = offset;
-        const uint32_t end = offset + count;
-        for (int ty = y0; ty < y1 && at < end; ++ty) {
-            for (int tx = x0; tx < x1 && at < end; ++tx) {
-                if (tile_hit(r, tx, ty, xy, conic, power)) {
-                    tiles[at] = static_cast<uint32_t>(ty * grid_x + tx);
-                    values[at] = gid;
-                    ++at;
-                }
-            }
-        }
-    }
-    __device__ __forceinline__ void emit(const Shape& s, uint32_t gid, uint32_t offset,
-                                         uint32_t count, int lane, uint32_t* tiles,
-                                         uint32_t* values) const {
-        const R r;
-        const float2 xy = make_float2(s.a.x, s.a.y);
-        const float3 conic = make_float3(s.a.z, s.a.w, s.b.x);
-        const float power = s.b.y;
-        const uint32_t lo = __float_as_uint(s.b.z), hi = __float_as_uint(s.b.w);
-        const int x0 = lo & 0xffff, y0 = lo >> 16, x1 = hi & 0xffff, y1 = hi >> 16;
-        const int w = x1 - x0, n = w * (y1 - y0);
-        const uint32_t lt = (1u << lane) - 1u;
-        uint32_t written = 0;
-        for (int base = 0; base < n && written < count; base += 32) {
-            const int t = base + lane;
-            const int tx = x0 + t % w, ty = y0 + t / w;
-            const bool hit = t < n && tile_hit(r, tx, ty, xy, conic, power);
-            const uint32_t m = __ballot_sync(0xffffffffu, hit);
-            if (hit) {
-                const uint32_t at = offset + written + __popc(m & lt);
-                tiles[at] = static_cast<uint32_t>(ty * grid_x + tx);
-                values[at] = gid;
-            }
-            written += __popc(m);
-        }
     }
 };
 

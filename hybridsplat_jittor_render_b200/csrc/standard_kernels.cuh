@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
             float4* cu = out.cull + static_cast<size_t>(idx) * kCullQuads;
             cu[0] = make_float4(cs.mx, cs.my, cs.k, cs.w0);
             cu[1] = make_float4(cs.hx, cs.hy, cs.yr, cs.gx);
-            cu[2] = make_float4(cs.gy, cs.r2, __int_as_float(cs.mode), 0.0f);
+            cu[2] = make_float4(cs.gy, cs.r2, __int_as_float(cs.mode), cs.ihy);
             cu[3] = make_float4(__uint_as_float(static_cast<uint32_t>(x0) | (static_cast<uint32_t>(y0) << 16)),
                                 __uint_as_float(static_cast<uint32_t>(x1) | (static_cast<uint32_t>(y1) << 16)),
                                 0.0f, 0.0f);
@@ -152,26 +152,40 @@ struct Emitter {
         CullShape c;
         c.mx = s.a.x; c.my = s.a.y; c.k = s.a.z; c.w0 = s.a.w;
         c.hx = s.b.x; c.hy = s.b.y; c.yr = s.b.z; c.gx = s.b.w;
-        c.gy = s.c.x; c.r2 = s.c.y; c.mode = __float_as_int(s.c.z);
+        c.gy = s.c.x; c.r2 = s.c.y; c.mode = __float_as_int(s.c.z); c.ihy = s.c.w;
         return c;
     }
     __device__ __forceinline__ uint32_t slots(const Shape& s) const {
         const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
         return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16));
     }
-    __device__ __forceinline__ bool pair_at(const Shape& s, uint32_t k, uint32_t& tile,
-                                            uint32_t& tag) const {
-        const CullShape c = unpack(s);
+    // Spans of the tile row the lane last worked on (consecutive pairs of a
+    // wide Gaussian share their row).
+    struct Cache {
+        uint32_t owner = 0xffffffffu;
+        int ty = 0;
+        BandSpans row, top, bottom;
+    };
+    __device__ __forceinline__ bool pair_at(const Shape& s, uint32_t owner, uint32_t k,
+                                            uint32_t& tile, uint32_t& tag, Cache& cache) const {
         const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
         const int x0 = lo & 0xffff, y0 = lo >> 16, w = static_cast<int>(hi & 0xffff) - x0;
         const int ty = y0 + static_cast<int>(k) / w, tx = x0 + static_cast<int>(k) % w;
         tile = static_cast<uint32_t>(ty) * grid_x + static_cast<uint32_t>(tx);
-        if (c.mode == kCullNever) {
+        if (__float_as_int(s.c.z) == kCullNever) {
             tag = masked ? (0xfu << kIndexBits) : 0u;
             return true;
         }
-        if (!tile_live(tile_row_spans(c, ty), tx)) return false;
-        tag = masked ? (quadrant_mask(c, tx, ty) << kIndexBits) : 0u;
+        if (cache.owner != owner || cache.ty != ty) {
+            const CullShape c = unpack(s);
+            cache.top = quadrant_band_spans(c, ty, 0);
+            cache.bottom = quadrant_band_spans(c, ty, 1);
+            cache.row = row_spans(cache.top, cache.bottom);
+            cache.owner = owner;
+            cache.ty = ty;
+        }
+        if (!tile_live(cache.row, tx)) return false;
+        tag = masked ? (quadrant_mask(cache.top, cache.bottom, tx) << kIndexBits) : 0u;
         return true;
     }
 };

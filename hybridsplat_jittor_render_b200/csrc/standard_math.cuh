@@ -228,15 +228,18 @@ enum CullMode : int { kCullEllipse = 0, kCullNever = 1, kCullAlways = 2 };
 // of rows then costs two square roots (the chord ends at the band's edges, or
 // the extreme point when its height is inside the band), so each band of a
 // Gaussian is reduced to two x-intervals (ellipse, disc) and a tile or
-// quadrant is live when its widened x-range meets one of them. Every step is
-// an explicitly rounded operation, so the preprocess (which counts the live
-// tiles) and the emission (which writes them) take identical decisions.
+// quadrant is live when its widened x-range meets one of them. The square
+// roots are the approximate hardware ones (relative error ~1e-7, far inside
+// the widening); every other step is an explicitly rounded operation, so the
+// preprocess (which counts the live tiles) and the emission (which writes
+// them) compute the same bits and take identical decisions.
 struct CullShape {
     float mx, my;     // ellipse centre (pixels)
     float k;          // chord-centre slope
     float w0;         // chord half-width at the centre height
     float hx, hy;     // half extents of the ellipse's bounding box
     float yr;         // height of the rightmost point (the leftmost is at -yr)
+    float ihy;        // 1 / hy
     float gx, gy, r2; // disc centre and squared radius
     int mode;         // kCullEllipse: test; kCullNever: every pixel may be live; kCullAlways: none
 };
@@ -244,7 +247,7 @@ struct CullShape {
 __device__ __forceinline__ CullShape cull_shape(float op, float x, float y, float3 tu, float3 tv,
                                                 float3 tw) {
     CullShape c;
-    c.mx = c.my = c.k = c.w0 = c.hx = c.hy = c.yr = 0.0f;
+    c.mx = c.my = c.k = c.w0 = c.hx = c.hy = c.yr = c.ihy = 0.0f;
     c.gx = x;
     c.gy = y;
     c.r2 = 0.0f;
@@ -279,6 +282,7 @@ __device__ __forceinline__ CullShape cull_shape(float op, float x, float y, floa
     c.hx = static_cast<float>(sqrt(sxx) * kWiden);
     c.hy = static_cast<float>(sqrt(syy) * kWiden);
     c.yr = static_cast<float>(sxy / sqrt(sxx) * kWiden);
+    c.ihy = static_cast<float>(1.0 / (sqrt(syy) * kWiden));
     c.mode = kCullEllipse;
     return c;
 }
@@ -293,9 +297,10 @@ __device__ __forceinline__ void ellipse_span(const CullShape& c, float ya, float
         r = 0.0f;
         return;
     }
-    const float t0 = div(y0, c.hy), t1 = div(y1, c.hy);  // in [-1, 1]
-    const float h0 = mul(c.w0, __fsqrt_rn(mul(sub(1.0f, t0), add(1.0f, t0))));
-    const float h1 = mul(c.w0, __fsqrt_rn(mul(sub(1.0f, t1), add(1.0f, t1))));
+    const float t0 = fminf(fmaxf(mul(y0, c.ihy), -1.0f), 1.0f);
+    const float t1 = fminf(fmaxf(mul(y1, c.ihy), -1.0f), 1.0f);
+    const float h0 = mul(c.w0, approx_sqrt(mul(sub(1.0f, t0), add(1.0f, t0))));
+    const float h1 = mul(c.w0, approx_sqrt(mul(sub(1.0f, t1), add(1.0f, t1))));
     const float c0 = mul(c.k, y0), c1 = mul(c.k, y1);
     float xl = fminf(sub(c0, h0), sub(c1, h1));
     float xr = fmaxf(add(c0, h0), add(c1, h1));
@@ -315,7 +320,7 @@ __device__ __forceinline__ void disc_span(const CullShape& c, float ya, float yb
         r = 0.0f;
         return;
     }
-    const float w = __fsqrt_rn(q);
+    const float w = approx_sqrt(q);
     l = sub(c.gx, w);
     r = add(c.gx, w);
 }
@@ -337,10 +342,31 @@ __device__ __forceinline__ BandSpans band_spans(const CullShape& c, float ya, fl
     return s;
 }
 
-// Tile row ty, widened by one pixel: rows [16 ty - 1, 16 ty + 16]; tile tx
-// of it is live when [16 tx - 1, 16 tx + 16] meets one of the spans.
+// Spans of the two 8-row quadrant bands of tile row ty, widened by one pixel:
+// rows [16 ty + 8 qy - 1, 16 ty + 8 qy + 8].
+__device__ __forceinline__ BandSpans quadrant_band_spans(const CullShape& c, int ty, int qy) {
+    const float ya = static_cast<float>(ty * 16 + qy * 8 - 1);
+    return band_spans(c, ya, add(ya, 9.0f));
+}
+
+__device__ __forceinline__ void hull(float al, float ar, float bl, float br, float& l, float& r) {
+    const bool a = al <= ar, b = bl <= br;
+    l = a && b ? fminf(al, bl) : (a ? al : (b ? bl : 1.0f));
+    r = a && b ? fmaxf(ar, br) : (a ? ar : (b ? br : 0.0f));
+}
+
+// Spans of tile row ty: the hulls of its two quadrant bands' ellipse and disc
+// spans (the row, widened by one pixel, is the union of the two bands); tile
+// tx is live when [16 tx - 1, 16 tx + 16] meets one of them.
+__device__ __forceinline__ BandSpans row_spans(const BandSpans& top, const BandSpans& bottom) {
+    BandSpans s;
+    hull(top.el, top.er, bottom.el, bottom.er, s.el, s.er);
+    hull(top.dl, top.dr, bottom.dl, bottom.dr, s.dl, s.dr);
+    return s;
+}
+
 __device__ __forceinline__ BandSpans tile_row_spans(const CullShape& c, int ty) {
-    return band_spans(c, static_cast<float>(ty * 16 - 1), static_cast<float>(ty * 16 + 16));
+    return row_spans(quadrant_band_spans(c, ty, 0), quadrant_band_spans(c, ty, 1));
 }
 
 __device__ __forceinline__ bool tile_live(const BandSpans& s, int tx) {
@@ -375,22 +401,19 @@ __device__ __forceinline__ int live_tiles(const BandSpans& s, int x0, int x1) {
     return ne + nd - (ne > 0 && nd > 0 ? both : 0);
 }
 
-// 4-bit mask of the 8x8 quadrants of live tile (tx, ty) that may hold a live
-// pixel; bit (qy * 2 + qx). Quadrants are widened by one pixel like tiles.
+// 4-bit mask of the 8x8 quadrants of live tile tx that may hold a live pixel,
+// from the spans of its row's two quadrant bands; bit (qy * 2 + qx).
 // Never empty for a live tile: a rounding disagreement between the tile and
 // quadrant tests falls back to all four quadrants.
-__device__ __forceinline__ uint32_t quadrant_mask(const CullShape& c, int tx, int ty) {
+__device__ __forceinline__ uint32_t quadrant_mask(const BandSpans& top, const BandSpans& bottom,
+                                                  int tx) {
     uint32_t mask = 0;
 #pragma unroll
-    for (int qy = 0; qy < 2; ++qy) {
-        const float ya = static_cast<float>(ty * 16 + qy * 8 - 1);
-        const BandSpans s = band_spans(c, ya, ya + 9.0f);
-#pragma unroll
-        for (int qx = 0; qx < 2; ++qx) {
-            const float x0 = static_cast<float>(tx * 16 + qx * 8 - 1);
-            if (meets(s.el, s.er, x0, x0 + 9.0f) || meets(s.dl, s.dr, x0, x0 + 9.0f))
-                mask |= 1u << (qy * 2 + qx);
-        }
+    for (int qx = 0; qx < 2; ++qx) {
+        const float x0 = static_cast<float>(tx * 16 + qx * 8 - 1), x1 = add(x0, 9.0f);
+        if (meets(top.el, top.er, x0, x1) || meets(top.dl, top.dr, x0, x1)) mask |= 1u << qx;
+        if (meets(bottom.el, bottom.er, x0, x1) || meets(bottom.dl, bottom.dr, x0, x1))
+            mask |= 1u << (2 + qx);
     }
     return mask != 0u ? mask : 0xfu;
 }
