@@ -28,15 +28,18 @@ namespace {
 
 constexpr int kWarps = kThreads / 32;
 
-// Pass kernels come in two tile sizes: 2048 items (8 per thread) while the
-// whole sort fits in about two waves of resident blocks, 4096 items (16 per
-// thread) above that. Larger tiles halve the rate at which tiles start, and
-// with it the number of predecessors a new tile finds holding only an
-// aggregate; the look-back of the large variant also reads more of them per
-// round trip.
+// Pass kernels come in two tile sizes: 2048 items (8 per thread) below 256K
+// items, 4096 items (16 per thread) from there on. Larger tiles halve the rate
+// at which tiles start, and with it the number of predecessors a new tile
+// finds holding only an aggregate; the look-back of the large variant also
+// reads more of them per round trip. Within a warp, items are ranked either
+// with __match_any_sync or with one ballot per digit bit; ballots measured
+// faster for full-width (four-pass) keys and for sorts of 8M items or more,
+// MATCH for the two-pass tile sorts below that.
 constexpr int kLargeItems = 16;
 constexpr int kLargeWindow = 16;
-constexpr uint32_t kLargeSortItems = 1u << 23;
+constexpr uint32_t kLargeTileItems = 1u << 18;
+constexpr uint32_t kBallotItems = 1u << 23;
 
 struct SortScratch {
     uint32_t* hist;       // [kMaxPasses][kBins]
@@ -147,7 +150,7 @@ __device__ __forceinline__ uint32_t block_exclusive_256(uint32_t v, uint32_t* wa
     return base + incl - v;
 }
 
-template <int kItems, int kWindow>
+template <int kItems, int kWindow, bool kBallot>
 __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel(
     const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, uint32_t count, int shift,
@@ -219,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
         const bool valid = i < n;
         const uint32_t dg = valid ? digit_of(tile_keys[i], shift, mask) : 0u;
         uint32_t peers;
-        if (kItems == kLargeItems) {
+        if (kBallot) {
             // lanes holding the same digit, one ballot per digit bit (cheaper
             // than __match_any_sync when many blocks share an SM)
             peers = __ballot_sync(0xffffffffu, valid);
@@ -386,11 +389,12 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
         return cudaErrorInvalidValue;
     }
     const uint32_t tiles = tiles_for(count);
-    const bool large = count >= kLargeSortItems;
+    const bool large = count >= kLargeTileItems;
     const uint32_t large_tiles =
         static_cast<uint32_t>((static_cast<uint64_t>(count) + kThreads * kLargeItems - 1) /
                               (kThreads * kLargeItems));
     const int passes = (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
+    const bool ballot = passes == kMaxPasses || count >= kBallotItems;
     // status words are laid out for 2048-item tiles, enough for either size
     const SortScratch s = sort_scratch(scratch, tiles, passes);
     cudaError_t st = cudaMemsetAsync(scratch, 0, s.zero_bytes, stream);
@@ -411,14 +415,19 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
     for (int shift = begin_bit; shift < end_bit; shift += kRadixBits, ++pass) {
         const int bits = min(kRadixBits, end_bit - shift);
         uint32_t* pass_status = s.status + static_cast<uint64_t>(pass) * tiles * kBins;
-        if (large) {
-            onesweep_kernel<kLargeItems, kLargeWindow><<<large_tiles, kThreads, 0, stream>>>(
+        if (large && ballot) {
+            onesweep_kernel<kLargeItems, kLargeWindow, true><<<large_tiles, kThreads, 0, stream>>>(
+                src_k, src_v, dst_k, dst_v, count, shift, bits, large_tiles,
+                s.hist + pass * kBins, s.counters + pass, pass_status, error);
+        } else if (large) {
+            onesweep_kernel<kLargeItems, kLargeWindow, false><<<large_tiles, kThreads, 0, stream>>>(
                 src_k, src_v, dst_k, dst_v, count, shift, bits, large_tiles,
                 s.hist + pass * kBins, s.counters + pass, pass_status, error);
         } else {
-            onesweep_kernel<kItemsPerThread, kLookBackWindow><<<tiles, kThreads, 0, stream>>>(
-                src_k, src_v, dst_k, dst_v, count, shift, bits, tiles, s.hist + pass * kBins,
-                s.counters + pass, pass_status, error);
+            onesweep_kernel<kItemsPerThread, kLookBackWindow, false>
+                <<<tiles, kThreads, 0, stream>>>(src_k, src_v, dst_k, dst_v, count, shift, bits,
+                                                 tiles, s.hist + pass * kBins, s.counters + pass,
+                                                 pass_status, error);
         }
         uint32_t* tk = src_k;
         uint32_t* tv = src_v;
