@@ -257,11 +257,10 @@ cudaError_t StandardPass::bin() {
             static_cast<uint32_t*>(geometry_scratch_), ctx_->device_error, first_pair);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
-        const Emitter em{gv_.cull, grid_x_, masked_};
-        bin::emit_flat_compact_kernel<Emitter>
-            <<<(c_.point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
-               stream>>>(static_cast<uint32_t>(c_.point_count), gv_.counts, first_pair, em,
-                         tile_ids, values_);
+        emit_rows_kernel<<<(c_.point_count + kEmitRowThreads - 1) / kEmitRowThreads,
+                           kEmitRowThreads, 0, stream>>>(
+            static_cast<uint32_t>(c_.point_count), gv_.counts, first_pair, gv_.cull, grid_x_,
+            masked_ ? 1 : 0, tile_ids, values_);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
         st = sort::sort_pairs(tile_ids, values_, alt_tiles, alt_values, emitted, 0,

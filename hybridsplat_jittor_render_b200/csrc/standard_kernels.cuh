@@ -131,64 +131,136 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     warp_add(out.totals + 2, emitted);
 }
 
-// Emits, for one Gaussian, the live tiles of its clipped rectangle (those the
-// preprocess counted) with the mask of the 8x8 quadrants that may hold a live
-// pixel (emit_flat_compact_kernel interface).
-struct Emitter {
-    const float4* cull;
-    uint32_t grid_x;
-    bool masked;
-
-    struct Shape {
-        float4 a, b, c;
-        float2 d;
-    };
-    __device__ __forceinline__ Shape load(uint32_t gid) const {
-        const float4* p = cull + static_cast<size_t>(gid) * kCullQuads;
-        const float4 d = p[3];
-        return Shape{p[0], p[1], p[2], make_float2(d.x, d.y)};
-    }
-    __device__ __forceinline__ static CullShape unpack(const Shape& s) {
-        CullShape c;
-        c.mx = s.a.x; c.my = s.a.y; c.k = s.a.z; c.w0 = s.a.w;
-        c.hx = s.b.x; c.hy = s.b.y; c.yr = s.b.z; c.gx = s.b.w;
-        c.gy = s.c.x; c.r2 = s.c.y; c.mode = __float_as_int(s.c.z); c.ihy = s.c.w;
-        return c;
-    }
-    __device__ __forceinline__ uint32_t slots(const Shape& s) const {
-        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
-        return ((hi & 0xffff) - (lo & 0xffff)) * ((hi >> 16) - (lo >> 16));
-    }
-    // Spans of the tile row the lane last worked on (consecutive pairs of a
-    // wide Gaussian share their row).
-    struct Cache {
-        uint32_t owner = 0xffffffffu;
-        int ty = 0;
-        BandSpans row, top, bottom;
-    };
-    __device__ __forceinline__ bool pair_at(const Shape& s, uint32_t owner, uint32_t k,
-                                            uint32_t& tile, uint32_t& tag, Cache& cache) const {
-        const uint32_t lo = __float_as_uint(s.d.x), hi = __float_as_uint(s.d.y);
-        const int x0 = lo & 0xffff, y0 = lo >> 16, w = static_cast<int>(hi & 0xffff) - x0;
-        const int ty = y0 + static_cast<int>(k) / w, tx = x0 + static_cast<int>(k) % w;
-        tile = static_cast<uint32_t>(ty) * grid_x + static_cast<uint32_t>(tx);
-        if (__float_as_int(s.c.z) == kCullNever) {
-            tag = masked ? (0xfu << kIndexBits) : 0u;
-            return true;
-        }
-        if (cache.owner != owner || cache.ty != ty) {
-            const CullShape c = unpack(s);
-            cache.top = quadrant_band_spans(c, ty, 0);
-            cache.bottom = quadrant_band_spans(c, ty, 1);
-            cache.row = row_spans(cache.top, cache.bottom);
-            cache.owner = owner;
-            cache.ty = ty;
-        }
-        if (!tile_live(cache.row, tx)) return false;
-        tag = masked ? (quadrant_mask(cache.top, cache.bottom, tx) << kIndexBits) : 0u;
-        return true;
-    }
+// Pair emission by rows. Each warp owns 32 Gaussians (in index order) and
+// walks the rows of their clipped boxes in chunks of 32 (Gaussian, row)
+// units: a lane takes one unit, computes the row's quadrant-band spans and
+// live columns with the same functions the preprocess counted them with
+// (row_columns), then the warp deals the chunk's live tiles to its lanes
+// round-robin. A lane finds the unit of a tile by binary search over the
+// units' inclusive tile counts, its column with RowColumns::at and its
+// quadrant mask from the unit's spans, and takes the next slot of the
+// Gaussian (one shared-memory counter per Gaussian; the slots of one
+// Gaussian are filled in any order, which the stable tile sort makes
+// irrelevant: each tile appears once per Gaussian). The value of a pair is
+// the Gaussian index | quadrant mask << kIndexBits (masked) or the index.
+struct RowUnit {
+    BandSpans top, bottom;
+    RowColumns cols;
+    int ty;
+    uint32_t owner;   // Gaussian within the block
+    uint32_t tiles;   // inclusive live-tile count over the chunk
+    int never;        // kCullNever: every tile, all quadrants
 };
+
+__device__ __forceinline__ CullShape load_cull_shape(const float4* cull, uint32_t gid, int& x0,
+                                                     int& y0, int& x1, int& y1) {
+    const float4* p = cull + static_cast<size_t>(gid) * kCullQuads;
+    const float4 a = p[0], b = p[1], c = p[2], d = p[3];
+    CullShape s;
+    s.mx = a.x; s.my = a.y; s.k = a.z; s.w0 = a.w;
+    s.hx = b.x; s.hy = b.y; s.yr = b.z; s.gx = b.w;
+    s.gy = c.x; s.r2 = c.y; s.mode = __float_as_int(c.z); s.ihy = c.w;
+    const uint32_t lo = __float_as_uint(d.x), hi = __float_as_uint(d.y);
+    x0 = lo & 0xffff;
+    y0 = lo >> 16;
+    x1 = hi & 0xffff;
+    y1 = hi >> 16;
+    return s;
+}
+
+constexpr int kEmitRowThreads = 256;
+
+static __global__ void __launch_bounds__(kEmitRowThreads) emit_rows_kernel(
+    uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
+    const float4* __restrict__ cull, uint32_t grid_x, int masked, uint32_t* __restrict__ tile_ids,
+    uint32_t* __restrict__ values) {
+    __shared__ RowUnit units[kEmitRowThreads];
+    __shared__ uint32_t cursor[kEmitRowThreads], counted[kEmitRowThreads],
+        offsets[kEmitRowThreads], rows_incl[kEmitRowThreads];
+    const uint32_t gid = blockIdx.x * kEmitRowThreads + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const uint32_t base = threadIdx.x & ~31u;
+    const uint32_t cnt = gid < count ? counts[gid] : 0u;
+    int bx0 = 0, by0 = 0, bx1 = 0, by1 = 0;
+    if (cnt != 0u) load_cull_shape(cull, gid, bx0, by0, bx1, by1);
+    cursor[threadIdx.x] = 0;
+    counted[threadIdx.x] = cnt;
+    offsets[threadIdx.x] = cnt != 0u ? first_pair[gid] : 0u;
+    uint32_t incl = cnt != 0u ? static_cast<uint32_t>(by1 - by0) : 0u;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+    }
+    rows_incl[threadIdx.x] = incl;
+    const uint32_t total_rows = __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();
+    RowUnit* my_units = units + base;
+    for (uint32_t u0 = 0; u0 < total_rows; u0 += 32) {
+        // 1. one (Gaussian, row) unit per lane
+        const uint32_t u = u0 + lane;
+        uint32_t n = 0;
+        RowUnit unit;
+        unit.cols = RowColumns{1, 0, 1, 0};
+        unit.never = 0;
+        unit.owner = 0;
+        unit.ty = 0;
+        if (u < total_rows) {
+            uint32_t j = 0;
+#pragma unroll
+            for (uint32_t step = 16; step >= 1; step >>= 1) {
+                if (rows_incl[base + j + step - 1] <= u) j += step;
+            }
+            const uint32_t owner = base + j;
+            const uint32_t r = u - (j == 0 ? 0u : rows_incl[owner - 1]);
+            int x0, y0, x1, y1;
+            const CullShape c = load_cull_shape(cull, blockIdx.x * kEmitRowThreads + owner, x0, y0,
+                                                x1, y1);
+            unit.owner = owner;
+            unit.ty = y0 + static_cast<int>(r);
+            if (c.mode == kCullNever) {
+                unit.never = 1;
+                unit.cols = RowColumns{x0, x1 - 1, 1, 0};
+            } else {
+                unit.top = quadrant_band_spans(c, unit.ty, 0);
+                unit.bottom = quadrant_band_spans(c, unit.ty, 1);
+                unit.cols = row_columns(row_spans(unit.top, unit.bottom), x0, x1);
+            }
+            n = static_cast<uint32_t>(unit.cols.count());
+        }
+        uint32_t tiles = n;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, tiles, off);
+            if (lane >= off) tiles += t;
+        }
+        unit.tiles = tiles;
+        my_units[lane] = unit;
+        const uint32_t chunk_tiles = __shfl_sync(0xffffffffu, tiles, 31);
+        __syncwarp();
+        // 2. the chunk's live tiles, round-robin over the lanes
+        for (uint32_t t = lane; t < chunk_tiles; t += 32) {
+            uint32_t j = 0;
+#pragma unroll
+            for (uint32_t step = 16; step >= 1; step >>= 1) {
+                if (my_units[j + step - 1].tiles <= t) j += step;
+            }
+            const RowUnit& w = my_units[j];
+            const int i = static_cast<int>(t - (j == 0 ? 0u : my_units[j - 1].tiles));
+            const int tx = w.cols.at(i);
+            uint32_t tag = 0;
+            if (masked) tag = (w.never ? 0xfu : quadrant_mask(w.top, w.bottom, tx)) << kIndexBits;
+            const uint32_t owner = w.owner;
+            const uint32_t slot = atomicAdd(&cursor[owner], 1u);
+            if (slot < counted[owner]) {
+                const uint32_t at = offsets[owner] + slot;
+                tile_ids[at] = static_cast<uint32_t>(w.ty) * grid_x + static_cast<uint32_t>(tx);
+                values[at] = (blockIdx.x * kEmitRowThreads + owner) | tag;
+            }
+        }
+        __syncwarp();
+    }
+}
 
 __device__ __forceinline__ BlendRecord load_record(const float4* q) {
     const float4 a = q[0], b = q[1], c = q[2], d = q[3], e = q[4];

@@ -387,18 +387,48 @@ __device__ __forceinline__ void span_columns(float l, float r, int& lo, int& hi)
     if (static_cast<float>((hi + 1) * 16 - 1) <= r) ++hi;
 }
 
+// The live tiles of one row of a clipped box [x0, x1): the columns whose
+// widened range meets the ellipse span, [elo, ehi], and those meeting the disc
+// span, [dlo, dhi] (either may be empty: lo > hi). The row's live tiles are
+// their union, listed ellipse columns first, then the disc columns outside
+// them (RowColumns::at).
+struct RowColumns {
+    int elo, ehi, dlo, dhi;
+    __device__ __forceinline__ int ellipse_count() const { return max(ehi - elo + 1, 0); }
+    __device__ __forceinline__ int disc_count() const { return max(dhi - dlo + 1, 0); }
+    // disc columns before the ellipse range that are not in it
+    __device__ __forceinline__ int disc_before() const {
+        return ellipse_count() == 0 ? disc_count() : max(min(dhi, elo - 1) - dlo + 1, 0);
+    }
+    __device__ __forceinline__ int count() const {
+        const int ne = ellipse_count(), nd = disc_count();
+        const int both = max(min(ehi, dhi) - max(elo, dlo) + 1, 0);
+        return ne + nd - (ne > 0 && nd > 0 ? both : 0);
+    }
+    // column of the i-th live tile, 0 <= i < count()
+    __device__ __forceinline__ int at(int i) const {
+        const int ne = ellipse_count();
+        if (i < ne) return elo + i;
+        const int j = i - ne, before = disc_before();
+        if (j < before) return dlo + j;
+        return max(dlo, ehi + 1) + (j - before);
+    }
+};
+
+__device__ __forceinline__ RowColumns row_columns(const BandSpans& s, int x0, int x1) {
+    RowColumns r{1, 0, 1, 0};
+    if (s.el <= s.er) span_columns(s.el, s.er, r.elo, r.ehi);
+    if (s.dl <= s.dr) span_columns(s.dl, s.dr, r.dlo, r.dhi);
+    r.elo = max(r.elo, x0);
+    r.ehi = min(r.ehi, x1 - 1);
+    r.dlo = max(r.dlo, x0);
+    r.dhi = min(r.dhi, x1 - 1);
+    return r;
+}
+
 // Number of tiles tx in [x0, x1) with tile_live(s, tx).
 __device__ __forceinline__ int live_tiles(const BandSpans& s, int x0, int x1) {
-    int elo = 1, ehi = 0, dlo = 1, dhi = 0;
-    if (s.el <= s.er) span_columns(s.el, s.er, elo, ehi);
-    if (s.dl <= s.dr) span_columns(s.dl, s.dr, dlo, dhi);
-    elo = max(elo, x0);
-    ehi = min(ehi, x1 - 1);
-    dlo = max(dlo, x0);
-    dhi = min(dhi, x1 - 1);
-    const int ne = max(ehi - elo + 1, 0), nd = max(dhi - dlo + 1, 0);
-    const int both = max(min(ehi, dhi) - max(elo, dlo) + 1, 0);
-    return ne + nd - (ne > 0 && nd > 0 ? both : 0);
+    return row_columns(s, x0, x1).count();
 }
 
 // 4-bit mask of the 8x8 quadrants of live tile tx that may hold a live pixel,

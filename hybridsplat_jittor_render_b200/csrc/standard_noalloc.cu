@@ -189,11 +189,9 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
             static_cast<uint32_t*>(l.geometry_scratch), l.error, first_pair);
         st = cudaGetLastError();
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
-        const Emitter em{l.cull, grid_x, true};
-        bin::emit_flat_compact_kernel<Emitter>
-            <<<(point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads, 0,
-               stream>>>(static_cast<uint32_t>(point_count), l.counts, first_pair, em, l.tile_ids,
-                         l.values);
+        emit_rows_kernel<<<(point_count + kEmitRowThreads - 1) / kEmitRowThreads, kEmitRowThreads, 0,
+                           stream>>>(static_cast<uint32_t>(point_count), l.counts, first_pair,
+                                     l.cull, grid_x, 1, l.tile_ids, l.values);
         st = cudaGetLastError();
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
         st = sort::sort_pairs(l.tile_ids, l.values, l.alt_tiles, l.alt_values, emitted, 0,
