@@ -34,6 +34,62 @@ __device__ __forceinline__ void warp_add(uint32_t* dst, uint32_t v) {
     if ((threadIdx.x & 31) == 0 && v != 0u) atomicAdd(dst, v);
 }
 
+// Live tiles of each lane's Gaussian (clipped box [x0, x1) x [y0, y1), cull
+// shape c), counted by the whole warp: the rows of the 32 boxes are dealt to
+// the lanes in chunks of 32 (Gaussian, row) units, a lane reading its unit's
+// shape from the owning lane by shuffles, and each unit's row_columns count is
+// added to the owner's total in `sums` (this warp's 32 words of shared
+// memory). These are the functions and inputs emit_rows_kernel lists the
+// tiles with, so the counts match the emission exactly. Every lane of the
+// warp must call this.
+__device__ __forceinline__ uint32_t warp_live_tiles(const CullShape& c, int x0, int y0, int x1,
+                                                    int y1, bool valid, uint32_t* sums) {
+    const int lane = threadIdx.x & 31;
+    const bool test = valid && c.mode == kCullEllipse && x1 > x0;
+    sums[lane] = (valid && c.mode == kCullNever) ? static_cast<uint32_t>((x1 - x0) * (y1 - y0)) : 0u;
+    uint32_t incl = test ? static_cast<uint32_t>(y1 - y0) : 0u;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+    }
+    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();
+    for (uint32_t u0 = 0; u0 < total; u0 += 32) {
+        const uint32_t u = u0 + lane;
+        int j = 0;
+#pragma unroll
+        for (int step = 16; step >= 1; step >>= 1) {
+            if (__shfl_sync(0xffffffffu, incl, j + step - 1) <= u) j += step;
+        }
+        const uint32_t before = __shfl_sync(0xffffffffu, incl, j > 0 ? j - 1 : 0);
+        CullShape o;
+        o.mx = __shfl_sync(0xffffffffu, c.mx, j);
+        o.my = __shfl_sync(0xffffffffu, c.my, j);
+        o.k = __shfl_sync(0xffffffffu, c.k, j);
+        o.w0 = __shfl_sync(0xffffffffu, c.w0, j);
+        o.hx = __shfl_sync(0xffffffffu, c.hx, j);
+        o.hy = __shfl_sync(0xffffffffu, c.hy, j);
+        o.yr = __shfl_sync(0xffffffffu, c.yr, j);
+        o.ihy = __shfl_sync(0xffffffffu, c.ihy, j);
+        o.gx = __shfl_sync(0xffffffffu, c.gx, j);
+        o.gy = __shfl_sync(0xffffffffu, c.gy, j);
+        o.r2 = __shfl_sync(0xffffffffu, c.r2, j);
+        o.mode = kCullEllipse;
+        const int ox0 = __shfl_sync(0xffffffffu, x0, j), ox1 = __shfl_sync(0xffffffffu, x1, j);
+        const int oy0 = __shfl_sync(0xffffffffu, y0, j);
+        if (u < total) {
+            const int ty = oy0 + static_cast<int>(u - (j > 0 ? before : 0u));
+            const BandSpans row =
+                row_spans(quadrant_band_spans(o, ty, 0), quadrant_band_spans(o, ty, 1));
+            const int n = row_columns(row, ox0, ox1).count();
+            if (n != 0) atomicAdd(&sums[j], static_cast<uint32_t>(n));
+        }
+    }
+    __syncwarp();
+    return sums[lane];
+}
+
 // preprocessCUDA<5> (forward.cu:148-251) plus the cull shape. A Gaussian
 // emits the tiles of its reference rectangle (getRect) that also lie in the
 // bounding box of its live region; `rendered` still counts the whole
@@ -50,6 +106,7 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     const bool active = idx < point_count;
     const R r;
     __shared__ float m[32];
+    __shared__ uint32_t live_sums[kPreThreads];
     if (threadIdx.x < 16) m[threadIdx.x] = viewmatrix[threadIdx.x];
     else if (threadIdx.x < 32) m[threadIdx.x] = projmatrix[threadIdx.x - 16];
     __syncthreads();
@@ -61,6 +118,12 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) out.totals[3] = *out.error;
     uint32_t area = 0, emitted = 0, violation = 0;
+    CullShape cs;
+    cs.mode = kCullAlways;
+    cs.mx = cs.my = cs.k = cs.w0 = cs.hx = cs.hy = cs.yr = cs.ihy = cs.gx = cs.gy = cs.r2 = 0.0f;
+    int x0 = 0, y0 = 0, x1 = 0, y1 = 0;
+    bool valid = false;
+    float depth = 0.0f;
     if (active) {
         // All inputs are requested before any arithmetic; scales and
         // rotations use 64/128-bit loads when their rows are aligned.
@@ -96,23 +159,16 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
             // pairs of the reference rectangle inside the rendered tile rows
             const uint32_t ry0 = max(g.rect_min.y, row_begin), ry1 = min(g.rect_max.y, row_end);
             area = ry1 > ry0 ? (g.rect_max.x - g.rect_min.x) * (ry1 - ry0) : 0u;
-            const CullShape cs = cull_shape(op, g.xy.x, g.xy.y, g.tu, g.tv, g.tw);
+            cs = cull_shape(op, g.xy.x, g.xy.y, g.tu, g.tv, g.tw);
+            valid = true;
+            depth = g.depth;
             int bx0, by0, bx1, by1;
-            int x0 = 0, y0 = 0, x1 = 0, y1 = 0;
             if (cull_tile_box(cs, bx0, by0, bx1, by1)) {
                 x0 = max(static_cast<int>(g.rect_min.x), bx0);
                 y0 = max(static_cast<int>(max(g.rect_min.y, row_begin)), by0);
                 x1 = min(static_cast<int>(g.rect_max.x), bx1 + 1);
                 y1 = min(static_cast<int>(min(g.rect_max.y, row_end)), by1 + 1);
                 if (x1 <= x0 || y1 <= y0) x0 = y0 = x1 = y1 = 0;
-            }
-            // pairs to emit: the live tiles of the clipped box, row by row
-            // (the emission makes the same per-tile decisions)
-            if (cs.mode == kCullNever) {
-                emitted = static_cast<uint32_t>((x1 - x0) * (y1 - y0));
-            } else {
-                for (int ty = y0; ty < y1; ++ty)
-                    emitted += static_cast<uint32_t>(live_tiles(tile_row_spans(cs, ty), x0, x1));
             }
             float4* cu = out.cull + static_cast<size_t>(idx) * kCullQuads;
             cu[0] = make_float4(cs.mx, cs.my, cs.k, cs.w0);
@@ -122,9 +178,13 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
                                 __uint_as_float(static_cast<uint32_t>(x1) | (static_cast<uint32_t>(y1) << 16)),
                                 0.0f, 0.0f);
             out.radii[idx] = static_cast<int32_t>(g.radius);
-            out.counts[idx] = emitted;
-            out.depth_keys[idx] = emitted != 0 ? __float_as_uint(g.depth) : 0xffffffffu;
         }
+    }
+    // pairs to emit: the live tiles of the clipped box (counted by the warp)
+    emitted = warp_live_tiles(cs, x0, y0, x1, y1, valid, live_sums + (threadIdx.x & ~31));
+    if (valid) {
+        out.counts[idx] = emitted;
+        out.depth_keys[idx] = emitted != 0 ? __float_as_uint(depth) : 0xffffffffu;
     }
     warp_add(out.totals + 0, area);
     warp_add(out.totals + 1, violation);

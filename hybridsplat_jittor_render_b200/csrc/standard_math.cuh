@@ -355,7 +355,7 @@ __device__ __forceinline__ void hull(float al, float ar, float bl, float br, flo
     r = a && b ? fmaxf(ar, br) : (a ? ar : (b ? br : 0.0f));
 }
 
-// Spans of tile row ty: the hulls of its two quadrant bands' ellipse and disc
+// Spans of a tile row: the hulls of its two quadrant bands' ellipse and disc
 // spans (the row, widened by one pixel, is the union of the two bands); tile
 // tx is live when [16 tx - 1, 16 tx + 16] meets one of them.
 __device__ __forceinline__ BandSpans row_spans(const BandSpans& top, const BandSpans& bottom) {
@@ -365,18 +365,10 @@ __device__ __forceinline__ BandSpans row_spans(const BandSpans& top, const BandS
     return s;
 }
 
-__device__ __forceinline__ BandSpans tile_row_spans(const CullShape& c, int ty) {
-    return row_spans(quadrant_band_spans(c, ty, 0), quadrant_band_spans(c, ty, 1));
-}
-
-__device__ __forceinline__ bool tile_live(const BandSpans& s, int tx) {
-    const float x0 = static_cast<float>(tx * 16 - 1), x1 = static_cast<float>(tx * 16 + 16);
-    return meets(s.el, s.er, x0, x1) || meets(s.dl, s.dr, x0, x1);
-}
-
-// Tile columns [lo, hi] whose widened range meets [l, r]: the first column
-// with 16 lo + 16 >= l and the last with 16 hi - 1 <= r, found from the
-// quotients and corrected with the same comparisons tile_live makes.
+// Tile columns [lo, hi] whose widened range [16 tx - 1, 16 tx + 16] meets
+// [l, r]: the first column with 16 lo + 16 >= l and the last with
+// 16 hi - 1 <= r, found from the quotients and corrected by those exact
+// comparisons.
 __device__ __forceinline__ void span_columns(float l, float r, int& lo, int& hi) {
     const float lc = fminf(fmaxf(l, -4.0e6f), 4.0e6f), rc = fminf(fmaxf(r, -4.0e6f), 4.0e6f);
     lo = static_cast<int>(ceilf(mul(sub(lc, 16.0f), 0.0625f)));
@@ -424,11 +416,6 @@ __device__ __forceinline__ RowColumns row_columns(const BandSpans& s, int x0, in
     r.dlo = max(r.dlo, x0);
     r.dhi = min(r.dhi, x1 - 1);
     return r;
-}
-
-// Number of tiles tx in [x0, x1) with tile_live(s, tx).
-__device__ __forceinline__ int live_tiles(const BandSpans& s, int x0, int x1) {
-    return row_columns(s, x0, x1).count();
 }
 
 // 4-bit mask of the 8x8 quadrants of live tile tx that may hold a live pixel,
