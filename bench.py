@@ -656,6 +656,11 @@ def roofline_and_baselines(args, frame, cams, stages, scene_np, clocks: dict) ->
             from hybridsplat_jittor_render_b200.native_runtime import bind_library
             ref = bind_library(ref_path, require_optix=False)
             rframe = Frame(scene_np, args.backend, frame.device, library=ref, concurrent=False)
+            # the same session priming as ours: one untimed render of each
+            # timed view sizes the reference's grow-only workspaces
+            for cam in {id(c): c for c in cams}.values():
+                rframe.set_camera(cam)
+                rframe.render()
             for s in range(args.warmup):
                 rframe.set_camera(cams[s])
                 rframe.render()

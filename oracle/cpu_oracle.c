@@ -755,3 +755,162 @@ API int64_t oracle_standard_forward(int P, const float* bg5, int W, int H, const
     free(gs);
     return all_pairs;
 }
+
+/* ---- checker of the standard backend's culling (test infrastructure) ----
+ *
+ * Restates the CUDA library's tile/quadrant culling (csrc/standard_math.cuh:
+ * cull_shape, cull_tile_box, the chord spans, row hulls, row columns and
+ * quadrant masks) with correctly rounded CPU arithmetic in place of the
+ * GPU's approximate square roots, and checks it against the reference's
+ * per-pixel arithmetic (forward.cu:345-393 as restated in st_blend): every
+ * 8x8 quadrant of a Gaussian's reference rectangle holding a pixel whose
+ * evaluation reaches alpha >= 1/255 must be emitted with its mask bit set.
+ * out[0] = quadrants holding such a pixel, out[1] = those the culling misses,
+ * out[2] = tiles emitted, out[3] = tiles of the reference rectangles. */
+typedef struct { float mx, my, k, w0, hx, hy, yr, ihy, gx, gy, r2; int mode; } CullC;
+enum { kCullEllipseC = 0, kCullNeverC = 1, kCullAlwaysC = 2 };
+
+static CullC cull_c(float op, float x, float y, const float* tu, const float* tv, const float* tw) {
+    CullC c;
+    memset(&c, 0, sizeof c);
+    c.gx = x;
+    c.gy = y;
+    if (!(op > 1.0f / 255.0f)) { c.mode = kCullAlwaysC; return c; }
+    const float cwf = 1.02f * (2.0f * logf(255.0f * op)) + 0.05f;
+    const double cw = (double)cwf * 1.0001;
+    c.r2 = (float)(0.5 * cw * 1.0001);
+    const double twx = tw[0], twy = tw[1], twz = tw[2];
+    const double d = cw * (twx * twx + twy * twy) - twz * twz;
+    c.mode = kCullNeverC;
+    if (!(d < -1e-6 * twz * twz)) return c;
+    const double fxy = cw / d, fz = -1.0 / d;
+    const double mx = fxy * ((double)tu[0] * twx + (double)tu[1] * twy) + fz * (double)tu[2] * twz;
+    const double my = fxy * ((double)tv[0] * twx + (double)tv[1] * twy) + fz * (double)tv[2] * twz;
+    const double quu = fxy * ((double)tu[0] * tu[0] + (double)tu[1] * tu[1]) + fz * (double)tu[2] * tu[2];
+    const double qvv = fxy * ((double)tv[0] * tv[0] + (double)tv[1] * tv[1]) + fz * (double)tv[2] * tv[2];
+    const double quv = fxy * ((double)tu[0] * tv[0] + (double)tu[1] * tv[1]) + fz * (double)tu[2] * tv[2];
+    const double sxx = mx * mx - quu, syy = my * my - qvv, sxy = mx * my - quv, det = sxx * syy - sxy * sxy;
+    if (!(sxx > 0 && syy > 0 && det > 0) || !(fabs(mx) < 1e7 && fabs(my) < 1e7)) return c;
+    const double s = 1.0003;
+    c.mx = (float)mx; c.my = (float)my; c.k = (float)(sxy / syy); c.w0 = (float)(sqrt(det / syy) * s);
+    c.hx = (float)(sqrt(sxx) * s); c.hy = (float)(sqrt(syy) * s); c.yr = (float)(sxy / sqrt(sxx) * s);
+    c.ihy = (float)(1.0 / (sqrt(syy) * s));
+    c.mode = kCullEllipseC;
+    return c;
+}
+
+static void espan_c(const CullC* c, float ya, float yb, float* l, float* r) {
+    const float y0 = fmaxf(ya - c->my, -c->hy), y1 = fminf(yb - c->my, c->hy);
+    if (!(y0 <= y1)) { *l = 1.0f; *r = 0.0f; return; }
+    const float t0 = fminf(fmaxf(y0 * c->ihy, -1.0f), 1.0f), t1 = fminf(fmaxf(y1 * c->ihy, -1.0f), 1.0f);
+    const float h0 = c->w0 * sqrtf((1.0f - t0) * (1.0f + t0)), h1 = c->w0 * sqrtf((1.0f - t1) * (1.0f + t1));
+    const float c0 = c->k * y0, c1 = c->k * y1;
+    float xl = fminf(c0 - h0, c1 - h1), xr = fmaxf(c0 + h0, c1 + h1);
+    if (y0 <= -c->yr && -c->yr <= y1) xl = fminf(xl, -c->hx);
+    if (y0 <= c->yr && c->yr <= y1) xr = fmaxf(xr, c->hx);
+    *l = c->mx + xl;
+    *r = c->mx + xr;
+}
+
+static void dspan_c(const CullC* c, float ya, float yb, float* l, float* r) {
+    const float dy = fmaxf(fmaxf(ya - c->gy, c->gy - yb), 0.0f);
+    const float q = c->r2 - dy * dy;
+    if (!(q >= 0.0f)) { *l = 1.0f; *r = 0.0f; return; }
+    const float w = sqrtf(q);
+    *l = c->gx - w;
+    *r = c->gx + w;
+}
+
+static int meets_c(float l, float r, float x0, float x1) { return x0 <= r && x1 >= l && l <= r; }
+
+static void hull_c(float al, float ar, float bl, float br, float* l, float* r) {
+    const int a = al <= ar, b = bl <= br;
+    *l = a && b ? fminf(al, bl) : (a ? al : (b ? bl : 1.0f));
+    *r = a && b ? fmaxf(ar, br) : (a ? ar : (b ? br : 0.0f));
+}
+
+/* Emitted? and mask of tile (tx, ty) for an ellipse-mode shape. */
+static unsigned tile_mask_c(const CullC* c, int tx, int ty) {
+    float s[2][4];
+    for (int qy = 0; qy < 2; ++qy) {
+        const float ya = (float)(ty * 16 + qy * 8 - 1);
+        espan_c(c, ya, ya + 9.0f, &s[qy][0], &s[qy][1]);
+        dspan_c(c, ya, ya + 9.0f, &s[qy][2], &s[qy][3]);
+    }
+    float el, er, dl, dr;
+    hull_c(s[0][0], s[0][1], s[1][0], s[1][1], &el, &er);
+    hull_c(s[0][2], s[0][3], s[1][2], s[1][3], &dl, &dr);
+    const float x0 = (float)(tx * 16 - 1), x1 = (float)(tx * 16 + 16);
+    if (!(meets_c(el, er, x0, x1) || meets_c(dl, dr, x0, x1))) return 0u;
+    unsigned m = 0;
+    for (int qy = 0; qy < 2; ++qy)
+        for (int qx = 0; qx < 2; ++qx) {
+            const float a = (float)(tx * 16 + qx * 8 - 1), b = a + 9.0f;
+            if (meets_c(s[qy][0], s[qy][1], a, b) || meets_c(s[qy][2], s[qy][3], a, b)) m |= 1u << (qy * 2 + qx);
+        }
+    return m ? m : 15u;
+}
+
+/* Does the evaluation of Gaussian record g at pixel (px, py) reach alpha >= 1/255? */
+static int pixel_live_c(const float* g, float px, float py) {
+    StPixel s;
+    memset(&s, 0, sizeof s);
+    s.t = 1.0f;
+    return st_blend(&s, px, py, g) != 0.0f || s.done;
+}
+
+API int oracle_standard_cull_check(int P, int W, int H, const float* means, const float* opac,
+                                   const float* scales, float mod, const float* rot,
+                                   const float* view, const float* proj, int threads,
+                                   int64_t* out) {
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+    const int gx = (W + 15) / 16, gy = (H + 15) / 16;
+    static const float zero5[5] = {0, 0, 0, 0, 0};
+    int64_t live_q = 0, missed = 0, emitted = 0, rect_tiles = 0;
+#pragma omp parallel for schedule(dynamic, 64) reduction(+ : live_q, missed, emitted, rect_tiles)
+    for (int i = 0; i < P; ++i) {
+        StGauss g;
+        st_preprocess_one(0, view, proj, W, H, gx, gy, means + 3 * (size_t)i, zero5, opac + i,
+                          scales + 2 * (size_t)i, mod, rot + 4 * (size_t)i, &g);
+        if (!g.valid) continue;
+        const float* R = g.rec;
+        const CullC c = cull_c(R[5], R[0], R[1], R + 11, R + 14, R + 17);
+        int bx0 = 0, by0 = 0, bx1 = -1, by1 = -1;
+        if (c.mode == kCullNeverC) {
+            bx0 = by0 = -1000000;
+            bx1 = by1 = 1000000;
+        } else if (c.mode == kCullEllipseC) {
+            const float rd = sqrtf(c.r2) + 1.0f, ex = c.hx + 1.0f, ey = c.hy + 1.0f;
+            bx0 = (int)floorf(fmaxf(fminf(c.gx - rd, c.mx - ex), -1e6f) * (1.0f / 16.0f));
+            by0 = (int)floorf(fmaxf(fminf(c.gy - rd, c.my - ey), -1e6f) * (1.0f / 16.0f));
+            bx1 = (int)floorf(fminf(fmaxf(c.gx + rd, c.mx + ex), 1e6f) * (1.0f / 16.0f));
+            by1 = (int)floorf(fminf(fmaxf(c.gy + rd, c.my + ey), 1e6f) * (1.0f / 16.0f));
+        }
+        for (int ty = g.rmin[1]; ty < g.rmax[1]; ++ty)
+            for (int tx = g.rmin[0]; tx < g.rmax[0]; ++tx) {
+                ++rect_tiles;
+                const int in_box = tx >= bx0 && tx <= bx1 && ty >= by0 && ty <= by1;
+                unsigned mask = 0;
+                if (in_box) mask = c.mode == kCullNeverC ? 15u : tile_mask_c(&c, tx, ty);
+                emitted += mask != 0u;
+                for (int q = 0; q < 4; ++q) {
+                    int live = 0;
+                    for (int k = 0; k < 64 && !live; ++k) {
+                        const int x = tx * 16 + (q & 1) * 8 + (k & 7), y = ty * 16 + (q >> 1) * 8 + (k >> 3);
+                        if (x < W && y < H) live = pixel_live_c(R, (float)x, (float)y);
+                    }
+                    live_q += live;
+                    missed += live && !(mask & (1u << q));
+                }
+            }
+    }
+    out[0] = live_q;
+    out[1] = missed;
+    out[2] = emitted;
+    out[3] = rect_tiles;
+    return 0;
+}
