@@ -307,8 +307,9 @@ __global__ void __launch_bounds__(kRenderThreads) render_kernel(
                 cursor = nb;
                 for (int j = 0; j < nb; ++j) {
                     const BlendRecord g = load_record(batch + j * 5);
-                    blend(r, s0, fx, fy0, g);
-                    blend(r, s1, fx, fy1, g);
+                    const ColumnTerms col = column_terms(r, fx, g);
+                    blend(r, s0, col, fy0, g);
+                    blend(r, s1, col, fy1, g);
                     if (__all_sync(0xffffffffu, s0.t < 0.0001f && s1.t < 0.0001f)) {
                         warp_done = true;
                         warp_done_at = base + j;
@@ -325,8 +326,9 @@ __global__ void __launch_bounds__(kRenderThreads) render_kernel(
             const int stop = tile_end == INT_MAX ? nb : tile_end - base + 1;
             for (int j = cursor; j < stop; ++j) {
                 const BlendRecord g = load_record(batch + j * 5);
-                blend(r, s0, fx, fy0, g);
-                blend(r, s1, fx, fy1, g);
+                const ColumnTerms col = column_terms(r, fx, g);
+                blend(r, s0, col, fy0, g);
+                blend(r, s1, col, fy1, g);
             }
             if (tile_end != INT_MAX) break;
         }

@@ -314,14 +314,26 @@ struct BlendRecord {
     float twx, twy, twz;
 };
 
+// The terms of an evaluation that depend only on the pixel column (k =
+// x Tw - Tu and x's offset from the centre), formed once for a lane's two
+// pixels, which share their column.
+struct ColumnTerms {
+    float kx, ky, kz, dx;
+};
+
+template <class R>
+__device__ __forceinline__ ColumnTerms column_terms(const R& r, float px, const BlendRecord& g) {
+    const int vk = r(S_K);
+    return ColumnTerms{msub(vk, px, g.twx, g.tux), msub(vk, px, g.twy, g.tuy),
+                       msub(vk, px, g.twz, g.tuz), sub(g.x, px)};
+}
+
 // pixel_shader (render.cu:77-136).
 template <class R>
-__device__ __forceinline__ void blend(const R& r, PixelState& s, float px, float py,
+__device__ __forceinline__ void blend(const R& r, PixelState& s, const ColumnTerms& col, float py,
                                       const BlendRecord& g) {
     const int vk = r(S_K);
-    const float kx = msub(vk, px, g.twx, g.tux);
-    const float ky = msub(vk, px, g.twy, g.tuy);
-    const float kz = msub(vk, px, g.twz, g.tuz);
+    const float kx = col.kx, ky = col.ky, kz = col.kz;
     const float lx = msub(vk, py, g.twx, g.tvx);
     const float ly = msub(vk, py, g.twy, g.tvy);
     const float lz = msub(vk, py, g.twz, g.tvz);
@@ -332,7 +344,7 @@ __device__ __forceinline__ void blend(const R& r, PixelState& s, float px, float
     const float sx = div(pxv, pzv);
     const float sy = div(pyv, pzv);
     const float rho3d = dot2(r(S_RHO3), sx, sx, sy, sy);
-    const float dx = sub(g.x, px);
+    const float dx = col.dx;
     const float dy = sub(g.y, py);
     const float rho2d = mul(2.0f, dot2(r(S_RHO2), dx, dx, dy, dy));
     const float rho = fminf(rho3d, rho2d);

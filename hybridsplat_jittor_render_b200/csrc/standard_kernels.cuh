@@ -413,8 +413,9 @@ __global__ void __launch_bounds__(kRenderThreads, 7) render_kernel(
             const int live_count = __popc(mask);
             for (int k = 0; k < live_count; ++k) {
                 const BlendRecord g = load_record(my_slots + k * kRecordQuads);
-                float w = blend(r, s0, fx, fy0, g);
-                w += blend(r, s1, fx, fy1, g);
+                const ColumnTerms col = column_terms(r, fx, g);
+                float w = blend(r, s0, col, fy0, g);
+                w += blend(r, s1, col, fy1, g);
                 if (__any_sync(0xffffffffu, w != 0.0f)) {
                     w = w + __shfl_xor_sync(0xffffffffu, w, 16);
                     w = w + __shfl_xor_sync(0xffffffffu, w, 8);
