@@ -12,9 +12,12 @@
 //    (rasterizer/flashgs_prepare.cpp:30-84, vendor/flashgs/model_utils.h:10-43)
 //    with glm::normalize as v * (1 / sqrt(dot(v, v))) and the vec4 dot as
 //    (x*x + y*y) + (z*z + w*w) (glm/detail/func_geometric.inl:58-90).
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <thread>
+#include <vector>
 
 #include "context.h"
 
@@ -74,12 +77,14 @@ float sigmoid_host(float value) { return 1.0f / (1.0f + std::exp(-value)); }
 
 }  // namespace
 
-void flashgs_prepare_host(uint64_t count, const float* opacity_raw, const float* scaling_raw,
-                          const float* rotation_raw, const float* specular_raw,
-                          const float* roughness_raw, float* opacity, float* scaling,
-                          float* rotation, float* covariance, float* specular,
-                          float* roughness) {
-    for (uint64_t i = 0; i < count; ++i) {
+namespace {
+
+void prepare_range(uint64_t first, uint64_t last, const float* opacity_raw,
+                   const float* scaling_raw, const float* rotation_raw,
+                   const float* specular_raw, const float* roughness_raw, float* opacity,
+                   float* scaling, float* rotation, float* covariance, float* specular,
+                   float* roughness) {
+    for (uint64_t i = first; i < last; ++i) {
         opacity[i] = sigmoid_host(opacity_raw[i]);
         const float sx = std::exp(scaling_raw[2 * i]);
         const float sy = std::exp(scaling_raw[2 * i + 1]);
@@ -139,4 +144,42 @@ void flashgs_prepare_host(uint64_t count, const float* opacity_raw, const float*
     }
 }
 
+
+}  // namespace
+
+// The reference loops over the Gaussians on one thread; every Gaussian's
+// arithmetic is independent, so large inputs are split into contiguous
+// ranges over the host's cores with identical per-element results.
+void flashgs_prepare_host(uint64_t count, const float* opacity_raw, const float* scaling_raw,
+                          const float* rotation_raw, const float* specular_raw,
+                          const float* roughness_raw, float* opacity, float* scaling,
+                          float* rotation, float* covariance, float* specular,
+                          float* roughness) {
+    constexpr uint64_t kPerThread = 1u << 16;
+    const unsigned cores = std::max(1u, std::thread::hardware_concurrency());
+    const uint64_t wanted = (count + kPerThread - 1) / kPerThread;
+    const unsigned threads = static_cast<unsigned>(std::min<uint64_t>(wanted, std::min(cores, 32u)));
+    if (threads <= 1) {
+        prepare_range(0, count, opacity_raw, scaling_raw, rotation_raw, specular_raw, roughness_raw,
+                      opacity, scaling, rotation, covariance, specular, roughness);
+        return;
+    }
+    std::vector<std::thread> pool;
+    pool.reserve(threads);
+    const uint64_t chunk = (count + threads - 1) / threads;
+    for (unsigned t = 0; t < threads; ++t) {
+        const uint64_t first = t * chunk, last = std::min(count, first + chunk);
+        if (first >= last) break;
+        try {
+            pool.emplace_back(prepare_range, first, last, opacity_raw, scaling_raw, rotation_raw,
+                              specular_raw, roughness_raw, opacity, scaling, rotation, covariance,
+                              specular, roughness);
+        } catch (...) {  // no thread available: this range on the calling thread
+            prepare_range(first, last, opacity_raw, scaling_raw, rotation_raw, specular_raw,
+                          roughness_raw, opacity, scaling, rotation, covariance, specular,
+                          roughness);
+        }
+    }
+    for (auto& th : pool) th.join();
+}
 }  // namespace hs

@@ -208,3 +208,16 @@ def test_fused_glue_validation(lib, symbol, args, expected):
     assert getattr(lib, symbol)(*args, err, len(err)) == expected
     if expected == 3:
         assert err.value.decode().startswith("precise_sh_to_rgb")
+
+
+def test_prepare_host_threads_bit_identical(lib):
+    """Large inputs are prepared on several host threads; every element must
+    equal the single-threaded result (ranges below 64K Gaussians run on the
+    calling thread)."""
+    n = 300_001
+    raw = _raw(n, 11)
+    whole = ops.flashgs_prepare_host(*raw)
+    parts = [ops.flashgs_prepare_host(*[a[i:i + 50_000] for a in raw]) for i in range(0, n, 50_000)]
+    for key, value in whole.items():
+        joined = np.concatenate([p[key] for p in parts])
+        assert np.array_equal(value.view(np.uint32), joined.view(np.uint32)), key
