@@ -822,6 +822,25 @@ int32_t hs_flashgs_debug_copy_v1(HsRasterizerHandle handle, uint64_t point_capac
     });
 }
 
+int32_t hs_b200_standard_debug_copy_v1(HsRasterizerHandle handle, uint64_t point_capacity,
+                                       float* points_xy2, float* transmats9,
+                                       float* normal_opacity4, char* error_text,
+                                       uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "standard debug copy received a null context",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        const cudaError_t e = hs::standard_debug_copy(handle, point_capacity, points_xy2,
+                                                      transmats9, normal_opacity4);
+        if (e != cudaSuccess) return cuda_failure(e, "standard debug copy", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
 int32_t hs_rasterizer_forward_f32_v1(
     HsRasterizerHandle handle, uint64_t point_count, const float* background5, int32_t width,
     int32_t height, const float* means3d, const float* colors5, const float* opacities,

@@ -104,6 +104,7 @@ struct HsRasterizerContext {
     uint64_t std_growth_count = 0;
     uint32_t* std_total_host = nullptr;    // mapped pinned readback of the pair totals
     uint32_t* std_total_mapped = nullptr;  // its device address
+    uint64_t std_last_point_count = 0;     // Gaussians of the last forward (debug copy)
 
     // deterministic FlashGS backend
     hs::DeviceBuffer fg_gaussian;   // records, keys, counts, depth order
@@ -241,6 +242,12 @@ cudaError_t flashgs_debug_copy(HsRasterizerContext* context, uint64_t point_capa
                                float* conic_opacity4, float* normal_opacity4, float* tu3,
                                float* tv3, float* tw3, uint64_t* sorted_keys,
                                uint32_t* sorted_values, int32_t* tile_ranges2);
+
+// Synchronous copy of the last standard forward's per-Gaussian blend state
+// (centre, Tu|Tv|Tw, normal|opacity) to host buffers. Entries of Gaussians
+// with radius 0 are unspecified.
+cudaError_t standard_debug_copy(HsRasterizerContext* context, uint64_t point_capacity,
+                                float* points_xy2, float* transmats9, float* normal_opacity4);
 
 // Standard five-channel forward (standard.cu) on call.stream.
 cudaError_t standard_forward(HsRasterizerContext* context, const StandardCall& call);

@@ -77,7 +77,8 @@ enum Site : int {
     // screen-space bounding box (standard)
     S_AABB_D_PAIR,     // 9*Tw.x^2 + 9*Tw.y^2
     S_AABB_D_TAIL,     //   - Tw.z^2          (0: fused Tw.z*Tw.z, 1: rounded square)
-    S_AABB_P_PAIR,     // f . (Tu*Tw) and f . (Tv*Tw), pair
+    S_AABB_PX_PAIR,    // f . (Tu*Tw), pair (centre x)
+    S_AABB_PY_PAIR,    // f . (Tv*Tw), pair (centre y)
     S_AABB_P_TAIL,     //   tail
     S_AABB_Q_PAIR,     // f . (Tu*Tu) and f . (Tv*Tv), pair
     S_AABB_Q_TAIL,     //   tail
@@ -133,20 +134,38 @@ __device__ __forceinline__ void splat_transform(const R& r, const float* view, c
     rm[2][0] = mul(2.0f, dot2(r(S_R20), qx, qz, qw, qy));
     rm[2][1] = mul(2.0f, diff2(r(S_R21), qy, qz, qw, qx));
     rm[2][2] = sub(1.0f, mul(2.0f, dot2(r(S_R22), qx, qx, qy, qy)));
-    // L = R * diag(mod*sx, mod*sy, 1): the zero products leave the values unchanged.
+    // L = R * diag(mod*sx, mod*sy, 1). GLM forms every product of the matrix
+    // products below, including those with the structural zeros of S,
+    // splat2world and ndc2pix. Such a product is a signed zero (NaN for an
+    // infinite factor): it leaves a non-zero sum unchanged but decides the
+    // sign of a zero one, so each is added here too (in any order: a sum of
+    // zeros is -0 exactly when every term is).
     const float s0 = mul(scale_modifier, scale.x), s1 = mul(scale_modifier, scale.y);
-    const float l0[3] = {mul(rm[0][0], s0), mul(rm[0][1], s0), mul(rm[0][2], s0)};
-    const float l1[3] = {mul(rm[1][0], s1), mul(rm[1][1], s1), mul(rm[1][2], s1)};
+    float zr[3][3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+#pragma unroll
+        for (int i = 0; i < 3; ++i) zr[c][i] = mul(rm[c][i], 0.0f);
+    float l0[3], l1[3], l2[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        l0[i] = add(add(mul(rm[0][i], s0), zr[1][i]), zr[2][i]);
+        l1[i] = add(add(zr[0][i], mul(rm[1][i], s1)), zr[2][i]);
+        l2[i] = add(add(zr[0][i], zr[1][i]), rm[2][i]);
+    }
     // B = splat2world^T * world2ndc, world2ndc[c][k] = proj[4k + c]:
     // B[c][i] = A[0][i]*proj[c] + A[1][i]*proj[4+c] + A[2][i]*proj[8+c] + A[3][i]*proj[12+c]
     // with A[.][0] = L0, A[.][1] = L1, A[.][2] = p and A[3] = (0, 0, 1).
     float b[4][3];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        b[c][0] = dot3(r(S_B0_PAIR), r(S_B0_TAIL), l0[0], proj[c], l0[1], proj[4 + c], l0[2],
-                       proj[8 + c]);
-        b[c][1] = dot3(r(S_B1_PAIR), r(S_B1_TAIL), l1[0], proj[c], l1[1], proj[4 + c], l1[2],
-                       proj[8 + c]);
+        const float zp = mul(0.0f, proj[12 + c]);  // A[3][0] = A[3][1] = +0
+        b[c][0] = add(dot3(r(S_B0_PAIR), r(S_B0_TAIL), l0[0], proj[c], l0[1], proj[4 + c], l0[2],
+                           proj[8 + c]),
+                      zp);
+        b[c][1] = add(dot3(r(S_B1_PAIR), r(S_B1_TAIL), l1[0], proj[c], l1[1], proj[4 + c], l1[2],
+                           proj[8 + c]),
+                      zp);
         b[c][2] = add(dot3(r(S_B2_PAIR), r(S_B2_TAIL), p.x, proj[c], p.y, proj[4 + c], p.z,
                            proj[8 + c]),
                       proj[12 + c]);
@@ -154,20 +173,25 @@ __device__ __forceinline__ void splat_transform(const R& r, const float* view, c
     // T = B * ndc2pix, ndc2pix columns (W/2,0,0,(W-1)/2), (0,H/2,0,(H-1)/2), (0,0,0,1).
     const float w2 = static_cast<float>(width) * 0.5f, wm = static_cast<float>(width - 1) * 0.5f;
     const float h2 = static_cast<float>(height) * 0.5f, hm = static_cast<float>(height - 1) * 0.5f;
-    tu = make_float3(mad(r(S_TN_U), b[3][0], wm, mul(b[0][0], w2)),
-                     mad(r(S_TN_U), b[3][1], wm, mul(b[0][1], w2)),
-                     mad(r(S_TN_U), b[3][2], wm, mul(b[0][2], w2)));
-    tv = make_float3(mad(r(S_TN_V), b[3][0], hm, mul(b[1][0], h2)),
-                     mad(r(S_TN_V), b[3][1], hm, mul(b[1][1], h2)),
-                     mad(r(S_TN_V), b[3][2], hm, mul(b[1][2], h2)));
-    tw = make_float3(b[3][0], b[3][1], b[3][2]);
-    // normal = view3x3 * L[2] with L[2] = R[2] (transformVec4x3).
-    normal.x = dot3(r(S_NRM_PAIR), r(S_NRM_TAIL), view[0], rm[2][0], view[4], rm[2][1], view[8],
-                    rm[2][2]);
-    normal.y = dot3(r(S_NRM_PAIR), r(S_NRM_TAIL), view[1], rm[2][0], view[5], rm[2][1], view[9],
-                    rm[2][2]);
-    normal.z = dot3(r(S_NRM_PAIR), r(S_NRM_TAIL), view[2], rm[2][0], view[6], rm[2][1], view[10],
-                    rm[2][2]);
+    float zb[3][3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+#pragma unroll
+        for (int i = 0; i < 3; ++i) zb[c][i] = mul(b[c][i], 0.0f);
+    float t[3][3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        t[0][i] = add(mad(r(S_TN_U), b[3][i], wm, mul(b[0][i], w2)), add(zb[1][i], zb[2][i]));
+        t[1][i] = add(mad(r(S_TN_V), b[3][i], hm, mul(b[1][i], h2)), add(zb[0][i], zb[2][i]));
+        t[2][i] = add(b[3][i], add(add(zb[0][i], zb[1][i]), zb[2][i]));
+    }
+    tu = make_float3(t[0][0], t[0][1], t[0][2]);
+    tv = make_float3(t[1][0], t[1][1], t[1][2]);
+    tw = make_float3(t[2][0], t[2][1], t[2][2]);
+    // normal = view3x3 * L[2] (transformVec4x3).
+    normal.x = dot3(r(S_NRM_PAIR), r(S_NRM_TAIL), view[0], l2[0], view[4], l2[1], view[8], l2[2]);
+    normal.y = dot3(r(S_NRM_PAIR), r(S_NRM_TAIL), view[1], l2[0], view[5], l2[1], view[9], l2[2]);
+    normal.z = dot3(r(S_NRM_PAIR), r(S_NRM_TAIL), view[2], l2[0], view[6], l2[1], view[10], l2[2]);
 }
 
 }  // namespace hs

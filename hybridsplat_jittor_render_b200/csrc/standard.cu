@@ -93,6 +93,38 @@ uint64_t standard_current_bytes(const HsRasterizerContext* ctx) {
 // library reports the violation instead.
 constexpr cudaError_t kPrefilteredViolation = cudaErrorInvalidValue;
 
+cudaError_t standard_debug_copy(HsRasterizerContext* ctx, uint64_t point_capacity,
+                                float* points_xy2, float* transmats9, float* normal_opacity4) {
+    using namespace st;
+    const uint64_t points = ctx->std_last_point_count;
+    if (points > 0 && ctx->std_geometry.ptr == nullptr) return cudaErrorInvalidResourceHandle;
+    if (point_capacity < points || points_xy2 == nullptr || transmats9 == nullptr ||
+        normal_opacity4 == nullptr) {
+        return cudaErrorInvalidValue;
+    }
+    cudaError_t st = cudaDeviceSynchronize();
+    if (st != cudaSuccess || points == 0) return st;
+    std::vector<float> rec(points * kRecordQuads * 4);
+    st = cudaMemcpy(rec.data(), geometry_views(ctx->std_geometry.ptr, points).records,
+                    rec.size() * sizeof(float), cudaMemcpyDeviceToHost);
+    if (st != cudaSuccess) return st;
+    // record layout: xy, n.xy | n.z, op, c0, c1 | c2, c3, c4, Tu.x | Tu.yz, Tv.xy | Tv.z, Tw
+    for (uint64_t i = 0; i < points; ++i) {
+        const float* q = rec.data() + i * kRecordQuads * 4;
+        points_xy2[2 * i] = q[0];
+        points_xy2[2 * i + 1] = q[1];
+        normal_opacity4[4 * i] = q[2];
+        normal_opacity4[4 * i + 1] = q[3];
+        normal_opacity4[4 * i + 2] = q[4];
+        normal_opacity4[4 * i + 3] = q[5];
+        float* t = transmats9 + 9 * i;
+        t[0] = q[11]; t[1] = q[12]; t[2] = q[13];
+        t[3] = q[14]; t[4] = q[15]; t[5] = q[16];
+        t[6] = q[17]; t[7] = q[18]; t[8] = q[19];
+    }
+    return cudaSuccess;
+}
+
 cudaError_t standard_release(HsRasterizerContext* ctx) {
     cudaError_t first = cudaSuccess;
     for (DeviceBuffer* b : {&ctx->std_geometry, &ctx->std_binning, &ctx->std_image}) {
@@ -192,6 +224,7 @@ cudaError_t StandardPass::begin() {
     }
     ctx_->std_peak_bytes = std::max(ctx_->std_peak_bytes, standard_current_bytes(ctx_));
     gv_ = geometry_views(ctx_->std_geometry.ptr, count_);
+    ctx_->std_last_point_count = count_;
     geometry_scratch_ = static_cast<unsigned char*>(ctx_->std_geometry.ptr) + geometry_used;
     ranges_ = static_cast<uint2*>(ctx_->std_image.ptr);
     tile_order_ = reinterpret_cast<uint32_t*>(ranges_ + tiles_);

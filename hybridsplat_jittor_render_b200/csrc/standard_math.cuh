@@ -24,7 +24,7 @@ __host__ __device__ constexpr int pinned_site(int site) {
         case S_QN_PAIR: return 1;      // x*x fused onto the rounded w*w
         case S_R00: return 2;          // 1 - 2(y*y + z*z) with both squares rounded
         case S_AABB_D_PAIR: return 1;  // 9*Tw.y^2 fused onto the rounded 9*Tw.x^2
-        case S_AABB_P_PAIR: return 2;  // f.x*(Tu.x*Tw.x) + f.y*(...), both rounded
+        case S_AABB_PX_PAIR: return 1; // centre x: f.y*(Tu.y*Tw.y) fused onto the rounded f.x*(...)
         case S_RHO2: return 1;         // d.y*d.y fused onto the rounded d.x*d.x
         default: return 0;
     }
@@ -80,9 +80,9 @@ __device__ __forceinline__ Projected project_gaussian(const R& r, const float* v
     if (d == 0.0f) return g;
     const float inv = div(1.0f, d);
     const float fx = mul(inv, 9.0f), fy = mul(inv, 9.0f), fz = -inv;
-    const float px = dot3(r(S_AABB_P_PAIR), r(S_AABB_P_TAIL), fx, mul(g.tu.x, g.tw.x), fy,
+    const float px = dot3(r(S_AABB_PX_PAIR), r(S_AABB_P_TAIL), fx, mul(g.tu.x, g.tw.x), fy,
                           mul(g.tu.y, g.tw.y), fz, mul(g.tu.z, g.tw.z));
-    const float py = dot3(r(S_AABB_P_PAIR), r(S_AABB_P_TAIL), fx, mul(g.tv.x, g.tw.x), fy,
+    const float py = dot3(r(S_AABB_PY_PAIR), r(S_AABB_P_TAIL), fx, mul(g.tv.x, g.tw.x), fy,
                           mul(g.tv.y, g.tw.y), fz, mul(g.tv.z, g.tw.z));
     const float qx = dot3(r(S_AABB_Q_PAIR), r(S_AABB_Q_TAIL), fx, mul(g.tu.x, g.tu.x), fy,
                           mul(g.tu.y, g.tu.y), fz, mul(g.tu.z, g.tu.z));

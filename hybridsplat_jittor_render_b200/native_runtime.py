@@ -212,6 +212,7 @@ class RasterizerCallV2(ctypes.Structure):
 EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "hs_b200_precise_sh_colors5_f32_v1": (_I32, [_V, _U32, _U32, _V, _V, _V, _V, _U64, _V, *_ERR]),
     "hs_b200_precise_fuse_maps_planar_f32_v1": (_I32, [_V, _V, _V, _V, _V, _V, _U64, *_ERR]),
+    "hs_b200_standard_debug_copy_v1": (_I32, [_V, _U64, _V, _V, _V, *_ERR]),
     "hs_b200_flashgs_forward_many_v2": (_I32, [ctypes.POINTER(FlashgsCallV2), _U32, _V, *_ERR]),
     "hs_b200_rasterizer_forward_many_v2": (_I32, [ctypes.POINTER(RasterizerCallV2), _U32, _V, *_ERR]),
     "hs_b200_stage_timing_enable_v1": (_I32, [_V, _I32, *_ERR]),
@@ -432,6 +433,22 @@ class NativeRendererContext:
             self.handle, points, pairs, tiles, *[arrays[n].ctypes.data for n in names], error, len(error)
         )
         check_status(status, "hs_flashgs_debug_copy_v1", error)
+        return arrays
+
+    def standard_debug_snapshot(self, point_count: int) -> dict[str, Any]:
+        """Host copies of the last standard forward's per-Gaussian blend state
+        (centre, Tu|Tv|Tw rows, normal|opacity) for its `point_count` Gaussians;
+        rows of Gaussians with radius 0 are unspecified."""
+        import numpy as np
+
+        _torch_synchronize(self._device)
+        arrays = {"points_xy": np.empty((point_count, 2), np.float32),
+                  "transmats": np.empty((point_count, 9), np.float32),
+                  "normal_opacity": np.empty((point_count, 4), np.float32)}
+        error = error_buffer()
+        status = self._library.hs_b200_standard_debug_copy_v1(
+            self.handle, point_count, *[a.ctypes.data for a in arrays.values()], error, len(error))
+        check_status(status, "hs_b200_standard_debug_copy_v1", error)
         return arrays
 
     def close(self) -> None:

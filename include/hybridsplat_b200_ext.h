@@ -199,6 +199,18 @@ HS_API int32_t hs_b200_precise_fuse_maps_planar_f32_v1(
     float* final_rgb, float* stored_reflection, uint64_t pixel_count, char* error_text,
     uint64_t error_capacity) HS_NOEXCEPT;
 
+/* Synchronous copy of the last standard forward's per-Gaussian blend state
+ * into HOST buffers: image-space centre points_xy2[P,2], the ray-splat
+ * transform rows transmats9[P,9] (Tu, Tv, Tw, the layout of the reference's
+ * transMats, forward.cu:194-198) and normal_opacity4[P,4] (the flipped normal
+ * and the opacity, forward.cu:248). Entries of Gaussians whose radius is 0
+ * are unspecified. point_capacity must hold the last call's point count.
+ * Diagnostic only; the standard counterpart of hs_flashgs_debug_copy_v1,
+ * which the reference library has no equivalent of. */
+HS_API int32_t hs_b200_standard_debug_copy_v1(
+    HsRasterizerHandle handle, uint64_t point_capacity, float* points_xy2, float* transmats9,
+    float* normal_opacity4, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
 #ifdef __cplusplus
 }
 #endif

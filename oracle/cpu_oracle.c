@@ -121,25 +121,35 @@ static void splat_transform(const float* view, const float* proj, const float p[
     rm[2][0] = 2.0f * dot2_f(qx, qz, qw, qy);
     rm[2][1] = 2.0f * diff2_f(qy, qz, qw, qx);
     rm[2][2] = 1.0f - 2.0f * dot2_f(qx, qx, qy, qy);
+    /* GLM forms the products with the structural zeros of S, splat2world and
+     * ndc2pix too: signed zeros (NaN for an infinite factor) that decide the
+     * sign of a zero result and leave every other value unchanged. */
     const float s0 = mod * sx, s1 = mod * sy;
-    const float l0[3] = {rm[0][0] * s0, rm[0][1] * s0, rm[0][2] * s0};
-    const float l1[3] = {rm[1][0] * s1, rm[1][1] * s1, rm[1][2] * s1};
+    float l0[3], l1[3], l2[3];
+    for (int i = 0; i < 3; ++i) {
+        const float z0 = rm[0][i] * 0.0f, z1 = rm[1][i] * 0.0f, z2 = rm[2][i] * 0.0f;
+        l0[i] = rm[0][i] * s0 + z1 + z2;
+        l1[i] = z0 + rm[1][i] * s1 + z2;
+        l2[i] = z0 + z1 + rm[2][i];
+    }
     float b[4][3];
     for (int c = 0; c < 4; ++c) {
-        b[c][0] = dot3_f(l0[0], proj[c], l0[1], proj[4 + c], l0[2], proj[8 + c]);
-        b[c][1] = dot3_f(l1[0], proj[c], l1[1], proj[4 + c], l1[2], proj[8 + c]);
+        const float zp = 0.0f * proj[12 + c];
+        b[c][0] = dot3_f(l0[0], proj[c], l0[1], proj[4 + c], l0[2], proj[8 + c]) + zp;
+        b[c][1] = dot3_f(l1[0], proj[c], l1[1], proj[4 + c], l1[2], proj[8 + c]) + zp;
         b[c][2] = dot3_f(p[0], proj[c], p[1], proj[4 + c], p[2], proj[8 + c]) + proj[12 + c];
     }
     const float w2 = (float)W * 0.5f, wm = (float)(W - 1) * 0.5f;
     const float h2 = (float)H * 0.5f, hm = (float)(H - 1) * 0.5f;
     for (int i = 0; i < 3; ++i) {
-        tu[i] = fmaf(b[3][i], wm, b[0][i] * w2);
-        tv[i] = fmaf(b[3][i], hm, b[1][i] * h2);
-        tw[i] = b[3][i];
+        const float z0 = b[0][i] * 0.0f, z1 = b[1][i] * 0.0f, z2 = b[2][i] * 0.0f;
+        tu[i] = fmaf(b[3][i], wm, b[0][i] * w2) + (z1 + z2);
+        tv[i] = fmaf(b[3][i], hm, b[1][i] * h2) + (z0 + z2);
+        tw[i] = b[3][i] + ((z0 + z1) + z2);
     }
-    n[0] = dot3_f(view[0], rm[2][0], view[4], rm[2][1], view[8], rm[2][2]);
-    n[1] = dot3_f(view[1], rm[2][0], view[5], rm[2][1], view[9], rm[2][2]);
-    n[2] = dot3_f(view[2], rm[2][0], view[6], rm[2][1], view[10], rm[2][2]);
+    n[0] = dot3_f(view[0], l2[0], view[4], l2[1], view[8], l2[2]);
+    n[1] = dot3_f(view[1], l2[0], view[5], l2[1], view[9], l2[2]);
+    n[2] = dot3_f(view[2], l2[0], view[6], l2[1], view[10], l2[2]);
 }
 
 /* ---------------------------------------------------------------- FlashGS */
@@ -311,7 +321,7 @@ static void fg_blend(FgPixel* s, float px, float py, const float* g) {
     const float sx = pxv / pzv, sy = pyv / pzv;
     const float rho3d = dot2_f(sx, sx, sy, sy);
     const float dx = g[0] - px, dy = g[1] - py;
-    const float rho2d = 2.0f * dot2_f(dx, dx, dy, dy);
+    const float rho2d = 2.0f * fmaf(dy, dy, dx * dx);
     const float rho = fminf(rho3d, rho2d);
     const float depth = rho3d <= rho2d ? dot2_f(sx, g[17], sy, g[18]) + g[19] : g[19];
     const float alpha = fminf(0.99f, g[5] * expf(-0.5f * rho));
@@ -556,11 +566,14 @@ static void st_preprocess_one(int idx, const float* view, const float* proj, int
     const float cosv = -dot3_f(pvx, n[0], pvy, n[1], pvz, n[2]);
     if (cosv == 0.0f) return;
     const float sign = cosv > 0.0f ? 1.0f : -1.0f;
-    const float d = fmaf(-tw[2], tw[2], dot2_f(9.0f, tw[0] * tw[0], 9.0f, tw[1] * tw[1]));
+    /* contraction forms of the reference standard build: 9*Tw.y^2 fused onto
+     * the rounded 9*Tw.x^2; the centre's x pair fuses its second product,
+     * its y pair its first */
+    const float d = fmaf(-tw[2], tw[2], fmaf(9.0f, tw[1] * tw[1], 9.0f * (tw[0] * tw[0])));
     if (d == 0.0f) return;
     const float inv = 1.0f / d;
     const float fxv = inv * 9.0f, fyv = inv * 9.0f, fzv = -inv;
-    const float px = dot3_f(fxv, tu[0] * tw[0], fyv, tu[1] * tw[1], fzv, tu[2] * tw[2]);
+    const float px = fmaf(fzv, tu[2] * tw[2], fmaf(fyv, tu[1] * tw[1], fxv * (tu[0] * tw[0])));
     const float py = dot3_f(fxv, tv[0] * tw[0], fyv, tv[1] * tw[1], fzv, tv[2] * tw[2]);
     const float qx = dot3_f(fxv, tu[0] * tu[0], fyv, tu[1] * tu[1], fzv, tu[2] * tu[2]);
     const float qy = dot3_f(fxv, tv[0] * tv[0], fyv, tv[1] * tv[1], fzv, tv[2] * tv[2]);
@@ -604,7 +617,7 @@ static float st_blend(StPixel* s, float px, float py, const float* g) {
     const float sx = pxv / pzv, sy = pyv / pzv;
     const float rho3d = dot2_f(sx, sx, sy, sy);
     const float dx = g[0] - px, dy = g[1] - py;
-    const float rho2d = 2.0f * dot2_f(dx, dx, dy, dy);
+    const float rho2d = 2.0f * fmaf(dy, dy, dx * dx);
     const float rho = fminf(rho3d, rho2d);
     const float depth = rho3d <= rho2d ? dot2_f(sx, g[17], sy, g[18]) + g[19] : g[19];
     if (depth < 0.2f) return 0.0f;

@@ -82,3 +82,42 @@ REF_EXPORT int ref_standard_render_direct(
     const cudaError_t status = cudaDeviceSynchronize();
     return static_cast<int>(status);
 }
+
+// 3. ref_standard_preprocess_direct runs the reference preprocess kernel
+//    (vendor/standard_rasterizer/forward.cu:148-251 via FORWARD::preprocess,
+//    forward.cu:483-537) with precomputed colours and no SH, and returns its
+//    per-Gaussian state: radii, image-space centres, view depths, the 3x3
+//    ray-splat transforms (Tu, Tv, Tw rows) and normal|opacity. The caller
+//    zero-fills the outputs; entries of culled Gaussians are left as they are.
+REF_EXPORT int ref_standard_preprocess_direct(
+    int count,
+    const float* means3d,
+    const float* scales2,
+    float scale_modifier,
+    const float* rotations4,
+    const float* opacities,
+    const float* colors5,
+    const float* viewmatrix,
+    const float* projmatrix,
+    int width,
+    int height,
+    float tan_fovx,
+    float tan_fovy,
+    int32_t* radii,
+    float2* means2d,
+    float* depths,
+    float* transmats9,
+    float* rgb5,
+    float4* normal_opacity,
+    uint32_t* tiles_touched) {
+    const dim3 grid((width + 15) / 16, (height + 15) / 16, 1);
+    const float focal_y = static_cast<float>(height) / (2.0f * tan_fovy);
+    const float focal_x = static_cast<float>(width) / (2.0f * tan_fovx);
+    FORWARD::preprocess(count, 0, 0, means3d, reinterpret_cast<const glm::vec2*>(scales2), scale_modifier,
+                        reinterpret_cast<const glm::vec4*>(rotations4), opacities, nullptr, nullptr, nullptr,
+                        colors5, viewmatrix, projmatrix, nullptr, width, height, focal_x, focal_y, tan_fovx,
+                        tan_fovy, radii, means2d, depths, transmats9, rgb5, normal_opacity, grid,
+                        tiles_touched, false);
+    const cudaError_t status = cudaDeviceSynchronize();
+    return static_cast<int>(status);
+}

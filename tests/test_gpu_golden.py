@@ -13,8 +13,7 @@ import pytest
 import torch
 
 from cases import CASES
-from helpers import (DEBUG_FIELDS, FLASHGS_OUT, bits_equal, camera_args, channel_errors, fixture_inputs,
-                     within_standard_tolerance)
+from helpers import (DEBUG_FIELDS, FLASHGS_OUT, bits_equal, camera_args, channel_errors, fixture_inputs)
 from hybridsplat_jittor_render_b200 import NativeRendererContext, ops
 
 pytestmark = pytest.mark.gpu
@@ -52,7 +51,7 @@ def test_flashgs_bit_exact(golden, ctx, case, group):
 
 @pytest.mark.parametrize("case", CASE_NAMES)
 @pytest.mark.parametrize("group", ["base", "reflection"])
-def test_standard_within_tolerance(golden, ctx, case, group):
+def test_standard_bit_exact(golden, ctx, case, group):
     data = golden(case)
     inputs = fixture_inputs(data, "standard", group)
     w, h = (int(v) for v in data["camera_size"])
@@ -62,8 +61,8 @@ def test_standard_within_tolerance(golden, ctx, case, group):
     torch.cuda.synchronize()
     color, aux = out.color.cpu().numpy(), out.auxiliary.cpu().numpy()
     ref_color, ref_aux = data[f"standard_{group}_out_color"], data[f"standard_{group}_out_auxiliary"]
-    assert within_standard_tolerance(color, ref_color), channel_errors(color, ref_color)
-    assert within_standard_tolerance(aux, ref_aux), channel_errors(aux, ref_aux)
+    assert bits_equal(color, ref_color), channel_errors(color, ref_color)
+    assert bits_equal(aux, ref_aux), channel_errors(aux, ref_aux)
     assert np.array_equal(out.radii.cpu().numpy(), data[f"standard_{group}_out_radii"])
     assert int(out.rendered.item()) == int(data[f"standard_{group}_out_rendered"][0])
     # Blend weights accumulate with atomics in both libraries (order-dependent sums).

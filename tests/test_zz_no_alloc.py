@@ -16,7 +16,7 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import STANDARD_MAX_ABS, fixture_inputs, within_standard_tolerance
+from helpers import STANDARD_MAX_ABS, fixture_inputs
 from hybridsplat_jittor_render_b200 import NativeRendererContext, ops
 from hybridsplat_jittor_render_b200 import native_runtime as nr
 
@@ -65,8 +65,7 @@ def test_noalloc_matches_context_path_twice(golden, case, group):
         assert status == 0, message
         assert int(rendered.item()) == int(ref.rendered.item())
         assert torch.equal(radii, ref.radii)
-        assert within_standard_tolerance(color.cpu().numpy(), ref.color.cpu().numpy())
-        assert within_standard_tolerance(aux.cpu().numpy(), ref.auxiliary.cpu().numpy())
+        assert torch.equal(color, ref.color) and torch.equal(aux, ref.auxiliary)
         np.testing.assert_allclose(weight.cpu().numpy(), ref.weight.cpu().numpy(), rtol=1e-5,
                                    atol=STANDARD_MAX_ABS)
 
