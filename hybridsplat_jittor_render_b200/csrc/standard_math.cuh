@@ -225,7 +225,7 @@ __device__ __forceinline__ float blend(const R& r, PixelState& s, const ColumnTe
 // m and S come from the dual conic of the disc, the same construction the
 // reference uses for its cutoff-3 AABB (forward.cu:119-145) with the cutoff
 // replaced by sqrt(c). The shape is computed in double precision with c
-// widened to 1.02 c + 0.05, and quadrant rectangles are widened by one pixel,
+// widened to 1.02 c + 0.05, and quadrant rectangles are widened by kCullPad,
 // so rounding in the per-pixel arithmetic cannot make a culled evaluation
 // live. Culling therefore never changes an output value; it only skips
 // evaluations that would have returned early.
@@ -354,11 +354,18 @@ __device__ __forceinline__ BandSpans band_spans(const CullShape& c, float ya, fl
     return s;
 }
 
-// Spans of the two 8-row quadrant bands of tile row ty, widened by one pixel:
-// rows [16 ty + 8 qy - 1, 16 ty + 8 qy + 8].
+// Pixels whose evaluation can be live lie inside the culling shapes, which
+// are already widened in their threshold and scale; tiles and quadrants are
+// further widened by kCullPad pixels on each side to cover the float rounding
+// of the span arithmetic (below 1e-3 px at screen coordinates under 4e6).
+// Every bound is an integer plus or minus kCullPad, exact in float.
+constexpr float kCullPad = 0.25f;
+
+// Spans of the two 8-row quadrant bands of tile row ty, widened by kCullPad:
+// rows [16 ty + 8 qy - pad, 16 ty + 8 qy + 7 + pad].
 __device__ __forceinline__ BandSpans quadrant_band_spans(const CullShape& c, int ty, int qy) {
-    const float ya = static_cast<float>(ty * 16 + qy * 8 - 1);
-    return band_spans(c, ya, add(ya, 9.0f));
+    const float y = static_cast<float>(ty * 16 + qy * 8);
+    return band_spans(c, y - kCullPad, y + (7.0f + kCullPad));
 }
 
 __device__ __forceinline__ void hull(float al, float ar, float bl, float br, float& l, float& r) {
@@ -368,8 +375,8 @@ __device__ __forceinline__ void hull(float al, float ar, float bl, float br, flo
 }
 
 // Spans of a tile row: the hulls of its two quadrant bands' ellipse and disc
-// spans (the row, widened by one pixel, is the union of the two bands); tile
-// tx is live when [16 tx - 1, 16 tx + 16] meets one of them.
+// spans (the row, widened by kCullPad, is the union of the two bands); tile
+// tx is live when [16 tx - pad, 16 tx + 15 + pad] meets one of them.
 __device__ __forceinline__ BandSpans row_spans(const BandSpans& top, const BandSpans& bottom) {
     BandSpans s;
     hull(top.el, top.er, bottom.el, bottom.er, s.el, s.er);
@@ -377,18 +384,18 @@ __device__ __forceinline__ BandSpans row_spans(const BandSpans& top, const BandS
     return s;
 }
 
-// Tile columns [lo, hi] whose widened range [16 tx - 1, 16 tx + 16] meets
-// [l, r]: the first column with 16 lo + 16 >= l and the last with
-// 16 hi - 1 <= r, found from the quotients and corrected by those exact
+// Tile columns [lo, hi] whose widened range [16 tx - pad, 16 tx + 15 + pad]
+// meets [l, r]: the first column with 16 lo + 15 + pad >= l and the last with
+// 16 hi - pad <= r, found from the quotients and corrected by those exact
 // comparisons.
 __device__ __forceinline__ void span_columns(float l, float r, int& lo, int& hi) {
     const float lc = fminf(fmaxf(l, -4.0e6f), 4.0e6f), rc = fminf(fmaxf(r, -4.0e6f), 4.0e6f);
-    lo = static_cast<int>(ceilf(mul(sub(lc, 16.0f), 0.0625f)));
-    hi = static_cast<int>(floorf(mul(add(rc, 1.0f), 0.0625f)));
-    if (!(static_cast<float>(lo * 16 + 16) >= l)) ++lo;
-    if (static_cast<float>((lo - 1) * 16 + 16) >= l) --lo;
-    if (!(static_cast<float>(hi * 16 - 1) <= r)) --hi;
-    if (static_cast<float>((hi + 1) * 16 - 1) <= r) ++hi;
+    lo = static_cast<int>(ceilf(mul(sub(lc, 15.0f + kCullPad), 0.0625f)));
+    hi = static_cast<int>(floorf(mul(add(rc, kCullPad), 0.0625f)));
+    if (!(static_cast<float>(lo * 16) + (15.0f + kCullPad) >= l)) ++lo;
+    if (static_cast<float>((lo - 1) * 16) + (15.0f + kCullPad) >= l) --lo;
+    if (!(static_cast<float>(hi * 16) - kCullPad <= r)) --hi;
+    if (static_cast<float>((hi + 1) * 16) - kCullPad <= r) ++hi;
 }
 
 // The live tiles of one row of a clipped box [x0, x1): the columns whose
@@ -439,7 +446,8 @@ __device__ __forceinline__ uint32_t quadrant_mask(const BandSpans& top, const Ba
     uint32_t mask = 0;
 #pragma unroll
     for (int qx = 0; qx < 2; ++qx) {
-        const float x0 = static_cast<float>(tx * 16 + qx * 8 - 1), x1 = add(x0, 9.0f);
+        const float x = static_cast<float>(tx * 16 + qx * 8);
+        const float x0 = x - kCullPad, x1 = x + (7.0f + kCullPad);
         if (meets(top.el, top.er, x0, x1) || meets(top.dl, top.dr, x0, x1)) mask |= 1u << qx;
         if (meets(bottom.el, bottom.er, x0, x1) || meets(bottom.dl, bottom.dr, x0, x1))
             mask |= 1u << (2 + qx);

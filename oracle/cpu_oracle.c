@@ -842,23 +842,25 @@ static void hull_c(float al, float ar, float bl, float br, float* l, float* r) {
     *r = a && b ? fmaxf(ar, br) : (a ? ar : (b ? br : 0.0f));
 }
 
-/* Emitted? and mask of tile (tx, ty) for an ellipse-mode shape. */
+/* Emitted? and mask of tile (tx, ty) for an ellipse-mode shape. Tiles and
+ * quadrants are widened by CULL_PAD pixels on each side (csrc kCullPad). */
+#define CULL_PAD 0.25f
 static unsigned tile_mask_c(const CullC* c, int tx, int ty) {
     float s[2][4];
     for (int qy = 0; qy < 2; ++qy) {
-        const float ya = (float)(ty * 16 + qy * 8 - 1);
-        espan_c(c, ya, ya + 9.0f, &s[qy][0], &s[qy][1]);
-        dspan_c(c, ya, ya + 9.0f, &s[qy][2], &s[qy][3]);
+        const float y = (float)(ty * 16 + qy * 8);
+        espan_c(c, y - CULL_PAD, y + (7.0f + CULL_PAD), &s[qy][0], &s[qy][1]);
+        dspan_c(c, y - CULL_PAD, y + (7.0f + CULL_PAD), &s[qy][2], &s[qy][3]);
     }
     float el, er, dl, dr;
     hull_c(s[0][0], s[0][1], s[1][0], s[1][1], &el, &er);
     hull_c(s[0][2], s[0][3], s[1][2], s[1][3], &dl, &dr);
-    const float x0 = (float)(tx * 16 - 1), x1 = (float)(tx * 16 + 16);
+    const float x0 = (float)(tx * 16) - CULL_PAD, x1 = (float)(tx * 16) + (15.0f + CULL_PAD);
     if (!(meets_c(el, er, x0, x1) || meets_c(dl, dr, x0, x1))) return 0u;
     unsigned m = 0;
     for (int qy = 0; qy < 2; ++qy)
         for (int qx = 0; qx < 2; ++qx) {
-            const float a = (float)(tx * 16 + qx * 8 - 1), b = a + 9.0f;
+            const float a = (float)(tx * 16 + qx * 8) - CULL_PAD, b = (float)(tx * 16 + qx * 8) + (7.0f + CULL_PAD);
             if (meets_c(s[qy][0], s[qy][1], a, b) || meets_c(s[qy][2], s[qy][3], a, b)) m |= 1u << (qy * 2 + qx);
         }
     return m ? m : 15u;
