@@ -231,9 +231,10 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
     }
 }
 
-// Rasterisation order of the tiles: longest pair lists first (buckets by
-// the bit length of the list length; any order inside a bucket), so that the
-// persistent rasterisers take the expensive tiles before the cheap ones.
+// Rasterisation order of the tiles: longest pair lists first (buckets of an
+// eighth of an octave of the list length: its bit length and the three bits
+// below the leading one; any order inside a bucket), so that the persistent
+// rasterisers take the expensive tiles before the cheap ones.
 // One block of kOrderThreads threads over tiles [tile_first, tile_first +
 // tile_count); `counter` (the rasteriser's work counter) is reset here.
 constexpr int kOrderThreads = 1024;
@@ -242,19 +243,26 @@ template <class Range>
 __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
     uint32_t tile_first, uint32_t tile_count, const Range* __restrict__ ranges,
     uint32_t* __restrict__ order, uint32_t* __restrict__ counter) {
-    __shared__ uint32_t hist[33];
-    __shared__ uint32_t next[33];
-    if (threadIdx.x < 33) hist[threadIdx.x] = 0;
+    constexpr uint32_t kBuckets = 33u * 8u;
+    __shared__ uint32_t hist[kBuckets];
+    __shared__ uint32_t next[kBuckets];
+    // bucket 8 * clz + (7 - next three bits): ascending buckets, descending lengths
+    auto bucket = [](uint32_t len) -> uint32_t {
+        if (len == 0u) return kBuckets - 1u;
+        const uint32_t lz = __clz(len);
+        return lz * 8u + (7u - (((len << lz) << 1) >> 29));
+    };
+    for (uint32_t b = threadIdx.x; b < kBuckets; b += kOrderThreads) hist[b] = 0;
     if (threadIdx.x == 0) *counter = 0;
     __syncthreads();
     for (uint32_t t = tile_first + threadIdx.x; t < tile_first + tile_count; t += kOrderThreads) {
         const uint32_t len = static_cast<uint32_t>(ranges[t].y - ranges[t].x);
-        atomicAdd(&hist[__clz(len)], 1u);
+        atomicAdd(&hist[bucket(len)], 1u);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         uint32_t run = 0;
-        for (int b = 0; b < 33; ++b) {
+        for (uint32_t b = 0; b < kBuckets; ++b) {
             next[b] = run;
             run += hist[b];
         }
@@ -262,7 +270,7 @@ __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
     __syncthreads();
     for (uint32_t t = tile_first + threadIdx.x; t < tile_first + tile_count; t += kOrderThreads) {
         const uint32_t len = static_cast<uint32_t>(ranges[t].y - ranges[t].x);
-        order[atomicAdd(&next[__clz(len)], 1u)] = t;
+        order[atomicAdd(&next[bucket(len)], 1u)] = t;
     }
 }
 
