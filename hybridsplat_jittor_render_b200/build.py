@@ -65,6 +65,7 @@ SOURCES = [
     ("sort.cu", "cuda", []),
     ("precise.cu", "cuda", ["--fmad=false"]),
     ("precise_exp.cu", "cuda", []),
+    ("postprocess.cu", "cuda", []),
     ("c_api.cpp", "cxx", []),
     ("host_math.cpp", "cxx", []),
     ("workspace.cpp", "cxx", []),

@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "context.h"
+#include "postprocess.h"
 #include "precise.h"
 
 namespace hs {
@@ -1016,6 +1017,126 @@ int32_t hs_b200_precise_fuse_maps_planar_f32_v1(const float* base_rgb,
                                                                 stored_reflection, pixel_count,
                                                                 nullptr);
                        });
+}
+
+int32_t hs_b200_pixel_rays_f32_v1(HsRasterizerHandle handle, int32_t width, int32_t height,
+                                  const float* inverse_intrinsics3x3, const float* rotation3x3,
+                                  float* scratch_n3, float* rays_n3, char* error_text,
+                                  uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (width < 0 || height < 0) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "pixel_rays width and height must be non-negative",
+                        error_text, error_capacity);
+        }
+        const uint64_t count = static_cast<uint64_t>(width) * static_cast<uint64_t>(height);
+        if (count == 0) return ok(error_text, error_capacity);
+        if (count > static_cast<uint64_t>(INT_MAX)) {
+            return fail(HS_STATUS_RANGE_ERROR, "pixel_rays pixel count exceeds cuBLAS int range",
+                        error_text, error_capacity);
+        }
+        if (handle == nullptr || inverse_intrinsics3x3 == nullptr || rotation3x3 == nullptr ||
+            scratch_n3 == nullptr || rays_n3 == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "pixel_rays received a null buffer", error_text,
+                        error_capacity);
+        }
+        if (scratch_n3 == rays_n3) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "pixel_rays scratch must not alias the rays",
+                        error_text, error_capacity);
+        }
+        const cudaError_t prior = cudaGetLastError();
+        if (prior != cudaSuccess)
+            return cuda_failure(prior, "pixel_rays preexisting CUDA error", error_text, error_capacity);
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        if (handle->math_tf32_blas == nullptr) {
+            return fail(HS_STATUS_INTERNAL_ERROR, "pixel_rays math context is not initialized",
+                        error_text, error_capacity);
+        }
+        // depth_to_normal (math.py:360-401): pixels (x, y, 1), then
+        // camera rays = pixels @ K^-T and world rays = camera rays @ R^T, each
+        // the cuBLAS call of precise_matmul_nt_n3k3 (TF32 tensor-op math).
+        cudaError_t ce = hs::post::pixel_grid(width, height, rays_n3, nullptr);
+        if (ce != cudaSuccess) return cuda_failure(ce, "pixel_rays grid", error_text, error_capacity);
+        const float alpha = 1.0f, beta = 0.0f;
+        cublasStatus_t bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3,
+                                        static_cast<int>(count), 3, &alpha, inverse_intrinsics3x3, 3,
+                                        rays_n3, 3, &beta, scratch_n3, 3);
+        if (bs == CUBLAS_STATUS_SUCCESS) {
+            bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3,
+                             static_cast<int>(count), 3, &alpha, rotation3x3, 3, scratch_n3, 3,
+                             &beta, rays_n3, 3);
+        }
+        if (bs != CUBLAS_STATUS_SUCCESS)
+            return cublas_failure(bs, "pixel_rays cublasSgemm", error_text, error_capacity);
+        ce = cudaGetLastError();
+        if (ce != cudaSuccess) return cuda_failure(ce, "pixel_rays execution", error_text, error_capacity);
+        handle->math_matmul_calls += 2;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_b200_standard_postprocess_f32_v1(
+    int32_t width, int32_t height, const float* color5, const float* aux7, const float* rays_n3,
+    const float* origin3, const float* normal_rotation3x3, double depth_ratio, float* rgb_map3,
+    float* acc_map, float* dpt_map, float* norm_map3, float* surf_norm_map3, float* dist_map,
+    float* spec_map, float* rough_map, char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (width < 0 || height < 0) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "standard_postprocess width and height must be non-negative", error_text,
+                        error_capacity);
+        }
+        if (!std::isfinite(depth_ratio)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "standard_postprocess depth_ratio must be finite", error_text,
+                        error_capacity);
+        }
+        const uint64_t pixels = static_cast<uint64_t>(width) * static_cast<uint64_t>(height);
+        const bool present = color5 != nullptr && aux7 != nullptr && rays_n3 != nullptr &&
+                             origin3 != nullptr && normal_rotation3x3 != nullptr &&
+                             rgb_map3 != nullptr && acc_map != nullptr && dpt_map != nullptr &&
+                             norm_map3 != nullptr && surf_norm_map3 != nullptr &&
+                             dist_map != nullptr && spec_map != nullptr && rough_map != nullptr;
+        // (1 - ratio) and ratio as float32 scalars of a double ratio (math.py:440-442).
+        const float keep = static_cast<float>(1.0 - depth_ratio);
+        const float ratio = static_cast<float>(depth_ratio);
+        return elementwise("standard_postprocess", pixels, present, error_text, error_capacity, [&] {
+            const hs::post::StandardMaps maps{rgb_map3,       acc_map,  dpt_map,  norm_map3,
+                                              surf_norm_map3, dist_map, spec_map, rough_map};
+            return hs::post::standard(width, height, color5, aux7, rays_n3, origin3,
+                                      normal_rotation3x3, keep, ratio, maps, nullptr);
+        });
+    });
+}
+
+int32_t hs_b200_flashgs_postprocess_f32_v1(int32_t width, int32_t height, const float* color3,
+                                           const float* other2, const float* depth1,
+                                           const float* alpha1, const float* normal3,
+                                           const float* normal_rotation3x3, float* rgb_map3,
+                                           float* acc_map, float* dpt_map, float* norm_map3,
+                                           float* surf_norm_map3, float* dist_map,
+                                           float* spec_map, char* error_text,
+                                           uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (width < 0 || height < 0) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "flashgs_postprocess width and height must be non-negative", error_text,
+                        error_capacity);
+        }
+        const uint64_t pixels = static_cast<uint64_t>(width) * static_cast<uint64_t>(height);
+        const bool present = color3 != nullptr && other2 != nullptr && depth1 != nullptr &&
+                             alpha1 != nullptr && normal3 != nullptr &&
+                             normal_rotation3x3 != nullptr && rgb_map3 != nullptr &&
+                             acc_map != nullptr && dpt_map != nullptr && norm_map3 != nullptr &&
+                             spec_map != nullptr;
+        return elementwise("flashgs_postprocess", pixels, present, error_text, error_capacity, [&] {
+            const hs::post::FlashgsMaps maps{rgb_map3, acc_map,  dpt_map, norm_map3,
+                                             surf_norm_map3, dist_map, spec_map};
+            return hs::post::flashgs(width, height, color3, other2, depth1, alpha1, normal3,
+                                     normal_rotation3x3, maps, nullptr);
+        });
+    });
 }
 
 int32_t hs_rasterizer_precise_direction_f32_v1(const float* points, const float* center,

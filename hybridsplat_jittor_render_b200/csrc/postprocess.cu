@@ -1,0 +1,209 @@
+// Raw-map postprocess of one view: the session's per-pixel steps after the
+// raster calls, fused into one pass per backend.
+//
+// Standard backend, postprocess_raster (math.py:426-463) with depth_to_normal
+// (math.py:351-423): from color[5,H,W] and aux[7,H,W] (depth, alpha,
+// normal[3], median depth, distortion) it writes the session's flattened HWC
+// maps
+//   rgb[HW,3], acc[HW], dpt[HW], norm[HW,3], surf_norm[HW,3], dist[HW],
+//   spec[HW], rough[HW]
+// where
+//   dpt        = precise_depth_divide(depth, alpha) * (1 - ratio)
+//                + nan_to_num(median) * ratio
+//   norm       = normal @ B           (B = world_view_transform[:3,:3]^T)
+//   xyz        = dpt * ray + origin   (ray: the per-view world-space pixel rays
+//                                      from the two TF32 GEMMs of
+//                                      depth_to_normal, origin = c2w[:3,3])
+//   surf_norm  = safe_normalize((xyz[y+1]-xyz[y-1]) x (xyz[x+1]-xyz[x-1]),
+//                               eps 1e-12) * alpha, zero on the image border
+// The divide, the non-finite mappings, the ray scaling and offset and the
+// finite differences are the reference's exactly rounded operations (each a
+// separate PyTorch/Jittor kernel there). The reference leaves the contraction
+// of the 3-term normal rotation, the cross product and the squared norm to
+// Jittor's code generator; here they are written as explicitly rounded
+// products and sums (no fused multiply-add).
+//
+// FlashGS backend, _flashgs_postprocess (renderer.py:176-202): rgb, acc, dpt
+// (nan_to_num(precise_depth_divide(depth, alpha))), norm (normal @ B), spec
+// (other[0]); surf_norm and dist are zero.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "fp.cuh"
+#include "postprocess.h"
+
+namespace hs {
+namespace post {
+namespace {
+
+constexpr int kThreads = 256;
+
+// _nan_to_num_like_pytorch (math.py:331-336): NaN and +inf -> 0, -inf -> -FLT_MAX.
+__device__ __forceinline__ float nan_to_num_session(float v) {
+    const uint32_t b = __float_as_uint(v);
+    if ((b & 0x7f800000u) != 0x7f800000u) return v;
+    return ((b & 0x007fffffu) != 0u || (b & 0x80000000u) == 0u) ? 0.0f : __uint_as_float(0xff7fffffu);
+}
+
+// precise_depth_divide (ops/jittor/precise_depth_divide_op.cc): the correctly
+// rounded quotient with the same non-finite mapping.
+__device__ __forceinline__ float depth_divide(float numerator, float denominator) {
+    return nan_to_num_session(div(numerator, denominator));
+}
+
+__device__ __forceinline__ float surface_depth(const float* aux, size_t plane, size_t p,
+                                               float keep, float ratio) {
+    const float expected = depth_divide(aux[p], aux[plane + p]);
+    const float median = nan_to_num_session(aux[5 * plane + p]);
+    return add(mul(expected, keep), mul(median, ratio));
+}
+
+// xyz = depth * ray + origin of pixel q (the two rounded steps of
+// depth_to_normal, math.py:409-413).
+__device__ __forceinline__ void world_point(const float* aux, const float* rays, size_t plane,
+                                            size_t q, float keep, float ratio, const float o[3],
+                                            float out[3]) {
+    const float d = surface_depth(aux, plane, q, keep, ratio);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) out[c] = add(mul(d, rays[3 * q + c]), o[c]);
+}
+
+// n @ B for a row vector n and a row-major 3x3 B.
+__device__ __forceinline__ void rotate(const float n[3], const float* b, float out[3]) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+        out[j] = add(add(mul(n[0], b[j]), mul(n[1], b[3 + j])), mul(n[2], b[6 + j]));
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) pixel_grid_kernel(int width, int height,
+                                                              float* __restrict__ out3) {
+    const uint64_t pixels = static_cast<uint64_t>(width) * height;
+    for (uint64_t p = blockIdx.x * uint64_t(kThreads) + threadIdx.x; p < pixels;
+         p += uint64_t(gridDim.x) * kThreads) {
+        out3[3 * p] = static_cast<float>(p % width);
+        out3[3 * p + 1] = static_cast<float>(p / width);
+        out3[3 * p + 2] = 1.0f;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) standard_kernel(
+    int width, int height, const float* __restrict__ color, const float* __restrict__ aux,
+    const float* __restrict__ rays, const float* __restrict__ origin3,
+    const float* __restrict__ rotation9, float keep, float ratio, StandardMaps maps) {
+    const size_t plane = static_cast<size_t>(width) * height;
+    float b[9], o[3];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) b[k] = rotation9[k];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) o[k] = origin3[k];
+    for (size_t p = blockIdx.x * size_t(kThreads) + threadIdx.x; p < plane;
+         p += size_t(gridDim.x) * kThreads) {
+        const int x = static_cast<int>(p % width), y = static_cast<int>(p / width);
+        const float alpha = aux[plane + p];
+        const float depth = surface_depth(aux, plane, p, keep, ratio);
+        const float n[3] = {aux[2 * plane + p], aux[3 * plane + p], aux[4 * plane + p]};
+        float nr[3];
+        rotate(n, b, nr);
+        float s[3] = {0.0f, 0.0f, 0.0f};
+        if (x > 0 && y > 0 && x < width - 1 && y < height - 1) {
+            // xyz of the four neighbours, then the central differences
+            float up[3], down[3], left[3], right[3];
+            world_point(aux, rays, plane, p - width, keep, ratio, o, up);
+            world_point(aux, rays, plane, p + width, keep, ratio, o, down);
+            world_point(aux, rays, plane, p - 1, keep, ratio, o, left);
+            world_point(aux, rays, plane, p + 1, keep, ratio, o, right);
+            float dx[3], dy[3];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                dx[c] = sub(down[c], up[c]);
+                dy[c] = sub(right[c], left[c]);
+            }
+            const float cr[3] = {sub(mul(dx[1], dy[2]), mul(dx[2], dy[1])),
+                                 sub(mul(dx[2], dy[0]), mul(dx[0], dy[2])),
+                                 sub(mul(dx[0], dy[1]), mul(dx[1], dy[0]))};
+            // norm.maximum(eps) with PyTorch's NaN propagation (fmaxf would drop a NaN)
+            const float length =
+                __fsqrt_rn(add(add(mul(cr[0], cr[0]), mul(cr[1], cr[1])), mul(cr[2], cr[2])));
+            const float norm = isnan(length) ? length : fmaxf(length, 1e-12f);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) s[c] = div(cr[c], norm);
+        }
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            maps.rgb3[3 * p + c] = color[c * plane + p];
+            maps.norm3[3 * p + c] = nr[c];
+            maps.surf_norm3[3 * p + c] = mul(s[c], alpha);
+        }
+        maps.acc[p] = alpha;
+        maps.dpt[p] = depth;
+        maps.dist[p] = aux[6 * plane + p];
+        maps.spec[p] = color[3 * plane + p];
+        maps.rough[p] = color[4 * plane + p];
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) flashgs_kernel(
+    int width, int height, const float* __restrict__ color3, const float* __restrict__ other2,
+    const float* __restrict__ depth1, const float* __restrict__ alpha1,
+    const float* __restrict__ normal3, const float* __restrict__ rotation9, FlashgsMaps maps) {
+    const size_t plane = static_cast<size_t>(width) * height;
+    float b[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) b[k] = rotation9[k];
+    for (size_t p = blockIdx.x * size_t(kThreads) + threadIdx.x; p < plane;
+         p += size_t(gridDim.x) * kThreads) {
+        const float alpha = alpha1[p];
+        const float n[3] = {normal3[p], normal3[plane + p], normal3[2 * plane + p]};
+        float nr[3];
+        rotate(n, b, nr);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            maps.rgb3[3 * p + c] = color3[c * plane + p];
+            maps.norm3[3 * p + c] = nr[c];
+            if (maps.surf_norm3 != nullptr) maps.surf_norm3[3 * p + c] = 0.0f;
+        }
+        maps.acc[p] = alpha;
+        maps.dpt[p] = depth_divide(depth1[p], alpha);
+        maps.spec[p] = other2[p];
+        if (maps.dist != nullptr) maps.dist[p] = 0.0f;
+    }
+}
+
+unsigned grid_for(uint64_t items) {
+    const uint64_t blocks = (items + kThreads - 1) / kThreads;
+    return static_cast<unsigned>(blocks < 148u * 16u ? (blocks > 0 ? blocks : 1) : 148u * 16u);
+}
+
+}  // namespace
+
+cudaError_t pixel_grid(int width, int height, float* out3, cudaStream_t s) {
+    const uint64_t pixels = static_cast<uint64_t>(width) * height;
+    if (pixels == 0) return cudaSuccess;
+    pixel_grid_kernel<<<grid_for(pixels), kThreads, 0, s>>>(width, height, out3);
+    return cudaGetLastError();
+}
+
+cudaError_t standard(int width, int height, const float* color5, const float* aux7,
+                     const float* rays3, const float* origin3, const float* rotation9, float keep,
+                     float ratio, const StandardMaps& maps, cudaStream_t s) {
+    const uint64_t pixels = static_cast<uint64_t>(width) * height;
+    if (pixels == 0) return cudaSuccess;
+    standard_kernel<<<grid_for(pixels), kThreads, 0, s>>>(width, height, color5, aux7, rays3,
+                                                          origin3, rotation9, keep, ratio, maps);
+    return cudaGetLastError();
+}
+
+cudaError_t flashgs(int width, int height, const float* color3, const float* other2,
+                    const float* depth1, const float* alpha1, const float* normal3,
+                    const float* rotation9, const FlashgsMaps& maps, cudaStream_t s) {
+    const uint64_t pixels = static_cast<uint64_t>(width) * height;
+    if (pixels == 0) return cudaSuccess;
+    flashgs_kernel<<<grid_for(pixels), kThreads, 0, s>>>(width, height, color3, other2, depth1,
+                                                         alpha1, normal3, rotation9, maps);
+    return cudaGetLastError();
+}
+
+}  // namespace post
+}  // namespace hs

@@ -16,6 +16,7 @@ import math
 from collections.abc import Sequence
 from typing import Any, NamedTuple
 
+import numpy as np
 import torch
 
 from . import native_runtime
@@ -545,3 +546,127 @@ def precise_disk_rotation(rotation_wxyz: torch.Tensor, *, library: ctypes.CDLL |
     out = torch.empty((count, 3, 3), dtype=torch.float32, device=rotation_wxyz.device)
     _elementwise("hs_rasterizer_precise_disk_rotation_f32_v1", library, _ptr(rotation_wxyz), count, _ptr(out))
     return out
+
+
+# ---------------------------------------------------------------- postprocess
+
+
+def precise_general_inverse(matrix: torch.Tensor, *, context: NativeRendererContext) -> torch.Tensor:
+    """Inverse of a row-major 3x3 or 4x4 device matrix by the reference's LU
+    route (hs_rasterizer_precise_general_inverse_f32_v2)."""
+    n = int(matrix.shape[0])
+    _check_tensor("matrix", matrix, (n, n))
+    matrix = matrix.contiguous()
+    out = torch.empty_like(matrix)
+    error = error_buffer()
+    status = context.library.hs_rasterizer_precise_general_inverse_f32_v2(context.handle, _ptr(matrix), n,
+                                                                          _ptr(out), error, len(error))
+    check_status(status, "hs_rasterizer_precise_general_inverse_f32_v2", error)
+    return out
+
+
+def precise_matmul_nt_n3k3(left: torch.Tensor, right: torch.Tensor, *,
+                           context: NativeRendererContext) -> torch.Tensor:
+    """left[N,3] @ right[3,3]^T through the reference's TF32 cuBLAS call
+    (hs_rasterizer_precise_matmul_nt_n3k3_f32_v2)."""
+    count = int(left.shape[0])
+    _check_tensor("left", left, (count, 3))
+    _check_tensor("right", right, (3, 3))
+    left, right = left.contiguous(), right.contiguous()
+    out = torch.empty_like(left)
+    error = error_buffer()
+    status = context.library.hs_rasterizer_precise_matmul_nt_n3k3_f32_v2(context.handle, _ptr(left), _ptr(right),
+                                                                        count, _ptr(out), error, len(error))
+    check_status(status, "hs_rasterizer_precise_matmul_nt_n3k3_f32_v2", error)
+    return out
+
+
+def session_focal_from_fov(length: int, fov: float) -> np.float32:
+    """The session's FP32 focal length from a field of view (math.py:339-348)."""
+    fov32 = np.float32(fov)
+    half = np.divide(fov32, np.float32(2.0), dtype=np.float32)
+    denominator = np.float32(2.0 * math.tan(float(half)))
+    return np.divide(np.float32(length), denominator, dtype=np.float32)
+
+
+def postprocess_camera(width: int, height: int, fov_x: float, fov_y: float, world_view_transform: torch.Tensor, *,
+                       context: NativeRendererContext) -> dict[str, torch.Tensor]:
+    """The per-view matrices of the standard postprocess (math.py:354-401,
+    426-433) on the device: the inverse intrinsics, the camera-to-world
+    rotation and origin, and the normal rotation world_view_transform[:3,:3]^T.
+    world_view_transform is the [4,4] matrix as the session stores it."""
+    _check_tensor("world_view_transform", world_view_transform, (4, 4))
+    f = np.float32
+    intrinsics = np.array([[session_focal_from_fov(width, fov_x), f(0.0), np.divide(f(width), f(2.0), dtype=f)],
+                           [f(0.0), session_focal_from_fov(height, fov_y), np.divide(f(height), f(2.0), dtype=f)],
+                           [f(0.0), f(0.0), f(1.0)]], dtype=f)
+    device = world_view_transform.device
+    inverse_intrinsics = precise_general_inverse(torch.from_numpy(intrinsics).to(device), context=context)
+    c2w = precise_general_inverse(world_view_transform.transpose(0, 1).contiguous(), context=context)
+    return {"inverse_intrinsics": inverse_intrinsics, "rotation": c2w[:3, :3].contiguous(),
+            "origin": c2w[:3, 3].contiguous(),
+            "normal_rotation": world_view_transform[:3, :3].transpose(0, 1).contiguous()}
+
+
+def pixel_rays(width: int, height: int, inverse_intrinsics: torch.Tensor, rotation: torch.Tensor, *,
+               context: NativeRendererContext, out: torch.Tensor | None = None,
+               scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """World-space rays [H*W,3] of every pixel, ((x, y, 1) @ K^-T) @ R^T with
+    the reference's TF32 GEMM for each product (hs_b200_pixel_rays_f32_v1)."""
+    _check_tensor("inverse_intrinsics", inverse_intrinsics, (3, 3))
+    _check_tensor("rotation", rotation, (3, 3))
+    f = dict(dtype=torch.float32, device=rotation.device)
+    rays = out if out is not None else torch.empty((height * width, 3), **f)
+    work = scratch if scratch is not None else torch.empty((height * width, 3), **f)
+    for name, t in (("out", rays), ("scratch", work)):
+        _check_tensor(name, t, (height * width, 3))
+    error = error_buffer()
+    status = context.library.hs_b200_pixel_rays_f32_v1(context.handle, int(width), int(height),
+                                                        _ptr(inverse_intrinsics.contiguous()),
+                                                        _ptr(rotation.contiguous()), _ptr(work), _ptr(rays),
+                                                        error, len(error))
+    check_status(status, "hs_b200_pixel_rays_f32_v1", error)
+    return rays
+
+
+STANDARD_MAPS = ("rgb_map", "acc_map", "dpt_map", "norm_map", "surf_norm_map", "dist_map", "spec_map", "rough_map")
+STANDARD_MAP_CHANNELS = (3, 1, 1, 3, 3, 1, 1, 1)
+
+
+def standard_postprocess(color: torch.Tensor, auxiliary: torch.Tensor, rays: torch.Tensor, origin: torch.Tensor,
+                         normal_rotation: torch.Tensor, *, depth_ratio: float = 0.0,
+                         library: ctypes.CDLL | None = None) -> dict[str, torch.Tensor]:
+    """postprocess_raster (math.py:426-463) of a standard raster call's
+    color[5,H,W] and auxiliary[7,H,W] in one pass
+    (hs_b200_standard_postprocess_f32_v1). Returns the session's maps, each
+    [1,H*W,C]."""
+    h, w = int(color.shape[1]), int(color.shape[2])
+    _check_tensor("color", color, (5, h, w))
+    _check_tensor("auxiliary", auxiliary, (7, h, w))
+    _check_tensor("rays", rays, (h * w, 3))
+    _check_tensor("origin", origin, (3,))
+    _check_tensor("normal_rotation", normal_rotation, (3, 3))
+    ratio = _finite("depth_ratio", depth_ratio)
+    f = dict(dtype=torch.float32, device=color.device)
+    maps = {name: torch.empty((1, h * w, c), **f) for name, c in zip(STANDARD_MAPS, STANDARD_MAP_CHANNELS)}
+    _elementwise("hs_b200_standard_postprocess_f32_v1", library, w, h, _ptr(color.contiguous()),
+                 _ptr(auxiliary.contiguous()), _ptr(rays.contiguous()), _ptr(origin.contiguous()),
+                 _ptr(normal_rotation.contiguous()), ratio, *[_ptr(maps[n]) for n in STANDARD_MAPS])
+    return maps
+
+
+def flashgs_postprocess(raster: FlashgsOutputs, normal_rotation: torch.Tensor, *,
+                        library: ctypes.CDLL | None = None) -> dict[str, torch.Tensor]:
+    """_flashgs_postprocess (renderer.py:176-202) of a FlashGS forward in one
+    pass (hs_b200_flashgs_postprocess_f32_v1); maps are [1,H*W,C]."""
+    h, w = int(raster.alpha.shape[1]), int(raster.alpha.shape[2])
+    _check_tensor("normal_rotation", normal_rotation, (3, 3))
+    f = dict(dtype=torch.float32, device=raster.alpha.device)
+    names = ("rgb_map", "acc_map", "dpt_map", "norm_map", "surf_norm_map", "dist_map", "spec_map")
+    channels = (3, 1, 1, 3, 3, 1, 1)
+    maps = {n: torch.empty((1, h * w, c), **f) for n, c in zip(names, channels)}
+    _elementwise("hs_b200_flashgs_postprocess_f32_v1", library, w, h, _ptr(raster.color.contiguous()),
+                 _ptr(raster.other.contiguous()), _ptr(raster.depth.contiguous()), _ptr(raster.alpha.contiguous()),
+                 _ptr(raster.normal.contiguous()), _ptr(normal_rotation.contiguous()),
+                 *[_ptr(maps[n]) for n in names])
+    return maps

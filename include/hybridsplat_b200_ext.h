@@ -211,6 +211,52 @@ HS_API int32_t hs_b200_standard_debug_copy_v1(
     HsRasterizerHandle handle, uint64_t point_capacity, float* points_xy2, float* transmats9,
     float* normal_opacity4, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
 
+/* World-space pixel rays of one view, the first half of the standard
+ * session's depth_to_normal (math.py:351-401): rays_n3[H*W,3] =
+ * ((x, y, 1) @ inverse_intrinsics3x3^T) @ rotation3x3^T for every pixel in
+ * row-major order, each product the cuBLAS call of
+ * hs_rasterizer_precise_matmul_nt_n3k3_f32_v2 (TF32 tensor-op math on the
+ * handle's math context), so the rays equal the reference session's.
+ * inverse_intrinsics3x3 is the inverse intrinsic matrix and rotation3x3 the
+ * camera-to-world rotation c2w[:3,:3], both row-major device matrices (the
+ * outputs of hs_rasterizer_precise_general_inverse_f32_v2). scratch_n3 is a
+ * device buffer of H*W*3 floats distinct from rays_n3. Legacy default stream. */
+HS_API int32_t hs_b200_pixel_rays_f32_v1(
+    HsRasterizerHandle handle, int32_t width, int32_t height, const float* inverse_intrinsics3x3,
+    const float* rotation3x3, float* scratch_n3, float* rays_n3, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+
+/* The standard session's raw-map postprocess of one view in one pass
+ * (postprocess_raster, math.py:426-463, with depth_to_normal): from the raster
+ * call's color5[5,H,W] and aux7[7,H,W], the pixel rays of
+ * hs_b200_pixel_rays_f32_v1, origin3 = c2w[:3,3] and normal_rotation3x3 =
+ * world_view_transform[:3,:3]^T (row-major), it writes the flattened HWC maps
+ * rgb_map3[H*W,3], acc_map, dpt_map (precise depth divide blended with the
+ * median by depth_ratio), norm_map3 (normal @ normal_rotation3x3),
+ * surf_norm_map3 (normalised cross product of the central differences of the
+ * depth-scaled rays, times alpha, zero on the border), dist_map, spec_map and
+ * rough_map ([H*W] each). All pointers are device pointers; legacy default
+ * stream. No counterpart in the reference library (the session runs these
+ * steps as separate framework kernels). */
+HS_API int32_t hs_b200_standard_postprocess_f32_v1(
+    int32_t width, int32_t height, const float* color5, const float* aux7, const float* rays_n3,
+    const float* origin3, const float* normal_rotation3x3, double depth_ratio, float* rgb_map3,
+    float* acc_map, float* dpt_map, float* norm_map3, float* surf_norm_map3, float* dist_map,
+    float* spec_map, float* rough_map, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
+/* The FlashGS session's raw-map postprocess (_flashgs_postprocess,
+ * renderer.py:176-202) in one pass: from a FlashGS forward's color3, other2,
+ * depth1, alpha1 and normal3 planes it writes rgb_map3[H*W,3], acc_map,
+ * dpt_map (precise depth divide with the session's non-finite mapping),
+ * norm_map3 (normal @ normal_rotation3x3) and spec_map (other[0]);
+ * surf_norm_map3 and dist_map, when not null, are zero-filled. All pointers
+ * are device pointers; legacy default stream. */
+HS_API int32_t hs_b200_flashgs_postprocess_f32_v1(
+    int32_t width, int32_t height, const float* color3, const float* other2, const float* depth1,
+    const float* alpha1, const float* normal3, const float* normal_rotation3x3, float* rgb_map3,
+    float* acc_map, float* dpt_map, float* norm_map3, float* surf_norm_map3, float* dist_map,
+    float* spec_map, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
 #ifdef __cplusplus
 }
 #endif

@@ -200,10 +200,19 @@ def test_prepare_host_empty_and_null(lib):
     ("hs_b200_precise_sh_colors5_f32_v1", (None, 8, 3, None, None, None, None, 10, None), 3),
     ("hs_b200_precise_fuse_maps_planar_f32_v1", (None, None, None, None, None, None, 0), 0),
     ("hs_b200_precise_fuse_maps_planar_f32_v1", (None, None, None, None, None, None, 10), 1),
+    ("hs_b200_standard_postprocess_f32_v1", (0, 7, *[None] * 5, 0.0, *[None] * 8), 0),
+    ("hs_b200_standard_postprocess_f32_v1", (4, 3, *[None] * 5, 0.0, *[None] * 8), 1),
+    ("hs_b200_standard_postprocess_f32_v1", (-1, 3, *[None] * 5, 0.0, *[None] * 8), 1),
+    ("hs_b200_standard_postprocess_f32_v1", (4, 3, *[None] * 5, float("inf"), *[None] * 8), 1),
+    ("hs_b200_flashgs_postprocess_f32_v1", (5, 0, *[None] * 13), 0),
+    ("hs_b200_flashgs_postprocess_f32_v1", (5, 2, *[None] * 13), 1),
+    ("hs_b200_pixel_rays_f32_v1", (None, 8, 8, None, None, None, None), 1),
+    ("hs_b200_pixel_rays_f32_v1", (None, 0, 8, None, None, None, None), 0),
 ])
 def test_fused_glue_validation(lib, symbol, args, expected):
-    """Argument checks of the fused view-glue entry points, before any launch;
-    the SH checks use the messages of hs_rasterizer_precise_sh_to_rgb_f32_v1."""
+    """Argument checks of the fused view-glue and postprocess entry points,
+    before any launch (an empty image is a successful no-op); the SH checks use
+    the messages of hs_rasterizer_precise_sh_to_rgb_f32_v1."""
     err = ctypes.create_string_buffer(256)
     assert getattr(lib, symbol)(*args, err, len(err)) == expected
     if expected == 3:

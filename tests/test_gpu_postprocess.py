@@ -1,0 +1,131 @@
+"""Fused raw-map postprocess of a view.
+
+* The per-view camera matrices (inverse intrinsics, camera-to-world rotation
+  and origin) and the world-space pixel rays equal, bit for bit, those the
+  reference library's own helpers produce (its general inverse and its TF32
+  N x 3 by 3 x 3 GEMM, applied as depth_to_normal applies them).
+* The fused standard and FlashGS postprocess equal, bit for bit, the CPU
+  restatement of the sessions' operation sequence (oracle/postprocess.py) on
+  the same raster outputs and rays, for the benchmark distributions and for a
+  frame with empty (alpha 0) pixels and non-finite median depths (NaN payloads
+  aside: the GPU's quiet NaN differs from numpy's).
+
+Skipped when the reference build (oracle/_ref) is absent.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import bits_equal
+from hybridsplat_jittor_render_b200 import NativeRendererContext, ops, scenes
+from oracle import postprocess as restated
+from test_gpu_reference import flashgs_inputs, standard_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def contexts(ref_library):
+    mine, ref = NativeRendererContext(0), NativeRendererContext(0, library=ref_library)
+    yield mine, ref
+    mine.close()
+    ref.close()
+
+
+def camera_inputs(cam):
+    """width, height, FoVx, FoVy and world_view_transform as the session holds them."""
+    return (cam.width, cam.height, 2.0 * math.atan(cam.tan_fovx), 2.0 * math.atan(cam.tan_fovy),
+            torch.from_numpy(np.ascontiguousarray(cam.world_view())).cuda())
+
+
+def host(t: torch.Tensor) -> np.ndarray:
+    return t.cpu().numpy()
+
+
+def bits_equal_any_nan(a: np.ndarray, b: np.ndarray) -> bool:
+    """Bit equality with every NaN equal to every other: the GPU's quiet NaN is
+    0x7fffffff, numpy's on x86 0xffc00000."""
+    if not np.array_equal(np.isnan(a), np.isnan(b)):
+        return False
+    return bits_equal(np.where(np.isnan(a), np.float32(0), a), np.where(np.isnan(b), np.float32(0), b))
+
+
+@pytest.mark.parametrize("camera", ["generic", "orbit"])
+def test_camera_matrices_and_rays_match_reference_helpers(contexts, camera):
+    mine, ref = contexts
+    cam = scenes.generic_camera("standard_1m", 3) if camera == "generic" else scenes.orbit_camera("standard_1m", 4)
+    w, h, fov_x, fov_y, wv = camera_inputs(cam)
+    ours = ops.postprocess_camera(w, h, fov_x, fov_y, wv, context=mine)
+    theirs = ops.postprocess_camera(w, h, fov_x, fov_y, wv, context=ref)
+    for name in ours:
+        assert bits_equal(host(ours[name]), host(theirs[name])), name
+    rays = ops.pixel_rays(w, h, ours["inverse_intrinsics"], ours["rotation"], context=mine)
+    ys, xs = torch.meshgrid(torch.arange(h, dtype=torch.float32), torch.arange(w, dtype=torch.float32),
+                            indexing="ij")
+    pixels = torch.stack([xs, ys, torch.ones_like(xs)], -1).reshape(-1, 3).cuda()
+    camera_rays = ops.precise_matmul_nt_n3k3(pixels, theirs["inverse_intrinsics"], context=ref)
+    reference_rays = ops.precise_matmul_nt_n3k3(camera_rays, theirs["rotation"], context=ref)
+    torch.cuda.synchronize()
+    assert bits_equal(host(rays), host(reference_rays))
+
+
+def standard_view(ctx, group, cam):
+    inputs = standard_inputs(group, cam)
+    out = ops.rasterize_forward(*inputs, width=cam.width, height=cam.height, scale_modifier=1.0,
+                                tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy, context=ctx)
+    w, h, fov_x, fov_y, wv = camera_inputs(cam)
+    matrices = ops.postprocess_camera(w, h, fov_x, fov_y, wv, context=ctx)
+    rays = ops.pixel_rays(w, h, matrices["inverse_intrinsics"], matrices["rotation"], context=ctx)
+    return out, matrices, rays
+
+
+@pytest.mark.parametrize("ratio", [0.0, 0.3])
+def test_standard_postprocess_matches_restatement(contexts, ratio):
+    ctx = contexts[0]
+    scene = scenes.make_scene("standard_1m", scale=0.1)
+    cam = scenes.generic_camera("standard_1m", 3)
+    out, matrices, rays = standard_view(ctx, scene["base"], cam)
+    # an empty block (alpha 0, depth 0 and a non-finite median) next to the rendered pixels
+    aux = out.auxiliary.clone()
+    aux[:, 100:180, 200:330] = 0.0
+    aux[5, 100:140, 200:260] = float("nan")
+    aux[5, 140:180, 200:260] = float("-inf")
+    maps = ops.standard_postprocess(out.color, aux, rays, matrices["origin"], matrices["normal_rotation"],
+                                    depth_ratio=ratio)
+    torch.cuda.synchronize()
+    expect = restated.standard_postprocess(host(out.color), host(aux), host(rays), host(matrices["origin"]),
+                                           host(matrices["normal_rotation"]), ratio)
+    alpha = host(aux)[1]
+    assert (alpha > 0).mean() > 0.5 and (alpha == 0).any()
+    assert set(maps) == set(expect)
+    for name, value in expect.items():
+        assert bits_equal_any_nan(host(maps[name]), value), name
+    # interior surface normals are unit vectors scaled by alpha
+    surf = host(maps["surf_norm_map"]).reshape(cam.height, cam.width, 3)[1:-1, 1:-1]
+    a = alpha[1:-1, 1:-1]
+    covered = a > 0.5
+    lengths = np.linalg.norm(surf[covered].astype(np.float64), axis=-1) / a[covered]
+    assert covered.sum() > 100_000 and np.mean(np.abs(lengths - 1.0) < 1e-5) > 0.999
+
+
+def test_flashgs_postprocess_matches_restatement(contexts):
+    ctx = contexts[0]
+    group = scenes.make_scene("flashgs_1m", scale=0.1)["base"]
+    cam = scenes.generic_camera("flashgs_1m", 3)
+    out = ops.flashgs_forward(*flashgs_inputs(group), width=cam.width, height=cam.height, use_sh=True,
+                              camera_position=cam.flashgs_position, camera_rotation=cam.flashgs_rotation9,
+                              focal_x=cam.fx, focal_y=cam.fy, context=ctx)
+    w, h, fov_x, fov_y, wv = camera_inputs(cam)
+    matrices = ops.postprocess_camera(w, h, fov_x, fov_y, wv, context=ctx)
+    maps = ops.flashgs_postprocess(out, matrices["normal_rotation"])
+    torch.cuda.synchronize()
+    expect = restated.flashgs_postprocess(host(out.color), host(out.other), host(out.depth), host(out.alpha),
+                                          host(out.normal), host(matrices["normal_rotation"]))
+    assert set(maps) == set(expect)
+    for name, value in expect.items():
+        assert bits_equal(host(maps[name]), value), name
