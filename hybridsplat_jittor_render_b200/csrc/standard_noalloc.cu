@@ -22,8 +22,9 @@
 // lazy module loading it occupies device memory only once this entry point
 // has been used on a device. Its address is fetched with
 // cudaGetSymbolAddress the first time the entry point runs on each device
-// (with that device current), so a caller should make one call before any
-// phase in which the runtime must not be asked to load modules.
+// (with that device current), so a caller should make its first call on each
+// device before any stream capture and before any phase in which the runtime
+// must not be asked to load modules.
 //
 // What must start at zero: only the look-back error word at the start of the
 // array; a device array is zero when the module loads and the word is never
@@ -56,7 +57,7 @@ constexpr uint32_t kMaxPairs = 262144;
 constexpr uint32_t kMaxTiles = 4096;
 constexpr uint64_t kScratchBytes = 8ull << 20;  // 8 MiB
 
-__device__ __align__(256) unsigned char g_scratch[kScratchBytes];
+static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_lock;

@@ -66,8 +66,8 @@ HS_API int32_t hs_b200_rasterizer_forward_rows_f32_v1(
  * any allocation: no context, no cudaMalloc/cudaFree/cudaHostAlloc. Every
  * scratch buffer comes from one 8 MiB device array inside the library (its
  * address is looked up with cudaGetSymbolAddress on the first call on each
- * device, so make one call before any phase where the runtime must not load
- * modules). No counterpart in the reference library. Same arguments as
+ * device, so make that first call before any stream capture and before any
+ * phase where the runtime must not load modules). No counterpart in the reference library. Same arguments as
  * hs_rasterizer_forward_f32_v1 with a device ordinal in place of the handle,
  * same outputs. Limits: point_count <= 16384, ceil(W/16)*ceil(H/16) <= 4096
  * tiles, <= 262144 emitted (tile, Gaussian) pairs; beyond them the call
