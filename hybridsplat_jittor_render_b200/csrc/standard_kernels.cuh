@@ -417,12 +417,16 @@ __global__ void __launch_bounds__(kRenderThreads, 7) render_kernel(
                 float w = blend(r, s0, col, fy0, g);
                 w += blend(r, s1, col, fy1, g);
                 if (__any_sync(0xffffffffu, w != 0.0f)) {
-                    w = w + __shfl_xor_sync(0xffffffffu, w, 16);
-                    w = w + __shfl_xor_sync(0xffffffffu, w, 8);
-                    w = w + __shfl_xor_sync(0xffffffffu, w, 4);
-                    w = w + __shfl_xor_sync(0xffffffffu, w, 2);
-                    w = w + __shfl_xor_sync(0xffffffffu, w, 1);
-                    if (lane == 0 && w != 0.0f) atomicAdd(weight + my_ids[k], w);
+                    // The Gaussian's blend weight over the warp's 64 pixels, summed
+                    // exactly in 2^-24 fixed point by one warp reduction (each
+                    // lane's w <= 2, so the sum stays below 2^31); the per-lane
+                    // rounding (<= 2^-25) is of the order of the float atomics'
+                    // own, which make this output order-dependent in both
+                    // libraries. Only the weights use it; colours are untouched.
+                    const uint32_t sum =
+                        __reduce_add_sync(0xffffffffu, __float2uint_rn(w * 16777216.0f));
+                    if (lane == 0 && sum != 0u)
+                        atomicAdd(weight + my_ids[k], __uint2float_rn(sum) * (1.0f / 16777216.0f));
                 }
             }
             __syncwarp();
