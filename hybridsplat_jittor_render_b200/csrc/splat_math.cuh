@@ -80,7 +80,8 @@ enum Site : int {
     S_AABB_PX_PAIR,    // f . (Tu*Tw), pair (centre x)
     S_AABB_PY_PAIR,    // f . (Tv*Tw), pair (centre y)
     S_AABB_P_TAIL,     //   tail
-    S_AABB_Q_PAIR,     // f . (Tu*Tu) and f . (Tv*Tv), pair
+    S_AABB_QX_PAIR,    // f . (Tu*Tu), pair (extent x)
+    S_AABB_QY_PAIR,    // f . (Tv*Tv), pair (extent y)
     S_AABB_Q_TAIL,     //   tail
     S_AABB_H,          // p*p - q            (0: fused, 1: rounded square)
     // per-pixel blend (both backends)

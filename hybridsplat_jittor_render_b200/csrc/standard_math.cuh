@@ -25,6 +25,7 @@ __host__ __device__ constexpr int pinned_site(int site) {
         case S_R00: return 2;          // 1 - 2(y*y + z*z) with both squares rounded
         case S_AABB_D_PAIR: return 1;  // 9*Tw.y^2 fused onto the rounded 9*Tw.x^2
         case S_AABB_PX_PAIR: return 1; // centre x: f.y*(Tu.y*Tw.y) fused onto the rounded f.x*(...)
+        case S_AABB_QX_PAIR: return 1; // extent x: f.y*(Tu.y*Tu.y) fused onto the rounded f.x*(...)
         case S_RHO2: return 1;         // d.y*d.y fused onto the rounded d.x*d.x
         default: return 0;
     }
@@ -84,9 +85,9 @@ __device__ __forceinline__ Projected project_gaussian(const R& r, const float* v
                           mul(g.tu.y, g.tw.y), fz, mul(g.tu.z, g.tw.z));
     const float py = dot3(r(S_AABB_PY_PAIR), r(S_AABB_P_TAIL), fx, mul(g.tv.x, g.tw.x), fy,
                           mul(g.tv.y, g.tw.y), fz, mul(g.tv.z, g.tw.z));
-    const float qx = dot3(r(S_AABB_Q_PAIR), r(S_AABB_Q_TAIL), fx, mul(g.tu.x, g.tu.x), fy,
+    const float qx = dot3(r(S_AABB_QX_PAIR), r(S_AABB_Q_TAIL), fx, mul(g.tu.x, g.tu.x), fy,
                           mul(g.tu.y, g.tu.y), fz, mul(g.tu.z, g.tu.z));
-    const float qy = dot3(r(S_AABB_Q_PAIR), r(S_AABB_Q_TAIL), fx, mul(g.tv.x, g.tv.x), fy,
+    const float qy = dot3(r(S_AABB_QY_PAIR), r(S_AABB_Q_TAIL), fx, mul(g.tv.x, g.tv.x), fy,
                           mul(g.tv.y, g.tv.y), fz, mul(g.tv.z, g.tv.z));
     const float h0x = msub(r(S_AABB_H), px, px, qx);
     const float h0y = msub(r(S_AABB_H), py, py, qy);

@@ -567,15 +567,15 @@ static void st_preprocess_one(int idx, const float* view, const float* proj, int
     if (cosv == 0.0f) return;
     const float sign = cosv > 0.0f ? 1.0f : -1.0f;
     /* contraction forms of the reference standard build: 9*Tw.y^2 fused onto
-     * the rounded 9*Tw.x^2; the centre's x pair fuses its second product,
-     * its y pair its first */
+     * the rounded 9*Tw.x^2; the x pairs of the centre and the extent fuse
+     * their second product, the y pairs their first */
     const float d = fmaf(-tw[2], tw[2], fmaf(9.0f, tw[1] * tw[1], 9.0f * (tw[0] * tw[0])));
     if (d == 0.0f) return;
     const float inv = 1.0f / d;
     const float fxv = inv * 9.0f, fyv = inv * 9.0f, fzv = -inv;
     const float px = fmaf(fzv, tu[2] * tw[2], fmaf(fyv, tu[1] * tw[1], fxv * (tu[0] * tw[0])));
     const float py = dot3_f(fxv, tv[0] * tw[0], fyv, tv[1] * tw[1], fzv, tv[2] * tw[2]);
-    const float qx = dot3_f(fxv, tu[0] * tu[0], fyv, tu[1] * tu[1], fzv, tu[2] * tu[2]);
+    const float qx = fmaf(fzv, tu[2] * tu[2], fmaf(fyv, tu[1] * tu[1], fxv * (tu[0] * tu[0])));
     const float qy = dot3_f(fxv, tv[0] * tv[0], fyv, tv[1] * tv[1], fzv, tv[2] * tv[2]);
     const float h0x = fmaf(px, px, -qx), h0y = fmaf(py, py, -qy);
     const float hx = sqrtf(1e-4f < h0x ? h0x : 1e-4f), hy = sqrtf(1e-4f < h0y ? h0y : 1e-4f);

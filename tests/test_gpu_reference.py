@@ -215,3 +215,36 @@ def test_degenerate_gaussians_standard_within_tolerance(contexts):
         assert all(mx <= 1e-5 and mn_ <= 1e-7 for mx, mn_ in channel_errors(a, b)), channel_errors(a, b)
         assert bits_equal(mine, ref), channel_errors(a, b)
     np.testing.assert_allclose(mw, rw, rtol=1e-3, atol=1e-2)
+
+
+LARGE_FRAMES = {"large_6m": (0.2, 5), "stress_4k": (0.3, 1)}
+
+
+@pytest.mark.parametrize("name", sorted(LARGE_FRAMES))
+def test_large_and_4k_frames_bit_exact(contexts, name):
+    """The 6M-scene distribution at 1920x1080 (1.2M Gaussians) and the inflated
+    4K stress distribution at 3840x2160 (0.9M Gaussians): standard colour, aux,
+    radii and pair counts and FlashGS outputs equal the reference build's."""
+    scale, view = LARGE_FRAMES[name]
+    group = scenes.make_scene(name, scale=scale)["base"]
+    cam = scenes.generic_camera(name, view)
+    inputs = standard_inputs(group, cam)
+    outs = []
+    for ctx in contexts:
+        o = ops.rasterize_forward(*inputs, width=cam.width, height=cam.height, scale_modifier=1.0,
+                                  tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy, context=ctx)
+        torch.cuda.synchronize()
+        outs.append([t.cpu().numpy() for t in o])
+    (mc, ma, _, mr, mn), (rc, ra, _, rr, rn) = outs
+    assert bits_equal(mc, rc) and bits_equal(ma, ra), (channel_errors(mc, rc), channel_errors(ma, ra))
+    assert np.array_equal(mr, rr) and np.array_equal(mn, rn)
+    fg = flashgs_inputs(group)
+    fouts = []
+    for ctx in contexts:
+        o = ops.flashgs_forward(*fg, width=cam.width, height=cam.height, use_sh=True,
+                                camera_position=cam.flashgs_position, camera_rotation=cam.flashgs_rotation9,
+                                focal_x=cam.fx, focal_y=cam.fy, context=ctx)
+        torch.cuda.synchronize()
+        fouts.append([t.cpu().numpy() for t in o])
+    for i, label in enumerate((*FLASHGS_OUT, "rendered")):
+        assert bits_equal(fouts[0][i], fouts[1][i]), label
