@@ -2,7 +2,8 @@
 
 The benchmark scene (1M base + 200k reflection Gaussians, 1292x839) is
 rendered by both libraries through the same C ABI on identical device
-inputs, from a generic rolled camera and an orbit camera. FlashGS must be
+inputs, from a generic rolled camera and an orbit camera; the 6M-scene and
+4K stress distributions are compared at their own resolutions. FlashGS must be
 bit-identical in every output map, preprocess field, sorted pair and tile
 range. The standard backend must be bit-identical in its colour and
 auxiliary maps, radii and pair count, and in every visible Gaussian's centre,
