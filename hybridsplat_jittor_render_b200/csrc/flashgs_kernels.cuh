@@ -35,7 +35,9 @@ __device__ __forceinline__ float4 f4(float a, float b, float c, float d) {
 constexpr int kSerialTiles = 4;
 
 template <class R>
-__global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
+// 12 blocks per SM (40 registers, a few spills): the kernel waits on its
+// input loads, and the extra resident warps hide more of that latency.
+__global__ void __launch_bounds__(kPreThreads, 12) preprocess_kernel(
     int point_count, Camera cam, const float* __restrict__ positions,
     const float* __restrict__ shs, const float* __restrict__ colors, int use_sh,
     const float* __restrict__ opacities, const float* __restrict__ cov6,
