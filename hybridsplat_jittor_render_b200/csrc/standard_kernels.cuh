@@ -228,7 +228,7 @@ __device__ __forceinline__ CullShape load_cull_shape(const float4* cull, uint32_
     return s;
 }
 
-constexpr int kEmitRowThreads = 256;
+constexpr int kEmitRowThreads = 128;
 
 static __global__ void __launch_bounds__(kEmitRowThreads) emit_rows_kernel(
     uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
