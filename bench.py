@@ -15,15 +15,24 @@ the reference and is timed separately there); its [P,3] colour output is a
 fixed synthetic input of the reflection raster.
 
 Output: one JSON line on rank 0 (driver contract). `value` is whole-job
-frames per second with device-resident inputs; `e2e` adds the per-frame
+frames per second with device-resident inputs, the median over repeated
+timed loops of exactly --steps steps each; `e2e` adds the per-frame
 host->device camera upload and the device->host read of the raw maps the
 session fetches (rgb, acc, depth, normal, spec, diffuse, reflection).
+`blocks` carries the other benchmark configurations measured by the same
+run: the FlashGS 20-view orbit (`flashgs`), the 6M + 1M 1920x1080 scene
+view-sharded over the GPUs (`large_6m`) and the 3840x2160 stress frame split
+into tile-row strips across the GPUs (`stress_4k`), each with the reference
+CUDA backend rebuilt for sm_100 on one GPU beside it.
 
 --impl reference times the reference's CPU-side path as restated by the CPU
-oracle (the reference has no CPU renderer) on the same workload.
-Multi-GPU (torchrun, N>1): every rank renders its own orbit views (weak
-scaling); the scene is broadcast once before timing; no collective runs
-inside the timed region.
+oracle (the reference has no CPU renderer) on the same workload, one full
+frame per step.
+Multi-GPU (torchrun, N>1): one process per GPU; the scene is broadcast once
+from rank 0 into every rank's device buffers through the library's NCCL
+communicator; every rank renders its own orbit views (weak scaling) or its
+own strip of one frame (strong scaling); no collective runs inside a timed
+region; per-step times are the max over ranks.
 """
 
 from __future__ import annotations
@@ -32,10 +41,12 @@ import argparse
 import json
 import math
 import os
+import statistics
 import subprocess
 import sys
 import tempfile
 import time
+from dataclasses import dataclass
 from pathlib import Path
 
 import numpy as np
@@ -44,14 +55,21 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "FPS @1292x839, 1M base+200k refl Gaussians, 1/2/4/8 B200; per-stage ms"
-SCENE = "standard_1m"
-# Further workloads (--workload): the large view-sharded scene and the 4K
-# stress frame sharded by tile strips; the default is the benchmark view above.
+
+
+@dataclass(frozen=True)
+class Workload:
+    scene: str
+    metric: str
+    sharding: str  # "view-sharded" (weak scaling) or "tile-strip" (strong scaling)
+
+
 WORKLOADS = {
-    "view": ("standard_1m", METRIC, "view-sharded"),
-    "large_6m": ("large_6m", "FPS @1920x1080, 6M base+1M refl Gaussians, 160-view orbit, view-sharded", "view-sharded"),
-    "stress_4k": ("stress_4k", "frames/s of one 3840x2160 frame, 3M base+500k refl (inflated scales), tile-strip sharded",
-                  "tile-strip"),
+    "view": Workload("standard_1m", METRIC, "view-sharded"),
+    "large_6m": Workload("large_6m", "FPS @1920x1080, 6M base+1M refl Gaussians, 160-view orbit, view-sharded",
+                         "view-sharded"),
+    "stress_4k": Workload("stress_4k", "frames/s of one 3840x2160 frame, 3M base+500k refl (inflated scales), "
+                          "tile-strip sharded", "tile-strip"),
 }
 SM_COUNT = 148
 # Algorithmic FP32 work of one pixel x Gaussian blend evaluation, counted
@@ -62,6 +80,11 @@ SM_COUNT = 148
 FLOP_STANDARD_DEAD = 39
 FLOP_STANDARD_LIVE = 76
 FLOP_FLASHGS = 75
+# Timed loops: each times exactly --steps steps; loops repeat until both
+# bounds are met and the median loop is reported.
+HEADLINE_MIN_SECONDS, HEADLINE_MIN_REPEATS = 3.0, 10
+BLOCK_MIN_SECONDS, BLOCK_MIN_REPEATS = 1.0, 5
+MAX_REPEATS = 2000
 
 
 def parse_args():
@@ -76,6 +99,10 @@ def parse_args():
     p.add_argument("--workload", choices=tuple(WORKLOADS), default="view")
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU oracle leg")
     p.add_argument("--no-reference-gpu", action="store_true", help="skip timing the reference CUDA rebuild")
+    p.add_argument("--no-blocks", action="store_true",
+                   help="skip the flashgs / large_6m / stress_4k blocks of the default run")
+    p.add_argument("--readback", choices=("after-call", "before-call"), default="before-call",
+                   help="e2e: queue frame s-1's map read-back before or after frame s's raster calls")
     p.add_argument("--scale", type=float, default=1.0, help="Gaussian-count scale (profiling runs only)")
     p.add_argument("--profile-frames", type=int, default=0,
                    help="render this many frames untimed and exit (a short, fixed launch sequence for ncu)")
@@ -84,23 +111,126 @@ def parse_args():
     return p.parse_args()
 
 
-# --------------------------------------------------------------------------- scene
+def emit(line: dict):
+    print(json.dumps(line), flush=True)
 
-def build_scene(scale: float):
+
+def scene_counts(name: str, scale: float) -> tuple[int, int]:
     from hybridsplat_jittor_render_b200 import scenes
-    return scenes.make_scene(SCENE, scale=scale)
+    spec = scenes.SCENES[name]
+    return (max(1, int(round(spec.base.count * scale))), max(1, int(round(spec.reflection.count * scale))))
 
 
-def reflection_trace_rgb(group) -> np.ndarray:
+def workload_config(workload: Workload, backend: str, scale: float, world: int) -> dict:
+    """The `config` of a bench line; both arms print the same dict."""
+    from hybridsplat_jittor_render_b200 import scenes
+    spec = scenes.SCENES[workload.scene]
+    nb, nr = scene_counts(workload.scene, scale)
+    what = (f"one {spec.width}x{spec.height} frame per step, tile rows split across the GPUs"
+            if workload.sharding == "tile-strip" else f"one {spec.width}x{spec.height} orbit view per step per GPU")
+    return {"workload": f"{backend} backend, {nb} base + {nr} reflection Gaussians, {what}",
+            "scene": workload.scene, "backend": backend, "gaussians": [nb, nr],
+            "resolution": [spec.width, spec.height], "parallelism": f"{workload.sharding} x{world}",
+            "l2": "inputs larger than L2"}
+
+
+def reflection_trace_rgb(count: int) -> np.ndarray:
     """Synthetic stand-in for the OptiX trace colour of the reflection Gaussians."""
     rng = np.random.default_rng(99)
-    return rng.random((group["xyz"].shape[0], 3)).astype(np.float32)
+    return rng.random((count, 3), dtype=np.float32)
 
+
+# --------------------------------------------------------------------------- multi-rank plumbing
+
+class Job:
+    """This process's rank: device, NCCL communicator (library), max over ranks."""
+
+    def __init__(self):
+        import torch
+        from hybridsplat_jittor_render_b200 import multigpu
+        info = multigpu.rank_info()
+        self.rank, self.world, self.local_rank = info.rank, info.world_size, info.local_rank
+        torch.cuda.set_device(self.local_rank)
+        self.device = torch.device("cuda", self.local_rank)
+        self.comm = multigpu.communicator(self.local_rank, timeout_s=300.0)
+
+    @property
+    def is_root(self) -> bool:
+        return self.rank == 0
+
+    def barrier(self):
+        self.comm.barrier()
+
+    def max(self, *values: float) -> list[float]:
+        return self.comm.allreduce_max(list(values))
+
+    def close(self):
+        self.comm.close()
+
+
+SCENE_FIELDS = (("xyz", 3), ("features_dc", 3), ("features_rest", 45), ("scaling", 2), ("rotation", 4),
+                ("opacity", 1), ("specular", 1), ("roughness", 1))
+FLASHGS_FIELDS = (("opacity", 1), ("covariance", 6), ("scaling", 2), ("rotation", 4), ("specular", 1),
+                  ("roughness", 1))
+
+
+def scene_layout(name: str, scale: float, flashgs: bool):
+    from hybridsplat_jittor_render_b200 import multigpu
+    shapes = []
+    for group, n in zip(("base", "reflection"), scene_counts(name, scale)):
+        shapes += [(f"{group}/{f}", (n, w)) for f, w in SCENE_FIELDS]
+        if flashgs:
+            shapes += [(f"{group}/fg_{f}", (n, w)) for f, w in FLASHGS_FIELDS]
+    shapes.append(("reflection/trace_rgb", (scene_counts(name, scale)[1], 3)))
+    return multigpu.PackedLayout.of(shapes)
+
+
+class DeviceScene:
+    """The scene's arrays in one device buffer, filled on rank 0 from the
+    seeded generator (plus the FlashGS host activation when asked for) and
+    broadcast once to every rank; `host` keeps rank 0's numpy copy."""
+
+    def __init__(self, job: Job, name: str, scale: float, flashgs: bool):
+        import torch
+        from hybridsplat_jittor_render_b200 import ops, scenes
+        self.name = name
+        self.counts = scene_counts(name, scale)
+        layout = scene_layout(name, scale, flashgs)
+        self.flat = torch.empty(layout.total, dtype=torch.float32, device=job.device)
+        self.host = None
+        if job.is_root:
+            raw = scenes.make_scene(name, scale=scale)
+            arrays = {}
+            for group in ("base", "reflection"):
+                g = raw[group]
+                n = g["xyz"].shape[0]
+                for f, w in SCENE_FIELDS:
+                    arrays[f"{group}/{f}"] = g[f].reshape(n, w)
+                if flashgs:
+                    pr = ops.flashgs_prepare_host(g["opacity"], g["scaling"], g["rotation"], g["specular"],
+                                                  g["roughness"])
+                    for f, w in FLASHGS_FIELDS:
+                        arrays[f"{group}/fg_{f}"] = pr[f].reshape(n, w)
+            arrays["reflection/trace_rgb"] = reflection_trace_rgb(self.counts[1])
+            staging = torch.empty(layout.total, dtype=torch.float32, pin_memory=True)
+            layout.pack(arrays, staging.numpy())
+            self.flat.copy_(staging, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            self.host = raw
+        job.comm.broadcast_buffer(self.flat, stream=torch.cuda.current_stream().cuda_stream)
+        self.views = layout.views(self.flat)
+
+    def group(self, group: str) -> dict:
+        pre = group + "/"
+        return {k[len(pre):]: v for k, v in self.views.items() if k.startswith(pre)}
+
+
+# --------------------------------------------------------------------------- the view
 
 class Frame:
     """Device-resident state and the per-view render sequence."""
 
-    def __init__(self, scene, backend: str, device, library=None, concurrent: bool = True):
+    def __init__(self, scene: DeviceScene, backend: str, device, library=None, concurrent: bool = True):
         import torch
         from hybridsplat_jittor_render_b200 import NativeRendererContext, ops, scenes
         self.torch, self.ops, self.scenes = torch, ops, scenes
@@ -110,39 +240,37 @@ class Frame:
         # sequential ones share one, as the reference session does.
         self.concurrent = concurrent
         self.ctx_r = NativeRendererContext(device.index or 0, library=library) if concurrent else self.ctx
-        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
-        b, r = scene["base"], scene["reflection"]
-        self.nb, self.nr = b["xyz"].shape[0], r["xyz"].shape[0]
+        b, r = scene.group("base"), scene.group("reflection")
+        self.nb, self.nr = scene.counts
+
+        def sh16(g):  # [P, 16, 3], DC first
+            return torch.cat([g["features_dc"].view(-1, 1, 3), g["features_rest"].view(-1, 15, 3)], 1)
+
         # session-init activation (not timed)
-        self.r_xyz, self.r_rot_raw = t(r["xyz"]), t(r["rotation"])
-        self.r_spec = ops.precise_sigmoid(t(r["specular"]), library=library)
-        self.r_rough = ops.precise_sigmoid(t(r["roughness"]), library=library)
-        self.trace_rgb = t(reflection_trace_rgb(r))
+        self.r_xyz, self.r_rot_raw = r["xyz"], r["rotation"]
+        self.r_spec = ops.precise_sigmoid(r["specular"], library=library)
+        self.r_rough = ops.precise_sigmoid(r["roughness"], library=library)
+        self.trace_rgb = r["trace_rgb"]
         if backend == "standard":
-            self.b_xyz = t(b["xyz"])
-            self.b_sh = t(np.ascontiguousarray(scenes.sh_features(b).transpose(0, 2, 1)))
-            self.b_spec = ops.precise_sigmoid(t(b["specular"]), library=library)
-            self.b_rough = ops.precise_sigmoid(t(b["roughness"]), library=library)
-            self.b_op = ops.precise_sigmoid(t(b["opacity"]), library=library)
-            self.b_scale = ops.precise_exp(t(b["scaling"]), library=library)
-            self.b_rot = ops.precise_normalize4(t(b["rotation"]), library=library)
-            self.r_op = ops.precise_sigmoid(t(r["opacity"]), library=library)
-            self.r_scale = ops.precise_exp(t(r["scaling"]), library=library)
+            self.b_xyz = b["xyz"]
+            self.b_sh = sh16(b).transpose(1, 2).contiguous()
+            self.b_spec = ops.precise_sigmoid(b["specular"], library=library)
+            self.b_rough = ops.precise_sigmoid(b["roughness"], library=library)
+            self.b_op = ops.precise_sigmoid(b["opacity"], library=library)
+            self.b_scale = ops.precise_exp(b["scaling"], library=library)
+            self.b_rot = ops.precise_normalize4(b["rotation"], library=library)
+            self.r_op = ops.precise_sigmoid(r["opacity"], library=library)
+            self.r_scale = ops.precise_exp(r["scaling"], library=library)
             self.r_rot = ops.precise_normalize4(self.r_rot_raw, library=library)
             self.r_colors = torch.cat([self.trace_rgb, self.r_spec, self.r_rough], 1).contiguous()
             self.bg5 = torch.zeros(5, device=device)
         else:
-            def prep(g):
+            def prep(g, colors):
                 n = g["xyz"].shape[0]
-                pr = ops.flashgs_prepare_host(g["opacity"], g["scaling"], g["rotation"], g["specular"],
-                                              g["roughness"])
-                return [t(g["xyz"]), t(scenes.sh_features(g).reshape(n, 48)), None, t(pr["opacity"]),
-                        t(pr["covariance"]), t(pr["scaling"]), t(pr["rotation"]), t(pr["specular"]),
-                        t(pr["roughness"])]
-            self.b_in = prep(b)
-            self.b_in[2] = torch.zeros((self.nb, 3), device=device)
-            self.r_in = prep(r)
-            self.r_in[2] = self.trace_rgb
+                return [g["xyz"], sh16(g).reshape(n, 48).contiguous(), colors, g["fg_opacity"], g["fg_covariance"],
+                        g["fg_scaling"], g["fg_rotation"], g["fg_specular"], g["fg_roughness"]]
+            self.b_in = prep(b, torch.zeros((self.nb, 3), device=device))
+            self.r_in = prep(r, self.trace_rgb)
         # This library fuses the view's glue (direction + SH + concatenation,
         # transposes + fusion); a library with only the reference ABI runs the
         # reference session's sequence.
@@ -152,14 +280,17 @@ class Frame:
         self.split = None  # list: per raster call stage timings (instrumented pass)
         self.tile_rows = None  # (begin, end): render only this strip of tile rows
 
+    def close(self):
+        self.ctx.close()
+        if self.ctx_r is not self.ctx:
+            self.ctx_r.close()
+
     def set_camera(self, cam, upload_from=None):
         """Per-view camera state. For the standard backend the matrices are
         device tensors (uploaded from pinned host memory when given)."""
         torch = self.torch
         self.cam = cam
-        host = upload_from if upload_from is not None else torch.from_numpy(np.concatenate(
-            [cam.world_view().reshape(-1), cam.full_proj().reshape(-1),
-             self.scenes.standard_camera_center(cam)]).astype(np.float32))
+        host = upload_from if upload_from is not None else torch.from_numpy(camera_row(cam, self.scenes))
         if self.backend == "standard":
             self.cam_dev = host.to(self.device, non_blocking=True)
             self.view, self.proj, self.center = self.cam_dev[:16].view(4, 4), self.cam_dev[16:32].view(4, 4), \
@@ -173,7 +304,6 @@ class Frame:
         postprocess_raster with depth_to_normal, math.py:426-463; FlashGS:
         _flashgs_postprocess, renderer.py:176-202). `events`, when given, is a
         list of 3 CUDA events around the camera matrices and rays and the maps."""
-        import math
         ops, cam, torch = self.ops, self.cam, self.torch
         rec = (lambda i: events[i].record()) if events else (lambda i: None)
         rec(0)
@@ -222,7 +352,6 @@ class Frame:
             refl_call = dict(background=self.bg5, means3d=self.r_xyz, colors=self.r_colors, opacities=self.r_op,
                              scales=self.r_scale, rotations=self.r_rot, context=self.ctx_r, **common)
             single, many = ops.rasterize_forward, ops.rasterize_forward_many
-            center = self.center
         else:
             common = dict(width=cam.width, height=cam.height, camera_position=cam.flashgs_position,
                           camera_rotation=cam.flashgs_rotation9, focal_x=cam.fx, focal_y=cam.fy,
@@ -232,7 +361,7 @@ class Frame:
             base_call = dict(zip(names, self.b_in), use_sh=True, context=self.ctx, **common)
             refl_call = dict(zip(names, self.r_in), use_sh=False, context=self.ctx_r, **common)
             single, many = ops.flashgs_forward, ops.flashgs_forward_many
-            center = self.center
+        center = self.center
         if sequential:
             base = single(**base_call)
             rec(1)
@@ -271,21 +400,25 @@ class Frame:
             acc, depth, normal, spec = base.alpha[0], base.depth[0], base.normal, base.other[0]
         return [fused["rgb_map"], acc, depth, normal, spec, fused["dif_rgb_map"], fused["ref_rgb_map"]]
 
-    def launches_per_step(self) -> int:
+    def launches_per_step(self, width: int, height: int) -> int:
         """Kernels of this library launched by one render() call (memsets and
-        copies excluded): per raster call preprocess, totals publication, depth-sort histogram +
-        4 passes, pair offsets, emission, tile-sort histogram + passes, ranges,
-        tile order and the rasteriser; plus the elementwise kernels of the view."""
-        from hybridsplat_jittor_render_b200.scenes import SCENES
-        spec = SCENES[SCENE]
-        tiles = ((spec.width + 15) // 16) * ((spec.height + 15) // 16)
+        copies excluded): per raster call preprocess, totals publication,
+        depth-sort histogram + 4 passes, pair offsets, emission, tile-sort
+        histogram + passes, ranges, tile order, wait-status publication and the
+        rasteriser; plus the elementwise kernels of the view."""
+        tiles = ((width + 15) // 16) * ((height + 15) // 16)
         tile_passes = math.ceil(max(1, int(tiles).bit_length()) / 8)
-        per_raster = 1 + 1 + (1 + 4) + 1 + 1 + (1 + tile_passes) + 1 + 1 + 1
+        per_raster = 1 + 1 + (1 + 4) + 1 + 1 + (1 + tile_passes) + 1 + 1 + 1 + 1
         if self.fused_glue:
             extra = 1 if self.backend == "standard" else 0  # direction + SH + concatenation
         else:
             extra = 2 if self.backend == "standard" else 0  # direction + SH
         return 2 * per_raster + extra + 3  # + reflection prefix, suffix, fusion
+
+
+def camera_row(cam, scenes) -> np.ndarray:
+    return np.concatenate([cam.world_view().reshape(-1), cam.full_proj().reshape(-1),
+                           scenes.standard_camera_center(cam)]).astype(np.float32)
 
 
 # --------------------------------------------------------------------------- clocks
@@ -343,21 +476,22 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------- CPU oracle
 
-def cpu_oracle_frame(scene, backend: str, row_stride: int, threads: int) -> dict:
-    """Times the CPU oracle on the benchmark frame (view 0), sampling every
-    `row_stride`-th tile row; returns the extrapolated full-frame time and,
-    per Gaussian group, the blend evaluations by the reference's rule and
-    those that changed a pixel."""
-    from hybridsplat_jittor_render_b200 import scenes
+def cpu_oracle_frame(scene_np, name: str, backend: str, row_stride: int, threads: int) -> dict:
+    """Times the CPU oracle on orbit view 0 of scene `name`, sampling every
+    `row_stride`-th tile row (1: the whole frame); returns the frame time
+    (blending and binning of the sampled rows scaled by row_stride) and, per
+    Gaussian group, the blend evaluations by the reference's rule and those
+    that changed a pixel."""
+    from hybridsplat_jittor_render_b200 import ops, scenes
     from oracle import oracle
-    cam = scenes.orbit_camera(SCENE, 0)
-    b, r = scene["base"], scene["reflection"]
+    cam = scenes.orbit_camera(name, 0)
     total_ms = 0.0
     evals, live = {}, {}
     t0 = time.perf_counter()
     for gname in ("base", "reflection"):
-        g = scene[gname]
+        g = scene_np[gname]
         n = g["xyz"].shape[0]
+        trace = reflection_trace_rgb(scene_np["reflection"]["xyz"].shape[0])
         stats = np.zeros(5, np.float64)
         if backend == "standard":
             center = scenes.standard_camera_center(cam)
@@ -365,7 +499,7 @@ def cpu_oracle_frame(scene, backend: str, row_stride: int, threads: int) -> dict
                 d = oracle.precise_direction(g["xyz"], center)
                 rgb = oracle.precise_sh_to_rgb(np.ascontiguousarray(scenes.sh_features(g).transpose(0, 2, 1)), d, 3)
             else:
-                rgb = reflection_trace_rgb(r)
+                rgb = trace
             colors = np.concatenate([rgb, oracle.precise_sigmoid(g["specular"]), oracle.precise_sigmoid(g["roughness"])], 1)
             inputs = {"background": np.zeros(5, np.float32), "means3d": g["xyz"], "colors": colors,
                       "opacities": oracle.precise_sigmoid(g["opacity"]), "scales": oracle.precise_exp(g["scaling"]),
@@ -374,10 +508,9 @@ def cpu_oracle_frame(scene, backend: str, row_stride: int, threads: int) -> dict
             oracle.standard_forward(inputs, width=cam.width, height=cam.height, threads=threads,
                                     row_stride=row_stride, stage_ms=stats)
         else:
-            from hybridsplat_jittor_render_b200 import ops
             pr = ops.flashgs_prepare_host(g["opacity"], g["scaling"], g["rotation"], g["specular"], g["roughness"])
             inputs = {"positions": g["xyz"], "shs": scenes.sh_features(g).reshape(n, 48),
-                      "colors": reflection_trace_rgb(r) if gname == "reflection" else np.zeros((n, 3), np.float32),
+                      "colors": trace if gname == "reflection" else np.zeros((n, 3), np.float32),
                       "opacities": pr["opacity"], "covariance": pr["covariance"], "scales": pr["scaling"],
                       "rotations": pr["rotation"], "specular": pr["specular"], "roughness": pr["roughness"]}
             oracle.flashgs_forward(inputs, width=cam.width, height=cam.height, use_sh=gname == "base",
@@ -392,142 +525,243 @@ def cpu_oracle_frame(scene, backend: str, row_stride: int, threads: int) -> dict
     return {"frame_ms": total_ms, "evaluations": evals, "live": live, "wall_s": wall}
 
 
-# --------------------------------------------------------------------------- arms
+# --------------------------------------------------------------------------- reference arm
 
-def emit(line: dict):
-    print(json.dumps(line), flush=True)
-
-
-def run_reference_arm(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+def run_reference_arm(args, workload: Workload) -> int:
+    """The reference's CPU path on the host cores: the reference has no CPU
+    renderer, so each step renders one full frame (base + reflection, every
+    tile row) with the CPU oracle's restatement of the reference kernels, on
+    all host threads. Rank 0 only."""
+    from hybridsplat_jittor_render_b200 import scenes
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if int(os.environ.get("RANK", "0")) != 0:
         return 0
     threads = len(os.sched_getaffinity(0))
-    scene = build_scene(args.scale)
-    stride = 8
-    for _ in range(max(0, args.warmup) and 1):
-        cpu_oracle_frame(scene, args.backend, stride, threads)
-    times = [cpu_oracle_frame(scene, args.backend, stride, threads)["frame_ms"] for _ in range(max(1, args.steps))]
-    ms = float(np.mean(times))
+    scene = scenes.make_scene(workload.scene, scale=args.scale)
+    for _ in range(min(1, max(0, args.warmup))):
+        cpu_oracle_frame(scene, workload.scene, args.backend, 1, threads)
+    times = [cpu_oracle_frame(scene, workload.scene, args.backend, 1, threads)["frame_ms"]
+             for _ in range(max(1, args.steps))]
+    ms = float(np.median(times))
     fps = 1000.0 / ms
-    sample = (f"each step renders every {stride}th tile row of the full {args.backend} frame (all Gaussians "
-              f"preprocessed); frame time = preprocess + {stride} x (binning + blending)")
-    emit({"metric": METRIC, "value": fps, "unit": "frames/s", "n_gpus": args.gpus, "steps": args.steps,
-          "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+    sample = (f"one full {args.backend} frame (base + reflection, all tile rows) per step by the CPU oracle "
+              f"(the reference has no CPU renderer; the oracle restates its kernels), {threads} threads, "
+              f"median of {len(times)} steps after {min(1, max(0, args.warmup))} warm-up frame")
+    emit({"metric": workload.metric, "value": fps, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+          "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+          "scaling": "strong" if workload.sharding == "tile-strip" else "weak",
           "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-          "config": {"workload": f"{args.backend} backend, 1M base + 200k reflection Gaussians, 1292x839, one view",
-                     "backend": args.backend, "l2": "inputs larger than L2"},
+          "config": workload_config(workload, args.backend, args.scale, world),
           "impl": "reference",
           "cpu_baseline": {"value": fps, "unit": "frames/s", "cores": threads, "kind": "port", "sample": sample},
           "e2e": {"value": fps, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
     return 0
 
 
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
-    from hybridsplat_jittor_render_b200 import multigpu, scenes
+# --------------------------------------------------------------------------- timing helpers
 
-    info = multigpu.init_process_group("nccl") if int(os.environ.get("WORLD_SIZE", "1")) > 1 else \
-        multigpu.rank_info()
-    torch.cuda.set_device(info.local_rank)
-    device = torch.device("cuda", info.local_rank)
-    world = info.world_size
+def views_for(job: Job, name: str, sharding: str, steps: int, warmup: int) -> list[int]:
+    from hybridsplat_jittor_render_b200 import scenes
+    if sharding == "tile-strip":
+        return [0] * (warmup + steps)
+    n_views = max(scenes.SCENES[name].views, 20)
+    return [(job.rank + job.world * s) % n_views for s in range(warmup + steps)]
 
-    scene_np = build_scene(args.scale) if info.is_root else None
-    if world > 1:
-        flat = None
-        if info.is_root:
-            flat = {f"{g}/{k}": torch.from_numpy(np.ascontiguousarray(v).astype(np.float32))
-                    for g in ("base", "reflection") for k, v in scene_np[g].items()}
-        rep = multigpu.broadcast_scene(flat, src=0, device=device)
-        scene_np = {"base": {}, "reflection": {}}
-        for key, v in rep.items():
-            g, k = key.split("/")
-            scene_np[g][k] = v.cpu().numpy()
-    library = None
-    if args.profile_frames > 0 and args.profile_reference:
-        from hybridsplat_jittor_render_b200.native_runtime import bind_library
-        library = bind_library(REPO / "oracle" / "_ref" / "libref_hybridsplat.so", require_optix=False)
-    frame = Frame(scene_np, args.backend, device, library=library, concurrent=not args.sequential)
-    spec = scenes.SCENES[SCENE]
-    strips = WORKLOADS[args.workload][2] == "tile-strip"
-    if strips:
-        # one frame, rows of 16x16 tiles split across the ranks (strong scaling)
-        grid_y = (spec.height + 15) // 16
-        frame.tile_rows = multigpu.tile_strips(grid_y, world)[info.rank]
-        views = [0] * (args.warmup + args.steps)
-    else:
-        n_views = max(spec.views, 20)
-        views = [(info.rank + world * s) % n_views for s in range(args.warmup + args.steps)]
-    cams = [scenes.orbit_camera(SCENE, v) for v in views]
-    if args.profile_frames > 0:
-        for s in range(args.profile_frames):
-            frame.set_camera(cams[s % len(cams)])
-            frame.render()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.destroy_process_group()
-        return 0
 
-    # Session priming: one untimed pass over the distinct views sizes the
-    # grow-only workspaces (as a long-running session would), then W warm-up
-    # steps.
-    # The per-view camera values of every step, resident on the device before
-    # the timed region like the scene (the end-to-end pass below uploads them
-    # from pinned host memory instead).
-    cam_rows = [torch.from_numpy(np.concatenate([c.world_view().reshape(-1), c.full_proj().reshape(-1),
-                                                 scenes.standard_camera_center(c)]).astype(np.float32))
-                for c in cams]
-    device_cams = [row.to(device) for row in cam_rows]
+def prime(frame: Frame, cams, warmup: int, device_cams):
+    """Session priming: one untimed render of each distinct view sizes the
+    grow-only workspaces (as a long-running session would), then the
+    warm-up steps."""
     for cam in {id(c): c for c in cams}.values():
         frame.set_camera(cam)
         frame.render()
-    for s in range(args.warmup):
+    for s in range(warmup):
         frame.set_camera(cams[s], upload_from=device_cams[s])
         frame.render()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    frame.torch.cuda.synchronize()
+
+
+def timed_loops(job: Job, frame: Frame, cams, device_cams, warmup: int, steps: int, min_seconds: float,
+                min_repeats: int) -> dict:
+    """Repeats a timed loop of exactly `steps` steps (CUDA events on the
+    launching stream, synchronised on both sides, after a barrier) until
+    min_seconds and min_repeats are reached; returns the per-step ms of the
+    median loop, max over ranks."""
+    torch = frame.torch
     stream = torch.cuda.current_stream()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(info.local_rank) as clocks:
-        torch.cuda.synchronize()
+
+    def one_loop():
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
-        for s in range(args.steps):
-            frame.set_camera(cams[args.warmup + s], upload_from=device_cams[args.warmup + s])
+        for s in range(steps):
+            frame.set_camera(cams[warmup + s], upload_from=device_cams[warmup + s])
             frame.render()
         end.record(stream)
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ms = start.elapsed_time(end) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    fps_total = (1 if strips else world) * 1000.0 / ms
+        return start, end
 
-    # per-stage ms (instrumented pass, not the headline): the view the CPU
-    # oracle counts evaluations on (view 0), CUDA events between the frame
-    # stages plus the library's own stage events inside each raster call
+    torch.cuda.synchronize()
+    s0, e0 = one_loop()
+    torch.cuda.synchronize()
+    first = s0.elapsed_time(e0)
+    repeats = int(min(MAX_REPEATS, max(min_repeats, math.ceil(min_seconds * 1000.0 / max(first, 1e-3)))))
+    repeats = int(job.max(float(repeats))[0])  # every rank runs the same number of loops
+    job.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    events = [one_loop() for _ in range(repeats)]
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    job.barrier()
+    loops = [a.elapsed_time(b) / steps for a, b in events]
+    median = float(statistics.median(loops))
+    worst = job.max(median)[0]
+    return {"ms_per_step": worst, "repeats": repeats, "loop_ms_min": min(loops) * steps,
+            "loop_ms_max": max(loops) * steps, "timed_wall_s": wall}
+
+
+def stage_split(frame: Frame, cam, steps: int) -> dict:
+    """Per-stage ms (instrumented pass, not the headline): CUDA events between
+    the frame's stages plus the library's own stage events inside each raster
+    call, the branches sequential."""
+    torch = frame.torch
     stage_names = ("base_raster", "reflection_prepare", "reflection_raster", "fusion")
     sums = np.zeros(4)
-    view0 = scenes.orbit_camera(SCENE, 0)
     for c in {id(c): c for c in (frame.ctx, frame.ctx_r)}.values():
         c.stage_timing(True)
         c.read_stage_timing()
     frame.split = []
-    for s in range(args.steps):
+    for _ in range(steps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-        frame.set_camera(view0)
+        frame.set_camera(cam)
         frame.render(ev)
         torch.cuda.synchronize()
         sums += [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
     for c in {id(c): c for c in (frame.ctx, frame.ctx_r)}.values():
         c.stage_timing(False)
     split, frame.split = frame.split, None
-    stages = {k: float(v / args.steps) for k, v in zip(stage_names, sums)}
+    stages = {k: float(v / steps) for k, v in zip(stage_names, sums)}
+    for group in ("base", "reflection"):
+        runs = [t for g, t in split if g == group]
+        for k in ("preprocess_ms", "binning_ms", "blend_ms"):
+            stages[f"{group}_{k}"] = float(np.mean([t[k] for t in runs]))
+    return stages
+
+
+def reference_rebuild(scene: DeviceScene, backend: str, device, cams, warmup: int, steps: int):
+    """The reference's own CUDA backend compiled for sm_100 from its sources
+    (oracle/_ref), same frames (whole frames: the reference has no strip
+    entry point), same device inputs, branches sequential as in the
+    reference session, one GPU; None when the rebuild is absent."""
+    import torch
+    ref_path = REPO / "oracle" / "_ref" / "libref_hybridsplat.so"
+    if not ref_path.exists():
+        return None
+    from hybridsplat_jittor_render_b200.native_runtime import bind_library
+    ref = bind_library(ref_path, require_optix=False)
+    rframe = Frame(scene, backend, device, library=ref, concurrent=False)
+    for cam in {id(c): c for c in cams}.values():
+        rframe.set_camera(cam)
+        rframe.render()
+    for s in range(warmup):
+        rframe.set_camera(cams[s])
+        rframe.render()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(steps):
+        rframe.set_camera(cams[warmup + s])
+        rframe.render()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    rframe.close()
+    return {"value": 1000.0 / ms, "unit": "frames/s", "ms_per_step": ms,
+            "what": "the reference's own CUDA backend compiled for sm_100 from its sources (oracle/_ref), "
+                    "same frames, same device inputs, one GPU"}
+
+
+# --------------------------------------------------------------------------- blocks
+
+def run_block(job: Job, args, scene: DeviceScene, workload: Workload, backend: str) -> dict:
+    """One further benchmark configuration in the same run: timed loops,
+    stage split on view 0 and (one GPU) the reference rebuild beside it."""
+    import torch
+    from hybridsplat_jittor_render_b200 import multigpu, scenes
+    spec = scenes.SCENES[workload.scene]
+    frame = Frame(scene, backend, job.device, concurrent=not args.sequential)
+    strips = workload.sharding == "tile-strip"
+    if strips:
+        frame.tile_rows = multigpu.tile_strips((spec.height + 15) // 16, job.world)[job.rank]
+    views = views_for(job, workload.scene, workload.sharding, args.steps, args.warmup)
+    cams = [scenes.orbit_camera(workload.scene, v) for v in views]
+    device_cams = [torch.from_numpy(camera_row(c, scenes)).to(job.device) for c in cams]
+    prime(frame, cams, args.warmup, device_cams)
+    job.barrier()
+    t = timed_loops(job, frame, cams, device_cams, args.warmup, args.steps, BLOCK_MIN_SECONDS, BLOCK_MIN_REPEATS)
+    ms = t["ms_per_step"]
+    out = {"metric": workload.metric, "value": (1 if strips else job.world) * 1000.0 / ms, "unit": "frames/s",
+           "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "repeats": t["repeats"],
+           "scaling": "strong" if strips else "weak",
+           "config": workload_config(workload, backend, args.scale, job.world)}
+    if job.world == 1:
+        out["stages_ms"] = stage_split(frame, scenes.orbit_camera(workload.scene, 0), min(args.steps, 10))
+        frame.close()
+        if not args.no_reference_gpu:
+            ref = reference_rebuild(scene, backend, job.device, cams, args.warmup, args.steps)
+            if ref is not None:
+                ref["ratio"] = ref["ms_per_step"] / ms
+                out["reference_cuda_rebuild"] = ref
+    else:
+        frame.close()
+    torch.cuda.synchronize()
+    return out
+
+
+# --------------------------------------------------------------------------- our arm
+
+def run_ours(args, workload: Workload) -> int:
+    import torch
+    from hybridsplat_jittor_render_b200 import multigpu, scenes
+
+    job = Job()
+    device = job.device
+    world = job.world
+    spec = scenes.SCENES[workload.scene]
+    strips = workload.sharding == "tile-strip"
+    blocks_on = not args.no_blocks and workload.scene == "standard_1m" and args.profile_frames == 0
+    scene = DeviceScene(job, workload.scene, args.scale,
+                        flashgs=args.backend == "flashgs" or (blocks_on and workload.scene == "standard_1m"))
+    library = None
+    if args.profile_frames > 0 and args.profile_reference:
+        from hybridsplat_jittor_render_b200.native_runtime import bind_library
+        library = bind_library(REPO / "oracle" / "_ref" / "libref_hybridsplat.so", require_optix=False)
+    frame = Frame(scene, args.backend, device, library=library, concurrent=not args.sequential)
+    if strips:
+        frame.tile_rows = multigpu.tile_strips((spec.height + 15) // 16, world)[job.rank]
+    views = views_for(job, workload.scene, workload.sharding, args.steps, args.warmup)
+    cams = [scenes.orbit_camera(workload.scene, v) for v in views]
+    if args.profile_frames > 0:
+        for s in range(args.profile_frames):
+            frame.set_camera(cams[s % len(cams)])
+            frame.render()
+        torch.cuda.synchronize()
+        job.close()
+        return 0
+
+    # The per-view camera values of every step, resident on the device before
+    # the timed region like the scene (the end-to-end pass below uploads them
+    # from pinned host memory instead).
+    cam_rows = [torch.from_numpy(camera_row(c, scenes)) for c in cams]
+    device_cams = [row.to(device) for row in cam_rows]
+    prime(frame, cams, args.warmup, device_cams)
+    job.barrier()
+    with ClockSampler(job.local_rank) as clocks:
+        t = timed_loops(job, frame, cams, device_cams, args.warmup, args.steps, HEADLINE_MIN_SECONDS,
+                        HEADLINE_MIN_REPEATS)
+    ms = t["ms_per_step"]
+    fps_total = (1 if strips else world) * 1000.0 / ms
+
+    stages = stage_split(frame, scenes.orbit_camera(workload.scene, 0), args.steps)
     # the session's raw-map postprocess of the base raster (not part of the
     # headline frame: the reference rebuild has no counterpart to time)
     base = frame.render()[0]
@@ -540,25 +774,71 @@ def run_ours(args):
             post += [ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])]
     stages["postprocess_camera_rays"] = float(post[0] / args.steps)
     stages["postprocess_maps"] = float(post[1] / args.steps)
-    for group in ("base", "reflection"):
-        runs = [t for g, t in split if g == group]
-        for k in ("preprocess_ms", "binning_ms", "blend_ms"):
-            stages[f"{group}_{k}"] = float(np.mean([t[k] for t in runs]))
 
-    # end-to-end through the public API with host buffers
+    e2e = end_to_end(job, frame, cams, cam_rows, args)
+
+    line = None
+    if job.is_root:
+        line = {"metric": workload.metric, "value": fps_total, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong" if strips else "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene with the benchmark "
+                "configuration's sizes and distributions; fixed synthetic trace colours)",
+                "config": workload_config(workload, args.backend, args.scale, world),
+                "timing": {"repeats": t["repeats"], "statistic": f"median of {t['repeats']} timed loops of exactly "
+                           f"{args.steps} steps, max over ranks", "loop_ms_min": t["loop_ms_min"],
+                           "loop_ms_max": t["loop_ms_max"], "timed_wall_s": t["timed_wall_s"],
+                           "priming": "one untimed render of each timed view before the warm-up steps",
+                           "branches": "sequential v1 calls" if args.sequential else
+                                       "base and reflection rasters in one concurrent call "
+                                       "(hs_b200_*_forward_many_v2)",
+                           "stages_ms": "from a separate pass with the branches sequential, each stage alone; "
+                                        "postprocess_* (the session's raw-map postprocess of the base raster: "
+                                        "camera matrices and TF32 pixel-ray GEMMs, then the fused maps kernel) "
+                                        "is outside the headline frame"},
+                "stages_ms": stages, "clocks": clocks.summary(), "e2e": e2e,
+                "gpu_launches": frame.launches_per_step(spec.width, spec.height) * args.steps * t["repeats"]}
+    if world == 1 and line is not None:
+        # single GPU: render-kernel roofline, CPU baseline, reference CUDA rebuild
+        line.update(roofline_and_baselines(args, workload, frame, cams, scene, stages, line["clocks"], ms))
+    frame.close()
+    frame = None
+    torch.cuda.synchronize()
+
+    if blocks_on:
+        blocks = {}
+        blocks["flashgs"] = run_block(job, args, scene, WORKLOADS["view"], "flashgs")
+        blocks["flashgs"]["what"] = ("FlashGS backend, 20-view orbit of the benchmark scene (config 2): "
+                                     "base FlashGS raster with SH, reflection prepare, reflection raster, fusion")
+        del scene
+        torch.cuda.empty_cache()
+        for name in ("large_6m", "stress_4k"):
+            big = DeviceScene(job, WORKLOADS[name].scene, args.scale, flashgs=False)
+            blocks[name] = run_block(job, args, big, WORKLOADS[name], "standard")
+            del big
+            torch.cuda.empty_cache()
+        if line is not None:
+            line["blocks"] = blocks
+    job.barrier()
+    job.close()
+    if line is not None:
+        emit(line)
+    return 0
+
+
+def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
+    """The same frames through the public API with host buffers: every step
+    uploads its camera from pinned host memory and reads the seven raw maps
+    back into pinned host memory (two slots) on a copy stream."""
+    import torch
+    stream = torch.cuda.current_stream()
     pinned_cam = [row.pin_memory() for row in cam_rows]
-    # Each frame's maps go back to pinned host memory on a copy stream (two
-    # host slots, as a streaming session would double-buffer them). The copies
-    # of frame s are queued once frame s + 1's raster calls have returned, so
-    # they run under that frame's binning and rendering and never share the
-    # device-to-host link with the small pair-count readbacks the raster calls
-    # wait for.
     res = frame.render()
     host_maps = [[torch.empty(m.shape, dtype=m.dtype, pin_memory=True) for m in frame.maps_for_host(res)]
                  for _ in range(2)]
     d2h = sum(m.numel() * m.element_size() for m in host_maps[0])
-    h2d = pinned_cam[0].numel() * 4 if args.backend == "standard" else 3 * 4
-    copy_stream = torch.cuda.Stream(device=device)
+    h2d = pinned_cam[0].numel() * 4 if frame.backend == "standard" else 3 * 4
+    copy_stream = torch.cuda.Stream(device=frame.device)
 
     def read_back(s, out, done):
         copy_stream.wait_event(done)
@@ -567,9 +847,12 @@ def run_ours(args):
                 dst.copy_(src, non_blocking=True)
                 src.record_stream(copy_stream)
 
-    def e2e_run(first, count):
+    def run(first, count):
         pending = None
         for s in range(first, first + count):
+            if args.readback == "before-call" and pending is not None:
+                read_back(*pending)
+                pending = None
             frame.set_camera(cams[s], upload_from=pinned_cam[s])
             out = frame.render()
             done = torch.cuda.Event()
@@ -581,19 +864,26 @@ def run_ours(args):
         stream.wait_stream(copy_stream)
         return pending[1]
 
-    # W untimed steps of the same pipeline: the caching allocator settles the
-    # blocks that the copy stream keeps alive one frame longer.
-    e2e_run(0, args.warmup)
+    # untimed steps of the same pipeline: the caching allocator settles the
+    # blocks that the copy stream keeps alive one frame longer
+    run(0, args.warmup)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    res = e2e_run(args.warmup, args.steps)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    # The same read-back alone (last frame's maps, same pinned slots): the
-    # host link bounds the end-to-end rate when it is slower than the render.
+    loops = []
+    res = None
+    job.barrier()
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        res = run(args.warmup, args.steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        loops.append(e0.elapsed_time(e1) / args.steps)
+    job.barrier()
+    e2e_ms = job.max(float(statistics.median(loops)))[0]
+    # The host-link ceiling: the same read-back alone (last frame's maps, same
+    # pinned slots), on every rank at once.
     maps = frame.maps_for_host(res)
+    job.barrier()
     c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(copy_stream):
         c0.record(copy_stream)
@@ -603,56 +893,21 @@ def run_ours(args):
         c1.record(copy_stream)
     torch.cuda.synchronize()
     d2h_ms = c0.elapsed_time(c1) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-
-    line = None
-    if info.is_root:
-        what = (f"one {spec.width}x{spec.height} frame per step, tile rows split across the GPUs" if strips else
-                f"one {spec.width}x{spec.height} orbit view per step per GPU")
-        line = {"metric": METRIC, "value": fps_total, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "strong" if strips else "weak",
-                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded scene with the benchmark "
-                "configuration's sizes and distributions; fixed synthetic trace colours)",
-                "config": {"workload": f"{args.backend} backend, {frame.nb} base + {frame.nr} reflection Gaussians, "
-                                       f"{what}",
-                           "scene": SCENE, "backend": args.backend, "gaussians": [frame.nb, frame.nr],
-                           "l2": "inputs larger than L2",
-                           "priming": "one untimed render of each timed view before the warm-up steps",
-                           "parallelism": f"{WORKLOADS[args.workload][2]} x{world}",
-                           "branches": "sequential v1 calls" if args.sequential else
-                                       "base and reflection rasters in one concurrent call "
-                                       "(hs_b200_*_forward_many_v2)",
-                           "stages_ms": "from a separate pass with the branches sequential, each stage alone; "
-                                        "postprocess_* (the session's raw-map postprocess of the base raster: "
-                                        "camera matrices and TF32 pixel-ray GEMMs, then the fused maps kernel) "
-                                        "is outside the headline frame"},
-                "stages_ms": stages, "clocks": clocks.summary(),
-                "e2e": {"value": (1 if strips else world) * 1000.0 / e2e_ms, "unit": "frames/s",
-                        "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h,
-                        "overlap": "maps of each frame copied to pinned host memory on a copy stream while "
-                                   "the next frame bins and renders (queued after its raster calls return)",
-                        "d2h_ms_alone": d2h_ms, "d2h_gbs_alone": d2h / (d2h_ms * 1e6)},
-                "gpu_launches": frame.launches_per_step() * args.steps}
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-        if line is not None:
-            emit(line)
-        return 0
-
-    # single GPU: render-kernel roofline, CPU baseline, reference CUDA rebuild
-    line.update(roofline_and_baselines(args, frame, cams, stages, scene_np, line["clocks"]))
-    emit(line)
-    return 0
+    d2h_worst = job.max(d2h_ms)[0]
+    job.barrier()
+    value = job.world * 1000.0 / e2e_ms
+    ceiling = job.world * 1000.0 / d2h_worst
+    return {"value": value, "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "overlap": ("maps of frame s-1 copied to pinned host memory on a copy stream queued before frame s's "
+                        "raster calls" if args.readback == "before-call" else
+                        "maps of frame s-1 copied on a copy stream queued after frame s's raster calls return"),
+            "statistic": "median of 5 loops of exactly --steps steps, max over ranks",
+            "d2h_ms_alone": d2h_worst, "d2h_gbs_alone_per_gpu": d2h / (d2h_worst * 1e6),
+            "host_link_ceiling_fps": ceiling, "fraction_of_host_link_ceiling": value / ceiling}
 
 
-def roofline_and_baselines(args, frame, cams, stages, scene_np, clocks: dict) -> dict:
-    import torch
+def roofline_and_baselines(args, workload: Workload, frame: Frame, cams, scene: DeviceScene, stages: dict,
+                           clocks: dict, headline_ms: float) -> dict:
     out = {}
     peaks = {}
     peak_path = REPO / "MEASURED_PEAKS.json"
@@ -660,8 +915,8 @@ def roofline_and_baselines(args, frame, cams, stages, scene_np, clocks: dict) ->
         peaks = json.loads(peak_path.read_text())
     threads = len(os.sched_getaffinity(0))
     cpu = None
-    if not args.no_cpu_baseline:
-        cpu = cpu_oracle_frame(scene_np, args.backend, 1, threads)
+    if not args.no_cpu_baseline and workload.scene == "standard_1m":
+        cpu = cpu_oracle_frame(scene.host, workload.scene, args.backend, 1, threads)
         out["cpu_baseline"] = {"value": 1000.0 / cpu["frame_ms"], "unit": "frames/s", "cores": threads,
                                "kind": "port",
                                "sample": f"one full {args.backend} frame (base + reflection) of the benchmark "
@@ -694,44 +949,19 @@ def roofline_and_baselines(args, frame, cams, stages, scene_np, clocks: dict) ->
                                           f"{sm_mhz:.0f} MHz (measured median SM clock under load); "
                                           "MEASURED_PEAKS.json has no FP32 figure"}
     if not args.no_reference_gpu:
-        ref_path = REPO / "oracle" / "_ref" / "libref_hybridsplat.so"
-        if ref_path.exists():
-            from hybridsplat_jittor_render_b200.native_runtime import bind_library
-            ref = bind_library(ref_path, require_optix=False)
-            rframe = Frame(scene_np, args.backend, frame.device, library=ref, concurrent=False)
-            # the same session priming as ours: one untimed render of each
-            # timed view sizes the reference's grow-only workspaces
-            for cam in {id(c): c for c in cams}.values():
-                rframe.set_camera(cam)
-                rframe.render()
-            for s in range(args.warmup):
-                rframe.set_camera(cams[s])
-                rframe.render()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for s in range(args.steps):
-                rframe.set_camera(cams[args.warmup + s])
-                rframe.render()
-            e1.record()
-            torch.cuda.synchronize()
-            ref_ms = e0.elapsed_time(e1) / args.steps
-            out["reference_cuda_rebuild"] = {"value": 1000.0 / ref_ms, "unit": "frames/s", "ms_per_step": ref_ms,
-                                             "what": "the reference's own CUDA backend compiled for sm_100 from its "
-                                                     "sources, same frame, same device inputs"}
-            rframe.ctx.close()
+        ref = reference_rebuild(scene, args.backend, frame.device, cams, args.warmup, args.steps)
+        if ref is not None:
+            ref["ratio"] = ref["ms_per_step"] / headline_ms
+            out["reference_cuda_rebuild"] = ref
     return out
 
 
 def main() -> int:
-    global SCENE, METRIC
     args = parse_args()
-    SCENE, METRIC, _ = WORKLOADS[args.workload]
-    if args.workload != "view":
-        args.no_cpu_baseline = True  # the CPU oracle would take minutes at these sizes
+    workload = WORKLOADS[args.workload]
     if args.impl == "reference":
-        return run_reference_arm(args)
-    return run_ours(args)
+        return run_reference_arm(args, workload)
+    return run_ours(args, workload)
 
 
 if __name__ == "__main__":

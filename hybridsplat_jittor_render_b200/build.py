@@ -67,6 +67,7 @@ SOURCES = [
     ("precise_exp.cu", "cuda", []),
     ("postprocess.cu", "cuda", []),
     ("c_api.cpp", "cxx", []),
+    ("comm.cpp", "cxx", []),
     ("host_math.cpp", "cxx", []),
     ("workspace.cpp", "cxx", []),
 ]
@@ -124,7 +125,7 @@ def build(force: bool = False, jobs: int = 8, verbose: bool = False) -> Path:
                 print(log, file=sys.stderr)
     tmp = LIBRARY.with_suffix(".so.tmp")
     link = [nvcc, "-shared", *ARCH, *[str(o) for o in objects], "-o", str(tmp),
-            f"-L{home / 'lib64'}", "-lcudart", "-lcublas", "-lcusolver"]
+            f"-L{home / 'lib64'}", "-lcudart", "-lcublas", "-lcusolver", "-ldl"]
     _run((link, "link"))
     tmp.replace(LIBRARY)
     return LIBRARY

@@ -41,6 +41,16 @@ static __global__ void publish_totals_kernel(const uint32_t* __restrict__ totals
     __threadfence_system();
 }
 
+// Publishes a call's look-back error word (set when a bounded wait of its
+// depth sort, pair-offset scan or tile sort gave up) to mapped pinned host
+// memory, after the last of those kernels: the host reads it once binning is
+// done and fails the same call.
+static __global__ void publish_error_kernel(const uint32_t* __restrict__ error,
+                                            volatile uint32_t* host) {
+    if (threadIdx.x == 0) host[0] = *reinterpret_cast<const volatile uint32_t*>(error);
+    __threadfence_system();
+}
+
 // Allocates the mapped pinned totals block of a context: *host for the host,
 // *device for kernels.
 inline cudaError_t alloc_mapped_totals(uint32_t** host, uint32_t** device) {
@@ -76,6 +86,7 @@ static __global__ void __launch_bounds__(kScanThreads) offsets_kernel(
     uint32_t* counter = control;
     uint32_t* status = control + 64;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (sort::wait_failed(error)) return;  // the depth order is not a permutation
     if (threadIdx.x == 0) tile_slot = atomicAdd(counter, 1u);
     __syncthreads();
     const uint32_t tile = tile_slot;
@@ -185,11 +196,14 @@ __global__ void __launch_bounds__(kRangeThreads) ranges_kernel(
 // `owner` names the Gaussian within the block, so an emitter may keep work
 // shared by consecutive pairs of one Gaussian in its Cache.
 // The value of a kept pair is the Gaussian index | tag. A Gaussian never
-// writes more than its counted pairs.
+// writes more than its counted pairs. Nothing is written when a bounded wait
+// of the call has given up (first_pair is then not a valid offset table).
 template <class Emitter>
 __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
     uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
-    Emitter em, uint32_t* __restrict__ tile_ids, uint32_t* __restrict__ values) {
+    Emitter em, uint32_t* __restrict__ tile_ids, uint32_t* __restrict__ values,
+    const uint32_t* __restrict__ error) {
+    if (sort::wait_failed(error)) return;
     __shared__ typename Emitter::Shape shapes[kEmitThreads];
     __shared__ uint32_t offsets[kEmitThreads], inclusive[kEmitThreads], cursor[kEmitThreads],
         counted[kEmitThreads];

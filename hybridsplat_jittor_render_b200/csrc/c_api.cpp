@@ -87,9 +87,32 @@ int32_t cuda_failure(cudaError_t error, const char* operation, char* error_text,
         error == cudaErrorMemoryAllocation ? HS_STATUS_OUT_OF_MEMORY : HS_STATUS_CUDA_ERROR;
     std::string message(operation);
     message += ": ";
-    message += cudaGetErrorString(error);
+    if (error == hs::kWaitGaveUp) {
+        message += "a bounded device wait gave up (a sort or scan look-back, or a bulk copy, "
+                   "did not complete within its limit); the outputs of this call are invalid";
+    } else {
+        message += cudaGetErrorString(error);
+    }
     return fail(status, message, error_text, error_capacity);
 }
+
+// Makes `device` current for the lifetime of the guard and restores the
+// caller's current device afterwards (entry points without a handle must not
+// change the device later allocations of the caller land on).
+class DeviceGuard {
+public:
+    DeviceGuard() { had_ = cudaGetDevice(&previous_) == cudaSuccess; }
+    cudaError_t select(int device) { return cudaSetDevice(device); }
+    ~DeviceGuard() {
+        if (had_) cudaSetDevice(previous_);
+    }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+private:
+    int previous_ = 0;
+    bool had_ = false;
+};
 
 int32_t cublas_failure(cublasStatus_t status, const char* operation, char* error_text,
                        uint64_t error_capacity) noexcept {
@@ -1376,6 +1399,18 @@ int32_t hs_rasterizer_precise_reflection_suffix_f32_v1(const float* xyz,
 
 // ---- extensions of this library (no counterpart in the reference ABI) ----
 
+int32_t hs_b200_test_stall_lookback_v1(HsRasterizerHandle handle, uint32_t tile,
+                                       char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "handle is null", error_text, error_capacity);
+        }
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        handle->test_stall_tile = tile;
+        return ok(error_text, error_capacity);
+    });
+}
+
 int32_t hs_b200_stage_timing_enable_v1(HsRasterizerHandle handle, int32_t enable, char* error_text,
                                        uint64_t error_capacity) noexcept {
     return guard(error_text, error_capacity, [&]() -> int32_t {
@@ -1443,7 +1478,8 @@ int32_t hs_b200_rasterizer_forward_noalloc_f32_v1(
             return fail(HS_STATUS_RANGE_ERROR, "device is outside the visible CUDA device range",
                         error_text, error_capacity);
         }
-        e = cudaSetDevice(device);
+        DeviceGuard device_guard;
+        e = device_guard.select(device);
         if (e != cudaSuccess) return cuda_failure(e, "cudaSetDevice", error_text, error_capacity);
         char limit[256] = {};
         e = hs::standard_forward_noalloc(

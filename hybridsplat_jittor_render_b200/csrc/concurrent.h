@@ -1,16 +1,19 @@
 // Concurrent execution of independent raster calls.
 //
-// A raster call has one host readback (its pair totals) between preprocess
-// and binning, so a call is split into three phases that queue work without
-// waiting on anything but that readback:
+// A raster call reads back its pair totals between preprocess and binning and
+// its wait-status word after binning, so a call is split into four phases
+// that wait on nothing but those two readbacks:
 //   begin()   workspaces, preprocess, totals readback, depth sort;
 //   bin()     waits for the totals, queues emission, tile sort, ranges;
-//   render()  queues the tile renderer.
+//   render()  queues the tile renderer;
+//   finish()  waits for the end of binning and fails the call if one of its
+//             bounded waits gave up (the renderer is already queued).
 // run_many() puts every call on its context's side stream and queues all
-// begin() phases, then all bin() phases, then all render() phases. The
-// renderers are persistent grids that fill the GPU, so each waits for the
-// binning of every call: the latency-bound preprocess and sorting stages of
-// the calls overlap one another instead of queueing behind a renderer.
+// begin() phases, then all bin() phases, then all render() phases, then
+// runs all finish() phases. The renderers are persistent grids that fill the
+// GPU, so each waits for the binning of every call: the latency-bound
+// preprocess and sorting stages of the calls overlap one another instead of
+// queueing behind a renderer.
 #pragma once
 
 #include <memory>
@@ -56,6 +59,8 @@ cudaError_t run_many(HsRasterizerContext* const* contexts, const Call* calls, ui
     }
     for (auto& p : passes)
         if (st == cudaSuccess) st = p->render();
+    for (auto& p : passes)
+        if (st == cudaSuccess) st = p->finish();
     // Join also after an error: the caller's stream stays ordered after
     // everything that was queued.
     for (uint32_t i = 0; i < count; ++i) {

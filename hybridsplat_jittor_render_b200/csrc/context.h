@@ -144,9 +144,13 @@ struct HsRasterizerContext {
 
     hs::StageTimer timer;
 
-    // Device status word shared by the look-back waits of every sort and scan
-    // of this context (bit 0: a wait gave up). Allocated and zeroed once.
+    // Device status word shared by the bounded waits of every sort and scan
+    // of this context (bit 0: a wait gave up). Allocated once, cleared at the
+    // start of every raster call and read back after its binning.
     uint32_t* device_error = nullptr;
+    // Test hook (hs_b200_test_stall_lookback_v1): the tile of the next raster
+    // call's first depth-sort pass that never publishes its look-back status.
+    uint32_t test_stall_tile = 0xffffffffu;
     cudaEvent_t std_count_event = nullptr;  // marks the standard totals readback
     cudaEvent_t fg_count_event = nullptr;   // marks the FlashGS totals readback
 
@@ -158,6 +162,10 @@ struct HsRasterizerContext {
 };
 
 namespace hs {
+
+// Status of a raster call whose bounded device wait gave up (a sort or scan
+// look-back, or a bulk copy, that did not complete within its bound).
+constexpr cudaError_t kWaitGaveUp = cudaErrorLaunchTimeout;
 
 uint64_t flashgs_current_bytes(const HsRasterizerContext* context);
 uint64_t standard_current_bytes(const HsRasterizerContext* context);

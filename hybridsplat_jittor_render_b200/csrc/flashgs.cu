@@ -142,6 +142,7 @@ public:
     cudaError_t begin();
     cudaError_t bin();
     cudaError_t render();
+    cudaError_t finish();
 
 private:
     HsRasterizerContext* ctx_;
@@ -156,6 +157,7 @@ private:
     uint32_t num_rendered_ = 0;
     GaussianViews gv_{};
     uint64_t sort_need_ = 0;
+    bool published_ = false;  // the error word follows binning (finish() reads it)
 };
 
 cudaError_t FlashgsPass::begin() {
@@ -212,7 +214,9 @@ cudaError_t FlashgsPass::begin() {
                           bin::scan_scratch_bytes(c_.point_count));
     st = ensure_buffer(ctx_->fg_sort, sort_need_, &ctx_->fg_growth_count);
     if (st != cudaSuccess) return st;
-    st = cudaMemsetAsync(gv_.total, 0, 4 * sizeof(uint32_t), stream);
+    // A wait that gave up in an earlier call must not fail this one.
+    st = cudaMemsetAsync(ctx_->device_error, 0, sizeof(uint32_t), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(gv_.total, 0, 4 * sizeof(uint32_t), stream);
     if (st != cudaSuccess) return st;
 
     const int blocks = (c_.point_count + kPreThreads - 1) / kPreThreads;
@@ -220,7 +224,7 @@ cudaError_t FlashgsPass::begin() {
         c_.point_count, cam_, c_.positions3, c_.shs48, c_.colors3, c_.use_sh ? 1 : 0,
         c_.opacities1, c_.covariance6, c_.scales2, c_.scale_modifier, c_.rotations4, c_.specular1,
         c_.roughness1, gv_.records, gv_.emit, gv_.keys, gv_.order, gv_.counts, gv_.total,
-        ctx_->device_error, static_cast<int>(c_.row_begin), static_cast<int>(c_.row_end));
+        static_cast<int>(c_.row_begin), static_cast<int>(c_.row_end));
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     bin::publish_totals_kernel<<<1, 32, 0, stream>>>(gv_.total, ctx_->fg_total_mapped);
@@ -231,8 +235,10 @@ cudaError_t FlashgsPass::begin() {
     // The depth sort does not depend on the pair count: queue it, then wait
     // for the count in bin() (the reference reads its counter back at this
     // point, flashgs_backend.cu:480-488).
+    const uint32_t stall = ctx_->test_stall_tile;  // test hook, one call only
+    ctx_->test_stall_tile = sort::kNoStall;
     return sort::sort_pairs(gv_.keys, gv_.order, gv_.alt_keys, gv_.alt_order, c_.point_count, 0,
-                            32, ctx_->fg_sort.ptr, stream, ctx_->device_error);
+                            32, ctx_->fg_sort.ptr, stream, ctx_->device_error, stall);
 }
 
 cudaError_t FlashgsPass::bin() {
@@ -242,7 +248,6 @@ cudaError_t FlashgsPass::bin() {
         st = cudaEventSynchronize(ctx_->fg_count_event);
         if (st != cudaSuccess) return st;
         num_rendered_ = ctx_->fg_total_host[0];
-        if (ctx_->fg_total_host[1] != 0) return cudaErrorLaunchTimeout;  // a look-back wait gave up
         if (num_rendered_ > static_cast<uint32_t>(INT_MAX) || num_rendered_ > sort::kMaxItems) {
             return cudaErrorInvalidValue;
         }
@@ -286,7 +291,7 @@ cudaError_t FlashgsPass::bin() {
             bin::emit_flat_compact_kernel<Emitter<HS_FLASHGS_ROUNDING>>
                 <<<(c_.point_count + bin::kEmitThreads - 1) / bin::kEmitThreads, bin::kEmitThreads,
                    0, stream>>>(static_cast<uint32_t>(c_.point_count), gv_.counts, first_pair, em,
-                                pv.tiles, pv.ids);
+                                pv.tiles, pv.ids, ctx_->device_error);
             st = cudaGetLastError();
             if (st != cudaSuccess) return st;
             st = sort::sort_pairs(pv.tiles, pv.ids, pv.alt_tiles, pv.alt_ids, num_rendered_, 0,
@@ -305,6 +310,15 @@ cudaError_t FlashgsPass::bin() {
         work_counter_);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
+    if (c_.point_count > 0) {
+        // The waits of the depth sort, offset scan and tile sort are over:
+        // their error word goes to the host, read by finish().
+        bin::publish_error_kernel<<<1, 32, 0, stream>>>(ctx_->device_error, ctx_->fg_total_mapped + 1);
+        st = cudaGetLastError();
+        if (st == cudaSuccess) st = cudaEventRecord(ctx_->fg_count_event, stream);
+        if (st != cudaSuccess) return st;
+        published_ = true;
+    }
     marks_.mark(2);
     return cudaSuccess;
 }
@@ -330,7 +344,7 @@ cudaError_t FlashgsPass::render() {
         std::min<uint64_t>(strip_tiles, static_cast<uint64_t>(sms) * std::max(per_sm, 1)));
     render_kernel<HS_FLASHGS_ROUNDING><<<render_blocks, kRenderThreads, 0, stream>>>(
         ranges_, tile_order_, strip_tiles, work_counter_, ids, gv_.records, c_.width, c_.height,
-        grid_x_, bg, bg_encoded, out);
+        grid_x_, bg, bg_encoded, out, published_ ? ctx_->device_error : nullptr);
     cudaError_t st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     marks_.mark(3);
@@ -352,6 +366,15 @@ cudaError_t FlashgsPass::render() {
     return cudaSuccess;
 }
 
+// Fails the call when one of its bounded waits gave up. The host waits for
+// the end of binning here, with the renderer already queued behind it.
+cudaError_t FlashgsPass::finish() {
+    if (!published_) return cudaSuccess;
+    const cudaError_t st = cudaEventSynchronize(ctx_->fg_count_event);
+    if (st != cudaSuccess) return st;
+    return ctx_->fg_total_host[1] != 0 ? kWaitGaveUp : cudaSuccess;
+}
+
 }  // namespace
 }  // namespace fg
 
@@ -360,6 +383,7 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, const FlashgsCall& call) {
     cudaError_t e = pass.begin();
     if (e == cudaSuccess) e = pass.bin();
     if (e == cudaSuccess) e = pass.render();
+    if (e == cudaSuccess) e = pass.finish();
     return e;
 }
 

@@ -45,12 +45,11 @@ __global__ void __launch_bounds__(kPreThreads, 12) preprocess_kernel(
     const float* __restrict__ specular, const float* __restrict__ roughness,
     float4* __restrict__ records, float4* __restrict__ emit, uint32_t* __restrict__ depth_keys,
     uint32_t* __restrict__ order, uint32_t* __restrict__ pair_counts,
-    uint32_t* __restrict__ totals, const uint32_t* __restrict__ error, int row_begin, int row_end) {
+    uint32_t* __restrict__ totals, int row_begin, int row_end) {
     const int idx = blockIdx.x * kPreThreads + threadIdx.x;
     const bool active = idx < point_count;
     const int lane = threadIdx.x & 31;
     const R r;
-    if (blockIdx.x == 0 && threadIdx.x == 0) totals[1] = *error;
     Projected g;
     g.in_front = false;
     g.touches = false;
@@ -260,7 +259,9 @@ __global__ void __launch_bounds__(kRenderThreads) render_kernel(
     const int2* __restrict__ ranges, const uint32_t* __restrict__ tile_order, uint32_t tile_count,
     uint32_t* __restrict__ work_counter, const uint32_t* __restrict__ gaussian_ids,
     const float4* __restrict__ records, int width, int height, int grid_x, float3 bg,
-    float3 bg_encoded, Outputs out) {
+    float3 bg_encoded, Outputs out, const uint32_t* __restrict__ error) {
+    // A bounded wait of this call gave up: the pair lists may hold any value.
+    if (sort::wait_failed(error)) return;
     __shared__ float4 batch[kBatch * 5];
     __shared__ int done_at[kRenderThreads / 32];
     __shared__ uint32_t next_tile;

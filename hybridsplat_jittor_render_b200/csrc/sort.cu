@@ -1,4 +1,4 @@
-// Onesweep stable LSD radix sort and single-pass exclusive scan (sort.cuh).
+// Onesweep stable LSD radix sort (sort.cuh).
 //
 // Scratch layout of sort_pairs (zeroed by one memset per sort):
 //   hist[kMaxPasses][kBins]        digit counts of every pass
@@ -127,10 +127,11 @@ __device__ __forceinline__ bool barrier_try_wait(uint64_t* barrier, uint32_t par
 
 // Bounded wait for phase 0 of the tile barrier; false when it gave up.
 __device__ __forceinline__ bool wait_tile(uint64_t* barrier) {
-    for (uint32_t spins = 0; spins < kSpinLimit; ++spins) {
-        if (barrier_try_wait(barrier, 0u)) return true;
+    WaitClock clock;
+    while (!barrier_try_wait(barrier, 0u)) {
+        if (clock.expired()) return false;
     }
-    return false;
+    return true;
 }
 
 // Exclusive scan of 256 values held one per thread (all kThreads threads).
@@ -155,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
     const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, uint32_t count, int shift,
     int bits, uint32_t tiles, const uint32_t* __restrict__ hist, uint32_t* __restrict__ counter,
-    uint32_t* __restrict__ status, uint32_t* __restrict__ error) {
+    uint32_t* __restrict__ status, uint32_t* __restrict__ error, uint32_t stall_tile) {
     constexpr uint32_t kTileItems = kThreads * kItems;
     constexpr uint32_t kWarpItems = kTileItems / kWarps;  // contiguous items per warp
     // The tile, in input order until step 4 permutes it into digit order.
@@ -168,6 +169,9 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
     __shared__ uint32_t tile_slot;
     __shared__ alignas(8) uint64_t loaded;    // completes when the bulk copies land
 
+    // An earlier pass gave up a wait: its output is not a permutation of the
+    // input, so this pass's histogram no longer matches it. Every block leaves.
+    if (wait_failed(error)) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t mask = (1u << bits) - 1u;
     if (threadIdx.x == 0) {
@@ -258,14 +262,15 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
 
     // 3. look-back across tiles for this digit
     uint32_t* my_status = status + static_cast<uint64_t>(tile) * kBins + b;
+    const bool publish = tile != stall_tile;  // test hook: a tile that never publishes
     if (tile == 0) {
-        store_status(my_status, kFlagInclusive | total);
-    } else {
+        if (publish) store_status(my_status, kFlagInclusive | total);
+    } else if (publish) {
         store_status(my_status, kFlagAggregate | total);
     }
     const uint32_t earlier =
         tile == 0 ? 0u : look_back<kWindow>(status + b, tile, kBins, error);
-    if (tile != 0) store_status(my_status, kFlagInclusive | ((earlier + total) & kValueMask));
+    if (tile != 0 && publish) store_status(my_status, kFlagInclusive | ((earlier + total) & kValueMask));
 
     // global start of each digit: exclusive scan of the pass histogram
     const uint32_t digit_global = block_exclusive_256(hist[b], warp_sums);
@@ -308,66 +313,6 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
     }
 }
 
-// Single-pass exclusive scan with decoupled look-back; one status word per
-// tile follows the counter word in scratch.
-__global__ void __launch_bounds__(kThreads) scan_kernel(const uint32_t* in,
-                                                        const uint32_t* __restrict__ gather,
-                                                        uint32_t* out, uint32_t* total,
-                                                        uint32_t count, uint32_t tiles,
-                                                        uint32_t* __restrict__ counter,
-                                                        uint32_t* __restrict__ status,
-                                                        uint32_t* __restrict__ error) {
-    __shared__ uint32_t warp_sums[kWarps];
-    __shared__ uint32_t tile_slot, tile_prefix;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) tile_slot = atomicAdd(counter, 1u);
-    __syncthreads();
-    const uint32_t tile = tile_slot;
-    // blocked arrangement: thread t owns items [8t, 8t + 8) of the tile
-    const uint64_t base = static_cast<uint64_t>(tile) * kTile +
-                          static_cast<uint64_t>(threadIdx.x) * kItemsPerThread;
-    uint32_t v[kItemsPerThread];
-    uint32_t local = 0;
-#pragma unroll
-    for (int k = 0; k < kItemsPerThread; ++k) {
-        const uint64_t i = base + k;
-        v[k] = i < count ? in[gather != nullptr ? gather[i] : i] : 0u;
-        local += v[k];
-    }
-    uint32_t incl = local;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += t;
-    }
-    if (lane == 31) warp_sums[warp] = incl;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        uint32_t sum = 0;
-        for (int w = 0; w < kWarps; ++w) sum += warp_sums[w];
-        uint32_t earlier = 0;
-        if (tile == 0) {
-            store_status(status, kFlagInclusive | (sum & kValueMask));
-        } else {
-            store_status(status + tile, kFlagAggregate | (sum & kValueMask));
-            earlier = look_back(status, tile, 1, error);
-            store_status(status + tile, kFlagInclusive | ((earlier + sum) & kValueMask));
-        }
-        tile_prefix = earlier;
-        if (tile == tiles - 1 && total != nullptr) *total = earlier + sum;
-    }
-    __syncthreads();
-    uint32_t run = tile_prefix;
-    for (int w = 0; w < warp; ++w) run += warp_sums[w];
-    run += incl - local;
-#pragma unroll
-    for (int k = 0; k < kItemsPerThread; ++k) {
-        const uint64_t i = base + k;
-        if (i < count) out[i] = run;
-        run += v[k];
-    }
-}
-
 }  // namespace
 
 uint64_t sort_scratch_bytes(uint32_t count) {
@@ -376,14 +321,9 @@ uint64_t sort_scratch_bytes(uint32_t count) {
            sizeof(uint32_t);
 }
 
-uint64_t scan_scratch_bytes(uint32_t count) {
-    const uint64_t tiles = tiles_for(count > 0 ? count : 1);
-    return (tiles + 64) * sizeof(uint32_t);
-}
-
 cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals,
                        uint32_t count, int begin_bit, int end_bit, void* scratch,
-                       cudaStream_t stream, uint32_t* error) {
+                       cudaStream_t stream, uint32_t* error, uint32_t stall_tile) {
     if (count == 0 || end_bit <= begin_bit) return cudaSuccess;
     if (count > kMaxItems || end_bit - begin_bit > kMaxPasses * kRadixBits) {
         return cudaErrorInvalidValue;
@@ -414,20 +354,21 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
     int pass = 0;
     for (int shift = begin_bit; shift < end_bit; shift += kRadixBits, ++pass) {
         const int bits = min(kRadixBits, end_bit - shift);
+        const uint32_t stall = pass == 0 ? stall_tile : kNoStall;
         uint32_t* pass_status = s.status + static_cast<uint64_t>(pass) * tiles * kBins;
         if (large && ballot) {
             onesweep_kernel<kLargeItems, kLargeWindow, true><<<large_tiles, kThreads, 0, stream>>>(
                 src_k, src_v, dst_k, dst_v, count, shift, bits, large_tiles,
-                s.hist + pass * kBins, s.counters + pass, pass_status, error);
+                s.hist + pass * kBins, s.counters + pass, pass_status, error, stall);
         } else if (large) {
             onesweep_kernel<kLargeItems, kLargeWindow, false><<<large_tiles, kThreads, 0, stream>>>(
                 src_k, src_v, dst_k, dst_v, count, shift, bits, large_tiles,
-                s.hist + pass * kBins, s.counters + pass, pass_status, error);
+                s.hist + pass * kBins, s.counters + pass, pass_status, error, stall);
         } else {
             onesweep_kernel<kItemsPerThread, kLookBackWindow, false>
                 <<<tiles, kThreads, 0, stream>>>(src_k, src_v, dst_k, dst_v, count, shift, bits,
                                                  tiles, s.hist + pass * kBins, s.counters + pass,
-                                                 pass_status, error);
+                                                 pass_status, error, stall);
         }
         uint32_t* tk = src_k;
         uint32_t* tv = src_v;
@@ -444,24 +385,6 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
                              cudaMemcpyDeviceToDevice, stream);
         if (st != cudaSuccess) return st;
     }
-    return cudaGetLastError();
-}
-
-cudaError_t exclusive_scan(const uint32_t* in, const uint32_t* gather, uint32_t* out,
-                           uint32_t* total, uint32_t count, void* scratch, cudaStream_t stream,
-                           uint32_t* error) {
-    if (count == 0) {
-        if (total != nullptr) return cudaMemsetAsync(total, 0, sizeof(uint32_t), stream);
-        return cudaSuccess;
-    }
-    if (count > kMaxItems) return cudaErrorInvalidValue;
-    const uint32_t tiles = tiles_for(count);
-    uint32_t* counter = static_cast<uint32_t*>(scratch);
-    uint32_t* status = counter + 64;
-    cudaError_t st = cudaMemsetAsync(scratch, 0, scan_scratch_bytes(count), stream);
-    if (st != cudaSuccess) return st;
-    scan_kernel<<<tiles, kThreads, 0, stream>>>(in, gather, out, total, count, tiles, counter,
-                                                status, error);
     return cudaGetLastError();
 }
 

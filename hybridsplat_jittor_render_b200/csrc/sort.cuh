@@ -1,6 +1,6 @@
-// Device-wide stable LSD radix sort of (uint32 key, uint32 value) pairs, a
-// single-pass exclusive scan, and the decoupled look-back primitive they
-// share.
+// Device-wide stable LSD radix sort of (uint32 key, uint32 value) pairs and
+// the decoupled look-back primitive it shares with the pair-offset scan
+// (binning.cuh).
 //
 // These replace the reference's CUB calls (vendor/flashgs/cuda_rasterizer/
 // sort.cu:29-58, rasterizer/full_rasterizer.cu:301-355). Only the ordering
@@ -33,35 +33,40 @@ constexpr uint32_t kFlagInclusive = 2u << 30;
 constexpr uint32_t kValueMask = (1u << 30) - 1u;
 constexpr uint32_t kMaxItems = kValueMask;           // counts must fit 30 bits
 
-// Bound on the spin iterations of one look-back step. A predecessor tile is
-// always resident (tiles are numbered in the order blocks start), so the
-// bound is never reached in a correct launch; reaching it sets bit 0 of the
-// error word and the wait gives up.
-constexpr uint32_t kSpinLimit = 1u << 24;
+// Every wait of the sort and scan kernels (a look-back on a predecessor's
+// status word, the tile's bulk copy) is bounded. A predecessor tile is always
+// resident (tiles are numbered in the order blocks start), so a wait in a
+// correct launch ends within microseconds; a wait still unanswered after
+// kWaitLimitNs of device time (%globaltimer), or after kSpinLimit polls
+// should the timer not advance, gives up: it sets bit 0 of the caller's error
+// word and returns. Every kernel that consumes a sort or scan result reads
+// that word first and does nothing when it is set, so a give-up never turns
+// into out-of-range indices downstream; the raster call reports it as an
+// error of the same call.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+constexpr uint32_t kSpinLimit = 1u << 28;
+
+// Test hook value: no tile stalls.
+constexpr uint32_t kNoStall = 0xffffffffu;
 
 inline uint32_t tiles_for(uint32_t count) { return (count + kTile - 1) / kTile; }
 
 // Scratch bytes needed by sort_pairs for `count` items.
 uint64_t sort_scratch_bytes(uint32_t count);
-// Scratch bytes needed by exclusive_scan for `count` items.
-uint64_t scan_scratch_bytes(uint32_t count);
 
 // Stable sort of keys[0, count) by bits [begin_bit, end_bit) of the key.
 // keys/vals hold the input and receive the output; alt_keys/alt_vals are
 // ping-pong buffers of the same size. scratch holds sort_scratch_bytes(count)
-// bytes; error (may be null) receives bit 0 if a look-back wait gave up.
+// bytes; error (may be null) receives bit 0 if a wait gave up, and when it is
+// already set on entry every pass does nothing. stall_tile is a test hook:
+// the block of that tile in the first pass never publishes its look-back
+// status, so the waits of its successors run out (kNoStall: none).
 // Launches: one memset, one histogram kernel, one kernel per 8-bit pass
 // (plus two copies when the pass count is odd).
 cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals,
                        uint32_t count, int begin_bit, int end_bit, void* scratch,
-                       cudaStream_t stream, uint32_t* error = nullptr);
-
-// out[i] = sum(in[gather[j]] for j < i) when gather != nullptr, else
-// sum(in[j] for j < i); *total = the full sum. out may alias in when
-// gather == nullptr. One memset and one kernel.
-cudaError_t exclusive_scan(const uint32_t* in, const uint32_t* gather, uint32_t* out,
-                           uint32_t* total, uint32_t count, void* scratch, cudaStream_t stream,
-                           uint32_t* error = nullptr);
+                       cudaStream_t stream, uint32_t* error = nullptr,
+                       uint32_t stall_tile = kNoStall);
 
 // Number of bits needed to hold values in [0, n): the reference's
 // getHigherMsb(n) for the tile count (sort.cu:141-156).
@@ -72,6 +77,33 @@ inline int bits_for_tiles(uint32_t n) {
 }
 
 // ---- device helpers shared with the fused scan-and-emit kernels ----
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Poll counter of one bounded wait: expired() is called once per
+// unsuccessful poll and turns true when the wait must give up.
+struct WaitClock {
+    uint64_t start = 0;
+    uint32_t polls = 0;
+    __device__ __forceinline__ bool expired() {
+        if (++polls > kSpinLimit) return true;
+        if ((polls & 31u) != 1u) return false;
+        const uint64_t now = global_ns();
+        if (start == 0) start = now;
+        return now - start > kWaitLimitNs;
+    }
+};
+
+// True when a bounded wait of this call has given up: the error word is
+// written by earlier kernels of the same stream (visible at kernel start) or
+// by other blocks of the running kernel.
+__device__ __forceinline__ bool wait_failed(const uint32_t* error) {
+    return error != nullptr && *reinterpret_cast<const volatile uint32_t*>(error) != 0u;
+}
 
 __device__ __forceinline__ uint32_t load_status(const uint32_t* p) {
     uint32_t v;
@@ -94,7 +126,7 @@ __device__ __forceinline__ uint32_t look_back(const uint32_t* status, uint32_t t
                                               uint32_t stride, uint32_t* error) {
     uint32_t prefix = 0;
     int64_t t = static_cast<int64_t>(tile) - 1;
-    uint32_t spins = 0;
+    WaitClock clock;
     while (t >= 0) {
         uint32_t s[kWindow];
 #pragma unroll
@@ -111,7 +143,7 @@ __device__ __forceinline__ uint32_t look_back(const uint32_t* status, uint32_t t
             k = i + 1;
         }
         if (k == 0) {
-            if (++spins > kSpinLimit) {
+            if (clock.expired()) {
                 if (error != nullptr) atomicOr(error, 1u);
                 return prefix;
             }

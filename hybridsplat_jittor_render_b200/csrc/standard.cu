@@ -57,7 +57,7 @@ struct GeometryViews {
     uint32_t* counts;
     uint32_t* alt_keys;
     uint32_t* alt_order;
-    uint32_t* totals;  // [0] reference pairs, [1] prefiltered violation, [2] emitted pairs, [3] errors
+    uint32_t* totals;  // [0] reference pairs, [1] prefiltered violation, [2] emitted pairs
 };
 
 GeometryViews geometry_views(void* base, uint64_t count) {
@@ -150,6 +150,7 @@ public:
     cudaError_t begin();
     cudaError_t bin();
     cudaError_t render();
+    cudaError_t finish();
 
 private:
     HsRasterizerContext* ctx_;
@@ -165,6 +166,7 @@ private:
     uint32_t* work_counter_ = nullptr;
     uint32_t* values_ = nullptr;
     bool masked_ = false;
+    bool published_ = false;  // the error word follows binning (finish() reads it)
 };
 
 cudaError_t StandardPass::begin() {
@@ -230,13 +232,15 @@ cudaError_t StandardPass::begin() {
     tile_order_ = reinterpret_cast<uint32_t*>(ranges_ + tiles_);
     work_counter_ = tile_order_ + tiles_;
 
-    st = cudaMemsetAsync(c_.output_weight, 0, count_ * sizeof(float), stream);
+    // A wait that gave up in an earlier call must not fail this one.
+    st = cudaMemsetAsync(ctx_->device_error, 0, sizeof(uint32_t), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(c_.output_weight, 0, count_ * sizeof(float), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(gv_.totals, 0, 4 * sizeof(uint32_t), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(ranges_, 0, tiles_ * sizeof(uint2), stream);
     if (st != cudaSuccess) return st;
     const int blocks = (c_.point_count + kPreThreads - 1) / kPreThreads;
     PreprocessOut po{gv_.records, gv_.cull, gv_.keys, gv_.order, gv_.counts, c_.output_radii,
-                     gv_.totals, ctx_->device_error};
+                     gv_.totals};
     preprocess_kernel<HS_STANDARD_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
         c_.point_count, c_.viewmatrix4x4, c_.projmatrix4x4, c_.width, c_.height, grid_x_, grid_y_,
         c_.means3d, c_.colors5, c_.opacities, c_.scales2, c_.scale_modifier, c_.rotations4,
@@ -249,8 +253,10 @@ cudaError_t StandardPass::begin() {
     if (st != cudaSuccess) return st;
     marks_.mark(1);
     // The depth sort does not depend on the totals: queue it before waiting.
+    const uint32_t stall = ctx_->test_stall_tile;  // test hook, one call only
+    ctx_->test_stall_tile = sort::kNoStall;
     return sort::sort_pairs(gv_.keys, gv_.order, gv_.alt_keys, gv_.alt_order, c_.point_count, 0, 32,
-                            geometry_scratch_, stream, ctx_->device_error);
+                            geometry_scratch_, stream, ctx_->device_error, stall);
 }
 
 cudaError_t StandardPass::bin() {
@@ -260,7 +266,6 @@ cudaError_t StandardPass::bin() {
     if (st != cudaSuccess) return st;
     const uint32_t rendered = ctx_->std_total_host[0];
     const uint32_t emitted = ctx_->std_total_host[2];
-    if (ctx_->std_total_host[3] != 0) return cudaErrorLaunchTimeout;  // a look-back wait gave up
     if (ctx_->std_total_host[1] != 0) return kPrefilteredViolation;
     if (rendered > static_cast<uint32_t>(INT_MAX) || emitted > sort::kMaxItems) {
         return cudaErrorInvalidValue;
@@ -293,7 +298,7 @@ cudaError_t StandardPass::bin() {
         emit_rows_kernel<<<(c_.point_count + kEmitRowThreads - 1) / kEmitRowThreads,
                            kEmitRowThreads, 0, stream>>>(
             static_cast<uint32_t>(c_.point_count), gv_.counts, first_pair, gv_.cull, grid_x_,
-            masked_ ? 1 : 0, tile_ids, values_);
+            masked_ ? 1 : 0, tile_ids, values_, ctx_->device_error);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
         st = sort::sort_pairs(tile_ids, values_, alt_tiles, alt_values, emitted, 0,
@@ -310,6 +315,13 @@ cudaError_t StandardPass::bin() {
         c_.row_begin * grid_x_, strip_tiles, ranges_, tile_order_, work_counter_);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
+    // The waits of the depth sort, offset scan and tile sort are over: their
+    // error word goes to the host, read by finish() once the renderer is queued.
+    bin::publish_error_kernel<<<1, 32, 0, stream>>>(ctx_->device_error, ctx_->std_total_mapped + 3);
+    st = cudaGetLastError();
+    if (st == cudaSuccess) st = cudaEventRecord(ctx_->std_count_event, stream);
+    if (st != cudaSuccess) return st;
+    published_ = true;
     marks_.mark(2);
     return cudaSuccess;
 }
@@ -332,15 +344,26 @@ cudaError_t StandardPass::render() {
     if (masked_) {
         render_kernel<HS_STANDARD_ROUNDING, true><<<render_blocks, kRenderThreads, 0, c_.stream>>>(
             ranges_, tile_order_, items, work_counter_, values_, gv_.records, c_.width, c_.height,
-            grid_x_, c_.background5, c_.output_color5, c_.output_aux7, c_.output_weight);
+            grid_x_, c_.background5, c_.output_color5, c_.output_aux7, c_.output_weight,
+            ctx_->device_error);
     } else {
         render_kernel<HS_STANDARD_ROUNDING, false><<<render_blocks, kRenderThreads, 0, c_.stream>>>(
             ranges_, tile_order_, items, work_counter_, values_, gv_.records, c_.width, c_.height,
-            grid_x_, c_.background5, c_.output_color5, c_.output_aux7, c_.output_weight);
+            grid_x_, c_.background5, c_.output_color5, c_.output_aux7, c_.output_weight,
+            ctx_->device_error);
     }
     const cudaError_t st = cudaGetLastError();
     marks_.mark(3);
     return st;
+}
+
+// Fails the call when one of its bounded waits gave up. The host waits for
+// the end of binning here, with the renderer already queued behind it.
+cudaError_t StandardPass::finish() {
+    if (!published_) return cudaSuccess;
+    const cudaError_t st = cudaEventSynchronize(ctx_->std_count_event);
+    if (st != cudaSuccess) return st;
+    return ctx_->std_total_host[3] != 0 ? kWaitGaveUp : cudaSuccess;
 }
 
 }  // namespace
@@ -351,6 +374,7 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, const StandardCall& call)
     cudaError_t e = pass.begin();
     if (e == cudaSuccess) e = pass.bin();
     if (e == cudaSuccess) e = pass.render();
+    if (e == cudaSuccess) e = pass.finish();
     return e;
 }
 

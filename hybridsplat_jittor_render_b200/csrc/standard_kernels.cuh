@@ -24,9 +24,7 @@ struct PreprocessOut {
     uint32_t* order;
     uint32_t* counts;        // pairs emitted per Gaussian
     int32_t* radii;
-    uint32_t* totals;        // [0] reference pair count, [1] prefiltered violation, [2] emitted,
-                             // [3] copy of the context's look-back error word
-    const uint32_t* error;   // the context's look-back error word
+    uint32_t* totals;        // [0] reference pair count, [1] prefiltered violation, [2] emitted
 };
 
 __device__ __forceinline__ void warp_add(uint32_t* dst, uint32_t v) {
@@ -116,7 +114,6 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
         view[k] = m[k];
         proj[k] = m[16 + k];
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) out.totals[3] = *out.error;
     uint32_t area = 0, emitted = 0, violation = 0;
     CullShape cs;
     cs.mode = kCullAlways;
@@ -233,7 +230,8 @@ constexpr int kEmitRowThreads = 128;
 static __global__ void __launch_bounds__(kEmitRowThreads) emit_rows_kernel(
     uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
     const float4* __restrict__ cull, uint32_t grid_x, int masked, uint32_t* __restrict__ tile_ids,
-    uint32_t* __restrict__ values) {
+    uint32_t* __restrict__ values, const uint32_t* __restrict__ error) {
+    if (sort::wait_failed(error)) return;  // first_pair is not a valid offset table
     __shared__ RowUnit units[kEmitRowThreads];
     __shared__ uint32_t cursor[kEmitRowThreads], counted[kEmitRowThreads],
         offsets[kEmitRowThreads], rows_incl[kEmitRowThreads];
@@ -364,7 +362,9 @@ __global__ void __launch_bounds__(kRenderThreads, 7) render_kernel(
     uint32_t* __restrict__ work_counter, const uint32_t* __restrict__ pair_values,
     const float4* __restrict__ records, int width, int height, uint32_t grid_x,
     const float* __restrict__ background5, float* __restrict__ color, float* __restrict__ aux,
-    float* __restrict__ weight) {
+    float* __restrict__ weight, const uint32_t* __restrict__ error) {
+    // A bounded wait of this call gave up: the pair lists may hold any value.
+    if (sort::wait_failed(error)) return;
     __shared__ float4 slots[kRenderThreads / 32][32 * kRecordQuads];
     __shared__ uint32_t slot_ids[kRenderThreads / 32][32];
     const R r;

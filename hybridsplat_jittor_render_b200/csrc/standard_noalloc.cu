@@ -26,10 +26,12 @@
 // device before any stream capture and before any phase in which the runtime
 // must not be asked to load modules.
 //
-// What must start at zero: only the look-back error word at the start of the
-// array; a device array is zero when the module loads and the word is never
-// cleared (a set word means a sort wait gave up and every later call fails).
-// All other scratch is cleared by the call itself before use.
+// What must start at zero: the wait-status word at the start of the array
+// (set when a bounded wait of a sort or scan gave up) and the per-call
+// counters; the call clears them itself before its first kernel, so a failed
+// call does not affect the next one. All other scratch is written before it is
+// read. A wait that gives up fails the same call: the word is read back after
+// the renderer is queued.
 //
 // Concurrency: all calls on one device share the array. A process-wide lock
 // serialises the host side and all work goes to the legacy default stream,
@@ -153,12 +155,13 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
     const Layout l = carve(base, kMaxPoints, kMaxPairs, kMaxTiles);
     if (l.used > kScratchBytes) return {cudaErrorInvalidValue, "scratch layout", l.used, kScratchBytes};
 
-    cudaError_t st = cudaMemsetAsync(output_weight, 0, point_count * sizeof(float), stream);
+    cudaError_t st = cudaMemsetAsync(l.error, 0, sizeof(uint32_t), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(output_weight, 0, point_count * sizeof(float), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(l.totals, 0, 4 * sizeof(uint32_t), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(l.ranges, 0, tiles * sizeof(uint2), stream);
     if (st != cudaSuccess) return {st, nullptr, 0, 0};
     const int blocks = (point_count + kPreThreads - 1) / kPreThreads;
-    PreprocessOut po{l.records, l.cull, l.keys, l.order, l.counts, output_radii, l.totals, l.error};
+    PreprocessOut po{l.records, l.cull, l.keys, l.order, l.counts, output_radii, l.totals};
     preprocess_kernel<HS_STANDARD_ROUNDING><<<blocks, kPreThreads, 0, stream>>>(
         point_count, viewmatrix4x4, projmatrix4x4, width, height, grid_x, grid_y, means3d,
         colors5, opacities, scales2, scale_modifier, rotations4, prefiltered ? 1 : 0, 0u, grid_y,
@@ -173,7 +176,6 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
     if (st != cudaSuccess) return {st, nullptr, 0, 0};
     const uint32_t rendered = totals[0];
     const uint32_t emitted = totals[2];
-    if (totals[3] != 0) return {cudaErrorLaunchTimeout, nullptr, 0, 0};
     if (totals[1] != 0) return {cudaErrorInvalidValue, nullptr, 0, 0};
     if (emitted > kMaxPairs) return {cudaSuccess, "emitted pair count", emitted, kMaxPairs};
     if (rendered > static_cast<uint32_t>(INT_MAX)) return {cudaErrorInvalidValue, nullptr, 0, 0};
@@ -192,7 +194,7 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
         emit_rows_kernel<<<(point_count + kEmitRowThreads - 1) / kEmitRowThreads, kEmitRowThreads, 0,
                            stream>>>(static_cast<uint32_t>(point_count), l.counts, first_pair,
-                                     l.cull, grid_x, 1, l.tile_ids, l.values);
+                                     l.cull, grid_x, 1, l.tile_ids, l.values, l.error);
         st = cudaGetLastError();
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
         st = sort::sort_pairs(l.tile_ids, l.values, l.alt_tiles, l.alt_values, emitted, 0,
@@ -218,8 +220,15 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
         std::min<uint32_t>(wanted, static_cast<uint32_t>(sms * std::max(per_sm, 1)));
     render_kernel<HS_STANDARD_ROUNDING, true><<<render_blocks, kRenderThreads, 0, stream>>>(
         l.ranges, l.tile_order, items, l.work_counter, l.values, l.records, width, height,
-        grid_x, background5, output_color5, output_aux7, output_weight);
-    return {cudaGetLastError(), nullptr, 0, 0};
+        grid_x, background5, output_color5, output_aux7, output_weight, l.error);
+    st = cudaGetLastError();
+    if (st != cudaSuccess) return {st, nullptr, 0, 0};
+    // The wait-status word of this call's sorts and scan (a blocking copy on
+    // the legacy stream: it completes after the renderer).
+    uint32_t gave_up = 0;
+    st = cudaMemcpy(&gave_up, l.error, sizeof(gave_up), cudaMemcpyDeviceToHost);
+    if (st != cudaSuccess) return {st, nullptr, 0, 0};
+    return {gave_up != 0 ? kWaitGaveUp : cudaSuccess, nullptr, 0, 0};
 }
 
 }  // namespace st_noalloc

@@ -220,6 +220,14 @@ EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
                                                   _V, _V, _V, *_ERR]),
     "hs_b200_flashgs_forward_many_v2": (_I32, [ctypes.POINTER(FlashgsCallV2), _U32, _V, *_ERR]),
     "hs_b200_rasterizer_forward_many_v2": (_I32, [ctypes.POINTER(RasterizerCallV2), _U32, _V, *_ERR]),
+    "hs_b200_test_stall_lookback_v1": (_I32, [_V, _U32, *_ERR]),
+    "hs_b200_comm_unique_id_v1": (_I32, [_V, *_ERR]),
+    "hs_b200_comm_create_v1": (_I32, [_I32, _I32, _I32, _V, ctypes.c_double, ctypes.POINTER(ctypes.c_void_p),
+                                      *_ERR]),
+    "hs_b200_comm_broadcast_v1": (_I32, [_V, _V, _U64, _I32, _V, *_ERR]),
+    "hs_b200_comm_allreduce_max_f64_v1": (_I32, [_V, _V, _V, _U32, *_ERR]),
+    "hs_b200_comm_barrier_v1": (_I32, [_V, *_ERR]),
+    "hs_b200_comm_destroy_v1": (_I32, [_V, *_ERR]),
     "hs_b200_stage_timing_enable_v1": (_I32, [_V, _I32, *_ERR]),
     "hs_b200_stage_timing_read_v1": (_I32, [_V, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_U64), *_ERR]),
     "hs_b200_flashgs_forward_rows_f32_v1": (
@@ -399,6 +407,15 @@ class NativeRendererContext:
                                                             len(error))
         check_status(status, "hs_b200_stage_timing_read_v1", error)
         return {"preprocess_ms": ms[0], "binning_ms": ms[1], "blend_ms": ms[2], "calls": int(calls.value)}
+
+    def stall_next_sort(self, tile: int) -> None:
+        """Test hook: the next raster call's depth sort runs with sort tile
+        `tile` of its first pass never publishing its look-back status, so the
+        bounded waits behind it run out and that call fails
+        (hs_b200_test_stall_lookback_v1)."""
+        error = error_buffer()
+        status = self._library.hs_b200_test_stall_lookback_v1(self.handle, int(tile), error, len(error))
+        check_status(status, "hs_b200_test_stall_lookback_v1", error)
 
     def release_workspace(self) -> None:
         _torch_synchronize(self._device)

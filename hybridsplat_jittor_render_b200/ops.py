@@ -405,6 +405,47 @@ def rasterize_forward_many(calls: Sequence[dict[str, Any]], *,
     return outs
 
 
+def rasterize_forward_noalloc(
+    background: torch.Tensor,
+    means3d: torch.Tensor,
+    colors: torch.Tensor,
+    opacities: torch.Tensor,
+    scales: torch.Tensor,
+    rotations: torch.Tensor,
+    viewmatrix: torch.Tensor,
+    projmatrix: torch.Tensor,
+    camera_position: torch.Tensor,
+    *,
+    width: int,
+    height: int,
+    scale_modifier: float,
+    tan_fovx: float,
+    tan_fovy: float,
+    prefiltered: bool = False,
+    out: RasterizerOutputs | None = None,
+    library: ctypes.CDLL | None = None,
+) -> RasterizerOutputs:
+    """rasterize_forward through hs_b200_rasterizer_forward_noalloc_f32_v1:
+    no context, no allocation inside the library (small views only: at most
+    16384 Gaussians, 4096 tiles and 262144 emitted pairs). The entry point
+    runs on the legacy default stream, so work queued on a non-default torch
+    stream (which may have produced the inputs) is waited for first."""
+    library = library if library is not None else load_native_library()
+    named, out = _rasterizer_arguments(
+        background, means3d, colors, opacities, scales, rotations, viewmatrix, projmatrix, camera_position,
+        width=width, height=height, scale_modifier=scale_modifier, tan_fovx=tan_fovx, tan_fovy=tan_fovy,
+        prefiltered=prefiltered, out=out)
+    stream = torch.cuda.current_stream(means3d.device)
+    if stream.cuda_stream != 0:
+        stream.synchronize()
+    error = error_buffer()
+    status = library.hs_b200_rasterizer_forward_noalloc_f32_v1(
+        means3d.device.index if means3d.device.index is not None else torch.cuda.current_device(),
+        *[named[k] for k in _RASTERIZER_ORDER], error, len(error))
+    check_status(status, "hs_b200_rasterizer_forward_noalloc_f32_v1", error)
+    return out
+
+
 def flashgs_prepare_host(
     opacity_raw, scaling_raw, rotation_raw, specular_raw, roughness_raw, *, library: ctypes.CDLL | None = None
 ) -> dict[str, Any]:

@@ -14,6 +14,20 @@
 extern "C" {
 #endif
 
+/* Test hook for the bounded device waits. Every wait of the sorts and scans
+ * behind the raster calls (a decoupled look-back on a predecessor block's
+ * status, the bulk copy of a sort tile) gives up after about one second of
+ * device time; the call then returns HS_STATUS_CUDA_ERROR naming the wait,
+ * its outputs are invalid, and the next call on the handle starts clean.
+ * This makes the next raster call on `handle` (either backend, v1 or many_v2)
+ * run its depth sort with the block of tile `tile` of the first pass never
+ * publishing its status, so the waits of the following blocks run out. One
+ * call only; tile = 0xffffffff cancels. A call with at most `tile` sort
+ * tiles is unaffected. No counterpart in the reference library. */
+HS_API int32_t hs_b200_test_stall_lookback_v1(
+    HsRasterizerHandle handle, uint32_t tile, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+
 /* Turns per-stage device timing of the raster calls (hs_flashgs_forward_f32_v1
  * and hs_rasterizer_forward_f32_v1) on or off for this handle. While on, each
  * raster call records four CUDA events on its stream: start, end of
@@ -74,8 +88,18 @@ HS_API int32_t hs_b200_rasterizer_forward_rows_f32_v1(
  * returns HS_STATUS_RANGE_ERROR naming the limit (the pair limit is known only
  * after preprocessing, so outputs are then incomplete). All calls on a device
  * share the array: they are serialised by a process-wide lock and run on the
- * legacy default stream. The call reads the pair count back with a blocking
- * copy into host stack memory. */
+ * legacy default stream, so calls that overlap on the GPU (for example the
+ * same work issued on other streams) would race; the call clears the words
+ * that must start at zero itself. Inputs must be complete before the call: a
+ * caller that produced them on a non-blocking stream synchronises that stream
+ * first (the legacy default stream does not wait for non-blocking streams).
+ * The call reads the pair count and, after queuing the renderer, its
+ * wait-status word back with blocking copies into host stack memory, so it
+ * returns once the frame is rendered; a bounded wait that gave up fails this
+ * call (HS_STATUS_CUDA_ERROR) and not the next. The caller's current device is
+ * restored on return. The scratch address is cached per device ordinal for
+ * the life of the process: do not use this entry point across
+ * cudaDeviceReset. */
 HS_API int32_t hs_b200_rasterizer_forward_noalloc_f32_v1(
     int32_t device, uint64_t point_count, const float* background5, int32_t width,
     int32_t height, const float* means3d, const float* colors5, const float* opacities,
@@ -256,6 +280,54 @@ HS_API int32_t hs_b200_flashgs_postprocess_f32_v1(
     const float* alpha1, const float* normal3, const float* normal_rotation3x3, float* rgb_map3,
     float* acc_map, float* dpt_map, float* norm_map3, float* surf_norm_map3, float* dist_map,
     float* spec_map, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
+/* ---- multi-GPU replicas: an NCCL communicator behind the C ABI ----
+ *
+ * One process per GPU. The forward renderer has no per-frame exchange (every
+ * GPU holds a replica of the Gaussians and renders its own views or its own
+ * strip of tile rows), so the only collectives are a broadcast of the scene
+ * arrays at session start, straight into each rank's device buffers, and a
+ * few host values (per-rank timings, a barrier). libnccl.so.2 is loaded with
+ * dlopen on first use. Communicators are created non-blocking and every
+ * operation is polled against timeout_s: a rank that never joins or leaves
+ * mid-operation makes the others return HS_STATUS_CUDA_ERROR (the
+ * communicator is then aborted and only hs_b200_comm_destroy_v1 remains
+ * valid) instead of hanging. Every call restores the caller's current
+ * device. No counterpart in the reference library (it has no multi-GPU
+ * path). */
+typedef struct HsB200Comm* HsB200CommHandle;
+
+/* A new 128-byte NCCL unique id (rank 0 creates it and hands it to the other
+ * ranks out of band). */
+HS_API int32_t hs_b200_comm_unique_id_v1(
+    uint8_t* id128, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
+/* Joins rank `rank` of `rank_count` on CUDA device `device`; returns once
+ * every rank has joined, or fails after timeout_s seconds. */
+HS_API int32_t hs_b200_comm_create_v1(
+    int32_t device, int32_t rank_count, int32_t rank, const uint8_t* id128, double timeout_s,
+    HsB200CommHandle* out_comm, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
+/* In-place broadcast of `bytes` bytes of device memory from rank `root`.
+ * Ordered after the work queued on `stream` (a cudaStream_t, NULL = legacy
+ * default stream) and returns when the data has arrived; `stream` is then
+ * ordered after the broadcast. */
+HS_API int32_t hs_b200_comm_broadcast_v1(
+    HsB200CommHandle comm, void* buffer, uint64_t bytes, int32_t root, void* stream,
+    char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
+/* out[i] = max over ranks of values[i] (host doubles, count <= 512). */
+HS_API int32_t hs_b200_comm_allreduce_max_f64_v1(
+    HsB200CommHandle comm, const double* values, double* out, uint32_t count, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+
+/* Returns once every rank has entered the barrier. */
+HS_API int32_t hs_b200_comm_barrier_v1(
+    HsB200CommHandle comm, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
+/* Finalizes and frees the communicator (null is accepted). */
+HS_API int32_t hs_b200_comm_destroy_v1(
+    HsB200CommHandle comm, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
 
 #ifdef __cplusplus
 }

@@ -17,7 +17,7 @@ import pytest
 import torch
 
 from helpers import STANDARD_MAX_ABS, fixture_inputs
-from hybridsplat_jittor_render_b200 import NativeRendererContext, ops
+from hybridsplat_jittor_render_b200 import NativeRendererContext, ops, scenes
 from hybridsplat_jittor_render_b200 import native_runtime as nr
 
 pytestmark = pytest.mark.gpu
@@ -81,3 +81,64 @@ def test_noalloc_rejects_sizes_beyond_its_limits(golden):
         big[key] = np.concatenate([inputs[key]] * 9, axis=0)  # 18000 Gaussians > 16384
     status, message, _ = noalloc_forward(lib, big, 96, 72)
     assert status == 3 and "point_count" in message and "16384" in message
+
+
+def large_footprint_inputs(count: int = 3000) -> tuple[dict, int, int]:
+    """`count` near-opaque Gaussians of scale 0.5 around the origin, seen from
+    distance 4 on a 1024x1024 view (exactly 4096 tiles): each covers hundreds
+    of tiles, so the emitted pairs far exceed the fixed pair limit."""
+    spec = scenes.SceneSpec("noalloc_pairs", scenes.GroupSpec(count), scenes.GroupSpec(1), 1024, 1024, 800.0)
+    cam = scenes.look_at_camera(spec, (0.0, -4.0, 1.0))
+    rng = np.random.default_rng(11)
+    q = rng.normal(size=(count, 4)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    inputs = {
+        "background": np.zeros(5, np.float32),
+        "means3d": rng.normal(0.0, 0.3, (count, 3)).astype(np.float32),
+        "colors": rng.random((count, 5), dtype=np.float32),
+        "opacities": np.full((count, 1), 0.99, np.float32),
+        "scales": np.full((count, 2), 0.5, np.float32),
+        "rotations": q,
+        "viewmatrix": cam.world_view(),
+        "projmatrix": cam.full_proj(),
+        "camera_position": scenes.standard_camera_center(cam),
+    }
+    return inputs, spec.width, spec.height
+
+
+def test_noalloc_rejects_too_many_emitted_pairs_then_recovers(golden):
+    lib = nr.load_native_library()
+    inputs, w, h = large_footprint_inputs()
+    assert inputs["means3d"].shape[0] <= 16384 and ((w + 15) // 16) * ((h + 15) // 16) <= 4096
+    with NativeRendererContext(0) as ctx:  # the context path has no pair limit
+        ref = ops.rasterize_forward(*[dev(v) for v in inputs.values()], width=w, height=h, scale_modifier=1.0,
+                                    tan_fovx=0.5, tan_fovy=0.5, context=ctx)
+        torch.cuda.synchronize()
+        assert int(ref.rendered.item()) > 262144
+    status, message, _ = noalloc_forward(lib, inputs, w, h)
+    assert status == 3 and "emitted pair count" in message and "262144" in message, message
+    # Nothing was written past the scratch array: a normal call that follows
+    # still equals the context path.
+    data = golden("small")
+    small = fixture_inputs(data, "standard", "base")
+    sw, sh = (int(v) for v in data["camera_size"])
+    with NativeRendererContext(0) as ctx:
+        ref = ops.rasterize_forward(*[dev(v) for v in small.values()], width=sw, height=sh, scale_modifier=1.0,
+                                    tan_fovx=0.5, tan_fovy=0.5, context=ctx)
+        torch.cuda.synchronize()
+    status, message, (color, aux, weight, radii, rendered) = noalloc_forward(lib, small, sw, sh)
+    assert status == 0, message
+    assert int(rendered.item()) == int(ref.rendered.item())
+    assert torch.equal(radii, ref.radii)
+    assert torch.equal(color, ref.color) and torch.equal(aux, ref.auxiliary)
+
+
+def test_noalloc_restores_the_callers_device(golden):
+    lib = nr.load_native_library()
+    data = golden("small")
+    inputs = fixture_inputs(data, "standard", "base")
+    w, h = (int(v) for v in data["camera_size"])
+    before = torch.cuda.current_device()
+    status, message, _ = noalloc_forward(lib, inputs, w, h)
+    assert status == 0, message
+    assert torch.cuda.current_device() == before
