@@ -10,9 +10,13 @@ with inputs resident in HBM:
   flashgs backend (--backend flashgs):
     base FlashGS raster (SH), reflection-ray generation, reflection FlashGS
     raster, fusion.
-The OptiX reflection trace is not part of the step (it runs on RT cores in
-the reference and is timed separately there); its [P,3] colour output is a
-fixed synthetic input of the reflection raster.
+The reflection trace is not part of the headline step (the reference runs
+it on OptiX and times it separately; its rebuild here cannot trace): there
+its [P,3] colour output is a fixed synthetic input of the reflection raster.
+The trace is timed on its own (`stages_ms.trace`, `stages_ms.trace_scene_build`)
+and in `blocks.view_with_trace`, the whole view with the traced colours
+feeding the reflection raster (this library's CUDA BVH tracer behind the
+reference's hs_optix_* entry points).
 
 Output: one JSON line on rank 0 (driver contract). `value` is whole-job
 frames per second with device-resident inputs, the median over repeated
@@ -108,6 +112,8 @@ def parse_args():
                    help="render this many frames untimed and exit (a short, fixed launch sequence for ncu)")
     p.add_argument("--profile-reference", action="store_true",
                    help="with --profile-frames: render with the reference CUDA rebuild (oracle/_ref)")
+    p.add_argument("--trace", action="store_true",
+                   help="with --profile-frames: trace the reflection colours of every frame")
     return p.parse_args()
 
 
@@ -279,6 +285,45 @@ class Frame:
         self.cam = None
         self.split = None  # list: per raster call stage timings (instrumented pass)
         self.tile_rows = None  # (begin, end): render only this strip of tile rows
+        self.r_scene = r
+        self.traced = False  # render() traces the reflection colours (enable_trace)
+
+    def enable_trace(self) -> float:
+        """Builds the reflection trace scene of the session (the disks of the
+        reflective Gaussians, hs_optix_build_scene_v1) and makes every view
+        trace its reflection colours. Returns the build's device ms."""
+        torch, ops = self.torch, self.ops
+        r = self.r_scene
+        self.r_scale_exp = ops.precise_exp(r["scaling"])
+        self.r_rot_unit = ops.precise_normalize4(self.r_rot_raw)
+        self.r_sh16 = torch.cat([r["features_dc"].view(-1, 1, 3), r["features_rest"].view(-1, 15, 3)], 1).contiguous()
+        self.r_op_act = ops.precise_sigmoid(r["opacity"])
+        self.r_others = torch.cat([self.r_spec, self.r_rough], 1).contiguous()
+        self.bg3 = torch.zeros(3, device=self.device)
+        vertices, triangles = ops.gaussian_disks(self.r_xyz, self.r_rot_raw, self.r_scale_exp)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.build_trace_scene(vertices, triangles, scene_signature=1, context=self.ctx_r)
+        e1.record()
+        torch.cuda.synchronize()
+        self.traced = True
+        return e0.elapsed_time(e1)
+
+    def trace(self, rays):
+        """The reflection trace of one view (hs_optix_trace_f32_v1): one ray
+        per reflective Gaussian from the prepared reflection rays."""
+        ops = self.ops
+        if self.backend == "standard":
+            view, proj = self.view, self.proj
+        else:
+            if getattr(self, "fg_view", None) is None or self.fg_cam is not self.cam:
+                t = lambda a: self.torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
+                self.fg_view, self.fg_proj, self.fg_cam = t(self.cam.world_view()), t(self.cam.full_proj()), self.cam
+            view, proj = self.fg_view, self.fg_proj
+        return ops.trace_reflection(rays[:, 12:15].contiguous(), rays[:, 9:12].contiguous(), self.bg3, self.r_xyz,
+                                    self.r_sh16, self.r_others, self.r_op_act, self.r_scale_exp, self.r_rot_unit,
+                                    view, proj, self.center, degree=3, use_others=False, context=self.ctx_r)
 
     def close(self):
         self.ctx.close()
@@ -370,6 +415,13 @@ class Frame:
         rot = ops.precise_reflection_prefix(self.r_rot_raw, library=lib)
         normal_raw = rot[:, :, 2].contiguous()
         rays = ops.precise_reflection_suffix(self.r_xyz, center, normal_raw, library=lib)
+        if self.traced:
+            # the traced colours feed the reflection raster, as in the session
+            traced = self.trace(rays).rgb
+            if self.backend == "standard":
+                refl_call["colors"] = torch.cat([traced, self.r_spec, self.r_rough], 1).contiguous()
+            else:
+                refl_call["colors"] = traced
         rec(2)
         if sequential:
             refl = single(**refl_call)
@@ -741,6 +793,8 @@ def run_ours(args, workload: Workload) -> int:
     views = views_for(job, workload.scene, workload.sharding, args.steps, args.warmup)
     cams = [scenes.orbit_camera(workload.scene, v) for v in views]
     if args.profile_frames > 0:
+        if args.trace:
+            frame.enable_trace()
         for s in range(args.profile_frames):
             frame.set_camera(cams[s % len(cams)])
             frame.render()
@@ -801,6 +855,11 @@ def run_ours(args, workload: Workload) -> int:
     if world == 1 and line is not None:
         # single GPU: render-kernel roofline, CPU baseline, reference CUDA rebuild
         line.update(roofline_and_baselines(args, workload, frame, cams, scene, stages, line["clocks"], ms))
+    traced = trace_block(job, args, frame, cams, device_cams, strips)
+    if line is not None:
+        stages["trace"] = traced.pop("trace_ms")
+        stages["trace_scene_build"] = traced.pop("scene_build_ms")
+        line.setdefault("blocks", {})["view_with_trace"] = traced
     frame.close()
     frame = None
     torch.cuda.synchronize()
@@ -818,12 +877,41 @@ def run_ours(args, workload: Workload) -> int:
             del big
             torch.cuda.empty_cache()
         if line is not None:
-            line["blocks"] = blocks
+            line.setdefault("blocks", {}).update(blocks)
     job.barrier()
     job.close()
     if line is not None:
         emit(line)
     return 0
+
+
+def trace_block(job: Job, args, frame: Frame, cams, device_cams, strips: bool) -> dict:
+    """The reflection trace: the session's scene build (once), one view's
+    trace timed alone (CUDA events around hs_optix_trace_f32_v1), and the
+    whole view with the traced colours feeding the reflection raster."""
+    import torch
+    build_ms = frame.enable_trace()
+    frame.set_camera(cams[0])
+    rays = frame.render()[3]
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps + 2):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        frame.trace(rays)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    trace_ms = float(statistics.median(times[2:]))
+    prime(frame, cams, args.warmup, device_cams)
+    job.barrier()
+    t = timed_loops(job, frame, cams, device_cams, args.warmup, args.steps, BLOCK_MIN_SECONDS, BLOCK_MIN_REPEATS)
+    return {"value": (1 if strips else job.world) * 1000.0 / t["ms_per_step"], "unit": "frames/s",
+            "ms_per_step": t["ms_per_step"], "steps": args.steps, "repeats": t["repeats"],
+            "what": "the headline view plus the reflection trace (hs_optix_trace_f32_v1, CUDA BVH tracer) whose "
+                    "colours feed the reflection raster, as the reference session renders a view",
+            "trace_ms": trace_ms, "scene_build_ms": build_ms,
+            "trace_rays": frame.nr}
 
 
 def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:

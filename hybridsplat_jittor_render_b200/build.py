@@ -63,6 +63,7 @@ SOURCES = [
     ("standard.cu", "cuda", []),
     ("standard_noalloc.cu", "cuda", []),
     ("sort.cu", "cuda", []),
+    ("trace.cu", "cuda", []),
     ("precise.cu", "cuda", ["--fmad=false"]),
     ("precise_exp.cu", "cuda", []),
     ("postprocess.cu", "cuda", []),

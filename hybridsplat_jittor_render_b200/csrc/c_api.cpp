@@ -577,7 +577,7 @@ int32_t hs_rasterizer_build_info(char* output_text, uint64_t output_capacity) no
         "\"flashgs_forward\":\"deterministic_depth_then_tile_sort_v1\","
         "\"flashgs_preprocess_invisible_slots\":\"zero\","
         "\"five_channel_rasterizer\":\"forward_v1\","
-        "\"optix_reflection_tracer\":\"unavailable\","
+        "\"optix_reflection_tracer\":\"cuda_bvh_v1\","
         "\"workspace_growth\":\"1.25x_align_2mib\"}";
     write_text(output_text, output_capacity, info);
     return std::strlen(info) + 1 > output_capacity ? HS_STATUS_RANGE_ERROR : HS_STATUS_OK;
@@ -719,6 +719,8 @@ int32_t hs_rasterizer_destroy(HsRasterizerHandle handle, char* error_text,
             if (e != cudaSuccess) return cuda_failure(e, "release FlashGS context", error_text, error_capacity);
             e = release_math(handle);
             if (e != cudaSuccess) return cuda_failure(e, "release math context", error_text, error_capacity);
+            e = hs::trace_release(handle);
+            if (e != cudaSuccess) return cuda_failure(e, "release trace scene", error_text, error_capacity);
             hs::stage_timing_destroy(handle->timer);
             if (handle->std_count_event != nullptr) cudaEventDestroy(handle->std_count_event);
             if (handle->fg_count_event != nullptr) cudaEventDestroy(handle->fg_count_event);
@@ -881,44 +883,157 @@ int32_t hs_rasterizer_forward_f32_v1(
         error_text, error_capacity);
 }
 
-// OptiX entry points: the OptiX SDK is not part of this build.
-static const char* kNoOptix =
-    "OptiX reflection tracing is not available in this build: the OptiX SDK is not part of it";
-
-int32_t hs_optix_build_scene_v1(HsRasterizerHandle, const float*, uint64_t, const int32_t*,
-                                uint64_t, uint64_t, int32_t, int32_t*, char* error_text,
+// Reflection-trace entry points (reference optix/optix_backend.cpp:375-662):
+// same arguments, checks, error texts and stats; the scene is a BVH built by
+// this library and the trace runs on CUDA cores (trace.cu), with no OptiX.
+int32_t hs_optix_build_scene_v1(HsRasterizerHandle handle, const float* vertices3,
+                                uint64_t vertex_count, const int32_t* triangles3,
+                                uint64_t triangle_count, uint64_t scene_signature, int32_t rebuild,
+                                int32_t* output_status, char* error_text,
                                 uint64_t error_capacity) noexcept {
-    if (error_capacity != 0 && error_text == nullptr) return HS_STATUS_INVALID_ARGUMENT;
-    return fail(HS_STATUS_INTERNAL_ERROR, kNoOptix, error_text, error_capacity);
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr || vertices3 == nullptr || triangles3 == nullptr ||
+            output_status == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX scene build received a null buffer",
+                        error_text, error_capacity);
+        }
+        if (vertex_count == 0 || triangle_count == 0 || vertex_count > UINT32_MAX ||
+            triangle_count > UINT32_MAX || scene_signature == 0 || (rebuild != 0 && rebuild != 1)) {
+            return fail(HS_STATUS_RANGE_ERROR, "OptiX scene dimensions or scalars are invalid",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        if (!rebuild && handle->tr_triangles != 0 && handle->tr_signature == scene_signature) {
+            const cudaError_t e = cudaMemsetAsync(output_status, 0, sizeof(int32_t), nullptr);
+            if (e != cudaSuccess) return cuda_failure(e, "write scene status", error_text, error_capacity);
+            return ok(error_text, error_capacity);
+        }
+        cudaError_t e = hs::ensure_device_error(handle);
+        if (e == cudaSuccess) e = cudaMemsetAsync(handle->device_error, 0, sizeof(uint32_t), nullptr);
+        if (e != cudaSuccess) return cuda_failure(e, "trace scene build", error_text, error_capacity);
+        if (handle->tr_pipeline_count == 0) handle->tr_pipeline_count = 1;
+        bool bad_index = false;
+        handle->tr_triangles = 0;
+        handle->tr_signature = 0;
+        e = hs::trace_build_scene(handle, vertices3, vertex_count, triangles3, triangle_count, &bad_index);
+        if (bad_index) {
+            return fail(HS_STATUS_INVALID_ARGUMENT,
+                        "OptiX scene triangle names a vertex outside the vertex buffer", error_text,
+                        error_capacity);
+        }
+        if (e != cudaSuccess) return cuda_failure(e, "trace scene build", error_text, error_capacity);
+        handle->tr_signature = scene_signature;
+        ++handle->tr_build_count;
+        e = cudaMemsetAsync(output_status, 0, sizeof(int32_t), nullptr);
+        if (e != cudaSuccess) return cuda_failure(e, "write scene status", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
 }
 
-int32_t hs_optix_trace_f32_v1(HsRasterizerHandle, uint64_t, const float*, const float*,
-                              const float*, const float*, const float*, uint32_t, uint32_t,
-                              const float*, const float*, const float*, float, const float*,
-                              const float*, const float*, const float*, int32_t, int32_t, float,
-                              int32_t, float*, float*, float*, float*, float*, float*, float*,
-                              float*, char* error_text, uint64_t error_capacity) noexcept {
-    if (error_capacity != 0 && error_text == nullptr) return HS_STATUS_INVALID_ARGUMENT;
-    return fail(HS_STATUS_INTERNAL_ERROR, kNoOptix, error_text, error_capacity);
+int32_t hs_optix_trace_f32_v1(
+    HsRasterizerHandle handle, uint64_t ray_count, const float* ray_origins3,
+    const float* ray_directions3, const float* background3, const float* means3d,
+    const float* shs_m3, uint32_t coefficient_count, uint32_t degree, const float* others2,
+    const float* opacities, const float* scales2, float scale_modifier, const float* rotations4,
+    const float* viewmatrix4x4, const float* projmatrix4x4, const float* camera_position3,
+    int32_t start_from_first, int32_t max_trace_depth, float specular_threshold, int32_t use_others,
+    float* output_rgb3, float* output_depth1, float* output_acc1, float* output_normal3,
+    float* output_dist1, float* output_aux2, float* output_mid32, float* output_wet1,
+    char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (handle == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX trace handle is null", error_text,
+                        error_capacity);
+        }
+        if (ray_count > UINT32_MAX || coefficient_count == 0 || coefficient_count > 16 ||
+            degree > 3 || coefficient_count < (degree + 1) * (degree + 1) ||
+            (start_from_first != 0 && start_from_first != 1) || (use_others != 0 && use_others != 1) ||
+            max_trace_depth < 0 || max_trace_depth > 1 || !std::isfinite(scale_modifier) ||
+            scale_modifier <= 0.0f || !std::isfinite(specular_threshold)) {
+            return fail(HS_STATUS_RANGE_ERROR, "OptiX trace dimensions or scalars are invalid",
+                        error_text, error_capacity);
+        }
+        if (ray_count != 0 &&
+            (ray_origins3 == nullptr || ray_directions3 == nullptr || background3 == nullptr ||
+             means3d == nullptr || shs_m3 == nullptr || others2 == nullptr || opacities == nullptr ||
+             scales2 == nullptr || rotations4 == nullptr || viewmatrix4x4 == nullptr ||
+             projmatrix4x4 == nullptr || camera_position3 == nullptr || output_rgb3 == nullptr ||
+             output_depth1 == nullptr || output_acc1 == nullptr || output_normal3 == nullptr ||
+             output_dist1 == nullptr || output_aux2 == nullptr || output_mid32 == nullptr ||
+             output_wet1 == nullptr)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX trace received a null non-empty buffer",
+                        error_text, error_capacity);
+        }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        if (handle->tr_triangles == 0) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX scene is not built", error_text,
+                        error_capacity);
+        }
+        if (ray_count == 0) return ok(error_text, error_capacity);
+        hs::TraceCall call;
+        call.ray_count = ray_count;
+        call.ray_origins3 = ray_origins3;
+        call.ray_directions3 = ray_directions3;
+        call.background3 = background3;
+        call.means3d = means3d;
+        call.shs_m3 = shs_m3;
+        call.coefficient_count = coefficient_count;
+        call.degree = degree;
+        call.others2 = others2;
+        call.opacities = opacities;
+        call.scales2 = scales2;
+        call.scale_modifier = scale_modifier;
+        call.rotations4 = rotations4;
+        call.viewmatrix4x4 = viewmatrix4x4;
+        call.projmatrix4x4 = projmatrix4x4;
+        call.camera_position3 = camera_position3;
+        call.start_from_first = start_from_first;
+        call.max_trace_depth = max_trace_depth;
+        call.specular_threshold = specular_threshold;
+        call.use_others = use_others;
+        call.output_rgb3 = output_rgb3;
+        call.output_depth1 = output_depth1;
+        call.output_acc1 = output_acc1;
+        call.output_normal3 = output_normal3;
+        call.output_dist1 = output_dist1;
+        call.output_aux2 = output_aux2;
+        call.output_mid32 = output_mid32;
+        call.output_wet1 = output_wet1;
+        const cudaError_t e = hs::trace_rays(handle, call);
+        if (e != cudaSuccess) return cuda_failure(e, "reflection trace", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
 }
 
 int32_t hs_optix_workspace_stats_v1(HsRasterizerHandle handle, HsOptixWorkspaceStatsV1* stats,
                                     char* error_text, uint64_t error_capacity) noexcept {
     return guard(error_text, error_capacity, [&]() -> int32_t {
         if (handle == nullptr || stats == nullptr) {
-            return fail(HS_STATUS_INVALID_ARGUMENT, "handle or OptiX stats is null", error_text,
+            return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX stats received a null pointer", error_text,
                         error_capacity);
         }
         if (stats->struct_size != sizeof(HsOptixWorkspaceStatsV1) ||
             stats->abi_version != HS_RASTERIZER_ABI_VERSION) {
-            return fail(HS_STATUS_ABI_MISMATCH, "OptiX workspace stats ABI does not match",
-                        error_text, error_capacity);
+            return fail(HS_STATUS_ABI_MISMATCH, "OptiX stats ABI mismatch", error_text,
+                        error_capacity);
         }
-        const uint32_t size = stats->struct_size, abi = stats->abi_version;
-        std::memset(stats, 0, sizeof(*stats));
-        stats->struct_size = size;
-        stats->abi_version = abi;
+        std::lock_guard<std::mutex> lock(handle->mutex);
         stats->device = handle->device;
+        stats->scene_ready = handle->tr_triangles != 0 ? 1u : 0u;
+        stats->params_bytes = 0;
+        stats->gas_output_bytes = handle->tr_scene.bytes;
+        stats->gas_scratch_bytes = handle->tr_scratch.bytes;
+        stats->dist3_bytes = 0;
+        stats->current_bytes = hs::trace_current_bytes(handle);
+        stats->peak_bytes = handle->tr_peak_bytes;
+        stats->growth_count = handle->tr_growth_count;
+        stats->scene_signature = handle->tr_signature;
+        stats->gas_build_count = handle->tr_build_count;
+        stats->pipeline_create_count = handle->tr_pipeline_count;
         return ok(error_text, error_capacity);
     });
 }
@@ -927,8 +1042,14 @@ int32_t hs_optix_release_scene_v1(HsRasterizerHandle handle, char* error_text,
                                   uint64_t error_capacity) noexcept {
     return guard(error_text, error_capacity, [&]() -> int32_t {
         if (handle == nullptr) {
-            return fail(HS_STATUS_INVALID_ARGUMENT, "handle is null", error_text, error_capacity);
+            return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX release handle is null", error_text,
+                        error_capacity);
         }
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        const cudaError_t e = hs::trace_release(handle);
+        if (e != cudaSuccess) return cuda_failure(e, "release trace scene", error_text, error_capacity);
         return ok(error_text, error_capacity);
     });
 }

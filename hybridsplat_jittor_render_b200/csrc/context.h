@@ -154,6 +154,18 @@ struct HsRasterizerContext {
     cudaEvent_t std_count_event = nullptr;  // marks the standard totals readback
     cudaEvent_t fg_count_event = nullptr;   // marks the FlashGS totals readback
 
+    // Reflection trace (hs_optix_*): the scene BVH and its build scratch.
+    hs::DeviceBuffer tr_scene;     // BVH nodes + triangle records (the GAS)
+    hs::DeviceBuffer tr_scratch;   // build scratch (boxes, codes, sort, tree)
+    hs::DeviceBuffer tr_rays;      // per-call ray order (keys, sort scratch)
+    uint64_t tr_triangles = 0;     // triangles of the built scene (0: none)
+    uint32_t tr_root = 0;
+    uint64_t tr_signature = 0;
+    uint64_t tr_build_count = 0;
+    uint64_t tr_pipeline_count = 0;
+    uint64_t tr_growth_count = 0;
+    uint64_t tr_peak_bytes = 0;
+
     // Concurrent calls (forward_many): this context's calls run on its own
     // non-blocking stream, ordered against the caller's stream by events.
     cudaStream_t side_stream = nullptr;
@@ -264,6 +276,51 @@ cudaError_t standard_forward(HsRasterizerContext* context, const StandardCall& c
 cudaError_t standard_forward_many(HsRasterizerContext* const* contexts,
                                   const StandardCall* calls, uint32_t count,
                                   cudaStream_t stream);
+
+// Arguments of one hs_optix_trace_f32_v1 call (device pointers; checked by
+// the entry point).
+struct TraceCall {
+    uint64_t ray_count = 0;
+    const float* ray_origins3 = nullptr;
+    const float* ray_directions3 = nullptr;
+    const float* background3 = nullptr;
+    const float* means3d = nullptr;
+    const float* shs_m3 = nullptr;
+    uint32_t coefficient_count = 0;
+    uint32_t degree = 0;
+    const float* others2 = nullptr;
+    const float* opacities = nullptr;
+    const float* scales2 = nullptr;
+    float scale_modifier = 1.0f;
+    const float* rotations4 = nullptr;
+    const float* viewmatrix4x4 = nullptr;
+    const float* projmatrix4x4 = nullptr;
+    const float* camera_position3 = nullptr;
+    int32_t start_from_first = 0;
+    int32_t max_trace_depth = 0;
+    float specular_threshold = 0.0f;
+    int32_t use_others = 0;
+    float* output_rgb3 = nullptr;
+    float* output_depth1 = nullptr;
+    float* output_acc1 = nullptr;
+    float* output_normal3 = nullptr;
+    float* output_dist1 = nullptr;
+    float* output_aux2 = nullptr;
+    float* output_mid32 = nullptr;
+    float* output_wet1 = nullptr;
+    cudaStream_t stream = nullptr;
+};
+
+// Builds the trace scene (BVH) of `triangle_count` triangles over
+// `vertex_count` vertices (trace.cu); *bad_index is set (and
+// cudaErrorInvalidValue returned) when a triangle names a vertex outside the
+// vertex range. Synchronous.
+cudaError_t trace_build_scene(HsRasterizerContext* context, const float* vertices3, uint64_t vertex_count,
+                              const int32_t* triangles3, uint64_t triangle_count, bool* bad_index);
+// Traces call.ray_count rays against the built scene on call.stream.
+cudaError_t trace_rays(HsRasterizerContext* context, const TraceCall& call);
+cudaError_t trace_release(HsRasterizerContext* context);
+uint64_t trace_current_bytes(const HsRasterizerContext* context);
 
 // FlashGS host-side camera matrices (preprocess.cu:599-627), column-major.
 void flashgs_camera_matrices(const float position[3], const float rotation9[9], int width,

@@ -47,6 +47,19 @@ class RasterizerOutputs(NamedTuple):
     rendered: torch.Tensor
 
 
+class TraceOutputs(NamedTuple):
+    """Outputs of trace_reflection, named as the reference's OptixTraceOutputs
+    fields (ops/optix.py)."""
+    rgb: torch.Tensor
+    depth: torch.Tensor
+    acc: torch.Tensor
+    normal: torch.Tensor
+    dist: torch.Tensor
+    aux: torch.Tensor
+    mid: torch.Tensor
+    wet: torch.Tensor
+
+
 def _check_tensor(name: str, value: torch.Tensor, shape: tuple[int, ...], dtype=torch.float32) -> None:
     if not isinstance(value, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
@@ -586,6 +599,90 @@ def precise_disk_rotation(rotation_wxyz: torch.Tensor, *, library: ctypes.CDLL |
     count = int(rotation_wxyz.shape[0])
     out = torch.empty((count, 3, 3), dtype=torch.float32, device=rotation_wxyz.device)
     _elementwise("hs_rasterizer_precise_disk_rotation_f32_v1", library, _ptr(rotation_wxyz), count, _ptr(out))
+    return out
+
+
+# ---------------------------------------------------------------- reflection trace
+
+
+def gaussian_disks(xyz: torch.Tensor, rotation_raw: torch.Tensor, scaling: torch.Tensor, *,
+                   library: ctypes.CDLL | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """The trace scene of a Gaussian group (math.py:253-298): each Gaussian's
+    disk as the square of +-3 sigma in its plane, two triangles
+    (4g, 4g+1, 4g+2) and (4g+1, 4g+2, 4g+3) over the corners (-3, 3),
+    (-3, -3), (3, 3), (3, -3). The rotation is hs_rasterizer_precise_disk_rotation_f32_v1
+    of the raw quaternions; corner = (R[:, 0] s0) sx + (R[:, 1] s1) sy + xyz
+    in float32 (the reference forms the same products with a framework
+    matmul). Returns vertices [4P, 3] float32 and triangles [2P, 3] int32."""
+    count = int(xyz.shape[0])
+    _check_tensor("xyz", xyz, (count, 3))
+    _check_tensor("rotation_raw", rotation_raw, (count, 4))
+    _check_tensor("scaling", scaling, (count, 2))
+    rot = precise_disk_rotation(rotation_raw, library=library)
+    col0 = rot[:, :, 0] * scaling[:, 0:1]
+    col1 = rot[:, :, 1] * scaling[:, 1:2]
+    corners = torch.tensor([[-3.0, 3.0], [-3.0, -3.0], [3.0, 3.0], [3.0, -3.0]], dtype=torch.float32,
+                           device=xyz.device)
+    vertices = (col0[:, None, :] * corners[None, :, 0:1] + col1[:, None, :] * corners[None, :, 1:2]) + \
+        xyz[:, None, :]
+    idx = torch.arange(count * 4, dtype=torch.int32, device=xyz.device).view(count, 4)
+    triangles = torch.stack((idx[:, :3], idx[:, 1:]), dim=1).reshape(-1, 3).contiguous()
+    return vertices.reshape(-1, 3).contiguous(), triangles
+
+
+def build_trace_scene(vertices: torch.Tensor, triangles: torch.Tensor, *, scene_signature: int = 1,
+                      rebuild: bool = True, context: NativeRendererContext) -> int:
+    """hs_optix_build_scene_v1 (reference ops/optix.py build_optix_scene):
+    the trace scene of vertices [V, 3] float32 and triangles [T, 3] int32;
+    returns the device status word (0)."""
+    vertex_count, triangle_count = int(vertices.shape[0]), int(triangles.shape[0])
+    _check_tensor("vertices", vertices, (vertex_count, 3))
+    _check_tensor("triangles", triangles, (triangle_count, 3), dtype=torch.int32)
+    status = torch.full((1,), -1, dtype=torch.int32, device=vertices.device)
+    error = error_buffer()
+    rc = context.library.hs_optix_build_scene_v1(context.handle, _ptr(vertices), vertex_count, _ptr(triangles),
+                                                 triangle_count, int(scene_signature), int(bool(rebuild)),
+                                                 _ptr(status), error, len(error))
+    check_status(rc, "hs_optix_build_scene_v1", error)
+    return int(status.item())
+
+
+def trace_reflection(ray_origins: torch.Tensor, ray_directions: torch.Tensor, background: torch.Tensor,
+                     means3d: torch.Tensor, shs: torch.Tensor, others: torch.Tensor, opacities: torch.Tensor,
+                     scales: torch.Tensor, rotations: torch.Tensor, viewmatrix: torch.Tensor,
+                     projmatrix: torch.Tensor, camera_position: torch.Tensor, *, degree: int,
+                     scale_modifier: float = 1.0, start_from_first: bool = False, max_trace_depth: int = 0,
+                     specular_threshold: float = 0.0, use_others: bool = True,
+                     context: NativeRendererContext, out: TraceOutputs | None = None) -> TraceOutputs:
+    """hs_optix_trace_f32_v1 (reference ops/optix.py trace_optix): one ray per
+    Gaussian of the traced group against the scene built by
+    build_trace_scene; shs is [P, M, 3]."""
+    count = int(ray_origins.shape[0])
+    coefficients = int(shs.shape[1])
+    for name, value, shape in (("ray_origins", ray_origins, (count, 3)), ("ray_directions", ray_directions, (count, 3)),
+                               ("background", background, (3,)), ("means3d", means3d, (count, 3)),
+                               ("shs", shs, (count, coefficients, 3)), ("others", others, (count, 2)),
+                               ("opacities", opacities, (count, 1)), ("scales", scales, (count, 2)),
+                               ("rotations", rotations, (count, 4)), ("viewmatrix", viewmatrix, (4, 4)),
+                               ("projmatrix", projmatrix, (4, 4)), ("camera_position", camera_position, (3,))):
+        _check_tensor(name, value, shape)
+    if isinstance(degree, bool) or not isinstance(degree, int) or degree not in range(4):
+        raise ValueError("degree must be an integer in [0, 3]")
+    if max_trace_depth not in (0, 1) or isinstance(max_trace_depth, bool):
+        raise ValueError("max_trace_depth must be 0 or 1")
+    if out is None:
+        f = dict(dtype=torch.float32, device=ray_origins.device)
+        out = TraceOutputs(torch.empty((count, 3), **f), torch.empty((count, 1), **f), torch.empty((count, 1), **f),
+                           torch.empty((count, 3), **f), torch.empty((count, 1), **f), torch.empty((count, 2), **f),
+                           torch.empty((count, 32), **f), torch.empty((count, 1), **f))
+    error = error_buffer()
+    rc = context.library.hs_optix_trace_f32_v1(
+        context.handle, count, _ptr(ray_origins), _ptr(ray_directions), _ptr(background), _ptr(means3d), _ptr(shs),
+        coefficients, degree, _ptr(others), _ptr(opacities), _ptr(scales), _finite("scale_modifier", scale_modifier),
+        _ptr(rotations), _ptr(viewmatrix), _ptr(projmatrix), _ptr(camera_position), int(bool(start_from_first)),
+        int(max_trace_depth), _finite("specular_threshold", specular_threshold), int(bool(use_others)),
+        *[_ptr(t) for t in out], error, len(error))
+    check_status(rc, "hs_optix_trace_f32_v1", error)
     return out
 
 

@@ -12,16 +12,17 @@ import sys
 from pathlib import Path
 
 ORACLE_DIR = Path(__file__).resolve().parent
-SOURCE = ORACLE_DIR / "cpu_oracle.c"
+SOURCES = (ORACLE_DIR / "cpu_oracle.c", ORACLE_DIR / "trace_oracle.c")
 LIBRARY = ORACLE_DIR / "libcpu_oracle.so"
 
 
 def build(force: bool = False) -> Path:
-    if not force and LIBRARY.exists() and LIBRARY.stat().st_mtime >= max(SOURCE.stat().st_mtime, Path(__file__).stat().st_mtime):
+    newest = max([src.stat().st_mtime for src in SOURCES] + [Path(__file__).stat().st_mtime])
+    if not force and LIBRARY.exists() and LIBRARY.stat().st_mtime >= newest:
         return LIBRARY
     cc = shutil.which("gcc") or "gcc"
     command = [cc, "-O2", "-std=c11", "-ffp-contract=off", "-fopenmp", "-fPIC", "-shared",
-               "-fvisibility=hidden", str(SOURCE), "-o", str(LIBRARY), "-lm"]
+               "-fvisibility=hidden", *[str(src) for src in SOURCES], "-o", str(LIBRARY), "-lm"]
     done = subprocess.run(command, capture_output=True, text=True)
     if done.returncode != 0:
         raise RuntimeError("CPU oracle build failed:\n" + " ".join(command) + "\n" + done.stderr)

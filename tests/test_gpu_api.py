@@ -102,9 +102,18 @@ def test_prefiltered_violation_is_reported_not_trapped(golden):
         assert int(out.rendered.item()) == 0
 
 
-def test_optix_entry_points_report_unavailable():
+def test_trace_scene_build_checks_arguments_like_the_reference():
+    """hs_optix_build_scene_v1 rejects null buffers (status 1) and zero sizes
+    or a zero signature (status 3) with the reference's texts
+    (optix_backend.cpp:375-400); release without a scene is fine."""
     with NativeRendererContext(0) as ctx:
         err = nr.error_buffer()
         status = ctx.library.hs_optix_build_scene_v1(ctx.handle, None, 0, None, 0, 0, 0, None, err, len(err))
-        assert status == 7 and b"OptiX" in err.value
+        assert status == 1 and b"null buffer" in err.value
+        v = torch.zeros((4, 3), device="cuda")
+        t = torch.tensor([[0, 1, 2]], dtype=torch.int32, device="cuda")
+        st = torch.zeros(1, dtype=torch.int32, device="cuda")
+        status = ctx.library.hs_optix_build_scene_v1(ctx.handle, v.data_ptr(), 4, t.data_ptr(), 1, 0, 0,
+                                                     st.data_ptr(), err, len(err))
+        assert status == 3 and b"dimensions or scalars" in err.value
         ctx.release_optix_scene()
