@@ -414,8 +414,7 @@ __global__ void __launch_bounds__(kRenderThreads, 7) render_kernel(
             for (int k = 0; k < live_count; ++k) {
                 const BlendRecord g = load_record(my_slots + k * kRecordQuads);
                 const ColumnTerms col = column_terms(r, fx, g);
-                float w = blend(r, s0, col, fy0, g);
-                w += blend(r, s1, col, fy1, g);
+                const float w = blend2(r, s0, s1, col, fy0, fy1, g);
                 if (__any_sync(0xffffffffu, w != 0.0f)) {
                     // The Gaussian's blend weight over the warp's 64 pixels, summed
                     // exactly in 2^-24 fixed point by one warp reduction (each

@@ -211,6 +211,79 @@ __device__ __forceinline__ float blend(const R& r, PixelState& s, const ColumnTe
     return w;
 }
 
+// The alpha of one pixel x Gaussian evaluation, with the operations of blend()
+// up to its alpha test but no early exit: `live` is false exactly where
+// blend() returns before its transmittance test (a done pixel, p.z == 0,
+// depth < near, power > 0, alpha < 1/255; NaNs pass as they do there).
+template <class R>
+__device__ __forceinline__ float alpha_of(const R& r, const PixelState& s, const ColumnTerms& col, float py,
+                                          const BlendRecord& g, float& depth, bool& live) {
+    const int vk = r(S_K);
+    const float lx = msub(vk, py, g.twx, g.tvx);
+    const float ly = msub(vk, py, g.twy, g.tvy);
+    const float lz = msub(vk, py, g.twz, g.tvz);
+    const int vc = r(S_CROSS);
+    const float pzv = diff2(vc, col.kx, ly, col.ky, lx);
+    const float pxv = diff2(vc, col.ky, lz, col.kz, ly);
+    const float pyv = diff2(vc, col.kz, lx, col.kx, lz);
+    const float sx = div(pxv, pzv);
+    const float sy = div(pyv, pzv);
+    const float rho3d = dot2(r(S_RHO3), sx, sx, sy, sy);
+    const float dy = sub(g.y, py);
+    const float rho2d = mul(2.0f, dot2(r(S_RHO2), col.dx, col.dx, dy, dy));
+    const float rho = fminf(rho3d, rho2d);
+    depth = rho3d <= rho2d ? add(dot2(r(S_DEPTH), sx, g.twx, sy, g.twy), g.twz) : g.twz;
+    const float power = mul(-0.5f, rho);
+    const float alpha = fminf(0.99f, mul(g.op, expf(power)));
+    live = !s.done && pzv != 0.0f && !(depth < kNear) && !(power > 0.0f) && !(alpha < 1.0f / 255.0f);
+    return alpha;
+}
+
+// The state update of blend() after its alpha test. Returns w.
+template <class R>
+__device__ __forceinline__ float apply(const R& r, PixelState& s, float alpha, float depth, const BlendRecord& g) {
+    const float test_t = mul(s.t, sub(1.0f, alpha));
+    if (test_t < 0.0001f) {
+        s.done = true;
+        return 0.0f;
+    }
+    const float w = mul(alpha, s.t);
+    const float a = sub(1.0f, s.t);
+    const float m = mul(kFar / (kFar - kNear), sub(1.0f, div(kNear, depth)));
+    const float mm = mul(m, m);
+    const int va = r(S_ACC);
+    const float dd = nmad(r(S_D2), mad(r(S_D1), mm, a, s.m2), mul(2.0f, m), s.m1);
+    s.dist = mad(va, dd, w, s.dist);
+    s.d = mad(va, depth, w, s.d);
+    s.m1 = mad(va, m, w, s.m1);
+    s.m2 = mad(va, mm, w, s.m2);
+    if (s.t > 0.5f) s.median = depth;
+    s.n[0] = mad(va, g.nx, w, s.n[0]);
+    s.n[1] = mad(va, g.ny, w, s.n[1]);
+    s.n[2] = mad(va, g.nz, w, s.n[2]);
+#pragma unroll
+    for (int k = 0; k < 5; ++k) s.c[k] = mad(va, g.c[k], w, s.c[k]);
+    s.t = test_t;
+    return w;
+}
+
+// blend() for a lane's two pixels (same column, rows py0 and py1): both
+// alphas are computed without branches, so their dependency chains
+// interleave; each update is applied where blend() would apply it. Returns
+// the sum of the two weights.
+template <class R>
+__device__ __forceinline__ float blend2(const R& r, PixelState& s0, PixelState& s1, const ColumnTerms& col,
+                                        float py0, float py1, const BlendRecord& g) {
+    float d0, d1;
+    bool live0, live1;
+    const float a0 = alpha_of(r, s0, col, py0, g, d0, live0);
+    const float a1 = alpha_of(r, s1, col, py1, g, d1, live1);
+    float w = 0.0f;
+    if (live0) w = apply(r, s0, a0, d0, g);
+    if (live1) w += apply(r, s1, a1, d1, g);
+    return w;
+}
+
 // ---------------------------------------------------------------- culling
 //
 // A pixel x Gaussian evaluation changes the pixel state only when
