@@ -21,9 +21,11 @@ copied into this repository. Two artefacts are produced:
     The host-only FlashGS NPZ activation (``rasterizer/flashgs_prepare.cpp``)
     built with g++; it runs on any CPU and pins the host activation bit-exactly.
 
-Usage: ``python oracle/build_ref.py [--reference /root/reference] [--jobs 8]``.
-When the reference checkout is absent the script does nothing and exits 0;
-prebuilt ``oracle/_ref`` files are then used as they are.
+Usage: ``python oracle/build_ref.py [--reference PATH] [--jobs 8]``. The
+reference checkout is ``--reference``, else the environment variable
+``HYBRIDSPLAT_REFERENCE_ROOT``, else a directory named ``reference`` beside
+the directory holding this repository. When it is absent the script does
+nothing and exits 0; prebuilt ``oracle/_ref`` files are then used as they are.
 """
 
 from __future__ import annotations
@@ -38,7 +40,14 @@ from pathlib import Path
 
 ORACLE_DIR = Path(__file__).resolve().parent
 OUT_DIR = ORACLE_DIR / "_ref"
-DEFAULT_REFERENCE = Path("/root/reference")
+REPO_DIR = ORACLE_DIR.parent
+
+
+def default_reference() -> Path:
+    """--reference default: $HYBRIDSPLAT_REFERENCE_ROOT, else ../reference
+    beside the repository."""
+    env = os.environ.get("HYBRIDSPLAT_REFERENCE_ROOT")
+    return Path(env) if env else REPO_DIR.parent / "reference"
 
 # Release-mode flags CMake adds for both languages (CMAKE_<LANG>_FLAGS_RELEASE).
 _RELEASE = ["-O3", "-DNDEBUG"]
@@ -128,9 +137,9 @@ def _compile(job: tuple[list[str], Path]) -> tuple[Path, str]:
     return target, completed.stderr
 
 
-def build(reference: Path = DEFAULT_REFERENCE, jobs: int = 8, force: bool = False) -> bool:
+def build(reference: Path | None = None, jobs: int = 8, force: bool = False) -> bool:
     """Build both oracle libraries. Returns False when the reference is absent."""
-    native = _native(reference)
+    native = _native(reference if reference is not None else default_reference())
     if not native.is_dir():
         return False
     cuda_home = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
@@ -190,7 +199,7 @@ def build(reference: Path = DEFAULT_REFERENCE, jobs: int = 8, force: bool = Fals
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
+    parser.add_argument("--reference", type=Path, default=None)
     parser.add_argument("--jobs", type=int, default=8)
     parser.add_argument("--force", action="store_true")
     arguments = parser.parse_args()
