@@ -994,6 +994,28 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
             "host_link_ceiling_fps": ceiling, "fraction_of_host_link_ceiling": value / ceiling}
 
 
+def cpu_stages_block() -> dict:
+    """The reference's CPU-side stages on the CPU plumbing workload (10k + 2k
+    Gaussians, SH 3, 20 views): checkpoint validation, activation, the
+    FlashGS host activation as shipped, both camera loaders and the camera
+    matrices, median wall ms on one thread. The stages that run the
+    reference's Python are read from the committed measurement (the
+    reference checkout is not on this host); the rest are timed here."""
+    from oracle import cpu_stages
+
+    block = {"workload": "cpu_plumbing (10000 base + 2000 reflective Gaussians, SH degree 3, 20 views "
+                         "1292x839)", "unit": "ms", "statistic": "median of 7 runs, one thread"}
+    if cpu_stages.RESULTS.exists():
+        committed = json.loads(cpu_stages.RESULTS.read_text())
+        block["all_stages"] = {"host": committed["host"], "total_ms": committed["total_ms"],
+                                   "stages_ms": {k: v["ms"] for k, v in committed["stages"].items()},
+                                   "source": "oracle/cpu_stages_config0.json (" + committed["command"] + ")"}
+    live = cpu_stages.host_stages(7)
+    block["gpu_host"] = {"host": cpu_stages.host_info(), "stages_ms": {k: v["ms"] for k, v in live.items()},
+                          "what": "stages that need no reference Python, timed live on this GPU host"}
+    return block
+
+
 def roofline_and_baselines(args, workload: Workload, frame: Frame, cams, scene: DeviceScene, stages: dict,
                            clocks: dict, headline_ms: float) -> dict:
     out = {}
@@ -1009,6 +1031,8 @@ def roofline_and_baselines(args, workload: Workload, frame: Frame, cams, scene: 
                                "kind": "port",
                                "sample": f"one full {args.backend} frame (base + reflection) of the benchmark "
                                          f"scene by the CPU oracle, {threads} threads, {cpu['wall_s']:.1f} s"}
+    if not args.no_cpu_baseline:
+        out["cpu_stages"] = cpu_stages_block()
     # Roofline of the dominant kernel: the rasteriser's launch for the base
     # group of view 0 (FP32-pipe bound). Work = the reference-rule
     # evaluations counted by the CPU oracle on the same view, split into
