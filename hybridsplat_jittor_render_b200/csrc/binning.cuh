@@ -76,11 +76,13 @@ __device__ __forceinline__ uint32_t warp_sum(uint32_t v) {
     return v;
 }
 
-// first_pair[order[i]] = sum(counts[order[j]] for j < i).
+// first_pair[order[i]] = sum(counts[order[j]] for j < i), for i below
+// *live_count (the Gaussians a dropping depth sort kept) or, when live_count
+// is null, below count. The grid covers count; blocks past the live items leave.
 static __global__ void __launch_bounds__(kScanThreads) offsets_kernel(
-    uint32_t count, const uint32_t* __restrict__ order, const uint32_t* __restrict__ counts,
-    uint32_t* __restrict__ control, uint32_t* __restrict__ error,
-    uint32_t* __restrict__ first_pair) {
+    uint32_t count, const uint32_t* __restrict__ live_count, const uint32_t* __restrict__ order,
+    const uint32_t* __restrict__ counts, uint32_t* __restrict__ control,
+    uint32_t* __restrict__ error, uint32_t* __restrict__ first_pair) {
     __shared__ uint32_t warp_sums[kScanThreads / 32];
     __shared__ uint32_t tile_slot, tile_prefix;
     uint32_t* counter = control;
@@ -90,6 +92,8 @@ static __global__ void __launch_bounds__(kScanThreads) offsets_kernel(
     if (threadIdx.x == 0) tile_slot = atomicAdd(counter, 1u);
     __syncthreads();
     const uint32_t tile = tile_slot;
+    if (live_count != nullptr) count = *live_count;
+    if (static_cast<uint64_t>(tile) * kScanTile >= count) return;  // no block waits on a later tile
     const uint64_t base = static_cast<uint64_t>(tile) * kScanTile +
                           static_cast<uint64_t>(threadIdx.x) * kScanItems;
     uint32_t gid[kScanItems], cnt[kScanItems];

@@ -216,7 +216,7 @@ cudaError_t FlashgsPass::begin() {
     if (st != cudaSuccess) return st;
     // A wait that gave up in an earlier call must not fail this one.
     st = cudaMemsetAsync(ctx_->device_error, 0, sizeof(uint32_t), stream);
-    if (st == cudaSuccess) st = cudaMemsetAsync(gv_.total, 0, 4 * sizeof(uint32_t), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(gv_.total, 0, 8 * sizeof(uint32_t), stream);
     if (st != cudaSuccess) return st;
 
     const int blocks = (c_.point_count + kPreThreads - 1) / kPreThreads;
@@ -237,8 +237,9 @@ cudaError_t FlashgsPass::begin() {
     // point, flashgs_backend.cu:480-488).
     const uint32_t stall = ctx_->test_stall_tile;  // test hook, one call only
     ctx_->test_stall_tile = sort::kNoStall;
+    // Gaussians without pairs are left out of it (total[4] counts the others).
     return sort::sort_pairs(gv_.keys, gv_.order, gv_.alt_keys, gv_.alt_order, c_.point_count, 0,
-                            32, ctx_->fg_sort.ptr, stream, ctx_->device_error, stall);
+                            32, ctx_->fg_sort.ptr, stream, ctx_->device_error, stall, gv_.total + 4);
 }
 
 cudaError_t FlashgsPass::bin() {
@@ -283,7 +284,7 @@ cudaError_t FlashgsPass::bin() {
             // the first pair slot of every Gaussian.
             uint32_t* first_pair = gv_.alt_keys;
             bin::offsets_kernel<<<bin::scan_tiles(c_.point_count), bin::kScanThreads, 0, stream>>>(
-                static_cast<uint32_t>(c_.point_count), gv_.order, gv_.counts,
+                static_cast<uint32_t>(c_.point_count), gv_.total + 4, gv_.order, gv_.counts,
                 static_cast<uint32_t*>(ctx_->fg_sort.ptr), ctx_->device_error, first_pair);
             st = cudaGetLastError();
             if (st != cudaSuccess) return st;

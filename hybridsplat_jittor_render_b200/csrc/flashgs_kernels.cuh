@@ -123,6 +123,9 @@ __global__ void __launch_bounds__(kPreThreads, 12) preprocess_kernel(
     const uint32_t hits = s_hits[threadIdx.x];
     const uint32_t total_hits = bin::warp_sum(hits);
     if (lane == 0 && total_hits != 0u) atomicAdd(totals, total_hits);
+    // Gaussians with pairs: the items the depth sort keeps (totals[4])
+    const uint32_t kept = bin::warp_sum(hits > 0 ? 1u : 0u);
+    if (lane == 0 && kept != 0u) atomicAdd(totals + 4, kept);
     if (!active) return;
     // Single-tile Gaussians always keep their record (preprocess.cu:482-506).
     const bool write = candidate && (full_area == 1u || hits > 0);
@@ -153,7 +156,9 @@ __global__ void __launch_bounds__(kPreThreads, 12) preprocess_kernel(
     const uint32_t lo = static_cast<uint32_t>(g.rect_min.x) | (static_cast<uint32_t>(area != 0u ? ry0 : 0) << 16);
     const uint32_t hi = static_cast<uint32_t>(g.rect_max.x) | (static_cast<uint32_t>(area != 0u ? ry1 : 0) << 16);
     em[1] = f4(g.conic.z, g.power, __uint_as_float(lo), __uint_as_float(hi));
-    depth_keys[idx] = hits > 0 ? __float_as_uint(g.depth) : 0xffffffffu;
+    // without pairs: the depth sort's dropped key, which a Gaussian with pairs
+    // never takes (a NaN depth's bits are at most 0xfffffffe here)
+    depth_keys[idx] = hits > 0 ? min(__float_as_uint(g.depth), sort::kDropKey - 1u) : sort::kDropKey;
     order[idx] = static_cast<uint32_t>(idx);
     pair_counts[idx] = hits;
 }

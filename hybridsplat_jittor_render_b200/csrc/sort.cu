@@ -67,13 +67,14 @@ __device__ __forceinline__ uint32_t digit_of(uint32_t key, int shift, uint32_t m
 // arrays are 16-byte aligned), per-block shared-memory counts.
 __global__ void __launch_bounds__(kThreads) histogram_kernel(const uint32_t* __restrict__ keys,
                                                              uint32_t count, int begin_bit,
-                                                             int end_bit,
+                                                             int end_bit, int drop,
                                                              uint32_t* __restrict__ hist) {
     __shared__ uint32_t bins[kMaxPasses][kBins];
     const int passes = (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
     for (int p = 0; p < passes; ++p) bins[p][threadIdx.x] = 0;
     __syncthreads();
     auto count_key = [&](uint32_t key) {
+        if (drop && key == kDropKey) return;  // left out of a dropping sort
         for (int p = 0; p < passes; ++p) {
             const int shift = begin_bit + p * kRadixBits;
             const int bits = min(kRadixBits, end_bit - shift);
@@ -154,8 +155,9 @@ __device__ __forceinline__ uint32_t block_exclusive_256(uint32_t v, uint32_t* wa
 template <int kItems, int kWindow, bool kBallot>
 __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel(
     const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
-    uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, uint32_t count, int shift,
-    int bits, uint32_t tiles, const uint32_t* __restrict__ hist, uint32_t* __restrict__ counter,
+    uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, uint32_t count,
+    const uint32_t* __restrict__ live_count, int drop, int shift, int bits,
+    const uint32_t* __restrict__ hist, uint32_t* __restrict__ counter,
     uint32_t* __restrict__ status, uint32_t* __restrict__ error, uint32_t stall_tile) {
     constexpr uint32_t kTileItems = kThreads * kItems;
     constexpr uint32_t kWarpItems = kTileItems / kWarps;  // contiguous items per warp
@@ -167,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
     __shared__ uint32_t global_base[kBins];   // destination of the digit run's first item
     __shared__ uint32_t warp_sums[kWarps];
     __shared__ uint32_t tile_slot;
+    __shared__ uint32_t tile_kept;            // items of the tile that are written
     __shared__ alignas(8) uint64_t loaded;    // completes when the bulk copies land
 
     // An earlier pass gave up a wait: its output is not a permutation of the
@@ -184,7 +187,12 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
     __syncthreads();
     const uint32_t tile = tile_slot;
     const uint64_t tile_begin = static_cast<uint64_t>(tile) * kTileItems;
-    const uint64_t left = count - tile_begin;
+    // Passes after a dropping first pass sort its *live_count survivors; the
+    // grid is sized for all items, and blocks past the survivors leave (no
+    // block waits on a later tile).
+    const uint32_t items = live_count != nullptr ? *live_count : count;
+    if (tile_begin >= items) return;
+    const uint64_t left = items - tile_begin;
     const uint32_t n = left < static_cast<uint64_t>(kTileItems) ? static_cast<uint32_t>(left)
                                                                 : kTileItems;
     const uint32_t bulk = n & ~3u;  // whole 16-byte groups go through the copy engine
@@ -223,8 +231,9 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
         const uint32_t i = seg + static_cast<uint32_t>(k) * 32u + lane;
-        const bool valid = i < n;
-        const uint32_t dg = valid ? digit_of(tile_keys[i], shift, mask) : 0u;
+        const uint32_t key = i < n ? tile_keys[i] : 0u;
+        const bool valid = i < n && !(drop && key == kDropKey);
+        const uint32_t dg = valid ? digit_of(key, shift, mask) : 0u;
         uint32_t peers;
         if (kBallot) {
             // lanes holding the same digit, one ballot per digit bit (cheaper
@@ -277,16 +286,19 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
     const uint32_t local_start = block_exclusive_256(total, warp_sums);
     digit_start[b] = local_start;
     global_base[b] = digit_global + earlier;
+    if (b == kBins - 1) tile_kept = local_start + total;
 
     // 4. permute the tile into digit order in place (keys, then values), then
     //    write digit runs
     uint32_t item[kItems];
     __syncthreads();  // digit_start / global_base
 #pragma unroll
+    bool keep[kItems];
     for (int k = 0; k < kItems; ++k) {
         const uint32_t i = seg + static_cast<uint32_t>(k) * 32u + lane;
         item[k] = tile_keys[i];
-        if (i < n) {
+        keep[k] = i < n && !(drop && item[k] == kDropKey);
+        if (keep[k]) {
             const uint32_t d = digit_of(item[k], shift, mask);
             rank[k] += digit_start[d] + warp_count[warp][d];  // final position in the tile
         }
@@ -294,17 +306,18 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
-        if (seg + static_cast<uint32_t>(k) * 32u + lane < n) tile_keys[rank[k]] = item[k];
+        if (keep[k]) tile_keys[rank[k]] = item[k];
     }
 #pragma unroll
     for (int k = 0; k < kItems; ++k) item[k] = tile_vals[seg + static_cast<uint32_t>(k) * 32u + lane];
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
-        if (seg + static_cast<uint32_t>(k) * 32u + lane < n) tile_vals[rank[k]] = item[k];
+        if (keep[k]) tile_vals[rank[k]] = item[k];
     }
     __syncthreads();
-    for (uint32_t i = threadIdx.x; i < n; i += kThreads) {
+    const uint32_t written = tile_kept;  // n unless the pass drops items
+    for (uint32_t i = threadIdx.x; i < written; i += kThreads) {
         const uint32_t k = tile_keys[i];
         const uint32_t d = digit_of(k, shift, mask);
         const uint32_t dst = global_base[d] + (i - digit_start[d]);
@@ -323,11 +336,16 @@ uint64_t sort_scratch_bytes(uint32_t count) {
 
 cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals,
                        uint32_t count, int begin_bit, int end_bit, void* scratch,
-                       cudaStream_t stream, uint32_t* error, uint32_t stall_tile) {
+                       cudaStream_t stream, uint32_t* error, uint32_t stall_tile,
+                       const uint32_t* kept) {
     if (count == 0 || end_bit <= begin_bit) return cudaSuccess;
     if (count > kMaxItems || end_bit - begin_bit > kMaxPasses * kRadixBits) {
         return cudaErrorInvalidValue;
     }
+    // dropping needs the whole key (the dropped key is all ones) and an even
+    // pass count (the survivors end in keys/vals without a copy)
+    if (kept != nullptr && (begin_bit != 0 || end_bit != 32)) return cudaErrorInvalidValue;
+    const int drop = kept != nullptr ? 1 : 0;
     const uint32_t tiles = tiles_for(count);
     const bool large = count >= kLargeTileItems;
     const uint32_t large_tiles =
@@ -345,7 +363,7 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
     }
     const uint32_t hist_cap = static_cast<uint32_t>(sms) * 8u;
     const uint32_t hist_blocks = tiles < hist_cap ? tiles : hist_cap;
-    histogram_kernel<<<hist_blocks, kThreads, 0, stream>>>(keys, count, begin_bit, end_bit,
+    histogram_kernel<<<hist_blocks, kThreads, 0, stream>>>(keys, count, begin_bit, end_bit, drop,
                                                            s.hist);
     uint32_t* src_k = keys;
     uint32_t* src_v = vals;
@@ -356,19 +374,23 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
         const int bits = min(kRadixBits, end_bit - shift);
         const uint32_t stall = pass == 0 ? stall_tile : kNoStall;
         uint32_t* pass_status = s.status + static_cast<uint64_t>(pass) * tiles * kBins;
+        // the first pass of a dropping sort reads every item and drops; the
+        // later ones sort the *kept survivors
+        const uint32_t* live = pass > 0 ? kept : nullptr;
+        const int pass_drop = pass == 0 ? drop : 0;
         if (large && ballot) {
             onesweep_kernel<kLargeItems, kLargeWindow, true><<<large_tiles, kThreads, 0, stream>>>(
-                src_k, src_v, dst_k, dst_v, count, shift, bits, large_tiles,
+                src_k, src_v, dst_k, dst_v, count, live, pass_drop, shift, bits,
                 s.hist + pass * kBins, s.counters + pass, pass_status, error, stall);
         } else if (large) {
             onesweep_kernel<kLargeItems, kLargeWindow, false><<<large_tiles, kThreads, 0, stream>>>(
-                src_k, src_v, dst_k, dst_v, count, shift, bits, large_tiles,
+                src_k, src_v, dst_k, dst_v, count, live, pass_drop, shift, bits,
                 s.hist + pass * kBins, s.counters + pass, pass_status, error, stall);
         } else {
             onesweep_kernel<kItemsPerThread, kLookBackWindow, false>
-                <<<tiles, kThreads, 0, stream>>>(src_k, src_v, dst_k, dst_v, count, shift, bits,
-                                                 tiles, s.hist + pass * kBins, s.counters + pass,
-                                                 pass_status, error, stall);
+                <<<tiles, kThreads, 0, stream>>>(src_k, src_v, dst_k, dst_v, count, live,
+                                                 pass_drop, shift, bits, s.hist + pass * kBins,
+                                                 s.counters + pass, pass_status, error, stall);
         }
         uint32_t* tk = src_k;
         uint32_t* tv = src_v;

@@ -54,6 +54,9 @@ inline uint32_t tiles_for(uint32_t count) { return (count + kTile - 1) / kTile; 
 // Scratch bytes needed by sort_pairs for `count` items.
 uint64_t sort_scratch_bytes(uint32_t count);
 
+// Key of an item that a dropping sort leaves out (see sort_pairs' kept).
+constexpr uint32_t kDropKey = 0xffffffffu;
+
 // Stable sort of keys[0, count) by bits [begin_bit, end_bit) of the key.
 // keys/vals hold the input and receive the output; alt_keys/alt_vals are
 // ping-pong buffers of the same size. scratch holds sort_scratch_bytes(count)
@@ -61,12 +64,18 @@ uint64_t sort_scratch_bytes(uint32_t count);
 // already set on entry every pass does nothing. stall_tile is a test hook:
 // the block of that tile in the first pass never publishes its look-back
 // status, so the waits of its successors run out (kNoStall: none).
+// kept (device word, may be null; full 32-bit sorts only): the items whose
+// key is kDropKey are left out. *kept, written by an earlier kernel of the
+// stream, must be the number of the other items; they are sorted into
+// keys/vals[0, *kept) in the same stable order, and the passes after the
+// first only touch those. The depth sorts use it to skip the Gaussians that
+// emit no pair.
 // Launches: one memset, one histogram kernel, one kernel per 8-bit pass
 // (plus two copies when the pass count is odd).
 cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals,
                        uint32_t count, int begin_bit, int end_bit, void* scratch,
                        cudaStream_t stream, uint32_t* error = nullptr,
-                       uint32_t stall_tile = kNoStall);
+                       uint32_t stall_tile = kNoStall, const uint32_t* kept = nullptr);
 
 // Number of bits needed to hold values in [0, n): the reference's
 // getHigherMsb(n) for the tile count (sort.cu:141-156).

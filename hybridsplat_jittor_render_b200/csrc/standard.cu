@@ -57,7 +57,8 @@ struct GeometryViews {
     uint32_t* counts;
     uint32_t* alt_keys;
     uint32_t* alt_order;
-    uint32_t* totals;  // [0] reference pairs, [1] prefiltered violation, [2] emitted pairs
+    uint32_t* totals;  // [0] reference pairs, [1] prefiltered violation, [2] emitted pairs,
+                       // [4] Gaussians with pairs
 };
 
 GeometryViews geometry_views(void* base, uint64_t count) {
@@ -235,7 +236,7 @@ cudaError_t StandardPass::begin() {
     // A wait that gave up in an earlier call must not fail this one.
     st = cudaMemsetAsync(ctx_->device_error, 0, sizeof(uint32_t), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(c_.output_weight, 0, count_ * sizeof(float), stream);
-    if (st == cudaSuccess) st = cudaMemsetAsync(gv_.totals, 0, 4 * sizeof(uint32_t), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(gv_.totals, 0, 8 * sizeof(uint32_t), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(ranges_, 0, tiles_ * sizeof(uint2), stream);
     if (st != cudaSuccess) return st;
     const int blocks = (c_.point_count + kPreThreads - 1) / kPreThreads;
@@ -253,10 +254,12 @@ cudaError_t StandardPass::begin() {
     if (st != cudaSuccess) return st;
     marks_.mark(1);
     // The depth sort does not depend on the totals: queue it before waiting.
+    // It leaves out the Gaussians that emit no pair (totals[4] counts the
+    // others, which alone enter the offset scan).
     const uint32_t stall = ctx_->test_stall_tile;  // test hook, one call only
     ctx_->test_stall_tile = sort::kNoStall;
     return sort::sort_pairs(gv_.keys, gv_.order, gv_.alt_keys, gv_.alt_order, c_.point_count, 0, 32,
-                            geometry_scratch_, stream, ctx_->device_error, stall);
+                            geometry_scratch_, stream, ctx_->device_error, stall, gv_.totals + 4);
 }
 
 cudaError_t StandardPass::bin() {
@@ -291,7 +294,7 @@ cudaError_t StandardPass::bin() {
         // first pair slot of every Gaussian.
         uint32_t* first_pair = gv_.alt_keys;
         bin::offsets_kernel<<<bin::scan_tiles(c_.point_count), bin::kScanThreads, 0, stream>>>(
-            static_cast<uint32_t>(c_.point_count), gv_.order, gv_.counts,
+            static_cast<uint32_t>(c_.point_count), gv_.totals + 4, gv_.order, gv_.counts,
             static_cast<uint32_t*>(geometry_scratch_), ctx_->device_error, first_pair);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;

@@ -24,7 +24,8 @@ struct PreprocessOut {
     uint32_t* order;
     uint32_t* counts;        // pairs emitted per Gaussian
     int32_t* radii;
-    uint32_t* totals;        // [0] reference pair count, [1] prefiltered violation, [2] emitted
+    uint32_t* totals;        // [0] reference pair count, [1] prefiltered violation, [2] emitted,
+                             // [4] Gaussians that emit pairs (kept by the depth sort)
 };
 
 __device__ __forceinline__ void warp_add(uint32_t* dst, uint32_t v) {
@@ -181,11 +182,15 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_kernel(
     emitted = warp_live_tiles(cs, x0, y0, x1, y1, valid, live_sums + (threadIdx.x & ~31));
     if (valid) {
         out.counts[idx] = emitted;
-        out.depth_keys[idx] = emitted != 0 ? __float_as_uint(depth) : 0xffffffffu;
+        // a Gaussian without pairs takes the depth sort's dropped key; one with
+        // pairs never does (a NaN depth's bits are at most 0xfffffffe here)
+        out.depth_keys[idx] = emitted != 0 ? min(__float_as_uint(depth), sort::kDropKey - 1u)
+                                           : sort::kDropKey;
     }
     warp_add(out.totals + 0, area);
     warp_add(out.totals + 1, violation);
     warp_add(out.totals + 2, emitted);
+    warp_add(out.totals + 4, emitted != 0 ? 1u : 0u);  // Gaussians the depth sort keeps
 }
 
 // Pair emission by rows. Each warp owns 32 Gaussians (in index order) and

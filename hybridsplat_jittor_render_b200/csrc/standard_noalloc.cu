@@ -157,7 +157,7 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
 
     cudaError_t st = cudaMemsetAsync(l.error, 0, sizeof(uint32_t), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(output_weight, 0, point_count * sizeof(float), stream);
-    if (st == cudaSuccess) st = cudaMemsetAsync(l.totals, 0, 4 * sizeof(uint32_t), stream);
+    if (st == cudaSuccess) st = cudaMemsetAsync(l.totals, 0, 8 * sizeof(uint32_t), stream);
     if (st == cudaSuccess) st = cudaMemsetAsync(l.ranges, 0, tiles * sizeof(uint2), stream);
     if (st != cudaSuccess) return {st, nullptr, 0, 0};
     const int blocks = (point_count + kPreThreads - 1) / kPreThreads;
@@ -188,7 +188,7 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
         uint32_t* first_pair = l.alt_keys;
         bin::offsets_kernel<<<bin::scan_tiles(point_count), bin::kScanThreads, 0, stream>>>(
-            static_cast<uint32_t>(point_count), l.order, l.counts,
+            static_cast<uint32_t>(point_count), nullptr, l.order, l.counts,
             static_cast<uint32_t*>(l.geometry_scratch), l.error, first_pair);
         st = cudaGetLastError();
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
