@@ -1199,22 +1199,30 @@ int32_t hs_b200_pixel_rays_f32_v1(HsRasterizerHandle handle, int32_t width, int3
         }
         // depth_to_normal (math.py:360-401): pixels (x, y, 1), then
         // camera rays = pixels @ K^-T and world rays = camera rays @ R^T, each
-        // the cuBLAS call of precise_matmul_nt_n3k3 (TF32 tensor-op math).
-        cudaError_t ce = hs::post::pixel_grid(width, height, rays_n3, nullptr);
-        if (ce != cudaSuccess) return cuda_failure(ce, "pixel_rays grid", error_text, error_capacity);
-        const float alpha = 1.0f, beta = 0.0f;
-        cublasStatus_t bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3,
-                                        static_cast<int>(count), 3, &alpha, inverse_intrinsics3x3, 3,
-                                        rays_n3, 3, &beta, scratch_n3, 3);
-        if (bs == CUBLAS_STATUS_SUCCESS) {
-            bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3,
-                             static_cast<int>(count), 3, &alpha, rotation3x3, 3, scratch_n3, 3,
-                             &beta, rays_n3, 3);
+        // the TF32 GEMM of precise_matmul_nt_n3k3: one tensor-core kernel
+        // (postprocess.cu), or for images of fewer than kMmaMinRows pixels the
+        // cuBLAS calls themselves through the scratch buffer.
+        if (count >= hs::post::kMmaMinRows) {
+            const cudaError_t ce = hs::post::pixel_rays(width, height, inverse_intrinsics3x3,
+                                                        rotation3x3, rays_n3, nullptr);
+            if (ce != cudaSuccess) return cuda_failure(ce, "pixel_rays execution", error_text, error_capacity);
+        } else {
+            cudaError_t ce = hs::post::pixel_grid(width, height, rays_n3, nullptr);
+            if (ce != cudaSuccess) return cuda_failure(ce, "pixel_rays grid", error_text, error_capacity);
+            const float alpha = 1.0f, beta = 0.0f;
+            cublasStatus_t bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3,
+                                            static_cast<int>(count), 3, &alpha, inverse_intrinsics3x3, 3,
+                                            rays_n3, 3, &beta, scratch_n3, 3);
+            if (bs == CUBLAS_STATUS_SUCCESS) {
+                bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3,
+                                 static_cast<int>(count), 3, &alpha, rotation3x3, 3, scratch_n3, 3,
+                                 &beta, rays_n3, 3);
+            }
+            if (bs != CUBLAS_STATUS_SUCCESS)
+                return cublas_failure(bs, "pixel_rays cublasSgemm", error_text, error_capacity);
+            ce = cudaGetLastError();
+            if (ce != cudaSuccess) return cuda_failure(ce, "pixel_rays execution", error_text, error_capacity);
         }
-        if (bs != CUBLAS_STATUS_SUCCESS)
-            return cublas_failure(bs, "pixel_rays cublasSgemm", error_text, error_capacity);
-        ce = cudaGetLastError();
-        if (ce != cudaSuccess) return cuda_failure(ce, "pixel_rays execution", error_text, error_capacity);
         handle->math_matmul_calls += 2;
         return ok(error_text, error_capacity);
     });
@@ -1430,15 +1438,24 @@ int32_t hs_rasterizer_precise_matmul_nt_n3k3_f32_v2(HsRasterizerHandle handle,
             return fail(HS_STATUS_INTERNAL_ERROR, "precise_matmul_nt_n3k3 math context is not initialized",
                         error_text, error_capacity);
         }
-        const float alpha = 1.0f, beta = 0.0f;
-        const cublasStatus_t bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3,
-                                              static_cast<int>(count), 3, &alpha, right3x3, 3,
-                                              left_n3, 3, &beta, output_n3, 3);
-        if (bs != CUBLAS_STATUS_SUCCESS)
-            return cublas_failure(bs, "precise_matmul_nt_n3k3 cublasSgemm", error_text, error_capacity);
-        const cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess)
-            return cuda_failure(e, "precise_matmul_nt_n3k3 execution", error_text, error_capacity);
+        // cublasSgemm(OP_T, OP_N, 3, count, 3) under TF32 tensor-op math in the
+        // reference; the same MMA products here (postprocess.cu), and that
+        // call itself below kMmaMinRows rows, where cuBLAS takes another path.
+        if (count >= hs::post::kMmaMinRows) {
+            const cudaError_t e = hs::post::matmul_nt_n3k3(left_n3, right3x3, count, output_n3, nullptr);
+            if (e != cudaSuccess)
+                return cuda_failure(e, "precise_matmul_nt_n3k3 execution", error_text, error_capacity);
+        } else {
+            const float alpha = 1.0f, beta = 0.0f;
+            const cublasStatus_t bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3,
+                                                  static_cast<int>(count), 3, &alpha, right3x3, 3,
+                                                  left_n3, 3, &beta, output_n3, 3);
+            if (bs != CUBLAS_STATUS_SUCCESS)
+                return cublas_failure(bs, "precise_matmul_nt_n3k3 cublasSgemm", error_text, error_capacity);
+            const cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess)
+                return cuda_failure(e, "precise_matmul_nt_n3k3 execution", error_text, error_capacity);
+        }
         ++handle->math_matmul_calls;
         return ok(error_text, error_capacity);
     });

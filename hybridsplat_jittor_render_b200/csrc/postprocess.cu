@@ -171,6 +171,117 @@ __global__ void __launch_bounds__(kThreads) flashgs_kernel(
     }
 }
 
+// ---- N x 3 by 3 x 3 products on the tensor cores (TF32) ----
+//
+// The reference forms these products with cublasSgemm(OP_T, OP_N, m = 3,
+// n = N, k = 3) under CUBLAS_TF32_TENSOR_OP_MATH (precise_matmul_nt_n3k3,
+// c_api.cpp:1673); on B200 that runs a CUTLASS-style TF32 tensor-op GEMM
+// with m16n8k8 MMAs. Its results are reproduced bit for bit by: operands
+// rounded from FP32 to TF32 to nearest, ties to even (CUTLASS's
+// round_to_nearest conversion for these targets; measured against the
+// reference library's cuBLAS results, where rounding half away from zero
+// and truncation both disagree), one m16n8k8 MMA per output block with the
+// three products in k slots 0..2 and zeros after them, FP32 accumulation
+// from zero, alpha = 1 and beta = 0. The warp below issues that instruction
+// with the GEMM's operand placement: A = the 3 x 3 matrix (rows = output
+// components, the GEMM's m), B = eight rows of the N x 3 operand (the
+// GEMM's n). For fewer than kMmaMinRows rows cuBLAS takes another path, and
+// the callers keep cuBLAS there.
+
+// FP32 -> TF32 (10-bit mantissa), round to nearest even; infinities and NaNs
+// pass unchanged (the MMA reads only the top 19 bits).
+__device__ __forceinline__ uint32_t tf32_rne(float x) {
+    const uint32_t b = __float_as_uint(x);
+    if ((b & 0x7f800000u) == 0x7f800000u) return b;
+    return (b + 0xfffu + ((b >> 13) & 1u)) & 0xffffe000u;
+}
+
+// D = A(16x8, rows g / g+8, cols t / t+4) * B(8x8, rows t / t+4, col g), C = 0.
+__device__ __forceinline__ void mma_tf32_k8(float d[4], uint32_t a0, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%10, %10, %10, %10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(0u), "r"(0u), "r"(0u), "r"(b0), "r"(0u), "f"(0.0f));
+}
+
+// Lane (g = lane / 4, t = lane % 4) holds A[g][t] of the 3 x 3 matrix.
+__device__ __forceinline__ uint32_t matrix_fragment(const float* m3x3, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    return (g < 3 && t < 3) ? tf32_rne(m3x3[3 * g + t]) : 0u;
+}
+
+// After mma_tf32_k8, lane (g, t) holds out[row 2t][g] in d[0] and
+// out[row 2t + 1][g] in d[1] for g < 3. Returns component t of row g (the B
+// fragment of a following product; t == 3 gives 0).
+__device__ __forceinline__ float transpose_fragment(const float d[4], int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const int src = (t < 3 ? t : 0) * 4 + (g >> 1);
+    const float v0 = __shfl_sync(0xffffffffu, d[0], src);
+    const float v1 = __shfl_sync(0xffffffffu, d[1], src);
+    return t < 3 ? ((g & 1) ? v1 : v0) : 0.0f;
+}
+
+__device__ __forceinline__ void store_fragment(const float d[4], uint64_t row0, uint64_t rows,
+                                               float* __restrict__ out3, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    if (g >= 3) return;
+    const uint64_t r0 = row0 + 2u * t, r1 = r0 + 1u;
+    if (r0 < rows) out3[3 * r0 + g] = d[0];
+    if (r1 < rows) out3[3 * r1 + g] = d[1];
+}
+
+constexpr int kMmaRowsPerWarp = 32;  // four groups of eight rows per loop trip
+
+// out[i] = left[i] @ right^T for N rows, or, when kPixels, the world rays of
+// the pixel grid: ((x, y, 1) @ first^T) @ second^T, both products rounded as
+// above and the intermediate kept in FP32 between them (the reference's two
+// GEMMs through a scratch buffer).
+template <bool kPixels>
+__global__ void __launch_bounds__(kThreads) tf32_rows3_kernel(
+    uint64_t rows, int width, const float* __restrict__ left3, const float* __restrict__ first,
+    const float* __restrict__ second, float* __restrict__ out3) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const uint32_t a_first = matrix_fragment(first, lane);
+    const uint32_t a_second = kPixels ? matrix_fragment(second, lane) : 0u;
+    const uint64_t warps = static_cast<uint64_t>(gridDim.x) * (kThreads / 32);
+    for (uint64_t base = (static_cast<uint64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5)) *
+                         kMmaRowsPerWarp;
+         base < rows; base += warps * kMmaRowsPerWarp) {
+#pragma unroll
+        for (int group = 0; group < kMmaRowsPerWarp / 8; ++group) {
+            const uint64_t row0 = base + 8u * group;
+            const uint64_t row = row0 + g;  // this lane's B row
+            uint32_t b0 = 0u;
+            if (row < rows && t < 3) {
+                float v;
+                if (kPixels) {
+                    v = t == 0 ? static_cast<float>(row % static_cast<uint64_t>(width))
+                               : (t == 1 ? static_cast<float>(row / static_cast<uint64_t>(width))
+                                         : 1.0f);
+                } else {
+                    v = left3[3 * row + t];
+                }
+                b0 = tf32_rne(v);
+            }
+            float d[4];
+            mma_tf32_k8(d, a_first, b0);
+            if (kPixels) {
+                const float cam = transpose_fragment(d, lane);
+                const uint32_t b1 = (row < rows && t < 3) ? tf32_rne(cam) : 0u;
+                mma_tf32_k8(d, a_second, b1);
+            }
+            store_fragment(d, row0, rows, out3, lane);
+        }
+    }
+}
+
+unsigned mma_grid_for(uint64_t rows) {
+    const uint64_t warps = (rows + kMmaRowsPerWarp - 1) / kMmaRowsPerWarp;
+    const uint64_t blocks = (warps + kThreads / 32 - 1) / (kThreads / 32);
+    return static_cast<unsigned>(blocks < 148u * 8u ? (blocks > 0 ? blocks : 1) : 148u * 8u);
+}
+
 unsigned grid_for(uint64_t items) {
     const uint64_t blocks = (items + kThreads - 1) / kThreads;
     return static_cast<unsigned>(blocks < 148u * 16u ? (blocks > 0 ? blocks : 1) : 148u * 16u);
@@ -182,6 +293,23 @@ cudaError_t pixel_grid(int width, int height, float* out3, cudaStream_t s) {
     const uint64_t pixels = static_cast<uint64_t>(width) * height;
     if (pixels == 0) return cudaSuccess;
     pixel_grid_kernel<<<grid_for(pixels), kThreads, 0, s>>>(width, height, out3);
+    return cudaGetLastError();
+}
+
+cudaError_t pixel_rays(int width, int height, const float* inverse_intrinsics3x3,
+                       const float* rotation3x3, float* rays3, cudaStream_t s) {
+    const uint64_t pixels = static_cast<uint64_t>(width) * height;
+    if (pixels == 0) return cudaSuccess;
+    tf32_rows3_kernel<true><<<mma_grid_for(pixels), kThreads, 0, s>>>(
+        pixels, width, nullptr, inverse_intrinsics3x3, rotation3x3, rays3);
+    return cudaGetLastError();
+}
+
+cudaError_t matmul_nt_n3k3(const float* left_n3, const float* right3x3, uint64_t rows,
+                           float* out_n3, cudaStream_t s) {
+    if (rows == 0) return cudaSuccess;
+    tf32_rows3_kernel<false><<<mma_grid_for(rows), kThreads, 0, s>>>(rows, 1, left_n3, right3x3,
+                                                                     nullptr, out_n3);
     return cudaGetLastError();
 }
 

@@ -36,6 +36,20 @@ struct FlashgsMaps {
 // pixels[H*W,3] = (x, y, 1), the input of depth_to_normal's first GEMM.
 cudaError_t pixel_grid(int width, int height, float* out3, cudaStream_t s);
 
+// Row counts from which the reference's TF32 cuBLAS GEMM takes its tensor-op
+// path, which pixel_rays and matmul_nt_n3k3 reproduce (below it, callers use
+// cuBLAS itself).
+constexpr uint64_t kMmaMinRows = 8;
+
+// rays[H*W,3] = ((x, y, 1) @ K^-T) @ R^T for every pixel, each product the
+// TF32 tensor-op GEMM of the reference (one MMA kernel, no scratch).
+cudaError_t pixel_rays(int width, int height, const float* inverse_intrinsics3x3,
+                       const float* rotation3x3, float* rays3, cudaStream_t s);
+
+// out[N,3] = left[N,3] @ right[3,3]^T, the reference's TF32 tensor-op GEMM.
+cudaError_t matmul_nt_n3k3(const float* left_n3, const float* right3x3, uint64_t rows,
+                           float* out_n3, cudaStream_t s);
+
 // keep = float(1 - ratio) and ratio as the caller rounded them.
 cudaError_t standard(int width, int height, const float* color5, const float* aux7,
                      const float* rays3, const float* origin3, const float* rotation9, float keep,

@@ -291,9 +291,9 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
     // 4. permute the tile into digit order in place (keys, then values), then
     //    write digit runs
     uint32_t item[kItems];
+    bool keep[kItems];
     __syncthreads();  // digit_start / global_base
 #pragma unroll
-    bool keep[kItems];
     for (int k = 0; k < kItems; ++k) {
         const uint32_t i = seg + static_cast<uint32_t>(k) * 32u + lane;
         item[k] = tile_keys[i];

@@ -705,8 +705,9 @@ def precise_general_inverse(matrix: torch.Tensor, *, context: NativeRendererCont
 
 def precise_matmul_nt_n3k3(left: torch.Tensor, right: torch.Tensor, *,
                            context: NativeRendererContext) -> torch.Tensor:
-    """left[N,3] @ right[3,3]^T through the reference's TF32 cuBLAS call
-    (hs_rasterizer_precise_matmul_nt_n3k3_f32_v2)."""
+    """left[N,3] @ right[3,3]^T rounded as the reference's TF32 tensor-op
+    cuBLAS GEMM rounds it (hs_rasterizer_precise_matmul_nt_n3k3_f32_v2; an
+    MMA kernel in this library)."""
     count = int(left.shape[0])
     _check_tensor("left", left, (count, 3))
     _check_tensor("right", right, (3, 3))
@@ -750,7 +751,9 @@ def pixel_rays(width: int, height: int, inverse_intrinsics: torch.Tensor, rotati
                context: NativeRendererContext, out: torch.Tensor | None = None,
                scratch: torch.Tensor | None = None) -> torch.Tensor:
     """World-space rays [H*W,3] of every pixel, ((x, y, 1) @ K^-T) @ R^T with
-    the reference's TF32 GEMM for each product (hs_b200_pixel_rays_f32_v1)."""
+    the reference's TF32 GEMM rounding for each product, in one tensor-core
+    kernel (hs_b200_pixel_rays_f32_v1; `scratch` is accepted for the ABI and
+    not written)."""
     _check_tensor("inverse_intrinsics", inverse_intrinsics, (3, 3))
     _check_tensor("rotation", rotation, (3, 3))
     f = dict(dtype=torch.float32, device=rotation.device)

@@ -238,13 +238,15 @@ HS_API int32_t hs_b200_standard_debug_copy_v1(
 /* World-space pixel rays of one view, the first half of the standard
  * session's depth_to_normal (math.py:351-401): rays_n3[H*W,3] =
  * ((x, y, 1) @ inverse_intrinsics3x3^T) @ rotation3x3^T for every pixel in
- * row-major order, each product the cuBLAS call of
- * hs_rasterizer_precise_matmul_nt_n3k3_f32_v2 (TF32 tensor-op math on the
- * handle's math context), so the rays equal the reference session's.
+ * row-major order, each product rounded as the TF32 tensor-op GEMM of
+ * hs_rasterizer_precise_matmul_nt_n3k3_f32_v2 rounds it, so the rays equal the
+ * reference session's; both products run in one tensor-core kernel.
  * inverse_intrinsics3x3 is the inverse intrinsic matrix and rotation3x3 the
  * camera-to-world rotation c2w[:3,:3], both row-major device matrices (the
- * outputs of hs_rasterizer_precise_general_inverse_f32_v2). scratch_n3 is a
- * device buffer of H*W*3 floats distinct from rays_n3. Legacy default stream. */
+ * outputs of hs_rasterizer_precise_general_inverse_f32_v2). scratch_n3 (H*W*3
+ * floats, distinct from rays_n3) is written only for images of fewer than 8
+ * pixels, which take the two cuBLAS calls themselves (cuBLAS rounds those
+ * differently). Legacy default stream. */
 HS_API int32_t hs_b200_pixel_rays_f32_v1(
     HsRasterizerHandle handle, int32_t width, int32_t height, const float* inverse_intrinsics3x3,
     const float* rotation3x3, float* scratch_n3, float* rays_n3, char* error_text,

@@ -55,10 +55,15 @@ def bits_equal_any_nan(a: np.ndarray, b: np.ndarray) -> bool:
     return bits_equal(np.where(np.isnan(a), np.float32(0), a), np.where(np.isnan(b), np.float32(0), b))
 
 
-@pytest.mark.parametrize("camera", ["generic", "orbit"])
+@pytest.mark.parametrize("camera", ["generic", "orbit", "stress_4k"])
 def test_camera_matrices_and_rays_match_reference_helpers(contexts, camera):
+    """The rays of this library's one-kernel MMA path against the reference's
+    two cuBLAS TF32 GEMMs; at 3840 x 2160 pixel columns above 2048 are not
+    TF32 values, so the operand rounding is exercised too."""
     mine, ref = contexts
-    cam = scenes.generic_camera("standard_1m", 3) if camera == "generic" else scenes.orbit_camera("standard_1m", 4)
+    cam = {"generic": lambda: scenes.generic_camera("standard_1m", 3),
+           "orbit": lambda: scenes.orbit_camera("standard_1m", 4),
+           "stress_4k": lambda: scenes.generic_camera("stress_4k", 1)}[camera]()
     w, h, fov_x, fov_y, wv = camera_inputs(cam)
     ours = ops.postprocess_camera(w, h, fov_x, fov_y, wv, context=mine)
     theirs = ops.postprocess_camera(w, h, fov_x, fov_y, wv, context=ref)
@@ -72,6 +77,41 @@ def test_camera_matrices_and_rays_match_reference_helpers(contexts, camera):
     reference_rays = ops.precise_matmul_nt_n3k3(camera_rays, theirs["rotation"], context=ref)
     torch.cuda.synchronize()
     assert bits_equal(host(rays), host(reference_rays))
+
+
+def tf32_halfway_values(rng, count):
+    """Values whose low 13 mantissa bits are exactly half a TF32 ulp, with
+    even and odd TF32 mantissas and both signs: rounding half away from zero
+    and half to even disagree on half of them."""
+    bits = rng.integers(0x30000000, 0x50000000, count, dtype=np.uint32)
+    bits = (bits & np.uint32(0xffffe000)) | np.uint32(0x1000)
+    bits |= rng.integers(0, 2, count, dtype=np.uint32) << np.uint32(31)
+    return bits.view(np.float32)
+
+
+@pytest.mark.parametrize("rows", [1, 5, 7, 8, 4096, 1_000_003])
+def test_tf32_matmul_matches_reference_cublas(contexts, rows):
+    """precise_matmul_nt_n3k3 (MMA kernel here from 8 rows, cublasSgemm with
+    TF32 tensor-op math in the reference) bit for bit on rows of mixed
+    magnitudes, TF32 halfway values (rounding half away from zero would
+    disagree on them), zeros and a ragged tail."""
+    mine, ref = contexts
+    rng = np.random.default_rng(rows)
+    left = (rng.standard_normal((rows, 3)) * np.exp2(rng.integers(-24, 24, (rows, 3)))).astype(np.float32)
+    flat = left.reshape(-1)
+    k = min(flat.size, 30_000)
+    flat[:k] = tf32_halfway_values(rng, k)
+    if rows > 4:
+        left[3] = 0.0
+        left[4] = [-0.0, 1.0, -1.0]
+    for right in (rng.standard_normal((3, 3)).astype(np.float32),
+                  tf32_halfway_values(rng, 9).reshape(3, 3)):
+        a = ops.precise_matmul_nt_n3k3(torch.from_numpy(left).cuda(), torch.from_numpy(right).cuda(),
+                                       context=mine)
+        b = ops.precise_matmul_nt_n3k3(torch.from_numpy(left).cuda(), torch.from_numpy(right).cuda(),
+                                       context=ref)
+        torch.cuda.synchronize()
+        assert bits_equal(host(a), host(b))
 
 
 def standard_view(ctx, group, cam):
