@@ -15,14 +15,20 @@
 //   leaves     the triangles' vertices in sorted order (48 bytes each);
 //   refit      one thread per leaf walks up; the second thread to reach a
 //              node writes both children's boxes into it (64 bytes per node)
-//              and continues.
+//              and continues;
+//   widen      each binary node's grandchildren (a leaf child stands for
+//              itself) become the four children of a wide node (128 bytes:
+//              one float4 per box coordinate of the four children, then their
+//              references), so a traversal from the root fetches every second
+//              binary level only, four boxes per fetch.
 // Trace (hs_optix_trace_f32_v1; reference optix_backend.cpp:460-617 and the
 // programs of vendor/optix_tracer/forward.cu:219-660): one thread per ray;
-// each trace step is a stack traversal of the BVH that keeps the 16 nearest
-// hits in a sorted per-thread buffer (shared memory), pruning boxes beyond
-// the 16th; the hits are then shaded front to back exactly as the reference
-// raygen program does, and the step restarts behind the last processed hit
-// while 16 or more hits were found.
+// each trace step is a stack traversal of the wide BVH (children pushed
+// farthest first) that keeps the 16 nearest hits in a sorted per-thread
+// buffer (shared memory), pruning boxes beyond the 16th; the hits are then
+// shaded front to back exactly as the reference raygen program does, and the
+// step restarts behind the last processed hit while 16 or more hits were
+// found. Which hits a step keeps does not depend on the traversal order.
 #include <math_constants.h>
 
 #include <algorithm>
@@ -261,9 +267,59 @@ __global__ void __launch_bounds__(kBuildThreads) refit_kernel(
 __global__ void single_root_kernel(const float4* __restrict__ lo, const float4* __restrict__ hi,
                                    float4* __restrict__ nodes) {
     nodes[0] = make_float4(lo[0].x, lo[0].y, lo[0].z, __uint_as_float(kLeafBit));
-    nodes[1] = make_float4(hi[0].x, hi[0].y, hi[0].z, __uint_as_float(kLeafBit));
+    nodes[1] = make_float4(hi[0].x, hi[0].y, hi[0].z, __uint_as_float(kNoChild));
     nodes[2] = make_float4(CUDART_INF_F, CUDART_INF_F, CUDART_INF_F, 0.0f);
-    nodes[3] = make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, 0.0f);
+    nodes[3] = make_float4(CUDART_INF_F, CUDART_INF_F, CUDART_INF_F, 0.0f);
+}
+
+// The wide tree: wide node i holds the grandchildren of binary node i (a
+// child that is a leaf, or empty, stands for itself), so that from the root
+// every second binary level is skipped. One thread per binary node; nodes
+// that the traversal never reaches (odd binary depths) are written too.
+// Empty slots get the box [+inf, +inf], which the slab test rejects, and
+// the reference kNoChild.
+__global__ void __launch_bounds__(kBuildThreads) widen_kernel(uint32_t internal,
+                                                              const float4* __restrict__ binary,
+                                                              float4* __restrict__ wide) {
+    const uint32_t i = blockIdx.x * kBuildThreads + threadIdx.x;
+    if (i >= internal) return;
+    float lx[4], ly[4], lz[4], hx[4], hy[4], hz[4];
+    uint32_t ref[4];
+    int k = 0;
+    const float4* node = binary + 4 * static_cast<uint64_t>(i);
+    const float4 q[4] = {node[0], node[1], node[2], node[3]};
+    for (int c = 0; c < 2; ++c) {
+        const float4 lo = q[2 * c], hi = q[2 * c + 1];
+        const uint32_t r = __float_as_uint(c == 0 ? q[0].w : q[1].w);
+        if (r == kNoChild || (r & kLeafBit) != 0u) {
+            lx[k] = lo.x; ly[k] = lo.y; lz[k] = lo.z;
+            hx[k] = hi.x; hy[k] = hi.y; hz[k] = hi.z;
+            ref[k++] = r;
+            continue;
+        }
+        const float4* child = binary + 4 * static_cast<uint64_t>(r);
+        const float4 g[4] = {child[0], child[1], child[2], child[3]};
+        for (int gc = 0; gc < 2; ++gc) {
+            const float4 glo = g[2 * gc], ghi = g[2 * gc + 1];
+            lx[k] = glo.x; ly[k] = glo.y; lz[k] = glo.z;
+            hx[k] = ghi.x; hy[k] = ghi.y; hz[k] = ghi.z;
+            ref[k++] = __float_as_uint(gc == 0 ? g[0].w : g[1].w);
+        }
+    }
+    for (; k < 4; ++k) {
+        lx[k] = ly[k] = lz[k] = hx[k] = hy[k] = hz[k] = CUDART_INF_F;
+        ref[k] = kNoChild;
+    }
+    float4* out = wide + kWideQuads * static_cast<uint64_t>(i);
+    out[0] = make_float4(lx[0], lx[1], lx[2], lx[3]);
+    out[1] = make_float4(hx[0], hx[1], hx[2], hx[3]);
+    out[2] = make_float4(ly[0], ly[1], ly[2], ly[3]);
+    out[3] = make_float4(hy[0], hy[1], hy[2], hy[3]);
+    out[4] = make_float4(lz[0], lz[1], lz[2], lz[3]);
+    out[5] = make_float4(hz[0], hz[1], hz[2], hz[3]);
+    out[6] = make_float4(__uint_as_float(ref[0]), __uint_as_float(ref[1]), __uint_as_float(ref[2]),
+                         __uint_as_float(ref[3]));
+    out[7] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 }
 
 // ------------------------------------------------------------------- trace
@@ -406,24 +462,40 @@ __device__ uint32_t collect(const Bvh& bvh, const float3& o, const float3& inv, 
             }
             continue;
         }
-        const float4* node = bvh.nodes + 4 * static_cast<uint64_t>(ref);
-        const float4 l0 = __ldg(node), h0 = __ldg(node + 1), l1 = __ldg(node + 2), h1 = __ldg(node + 3);
+        const float4* node = bvh.nodes + kWideQuads * static_cast<uint64_t>(ref);
+        const float4 minx = __ldg(node), maxx = __ldg(node + 1), miny = __ldg(node + 2),
+                     maxy = __ldg(node + 3), minz = __ldg(node + 4), maxz = __ldg(node + 5);
+        const uint4 refs = __ldg(reinterpret_cast<const uint4*>(node + 6));
         const float box_limit = limit * 1.000244140625f;
-        float e0, e1;
-        const bool b0 = hit_box(o, inv, l0, h0, box_limit, e0);
-        const bool b1 = hit_box(o, inv, l1, h1, box_limit, e1);
-        const uint32_t c0 = __float_as_uint(l0.w), c1 = __float_as_uint(h0.w);
-        // Never taken: at most one entry per level above this node (the tree
-        // is at most 64 internal nodes deep) plus these two.
-        if (sp + 2 > kStackDepth) break;
-        if (b0 && b1) {
-            const bool near0 = e0 <= e1;  // nearer child on top
-            stack[sp++] = near0 ? c1 : c0;
-            stack[sp++] = near0 ? c0 : c1;
-        } else if (b0) {
-            stack[sp++] = c0;
-        } else if (b1) {
-            stack[sp++] = c1;
+        // the children whose box the ray enters before box_limit, by entry
+        // distance (a 4-element sorting network; missed ones at +inf)
+        float e[4];
+        uint32_t c[4] = {refs.x, refs.y, refs.z, refs.w};
+        e[0] = hit_box(o, inv, minx.x, miny.x, minz.x, maxx.x, maxy.x, maxz.x, box_limit, e[0]) ? e[0] : CUDART_INF_F;
+        e[1] = hit_box(o, inv, minx.y, miny.y, minz.y, maxx.y, maxy.y, maxz.y, box_limit, e[1]) ? e[1] : CUDART_INF_F;
+        e[2] = hit_box(o, inv, minx.z, miny.z, minz.z, maxx.z, maxy.z, maxz.z, box_limit, e[2]) ? e[2] : CUDART_INF_F;
+        e[3] = hit_box(o, inv, minx.w, miny.w, minz.w, maxx.w, maxy.w, maxz.w, box_limit, e[3]) ? e[3] : CUDART_INF_F;
+        auto order2 = [&](int a, int b) {
+            if (e[b] < e[a]) {
+                const float te = e[a];
+                e[a] = e[b];
+                e[b] = te;
+                const uint32_t tc = c[a];
+                c[a] = c[b];
+                c[b] = tc;
+            }
+        };
+        order2(0, 1);
+        order2(2, 3);
+        order2(0, 2);
+        order2(1, 3);
+        order2(1, 2);
+        // Never taken: at most 3 entries per wide level above this node (32
+        // levels) plus these four.
+        if (sp + 4 > kStackDepth) break;
+        // farthest first, so that the nearest is popped next
+        for (int k = 3; k >= 0; --k) {
+            if (e[k] != CUDART_INF_F && c[k] != kNoChild) stack[sp++] = c[k];
         }
     }
     return found;
@@ -634,6 +706,7 @@ struct BuildLayout {
     uint32_t* parents;
     uint32_t* visits;
     float4* node_boxes;
+    float4* binary;  // binary radix tree: 4 float4 per internal node
     uint32_t* bounds;
     uint32_t* status;
     void* sort_scratch;
@@ -653,6 +726,7 @@ BuildLayout build_layout(void* base, uint64_t n) {
     l.parents = c.take<uint32_t>(2 * n);
     l.visits = c.take<uint32_t>(n);
     l.node_boxes = c.take<float4>(2 * n);
+    l.binary = c.take<float4>(4 * std::max<uint64_t>(n > 0 ? n - 1 : 1, 1));
     l.bounds = c.take<uint32_t>(64);
     l.status = c.take<uint32_t>(64);
     l.sort_scratch = c.take<unsigned char>(sort::sort_scratch_bytes(static_cast<uint32_t>(n)));
@@ -670,7 +744,7 @@ struct SceneLayout {
 SceneLayout scene_layout(void* base, uint64_t n) {
     Carver c(base);
     SceneLayout l;
-    l.nodes = c.take<float4>(4 * std::max<uint64_t>(n > 0 ? n - 1 : 1, 1));
+    l.nodes = c.take<float4>(kWideQuads * std::max<uint64_t>(n > 0 ? n - 1 : 1, 1));
     l.tris = c.take<float4>(3 * n);
     l.bounds = c.take<float>(64);
     l.bytes = c.offset;
@@ -755,10 +829,13 @@ cudaError_t trace_build_scene(HsRasterizerContext* ctx, const float* vertices3, 
         hierarchy_kernel<<<static_cast<unsigned>((n - 1 + kBuildThreads - 1) / kBuildThreads), kBuildThreads, 0,
                            stream>>>(n32, l.keys, l.children, l.parents);
         refit_kernel<<<blocks, kBuildThreads, 0, stream>>>(n32, l.vals, l.lo, l.hi, l.children, l.parents,
-                                                           l.visits, l.node_boxes, sl.nodes);
+                                                           l.visits, l.node_boxes, l.binary);
     } else {
-        single_root_kernel<<<1, 1, 0, stream>>>(l.lo, l.hi, sl.nodes);
+        single_root_kernel<<<1, 1, 0, stream>>>(l.lo, l.hi, l.binary);
     }
+    const uint32_t internal = n >= 2 ? n32 - 1 : 1u;
+    widen_kernel<<<(internal + kBuildThreads - 1) / kBuildThreads, kBuildThreads, 0, stream>>>(internal, l.binary,
+                                                                                              sl.nodes);
     leaves_kernel<<<blocks, kBuildThreads, 0, stream>>>(n32, l.vals, vertices3, vertex_count, triangles3, sl.tris);
     scene_bounds_kernel<<<1, 32, 0, stream>>>(l.bounds, sl.bounds);
     st = cudaGetLastError();

@@ -35,17 +35,25 @@ constexpr float kFilterInvSquare = 2.0f;
 constexpr float kTThreshold = 0.0001f;
 constexpr int kMidChannels = 16;           // MID_CHANNELS per trace depth
 constexpr uint32_t kLeafBit = 0x80000000u; // child reference: leaf slot
-constexpr int kStackDepth = 72;         // traversal stack (tree depth <= 64)
+constexpr uint32_t kNoChild = 0xffffffffu; // empty child slot of a wide node
+// Traversal stack: the binary tree is at most 64 internal nodes deep, so a
+// root-to-leaf path crosses at most 32 wide nodes, each leaving at most 3
+// siblings on the stack, plus the 4 children of the last one.
+constexpr int kStackDepth = 104;
 constexpr int kMaxTraceSteps = 4096;    // trace steps (16 hits each) per segment
 
-// BVH over the scene triangles (binary, children's boxes stored in the
-// parent): node k = 4 float4 {c0 min | c0 ref, c0 max | c1 ref, c1 min,
-// c1 max}; a child reference with kLeafBit names a leaf slot, whose triangle
-// is 3 float4 {v0 | primitive index, v1, v2} in `tris`.
+// BVH over the scene triangles, 4 children per node (the binary radix tree
+// with every second level collapsed; children's boxes stored in the parent,
+// one coordinate of the four children per float4): node k = 8 float4
+// {min x, max x, min y, max y, min z, max z, child references, unused}; a
+// child reference with kLeafBit names a leaf slot, whose triangle is
+// 3 float4 {v0 | primitive index, v1, v2} in `tris`; kNoChild an empty slot
+// (its box is empty).
+constexpr int kWideQuads = 8;
 struct Bvh {
     const float4* nodes;
     const float4* tris;
-    uint32_t root;  // child reference of the root
+    uint32_t root;  // reference of the root node
 };
 
 __device__ __forceinline__ float3 f3(float x, float y, float z) { return make_float3(x, y, z); }
@@ -111,11 +119,11 @@ __device__ __forceinline__ float hit_triangle(const float3& o, const RayShear& r
 }
 
 // Slab test of the box [lo, hi] against [0, limit]; inv = 1 / d per axis.
-__device__ __forceinline__ bool hit_box(const float3& o, const float3& inv, const float4& lo,
-                                        const float4& hi, float limit, float& entry) {
-    const float tx0 = mul(sub(lo.x, o.x), inv.x), tx1 = mul(sub(hi.x, o.x), inv.x);
-    const float ty0 = mul(sub(lo.y, o.y), inv.y), ty1 = mul(sub(hi.y, o.y), inv.y);
-    const float tz0 = mul(sub(lo.z, o.z), inv.z), tz1 = mul(sub(hi.z, o.z), inv.z);
+__device__ __forceinline__ bool hit_box(const float3& o, const float3& inv, float lx, float ly, float lz,
+                                        float hx, float hy, float hz, float limit, float& entry) {
+    const float tx0 = mul(sub(lx, o.x), inv.x), tx1 = mul(sub(hx, o.x), inv.x);
+    const float ty0 = mul(sub(ly, o.y), inv.y), ty1 = mul(sub(hy, o.y), inv.y);
+    const float tz0 = mul(sub(lz, o.z), inv.z), tz1 = mul(sub(hz, o.z), inv.z);
     const float tn = fmaxf(fmaxf(fminf(tx0, tx1), fminf(ty0, ty1)), fmaxf(fminf(tz0, tz1), 0.0f));
     const float tf = fminf(fminf(fmaxf(tx0, tx1), fmaxf(ty0, ty1)), fminf(fmaxf(tz0, tz1), limit));
     entry = tn;
