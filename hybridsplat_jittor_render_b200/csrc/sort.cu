@@ -1,25 +1,36 @@
-// Onesweep stable LSD radix sort (sort.cuh).
+// Stable LSD radix sort (sort.cuh), 8-bit digits, in one of two pass forms.
 //
-// Scratch layout of sort_pairs (zeroed by one memset per sort):
-//   hist[kMaxPasses][kBins]        digit counts of every pass
-//   tile_counter[kMaxPasses]       dynamic tile numbering per pass
+// Onesweep (below 2M items). Scratch (zeroed by one memset per sort):
+//   hist[kMaxPasses][kBins]          digit counts of every pass
+//   tile_counter[kMaxPasses]         dynamic tile numbering per pass
 //   status[kMaxPasses][tiles][kBins] look-back words
-// Each pass kernel block:
-//   1. takes the next tile number (so every earlier tile's block has
-//      already started and will publish without waiting on this one) and
-//      copies the tile's keys and values into shared memory with two bulk
-//      asynchronous copies (the TMA engine; a ragged tail of < 4 items with
-//      plain loads), so no thread holds the items in registers while ranking;
-//   2. ranks its 2048 items stably: warp w owns the contiguous segment
-//      [256w, 256w + 256) and walks it 32 items at a time with
-//      __match_any_sync on the digit; per-warp digit counts are prefixed
-//      across warps;
-//   3. publishes its per-digit counts, looks back for the counts of all
-//      earlier tiles, publishes the inclusive sums;
-//   4. permutes the tile in shared memory into digit order and writes each
+// One histogram kernel reads the keys once for all passes; then each pass is
+// one kernel whose blocks
+//   1. take the next tile number (so every earlier tile's block has already
+//      started and will publish without waiting on this one) and copy the
+//      tile's keys and values into shared memory with two bulk asynchronous
+//      copies (the TMA engine; a ragged tail of < 4 items with plain loads),
+//      so no thread holds the items in registers while ranking;
+//   2. rank the tile stably: warp w owns a contiguous segment and walks it 32
+//      items at a time, grouping equal digits with __match_any_sync (or one
+//      ballot per digit bit); per-warp digit counts are prefixed across warps;
+//   3. publish their per-digit counts, look back for the counts of all earlier
+//      tiles and publish the inclusive sums;
+//   4. permute the tile in shared memory into digit order and write each
 //      digit run to consecutive global positions (coalesced).
-// Keeping the tile in shared memory instead of registers lets six blocks
+// Keeping the tile in shared memory instead of registers lets several blocks
 // share an SM, which hides the latency of the look-back.
+//
+// Reduce-then-scan (from 2M items). Scratch: counts[kBins][tiles], totals.
+// Each pass is a count kernel (per 4096-item tile, the digit counts), a scan
+// kernel (per digit, the exclusive prefix across tiles and the total) and a
+// scatter kernel whose blocks do steps 1, 2 and 4 with the destination of each
+// digit run read from the scan: no block waits on another. When all resident
+// blocks start together, a onesweep tile walks back over many predecessors
+// that have only published their aggregate; at these sizes that walk cost more
+// than the two extra launches.
+#include <utility>
+
 #include "sort.cuh"
 
 namespace hs {
@@ -40,6 +51,11 @@ constexpr int kLargeItems = 16;
 constexpr int kLargeWindow = 16;
 constexpr uint32_t kLargeTileItems = 1u << 18;
 constexpr uint32_t kBallotItems = 1u << 23;
+// From 2M items a pass is three kernels (count, scan across tiles, scatter)
+// instead of one with a decoupled look-back: measured on a B200, 3.66M 13-bit
+// keys 124 -> 109 us and 30M 15-bit keys 620 -> 487 us, while below about 1M
+// items the extra launches cost more than the look-back.
+constexpr uint32_t kSplitItems = 1u << 21;
 
 struct SortScratch {
     uint32_t* hist;       // [kMaxPasses][kBins]
@@ -152,86 +168,96 @@ __device__ __forceinline__ uint32_t block_exclusive_256(uint32_t v, uint32_t* wa
     return base + incl - v;
 }
 
-template <int kItems, int kWindow, bool kBallot>
-__global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel(
-    const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
-    uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, uint32_t count,
-    const uint32_t* __restrict__ live_count, int drop, int shift, int bits,
-    const uint32_t* __restrict__ hist, uint32_t* __restrict__ counter,
-    uint32_t* __restrict__ status, uint32_t* __restrict__ error, uint32_t stall_tile) {
-    constexpr uint32_t kTileItems = kThreads * kItems;
-    constexpr uint32_t kWarpItems = kTileItems / kWarps;  // contiguous items per warp
-    // The tile, in input order until step 4 permutes it into digit order.
-    __shared__ alignas(16) uint32_t tile_keys[kTileItems];
-    __shared__ alignas(16) uint32_t tile_vals[kTileItems];
-    __shared__ uint32_t warp_count[kWarps][kBins];
-    __shared__ uint32_t digit_start[kBins];   // first local position of each digit
-    __shared__ uint32_t global_base[kBins];   // destination of the digit run's first item
-    __shared__ uint32_t warp_sums[kWarps];
-    __shared__ uint32_t tile_slot;
-    __shared__ uint32_t tile_kept;            // items of the tile that are written
-    __shared__ alignas(8) uint64_t loaded;    // completes when the bulk copies land
+// ---- the tile of one pass block, shared by both pass forms ----
 
-    // An earlier pass gave up a wait: its output is not a permutation of the
-    // input, so this pass's histogram no longer matches it. Every block leaves.
-    if (wait_failed(error)) return;
+template <int kItems>
+struct PassTile {
+    static constexpr uint32_t kTileItems = kThreads * kItems;
+    // The tile, in input order until it is permuted into digit order.
+    alignas(16) uint32_t keys[kTileItems];
+    alignas(16) uint32_t vals[kTileItems];
+    uint32_t warp_count[kWarps][kBins];
+    uint32_t digit_start[kBins];   // first local position of each digit
+    uint32_t global_base[kBins];   // destination of the digit run's first item
+    uint32_t warp_sums[kWarps];
+    uint32_t slot;
+    uint32_t kept;                 // items of the tile that are written
+    alignas(8) uint64_t loaded;    // completes when the bulk copies land
+};
+
+// Barrier set-up and per-warp digit counts cleared; ends with a block barrier.
+template <int kItems>
+__device__ __forceinline__ void tile_begin(PassTile<kItems>& t) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t mask = (1u << bits) - 1u;
     if (threadIdx.x == 0) {
-        tile_slot = atomicAdd(counter, 1u);
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(shared_address(&loaded))
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(shared_address(&t.loaded))
                      : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    for (int b = lane; b < kBins; b += 32) warp_count[warp][b] = 0;
+    for (int b = lane; b < kBins; b += 32) t.warp_count[warp][b] = 0;
     __syncthreads();
-    const uint32_t tile = tile_slot;
-    const uint64_t tile_begin = static_cast<uint64_t>(tile) * kTileItems;
-    // Passes after a dropping first pass sort its *live_count survivors; the
-    // grid is sized for all items, and blocks past the survivors leave (no
-    // block waits on a later tile).
-    const uint32_t items = live_count != nullptr ? *live_count : count;
-    if (tile_begin >= items) return;
-    const uint64_t left = items - tile_begin;
-    const uint32_t n = left < static_cast<uint64_t>(kTileItems) ? static_cast<uint32_t>(left)
-                                                                : kTileItems;
-    const uint32_t bulk = n & ~3u;  // whole 16-byte groups go through the copy engine
+}
 
-    // 1. load the tile
+// Copies keys/values [begin, begin + n) into the tile: whole 16-byte groups
+// with two bulk asynchronous copies (the TMA engine), a ragged tail of < 4
+// items with plain loads.
+template <int kItems>
+__device__ __forceinline__ void tile_issue_load(PassTile<kItems>& t, const uint32_t* keys_in,
+                                                const uint32_t* vals_in, uint64_t begin, uint32_t n) {
+    const uint32_t bulk = n & ~3u;
     if (threadIdx.x == 0) {
         if (bulk != 0u) {
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
-                         ::"r"(shared_address(&loaded)), "r"(2u * bulk * 4u) : "memory");
-            bulk_load(tile_keys, keys_in + tile_begin, bulk * 4u, &loaded);
-            bulk_load(tile_vals, vals_in + tile_begin, bulk * 4u, &loaded);
+                         ::"r"(shared_address(&t.loaded)), "r"(2u * bulk * 4u) : "memory");
+            bulk_load(t.keys, keys_in + begin, bulk * 4u, &t.loaded);
+            bulk_load(t.vals, vals_in + begin, bulk * 4u, &t.loaded);
         } else {
             asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];"
-                         ::"r"(shared_address(&loaded)) : "memory");
+                         ::"r"(shared_address(&t.loaded)) : "memory");
         }
     }
     if (threadIdx.x < n - bulk) {
-        tile_keys[bulk + threadIdx.x] = keys_in[tile_begin + bulk + threadIdx.x];
-        tile_vals[bulk + threadIdx.x] = vals_in[tile_begin + bulk + threadIdx.x];
+        t.keys[bulk + threadIdx.x] = keys_in[begin + bulk + threadIdx.x];
+        t.vals[bulk + threadIdx.x] = vals_in[begin + bulk + threadIdx.x];
     }
-    const bool landed = wait_tile(&loaded);
+}
+
+// Waits (bounded) for the tile's copies; false, with the error reported, when
+// the wait gave up (the block must then leave).
+template <int kItems>
+__device__ __forceinline__ bool tile_wait_load(PassTile<kItems>& t, uint32_t* error) {
+    const bool landed = wait_tile(&t.loaded);
     if (!__syncthreads_and(landed)) {
         // The copies did not complete within the bound: report, wait once more
         // (bounded) so that no copy is left writing this block's shared memory.
         if (threadIdx.x == 0) {
             if (error != nullptr) atomicOr(error, 1u);
-            wait_tile(&loaded);
+            wait_tile(&t.loaded);
         }
-        return;
+        return false;
     }
+    return true;
+}
 
-    // 2. stable ranking within the tile
+// Stable ranking of the tile's n items by digit: warp w owns the contiguous
+// segment [w kItems 32, (w + 1) kItems 32) and walks it 32 items at a time,
+// grouping equal digits with __match_any_sync or one ballot per digit bit.
+// On return rank[] holds each item's position among equal digits of its
+// warp's earlier items, warp_count[w][d] the exclusive prefix of warp w for
+// digit d, and the result is this thread's digit's (threadIdx.x) tile total.
+// Dropped items (drop and key == kDropKey) take no rank.
+template <int kItems, bool kBallot>
+__device__ __forceinline__ uint32_t tile_rank(PassTile<kItems>& t, uint32_t n, int drop, int shift,
+                                              int bits, uint32_t (&rank)[kItems]) {
+    constexpr uint32_t kWarpItems = PassTile<kItems>::kTileItems / kWarps;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t mask = (1u << bits) - 1u;
     const uint32_t seg = static_cast<uint32_t>(warp) * kWarpItems;
     const uint32_t lt_mask = (1u << lane) - 1u;
-    uint32_t rank[kItems];
 #pragma unroll
     for (int k = 0; k < kItems; ++k) {
         const uint32_t i = seg + static_cast<uint32_t>(k) * 32u + lane;
-        const uint32_t key = i < n ? tile_keys[i] : 0u;
+        const uint32_t key = i < n ? t.keys[i] : 0u;
         const bool valid = i < n && !(drop && key == kDropKey);
         const uint32_t dg = valid ? digit_of(key, shift, mask) : 0u;
         uint32_t peers;
@@ -251,25 +277,116 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
             peers = __match_any_sync(0xffffffffu, valid ? static_cast<int>(dg) : -1);
         }
         const int dig = valid ? static_cast<int>(dg) : -1;
-        const uint32_t before = dig >= 0 ? warp_count[warp][dig] : 0u;
+        const uint32_t before = dig >= 0 ? t.warp_count[warp][dig] : 0u;
         __syncwarp();
         rank[k] = before + __popc(peers & lt_mask);
         const int leader = __ffs(peers) - 1;
-        if (dig >= 0 && lane == leader) warp_count[warp][dig] = before + __popc(peers);
+        if (dig >= 0 && lane == leader) t.warp_count[warp][dig] = before + __popc(peers);
         __syncwarp();
     }
     __syncthreads();
     // per-digit totals of the tile and the exclusive per-warp prefixes
-    const int b = threadIdx.x;  // one digit per thread
+    const int b = threadIdx.x;
     uint32_t total = 0;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
-        const uint32_t c = warp_count[w][b];
-        warp_count[w][b] = total;
+        const uint32_t c = t.warp_count[w][b];
+        t.warp_count[w][b] = total;
         total += c;
     }
+    return total;
+}
 
-    // 3. look-back across tiles for this digit
+// With global_base[] set for every digit: the tile's digit starts from the
+// totals, the tile permuted in place into digit order (keys, then values),
+// each digit run written to consecutive global positions.
+template <int kItems>
+__device__ __forceinline__ void tile_scatter(PassTile<kItems>& t, uint32_t n, int drop, int shift,
+                                             int bits, uint32_t total, uint32_t (&rank)[kItems],
+                                             uint32_t* keys_out, uint32_t* vals_out) {
+    constexpr uint32_t kWarpItems = PassTile<kItems>::kTileItems / kWarps;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t mask = (1u << bits) - 1u;
+    const uint32_t seg = static_cast<uint32_t>(warp) * kWarpItems;
+    const int b = threadIdx.x;
+    const uint32_t local_start = block_exclusive_256(total, t.warp_sums);
+    t.digit_start[b] = local_start;
+    if (b == kBins - 1) t.kept = local_start + total;
+    uint32_t item[kItems];
+    bool keep[kItems];
+    __syncthreads();  // digit_start, global_base
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        const uint32_t i = seg + static_cast<uint32_t>(k) * 32u + lane;
+        item[k] = t.keys[i];
+        keep[k] = i < n && !(drop && item[k] == kDropKey);
+        if (keep[k]) {
+            const uint32_t d = digit_of(item[k], shift, mask);
+            rank[k] += t.digit_start[d] + t.warp_count[warp][d];  // final position in the tile
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        if (keep[k]) t.keys[rank[k]] = item[k];
+    }
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) item[k] = t.vals[seg + static_cast<uint32_t>(k) * 32u + lane];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+        if (keep[k]) t.vals[rank[k]] = item[k];
+    }
+    __syncthreads();
+    const uint32_t written = t.kept;  // n unless the pass drops items
+    for (uint32_t i = threadIdx.x; i < written; i += kThreads) {
+        const uint32_t k = t.keys[i];
+        const uint32_t d = digit_of(k, shift, mask);
+        const uint32_t dst = t.global_base[d] + (i - t.digit_start[d]);
+        keys_out[dst] = k;
+        vals_out[dst] = t.vals[i];
+    }
+}
+
+// Items of a pass: *live_count after a dropping first pass, else count.
+__device__ __forceinline__ uint32_t pass_items(uint32_t count, const uint32_t* live_count) {
+    return live_count != nullptr ? *live_count : count;
+}
+
+// ---- onesweep pass: one kernel, cross-tile prefix by decoupled look-back ----
+
+template <int kItems, int kWindow, bool kBallot>
+__global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel(
+    const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+    uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, uint32_t count,
+    const uint32_t* __restrict__ live_count, int drop, int shift, int bits,
+    const uint32_t* __restrict__ hist, uint32_t* __restrict__ counter,
+    uint32_t* __restrict__ status, uint32_t* __restrict__ error, uint32_t stall_tile) {
+    constexpr uint32_t kTileItems = PassTile<kItems>::kTileItems;
+    __shared__ PassTile<kItems> t;
+    // An earlier pass gave up a wait: its output is not a permutation of the
+    // input, so this pass's histogram no longer matches it. Every block leaves.
+    if (wait_failed(error)) return;
+    if (threadIdx.x == 0) t.slot = atomicAdd(counter, 1u);
+    tile_begin(t);
+    // Tiles are numbered in the order blocks start, so every earlier tile's
+    // block has started and will publish without waiting on this one.
+    const uint32_t tile = t.slot;
+    const uint64_t tile_begin_item = static_cast<uint64_t>(tile) * kTileItems;
+    // Passes after a dropping first pass sort its *live_count survivors; the
+    // grid is sized for all items, and blocks past the survivors leave (no
+    // block waits on a later tile).
+    const uint32_t items = pass_items(count, live_count);
+    if (tile_begin_item >= items) return;
+    const uint64_t left = items - tile_begin_item;
+    const uint32_t n = left < static_cast<uint64_t>(kTileItems) ? static_cast<uint32_t>(left) : kTileItems;
+    tile_issue_load(t, keys_in, vals_in, tile_begin_item, n);
+    if (!tile_wait_load(t, error)) return;
+    uint32_t rank[kItems];
+    const uint32_t total = tile_rank<kItems, kBallot>(t, n, drop, shift, bits, rank);
+
+    // look-back across tiles for this thread's digit
+    const int b = threadIdx.x;
     uint32_t* my_status = status + static_cast<uint64_t>(tile) * kBins + b;
     const bool publish = tile != stall_tile;  // test hook: a tile that never publishes
     if (tile == 0) {
@@ -280,79 +397,161 @@ __global__ void __launch_bounds__(kThreads, kItems == 8 ? 5 : 4) onesweep_kernel
     const uint32_t earlier =
         tile == 0 ? 0u : look_back<kWindow>(status + b, tile, kBins, error);
     if (tile != 0 && publish) store_status(my_status, kFlagInclusive | ((earlier + total) & kValueMask));
-
     // global start of each digit: exclusive scan of the pass histogram
-    const uint32_t digit_global = block_exclusive_256(hist[b], warp_sums);
-    const uint32_t local_start = block_exclusive_256(total, warp_sums);
-    digit_start[b] = local_start;
-    global_base[b] = digit_global + earlier;
-    if (b == kBins - 1) tile_kept = local_start + total;
+    t.global_base[b] = block_exclusive_256(hist[b], t.warp_sums) + earlier;
+    tile_scatter(t, n, drop, shift, bits, total, rank, keys_out, vals_out);
+}
 
-    // 4. permute the tile into digit order in place (keys, then values), then
-    //    write digit runs
-    uint32_t item[kItems];
-    bool keep[kItems];
-    __syncthreads();  // digit_start / global_base
-#pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-        const uint32_t i = seg + static_cast<uint32_t>(k) * 32u + lane;
-        item[k] = tile_keys[i];
-        keep[k] = i < n && !(drop && item[k] == kDropKey);
-        if (keep[k]) {
-            const uint32_t d = digit_of(item[k], shift, mask);
-            rank[k] += digit_start[d] + warp_count[warp][d];  // final position in the tile
+// ---- reduce-then-scan pass: count, scan across tiles, scatter ----
+
+// Per tile, the digit counts of its items, stored digit-major:
+// counts[digit * tiles + tile]. Tiles past the items write zeros.
+template <int kItems>
+__global__ void __launch_bounds__(kThreads) count_kernel(
+    const uint32_t* __restrict__ keys, uint32_t count, const uint32_t* __restrict__ live_count,
+    int drop, int shift, int bits, uint32_t tiles, uint32_t* __restrict__ counts,
+    const uint32_t* __restrict__ error) {
+    constexpr uint32_t kTileItems = kThreads * kItems;
+    __shared__ uint32_t bins[kBins];
+    if (wait_failed(error)) return;  // the scan and scatter of this pass leave too
+    bins[threadIdx.x] = 0;
+    __syncthreads();
+    const uint32_t mask = (1u << bits) - 1u;
+    const uint32_t items = pass_items(count, live_count);
+    const uint64_t begin = static_cast<uint64_t>(blockIdx.x) * kTileItems;
+    if (begin < items) {
+        const uint32_t n = items - begin < kTileItems ? static_cast<uint32_t>(items - begin) : kTileItems;
+        const uint32_t* tile = keys + begin;
+        auto add = [&](uint32_t key) {
+            if (!(drop && key == kDropKey)) atomicAdd(&bins[digit_of(key, shift, mask)], 1u);
+        };
+        // 16-byte loads: a tile starts at a multiple of kTileItems items of a
+        // 16-byte aligned array
+        const uint32_t quads = n / 4u;
+        for (uint32_t q = threadIdx.x; q < quads; q += kThreads) {
+            const uint4 v = reinterpret_cast<const uint4*>(tile)[q];
+            add(v.x);
+            add(v.y);
+            add(v.z);
+            add(v.w);
         }
+        if (threadIdx.x < n - quads * 4u) add(tile[quads * 4u + threadIdx.x]);
     }
     __syncthreads();
-#pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-        if (keep[k]) tile_keys[rank[k]] = item[k];
+    counts[static_cast<uint64_t>(threadIdx.x) * tiles + blockIdx.x] = bins[threadIdx.x];
+}
+
+// One block per digit: that digit's counts across the tiles replaced by their
+// exclusive prefix, and the digit's total.
+__global__ void __launch_bounds__(kThreads) scan_kernel(uint32_t* __restrict__ counts, uint32_t tiles,
+                                                        uint32_t* __restrict__ totals,
+                                                        const uint32_t* __restrict__ error) {
+    __shared__ uint32_t warp_sums[kWarps];
+    if (wait_failed(error)) return;
+    uint32_t* row = counts + static_cast<uint64_t>(blockIdx.x) * tiles;
+    const uint32_t per = (tiles + kThreads - 1) / kThreads;
+    const uint32_t first = threadIdx.x * per;
+    const uint32_t last = min(first + per, tiles);
+    uint32_t sum = 0;
+    for (uint32_t i = first; i < last; ++i) sum += row[i];
+    uint32_t run = block_exclusive_256(sum, warp_sums);
+    for (uint32_t i = first; i < last; ++i) {
+        const uint32_t c = row[i];
+        row[i] = run;
+        run += c;
     }
-#pragma unroll
-    for (int k = 0; k < kItems; ++k) item[k] = tile_vals[seg + static_cast<uint32_t>(k) * 32u + lane];
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-        if (keep[k]) tile_vals[rank[k]] = item[k];
-    }
-    __syncthreads();
-    const uint32_t written = tile_kept;  // n unless the pass drops items
-    for (uint32_t i = threadIdx.x; i < written; i += kThreads) {
-        const uint32_t k = tile_keys[i];
-        const uint32_t d = digit_of(k, shift, mask);
-        const uint32_t dst = global_base[d] + (i - digit_start[d]);
-        keys_out[dst] = k;
-        vals_out[dst] = tile_vals[i];
-    }
+    if (threadIdx.x == kThreads - 1) totals[blockIdx.x] = run;
+}
+
+// Tile blockIdx.x ranked and scattered to (start of its digit) + (this tile's
+// prefix for the digit); the digit starts are the exclusive scan of the 256
+// totals, which every block forms. No block waits on another.
+template <int kItems, bool kBallot>
+__global__ void __launch_bounds__(kThreads, 4) scatter_kernel(
+    const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+    uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, uint32_t count,
+    const uint32_t* __restrict__ live_count, int drop, int shift, int bits, uint32_t tiles,
+    const uint32_t* __restrict__ prefix, const uint32_t* __restrict__ totals,
+    uint32_t* __restrict__ error) {
+    constexpr uint32_t kTileItems = PassTile<kItems>::kTileItems;
+    __shared__ PassTile<kItems> t;
+    if (wait_failed(error)) return;
+    const uint32_t items = pass_items(count, live_count);
+    const uint32_t tile = blockIdx.x;
+    const uint64_t tile_begin_item = static_cast<uint64_t>(tile) * kTileItems;
+    if (tile_begin_item >= items) return;
+    tile_begin(t);
+    const uint64_t left = items - tile_begin_item;
+    const uint32_t n = left < static_cast<uint64_t>(kTileItems) ? static_cast<uint32_t>(left) : kTileItems;
+    tile_issue_load(t, keys_in, vals_in, tile_begin_item, n);
+    // the destinations do not depend on the tile: formed while it lands
+    const int b = threadIdx.x;
+    t.global_base[b] = block_exclusive_256(totals[b], t.warp_sums) + prefix[static_cast<uint64_t>(b) * tiles + tile];
+    if (!tile_wait_load(t, error)) return;
+    uint32_t rank[kItems];
+    const uint32_t total = tile_rank<kItems, kBallot>(t, n, drop, shift, bits, rank);
+    tile_scatter(t, n, drop, shift, bits, total, rank, keys_out, vals_out);
 }
 
 }  // namespace
 
 uint64_t sort_scratch_bytes(uint32_t count) {
     const uint64_t tiles = tiles_for(count > 0 ? count : 1);
-    return (static_cast<uint64_t>(kMaxPasses) * kBins + 64 + kMaxPasses * tiles * kBins) *
-           sizeof(uint32_t);
+    // onesweep: histograms, counters, look-back words of every pass
+    const uint64_t onesweep = static_cast<uint64_t>(kMaxPasses) * kBins + 64 + kMaxPasses * tiles * kBins;
+    // reduce-then-scan: per-digit counts of every 4096-item tile, the totals
+    const uint64_t large_tiles = (static_cast<uint64_t>(count) + kThreads * kLargeItems - 1) / (kThreads * kLargeItems);
+    const uint64_t split = static_cast<uint64_t>(kBins) * large_tiles + kBins + 64;
+    return (onesweep > split ? onesweep : split) * sizeof(uint32_t);
 }
 
-cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals,
-                       uint32_t count, int begin_bit, int end_bit, void* scratch,
-                       cudaStream_t stream, uint32_t* error, uint32_t stall_tile,
-                       const uint32_t* kept) {
-    if (count == 0 || end_bit <= begin_bit) return cudaSuccess;
-    if (count > kMaxItems || end_bit - begin_bit > kMaxPasses * kRadixBits) {
-        return cudaErrorInvalidValue;
+namespace {
+
+// Reduce-then-scan passes (count, scan, scatter kernels per pass).
+cudaError_t sort_split(uint32_t*& src_k, uint32_t*& src_v, uint32_t*& dst_k, uint32_t*& dst_v,
+                       uint32_t count, int begin_bit, int end_bit, void* scratch, cudaStream_t stream,
+                       uint32_t* error, const uint32_t* kept, int drop, bool ballot) {
+    const uint32_t tiles =
+        static_cast<uint32_t>((static_cast<uint64_t>(count) + kThreads * kLargeItems - 1) / (kThreads * kLargeItems));
+    uint32_t* counts = static_cast<uint32_t*>(scratch);
+    uint32_t* totals = counts + static_cast<uint64_t>(kBins) * tiles;
+    int pass = 0;
+    for (int shift = begin_bit; shift < end_bit; shift += kRadixBits, ++pass) {
+        const int bits = min(kRadixBits, end_bit - shift);
+        const uint32_t* live = pass > 0 ? kept : nullptr;
+        const int pass_drop = pass == 0 ? drop : 0;
+        count_kernel<kLargeItems><<<tiles, kThreads, 0, stream>>>(src_k, count, live, pass_drop, shift, bits,
+                                                                  tiles, counts, error);
+        scan_kernel<<<1u << bits, kThreads, 0, stream>>>(counts, tiles, totals, error);
+        if (bits < kRadixBits) {
+            // digits from 2^bits on hold no item: their totals are zero
+            const cudaError_t st = cudaMemsetAsync(totals + (1u << bits), 0,
+                                                   (kBins - (1u << bits)) * sizeof(uint32_t), stream);
+            if (st != cudaSuccess) return st;
+        }
+        if (ballot) {
+            scatter_kernel<kLargeItems, true><<<tiles, kThreads, 0, stream>>>(
+                src_k, src_v, dst_k, dst_v, count, live, pass_drop, shift, bits, tiles, counts, totals, error);
+        } else {
+            scatter_kernel<kLargeItems, false><<<tiles, kThreads, 0, stream>>>(
+                src_k, src_v, dst_k, dst_v, count, live, pass_drop, shift, bits, tiles, counts, totals, error);
+        }
+        std::swap(src_k, dst_k);
+        std::swap(src_v, dst_v);
     }
-    // dropping needs the whole key (the dropped key is all ones) and an even
-    // pass count (the survivors end in keys/vals without a copy)
-    if (kept != nullptr && (begin_bit != 0 || end_bit != 32)) return cudaErrorInvalidValue;
-    const int drop = kept != nullptr ? 1 : 0;
+    return cudaSuccess;
+}
+
+// Onesweep passes (histogram of every pass, then one kernel per pass).
+cudaError_t sort_onesweep(uint32_t*& src_k, uint32_t*& src_v, uint32_t*& dst_k, uint32_t*& dst_v,
+                          uint32_t count, int begin_bit, int end_bit, void* scratch, cudaStream_t stream,
+                          uint32_t* error, uint32_t stall_tile, const uint32_t* kept, int drop, bool ballot) {
     const uint32_t tiles = tiles_for(count);
     const bool large = count >= kLargeTileItems;
     const uint32_t large_tiles =
         static_cast<uint32_t>((static_cast<uint64_t>(count) + kThreads * kLargeItems - 1) /
                               (kThreads * kLargeItems));
     const int passes = (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
-    const bool ballot = passes == kMaxPasses || count >= kBallotItems;
     // status words are laid out for 2048-item tiles, enough for either size
     const SortScratch s = sort_scratch(scratch, tiles, passes);
     cudaError_t st = cudaMemsetAsync(scratch, 0, s.zero_bytes, stream);
@@ -363,12 +562,7 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
     }
     const uint32_t hist_cap = static_cast<uint32_t>(sms) * 8u;
     const uint32_t hist_blocks = tiles < hist_cap ? tiles : hist_cap;
-    histogram_kernel<<<hist_blocks, kThreads, 0, stream>>>(keys, count, begin_bit, end_bit, drop,
-                                                           s.hist);
-    uint32_t* src_k = keys;
-    uint32_t* src_v = vals;
-    uint32_t* dst_k = alt_keys;
-    uint32_t* dst_v = alt_vals;
+    histogram_kernel<<<hist_blocks, kThreads, 0, stream>>>(src_k, count, begin_bit, end_bit, drop, s.hist);
     int pass = 0;
     for (int shift = begin_bit; shift < end_bit; shift += kRadixBits, ++pass) {
         const int bits = min(kRadixBits, end_bit - shift);
@@ -392,20 +586,46 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
                                                  pass_drop, shift, bits, s.hist + pass * kBins,
                                                  s.counters + pass, pass_status, error, stall);
         }
-        uint32_t* tk = src_k;
-        uint32_t* tv = src_v;
-        src_k = dst_k;
-        src_v = dst_v;
-        dst_k = tk;
-        dst_v = tv;
+        std::swap(src_k, dst_k);
+        std::swap(src_v, dst_v);
     }
-    if (pass & 1) {
-        st = cudaMemcpyAsync(keys, src_k, static_cast<size_t>(count) * sizeof(uint32_t),
+    return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals,
+                       uint32_t count, int begin_bit, int end_bit, void* scratch,
+                       cudaStream_t stream, uint32_t* error, uint32_t stall_tile,
+                       const uint32_t* kept) {
+    if (count == 0 || end_bit <= begin_bit) return cudaSuccess;
+    if (count > kMaxItems || end_bit - begin_bit > kMaxPasses * kRadixBits) {
+        return cudaErrorInvalidValue;
+    }
+    // dropping needs the whole key (the dropped key is all ones) and an even
+    // pass count (the survivors end in keys/vals without a copy)
+    if (kept != nullptr && (begin_bit != 0 || end_bit != 32)) return cudaErrorInvalidValue;
+    const int drop = kept != nullptr ? 1 : 0;
+    const int passes = (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
+    const bool ballot = passes == kMaxPasses || count >= kBallotItems;
+    uint32_t* src_k = keys;
+    uint32_t* src_v = vals;
+    uint32_t* dst_k = alt_keys;
+    uint32_t* dst_v = alt_vals;
+    const cudaError_t st =
+        count >= kSplitItems
+            ? sort_split(src_k, src_v, dst_k, dst_v, count, begin_bit, end_bit, scratch, stream, error, kept,
+                         drop, ballot)
+            : sort_onesweep(src_k, src_v, dst_k, dst_v, count, begin_bit, end_bit, scratch, stream, error,
+                            stall_tile, kept, drop, ballot);
+    if (st != cudaSuccess) return st;
+    if (passes & 1) {
+        cudaError_t cs = cudaMemcpyAsync(keys, src_k, static_cast<size_t>(count) * sizeof(uint32_t),
+                                         cudaMemcpyDeviceToDevice, stream);
+        if (cs != cudaSuccess) return cs;
+        cs = cudaMemcpyAsync(vals, src_v, static_cast<size_t>(count) * sizeof(uint32_t),
                              cudaMemcpyDeviceToDevice, stream);
-        if (st != cudaSuccess) return st;
-        st = cudaMemcpyAsync(vals, src_v, static_cast<size_t>(count) * sizeof(uint32_t),
-                             cudaMemcpyDeviceToDevice, stream);
-        if (st != cudaSuccess) return st;
+        if (cs != cudaSuccess) return cs;
     }
     return cudaGetLastError();
 }
