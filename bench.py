@@ -18,11 +18,18 @@ and in `blocks.view_with_trace`, the whole view with the traced colours
 feeding the reflection raster (this library's CUDA BVH tracer behind the
 reference's hs_optix_* entry points).
 
+Both steps end with the session's raw-map postprocess of the base raster
+(standard: camera matrices and TF32 pixel rays on a side stream beside the
+rasters, then the fused maps kernel with the surface normals; FlashGS: its
+maps kernel); the reference rebuild's frame has no postprocess (the
+reference's is Jittor code).
+
 Output: one JSON line on rank 0 (driver contract). `value` is whole-job
 frames per second with device-resident inputs, the median over repeated
 timed loops of exactly --steps steps each; `e2e` adds the per-frame
-host->device camera upload and the device->host read of the raw maps the
-session fetches (rgb, acc, depth, normal, spec, diffuse, reflection).
+host->device camera upload and the device->host read of the eight maps the
+session fetches (rgb, acc, dpt, norm, surf_norm, spec, diffuse and
+reflection rgb).
 `blocks` carries the other benchmark configurations measured by the same
 run: the FlashGS 20-view orbit (`flashgs`), the 6M + 1M 1920x1080 scene
 view-sharded over the GPUs (`large_6m`) and the 3840x2160 stress frame split
@@ -282,6 +289,13 @@ class Frame:
         # reference session's sequence.
         lib = library if library is not None else ops.load_native_library()
         self.fused_glue = hasattr(lib, "hs_b200_precise_sh_colors5_f32_v1")
+        # The session's raw-map postprocess is part of the frame with this
+        # library (the reference's is Jittor code, which its rebuild lacks):
+        # the camera terms and pixel rays on a side stream beside the rasters,
+        # then one maps kernel after them.
+        self.with_post = hasattr(lib, "hs_b200_postprocess_camera_f32_v1")
+        self.post_stream = torch.cuda.Stream(device=device) if self.with_post else None
+        self.cam_terms_buf = self.rays_buf = None
         self.cam = None
         self.split = None  # list: per raster call stage timings (instrumented pass)
         self.tile_rows = None  # (begin, end): render only this strip of tile rows
@@ -302,13 +316,17 @@ class Frame:
         self.bg3 = torch.zeros(3, device=self.device)
         vertices, triangles = ops.gaussian_disks(self.r_xyz, self.r_rot_raw, self.r_scale_exp)
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        ops.build_trace_scene(vertices, triangles, scene_signature=1, context=self.ctx_r)
-        e1.record()
-        torch.cuda.synchronize()
+        times = []
+        for signature in range(1, 5):  # the first build also allocates the scene's buffers
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ops.build_trace_scene(vertices, triangles, scene_signature=signature, context=self.ctx_r)
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
         self.traced = True
-        return e0.elapsed_time(e1)
+        self.trace_first_build_ms = times[0]
+        return float(np.median(times[1:]))
 
     def trace(self, rays):
         """The reflection trace of one view (hs_optix_trace_f32_v1): one ray
@@ -336,50 +354,35 @@ class Frame:
         torch = self.torch
         self.cam = cam
         host = upload_from if upload_from is not None else torch.from_numpy(camera_row(cam, self.scenes))
-        if self.backend == "standard":
-            self.cam_dev = host.to(self.device, non_blocking=True)
-            self.view, self.proj, self.center = self.cam_dev[:16].view(4, 4), self.cam_dev[16:32].view(4, 4), \
-                self.cam_dev[32:35]
-        else:
-            # FlashGS takes the camera as host values; only the ray centre is uploaded
-            self.center = host[32:35].to(self.device, non_blocking=True)
-
-    def postprocess(self, base, events=None):
-        """The session's raw-map postprocess of the base raster (standard:
-        postprocess_raster with depth_to_normal, math.py:426-463; FlashGS:
-        _flashgs_postprocess, renderer.py:176-202). `events`, when given, is a
-        list of 3 CUDA events around the camera matrices and rays and the maps."""
-        ops, cam, torch = self.ops, self.cam, self.torch
-        rec = (lambda i: events[i].record()) if events else (lambda i: None)
-        rec(0)
-        if self.backend == "standard":
-            m = ops.postprocess_camera(cam.width, cam.height, 2.0 * math.atan(cam.tan_fovx),
-                                       2.0 * math.atan(cam.tan_fovy), self.view, context=self.ctx)
-            if getattr(self, "rays", None) is None:
-                f = dict(dtype=torch.float32, device=self.device)
-                self.rays = torch.empty((cam.width * cam.height, 3), **f)
-                self.rays_scratch = torch.empty((cam.width * cam.height, 3), **f)
-            rays = ops.pixel_rays(cam.width, cam.height, m["inverse_intrinsics"], m["rotation"], context=self.ctx,
-                                  out=self.rays, scratch=self.rays_scratch)
-            rec(1)
-            maps = ops.standard_postprocess(base.color, base.auxiliary, rays, m["origin"], m["normal_rotation"],
-                                            library=self.library)
-        else:
-            wv = torch.from_numpy(np.ascontiguousarray(cam.world_view()[:3, :3].T)).to(self.device)
-            rec(1)
-            maps = ops.flashgs_postprocess(base, wv, library=self.library)
-        rec(2)
-        return maps
+        self.cam_dev = host.to(self.device, non_blocking=True)
+        self.view, self.proj, self.center = self.cam_dev[:16].view(4, 4), self.cam_dev[16:32].view(4, 4), \
+            self.cam_dev[32:35]
+        # FlashGS takes the camera as host values; the device row gives the
+        # ray centre and the postprocess's normal rotation
 
     def render(self, events=None):
-        """One view. `events`, when given, is a list of 5 CUDA events recorded
-        between the stages (base, reflection prepare, reflection, fusion); the
+        """One view. `events`, when given, is a list of CUDA events recorded
+        between the stages (base, reflection prepare, reflection, fusion, and
+        with the postprocess its camera terms and its maps: 5 or 7 events); the
         branches then run one after the other so that each stage is timed
         alone. Otherwise, with self.concurrent, both raster branches go to the
-        library in one concurrent call."""
+        library in one concurrent call, and the postprocess's camera terms and
+        pixel rays run on a side stream beside them."""
         ops, torch, cam, lib = self.ops, self.torch, self.cam, self.library
         sequential = events is not None or not self.concurrent
         rec = (lambda i: events[i].record()) if events else (lambda i: None)
+        post = self.with_post
+        terms = None
+        fov_x, fov_y = 2.0 * math.atan(cam.tan_fovx), 2.0 * math.atan(cam.tan_fovy)
+        if post and self.backend == "standard" and self.cam_terms_buf is None:
+            f = dict(dtype=torch.float32, device=self.device)
+            self.cam_terms_buf = torch.empty(30, **f)
+            self.rays_buf = torch.empty((cam.height * cam.width, 3), **f)
+        if post and self.backend == "standard" and events is None:
+            self.post_stream.wait_stream(torch.cuda.current_stream(self.device))
+            terms = ops.postprocess_camera_rays(cam.width, cam.height, fov_x, fov_y, self.view, context=self.ctx,
+                                                stream=self.post_stream.cuda_stream, camera=self.cam_terms_buf,
+                                                rays=self.rays_buf)
         rec(0)
         if self.backend == "standard":
             if self.fused_glue:
@@ -441,11 +444,34 @@ class Frame:
                                           refl.color[:3].permute(1, 2, 0).contiguous(),
                                           spec.permute(1, 2, 0).contiguous(), library=lib)
         rec(4)
-        return base, refl, fused, rays
+        maps = None
+        if post:
+            if self.backend == "standard":
+                if terms is None:  # instrumented pass: the camera terms alone, on this stream
+                    terms = ops.postprocess_camera_rays(cam.width, cam.height, fov_x, fov_y, self.view,
+                                                        context=self.ctx, camera=self.cam_terms_buf,
+                                                        rays=self.rays_buf)
+                else:
+                    torch.cuda.current_stream(self.device).wait_stream(self.post_stream)
+                rec(5)
+                maps = ops.standard_postprocess(base.color, base.auxiliary, terms["rays"], terms["origin"],
+                                                terms["normal_rotation"], library=lib)
+            else:
+                normal_rotation = self.view[:3, :3].t().contiguous()
+                rec(5)
+                maps = ops.flashgs_postprocess(base, normal_rotation, library=lib)
+            rec(6)
+        return base, refl, fused, rays, maps
 
     def maps_for_host(self, result):
-        """The raw maps the session reads back: rgb, acc, depth, normal, spec, diffuse, reflection."""
-        base, _, fused, _ = result
+        """The maps the session reads back (session.py:33-42): rgb, acc, dpt,
+        norm, surf_norm, spec, diffuse and reflection rgb, with the
+        postprocess; without it (the reference rebuild) the raw planes they
+        come from (no surface normals)."""
+        base, _, fused, _, maps = result
+        if maps is not None:
+            return [fused["rgb_map"], maps["acc_map"], maps["dpt_map"], maps["norm_map"], maps["surf_norm_map"],
+                    maps["spec_map"], fused["dif_rgb_map"], fused["ref_rgb_map"]]
         if self.backend == "standard":
             acc, depth, normal, spec = base.auxiliary[1], base.auxiliary[0], base.auxiliary[2:5], base.color[3]
         else:
@@ -465,6 +491,11 @@ class Frame:
             extra = 1 if self.backend == "standard" else 0  # direction + SH + concatenation
         else:
             extra = 2 if self.backend == "standard" else 0  # direction + SH
+        if self.with_post:
+            # standard: camera inputs, 2 inverse transposes, camera pack, pixel
+            # rays, maps (the inverses' cuSOLVER/cuBLAS kernels are not ours);
+            # FlashGS: maps
+            extra += 6 if self.backend == "standard" else 1
         return 2 * per_raster + extra + 3  # + reflection prefix, suffix, fusion
 
 
@@ -677,17 +708,20 @@ def stage_split(frame: Frame, cam, steps: int) -> dict:
     call, the branches sequential."""
     torch = frame.torch
     stage_names = ("base_raster", "reflection_prepare", "reflection_raster", "fusion")
-    sums = np.zeros(4)
+    if frame.with_post:
+        stage_names += ("postprocess_camera_rays", "postprocess_maps")
+    n = len(stage_names)
+    sums = np.zeros(n)
     for c in {id(c): c for c in (frame.ctx, frame.ctx_r)}.values():
         c.stage_timing(True)
         c.read_stage_timing()
     frame.split = []
     for _ in range(steps):
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(n + 1)]
         frame.set_camera(cam)
         frame.render(ev)
         torch.cuda.synchronize()
-        sums += [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
+        sums += [ev[i].elapsed_time(ev[i + 1]) for i in range(n)]
     for c in {id(c): c for c in (frame.ctx, frame.ctx_r)}.values():
         c.stage_timing(False)
     split, frame.split = frame.split, None
@@ -816,18 +850,6 @@ def run_ours(args, workload: Workload) -> int:
     fps_total = (1 if strips else world) * 1000.0 / ms
 
     stages = stage_split(frame, scenes.orbit_camera(workload.scene, 0), args.steps)
-    # the session's raw-map postprocess of the base raster (not part of the
-    # headline frame: the reference rebuild has no counterpart to time)
-    base = frame.render()[0]
-    post = np.zeros(2)
-    for s in range(args.steps + 2):
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-        frame.postprocess(base, ev)
-        torch.cuda.synchronize()
-        if s >= 2:
-            post += [ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])]
-    stages["postprocess_camera_rays"] = float(post[0] / args.steps)
-    stages["postprocess_maps"] = float(post[1] / args.steps)
 
     e2e = end_to_end(job, frame, cams, cam_rows, args)
 
@@ -847,9 +869,11 @@ def run_ours(args, workload: Workload) -> int:
                                        "base and reflection rasters in one concurrent call "
                                        "(hs_b200_*_forward_many_v2)",
                            "stages_ms": "from a separate pass with the branches sequential, each stage alone; "
-                                        "postprocess_* (the session's raw-map postprocess of the base raster: "
-                                        "camera matrices and TF32 pixel-ray GEMMs, then the fused maps kernel) "
-                                        "is outside the headline frame"},
+                                        "postprocess_camera_rays (camera matrices and the TF32 pixel rays, which "
+                                        "in the headline frame run on a side stream beside the rasters) and "
+                                        "postprocess_maps (the fused maps kernel after them) are part of the frame",
+                           "postprocess": "in the frame (session raw-map postprocess of the base raster); the "
+                                          "reference rebuild's frame has none (its postprocess is Jittor code)"},
                 "stages_ms": stages, "clocks": clocks.summary(), "e2e": e2e,
                 "gpu_launches": frame.launches_per_step(spec.width, spec.height) * args.steps * t["repeats"]}
     if world == 1 and line is not None:
@@ -859,6 +883,7 @@ def run_ours(args, workload: Workload) -> int:
     if line is not None:
         stages["trace"] = traced.pop("trace_ms")
         stages["trace_scene_build"] = traced.pop("scene_build_ms")
+        stages["trace_scene_first_build"] = traced.pop("scene_first_build_ms")
         line.setdefault("blocks", {})["view_with_trace"] = traced
     frame.close()
     frame = None
@@ -910,14 +935,14 @@ def trace_block(job: Job, args, frame: Frame, cams, device_cams, strips: bool) -
             "ms_per_step": t["ms_per_step"], "steps": args.steps, "repeats": t["repeats"],
             "what": "the headline view plus the reflection trace (hs_optix_trace_f32_v1, CUDA BVH tracer) whose "
                     "colours feed the reflection raster, as the reference session renders a view",
-            "trace_ms": trace_ms, "scene_build_ms": build_ms,
+            "trace_ms": trace_ms, "scene_build_ms": build_ms, "scene_first_build_ms": frame.trace_first_build_ms,
             "trace_rays": frame.nr}
 
 
 def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
     """The same frames through the public API with host buffers: every step
-    uploads its camera from pinned host memory and reads the seven raw maps
-    back into pinned host memory (two slots) on a copy stream."""
+    uploads its camera from pinned host memory and reads the session's eight
+    maps back into pinned host memory (two slots) on a copy stream."""
     import torch
     stream = torch.cuda.current_stream()
     pinned_cam = [row.pin_memory() for row in cam_rows]
@@ -925,7 +950,7 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
     host_maps = [[torch.empty(m.shape, dtype=m.dtype, pin_memory=True) for m in frame.maps_for_host(res)]
                  for _ in range(2)]
     d2h = sum(m.numel() * m.element_size() for m in host_maps[0])
-    h2d = pinned_cam[0].numel() * 4 if frame.backend == "standard" else 3 * 4
+    h2d = pinned_cam[0].numel() * 4  # the camera row: view, projection, centre
     copy_stream = torch.cuda.Stream(device=frame.device)
 
     def read_back(s, out, done):

@@ -57,6 +57,15 @@ constexpr uint64_t kMathInfoOffset = 1280;
 constexpr uint64_t kMathFactorArrayOffset = 1536;
 constexpr uint64_t kMathRhsArrayOffset = 1792;
 constexpr uint64_t kMathSolverWorkspaceOffset = 2048;
+// Region of the view-camera entry (hs_b200_postprocess_camera_f32_v1), so
+// that it may run on a caller's stream beside the legacy-stream helpers: its
+// own inverse buffers at the offsets above relative to kMathViewOffset, and
+// K, world_view^T and the camera-to-world matrix in the first 256 bytes.
+constexpr uint64_t kMathViewOffset = 1024 * 1024;
+constexpr uint64_t kMathViewK = kMathViewOffset;
+constexpr uint64_t kMathViewWt = kMathViewOffset + 64;
+constexpr uint64_t kMathViewC2w = kMathViewOffset + 128;
+constexpr uint64_t kMathViewRays = kMathViewOffset + 256;  // 64 floats: rays of images under 8 pixels
 
 unsigned char* math_at(HsRasterizerContext* c, uint64_t offset) {
     return static_cast<unsigned char*>(c->math_workspace) + offset;
@@ -159,6 +168,11 @@ int32_t guard(char* error_text, uint64_t error_capacity, Function&& function) no
 
 cudaError_t release_math(HsRasterizerContext* c) noexcept {
     cudaError_t first = cudaSuccess;
+    if (c->view_camera_event != nullptr) {
+        const cudaError_t e = cudaEventDestroy(c->view_camera_event);
+        if (first == cudaSuccess) first = e;
+        c->view_camera_event = nullptr;
+    }
     if (c->math_workspace != nullptr) {
         const cudaError_t e = cudaFree(c->math_workspace);
         if (first == cudaSuccess) first = e;
@@ -226,12 +240,20 @@ int32_t initialize_math(HsRasterizerContext* c, char* error_text, uint64_t error
         cs = cudaMemcpy(math_at(c, kMathFactorArrayOffset), &factor, sizeof(factor), cudaMemcpyHostToDevice);
     if (cs == cudaSuccess)
         cs = cudaMemcpy(math_at(c, kMathRhsArrayOffset), &rhs, sizeof(rhs), cudaMemcpyHostToDevice);
+    float* view_factor = reinterpret_cast<float*>(math_at(c, kMathViewOffset + kMathFactorOffset));
+    float* view_rhs = reinterpret_cast<float*>(math_at(c, kMathViewOffset + kMathRhsOffset));
+    if (cs == cudaSuccess)
+        cs = cudaMemcpy(math_at(c, kMathViewOffset + kMathFactorArrayOffset), &view_factor, sizeof(view_factor),
+                        cudaMemcpyHostToDevice);
+    if (cs == cudaSuccess)
+        cs = cudaMemcpy(math_at(c, kMathViewOffset + kMathRhsArrayOffset), &view_rhs, sizeof(view_rhs),
+                        cudaMemcpyHostToDevice);
     if (cs != cudaSuccess)
         return cuda_failure(cs, "math workspace initialization", error_text, error_capacity);
     ss = cusolverDnSgetrf_bufferSize(c->math_solver, 4, 4, factor, 4, &c->math_inverse_workspace_count);
     if (ss != CUSOLVER_STATUS_SUCCESS)
         return cusolver_failure(ss, "math inverse workspace query", error_text, error_capacity);
-    if (kMathSolverWorkspaceOffset + uint64_t(c->math_inverse_workspace_count) * sizeof(float) >
+    if (kMathViewOffset + kMathSolverWorkspaceOffset + uint64_t(c->math_inverse_workspace_count) * sizeof(float) >
         kMathWorkspaceBytes) {
         return fail(HS_STATUS_RANGE_ERROR, "math inverse workspace exceeds persistent allocation",
                     error_text, error_capacity);
@@ -1334,6 +1356,69 @@ int32_t hs_rasterizer_precise_camera_center_f32_v2(HsRasterizerHandle handle,
     });
 }
 
+namespace {
+
+// Buffers of one general inverse (device memory of the math workspace).
+struct InverseBuffers {
+    float* factor;
+    float* rhs;
+    float* work;
+    int* pivots;
+    int* info;
+    float** factor_array;  // device array holding `factor`
+    float** rhs_array;     // device array holding `rhs`
+};
+
+InverseBuffers inverse_buffers(HsRasterizerContext* c, uint64_t base) {
+    return InverseBuffers{reinterpret_cast<float*>(math_at(c, base + kMathFactorOffset)),
+                          reinterpret_cast<float*>(math_at(c, base + kMathRhsOffset)),
+                          reinterpret_cast<float*>(math_at(c, base + kMathSolverWorkspaceOffset)),
+                          reinterpret_cast<int*>(math_at(c, base + kMathPivotsOffset)),
+                          reinterpret_cast<int*>(math_at(c, base + kMathInfoOffset)),
+                          reinterpret_cast<float**>(math_at(c, base + kMathFactorArrayOffset)),
+                          reinterpret_cast<float**>(math_at(c, base + kMathRhsArrayOffset))};
+}
+
+// linalg_inv_ex as in reference c_api.cpp:1493-1600: identity RHS, LU of the
+// row-major n x n `input` read as column-major A^T (cusolverDnSgetrf), getrs
+// with OP_T (cublasSgetrsBatched), the column-major solution transposed into
+// row-major `output`. The caller holds the handle's mutex and has bound the
+// handle's solver and TF32 BLAS to `stream`.
+int32_t general_inverse(HsRasterizerContext* h, const float* input, int n, const InverseBuffers& b,
+                        float* output, cudaStream_t stream, char* error_text, uint64_t error_capacity) {
+    const size_t bytes = static_cast<size_t>(n) * n * sizeof(float);
+    cudaError_t ce = cudaMemcpyAsync(b.rhs, math_at(h, n == 3 ? kMathIdentity3Offset : kMathIdentity4Offset),
+                                     bytes, cudaMemcpyDeviceToDevice, stream);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(b.factor, input, bytes, cudaMemcpyDeviceToDevice, stream);
+    if (ce != cudaSuccess)
+        return cuda_failure(ce, "precise_general_inverse identity/input copy", error_text, error_capacity);
+    int work_count = 0;
+    cusolverStatus_t ss = cusolverDnSgetrf_bufferSize(h->math_solver, n, n, b.factor, n, &work_count);
+    if (ss != CUSOLVER_STATUS_SUCCESS)
+        return cusolver_failure(ss, "precise_general_inverse cusolverDnSgetrf_bufferSize", error_text,
+                                error_capacity);
+    if (work_count > h->math_inverse_workspace_count) {
+        return fail(HS_STATUS_RANGE_ERROR, "precise_general_inverse persistent workspace is too small",
+                    error_text, error_capacity);
+    }
+    ss = cusolverDnSgetrf(h->math_solver, n, n, b.factor, n, b.work, b.pivots, b.info);
+    if (ss != CUSOLVER_STATUS_SUCCESS)
+        return cusolver_failure(ss, "precise_general_inverse cusolverDnSgetrf", error_text, error_capacity);
+    int32_t* solve_info = &h->math_solve_info[h->math_general_inverse_calls % 16];
+    *solve_info = 0;
+    const cublasStatus_t bs = cublasSgetrsBatched(h->math_tf32_blas, CUBLAS_OP_T, n, n, b.factor_array, n,
+                                                  b.pivots, b.rhs_array, n, solve_info, 1);
+    if (bs != CUBLAS_STATUS_SUCCESS)
+        return cublas_failure(bs, "precise_general_inverse cublasSgetrsBatched", error_text, error_capacity);
+    ce = hs::precise::column_to_row_major(b.rhs, static_cast<uint32_t>(n), output, stream);
+    if (ce != cudaSuccess)
+        return cuda_failure(ce, "precise_general_inverse output transpose", error_text, error_capacity);
+    ++h->math_general_inverse_calls;
+    return HS_STATUS_OK;
+}
+
+}  // namespace
+
 int32_t hs_rasterizer_precise_general_inverse_f32_v2(HsRasterizerHandle handle,
                                                      const float* input, uint32_t dimension,
                                                      float* output, char* error_text,
@@ -1361,51 +1446,125 @@ int32_t hs_rasterizer_precise_general_inverse_f32_v2(HsRasterizerHandle handle,
                         "precise_general_inverse math context is not initialized", error_text,
                         error_capacity);
         }
-        // linalg_inv_ex as in reference c_api.cpp:1493-1600: identity RHS, LU of
-        // the row-major input read as column-major A^T, getrs with OP_T.
-        const int n = static_cast<int>(dimension);
-        float* factor = reinterpret_cast<float*>(math_at(handle, kMathFactorOffset));
-        float* rhs = reinterpret_cast<float*>(math_at(handle, kMathRhsOffset));
-        float* work = reinterpret_cast<float*>(math_at(handle, kMathSolverWorkspaceOffset));
-        int* pivots = reinterpret_cast<int*>(math_at(handle, kMathPivotsOffset));
-        int* info = reinterpret_cast<int*>(math_at(handle, kMathInfoOffset));
-        float** factor_array = reinterpret_cast<float**>(math_at(handle, kMathFactorArrayOffset));
-        float** rhs_array = reinterpret_cast<float**>(math_at(handle, kMathRhsArrayOffset));
-        const size_t bytes = static_cast<size_t>(n) * n * sizeof(float);
-        cudaError_t ce = cudaMemcpyAsync(
-            rhs, math_at(handle, n == 3 ? kMathIdentity3Offset : kMathIdentity4Offset), bytes,
-            cudaMemcpyDeviceToDevice, nullptr);
-        if (ce == cudaSuccess) ce = cudaMemcpyAsync(factor, input, bytes, cudaMemcpyDeviceToDevice, nullptr);
-        if (ce != cudaSuccess)
-            return cuda_failure(ce, "precise_general_inverse identity/input copy", error_text, error_capacity);
-        int work_count = 0;
-        cusolverStatus_t ss = cusolverDnSgetrf_bufferSize(handle->math_solver, n, n, factor, n, &work_count);
-        if (ss != CUSOLVER_STATUS_SUCCESS)
-            return cusolver_failure(ss, "precise_general_inverse cusolverDnSgetrf_bufferSize",
-                                    error_text, error_capacity);
-        if (work_count > handle->math_inverse_workspace_count) {
-            return fail(HS_STATUS_RANGE_ERROR, "precise_general_inverse persistent workspace is too small",
-                        error_text, error_capacity);
-        }
-        ss = cusolverDnSgetrf(handle->math_solver, n, n, factor, n, work, pivots, info);
-        if (ss != CUSOLVER_STATUS_SUCCESS)
-            return cusolver_failure(ss, "precise_general_inverse cusolverDnSgetrf", error_text, error_capacity);
-        int32_t* solve_info = &handle->math_solve_info[handle->math_general_inverse_calls % 16];
-        *solve_info = 0;
-        const cublasStatus_t bs = cublasSgetrsBatched(handle->math_tf32_blas, CUBLAS_OP_T, n, n,
-                                                      factor_array, n, pivots, rhs_array, n,
-                                                      solve_info, 1);
-        if (bs != CUBLAS_STATUS_SUCCESS)
-            return cublas_failure(bs, "precise_general_inverse cublasSgetrsBatched", error_text,
-                                  error_capacity);
-        ce = hs::precise::column_to_row_major(rhs, dimension, output, nullptr);
-        if (ce != cudaSuccess)
-            return cuda_failure(ce, "precise_general_inverse output transpose", error_text, error_capacity);
+        const int32_t status = general_inverse(handle, input, static_cast<int>(dimension),
+                                               inverse_buffers(handle, 0), output, nullptr, error_text,
+                                               error_capacity);
+        if (status != HS_STATUS_OK) return status;
         const cudaError_t trailing = cudaGetLastError();
         if (trailing != cudaSuccess)
             return cuda_failure(trailing, "precise_general_inverse trailing CUDA error", error_text,
                                 error_capacity);
-        ++handle->math_general_inverse_calls;
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_b200_postprocess_camera_f32_v1(HsRasterizerHandle handle, int32_t width, int32_t height,
+                                          double fov_x, double fov_y, const float* world_view4x4,
+                                          float* camera30, float* rays_n3, void* stream, char* error_text,
+                                          uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (width <= 0 || height <= 0) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "postprocess_camera width and height must be positive",
+                        error_text, error_capacity);
+        }
+        const uint64_t count = static_cast<uint64_t>(width) * static_cast<uint64_t>(height);
+        if (count > static_cast<uint64_t>(INT_MAX)) {
+            return fail(HS_STATUS_RANGE_ERROR, "postprocess_camera pixel count exceeds cuBLAS int range",
+                        error_text, error_capacity);
+        }
+        if (!std::isfinite(fov_x) || !std::isfinite(fov_y)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "postprocess_camera fields of view must be finite",
+                        error_text, error_capacity);
+        }
+        if (handle == nullptr || world_view4x4 == nullptr || camera30 == nullptr || rays_n3 == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "postprocess_camera received a null buffer", error_text,
+                        error_capacity);
+        }
+        const cudaError_t prior = cudaGetLastError();
+        if (prior != cudaSuccess)
+            return cuda_failure(prior, "postprocess_camera preexisting CUDA error", error_text, error_capacity);
+        const int32_t ds = select_device(handle, error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        std::lock_guard<std::mutex> lock(handle->mutex);
+        if (handle->math_workspace == nullptr || handle->math_solver == nullptr ||
+            handle->math_tf32_blas == nullptr) {
+            return fail(HS_STATUS_INTERNAL_ERROR, "postprocess_camera math context is not initialized",
+                        error_text, error_capacity);
+        }
+        // The intrinsics as depth_to_normal builds them (math.py:338-389):
+        // focal = float32(length) / float32(2 tan(float32(fov) / 2)) with the
+        // tangent in double, principal point float32(length) / 2.
+        auto focal = [](int length, double fov) {
+            const float half = static_cast<float>(fov) / 2.0f;
+            const float denominator = static_cast<float>(2.0 * std::tan(static_cast<double>(half)));
+            return static_cast<float>(length) / denominator;
+        };
+        const float fx = focal(width, fov_x), fy = focal(height, fov_y);
+        const float cx = static_cast<float>(width) / 2.0f, cy = static_cast<float>(height) / 2.0f;
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        float* k9 = reinterpret_cast<float*>(math_at(handle, kMathViewK));
+        float* wt16 = reinterpret_cast<float*>(math_at(handle, kMathViewWt));
+        float* c2w16 = reinterpret_cast<float*>(math_at(handle, kMathViewC2w));
+        // the region is this entry's own: order after the previous call's use of it
+        cudaError_t ce = cudaSuccess;
+        if (handle->view_camera_event == nullptr) {
+            ce = cudaEventCreateWithFlags(&handle->view_camera_event, cudaEventDisableTiming);
+        } else {
+            ce = cudaStreamWaitEvent(s, handle->view_camera_event, 0);
+        }
+        if (ce == cudaSuccess) ce = hs::post::camera_inputs(fx, cx, fy, cy, world_view4x4, k9, wt16, s);
+        if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera inputs", error_text, error_capacity);
+        // the two inverses of precise_general_inverse, on `stream`
+        cublasStatus_t bs = cublasSetStream(handle->math_tf32_blas, s);
+        cusolverStatus_t ss = cusolverDnSetStream(handle->math_solver, s);
+        int32_t status = HS_STATUS_OK;
+        if (bs != CUBLAS_STATUS_SUCCESS) {
+            status = cublas_failure(bs, "postprocess_camera cublasSetStream", error_text, error_capacity);
+        } else if (ss != CUSOLVER_STATUS_SUCCESS) {
+            status = cusolver_failure(ss, "postprocess_camera cusolverDnSetStream", error_text, error_capacity);
+        } else {
+            const InverseBuffers view = inverse_buffers(handle, kMathViewOffset);
+            status = general_inverse(handle, k9, 3, view, camera30, s, error_text, error_capacity);
+            if (status == HS_STATUS_OK)
+                status = general_inverse(handle, wt16, 4, view, c2w16, s, error_text, error_capacity);
+            // images under kMmaMinRows pixels: the reference's cuBLAS products on this stream
+            if (status == HS_STATUS_OK && count < hs::post::kMmaMinRows) {
+                float* scratch = reinterpret_cast<float*>(math_at(handle, kMathViewRays));
+                ce = hs::post::camera_pack(c2w16, world_view4x4, camera30, s);
+                if (ce == cudaSuccess) ce = hs::post::pixel_grid(width, height, rays_n3, s);
+                const float alpha = 1.0f, beta = 0.0f;
+                if (ce != cudaSuccess) {
+                    status = cuda_failure(ce, "postprocess_camera rays", error_text, error_capacity);
+                } else {
+                    bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3, static_cast<int>(count),
+                                     3, &alpha, camera30, 3, rays_n3, 3, &beta, scratch, 3);
+                    if (bs == CUBLAS_STATUS_SUCCESS)
+                        bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3, static_cast<int>(count),
+                                         3, &alpha, camera30 + 9, 3, scratch, 3, &beta, rays_n3, 3);
+                    if (bs != CUBLAS_STATUS_SUCCESS)
+                        status = cublas_failure(bs, "postprocess_camera cublasSgemm", error_text, error_capacity);
+                }
+            }
+        }
+        // the handles go back to the legacy default stream of the other helpers
+        const cublasStatus_t rb = cublasSetStream(handle->math_tf32_blas, nullptr);
+        const cusolverStatus_t rs = cusolverDnSetStream(handle->math_solver, nullptr);
+        if (status != HS_STATUS_OK) return status;
+        if (rb != CUBLAS_STATUS_SUCCESS)
+            return cublas_failure(rb, "postprocess_camera cublasSetStream", error_text, error_capacity);
+        if (rs != CUSOLVER_STATUS_SUCCESS)
+            return cusolver_failure(rs, "postprocess_camera cusolverDnSetStream", error_text, error_capacity);
+        if (count >= hs::post::kMmaMinRows) {
+            ce = hs::post::camera_pack(c2w16, world_view4x4, camera30, s);
+            if (ce == cudaSuccess) ce = hs::post::pixel_rays(width, height, camera30, camera30 + 9, rays_n3, s);
+            if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera rays", error_text, error_capacity);
+        }
+        ce = cudaEventRecord(handle->view_camera_event, s);
+        if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera event", error_text, error_capacity);
+        handle->math_matmul_calls += 2;
+        const cudaError_t trailing = cudaGetLastError();
+        if (trailing != cudaSuccess)
+            return cuda_failure(trailing, "postprocess_camera execution", error_text, error_capacity);
         return ok(error_text, error_capacity);
     });
 }

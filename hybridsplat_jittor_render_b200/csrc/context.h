@@ -136,6 +136,7 @@ struct HsRasterizerContext {
     uint64_t math_growth_count = 0;
     int32_t math_inverse_workspace_count = 0;
     int32_t math_solve_info[16] = {};
+    cudaEvent_t view_camera_event = nullptr;  // end of the last view-camera call (its workspace region)
     uint64_t math_handle_create_count = 0;
     uint64_t math_camera_center_calls = 0;
     uint64_t math_general_inverse_calls = 0;

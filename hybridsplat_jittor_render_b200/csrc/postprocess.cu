@@ -276,6 +276,27 @@ __global__ void __launch_bounds__(kThreads) tf32_rows3_kernel(
     }
 }
 
+__global__ void camera_inputs_kernel(float fx, float cx, float fy, float cy, const float* __restrict__ wv,
+                                     float* __restrict__ k9, float* __restrict__ wt16) {
+    const int i = threadIdx.x;
+    if (i < 9) {
+        const float k[9] = {fx, 0.0f, cx, 0.0f, fy, cy, 0.0f, 0.0f, 1.0f};
+        k9[i] = k[i];
+    }
+    if (i < 16) wt16[i] = wv[4 * (i % 4) + i / 4];
+}
+
+__global__ void camera_pack_kernel(const float* __restrict__ c2w, const float* __restrict__ wv,
+                                   float* __restrict__ out) {
+    const int i = threadIdx.x;
+    if (i < 9) {
+        const int r = i / 3, c = i % 3;
+        out[9 + i] = c2w[4 * r + c];    // rotation c2w[:3,:3]
+        out[21 + i] = wv[4 * c + r];    // normal rotation world_view[:3,:3]^T
+    }
+    if (i < 3) out[18 + i] = c2w[4 * i + 3];  // origin c2w[:3,3]
+}
+
 unsigned mma_grid_for(uint64_t rows) {
     const uint64_t warps = (rows + kMmaRowsPerWarp - 1) / kMmaRowsPerWarp;
     const uint64_t blocks = (warps + kThreads / 32 - 1) / (kThreads / 32);
@@ -310,6 +331,17 @@ cudaError_t matmul_nt_n3k3(const float* left_n3, const float* right3x3, uint64_t
     if (rows == 0) return cudaSuccess;
     tf32_rows3_kernel<false><<<mma_grid_for(rows), kThreads, 0, s>>>(rows, 1, left_n3, right3x3,
                                                                      nullptr, out_n3);
+    return cudaGetLastError();
+}
+
+cudaError_t camera_inputs(float fx, float cx, float fy, float cy, const float* world_view4x4, float* k9,
+                          float* wt16, cudaStream_t s) {
+    camera_inputs_kernel<<<1, 32, 0, s>>>(fx, cx, fy, cy, world_view4x4, k9, wt16);
+    return cudaGetLastError();
+}
+
+cudaError_t camera_pack(const float* c2w16, const float* world_view4x4, float* out30, cudaStream_t s) {
+    camera_pack_kernel<<<1, 32, 0, s>>>(c2w16, world_view4x4, out30);
     return cudaGetLastError();
 }
 

@@ -50,6 +50,16 @@ cudaError_t pixel_rays(int width, int height, const float* inverse_intrinsics3x3
 cudaError_t matmul_nt_n3k3(const float* left_n3, const float* right3x3, uint64_t rows,
                            float* out_n3, cudaStream_t s);
 
+// The inputs of a view's two camera inverses: K = [[fx, 0, cx], [0, fy, cy],
+// [0, 0, 1]] into k9 and world_view4x4 transposed into wt16 (row-major).
+cudaError_t camera_inputs(float fx, float cx, float fy, float cy, const float* world_view4x4, float* k9,
+                          float* wt16, cudaStream_t s);
+
+// From the camera-to-world matrix c2w16 (row-major 4x4) and world_view4x4:
+// out[9..17] = c2w[:3,:3], out[18..20] = c2w[:3,3], out[21..29] =
+// world_view[:3,:3]^T (out[0..8], the inverse intrinsics, are not touched).
+cudaError_t camera_pack(const float* c2w16, const float* world_view4x4, float* out30, cudaStream_t s);
+
 // keep = float(1 - ratio) and ratio as the caller rounded them.
 cudaError_t standard(int width, int height, const float* color5, const float* aux7,
                      const float* rays3, const float* origin3, const float* rotation9, float keep,

@@ -213,6 +213,8 @@ EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "hs_b200_precise_sh_colors5_f32_v1": (_I32, [_V, _U32, _U32, _V, _V, _V, _V, _U64, _V, *_ERR]),
     "hs_b200_precise_fuse_maps_planar_f32_v1": (_I32, [_V, _V, _V, _V, _V, _V, _U64, *_ERR]),
     "hs_b200_standard_debug_copy_v1": (_I32, [_V, _U64, _V, _V, _V, *_ERR]),
+    "hs_b200_postprocess_camera_f32_v1": (_I32, [_V, _I32, _I32, ctypes.c_double, ctypes.c_double, _V, _V, _V, _V,
+                                                   *_ERR]),
     "hs_b200_pixel_rays_f32_v1": (_I32, [_V, _I32, _I32, _V, _V, _V, _V, *_ERR]),
     "hs_b200_standard_postprocess_f32_v1": (_I32, [_I32, _I32, _V, _V, _V, _V, _V, ctypes.c_double,
                                                    _V, _V, _V, _V, _V, _V, _V, _V, *_ERR]),

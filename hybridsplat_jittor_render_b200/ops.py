@@ -770,6 +770,31 @@ def pixel_rays(width: int, height: int, inverse_intrinsics: torch.Tensor, rotati
     return rays
 
 
+def postprocess_camera_rays(width: int, height: int, fov_x: float, fov_y: float, world_view_transform: torch.Tensor,
+                            *, context: NativeRendererContext, stream: int | None = None,
+                            camera: torch.Tensor | None = None, rays: torch.Tensor | None = None
+                            ) -> dict[str, torch.Tensor]:
+    """postprocess_camera and pixel_rays in one call on `stream` (a raw
+    cudaStream_t; None = the legacy default stream), so that a session can
+    run them beside the raster calls (hs_b200_postprocess_camera_f32_v1).
+    Returns the same matrices as postprocess_camera (views of one 30-float
+    buffer) and the rays."""
+    _check_tensor("world_view_transform", world_view_transform, (4, 4))
+    device = world_view_transform.device
+    f = dict(dtype=torch.float32, device=device)
+    camera = camera if camera is not None else torch.empty(30, **f)
+    rays = rays if rays is not None else torch.empty((height * width, 3), **f)
+    _check_tensor("camera", camera, (30,))
+    _check_tensor("rays", rays, (height * width, 3))
+    error = error_buffer()
+    status = context.library.hs_b200_postprocess_camera_f32_v1(
+        context.handle, int(width), int(height), float(fov_x), float(fov_y), _ptr(world_view_transform.contiguous()),
+        _ptr(camera), _ptr(rays), stream, error, len(error))
+    check_status(status, "hs_b200_postprocess_camera_f32_v1", error)
+    return {"inverse_intrinsics": camera[0:9].view(3, 3), "rotation": camera[9:18].view(3, 3),
+            "origin": camera[18:21], "normal_rotation": camera[21:30].view(3, 3), "rays": rays}
+
+
 STANDARD_MAPS = ("rgb_map", "acc_map", "dpt_map", "norm_map", "surf_norm_map", "dist_map", "spec_map", "rough_map")
 STANDARD_MAP_CHANNELS = (3, 1, 1, 3, 3, 1, 1, 1)
 

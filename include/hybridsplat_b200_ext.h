@@ -252,6 +252,25 @@ HS_API int32_t hs_b200_pixel_rays_f32_v1(
     const float* rotation3x3, float* scratch_n3, float* rays_n3, char* error_text,
     uint64_t error_capacity) HS_NOEXCEPT;
 
+/* The per-view camera terms of the standard postprocess in one call on
+ * `stream` (a cudaStream_t; NULL = legacy default stream), so that a session
+ * can compute them beside the raster calls: the intrinsics built as
+ * depth_to_normal builds them from width, height and the fields of view
+ * (math.py:338-389), their inverse and the inverse of world_view_transform^T
+ * through the two precise_general_inverse computations, and the world-space
+ * pixel rays of hs_b200_pixel_rays_f32_v1. Writes camera30 (device, 30 floats,
+ * row-major): [0..8] the inverse intrinsics, [9..17] the camera-to-world
+ * rotation c2w[:3,:3], [18..20] the origin c2w[:3,3], [21..29] the normal
+ * rotation world_view_transform[:3,:3]^T; and rays_n3 (device, H*W*3). All
+ * bit-identical to ops of the same names on the legacy stream. world_view4x4
+ * is the [4,4] device matrix as the session stores it. Calls on one handle
+ * are ordered among themselves (they share a workspace region); they do not
+ * share it with the other helpers. */
+HS_API int32_t hs_b200_postprocess_camera_f32_v1(
+    HsRasterizerHandle handle, int32_t width, int32_t height, double fov_x, double fov_y,
+    const float* world_view4x4, float* camera30, float* rays_n3, void* stream, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+
 /* The standard session's raw-map postprocess of one view in one pass
  * (postprocess_raster, math.py:426-463, with depth_to_normal): from the raster
  * call's color5[5,H,W] and aux7[7,H,W], the pixel rays of

@@ -208,6 +208,10 @@ def test_prepare_host_empty_and_null(lib):
     ("hs_b200_flashgs_postprocess_f32_v1", (5, 2, *[None] * 13), 1),
     ("hs_b200_pixel_rays_f32_v1", (None, 8, 8, None, None, None, None), 1),
     ("hs_b200_pixel_rays_f32_v1", (None, 0, 8, None, None, None, None), 0),
+    ("hs_b200_postprocess_camera_f32_v1", (None, 8, 8, 1.0, 1.0, None, None, None, None), 1),
+    ("hs_b200_postprocess_camera_f32_v1", (None, 0, 8, 1.0, 1.0, None, None, None, None), 1),
+    ("hs_b200_postprocess_camera_f32_v1", (None, 8, 8, float("nan"), 1.0, None, None, None, None), 1),
+    ("hs_b200_postprocess_camera_f32_v1", (None, 65536, 65536, 1.0, 1.0, None, None, None, None), 3),
 ])
 def test_fused_glue_validation(lib, symbol, args, expected):
     """Argument checks of the fused view-glue and postprocess entry points,
@@ -216,7 +220,8 @@ def test_fused_glue_validation(lib, symbol, args, expected):
     err = ctypes.create_string_buffer(256)
     assert getattr(lib, symbol)(*args, err, len(err)) == expected
     if expected == 3:
-        assert err.value.decode().startswith("precise_sh_to_rgb")
+        prefix = "precise_sh_to_rgb" if "sh_colors5" in symbol else "postprocess_camera"
+        assert err.value.decode().startswith(prefix)
 
 
 def test_prepare_host_threads_bit_identical(lib):

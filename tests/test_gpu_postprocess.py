@@ -79,6 +79,31 @@ def test_camera_matrices_and_rays_match_reference_helpers(contexts, camera):
     assert bits_equal(host(rays), host(reference_rays))
 
 
+@pytest.mark.parametrize("camera", ["generic", "stress_4k", "tiny"])
+def test_camera_entry_on_a_side_stream_matches_the_helpers(contexts, camera):
+    """hs_b200_postprocess_camera_f32_v1 on a side stream: matrices and rays
+    bit-identical to postprocess_camera + pixel_rays on the legacy stream,
+    also for an image under 8 pixels (the cuBLAS path)."""
+    mine = contexts[0]
+    if camera == "tiny":
+        spec = scenes.SceneSpec("tiny", scenes.GroupSpec(1), scenes.GroupSpec(1), 3, 2, 2.5)
+        cam = scenes.generic_camera(spec, 2)
+    else:
+        cam = scenes.generic_camera("standard_1m" if camera == "generic" else camera, 3)
+    w, h, fov_x, fov_y, wv = camera_inputs(cam)
+    m = ops.postprocess_camera(w, h, fov_x, fov_y, wv, context=mine)
+    rays = ops.pixel_rays(w, h, m["inverse_intrinsics"], m["rotation"], context=mine)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    for _ in range(2):  # the second call reuses the entry's workspace region
+        with torch.cuda.stream(side):
+            got = ops.postprocess_camera_rays(w, h, fov_x, fov_y, wv, context=mine, stream=side.cuda_stream)
+        side.synchronize()
+        for name in ("inverse_intrinsics", "rotation", "origin", "normal_rotation"):
+            assert bits_equal(host(got[name].contiguous()), host(m[name])), name
+        assert bits_equal(host(got["rays"]), host(rays))
+
+
 def tf32_halfway_values(rng, count):
     """Values whose low 13 mantissa bits are exactly half a TF32 ulp, with
     even and odd TF32 mantissas and both signs: rounding half away from zero
