@@ -16,11 +16,11 @@
 //   refit      one thread per leaf walks up; the second thread to reach a
 //              node writes both children's boxes into it (64 bytes per node)
 //              and continues;
-//   widen      each binary node's grandchildren (a leaf child stands for
-//              itself) become the four children of a wide node (128 bytes:
-//              one float4 per box coordinate of the four children, then their
-//              references), so a traversal from the root fetches every second
-//              binary level only, four boxes per fetch.
+//   widen      each binary node's two children, the larger internal ones
+//              expanded by surface area until there are four, become the
+//              children of a wide node (128 bytes: one float4 per box
+//              coordinate of the four children, then their references), so a
+//              traversal fetches four boxes per node.
 // Trace (hs_optix_trace_f32_v1; reference optix_backend.cpp:460-617 and the
 // programs of vendor/optix_tracer/forward.cu:219-660): one thread per ray;
 // each trace step is a stack traversal of the wide BVH (children pushed
@@ -272,12 +272,13 @@ __global__ void single_root_kernel(const float4* __restrict__ lo, const float4* 
     nodes[3] = make_float4(CUDART_INF_F, CUDART_INF_F, CUDART_INF_F, 0.0f);
 }
 
-// The wide tree: wide node i holds the grandchildren of binary node i (a
-// child that is a leaf, or empty, stands for itself), so that from the root
-// every second binary level is skipped. One thread per binary node; nodes
-// that the traversal never reaches (odd binary depths) are written too.
-// Empty slots get the box [+inf, +inf], which the slab test rejects, and
-// the reference kNoChild.
+// The wide tree: wide node i holds up to four binary nodes that together
+// cover binary node i's subtree: its two children, then, while a slot is
+// free, the internal one of largest box surface area replaced by its two
+// children (leaves and empty children stand for themselves). One thread per
+// binary node; nodes that the traversal never reaches are written too.
+// Empty slots get the box [+inf, +inf], which the slab test rejects, and the
+// reference kNoChild.
 __global__ void __launch_bounds__(kBuildThreads) widen_kernel(uint32_t internal,
                                                               const float4* __restrict__ binary,
                                                               float4* __restrict__ wide) {
@@ -286,25 +287,36 @@ __global__ void __launch_bounds__(kBuildThreads) widen_kernel(uint32_t internal,
     float lx[4], ly[4], lz[4], hx[4], hy[4], hz[4];
     uint32_t ref[4];
     int k = 0;
+    auto take = [&](const float4* node, int c) {
+        const float4 lo = node[2 * c], hi = node[2 * c + 1];
+        lx[k] = lo.x; ly[k] = lo.y; lz[k] = lo.z;
+        hx[k] = hi.x; hy[k] = hi.y; hz[k] = hi.z;
+        ref[k++] = __float_as_uint(c == 0 ? node[0].w : node[1].w);
+    };
     const float4* node = binary + 4 * static_cast<uint64_t>(i);
-    const float4 q[4] = {node[0], node[1], node[2], node[3]};
-    for (int c = 0; c < 2; ++c) {
-        const float4 lo = q[2 * c], hi = q[2 * c + 1];
-        const uint32_t r = __float_as_uint(c == 0 ? q[0].w : q[1].w);
-        if (r == kNoChild || (r & kLeafBit) != 0u) {
-            lx[k] = lo.x; ly[k] = lo.y; lz[k] = lo.z;
-            hx[k] = hi.x; hy[k] = hi.y; hz[k] = hi.z;
-            ref[k++] = r;
-            continue;
+    take(node, 0);
+    take(node, 1);
+    // greedy: expand the internal child with the largest surface area
+    while (k < 4) {
+        int best = -1;
+        float best_area = -1.0f;
+        for (int j = 0; j < k; ++j) {
+            if (ref[j] == kNoChild || (ref[j] & kLeafBit) != 0u) continue;
+            const float dx = hx[j] - lx[j], dy = hy[j] - ly[j], dz = hz[j] - lz[j];
+            const float area = dx * dy + dy * dz + dz * dx;
+            if (area > best_area) {
+                best_area = area;
+                best = j;
+            }
         }
-        const float4* child = binary + 4 * static_cast<uint64_t>(r);
-        const float4 g[4] = {child[0], child[1], child[2], child[3]};
-        for (int gc = 0; gc < 2; ++gc) {
-            const float4 glo = g[2 * gc], ghi = g[2 * gc + 1];
-            lx[k] = glo.x; ly[k] = glo.y; lz[k] = glo.z;
-            hx[k] = ghi.x; hy[k] = ghi.y; hz[k] = ghi.z;
-            ref[k++] = __float_as_uint(gc == 0 ? g[0].w : g[1].w);
-        }
+        if (best < 0) break;
+        const float4* child = binary + 4 * static_cast<uint64_t>(ref[best]);
+        // the expanded child's slot takes its first child, a new slot its second
+        const int last = k;
+        take(child, 1);
+        k = best;
+        take(child, 0);
+        k = last + 1;
     }
     for (; k < 4; ++k) {
         lx[k] = ly[k] = lz[k] = hx[k] = hy[k] = hz[k] = CUDART_INF_F;

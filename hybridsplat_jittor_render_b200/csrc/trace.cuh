@@ -36,9 +36,9 @@ constexpr float kTThreshold = 0.0001f;
 constexpr int kMidChannels = 16;           // MID_CHANNELS per trace depth
 constexpr uint32_t kLeafBit = 0x80000000u; // child reference: leaf slot
 constexpr uint32_t kNoChild = 0xffffffffu; // empty child slot of a wide node
-// Traversal stack: the binary tree is at most 64 internal nodes deep, so a
-// root-to-leaf path crosses at most 32 wide nodes, each leaving at most 3
-// siblings on the stack, plus the 4 children of the last one.
+// Traversal stack: every entry left on it is the other child of a binary
+// node on the current root-to-node path of the binary tree, which is at most
+// 64 internal nodes deep; plus the 4 children of the node being expanded.
 constexpr int kStackDepth = 104;
 constexpr int kMaxTraceSteps = 4096;    // trace steps (16 hits each) per segment
 
