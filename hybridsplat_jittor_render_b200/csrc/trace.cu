@@ -502,8 +502,8 @@ __device__ uint32_t collect(const Bvh& bvh, const float3& o, const float3& inv, 
         order2(0, 2);
         order2(1, 3);
         order2(1, 2);
-        // Never taken: at most 3 entries per wide level above this node (32
-        // levels) plus these four.
+        // Never taken: at most 3 entries per wide level above this node (at
+        // most 64 levels) plus these four.
         if (sp + 4 > kStackDepth) break;
         // farthest first, so that the nearest is popped next
         for (int k = 3; k >= 0; --k) {

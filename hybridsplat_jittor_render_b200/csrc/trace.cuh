@@ -36,10 +36,11 @@ constexpr float kTThreshold = 0.0001f;
 constexpr int kMidChannels = 16;           // MID_CHANNELS per trace depth
 constexpr uint32_t kLeafBit = 0x80000000u; // child reference: leaf slot
 constexpr uint32_t kNoChild = 0xffffffffu; // empty child slot of a wide node
-// Traversal stack: every entry left on it is the other child of a binary
-// node on the current root-to-node path of the binary tree, which is at most
-// 64 internal nodes deep; plus the 4 children of the node being expanded.
-constexpr int kStackDepth = 104;
+// Traversal stack: a wide node's children lie at least one binary level below
+// it and the binary tree is at most 64 internal nodes deep, so the path of
+// wide nodes being traversed is at most 64 long; each leaves at most 3
+// siblings on the stack, plus the 4 children of the node being expanded.
+constexpr int kStackDepth = 3 * 64 + 4;
 constexpr int kMaxTraceSteps = 4096;    // trace steps (16 hits each) per segment
 
 // BVH over the scene triangles, 4 children per node (the binary radix tree
