@@ -64,6 +64,7 @@ SOURCES = [
     ("standard_noalloc.cu", "cuda", []),
     ("sort.cu", "cuda", []),
     ("trace.cu", "cuda", []),
+    ("view.cu", "cuda", []),
     ("precise.cu", "cuda", ["--fmad=false"]),
     ("precise_exp.cu", "cuda", []),
     ("postprocess.cu", "cuda", []),

@@ -25,6 +25,7 @@
 
 #include "context.h"
 #include "postprocess.h"
+#include "view.h"
 #include "precise.h"
 
 namespace hs {
@@ -1458,6 +1459,91 @@ int32_t hs_rasterizer_precise_general_inverse_f32_v2(HsRasterizerHandle handle,
     });
 }
 
+namespace {
+
+// The view's camera terms of the standard postprocess on `stream`
+// (hs_b200_postprocess_camera_f32_v1 after its argument checks; the caller
+// holds h's mutex on h's device).
+int32_t camera_terms(HsRasterizerContext* h, int32_t width, int32_t height, double fov_x, double fov_y,
+                     const float* world_view4x4, float* camera30, float* rays_n3, cudaStream_t stream,
+                     char* error_text, uint64_t error_capacity) {
+    const uint64_t count = static_cast<uint64_t>(width) * static_cast<uint64_t>(height);
+    // The intrinsics as depth_to_normal builds them (math.py:338-389):
+    // focal = float32(length) / float32(2 tan(float32(fov) / 2)) with the
+    // tangent in double, principal point float32(length) / 2.
+    auto focal = [](int length, double fov) {
+        const float half = static_cast<float>(fov) / 2.0f;
+        const float denominator = static_cast<float>(2.0 * std::tan(static_cast<double>(half)));
+        return static_cast<float>(length) / denominator;
+    };
+    const float fx = focal(width, fov_x), fy = focal(height, fov_y);
+    const float cx = static_cast<float>(width) / 2.0f, cy = static_cast<float>(height) / 2.0f;
+    const cudaStream_t s = stream;
+    float* k9 = reinterpret_cast<float*>(math_at(h, kMathViewK));
+    float* wt16 = reinterpret_cast<float*>(math_at(h, kMathViewWt));
+    float* c2w16 = reinterpret_cast<float*>(math_at(h, kMathViewC2w));
+    // the region is this entry's own: order after the previous call's use of it
+    cudaError_t ce = cudaSuccess;
+    if (h->view_camera_event == nullptr) {
+        ce = cudaEventCreateWithFlags(&h->view_camera_event, cudaEventDisableTiming);
+    } else {
+        ce = cudaStreamWaitEvent(s, h->view_camera_event, 0);
+    }
+    if (ce == cudaSuccess) ce = hs::post::camera_inputs(fx, cx, fy, cy, world_view4x4, k9, wt16, s);
+    if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera inputs", error_text, error_capacity);
+    // the two inverses of precise_general_inverse, on `stream`
+    cublasStatus_t bs = cublasSetStream(h->math_tf32_blas, s);
+    cusolverStatus_t ss = cusolverDnSetStream(h->math_solver, s);
+    int32_t status = HS_STATUS_OK;
+    if (bs != CUBLAS_STATUS_SUCCESS) {
+        status = cublas_failure(bs, "postprocess_camera cublasSetStream", error_text, error_capacity);
+    } else if (ss != CUSOLVER_STATUS_SUCCESS) {
+        status = cusolver_failure(ss, "postprocess_camera cusolverDnSetStream", error_text, error_capacity);
+    } else {
+        const InverseBuffers view = inverse_buffers(h, kMathViewOffset);
+        status = general_inverse(h, k9, 3, view, camera30, s, error_text, error_capacity);
+        if (status == HS_STATUS_OK)
+            status = general_inverse(h, wt16, 4, view, c2w16, s, error_text, error_capacity);
+        // images under kMmaMinRows pixels: the reference's cuBLAS products on this stream
+        if (status == HS_STATUS_OK && count < hs::post::kMmaMinRows) {
+            float* scratch = reinterpret_cast<float*>(math_at(h, kMathViewRays));
+            ce = hs::post::camera_pack(c2w16, world_view4x4, camera30, s);
+            if (ce == cudaSuccess) ce = hs::post::pixel_grid(width, height, rays_n3, s);
+            const float alpha = 1.0f, beta = 0.0f;
+            if (ce != cudaSuccess) {
+                status = cuda_failure(ce, "postprocess_camera rays", error_text, error_capacity);
+            } else {
+                bs = cublasSgemm(h->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3, static_cast<int>(count),
+                                 3, &alpha, camera30, 3, rays_n3, 3, &beta, scratch, 3);
+                if (bs == CUBLAS_STATUS_SUCCESS)
+                    bs = cublasSgemm(h->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3, static_cast<int>(count),
+                                     3, &alpha, camera30 + 9, 3, scratch, 3, &beta, rays_n3, 3);
+                if (bs != CUBLAS_STATUS_SUCCESS)
+                    status = cublas_failure(bs, "postprocess_camera cublasSgemm", error_text, error_capacity);
+            }
+        }
+    }
+    // the handles go back to the legacy default stream of the other helpers
+    const cublasStatus_t rb = cublasSetStream(h->math_tf32_blas, nullptr);
+    const cusolverStatus_t rs = cusolverDnSetStream(h->math_solver, nullptr);
+    if (status != HS_STATUS_OK) return status;
+    if (rb != CUBLAS_STATUS_SUCCESS)
+        return cublas_failure(rb, "postprocess_camera cublasSetStream", error_text, error_capacity);
+    if (rs != CUSOLVER_STATUS_SUCCESS)
+        return cusolver_failure(rs, "postprocess_camera cusolverDnSetStream", error_text, error_capacity);
+    if (count >= hs::post::kMmaMinRows) {
+        ce = hs::post::camera_pack(c2w16, world_view4x4, camera30, s);
+        if (ce == cudaSuccess) ce = hs::post::pixel_rays(width, height, camera30, camera30 + 9, rays_n3, s);
+        if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera rays", error_text, error_capacity);
+    }
+    ce = cudaEventRecord(h->view_camera_event, s);
+    if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera event", error_text, error_capacity);
+    h->math_matmul_calls += 2;
+    return HS_STATUS_OK;
+}
+
+}  // namespace
+
 int32_t hs_b200_postprocess_camera_f32_v1(HsRasterizerHandle handle, int32_t width, int32_t height,
                                           double fov_x, double fov_y, const float* world_view4x4,
                                           float* camera30, float* rays_n3, void* stream, char* error_text,
@@ -1491,76 +1577,9 @@ int32_t hs_b200_postprocess_camera_f32_v1(HsRasterizerHandle handle, int32_t wid
             return fail(HS_STATUS_INTERNAL_ERROR, "postprocess_camera math context is not initialized",
                         error_text, error_capacity);
         }
-        // The intrinsics as depth_to_normal builds them (math.py:338-389):
-        // focal = float32(length) / float32(2 tan(float32(fov) / 2)) with the
-        // tangent in double, principal point float32(length) / 2.
-        auto focal = [](int length, double fov) {
-            const float half = static_cast<float>(fov) / 2.0f;
-            const float denominator = static_cast<float>(2.0 * std::tan(static_cast<double>(half)));
-            return static_cast<float>(length) / denominator;
-        };
-        const float fx = focal(width, fov_x), fy = focal(height, fov_y);
-        const float cx = static_cast<float>(width) / 2.0f, cy = static_cast<float>(height) / 2.0f;
-        const cudaStream_t s = static_cast<cudaStream_t>(stream);
-        float* k9 = reinterpret_cast<float*>(math_at(handle, kMathViewK));
-        float* wt16 = reinterpret_cast<float*>(math_at(handle, kMathViewWt));
-        float* c2w16 = reinterpret_cast<float*>(math_at(handle, kMathViewC2w));
-        // the region is this entry's own: order after the previous call's use of it
-        cudaError_t ce = cudaSuccess;
-        if (handle->view_camera_event == nullptr) {
-            ce = cudaEventCreateWithFlags(&handle->view_camera_event, cudaEventDisableTiming);
-        } else {
-            ce = cudaStreamWaitEvent(s, handle->view_camera_event, 0);
-        }
-        if (ce == cudaSuccess) ce = hs::post::camera_inputs(fx, cx, fy, cy, world_view4x4, k9, wt16, s);
-        if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera inputs", error_text, error_capacity);
-        // the two inverses of precise_general_inverse, on `stream`
-        cublasStatus_t bs = cublasSetStream(handle->math_tf32_blas, s);
-        cusolverStatus_t ss = cusolverDnSetStream(handle->math_solver, s);
-        int32_t status = HS_STATUS_OK;
-        if (bs != CUBLAS_STATUS_SUCCESS) {
-            status = cublas_failure(bs, "postprocess_camera cublasSetStream", error_text, error_capacity);
-        } else if (ss != CUSOLVER_STATUS_SUCCESS) {
-            status = cusolver_failure(ss, "postprocess_camera cusolverDnSetStream", error_text, error_capacity);
-        } else {
-            const InverseBuffers view = inverse_buffers(handle, kMathViewOffset);
-            status = general_inverse(handle, k9, 3, view, camera30, s, error_text, error_capacity);
-            if (status == HS_STATUS_OK)
-                status = general_inverse(handle, wt16, 4, view, c2w16, s, error_text, error_capacity);
-            // images under kMmaMinRows pixels: the reference's cuBLAS products on this stream
-            if (status == HS_STATUS_OK && count < hs::post::kMmaMinRows) {
-                float* scratch = reinterpret_cast<float*>(math_at(handle, kMathViewRays));
-                ce = hs::post::camera_pack(c2w16, world_view4x4, camera30, s);
-                if (ce == cudaSuccess) ce = hs::post::pixel_grid(width, height, rays_n3, s);
-                const float alpha = 1.0f, beta = 0.0f;
-                if (ce != cudaSuccess) {
-                    status = cuda_failure(ce, "postprocess_camera rays", error_text, error_capacity);
-                } else {
-                    bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3, static_cast<int>(count),
-                                     3, &alpha, camera30, 3, rays_n3, 3, &beta, scratch, 3);
-                    if (bs == CUBLAS_STATUS_SUCCESS)
-                        bs = cublasSgemm(handle->math_tf32_blas, CUBLAS_OP_T, CUBLAS_OP_N, 3, static_cast<int>(count),
-                                         3, &alpha, camera30 + 9, 3, scratch, 3, &beta, rays_n3, 3);
-                    if (bs != CUBLAS_STATUS_SUCCESS)
-                        status = cublas_failure(bs, "postprocess_camera cublasSgemm", error_text, error_capacity);
-                }
-            }
-        }
-        // the handles go back to the legacy default stream of the other helpers
-        const cublasStatus_t rb = cublasSetStream(handle->math_tf32_blas, nullptr);
-        const cusolverStatus_t rs = cusolverDnSetStream(handle->math_solver, nullptr);
+        const int32_t status = camera_terms(handle, width, height, fov_x, fov_y, world_view4x4, camera30, rays_n3,
+                                            static_cast<cudaStream_t>(stream), error_text, error_capacity);
         if (status != HS_STATUS_OK) return status;
-        if (rb != CUBLAS_STATUS_SUCCESS)
-            return cublas_failure(rb, "postprocess_camera cublasSetStream", error_text, error_capacity);
-        if (rs != CUSOLVER_STATUS_SUCCESS)
-            return cusolver_failure(rs, "postprocess_camera cusolverDnSetStream", error_text, error_capacity);
-        if (count >= hs::post::kMmaMinRows) {
-            ce = hs::post::camera_pack(c2w16, world_view4x4, camera30, s);
-            if (ce == cudaSuccess) ce = hs::post::pixel_rays(width, height, camera30, camera30 + 9, rays_n3, s);
-            if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera rays", error_text, error_capacity);
-        }
-        ce = cudaEventRecord(handle->view_camera_event, s);
-        if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera event", error_text, error_capacity);
         handle->math_matmul_calls += 2;
         const cudaError_t trailing = cudaGetLastError();
         if (trailing != cudaSuccess)
@@ -1833,6 +1852,222 @@ int32_t hs_b200_rasterizer_forward_rows_f32_v1(
     a.tile_row_begin = tile_row_begin;
     a.tile_row_end = tile_row_end == UINT32_MAX ? UINT32_MAX - 1 : tile_row_end;
     return rasterizer_entry(a, error_text, error_capacity);
+}
+
+int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text,
+                                 uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (v == nullptr || v->struct_size < sizeof(HsB200StandardViewV2)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "standard view is null or its struct_size is too small",
+                        error_text, error_capacity);
+        }
+        // the two raster calls, checked as the concurrent entry checks them
+        auto raster_args = [&](const HsB200StandardGroupV2& g, HsRasterizerHandle handle) {
+            HsB200RasterizerCallV2 a{};
+            a.handle = handle;
+            a.point_count = g.count;
+            a.background5 = g.background5;
+            a.width = v->width;
+            a.height = v->height;
+            a.means3d = g.means3d;
+            a.colors5 = g.colors5;
+            a.opacities = g.opacities;
+            a.scales2 = g.scales2;
+            a.scale_modifier = 1.0f;
+            a.prefiltered = 0;
+            a.rotations4 = g.rotations4;
+            a.viewmatrix4x4 = v->viewmatrix4x4;
+            a.projmatrix4x4 = v->projmatrix4x4;
+            a.camera_position3 = v->camera_position3;
+            a.tan_fovx = v->tan_fovx;
+            a.tan_fovy = v->tan_fovy;
+            a.output_color5 = g.output_color5;
+            a.output_aux7 = g.output_aux7;
+            a.output_weight = g.output_weight;
+            a.output_radii = g.output_radii;
+            a.output_rendered = g.output_rendered;
+            a.tile_row_begin = 0;
+            a.tile_row_end = UINT32_MAX;
+            return a;
+        };
+        hs::StandardCall calls[2];
+        HsRasterizerContext* contexts[2] = {v->base_handle, v->reflection_handle};
+        const HsB200RasterizerCallV2 base_args = raster_args(v->base, v->base_handle);
+        const HsB200RasterizerCallV2 refl_args = raster_args(v->reflection, v->reflection_handle);
+        int32_t cs = check_rasterizer(base_args, &calls[0], error_text, error_capacity);
+        if (cs == HS_STATUS_OK) cs = check_rasterizer(refl_args, &calls[1], error_text, error_capacity);
+        if (cs != HS_STATUS_OK) return cs;
+        if (contexts[0] == contexts[1]) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "standard view needs two distinct handles", error_text,
+                        error_capacity);
+        }
+        const uint64_t nb = v->base.count, nr = v->reflection.count;
+        if (v->sh_coefficients == 0 || v->sh_coefficients > 16 || v->sh_degree > 3 ||
+            v->sh_coefficients < (v->sh_degree + 1) * (v->sh_degree + 1)) {
+            return fail(HS_STATUS_RANGE_ERROR, "standard view SH dimensions are invalid", error_text,
+                        error_capacity);
+        }
+        if ((nb != 0 && (v->base_sh == nullptr || v->base.specular == nullptr || v->base.roughness == nullptr)) ||
+            (nr != 0 && (v->reflection_rotation_raw4 == nullptr || v->reflection_rotation9 == nullptr ||
+                         v->reflection_normal3 == nullptr || v->reflection_rays36 == nullptr ||
+                         v->reflection_ray_origins3 == nullptr || v->reflection_ray_directions3 == nullptr ||
+                         v->reflection.specular == nullptr || v->reflection.roughness == nullptr ||
+                         (v->trace == 0 && v->reflection_rgb3 == nullptr))) ||
+            v->fused_rgb3 == nullptr || v->diffuse_rgb3 == nullptr || v->reflection_rgb_map3 == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "standard view received a null required buffer", error_text,
+                        error_capacity);
+        }
+        if (v->trace != 0 && v->trace != 1) {
+            return fail(HS_STATUS_RANGE_ERROR, "standard view trace must be 0 or 1", error_text, error_capacity);
+        }
+        if (v->trace == 1) {
+            if (v->trace_coefficients == 0 || v->trace_coefficients > 16 || v->trace_degree > 3 ||
+                v->trace_coefficients < (v->trace_degree + 1) * (v->trace_degree + 1) ||
+                (v->use_others != 0 && v->use_others != 1) || v->max_trace_depth < 0 || v->max_trace_depth > 1 ||
+                !std::isfinite(v->specular_threshold) || nr > UINT32_MAX) {
+                return fail(HS_STATUS_RANGE_ERROR, "OptiX trace dimensions or scalars are invalid", error_text,
+                            error_capacity);
+            }
+            if (nr != 0 && (v->trace_background3 == nullptr || v->reflection_shs == nullptr ||
+                            v->reflection_others2 == nullptr || v->trace_rgb3 == nullptr ||
+                            v->trace_depth1 == nullptr || v->trace_acc1 == nullptr || v->trace_normal3 == nullptr ||
+                            v->trace_dist1 == nullptr || v->trace_aux2 == nullptr || v->trace_mid32 == nullptr ||
+                            v->trace_wet1 == nullptr)) {
+                return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX trace received a null non-empty buffer", error_text,
+                            error_capacity);
+            }
+        }
+        const bool post = v->camera30 != nullptr;
+        const uint64_t pixels = static_cast<uint64_t>(v->width) * static_cast<uint64_t>(v->height);
+        if (post) {
+            if (!std::isfinite(v->fov_x) || !std::isfinite(v->fov_y) || !std::isfinite(v->depth_ratio)) {
+                return fail(HS_STATUS_INVALID_ARGUMENT, "standard view postprocess scalars must be finite",
+                            error_text, error_capacity);
+            }
+            if (pixels > static_cast<uint64_t>(INT_MAX)) {
+                return fail(HS_STATUS_RANGE_ERROR, "postprocess_camera pixel count exceeds cuBLAS int range",
+                            error_text, error_capacity);
+            }
+            if (v->pixel_rays3 == nullptr || v->rgb_map3 == nullptr || v->acc_map == nullptr ||
+                v->dpt_map == nullptr || v->norm_map3 == nullptr || v->surf_norm_map3 == nullptr ||
+                v->dist_map == nullptr || v->spec_map == nullptr || v->rough_map == nullptr) {
+                return fail(HS_STATUS_INVALID_ARGUMENT, "standard view postprocess received a null buffer",
+                            error_text, error_capacity);
+            }
+        }
+        // every argument is checked; only now are the handles read
+        if (contexts[0]->device != contexts[1]->device) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "standard view handles must be of one device", error_text,
+                        error_capacity);
+        }
+        const int32_t ds = select_device(contexts[0], error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        HsRasterizerContext* first = contexts[0] < contexts[1] ? contexts[0] : contexts[1];
+        HsRasterizerContext* second = contexts[0] < contexts[1] ? contexts[1] : contexts[0];
+        std::lock_guard<std::mutex> lock_first(first->mutex);
+        std::lock_guard<std::mutex> lock_second(second->mutex);
+        HsRasterizerContext* base = contexts[0];
+        HsRasterizerContext* refl = contexts[1];
+        if (post && (base->math_workspace == nullptr || base->math_solver == nullptr ||
+                     base->math_tf32_blas == nullptr)) {
+            return fail(HS_STATUS_INTERNAL_ERROR, "postprocess_camera math context is not initialized",
+                        error_text, error_capacity);
+        }
+        if (v->trace == 1 && refl->tr_triangles == 0) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX scene is not built", error_text, error_capacity);
+        }
+        const cudaStream_t s = static_cast<cudaStream_t>(v->stream);
+        cudaError_t e = cudaSuccess;
+        // postprocess camera terms: only the camera, so beside everything else
+        if (post) {
+            e = hs::ensure_post_stream(base);
+            if (e == cudaSuccess) e = cudaEventRecord(base->post_fork_event, s);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(base->post_stream, base->post_fork_event, 0);
+            if (e != cudaSuccess) return cuda_failure(e, "standard view fork", error_text, error_capacity);
+            const int32_t ps = camera_terms(base, v->width, v->height, v->fov_x, v->fov_y, v->viewmatrix4x4,
+                                            v->camera30, v->pixel_rays3, base->post_stream, error_text,
+                                            error_capacity);
+            if (ps != HS_STATUS_OK) return ps;
+            e = cudaEventRecord(base->post_done_event, base->post_stream);
+            if (e != cudaSuccess) return cuda_failure(e, "standard view join", error_text, error_capacity);
+        }
+        // base colours, reflection preparation, trace, reflection colours
+        e = hs::precise::sh_colors5(v->base_sh, v->sh_coefficients, v->sh_degree, v->base.means3d,
+                                    v->camera_position3, v->base.specular, v->base.roughness, nb,
+                                    v->base.colors5, s);
+        if (e == cudaSuccess) e = hs::precise::reflection_prefix(v->reflection_rotation_raw4, nr,
+                                                                 v->reflection_rotation9, s);
+        if (e == cudaSuccess) e = hs::view::normal_column(v->reflection_rotation9, nr, v->reflection_normal3, s);
+        if (e == cudaSuccess) e = hs::precise::reflection_suffix(v->reflection.means3d, v->camera_position3,
+                                                                 v->reflection_normal3, nr, v->reflection_rays36, s);
+        if (e == cudaSuccess) e = hs::view::split_rays(v->reflection_rays36, nr, v->reflection_ray_origins3,
+                                                       v->reflection_ray_directions3, s);
+        if (e != cudaSuccess) return cuda_failure(e, "standard view preparation", error_text, error_capacity);
+        const float* reflection_rgb = v->reflection_rgb3;
+        if (v->trace == 1 && nr != 0) {
+            hs::TraceCall t;
+            t.ray_count = nr;
+            t.ray_origins3 = v->reflection_ray_origins3;
+            t.ray_directions3 = v->reflection_ray_directions3;
+            t.background3 = v->trace_background3;
+            t.means3d = v->reflection.means3d;
+            t.shs_m3 = v->reflection_shs;
+            t.coefficient_count = v->trace_coefficients;
+            t.degree = v->trace_degree;
+            t.others2 = v->reflection_others2;
+            t.opacities = v->reflection.opacities;
+            t.scales2 = v->reflection.scales2;
+            t.scale_modifier = 1.0f;
+            t.rotations4 = v->reflection.rotations4;
+            t.viewmatrix4x4 = v->viewmatrix4x4;
+            t.projmatrix4x4 = v->projmatrix4x4;
+            t.camera_position3 = v->camera_position3;
+            t.start_from_first = 0;
+            t.max_trace_depth = v->max_trace_depth;
+            t.specular_threshold = v->specular_threshold;
+            t.use_others = v->use_others;
+            t.output_rgb3 = v->trace_rgb3;
+            t.output_depth1 = v->trace_depth1;
+            t.output_acc1 = v->trace_acc1;
+            t.output_normal3 = v->trace_normal3;
+            t.output_dist1 = v->trace_dist1;
+            t.output_aux2 = v->trace_aux2;
+            t.output_mid32 = v->trace_mid32;
+            t.output_wet1 = v->trace_wet1;
+            t.stream = s;
+            e = hs::trace_rays(refl, t);
+            if (e != cudaSuccess) return cuda_failure(e, "reflection trace", error_text, error_capacity);
+            reflection_rgb = v->trace_rgb3;
+        }
+        e = hs::view::colors5(reflection_rgb, v->reflection.specular, v->reflection.roughness, nr,
+                              v->reflection.colors5, s);
+        if (e != cudaSuccess) return cuda_failure(e, "standard view colours", error_text, error_capacity);
+        // both raster calls, concurrently
+        e = hs::standard_forward_many(contexts, calls, 2, s);
+        if (e != cudaSuccess) return cuda_failure(e, "concurrent five-channel rasterizer forward", error_text,
+                                                  error_capacity);
+        // fusion from the colour planes (renderer.py:326, math.py:301-311)
+        e = hs::precise::fuse_maps_planar(v->base.output_color5, v->reflection.output_color5,
+                                          v->base.output_color5 + 3 * pixels, v->diffuse_rgb3, v->fused_rgb3,
+                                          v->reflection_rgb_map3, pixels, s);
+        if (e != cudaSuccess) return cuda_failure(e, "standard view fusion", error_text, error_capacity);
+        if (post) {
+            e = cudaStreamWaitEvent(s, base->post_done_event, 0);
+            if (e != cudaSuccess) return cuda_failure(e, "standard view join", error_text, error_capacity);
+            // (1 - ratio) and ratio as float32 scalars of a double ratio (math.py:440-442)
+            const float keep = static_cast<float>(1.0 - v->depth_ratio);
+            const float ratio = static_cast<float>(v->depth_ratio);
+            const hs::post::StandardMaps maps{v->rgb_map3, v->acc_map, v->dpt_map, v->norm_map3,
+                                             v->surf_norm_map3, v->dist_map, v->spec_map, v->rough_map};
+            e = hs::post::standard(v->width, v->height, v->base.output_color5, v->base.output_aux7, v->pixel_rays3,
+                                   v->camera30 + 18, v->camera30 + 21, keep, ratio, maps, s);
+            if (e != cudaSuccess) return cuda_failure(e, "standard view postprocess", error_text, error_capacity);
+        }
+        const cudaError_t trailing = cudaGetLastError();
+        if (trailing != cudaSuccess)
+            return cuda_failure(trailing, "standard view execution", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
 }
 
 int32_t hs_b200_flashgs_forward_many_v2(const HsB200FlashgsCallV2* calls, uint32_t call_count,

@@ -85,6 +85,8 @@ cudaError_t stage_timing_read(StageTimer& timer, double out_ms[3], uint64_t* cal
 cudaError_t ensure_device_error(HsRasterizerContext* context);
 // Creates context->side_stream, side_event and fork_event on first use.
 cudaError_t ensure_side_stream(HsRasterizerContext* context);
+// The stream and events of the per-view entry's postprocess camera terms.
+cudaError_t ensure_post_stream(HsRasterizerContext* context);
 void destroy_side_stream(HsRasterizerContext* context);
 void stage_timing_destroy(StageTimer& timer);
 
@@ -171,6 +173,9 @@ struct HsRasterizerContext {
     // non-blocking stream, ordered against the caller's stream by events.
     cudaStream_t side_stream = nullptr;
     cudaEvent_t side_event = nullptr;  // phase marks on side_stream
+    cudaStream_t post_stream = nullptr;      // the per-view entry's postprocess camera terms
+    cudaEvent_t post_fork_event = nullptr;   // recorded on the view's stream before them
+    cudaEvent_t post_done_event = nullptr;   // recorded on post_stream after them
     cudaEvent_t fork_event = nullptr;  // recorded on the caller's stream
 };
 

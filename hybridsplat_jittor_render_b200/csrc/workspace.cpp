@@ -121,13 +121,30 @@ cudaError_t ensure_side_stream(HsRasterizerContext* context) {
     return st;
 }
 
+cudaError_t ensure_post_stream(HsRasterizerContext* context) {
+    cudaError_t st = cudaSuccess;
+    if (context->post_stream == nullptr)
+        st = cudaStreamCreateWithFlags(&context->post_stream, cudaStreamNonBlocking);
+    if (st == cudaSuccess && context->post_fork_event == nullptr)
+        st = cudaEventCreateWithFlags(&context->post_fork_event, cudaEventDisableTiming);
+    if (st == cudaSuccess && context->post_done_event == nullptr)
+        st = cudaEventCreateWithFlags(&context->post_done_event, cudaEventDisableTiming);
+    return st;
+}
+
 void destroy_side_stream(HsRasterizerContext* context) {
     if (context->side_stream != nullptr) cudaStreamDestroy(context->side_stream);
     if (context->side_event != nullptr) cudaEventDestroy(context->side_event);
     if (context->fork_event != nullptr) cudaEventDestroy(context->fork_event);
+    if (context->post_stream != nullptr) cudaStreamDestroy(context->post_stream);
+    if (context->post_fork_event != nullptr) cudaEventDestroy(context->post_fork_event);
+    if (context->post_done_event != nullptr) cudaEventDestroy(context->post_done_event);
     context->side_stream = nullptr;
     context->side_event = nullptr;
     context->fork_event = nullptr;
+    context->post_stream = nullptr;
+    context->post_fork_event = nullptr;
+    context->post_done_event = nullptr;
 }
 
 void stage_timing_destroy(StageTimer& timer) {

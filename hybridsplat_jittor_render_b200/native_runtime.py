@@ -209,6 +209,44 @@ class RasterizerCallV2(ctypes.Structure):
     ]
 
 
+class StandardGroupV2(ctypes.Structure):
+    """HsB200StandardGroupV2 (include/hybridsplat_b200_ext.h)."""
+    _fields_ = [
+        ("count", ctypes.c_uint64), ("means3d", ctypes.c_void_p), ("opacities", ctypes.c_void_p),
+        ("scales2", ctypes.c_void_p), ("rotations4", ctypes.c_void_p), ("specular", ctypes.c_void_p),
+        ("roughness", ctypes.c_void_p), ("background5", ctypes.c_void_p), ("colors5", ctypes.c_void_p),
+        ("output_color5", ctypes.c_void_p), ("output_aux7", ctypes.c_void_p), ("output_weight", ctypes.c_void_p),
+        ("output_radii", ctypes.c_void_p), ("output_rendered", ctypes.c_void_p),
+    ]
+
+
+class StandardViewV2(ctypes.Structure):
+    """HsB200StandardViewV2 (include/hybridsplat_b200_ext.h)."""
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("base_handle", ctypes.c_void_p), ("reflection_handle", ctypes.c_void_p),
+        ("width", ctypes.c_int32), ("height", ctypes.c_int32), ("tan_fovx", ctypes.c_float),
+        ("tan_fovy", ctypes.c_float), ("fov_x", ctypes.c_double), ("fov_y", ctypes.c_double),
+        ("viewmatrix4x4", ctypes.c_void_p), ("projmatrix4x4", ctypes.c_void_p),
+        ("camera_position3", ctypes.c_void_p), ("base", StandardGroupV2), ("reflection", StandardGroupV2),
+        ("base_sh", ctypes.c_void_p), ("sh_coefficients", ctypes.c_uint32), ("sh_degree", ctypes.c_uint32),
+        ("reflection_rotation_raw4", ctypes.c_void_p), ("reflection_rotation9", ctypes.c_void_p),
+        ("reflection_normal3", ctypes.c_void_p), ("reflection_rays36", ctypes.c_void_p),
+        ("reflection_ray_origins3", ctypes.c_void_p), ("reflection_ray_directions3", ctypes.c_void_p),
+        ("reflection_rgb3", ctypes.c_void_p), ("trace", ctypes.c_int32), ("trace_background3", ctypes.c_void_p),
+        ("reflection_shs", ctypes.c_void_p), ("trace_coefficients", ctypes.c_uint32),
+        ("trace_degree", ctypes.c_uint32), ("reflection_others2", ctypes.c_void_p), ("use_others", ctypes.c_int32),
+        ("max_trace_depth", ctypes.c_int32), ("specular_threshold", ctypes.c_float),
+        ("trace_rgb3", ctypes.c_void_p), ("trace_depth1", ctypes.c_void_p), ("trace_acc1", ctypes.c_void_p),
+        ("trace_normal3", ctypes.c_void_p), ("trace_dist1", ctypes.c_void_p), ("trace_aux2", ctypes.c_void_p),
+        ("trace_mid32", ctypes.c_void_p), ("trace_wet1", ctypes.c_void_p), ("fused_rgb3", ctypes.c_void_p),
+        ("diffuse_rgb3", ctypes.c_void_p), ("reflection_rgb_map3", ctypes.c_void_p),
+        ("depth_ratio", ctypes.c_double), ("camera30", ctypes.c_void_p), ("pixel_rays3", ctypes.c_void_p),
+        ("rgb_map3", ctypes.c_void_p), ("acc_map", ctypes.c_void_p), ("dpt_map", ctypes.c_void_p),
+        ("norm_map3", ctypes.c_void_p), ("surf_norm_map3", ctypes.c_void_p), ("dist_map", ctypes.c_void_p),
+        ("spec_map", ctypes.c_void_p), ("rough_map", ctypes.c_void_p), ("stream", ctypes.c_void_p),
+    ]
+
+
 EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "hs_b200_precise_sh_colors5_f32_v1": (_I32, [_V, _U32, _U32, _V, _V, _V, _V, _U64, _V, *_ERR]),
     "hs_b200_precise_fuse_maps_planar_f32_v1": (_I32, [_V, _V, _V, _V, _V, _V, _U64, *_ERR]),
@@ -222,6 +260,7 @@ EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
                                                   _V, _V, _V, *_ERR]),
     "hs_b200_flashgs_forward_many_v2": (_I32, [ctypes.POINTER(FlashgsCallV2), _U32, _V, *_ERR]),
     "hs_b200_rasterizer_forward_many_v2": (_I32, [ctypes.POINTER(RasterizerCallV2), _U32, _V, *_ERR]),
+    "hs_b200_standard_view_v2": (_I32, [ctypes.POINTER(StandardViewV2), *_ERR]),
     "hs_b200_test_stall_lookback_v1": (_I32, [_V, _U32, *_ERR]),
     "hs_b200_comm_unique_id_v1": (_I32, [_V, *_ERR]),
     "hs_b200_comm_create_v1": (_I32, [_I32, _I32, _I32, _V, ctypes.c_double, ctypes.POINTER(ctypes.c_void_p),

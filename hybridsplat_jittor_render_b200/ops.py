@@ -836,3 +836,149 @@ def flashgs_postprocess(raster: FlashgsOutputs, normal_rotation: torch.Tensor, *
                  _ptr(raster.normal.contiguous()), _ptr(normal_rotation.contiguous()),
                  *[_ptr(maps[n]) for n in names])
     return maps
+
+
+# ---------------------------------------------------------------- one view
+
+
+class StandardViewOutputs(NamedTuple):
+    """Everything standard_view writes: both raster calls' outputs, the
+    colours they took, the reflection preparation, the trace (when traced),
+    the fused maps and, with the postprocess, its camera terms and maps."""
+    base: RasterizerOutputs
+    reflection: RasterizerOutputs
+    base_colors: torch.Tensor
+    reflection_colors: torch.Tensor
+    reflection_rotation: torch.Tensor
+    reflection_normal: torch.Tensor
+    reflection_rays: torch.Tensor
+    ray_origins: torch.Tensor
+    ray_directions: torch.Tensor
+    trace: TraceOutputs | None
+    fused: dict[str, torch.Tensor]
+    camera: dict[str, torch.Tensor] | None
+    maps: dict[str, torch.Tensor] | None
+
+
+_GROUP_KEYS = ("means3d", "opacities", "scales", "rotations", "specular", "roughness")
+
+
+def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Tensor], viewmatrix: torch.Tensor,
+                  projmatrix: torch.Tensor, camera_position: torch.Tensor, background: torch.Tensor, *,
+                  width: int, height: int, tan_fovx: float, tan_fovy: float, sh_degree: int,
+                  base_context: NativeRendererContext, reflection_context: NativeRendererContext,
+                  trace: dict[str, Any] | None = None, postprocess: dict[str, float] | None = None,
+                  stream: int | None = None) -> StandardViewOutputs:
+    """One view of the standard session (render_hybridsplat_view,
+    renderer.py:232-341, and postprocess_raster, math.py:426-463) in one call
+    (hs_b200_standard_view_v2).
+
+    ``base`` holds the activated base group (``means3d``, ``opacities``,
+    ``scales``, ``rotations``, ``specular``, ``roughness``) and its SH ``sh``
+    [P,3,C] (channel-major); ``reflection`` the activated reflection group,
+    its raw quaternions ``rotations_raw`` and, unless traced, its colours
+    ``rgb`` [R,3]. ``trace`` (optional) traces the reflection colours on
+    reflection_context's built scene: ``background`` [3], ``shs`` [R,C,3],
+    ``others`` [R,2], ``degree``, and optionally ``use_others`` (True),
+    ``max_trace_depth`` (0), ``specular_threshold`` (0.0), as trace_reflection.
+    ``postprocess`` (optional) adds the raw-map postprocess: ``fov_x``,
+    ``fov_y`` and ``depth_ratio`` (0.0). ``background`` is the raster calls'
+    [5]. ``stream`` as in rasterize_forward_many. Every output equals that of
+    the same steps called one by one.
+    """
+    if base_context is reflection_context:
+        raise ValueError("standard_view needs two distinct contexts")
+    device = viewmatrix.device
+    f = dict(dtype=torch.float32, device=device)
+    sh = base["sh"].contiguous()
+    nb, nr = int(base["means3d"].shape[0]), int(reflection["means3d"].shape[0])
+    _check_tensor("base sh", sh, (nb, 3, int(sh.shape[-1])))
+    _check_tensor("reflection rotations_raw", reflection["rotations_raw"], (nr, 4))
+    if isinstance(sh_degree, bool) or not isinstance(sh_degree, int) or sh_degree not in range(4):
+        raise ValueError("sh_degree must be an integer in [0, 3]")
+    base_colors, refl_colors = torch.empty((nb, 5), **f), torch.empty((nr, 5), **f)
+    for name, group, n in (("base", base, nb), ("reflection", reflection, nr)):
+        _check_tensor(f"{name} specular", group["specular"], (n, 1))
+        _check_tensor(f"{name} roughness", group["roughness"], (n, 1))
+    common = dict(width=width, height=height, scale_modifier=1.0, tan_fovx=tan_fovx, tan_fovy=tan_fovy)
+    named_b, out_b = _rasterizer_arguments(background, base["means3d"], base_colors, base["opacities"],
+                                           base["scales"], base["rotations"], viewmatrix, projmatrix,
+                                           camera_position, **common)
+    named_r, out_r = _rasterizer_arguments(background, reflection["means3d"], refl_colors, reflection["opacities"],
+                                           reflection["scales"], reflection["rotations"], viewmatrix, projmatrix,
+                                           camera_position, **common)
+
+    def group(named, g):
+        return native_runtime.StandardGroupV2(
+            count=named["point_count"], means3d=named["means3d"], opacities=named["opacities"],
+            scales2=named["scales2"], rotations4=named["rotations4"], specular=_ptr(g["specular"]),
+            roughness=_ptr(g["roughness"]), background5=named["background5"], colors5=named["colors5"],
+            output_color5=named["output_color5"], output_aux7=named["output_aux7"],
+            output_weight=named["output_weight"], output_radii=named["output_radii"],
+            output_rendered=named["output_rendered"])
+
+    rotation, normal = torch.empty((nr, 3, 3), **f), torch.empty((nr, 3), **f)
+    rays, origins, directions = torch.empty((nr, 36), **f), torch.empty((nr, 3), **f), torch.empty((nr, 3), **f)
+    pixels = width * height
+    fused = {k: torch.empty((height, width, 3), **f) for k in ("rgb_map", "dif_rgb_map", "ref_rgb_map")}
+    view = native_runtime.StandardViewV2(
+        struct_size=ctypes.sizeof(native_runtime.StandardViewV2), base_handle=base_context.handle,
+        reflection_handle=reflection_context.handle, width=width, height=height, tan_fovx=named_b["tan_fovx"],
+        tan_fovy=named_b["tan_fovy"], viewmatrix4x4=_ptr(viewmatrix), projmatrix4x4=_ptr(projmatrix),
+        camera_position3=_ptr(camera_position), base=group(named_b, base), reflection=group(named_r, reflection),
+        base_sh=_ptr(sh), sh_coefficients=int(sh.shape[-1]), sh_degree=sh_degree,
+        reflection_rotation_raw4=_ptr(reflection["rotations_raw"]), reflection_rotation9=_ptr(rotation),
+        reflection_normal3=_ptr(normal), reflection_rays36=_ptr(rays), reflection_ray_origins3=_ptr(origins),
+        reflection_ray_directions3=_ptr(directions), fused_rgb3=_ptr(fused["rgb_map"]),
+        diffuse_rgb3=_ptr(fused["dif_rgb_map"]), reflection_rgb_map3=_ptr(fused["ref_rgb_map"]), stream=stream)
+    traced = None
+    if trace is None:
+        rgb = reflection["rgb"]
+        _check_tensor("reflection rgb", rgb, (nr, 3))
+        view.reflection_rgb3 = _ptr(rgb)
+    else:
+        shs = trace["shs"]
+        coefficients = int(shs.shape[1])
+        _check_tensor("trace background", trace["background"], (3,))
+        _check_tensor("trace shs", shs, (nr, coefficients, 3))
+        _check_tensor("trace others", trace["others"], (nr, 2))
+        degree = trace["degree"]
+        if isinstance(degree, bool) or not isinstance(degree, int) or degree not in range(4):
+            raise ValueError("degree must be an integer in [0, 3]")
+        depth = trace.get("max_trace_depth", 0)
+        if depth not in (0, 1) or isinstance(depth, bool):
+            raise ValueError("max_trace_depth must be 0 or 1")
+        traced = TraceOutputs(torch.empty((nr, 3), **f), torch.empty((nr, 1), **f), torch.empty((nr, 1), **f),
+                              torch.empty((nr, 3), **f), torch.empty((nr, 1), **f), torch.empty((nr, 2), **f),
+                              torch.empty((nr, 32), **f), torch.empty((nr, 1), **f))
+        view.trace = 1
+        view.trace_background3 = _ptr(trace["background"])
+        view.reflection_shs = _ptr(shs)
+        view.trace_coefficients = coefficients
+        view.trace_degree = degree
+        view.reflection_others2 = _ptr(trace["others"])
+        view.use_others = int(bool(trace.get("use_others", True)))
+        view.max_trace_depth = int(depth)
+        view.specular_threshold = _finite("specular_threshold", trace.get("specular_threshold", 0.0))
+        for field, t in zip(("trace_rgb3", "trace_depth1", "trace_acc1", "trace_normal3", "trace_dist1",
+                             "trace_aux2", "trace_mid32", "trace_wet1"), traced):
+            setattr(view, field, _ptr(t))
+    camera = maps = None
+    if postprocess is not None:
+        camera_buf, pixel_rays = torch.empty(30, **f), torch.empty((pixels, 3), **f)
+        maps = {name: torch.empty((1, pixels, c), **f) for name, c in zip(STANDARD_MAPS, STANDARD_MAP_CHANNELS)}
+        view.fov_x = _finite("fov_x", postprocess["fov_x"])
+        view.fov_y = _finite("fov_y", postprocess["fov_y"])
+        view.depth_ratio = _finite("depth_ratio", postprocess.get("depth_ratio", 0.0))
+        view.camera30 = _ptr(camera_buf)
+        view.pixel_rays3 = _ptr(pixel_rays)
+        for field, name in zip(("rgb_map3", "acc_map", "dpt_map", "norm_map3", "surf_norm_map3", "dist_map",
+                                "spec_map", "rough_map"), STANDARD_MAPS):
+            setattr(view, field, _ptr(maps[name]))
+        camera = {"inverse_intrinsics": camera_buf[0:9].view(3, 3), "rotation": camera_buf[9:18].view(3, 3),
+                  "origin": camera_buf[18:21], "normal_rotation": camera_buf[21:30].view(3, 3), "rays": pixel_rays}
+    error = error_buffer()
+    status = base_context.library.hs_b200_standard_view_v2(ctypes.byref(view), error, len(error))
+    check_status(status, "hs_b200_standard_view_v2", error)
+    return StandardViewOutputs(out_b, out_r, base_colors, refl_colors, rotation, normal, rays, origins, directions,
+                               traced, fused, camera, maps)

@@ -199,6 +199,110 @@ HS_API int32_t hs_b200_rasterizer_forward_many_v2(
     const HsB200RasterizerCallV2* calls, uint32_t call_count, void* stream, char* error_text,
     uint64_t error_capacity) HS_NOEXCEPT;
 
+/* ---- one whole standard view in one call ----
+ *
+ * The session's per-view sequence of the standard backend
+ * (render_hybridsplat_view, renderer.py:232-341, with postprocess_raster,
+ * math.py:426-463) as one entry point, on `stream` (NULL = the legacy default
+ * stream): base colours (direction + SH + concatenation), reflection prefix
+ * and suffix, the reflection trace (optional: on reflection_handle's built
+ * scene) or given reflection colours, the base and reflection raster calls
+ * run concurrently (as hs_b200_rasterizer_forward_many_v2), the fusion from
+ * the raster calls' colour planes, and (optional) the raw-map postprocess
+ * whose camera terms and pixel rays run on a side stream beside the rasters.
+ * Every output equals that of the same steps called one by one. The host
+ * waits once per raster call for its pair count, as the v1 calls do (the pair
+ * capacity is grown on the host), so a view cannot be captured in a CUDA
+ * graph. All buffers are device memory. No counterpart in the reference
+ * library. */
+typedef struct HsB200StandardGroupV2 {
+    uint64_t count;
+    const float* means3d;       /* [P,3] */
+    const float* opacities;     /* [P,1] activated */
+    const float* scales2;       /* [P,2] activated */
+    const float* rotations4;    /* [P,4] activated (normalised) */
+    const float* specular;      /* [P,1] activated */
+    const float* roughness;     /* [P,1] activated */
+    const float* background5;
+    float* colors5;             /* [P,5] written: the raster call's colours */
+    float* output_color5;       /* raster call outputs, as hs_rasterizer_forward_f32_v1 */
+    float* output_aux7;
+    float* output_weight;
+    int32_t* output_radii;
+    int32_t* output_rendered;
+} HsB200StandardGroupV2;
+
+typedef struct HsB200StandardViewV2 {
+    uint32_t struct_size;                 /* sizeof(HsB200StandardViewV2) */
+    HsRasterizerHandle base_handle;       /* base raster and the postprocess's camera terms */
+    HsRasterizerHandle reflection_handle; /* reflection raster and the trace scene (distinct handle) */
+    int32_t width;
+    int32_t height;
+    float tan_fovx;
+    float tan_fovy;
+    double fov_x;                          /* FoVx, FoVy of the camera (postprocess intrinsics) */
+    double fov_y;
+    const float* viewmatrix4x4;            /* world_view_transform as the session stores it */
+    const float* projmatrix4x4;            /* full_proj_transform */
+    const float* camera_position3;         /* camera centre */
+    HsB200StandardGroupV2 base;
+    HsB200StandardGroupV2 reflection;
+    /* base colours: sh[P,3,sh_coefficients] channel-major, active degree */
+    const float* base_sh;
+    uint32_t sh_coefficients;
+    uint32_t sh_degree;
+    /* reflection preparation (written): prefix [R,9], normal column [R,3],
+     * suffix [R,36], the trace's ray origins and directions [R,3] */
+    const float* reflection_rotation_raw4;
+    float* reflection_rotation9;
+    float* reflection_normal3;
+    float* reflection_rays36;
+    float* reflection_ray_origins3;
+    float* reflection_ray_directions3;
+    /* reflection colours: trace == 0 takes reflection_rgb3 [R,3]; trace == 1
+     * traces (hs_optix_trace_f32_v1 arguments below, rays from the suffix,
+     * scale modifier 1, start_from_first 0) and writes its outputs */
+    const float* reflection_rgb3;
+    int32_t trace;
+    const float* trace_background3;
+    const float* reflection_shs;          /* [R,coefficients,3] */
+    uint32_t trace_coefficients;
+    uint32_t trace_degree;
+    const float* reflection_others2;      /* [R,2]; read when use_others */
+    int32_t use_others;
+    int32_t max_trace_depth;
+    float specular_threshold;
+    float* trace_rgb3;
+    float* trace_depth1;
+    float* trace_acc1;
+    float* trace_normal3;
+    float* trace_dist1;
+    float* trace_aux2;
+    float* trace_mid32;
+    float* trace_wet1;
+    /* fusion: [H*W,3] each */
+    float* fused_rgb3;
+    float* diffuse_rgb3;
+    float* reflection_rgb_map3;
+    /* postprocess (when camera30 is not NULL): hs_b200_postprocess_camera_f32_v1
+     * and hs_b200_standard_postprocess_f32_v1 */
+    double depth_ratio;
+    float* camera30;
+    float* pixel_rays3;
+    float* rgb_map3;
+    float* acc_map;
+    float* dpt_map;
+    float* norm_map3;
+    float* surf_norm_map3;
+    float* dist_map;
+    float* spec_map;
+    float* rough_map;
+    void* stream;
+} HsB200StandardViewV2;
+
+HS_API int32_t hs_b200_standard_view_v2(
+    const HsB200StandardViewV2* view, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
 /* The standard branch's colours in one pass: hs_rasterizer_precise_direction_f32_v1
  * of points[count,3] from center3, hs_rasterizer_precise_sh_to_rgb_f32_v1 of
  * sh[count,3,coefficient_count] (channel-major, as the reference passes its

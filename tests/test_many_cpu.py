@@ -1,14 +1,18 @@
-"""Host side of the concurrent raster entry points (hs_b200_*_forward_many_v2).
+"""Host side of the concurrent raster entry points (hs_b200_*_forward_many_v2)
+and of the one-view entry point (hs_b200_standard_view_v2).
 
 The call structs of include/hybridsplat_b200_ext.h must match their ctypes
-mirrors field by field, and every call is checked, with the messages of the
-single-call entry points, before any handle is used.
+mirrors field by field (names, types, and the offsets a C compiler gives
+them), and every call is checked, with the messages of the single-call entry
+points, before any handle is used.
 """
 
 from __future__ import annotations
 
 import ctypes
 import re
+import shutil
+import subprocess
 
 import pytest
 
@@ -19,15 +23,18 @@ from hybridsplat_jittor_render_b200 import ops
 EXT_HEADER = REPO / "include" / "hybridsplat_b200_ext.h"
 C_TYPES = {
     "HsRasterizerHandle": ctypes.c_void_p, "uint64_t": ctypes.c_uint64, "int32_t": ctypes.c_int32,
-    "uint32_t": ctypes.c_uint32, "float": ctypes.c_float,
+    "uint32_t": ctypes.c_uint32, "float": ctypes.c_float, "double": ctypes.c_double,
+    "HsB200StandardGroupV2": nr.StandardGroupV2,
 }
+MIRRORS = [("HsB200FlashgsCallV2", nr.FlashgsCallV2), ("HsB200RasterizerCallV2", nr.RasterizerCallV2),
+           ("HsB200StandardGroupV2", nr.StandardGroupV2), ("HsB200StandardViewV2", nr.StandardViewV2)]
 
 
 def header_struct(name: str) -> list[tuple[str, object]]:
     body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), EXT_HEADER.read_text(), re.S).group(1)
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
     fields = []
     for decl in filter(None, (d.strip() for d in body.split(";"))):
-        decl = re.sub(r"/\*.*?\*/", "", decl, flags=re.S).strip()
         ctype, field = decl.rsplit(None, 1)
         if field.startswith("*") or ctype.endswith("*"):
             fields.append((field.lstrip("*"), ctypes.c_void_p))
@@ -36,10 +43,28 @@ def header_struct(name: str) -> list[tuple[str, object]]:
     return fields
 
 
-@pytest.mark.parametrize("name,mirror", [("HsB200FlashgsCallV2", nr.FlashgsCallV2),
-                                         ("HsB200RasterizerCallV2", nr.RasterizerCallV2)])
+@pytest.mark.parametrize("name,mirror", MIRRORS)
 def test_call_structs_match_header(name, mirror):
     assert [(f, t) for f, t in mirror._fields_] == header_struct(name)
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs a C compiler")
+def test_call_struct_offsets_match_the_c_compiler(tmp_path):
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "hybridsplat_b200_ext.h"', "int main(void) {"]
+    expected = []
+    for name, mirror in MIRRORS:
+        lines.append(f'printf("%zu\\n", sizeof({name}));')
+        expected.append(ctypes.sizeof(mirror))
+        for field, _ in mirror._fields_:
+            lines.append(f'printf("%zu\\n", offsetof({name}, {field}));')
+            expected.append(getattr(mirror, field).offset)
+    lines += ["return 0;", "}"]
+    source, binary = tmp_path / "layout.c", tmp_path / "layout"
+    source.write_text("\n".join(lines))
+    subprocess.run(["gcc", "-std=c99", "-I", str(REPO / "include"), str(source), "-o", str(binary)], check=True)
+    printed = [int(v) for v in subprocess.run([str(binary)], check=True, capture_output=True,
+                                              text=True).stdout.split()]
+    assert printed == expected
 
 
 def test_struct_fields_cover_the_single_call_arguments():
@@ -122,3 +147,52 @@ def test_ops_rows_fields():
     assert ops._rows_fields(None) == {"tile_row_begin": 0, "tile_row_end": 0xFFFFFFFF}
     assert ops._rows_fields((1, 3)) == {"tile_row_begin": 1, "tile_row_end": 3}
     assert ops._rows_fields((0, 0xFFFFFFFF))["tile_row_end"] == 0xFFFFFFFE
+
+
+def _view_struct(**over):
+    dummy = 16
+    group = dict(count=0, background5=dummy, colors5=dummy, output_color5=dummy, output_aux7=dummy,
+                 output_rendered=dummy)
+    v = nr.StandardViewV2(struct_size=ctypes.sizeof(nr.StandardViewV2), base_handle=16, reflection_handle=32,
+                          width=64, height=48, tan_fovx=0.5, tan_fovy=0.5, base=nr.StandardGroupV2(**group),
+                          reflection=nr.StandardGroupV2(**group), sh_coefficients=16, sh_degree=3,
+                          fused_rgb3=dummy, diffuse_rgb3=dummy, reflection_rgb_map3=dummy)
+    for k, val in over.items():
+        if "." in k:
+            outer, inner = k.split(".")
+            setattr(getattr(v, outer), inner, val)
+        else:
+            setattr(v, k, val)
+    return v
+
+
+def _view(lib, v):
+    err = ctypes.create_string_buffer(512)
+    status = lib.hs_b200_standard_view_v2(None if v is None else ctypes.byref(v), err, len(err))
+    return status, err.value.decode()
+
+
+@pytest.mark.parametrize("over,expected", [
+    (dict(struct_size=8), (1, "standard view is null or its struct_size is too small")),
+    (dict(base_handle=None), (1, "rasterizer received a null required handle or buffer")),
+    (dict(**{"reflection.output_aux7": None}), (1, "rasterizer received a null required handle or buffer")),
+    (dict(width=0), (3, "rasterizer dimensions or scalar arguments are invalid")),
+    (dict(**{"base.count": 5}), (1, "non-empty rasterizer input contains a null buffer")),
+    (dict(reflection_handle=16), (1, "standard view needs two distinct handles")),
+    (dict(sh_coefficients=4, sh_degree=2), (3, "standard view SH dimensions are invalid")),
+    (dict(sh_coefficients=17), (3, "standard view SH dimensions are invalid")),
+    (dict(fused_rgb3=None), (1, "standard view received a null required buffer")),
+    (dict(trace=2), (3, "standard view trace must be 0 or 1")),
+    (dict(trace=1, trace_coefficients=16, trace_degree=3, max_trace_depth=2),
+     (3, "OptiX trace dimensions or scalars are invalid")),
+    (dict(camera30=16, fov_x=float("nan")), (1, "standard view postprocess scalars must be finite")),
+    (dict(camera30=16, width=70000, height=70000), (3, "postprocess_camera pixel count exceeds cuBLAS int range")),
+    (dict(camera30=16), (1, "standard view postprocess received a null buffer")),
+])
+def test_view_checks_every_argument_before_the_handles(lib, over, expected):
+    # both handles are fake: a check that passed would read them
+    assert _view(lib, _view_struct(**over)) == expected
+
+
+def test_view_null(lib):
+    assert _view(lib, None) == (1, "standard view is null or its struct_size is too small")
