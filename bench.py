@@ -18,6 +18,10 @@ and in `blocks.view_with_trace`, the whole view with the traced colours
 feeding the reflection raster (this library's CUDA BVH tracer behind the
 reference's hs_optix_* entry points).
 
+A standard step is one library call per view (hs_b200_standard_view_v2, the
+same steps in the same order); --no-view-entry issues them as the session's
+separate calls instead.
+
 Both steps end with the session's raw-map postprocess of the base raster
 (standard: camera matrices and TF32 pixel rays on a side stream beside the
 rasters, then the fused maps kernel with the surface normals; FlashGS: its
@@ -112,7 +116,7 @@ def parse_args():
     p.add_argument("--no-reference-gpu", action="store_true", help="skip timing the reference CUDA rebuild")
     p.add_argument("--no-blocks", action="store_true",
                    help="skip the flashgs / large_6m / stress_4k blocks of the default run")
-    p.add_argument("--readback", choices=("after-call", "before-call"), default="before-call",
+    p.add_argument("--readback", choices=("after-call", "before-call"), default="after-call",
                    help="e2e: queue frame s-1's map read-back before or after frame s's raster calls")
     p.add_argument("--scale", type=float, default=1.0, help="Gaussian-count scale (profiling runs only)")
     p.add_argument("--profile-frames", type=int, default=0,
@@ -121,6 +125,8 @@ def parse_args():
                    help="with --profile-frames: render with the reference CUDA rebuild (oracle/_ref)")
     p.add_argument("--trace", action="store_true",
                    help="with --profile-frames: trace the reflection colours of every frame")
+    p.add_argument("--no-view-entry", action="store_true",
+                   help="standard views as the session's separate calls instead of hs_b200_standard_view_v2")
     return p.parse_args()
 
 
@@ -301,6 +307,9 @@ class Frame:
         self.tile_rows = None  # (begin, end): render only this strip of tile rows
         self.r_scene = r
         self.traced = False  # render() traces the reflection colours (enable_trace)
+        # Standard views go to the library as one call (hs_b200_standard_view_v2)
+        # unless instrumented, rendered in strips or run sequentially.
+        self.view_entry = backend == "standard" and hasattr(lib, "hs_b200_standard_view_v2")
 
     def enable_trace(self) -> float:
         """Builds the reflection trace scene of the session (the disks of the
@@ -370,6 +379,8 @@ class Frame:
         pixel rays run on a side stream beside them."""
         ops, torch, cam, lib = self.ops, self.torch, self.cam, self.library
         sequential = events is not None or not self.concurrent
+        if self.one_call(events):
+            return self.render_one_call()
         rec = (lambda i: events[i].record()) if events else (lambda i: None)
         post = self.with_post
         terms = None
@@ -463,6 +474,31 @@ class Frame:
             rec(6)
         return base, refl, fused, rays, maps
 
+    def one_call(self, events=None) -> bool:
+        return self.view_entry and events is None and self.concurrent and self.tile_rows is None
+
+    def render_one_call(self):
+        """The whole standard view as one library call (ops.standard_view):
+        the same steps as render(), in the same order, on the current stream,
+        with the camera terms on the library's side stream."""
+        torch, cam = self.torch, self.cam
+        base = dict(means3d=self.b_xyz, opacities=self.b_op, scales=self.b_scale, rotations=self.b_rot,
+                    specular=self.b_spec, roughness=self.b_rough, sh=self.b_sh)
+        refl = dict(means3d=self.r_xyz, opacities=self.r_op, scales=self.r_scale, rotations=self.r_rot,
+                    rotations_raw=self.r_rot_raw, specular=self.r_spec, roughness=self.r_rough, rgb=self.trace_rgb)
+        trace = (dict(background=self.bg3, shs=self.r_sh16, others=self.r_others, degree=3, use_others=False)
+                 if self.traced else None)
+        post = None
+        if self.with_post:
+            post = {"fov_x": 2.0 * math.atan(cam.tan_fovx), "fov_y": 2.0 * math.atan(cam.tan_fovy),
+                    "depth_ratio": 0.0}
+        out = self.ops.standard_view(base, refl, self.view, self.proj, self.center, self.bg5, width=cam.width,
+                                     height=cam.height, tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy, sh_degree=3,
+                                     base_context=self.ctx, reflection_context=self.ctx_r, trace=trace,
+                                     postprocess=post,
+                                     stream=torch.cuda.current_stream(self.device).cuda_stream)
+        return out.base, out.reflection, out.fused, out.reflection_rays, out.maps
+
     def maps_for_host(self, result):
         """The maps the session reads back (session.py:33-42): rgb, acc, dpt,
         norm, surf_norm, spec, diffuse and reflection rgb, with the
@@ -496,6 +532,10 @@ class Frame:
             # rays, maps (the inverses' cuSOLVER/cuBLAS kernels are not ours);
             # FlashGS: maps
             extra += 6 if self.backend == "standard" else 1
+        if self.one_call():
+            # the one-call entry prepares the reflection in one kernel (prefix,
+            # normal column, suffix, colours); traced, the colours follow the trace
+            extra -= 0 if self.traced else 1
         return 2 * per_raster + extra + 3  # + reflection prefix, suffix, fusion
 
 
@@ -775,6 +815,7 @@ def run_block(job: Job, args, scene: DeviceScene, workload: Workload, backend: s
     from hybridsplat_jittor_render_b200 import multigpu, scenes
     spec = scenes.SCENES[workload.scene]
     frame = Frame(scene, backend, job.device, concurrent=not args.sequential)
+    frame.view_entry &= not args.no_view_entry
     strips = workload.sharding == "tile-strip"
     if strips:
         frame.tile_rows = multigpu.tile_strips((spec.height + 15) // 16, job.world)[job.rank]
@@ -822,6 +863,7 @@ def run_ours(args, workload: Workload) -> int:
         from hybridsplat_jittor_render_b200.native_runtime import bind_library
         library = bind_library(REPO / "oracle" / "_ref" / "libref_hybridsplat.so", require_optix=False)
     frame = Frame(scene, args.backend, device, library=library, concurrent=not args.sequential)
+    frame.view_entry &= not args.no_view_entry
     if strips:
         frame.tile_rows = multigpu.tile_strips((spec.height + 15) // 16, world)[job.rank]
     views = views_for(job, workload.scene, workload.sharding, args.steps, args.warmup)
@@ -866,6 +908,8 @@ def run_ours(args, workload: Workload) -> int:
                            "loop_ms_max": t["loop_ms_max"], "timed_wall_s": t["timed_wall_s"],
                            "priming": "one untimed render of each timed view before the warm-up steps",
                            "branches": "sequential v1 calls" if args.sequential else
+                                       "the whole view in one call (hs_b200_standard_view_v2: both rasters "
+                                       "concurrent, camera terms on a side stream)" if frame.one_call() else
                                        "base and reflection rasters in one concurrent call "
                                        "(hs_b200_*_forward_many_v2)",
                            "stages_ms": "from a separate pass with the branches sequential, each stage alone; "

@@ -1910,7 +1910,6 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
         if ((nb != 0 && (v->base_sh == nullptr || v->base.specular == nullptr || v->base.roughness == nullptr)) ||
             (nr != 0 && (v->reflection_rotation_raw4 == nullptr || v->reflection_rotation9 == nullptr ||
                          v->reflection_normal3 == nullptr || v->reflection_rays36 == nullptr ||
-                         v->reflection_ray_origins3 == nullptr || v->reflection_ray_directions3 == nullptr ||
                          v->reflection.specular == nullptr || v->reflection.roughness == nullptr ||
                          (v->trace == 0 && v->reflection_rgb3 == nullptr))) ||
             v->fused_rgb3 == nullptr || v->diffuse_rgb3 == nullptr || v->reflection_rgb_map3 == nullptr) {
@@ -1928,7 +1927,8 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
                 return fail(HS_STATUS_RANGE_ERROR, "OptiX trace dimensions or scalars are invalid", error_text,
                             error_capacity);
             }
-            if (nr != 0 && (v->trace_background3 == nullptr || v->reflection_shs == nullptr ||
+            if (nr != 0 && (v->reflection_ray_origins3 == nullptr || v->reflection_ray_directions3 == nullptr ||
+                            v->trace_background3 == nullptr || v->reflection_shs == nullptr ||
                             v->reflection_others2 == nullptr || v->trace_rgb3 == nullptr ||
                             v->trace_depth1 == nullptr || v->trace_acc1 == nullptr || v->trace_normal3 == nullptr ||
                             v->trace_dist1 == nullptr || v->trace_aux2 == nullptr || v->trace_mid32 == nullptr ||
@@ -1992,19 +1992,22 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
             if (e != cudaSuccess) return cuda_failure(e, "standard view join", error_text, error_capacity);
         }
         // base colours, reflection preparation, trace, reflection colours
+        const bool traced = v->trace == 1;
         e = hs::precise::sh_colors5(v->base_sh, v->sh_coefficients, v->sh_degree, v->base.means3d,
                                     v->camera_position3, v->base.specular, v->base.roughness, nb,
                                     v->base.colors5, s);
-        if (e == cudaSuccess) e = hs::precise::reflection_prefix(v->reflection_rotation_raw4, nr,
-                                                                 v->reflection_rotation9, s);
-        if (e == cudaSuccess) e = hs::view::normal_column(v->reflection_rotation9, nr, v->reflection_normal3, s);
-        if (e == cudaSuccess) e = hs::precise::reflection_suffix(v->reflection.means3d, v->camera_position3,
-                                                                 v->reflection_normal3, nr, v->reflection_rays36, s);
-        if (e == cudaSuccess) e = hs::view::split_rays(v->reflection_rays36, nr, v->reflection_ray_origins3,
-                                                       v->reflection_ray_directions3, s);
+        // prefix, normal column, suffix and (traced) the ray split or
+        // (untraced) the reflection colours, in one pass
+        if (e == cudaSuccess) {
+            e = hs::precise::reflection_view(
+                v->reflection_rotation_raw4, v->reflection.means3d, v->camera_position3, nr,
+                v->reflection_rotation9, v->reflection_normal3, v->reflection_rays36,
+                traced ? v->reflection_ray_origins3 : nullptr, traced ? v->reflection_ray_directions3 : nullptr,
+                v->reflection_rgb3, v->reflection.specular, v->reflection.roughness,
+                traced ? nullptr : v->reflection.colors5, s);
+        }
         if (e != cudaSuccess) return cuda_failure(e, "standard view preparation", error_text, error_capacity);
-        const float* reflection_rgb = v->reflection_rgb3;
-        if (v->trace == 1 && nr != 0) {
+        if (traced && nr != 0) {
             hs::TraceCall t;
             t.ray_count = nr;
             t.ray_origins3 = v->reflection_ray_origins3;
@@ -2037,11 +2040,10 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
             t.stream = s;
             e = hs::trace_rays(refl, t);
             if (e != cudaSuccess) return cuda_failure(e, "reflection trace", error_text, error_capacity);
-            reflection_rgb = v->trace_rgb3;
+            e = hs::view::colors5(v->trace_rgb3, v->reflection.specular, v->reflection.roughness, nr,
+                                  v->reflection.colors5, s);
+            if (e != cudaSuccess) return cuda_failure(e, "standard view colours", error_text, error_capacity);
         }
-        e = hs::view::colors5(reflection_rgb, v->reflection.specular, v->reflection.roughness, nr,
-                              v->reflection.colors5, s);
-        if (e != cudaSuccess) return cuda_failure(e, "standard view colours", error_text, error_capacity);
         // both raster calls, concurrently
         e = hs::standard_forward_many(contexts, calls, 2, s);
         if (e != cudaSuccess) return cuda_failure(e, "concurrent five-channel rasterizer forward", error_text,

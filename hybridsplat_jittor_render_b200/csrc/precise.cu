@@ -297,26 +297,32 @@ __global__ void fuse_maps_planar_kernel(const float* __restrict__ base,
     }
 }
 
+// precise_reflection_trace.cu:119-183: the matrix entries contract the
+// leading product with the following add/sub (one fma each).
+__device__ __forceinline__ void prefix_matrix(const float* q, float o[9]) {
+    float w, x, y, z;
+    twice_normalized(q, w, x, y, z);
+    const float wz = mul(w, z), wy = mul(w, y), wx = mul(w, x);
+    const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
+    o[0] = sub(1.0f, mul(2.0f, fma(y, y, zz)));
+    o[1] = mul(2.0f, fma(x, y, sub(0.0f, wz)));
+    o[2] = mul(2.0f, fma(x, z, wy));
+    o[3] = mul(2.0f, fma(x, y, wz));
+    o[4] = sub(1.0f, mul(2.0f, fma(x, x, zz)));
+    o[5] = mul(2.0f, fma(y, z, sub(0.0f, wx)));
+    o[6] = mul(2.0f, fma(x, z, sub(0.0f, wy)));
+    o[7] = mul(2.0f, fma(y, z, wx));
+    o[8] = sub(1.0f, mul(2.0f, fma(x, x, yy)));
+}
+
 __global__ void reflection_prefix_kernel(const float* __restrict__ rot, uint64_t count,
                                          float* __restrict__ out) {
-    // precise_reflection_trace.cu:119-183: the matrix entries contract the
-    // leading product with the following add/sub (one fma each).
     for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < count;
          i += uint64_t(gridDim.x) * blockDim.x) {
-        float w, x, y, z;
-        twice_normalized(rot + 4 * i, w, x, y, z);
-        const float wz = mul(w, z), wy = mul(w, y), wx = mul(w, x);
-        const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
-        float* o = out + 9 * i;
-        o[0] = sub(1.0f, mul(2.0f, fma(y, y, zz)));
-        o[1] = mul(2.0f, fma(x, y, sub(0.0f, wz)));
-        o[2] = mul(2.0f, fma(x, z, wy));
-        o[3] = mul(2.0f, fma(x, y, wz));
-        o[4] = sub(1.0f, mul(2.0f, fma(x, x, zz)));
-        o[5] = mul(2.0f, fma(y, z, sub(0.0f, wx)));
-        o[6] = mul(2.0f, fma(x, z, sub(0.0f, wy)));
-        o[7] = mul(2.0f, fma(y, z, wx));
-        o[8] = sub(1.0f, mul(2.0f, fma(x, x, yy)));
+        float o[9];
+        prefix_matrix(rot + 4 * i, o);
+#pragma unroll
+        for (int k = 0; k < 9; ++k) out[9 * i + k] = o[k];
     }
 }
 
@@ -358,55 +364,116 @@ __device__ __forceinline__ float normalize3_add(float& x, float& y, float& z) {
 constexpr int kSuffixThreads = 128;
 constexpr int kSuffixStride = 37;
 
+// precise_reflection_trace.cu:185-330: the 36-float row of one reflective
+// Gaussian at p with raw normal n, seen from camera centre c.
+__device__ __forceinline__ void suffix_row(float px, float py, float pz, float cx, float cy, float cz,
+                                           float inx, float iny, float inz, float values[36]) {
+    float vx = sub(cx, px), vy = sub(cy, py), vz = sub(cz, pz);
+    normalize3_add(vx, vy, vz);
+    // Facing flip against -(p - c), dot reduced as (x + z) + y.
+    const float tx = sub(0.0f, sub(px, cx));
+    const float ty = sub(0.0f, sub(py, cy));
+    const float tz = sub(0.0f, sub(pz, cz));
+    const float flip_dot = add(add(mul(inx, tx), mul(inz, tz)), mul(iny, ty));
+    const bool positive = flip_dot >= 0.0f;
+    const float sign = positive ? 1.0f : -1.0f;
+    const float nrx = mul(inx, sign), nry = mul(iny, sign), nrz = mul(inz, sign);
+    const float nn = norm3_torch(nrx, nry, nrz);
+    const float nden = nn < 1.0e-20f ? 1.0e-20f : nn;
+    const float nx = div(nrx, nden), ny = div(nry, nden), nz = div(nrz, nden);
+    const float rpx = mul(nx, vx), rpy = mul(ny, vy), rpz = mul(nz, vz);
+    const float dot_nv = add(add(rpx, rpz), rpy);
+    const float two_dot = mul(2.0f, dot_nv);
+    const float snx = mul(two_dot, nx), sny = mul(two_dot, ny), snz = mul(two_dot, nz);
+    const float rx = sub(snx, vx), ry = sub(sny, vy), rz = sub(snz, vz);
+    float dx = rx, dy = ry, dz = rz;
+    const float ray_den = normalize3_add(dx, dy, dz);
+    const float ox = mul(0.05f, dx), oy = mul(0.05f, dy), oz = mul(0.05f, dz);
+    const float row[36] = {vx,  vy,  vz,  nx,  ny,  nz,  rx,  ry,  rz,
+                           dx,  dy,  dz,  add(px, ox), add(py, oy), add(pz, oz),
+                           positive ? 1.0f : 0.0f,
+                           inx, iny, inz, nrx, nry, nrz, nden, rpx, rpy, rpz,
+                           dot_nv, two_dot, snx, sny, snz, ray_den, ox, oy, oz,
+                           flip_dot};
+#pragma unroll
+    for (int k = 0; k < 36; ++k) values[k] = row[k];
+}
+
+// The block's 36-float rows, staged in shared memory (padded to 37 words),
+// written with coalesced stores.
+__device__ __forceinline__ void store_rows(const float* rows, uint64_t first, uint32_t n, float* out36) {
+    float* dst = out36 + first * 36;
+    for (uint32_t f = threadIdx.x; f < n * 36; f += kSuffixThreads) {
+        dst[f] = rows[(f / 36) * kSuffixStride + f % 36];
+    }
+}
+
 __global__ void __launch_bounds__(kSuffixThreads) reflection_suffix_kernel(
     const float* __restrict__ xyz, const float* __restrict__ center,
     const float* __restrict__ normal_raw, uint64_t count, float* __restrict__ out36) {
-    // precise_reflection_trace.cu:185-330
     __shared__ float rows[kSuffixThreads * kSuffixStride];
     const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kSuffixThreads;
     const uint64_t left = count - first;
     const uint32_t n = left < kSuffixThreads ? static_cast<uint32_t>(left) : kSuffixThreads;
     if (threadIdx.x < n) {
         const uint64_t i = first + threadIdx.x;
-        const float cx = center[0], cy = center[1], cz = center[2];
-        const float px = xyz[3 * i], py = xyz[3 * i + 1], pz = xyz[3 * i + 2];
-        float vx = sub(cx, px), vy = sub(cy, py), vz = sub(cz, pz);
-        normalize3_add(vx, vy, vz);
-        const float inx = normal_raw[3 * i], iny = normal_raw[3 * i + 1], inz = normal_raw[3 * i + 2];
-        // Facing flip against -(p - c), dot reduced as (x + z) + y.
-        const float tx = sub(0.0f, sub(px, cx));
-        const float ty = sub(0.0f, sub(py, cy));
-        const float tz = sub(0.0f, sub(pz, cz));
-        const float flip_dot = add(add(mul(inx, tx), mul(inz, tz)), mul(iny, ty));
-        const bool positive = flip_dot >= 0.0f;
-        const float sign = positive ? 1.0f : -1.0f;
-        const float nrx = mul(inx, sign), nry = mul(iny, sign), nrz = mul(inz, sign);
-        const float nn = norm3_torch(nrx, nry, nrz);
-        const float nden = nn < 1.0e-20f ? 1.0e-20f : nn;
-        const float nx = div(nrx, nden), ny = div(nry, nden), nz = div(nrz, nden);
-        const float rpx = mul(nx, vx), rpy = mul(ny, vy), rpz = mul(nz, vz);
-        const float dot_nv = add(add(rpx, rpz), rpy);
-        const float two_dot = mul(2.0f, dot_nv);
-        const float snx = mul(two_dot, nx), sny = mul(two_dot, ny), snz = mul(two_dot, nz);
-        const float rx = sub(snx, vx), ry = sub(sny, vy), rz = sub(snz, vz);
-        float dx = rx, dy = ry, dz = rz;
-        const float ray_den = normalize3_add(dx, dy, dz);
-        const float ox = mul(0.05f, dx), oy = mul(0.05f, dy), oz = mul(0.05f, dz);
-        const float values[36] = {vx,  vy,  vz,  nx,  ny,  nz,  rx,  ry,  rz,
-                                  dx,  dy,  dz,  add(px, ox), add(py, oy), add(pz, oz),
-                                  positive ? 1.0f : 0.0f,
-                                  inx, iny, inz, nrx, nry, nrz, nden, rpx, rpy, rpz,
-                                  dot_nv, two_dot, snx, sny, snz, ray_den, ox, oy, oz,
-                                  flip_dot};
+        float values[36];
+        suffix_row(xyz[3 * i], xyz[3 * i + 1], xyz[3 * i + 2], center[0], center[1], center[2],
+                   normal_raw[3 * i], normal_raw[3 * i + 1], normal_raw[3 * i + 2], values);
         float* row = rows + threadIdx.x * kSuffixStride;
 #pragma unroll
         for (int k = 0; k < 36; ++k) row[k] = values[k];
     }
     __syncthreads();
-    float* dst = out36 + first * 36;
-    for (uint32_t f = threadIdx.x; f < n * 36; f += kSuffixThreads) {
-        dst[f] = rows[(f / 36) * kSuffixStride + f % 36];
+    store_rows(rows, first, n, out36);
+}
+
+// One view's reflection preparation in one pass (renderer.py:267-280): the
+// prefix rotation rot9, its third column normal3 (the raw normal), the
+// suffix row out36 and, when the pointers are given, the trace's ray origins
+// (row columns 12..14) and directions (9..11) and the raster colours
+// colors5 = [rgb3, specular, roughness]. Each value is computed by the same
+// functions as the separate kernels, so they are bit-identical to them.
+__global__ void __launch_bounds__(kSuffixThreads) reflection_view_kernel(
+    const float* __restrict__ rot_raw, const float* __restrict__ xyz, const float* __restrict__ center,
+    uint64_t count, float* __restrict__ rot9, float* __restrict__ normal3, float* __restrict__ out36,
+    float* __restrict__ origins3, float* __restrict__ directions3, const float* __restrict__ rgb3,
+    const float* __restrict__ specular, const float* __restrict__ roughness, float* __restrict__ colors5) {
+    __shared__ float rows[kSuffixThreads * kSuffixStride];
+    const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kSuffixThreads;
+    const uint64_t left = count - first;
+    const uint32_t n = left < kSuffixThreads ? static_cast<uint32_t>(left) : kSuffixThreads;
+    if (threadIdx.x < n) {
+        const uint64_t i = first + threadIdx.x;
+        float o[9];
+        prefix_matrix(rot_raw + 4 * i, o);
+#pragma unroll
+        for (int k = 0; k < 9; ++k) rot9[9 * i + k] = o[k];
+        normal3[3 * i] = o[2];
+        normal3[3 * i + 1] = o[5];
+        normal3[3 * i + 2] = o[8];
+        float values[36];
+        suffix_row(xyz[3 * i], xyz[3 * i + 1], xyz[3 * i + 2], center[0], center[1], center[2], o[2], o[5],
+                   o[8], values);
+        if (origins3 != nullptr) {
+            for (int c = 0; c < 3; ++c) {
+                origins3[3 * i + c] = values[12 + c];
+                directions3[3 * i + c] = values[9 + c];
+            }
+        }
+        if (colors5 != nullptr) {
+            colors5[5 * i] = rgb3[3 * i];
+            colors5[5 * i + 1] = rgb3[3 * i + 1];
+            colors5[5 * i + 2] = rgb3[3 * i + 2];
+            colors5[5 * i + 3] = specular[i];
+            colors5[5 * i + 4] = roughness[i];
+        }
+        float* row = rows + threadIdx.x * kSuffixStride;
+#pragma unroll
+        for (int k = 0; k < 36; ++k) row[k] = values[k];
     }
+    __syncthreads();
+    store_rows(rows, first, n, out36);
 }
 
 unsigned grid_for(uint64_t count) {
@@ -516,6 +583,17 @@ cudaError_t reflection_suffix(const float* xyz, const float* center, const float
     if (count == 0) return cudaSuccess;
     reflection_suffix_kernel<<<static_cast<unsigned>((count + kSuffixThreads - 1) / kSuffixThreads),
                                kSuffixThreads, 0, s>>>(xyz, center, normal_raw, count, out36);
+    return cudaGetLastError();
+}
+
+cudaError_t reflection_view(const float* rot_raw, const float* xyz, const float* center, uint64_t count,
+                            float* rot9, float* normal3, float* out36, float* origins3, float* directions3,
+                            const float* rgb3, const float* specular, const float* roughness, float* colors5,
+                            cudaStream_t s) {
+    if (count == 0) return cudaSuccess;
+    reflection_view_kernel<<<static_cast<unsigned>((count + kSuffixThreads - 1) / kSuffixThreads),
+                             kSuffixThreads, 0, s>>>(rot_raw, xyz, center, count, rot9, normal3, out36, origins3,
+                                                     directions3, rgb3, specular, roughness, colors5);
     return cudaGetLastError();
 }
 

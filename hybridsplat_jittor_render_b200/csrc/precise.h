@@ -30,6 +30,14 @@ cudaError_t reflection_prefix(const float* rot, uint64_t count, float* out, cuda
 cudaError_t reflection_suffix(const float* xyz, const float* center, const float* normal_raw,
                               uint64_t count, float* out36, cudaStream_t s);
 cudaError_t disk_rotation(const float* rot, uint64_t count, float* out, cudaStream_t s);
+// reflection_prefix, its third column (normal3), reflection_suffix and, when
+// origins3 / colors5 are not null, the suffix rows' ray origins and
+// directions and [rgb3, specular, roughness], in one pass; bit-identical to
+// the separate kernels.
+cudaError_t reflection_view(const float* rot_raw, const float* xyz, const float* center, uint64_t count,
+                            float* rot9, float* normal3, float* out36, float* origins3, float* directions3,
+                            const float* rgb3, const float* specular, const float* roughness, float* colors5,
+                            cudaStream_t s);
 
 // Tiny kernels used around the cuBLAS / cuSOLVER camera helpers.
 cudaError_t negate9(const float* in, float* out, cudaStream_t s);

@@ -843,8 +843,9 @@ def flashgs_postprocess(raster: FlashgsOutputs, normal_rotation: torch.Tensor, *
 
 class StandardViewOutputs(NamedTuple):
     """Everything standard_view writes: both raster calls' outputs, the
-    colours they took, the reflection preparation, the trace (when traced),
-    the fused maps and, with the postprocess, its camera terms and maps."""
+    colours they took, the reflection preparation, the trace and its ray
+    origins and directions (when traced, else None), the fused maps and, with
+    the postprocess, its camera terms and maps (else None)."""
     base: RasterizerOutputs
     reflection: RasterizerOutputs
     base_colors: torch.Tensor
@@ -917,8 +918,8 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
             output_weight=named["output_weight"], output_radii=named["output_radii"],
             output_rendered=named["output_rendered"])
 
-    rotation, normal = torch.empty((nr, 3, 3), **f), torch.empty((nr, 3), **f)
-    rays, origins, directions = torch.empty((nr, 36), **f), torch.empty((nr, 3), **f), torch.empty((nr, 3), **f)
+    rotation, normal, rays = torch.empty((nr, 3, 3), **f), torch.empty((nr, 3), **f), torch.empty((nr, 36), **f)
+    origins = directions = None
     pixels = width * height
     fused = {k: torch.empty((height, width, 3), **f) for k in ("rgb_map", "dif_rgb_map", "ref_rgb_map")}
     view = native_runtime.StandardViewV2(
@@ -928,8 +929,7 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
         camera_position3=_ptr(camera_position), base=group(named_b, base), reflection=group(named_r, reflection),
         base_sh=_ptr(sh), sh_coefficients=int(sh.shape[-1]), sh_degree=sh_degree,
         reflection_rotation_raw4=_ptr(reflection["rotations_raw"]), reflection_rotation9=_ptr(rotation),
-        reflection_normal3=_ptr(normal), reflection_rays36=_ptr(rays), reflection_ray_origins3=_ptr(origins),
-        reflection_ray_directions3=_ptr(directions), fused_rgb3=_ptr(fused["rgb_map"]),
+        reflection_normal3=_ptr(normal), reflection_rays36=_ptr(rays), fused_rgb3=_ptr(fused["rgb_map"]),
         diffuse_rgb3=_ptr(fused["dif_rgb_map"]), reflection_rgb_map3=_ptr(fused["ref_rgb_map"]), stream=stream)
     traced = None
     if trace is None:
@@ -951,7 +951,10 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
         traced = TraceOutputs(torch.empty((nr, 3), **f), torch.empty((nr, 1), **f), torch.empty((nr, 1), **f),
                               torch.empty((nr, 3), **f), torch.empty((nr, 1), **f), torch.empty((nr, 2), **f),
                               torch.empty((nr, 32), **f), torch.empty((nr, 1), **f))
+        origins, directions = torch.empty((nr, 3), **f), torch.empty((nr, 3), **f)
         view.trace = 1
+        view.reflection_ray_origins3 = _ptr(origins)
+        view.reflection_ray_directions3 = _ptr(directions)
         view.trace_background3 = _ptr(trace["background"])
         view.reflection_shs = _ptr(shs)
         view.trace_coefficients = coefficients

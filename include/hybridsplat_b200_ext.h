@@ -252,7 +252,8 @@ typedef struct HsB200StandardViewV2 {
     uint32_t sh_coefficients;
     uint32_t sh_degree;
     /* reflection preparation (written): prefix [R,9], normal column [R,3],
-     * suffix [R,36], the trace's ray origins and directions [R,3] */
+     * suffix [R,36]; with trace == 1 also the trace's ray origins and
+     * directions [R,3] (suffix columns 12..14 and 9..11; unused otherwise) */
     const float* reflection_rotation_raw4;
     float* reflection_rotation9;
     float* reflection_normal3;

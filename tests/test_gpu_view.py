@@ -99,9 +99,9 @@ def check(one, ref):
     bits(one.reflection_rotation, ref["rotation"], "reflection rotation")
     bits(one.reflection_normal, ref["normal"], "reflection normal")
     bits(one.reflection_rays, ref["rays"], "reflection rays")
-    bits(one.ray_origins, ref["rays"][:, 12:15], "ray origins")
-    bits(one.ray_directions, ref["rays"][:, 9:12], "ray directions")
     if ref["trace"] is not None:
+        bits(one.ray_origins, ref["rays"][:, 12:15], "ray origins")
+        bits(one.ray_directions, ref["rays"][:, 9:12], "ray directions")
         for field in ops.TraceOutputs._fields:
             bits(getattr(one.trace, field), getattr(ref["trace"], field), f"trace.{field}")
     for k in ref["fused"]:
