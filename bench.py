@@ -18,9 +18,9 @@ and in `blocks.view_with_trace`, the whole view with the traced colours
 feeding the reflection raster (this library's CUDA BVH tracer behind the
 reference's hs_optix_* entry points).
 
-A standard step is one library call per view (hs_b200_standard_view_v2, the
-same steps in the same order); --no-view-entry issues them as the session's
-separate calls instead.
+A step is one library call per view (hs_b200_standard_view_v2 or
+hs_b200_flashgs_view_v2, the same steps in the same order); --no-view-entry
+issues them as the session's separate calls instead.
 
 Both steps end with the session's raw-map postprocess of the base raster
 (standard: camera matrices and TF32 pixel rays on a side stream beside the
@@ -307,9 +307,10 @@ class Frame:
         self.tile_rows = None  # (begin, end): render only this strip of tile rows
         self.r_scene = r
         self.traced = False  # render() traces the reflection colours (enable_trace)
-        # Standard views go to the library as one call (hs_b200_standard_view_v2)
-        # unless instrumented, rendered in strips or run sequentially.
-        self.view_entry = backend == "standard" and hasattr(lib, "hs_b200_standard_view_v2")
+        # Views go to the library as one call (hs_b200_standard_view_v2,
+        # hs_b200_flashgs_view_v2) unless instrumented, rendered in strips or
+        # run sequentially.
+        self.view_entry = hasattr(lib, f"hs_b200_{backend}_view_v2")
 
     def enable_trace(self) -> float:
         """Builds the reflection trace scene of the session (the disks of the
@@ -341,13 +342,7 @@ class Frame:
         """The reflection trace of one view (hs_optix_trace_f32_v1): one ray
         per reflective Gaussian from the prepared reflection rays."""
         ops = self.ops
-        if self.backend == "standard":
-            view, proj = self.view, self.proj
-        else:
-            if getattr(self, "fg_view", None) is None or self.fg_cam is not self.cam:
-                t = lambda a: self.torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
-                self.fg_view, self.fg_proj, self.fg_cam = t(self.cam.world_view()), t(self.cam.full_proj()), self.cam
-            view, proj = self.fg_view, self.fg_proj
+        view, proj = self.view, self.proj
         return ops.trace_reflection(rays[:, 12:15].contiguous(), rays[:, 9:12].contiguous(), self.bg3, self.r_xyz,
                                     self.r_sh16, self.r_others, self.r_op_act, self.r_scale_exp, self.r_rot_unit,
                                     view, proj, self.center, degree=3, use_others=False, context=self.ctx_r)
@@ -478,10 +473,27 @@ class Frame:
         return self.view_entry and events is None and self.concurrent and self.tile_rows is None
 
     def render_one_call(self):
-        """The whole standard view as one library call (ops.standard_view):
-        the same steps as render(), in the same order, on the current stream,
-        with the camera terms on the library's side stream."""
+        """The whole view as one library call (ops.standard_view,
+        ops.flashgs_view): the same steps as render(), in the same order, on
+        the current stream (standard: the camera terms on the library's side
+        stream)."""
         torch, cam = self.torch, self.cam
+        if self.backend == "flashgs":
+            common = dict(width=cam.width, height=cam.height, camera_position=cam.flashgs_position,
+                          camera_rotation=cam.flashgs_rotation9, focal_x=cam.fx, focal_y=cam.fy,
+                          initial_pair_capacity=2_000_000)
+            names = ("positions", "shs", "colors", "opacities", "covariance", "scales", "rotations", "specular",
+                     "roughness")
+            group = dict(means3d=self.r_xyz, rotations_raw=self.r_rot_raw)
+            trace = None
+            if self.traced:
+                group.update(opacities=self.r_op_act, scales=self.r_scale_exp, rotations=self.r_rot_unit)
+                trace = dict(background=self.bg3, shs=self.r_sh16, others=self.r_others, degree=3, use_others=False)
+            out = self.ops.flashgs_view(dict(zip(names, self.b_in), **common), dict(zip(names, self.r_in), **common),
+                                        group, self.view, self.proj, self.center, base_context=self.ctx,
+                                        reflection_context=self.ctx_r, trace=trace, postprocess=self.with_post,
+                                        stream=torch.cuda.current_stream(self.device).cuda_stream)
+            return out.base, out.reflection, out.fused, out.reflection_rays, out.maps
         base = dict(means3d=self.b_xyz, opacities=self.b_op, scales=self.b_scale, rotations=self.b_rot,
                     specular=self.b_spec, roughness=self.b_rough, sh=self.b_sh)
         refl = dict(means3d=self.r_xyz, opacities=self.r_op, scales=self.r_scale, rotations=self.r_rot,
@@ -533,9 +545,10 @@ class Frame:
             # FlashGS: maps
             extra += 6 if self.backend == "standard" else 1
         if self.one_call():
-            # the one-call entry prepares the reflection in one kernel (prefix,
-            # normal column, suffix, colours); traced, the colours follow the trace
-            extra -= 0 if self.traced else 1
+            # the one-call entries prepare the reflection in one kernel (prefix,
+            # normal column, suffix and the standard colours); a traced
+            # standard view concatenates its colours after the trace
+            extra -= 0 if (self.traced and self.backend == "standard") else 1
         return 2 * per_raster + extra + 3  # + reflection prefix, suffix, fusion
 
 
@@ -908,8 +921,8 @@ def run_ours(args, workload: Workload) -> int:
                            "loop_ms_max": t["loop_ms_max"], "timed_wall_s": t["timed_wall_s"],
                            "priming": "one untimed render of each timed view before the warm-up steps",
                            "branches": "sequential v1 calls" if args.sequential else
-                                       "the whole view in one call (hs_b200_standard_view_v2: both rasters "
-                                       "concurrent, camera terms on a side stream)" if frame.one_call() else
+                                       f"the whole view in one call (hs_b200_{args.backend}_view_v2: both "
+                                       "rasters concurrent)" if frame.one_call() else
                                        "base and reflection rasters in one concurrent call "
                                        "(hs_b200_*_forward_many_v2)",
                            "stages_ms": "from a separate pass with the branches sequential, each stage alone; "

@@ -585,6 +585,75 @@ int32_t many_entry(const Args* calls, uint32_t call_count, void* stream, const c
     });
 }
 
+// The trace section shared by the one-view entries (fields of the same
+// names in HsB200StandardViewV2 and HsB200FlashgsViewV2): the checks of
+// hs_optix_trace_f32_v1 on its arguments, and the call itself.
+template <class View>
+int32_t check_view_trace(const View& v, uint64_t rays, const float* shs, const float* others, const char* what,
+                         char* error_text, uint64_t error_capacity) {
+    if (v.trace != 0 && v.trace != 1) {
+        return fail(HS_STATUS_RANGE_ERROR, std::string(what) + " trace must be 0 or 1", error_text,
+                    error_capacity);
+    }
+    if (v.trace == 0) return HS_STATUS_OK;
+    if (v.trace_coefficients == 0 || v.trace_coefficients > 16 || v.trace_degree > 3 ||
+        v.trace_coefficients < (v.trace_degree + 1) * (v.trace_degree + 1) ||
+        (v.use_others != 0 && v.use_others != 1) || v.max_trace_depth < 0 || v.max_trace_depth > 1 ||
+        !std::isfinite(v.specular_threshold) || rays > UINT32_MAX) {
+        return fail(HS_STATUS_RANGE_ERROR, "OptiX trace dimensions or scalars are invalid", error_text,
+                    error_capacity);
+    }
+    if (rays != 0 && (v.reflection_ray_origins3 == nullptr || v.reflection_ray_directions3 == nullptr ||
+                      v.trace_background3 == nullptr || shs == nullptr || others == nullptr ||
+                      v.trace_rgb3 == nullptr || v.trace_depth1 == nullptr || v.trace_acc1 == nullptr ||
+                      v.trace_normal3 == nullptr || v.trace_dist1 == nullptr || v.trace_aux2 == nullptr ||
+                      v.trace_mid32 == nullptr || v.trace_wet1 == nullptr)) {
+        return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX trace received a null non-empty buffer", error_text,
+                    error_capacity);
+    }
+    return HS_STATUS_OK;
+}
+
+// hs_optix_trace_f32_v1 of a view: scale modifier 1, start_from_first 0, the
+// rays of the view's reflection preparation (renderer.py:281-301, 385-405).
+template <class View>
+hs::TraceCall view_trace_call(const View& v, uint64_t rays, const float* means3d, const float* shs,
+                              const float* others, const float* opacities, const float* scales2,
+                              const float* rotations4, const float* view4x4, const float* proj4x4,
+                              const float* center3, cudaStream_t stream) {
+    hs::TraceCall t;
+    t.ray_count = rays;
+    t.ray_origins3 = v.reflection_ray_origins3;
+    t.ray_directions3 = v.reflection_ray_directions3;
+    t.background3 = v.trace_background3;
+    t.means3d = means3d;
+    t.shs_m3 = shs;
+    t.coefficient_count = v.trace_coefficients;
+    t.degree = v.trace_degree;
+    t.others2 = others;
+    t.opacities = opacities;
+    t.scales2 = scales2;
+    t.scale_modifier = 1.0f;
+    t.rotations4 = rotations4;
+    t.viewmatrix4x4 = view4x4;
+    t.projmatrix4x4 = proj4x4;
+    t.camera_position3 = center3;
+    t.start_from_first = 0;
+    t.max_trace_depth = v.max_trace_depth;
+    t.specular_threshold = v.specular_threshold;
+    t.use_others = v.use_others;
+    t.output_rgb3 = v.trace_rgb3;
+    t.output_depth1 = v.trace_depth1;
+    t.output_acc1 = v.trace_acc1;
+    t.output_normal3 = v.trace_normal3;
+    t.output_dist1 = v.trace_dist1;
+    t.output_aux2 = v.trace_aux2;
+    t.output_mid32 = v.trace_mid32;
+    t.output_wet1 = v.trace_wet1;
+    t.stream = stream;
+    return t;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1916,27 +1985,9 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
             return fail(HS_STATUS_INVALID_ARGUMENT, "standard view received a null required buffer", error_text,
                         error_capacity);
         }
-        if (v->trace != 0 && v->trace != 1) {
-            return fail(HS_STATUS_RANGE_ERROR, "standard view trace must be 0 or 1", error_text, error_capacity);
-        }
-        if (v->trace == 1) {
-            if (v->trace_coefficients == 0 || v->trace_coefficients > 16 || v->trace_degree > 3 ||
-                v->trace_coefficients < (v->trace_degree + 1) * (v->trace_degree + 1) ||
-                (v->use_others != 0 && v->use_others != 1) || v->max_trace_depth < 0 || v->max_trace_depth > 1 ||
-                !std::isfinite(v->specular_threshold) || nr > UINT32_MAX) {
-                return fail(HS_STATUS_RANGE_ERROR, "OptiX trace dimensions or scalars are invalid", error_text,
-                            error_capacity);
-            }
-            if (nr != 0 && (v->reflection_ray_origins3 == nullptr || v->reflection_ray_directions3 == nullptr ||
-                            v->trace_background3 == nullptr || v->reflection_shs == nullptr ||
-                            v->reflection_others2 == nullptr || v->trace_rgb3 == nullptr ||
-                            v->trace_depth1 == nullptr || v->trace_acc1 == nullptr || v->trace_normal3 == nullptr ||
-                            v->trace_dist1 == nullptr || v->trace_aux2 == nullptr || v->trace_mid32 == nullptr ||
-                            v->trace_wet1 == nullptr)) {
-                return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX trace received a null non-empty buffer", error_text,
-                            error_capacity);
-            }
-        }
+        const int32_t ts = check_view_trace(*v, nr, v->reflection_shs, v->reflection_others2, "standard view",
+                                            error_text, error_capacity);
+        if (ts != HS_STATUS_OK) return ts;
         const bool post = v->camera30 != nullptr;
         const uint64_t pixels = static_cast<uint64_t>(v->width) * static_cast<uint64_t>(v->height);
         if (post) {
@@ -2008,36 +2059,10 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
         }
         if (e != cudaSuccess) return cuda_failure(e, "standard view preparation", error_text, error_capacity);
         if (traced && nr != 0) {
-            hs::TraceCall t;
-            t.ray_count = nr;
-            t.ray_origins3 = v->reflection_ray_origins3;
-            t.ray_directions3 = v->reflection_ray_directions3;
-            t.background3 = v->trace_background3;
-            t.means3d = v->reflection.means3d;
-            t.shs_m3 = v->reflection_shs;
-            t.coefficient_count = v->trace_coefficients;
-            t.degree = v->trace_degree;
-            t.others2 = v->reflection_others2;
-            t.opacities = v->reflection.opacities;
-            t.scales2 = v->reflection.scales2;
-            t.scale_modifier = 1.0f;
-            t.rotations4 = v->reflection.rotations4;
-            t.viewmatrix4x4 = v->viewmatrix4x4;
-            t.projmatrix4x4 = v->projmatrix4x4;
-            t.camera_position3 = v->camera_position3;
-            t.start_from_first = 0;
-            t.max_trace_depth = v->max_trace_depth;
-            t.specular_threshold = v->specular_threshold;
-            t.use_others = v->use_others;
-            t.output_rgb3 = v->trace_rgb3;
-            t.output_depth1 = v->trace_depth1;
-            t.output_acc1 = v->trace_acc1;
-            t.output_normal3 = v->trace_normal3;
-            t.output_dist1 = v->trace_dist1;
-            t.output_aux2 = v->trace_aux2;
-            t.output_mid32 = v->trace_mid32;
-            t.output_wet1 = v->trace_wet1;
-            t.stream = s;
+            const hs::TraceCall t = view_trace_call(*v, nr, v->reflection.means3d, v->reflection_shs,
+                                                    v->reflection_others2, v->reflection.opacities,
+                                                    v->reflection.scales2, v->reflection.rotations4,
+                                                    v->viewmatrix4x4, v->projmatrix4x4, v->camera_position3, s);
             e = hs::trace_rays(refl, t);
             if (e != cudaSuccess) return cuda_failure(e, "reflection trace", error_text, error_capacity);
             e = hs::view::colors5(v->trace_rgb3, v->reflection.specular, v->reflection.roughness, nr,
@@ -2068,6 +2093,119 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
         const cudaError_t trailing = cudaGetLastError();
         if (trailing != cudaSuccess)
             return cuda_failure(trailing, "standard view execution", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_b200_flashgs_view_v2(const HsB200FlashgsViewV2* v, char* error_text,
+                                uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (v == nullptr || v->struct_size < sizeof(HsB200FlashgsViewV2)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "FlashGS view is null or its struct_size is too small",
+                        error_text, error_capacity);
+        }
+        const bool traced = v->trace == 1;
+        // the two raster calls, checked as the concurrent entry checks them;
+        // traced, the reflection call takes the trace's colours
+        HsB200FlashgsCallV2 refl_args = v->reflection;
+        if (traced) refl_args.colors3 = v->trace_rgb3;
+        hs::FlashgsCall calls[2];
+        int32_t cs = check_flashgs(v->base, &calls[0], error_text, error_capacity);
+        if (cs == HS_STATUS_OK) cs = check_flashgs(refl_args, &calls[1], error_text, error_capacity);
+        if (cs != HS_STATUS_OK) return cs;
+        HsRasterizerContext* contexts[2] = {v->base.handle, v->reflection.handle};
+        if (contexts[0] == contexts[1]) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "FlashGS view needs two distinct handles", error_text,
+                        error_capacity);
+        }
+        if (v->base.use_sh != 1 || v->reflection.use_sh != 0) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "FlashGS view takes the base call with SH, the reflection "
+                        "call with colours", error_text, error_capacity);
+        }
+        if (v->base.width != v->reflection.width || v->base.height != v->reflection.height ||
+            v->base.tile_row_begin != 0 || v->base.tile_row_end != UINT32_MAX ||
+            v->reflection.tile_row_begin != 0 || v->reflection.tile_row_end != UINT32_MAX) {
+            return fail(HS_STATUS_RANGE_ERROR, "FlashGS view calls must render the same whole frame", error_text,
+                        error_capacity);
+        }
+        const uint64_t nr = v->reflection.point_count;
+        if ((nr != 0 && (v->trace_means3d == nullptr || v->trace_rotation_raw4 == nullptr ||
+                         v->reflection_rotation9 == nullptr || v->reflection_normal3 == nullptr ||
+                         v->reflection_rays36 == nullptr)) ||
+            v->camera_center3 == nullptr || v->fused_rgb3 == nullptr || v->diffuse_rgb3 == nullptr ||
+            v->reflection_rgb_map3 == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "FlashGS view received a null required buffer", error_text,
+                        error_capacity);
+        }
+        const int32_t ts = check_view_trace(*v, nr, v->trace_shs, v->trace_others2, "FlashGS view", error_text,
+                                            error_capacity);
+        if (ts != HS_STATUS_OK) return ts;
+        if (traced && ((nr != 0 && (v->trace_opacities == nullptr || v->trace_scales2 == nullptr ||
+                                    v->trace_rotations4 == nullptr)) ||
+                       v->world_view4x4 == nullptr || v->full_proj4x4 == nullptr)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX trace received a null non-empty buffer", error_text,
+                        error_capacity);
+        }
+        if (v->postprocess != 0 && v->postprocess != 1) {
+            return fail(HS_STATUS_RANGE_ERROR, "FlashGS view postprocess must be 0 or 1", error_text,
+                        error_capacity);
+        }
+        if (v->postprocess == 1 && (v->world_view4x4 == nullptr || v->rgb_map3 == nullptr ||
+                                    v->acc_map == nullptr || v->dpt_map == nullptr || v->norm_map3 == nullptr ||
+                                    v->spec_map == nullptr)) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "FlashGS view postprocess received a null buffer", error_text,
+                        error_capacity);
+        }
+        // every argument is checked; only now are the handles read
+        if (contexts[0]->device != contexts[1]->device) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "FlashGS view handles must be of one device", error_text,
+                        error_capacity);
+        }
+        const int32_t ds = select_device(contexts[0], error_text, error_capacity);
+        if (ds != HS_STATUS_OK) return ds;
+        HsRasterizerContext* first = contexts[0] < contexts[1] ? contexts[0] : contexts[1];
+        HsRasterizerContext* second = contexts[0] < contexts[1] ? contexts[1] : contexts[0];
+        std::lock_guard<std::mutex> lock_first(first->mutex);
+        std::lock_guard<std::mutex> lock_second(second->mutex);
+        HsRasterizerContext* refl = contexts[1];
+        if (traced && refl->tr_triangles == 0) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX scene is not built", error_text, error_capacity);
+        }
+        const cudaStream_t s = static_cast<cudaStream_t>(v->stream);
+        // prefix, normal column, suffix and (traced) the ray split, in one pass
+        cudaError_t e = hs::precise::reflection_view(
+            v->trace_rotation_raw4, v->trace_means3d, v->camera_center3, nr, v->reflection_rotation9,
+            v->reflection_normal3, v->reflection_rays36, traced ? v->reflection_ray_origins3 : nullptr,
+            traced ? v->reflection_ray_directions3 : nullptr, nullptr, nullptr, nullptr, nullptr, s);
+        if (e != cudaSuccess) return cuda_failure(e, "FlashGS view preparation", error_text, error_capacity);
+        if (traced && nr != 0) {
+            const hs::TraceCall t = view_trace_call(*v, nr, v->trace_means3d, v->trace_shs, v->trace_others2,
+                                                    v->trace_opacities, v->trace_scales2, v->trace_rotations4,
+                                                    v->world_view4x4, v->full_proj4x4, v->camera_center3, s);
+            e = hs::trace_rays(refl, t);
+            if (e != cudaSuccess) return cuda_failure(e, "reflection trace", error_text, error_capacity);
+        }
+        // both raster calls, concurrently
+        e = hs::flashgs_forward_many(contexts, calls, 2, s);
+        if (e != cudaSuccess) return cuda_failure(e, "concurrent FlashGS forward", error_text, error_capacity);
+        // fusion from the colour planes; specular is the base call's other[0]
+        // (renderer.py:420-427)
+        const uint64_t pixels = static_cast<uint64_t>(v->base.width) * static_cast<uint64_t>(v->base.height);
+        e = hs::precise::fuse_maps_planar(v->base.output_color3, v->reflection.output_color3,
+                                          v->base.output_other2, v->diffuse_rgb3, v->fused_rgb3,
+                                          v->reflection_rgb_map3, pixels, s);
+        if (e != cudaSuccess) return cuda_failure(e, "FlashGS view fusion", error_text, error_capacity);
+        if (v->postprocess == 1) {
+            const hs::post::FlashgsMaps maps{v->rgb_map3, v->acc_map, v->dpt_map, v->norm_map3,
+                                             v->surf_norm_map3, v->dist_map, v->spec_map};
+            e = hs::post::flashgs_from_view(v->base.width, v->base.height, v->base.output_color3,
+                                            v->base.output_other2, v->base.output_depth1, v->base.output_alpha1,
+                                            v->base.output_normal3, v->world_view4x4, maps, s);
+            if (e != cudaSuccess) return cuda_failure(e, "FlashGS view postprocess", error_text, error_capacity);
+        }
+        const cudaError_t trailing = cudaGetLastError();
+        if (trailing != cudaSuccess)
+            return cuda_failure(trailing, "FlashGS view execution", error_text, error_capacity);
         return ok(error_text, error_capacity);
     });
 }

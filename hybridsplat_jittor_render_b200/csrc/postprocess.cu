@@ -144,14 +144,17 @@ __global__ void __launch_bounds__(kThreads) standard_kernel(
     }
 }
 
+// kFromView: `rotation` is the row-major world_view_transform (4 x 4) and the
+// normal rotation world_view[:3,:3]^T is read from it in place.
+template <bool kFromView>
 __global__ void __launch_bounds__(kThreads) flashgs_kernel(
     int width, int height, const float* __restrict__ color3, const float* __restrict__ other2,
     const float* __restrict__ depth1, const float* __restrict__ alpha1,
-    const float* __restrict__ normal3, const float* __restrict__ rotation9, FlashgsMaps maps) {
+    const float* __restrict__ normal3, const float* __restrict__ rotation, FlashgsMaps maps) {
     const size_t plane = static_cast<size_t>(width) * height;
     float b[9];
 #pragma unroll
-    for (int k = 0; k < 9; ++k) b[k] = rotation9[k];
+    for (int k = 0; k < 9; ++k) b[k] = kFromView ? rotation[4 * (k % 3) + k / 3] : rotation[k];
     for (size_t p = blockIdx.x * size_t(kThreads) + threadIdx.x; p < plane;
          p += size_t(gridDim.x) * kThreads) {
         const float alpha = alpha1[p];
@@ -360,8 +363,18 @@ cudaError_t flashgs(int width, int height, const float* color3, const float* oth
                     const float* rotation9, const FlashgsMaps& maps, cudaStream_t s) {
     const uint64_t pixels = static_cast<uint64_t>(width) * height;
     if (pixels == 0) return cudaSuccess;
-    flashgs_kernel<<<grid_for(pixels), kThreads, 0, s>>>(width, height, color3, other2, depth1,
-                                                         alpha1, normal3, rotation9, maps);
+    flashgs_kernel<false><<<grid_for(pixels), kThreads, 0, s>>>(width, height, color3, other2, depth1,
+                                                                alpha1, normal3, rotation9, maps);
+    return cudaGetLastError();
+}
+
+cudaError_t flashgs_from_view(int width, int height, const float* color3, const float* other2,
+                              const float* depth1, const float* alpha1, const float* normal3,
+                              const float* world_view4x4, const FlashgsMaps& maps, cudaStream_t s) {
+    const uint64_t pixels = static_cast<uint64_t>(width) * height;
+    if (pixels == 0) return cudaSuccess;
+    flashgs_kernel<true><<<grid_for(pixels), kThreads, 0, s>>>(width, height, color3, other2, depth1,
+                                                               alpha1, normal3, world_view4x4, maps);
     return cudaGetLastError();
 }
 

@@ -68,6 +68,11 @@ cudaError_t standard(int width, int height, const float* color5, const float* au
 cudaError_t flashgs(int width, int height, const float* color3, const float* other2,
                     const float* depth1, const float* alpha1, const float* normal3,
                     const float* rotation9, const FlashgsMaps& maps, cudaStream_t s);
+// flashgs() with the normal rotation world_view[:3,:3]^T read from the
+// row-major world_view_transform (_flashgs_postprocess, renderer.py:188).
+cudaError_t flashgs_from_view(int width, int height, const float* color3, const float* other2,
+                              const float* depth1, const float* alpha1, const float* normal3,
+                              const float* world_view4x4, const FlashgsMaps& maps, cudaStream_t s);
 
 }  // namespace post
 }  // namespace hs

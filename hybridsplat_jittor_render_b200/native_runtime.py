@@ -247,6 +247,29 @@ class StandardViewV2(ctypes.Structure):
     ]
 
 
+class FlashgsViewV2(ctypes.Structure):
+    """HsB200FlashgsViewV2 (include/hybridsplat_b200_ext.h)."""
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("base", FlashgsCallV2), ("reflection", FlashgsCallV2),
+        ("world_view4x4", ctypes.c_void_p), ("full_proj4x4", ctypes.c_void_p), ("camera_center3", ctypes.c_void_p),
+        ("trace_means3d", ctypes.c_void_p), ("trace_rotation_raw4", ctypes.c_void_p),
+        ("reflection_rotation9", ctypes.c_void_p), ("reflection_normal3", ctypes.c_void_p),
+        ("reflection_rays36", ctypes.c_void_p), ("reflection_ray_origins3", ctypes.c_void_p),
+        ("reflection_ray_directions3", ctypes.c_void_p), ("trace", ctypes.c_int32),
+        ("trace_background3", ctypes.c_void_p), ("trace_shs", ctypes.c_void_p),
+        ("trace_coefficients", ctypes.c_uint32), ("trace_degree", ctypes.c_uint32),
+        ("trace_others2", ctypes.c_void_p), ("trace_opacities", ctypes.c_void_p), ("trace_scales2", ctypes.c_void_p),
+        ("trace_rotations4", ctypes.c_void_p), ("use_others", ctypes.c_int32), ("max_trace_depth", ctypes.c_int32),
+        ("specular_threshold", ctypes.c_float), ("trace_rgb3", ctypes.c_void_p), ("trace_depth1", ctypes.c_void_p),
+        ("trace_acc1", ctypes.c_void_p), ("trace_normal3", ctypes.c_void_p), ("trace_dist1", ctypes.c_void_p),
+        ("trace_aux2", ctypes.c_void_p), ("trace_mid32", ctypes.c_void_p), ("trace_wet1", ctypes.c_void_p),
+        ("fused_rgb3", ctypes.c_void_p), ("diffuse_rgb3", ctypes.c_void_p), ("reflection_rgb_map3", ctypes.c_void_p),
+        ("postprocess", ctypes.c_int32), ("rgb_map3", ctypes.c_void_p), ("acc_map", ctypes.c_void_p),
+        ("dpt_map", ctypes.c_void_p), ("norm_map3", ctypes.c_void_p), ("surf_norm_map3", ctypes.c_void_p),
+        ("dist_map", ctypes.c_void_p), ("spec_map", ctypes.c_void_p), ("stream", ctypes.c_void_p),
+    ]
+
+
 EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "hs_b200_precise_sh_colors5_f32_v1": (_I32, [_V, _U32, _U32, _V, _V, _V, _V, _U64, _V, *_ERR]),
     "hs_b200_precise_fuse_maps_planar_f32_v1": (_I32, [_V, _V, _V, _V, _V, _V, _U64, *_ERR]),
@@ -261,6 +284,7 @@ EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "hs_b200_flashgs_forward_many_v2": (_I32, [ctypes.POINTER(FlashgsCallV2), _U32, _V, *_ERR]),
     "hs_b200_rasterizer_forward_many_v2": (_I32, [ctypes.POINTER(RasterizerCallV2), _U32, _V, *_ERR]),
     "hs_b200_standard_view_v2": (_I32, [ctypes.POINTER(StandardViewV2), *_ERR]),
+    "hs_b200_flashgs_view_v2": (_I32, [ctypes.POINTER(FlashgsViewV2), *_ERR]),
     "hs_b200_test_stall_lookback_v1": (_I32, [_V, _U32, *_ERR]),
     "hs_b200_comm_unique_id_v1": (_I32, [_V, *_ERR]),
     "hs_b200_comm_create_v1": (_I32, [_I32, _I32, _I32, _V, ctypes.c_double, ctypes.POINTER(ctypes.c_void_p),

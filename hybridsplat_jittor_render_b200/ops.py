@@ -985,3 +985,124 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
     check_status(status, "hs_b200_standard_view_v2", error)
     return StandardViewOutputs(out_b, out_r, base_colors, refl_colors, rotation, normal, rays, origins, directions,
                                traced, fused, camera, maps)
+
+
+class FlashgsViewOutputs(NamedTuple):
+    """Everything flashgs_view writes (the FlashGS counterpart of
+    StandardViewOutputs; no raster colours are formed, the base call shades
+    with SH and the reflection call takes the trace's or the given colours)."""
+    base: FlashgsOutputs
+    reflection: FlashgsOutputs
+    reflection_rotation: torch.Tensor
+    reflection_normal: torch.Tensor
+    reflection_rays: torch.Tensor
+    ray_origins: torch.Tensor | None
+    ray_directions: torch.Tensor | None
+    trace: TraceOutputs | None
+    fused: dict[str, torch.Tensor]
+    maps: dict[str, torch.Tensor] | None
+
+
+FLASHGS_MAPS = ("rgb_map", "acc_map", "dpt_map", "norm_map", "surf_norm_map", "dist_map", "spec_map")
+FLASHGS_MAP_CHANNELS = (3, 1, 1, 3, 3, 1, 1)
+
+
+def flashgs_view(base: dict[str, Any], reflection: dict[str, Any], trace_group: dict[str, torch.Tensor],
+                 world_view: torch.Tensor, full_proj: torch.Tensor, camera_center: torch.Tensor, *,
+                 base_context: NativeRendererContext, reflection_context: NativeRendererContext,
+                 trace: dict[str, Any] | None = None, postprocess: bool = False,
+                 stream: int | None = None) -> FlashgsViewOutputs:
+    """One view of the FlashGS session (render_hybridsplat_flashgs_view,
+    renderer.py:344-446, with _flashgs_postprocess) in one call
+    (hs_b200_flashgs_view_v2).
+
+    ``base`` and ``reflection`` hold the arguments of flashgs_forward by name
+    (no ``context``); the base call shades with SH (``use_sh=True``), the
+    reflection call takes ``colors`` unless traced. ``trace_group`` is the
+    standard-activated reflection group the session traces: ``means3d``,
+    ``rotations_raw`` and, when traced, ``opacities``, ``scales``,
+    ``rotations``. ``trace`` as in standard_view (``background``, ``shs``,
+    ``others``, ``degree``, optional ``use_others``, ``max_trace_depth``,
+    ``specular_threshold``); ``world_view``, ``full_proj`` and
+    ``camera_center`` are the view's device camera. ``postprocess`` adds the
+    FlashGS raw maps. Every output equals that of the same steps called one by
+    one.
+    """
+    if base_context is reflection_context:
+        raise ValueError("flashgs_view needs two distinct contexts")
+    _check_tensor("world_view", world_view, (4, 4))
+    _check_tensor("full_proj", full_proj, (4, 4))
+    _check_tensor("camera_center", camera_center, (3,))
+    device = world_view.device
+    f = dict(dtype=torch.float32, device=device)
+    nr = int(reflection["positions"].shape[0])
+    _check_tensor("trace means3d", trace_group["means3d"], (nr, 3))
+    _check_tensor("trace rotations_raw", trace_group["rotations_raw"], (nr, 4))
+    traced = None
+    reflection = dict(reflection)
+    if trace is not None:
+        traced = TraceOutputs(torch.empty((nr, 3), **f), torch.empty((nr, 1), **f), torch.empty((nr, 1), **f),
+                              torch.empty((nr, 3), **f), torch.empty((nr, 1), **f), torch.empty((nr, 2), **f),
+                              torch.empty((nr, 32), **f), torch.empty((nr, 1), **f))
+        reflection["colors"] = traced.rgb
+    named_b, out_b, hold_b = _flashgs_arguments(**dict(base, use_sh=True))
+    named_r, out_r, hold_r = _flashgs_arguments(**dict(reflection, use_sh=False))
+    whole = _rows_fields(None)
+    rotation, normal, rays = torch.empty((nr, 3, 3), **f), torch.empty((nr, 3), **f), torch.empty((nr, 36), **f)
+    origins = directions = None
+    h, w = int(named_b["height"]), int(named_b["width"])
+    fused = {k: torch.empty((h, w, 3), **f) for k in ("rgb_map", "dif_rgb_map", "ref_rgb_map")}
+    view = native_runtime.FlashgsViewV2(
+        struct_size=ctypes.sizeof(native_runtime.FlashgsViewV2),
+        base=native_runtime.FlashgsCallV2(handle=base_context.handle, **named_b, **whole),
+        reflection=native_runtime.FlashgsCallV2(handle=reflection_context.handle, **named_r, **whole),
+        world_view4x4=_ptr(world_view), full_proj4x4=_ptr(full_proj), camera_center3=_ptr(camera_center),
+        trace_means3d=_ptr(trace_group["means3d"]), trace_rotation_raw4=_ptr(trace_group["rotations_raw"]),
+        reflection_rotation9=_ptr(rotation), reflection_normal3=_ptr(normal), reflection_rays36=_ptr(rays),
+        fused_rgb3=_ptr(fused["rgb_map"]), diffuse_rgb3=_ptr(fused["dif_rgb_map"]),
+        reflection_rgb_map3=_ptr(fused["ref_rgb_map"]), stream=stream)
+    if trace is not None:
+        shs = trace["shs"]
+        coefficients = int(shs.shape[1])
+        for name, t, shape in (("trace background", trace["background"], (3,)),
+                               ("trace shs", shs, (nr, coefficients, 3)), ("trace others", trace["others"], (nr, 2)),
+                               ("trace opacities", trace_group["opacities"], (nr, 1)),
+                               ("trace scales", trace_group["scales"], (nr, 2)),
+                               ("trace rotations", trace_group["rotations"], (nr, 4))):
+            _check_tensor(name, t, shape)
+        degree = trace["degree"]
+        if isinstance(degree, bool) or not isinstance(degree, int) or degree not in range(4):
+            raise ValueError("degree must be an integer in [0, 3]")
+        depth = trace.get("max_trace_depth", 0)
+        if depth not in (0, 1) or isinstance(depth, bool):
+            raise ValueError("max_trace_depth must be 0 or 1")
+        origins, directions = torch.empty((nr, 3), **f), torch.empty((nr, 3), **f)
+        view.reflection_ray_origins3 = _ptr(origins)
+        view.reflection_ray_directions3 = _ptr(directions)
+        view.trace = 1
+        view.trace_background3 = _ptr(trace["background"])
+        view.trace_shs = _ptr(shs)
+        view.trace_coefficients = coefficients
+        view.trace_degree = degree
+        view.trace_others2 = _ptr(trace["others"])
+        view.trace_opacities = _ptr(trace_group["opacities"])
+        view.trace_scales2 = _ptr(trace_group["scales"])
+        view.trace_rotations4 = _ptr(trace_group["rotations"])
+        view.use_others = int(bool(trace.get("use_others", True)))
+        view.max_trace_depth = int(depth)
+        view.specular_threshold = _finite("specular_threshold", trace.get("specular_threshold", 0.0))
+        for field, t in zip(("trace_rgb3", "trace_depth1", "trace_acc1", "trace_normal3", "trace_dist1",
+                             "trace_aux2", "trace_mid32", "trace_wet1"), traced):
+            setattr(view, field, _ptr(t))
+    maps = None
+    if postprocess:
+        maps = {n: torch.empty((1, h * w, c), **f) for n, c in zip(FLASHGS_MAPS, FLASHGS_MAP_CHANNELS)}
+        view.postprocess = 1
+        for field, name in zip(("rgb_map3", "acc_map", "dpt_map", "norm_map3", "surf_norm_map3", "dist_map",
+                                "spec_map"), FLASHGS_MAPS):
+            setattr(view, field, _ptr(maps[name]))
+    error = error_buffer()
+    status = base_context.library.hs_b200_flashgs_view_v2(ctypes.byref(view), error, len(error))
+    del hold_b, hold_r
+    check_status(status, "hs_b200_flashgs_view_v2", error)
+    return FlashgsViewOutputs(out_b, out_r, rotation, normal, rays, origins, directions, traced, fused, maps)

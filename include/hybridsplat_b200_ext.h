@@ -304,6 +304,82 @@ typedef struct HsB200StandardViewV2 {
 HS_API int32_t hs_b200_standard_view_v2(
     const HsB200StandardViewV2* view, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
 
+/* ---- one whole FlashGS view in one call ----
+ *
+ * The session's per-view sequence of the FlashGS backend
+ * (render_hybridsplat_flashgs_view, renderer.py:344-446, with
+ * _flashgs_postprocess, renderer.py:176-202) as one entry point, on `stream`
+ * (NULL = the legacy default stream): the reflection preparation from the
+ * trace group (the standard-activated reflection Gaussians the session traces),
+ * the reflection trace (optional: on reflection.handle's built scene; its
+ * colours then feed the reflection raster) or given reflection colours, the
+ * base (use_sh = 1) and reflection (use_sh = 0) FlashGS calls run
+ * concurrently (as hs_b200_flashgs_forward_many_v2), the fusion from the
+ * raster calls' colour planes and (optional) the FlashGS raw-map
+ * postprocess. Every output equals that of the same steps called one by one.
+ * The host waits once per raster call for its pair count, as the v1 calls do.
+ * Device buffers, except the FlashGS calls' host camera values. No
+ * counterpart in the reference library. */
+typedef struct HsB200FlashgsViewV2 {
+    uint32_t struct_size;                  /* sizeof(HsB200FlashgsViewV2) */
+    HsB200FlashgsCallV2 base;              /* use_sh = 1; tile rows must be the whole frame */
+    HsB200FlashgsCallV2 reflection;        /* use_sh = 0; colors3 is ignored when trace == 1 */
+    const float* world_view4x4;            /* device world_view_transform (trace, postprocess) */
+    const float* full_proj4x4;             /* device full_proj_transform (trace) */
+    const float* camera_center3;           /* device camera centre (reflection rays, trace) */
+    /* the trace group, reflection.point_count Gaussians: xyz [R,3], raw
+     * quaternions [R,4]; the preparation writes prefix [R,9], normal column
+     * [R,3], suffix [R,36] and, with trace == 1, the ray origins and
+     * directions [R,3] */
+    const float* trace_means3d;
+    const float* trace_rotation_raw4;
+    float* reflection_rotation9;
+    float* reflection_normal3;
+    float* reflection_rays36;
+    float* reflection_ray_origins3;
+    float* reflection_ray_directions3;
+    /* trace == 1: hs_optix_trace_f32_v1 of the trace group (scale modifier 1,
+     * start_from_first 0); trace_rgb3 becomes the reflection call's colours */
+    int32_t trace;
+    const float* trace_background3;
+    const float* trace_shs;                /* [R,coefficients,3] */
+    uint32_t trace_coefficients;
+    uint32_t trace_degree;
+    const float* trace_others2;            /* [R,2]; read when use_others */
+    const float* trace_opacities;          /* [R,1] activated */
+    const float* trace_scales2;            /* [R,2] activated */
+    const float* trace_rotations4;         /* [R,4] normalised */
+    int32_t use_others;
+    int32_t max_trace_depth;
+    float specular_threshold;
+    float* trace_rgb3;
+    float* trace_depth1;
+    float* trace_acc1;
+    float* trace_normal3;
+    float* trace_dist1;
+    float* trace_aux2;
+    float* trace_mid32;
+    float* trace_wet1;
+    /* fusion: [H*W,3] each */
+    float* fused_rgb3;
+    float* diffuse_rgb3;
+    float* reflection_rgb_map3;
+    /* postprocess == 1: hs_b200_flashgs_postprocess_f32_v1 of the base call
+     * with the normal rotation world_view[:3,:3]^T; maps [H*W,C] */
+    int32_t postprocess;
+    float* rgb_map3;
+    float* acc_map;
+    float* dpt_map;
+    float* norm_map3;
+    float* surf_norm_map3;
+    float* dist_map;
+    float* spec_map;
+    void* stream;
+} HsB200FlashgsViewV2;
+
+HS_API int32_t hs_b200_flashgs_view_v2(
+    const HsB200FlashgsViewV2* view, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
 /* The standard branch's colours in one pass: hs_rasterizer_precise_direction_f32_v1
  * of points[count,3] from center3, hs_rasterizer_precise_sh_to_rgb_f32_v1 of
  * sh[count,3,coefficient_count] (channel-major, as the reference passes its

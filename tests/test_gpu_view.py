@@ -173,3 +173,112 @@ def test_view_needs_a_built_scene_and_two_contexts():
         # the context stays usable
         ops.standard_view(*args, base_context=ctx, reflection_context=ctx_r, **kw)
         torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------- FlashGS views
+
+
+def make_flashgs_view(spec, cam, *, empty_reflection=False):
+    scene = scenes.make_scene(spec)
+    b, r = scene["base"], scene["reflection"]
+    if empty_reflection:
+        r = {k: v[:0] for k, v in r.items()}
+    nb, nr = b["xyz"].shape[0], r["xyz"].shape[0]
+
+    def flashgs_inputs(g, n, colors):
+        prep = ops.flashgs_prepare_host(g["opacity"], g["scaling"], g["rotation"], g["specular"], g["roughness"])
+        return {"positions": dev(g["xyz"]), "shs": dev(scenes.sh_features(g).reshape(n, 48)), "colors": dev(colors),
+                "opacities": dev(prep["opacity"]), "covariance": dev(prep["covariance"]),
+                "scales": dev(prep["scaling"]), "rotations": dev(prep["rotation"]),
+                "specular": dev(prep["specular"]), "roughness": dev(prep["roughness"])}
+
+    cam_args = dict(width=cam.width, height=cam.height, camera_position=cam.flashgs_position,
+                    camera_rotation=cam.flashgs_rotation9, focal_x=cam.fx, focal_y=cam.fy)
+    rgb = np.random.default_rng(6).random((nr, 3), dtype=np.float32)
+    base = dict(flashgs_inputs(b, nb, np.zeros((nb, 3), np.float32)), **cam_args)
+    refl = dict(flashgs_inputs(r, nr, rgb), **cam_args)
+    # the standard-activated reflection group the session traces
+    group = {"means3d": dev(r["xyz"]), "rotations_raw": dev(r["rotation"]),
+             "opacities": ops.precise_sigmoid(dev(r["opacity"])), "scales": ops.precise_exp(dev(r["scaling"])),
+             "rotations": ops.precise_normalize4(dev(r["rotation"]))}
+    others = torch.cat([ops.precise_sigmoid(dev(r["specular"])), ops.precise_sigmoid(dev(r["roughness"]))],
+                       1).contiguous()
+    trace = {"background": torch.zeros(3, device="cuda"), "shs": dev(scenes.sh_features(r)), "others": others,
+             "degree": 3, "use_others": False}
+    camera = {"world_view": dev(cam.world_view()), "full_proj": dev(cam.full_proj()),
+              "camera_center": dev(scenes.standard_camera_center(cam))}
+    return base, refl, group, trace, camera
+
+
+def flashgs_steps(base, refl, group, trace, camera, ctx, ctx_r, traced):
+    view, proj, center = camera["world_view"], camera["full_proj"], camera["camera_center"]
+    b_out = ops.flashgs_forward(**base, use_sh=True, context=ctx)
+    rot = ops.precise_reflection_prefix(group["rotations_raw"])
+    normal = rot[:, :, 2].contiguous()
+    rays = ops.precise_reflection_suffix(group["means3d"], center, normal)
+    traced_out = None
+    refl = dict(refl)
+    if traced:
+        traced_out = ops.trace_reflection(rays[:, 12:15].contiguous(), rays[:, 9:12].contiguous(), trace["background"],
+                                          group["means3d"], trace["shs"], trace["others"], group["opacities"],
+                                          group["scales"], group["rotations"], view, proj, center, degree=3,
+                                          use_others=False, context=ctx_r)
+        refl["colors"] = traced_out.rgb
+    r_out = ops.flashgs_forward(**refl, use_sh=False, context=ctx_r)
+    fused = ops.precise_fuse_maps_planar(b_out.color, r_out.color, b_out.other[0:1].contiguous())
+    maps = ops.flashgs_postprocess(b_out, view[:3, :3].t().contiguous())
+    return dict(base=b_out, reflection=r_out, rotation=rot, normal=normal, rays=rays, trace=traced_out,
+                fused=fused, maps=maps)
+
+
+def run_flashgs_view(spec, cam, *, traced, empty_reflection=False, torch_stream=None):
+    base, refl, group, trace, camera = make_flashgs_view(spec, cam, empty_reflection=empty_reflection)
+    with NativeRendererContext(0) as ctx, NativeRendererContext(0) as ctx_r:
+        if traced:
+            v, t = ops.gaussian_disks(group["means3d"], group["rotations_raw"], group["scales"])
+            ops.build_trace_scene(v, t, scene_signature=1, context=ctx_r)
+        ref = flashgs_steps(base, refl, group, trace, camera, ctx, ctx_r, traced)
+        torch.cuda.synchronize()
+        stream = torch_stream or torch.cuda.current_stream()
+        with torch.cuda.stream(stream):
+            one = ops.flashgs_view(base, refl, group, camera["world_view"], camera["full_proj"],
+                                   camera["camera_center"], base_context=ctx, reflection_context=ctx_r,
+                                   trace=trace if traced else None, postprocess=True,
+                                   stream=stream.cuda_stream if torch_stream is not None else None)
+        torch.cuda.synchronize()
+    for name in ("base", "reflection"):
+        for field in ops.FlashgsOutputs._fields:
+            bits(getattr(getattr(one, name), field), getattr(ref[name], field), f"{name}.{field}")
+    bits(one.reflection_rotation, ref["rotation"], "reflection rotation")
+    bits(one.reflection_normal, ref["normal"], "reflection normal")
+    bits(one.reflection_rays, ref["rays"], "reflection rays")
+    if traced:
+        bits(one.ray_origins, ref["rays"][:, 12:15], "ray origins")
+        bits(one.ray_directions, ref["rays"][:, 9:12], "ray directions")
+        for field in ops.TraceOutputs._fields:
+            bits(getattr(one.trace, field), getattr(ref["trace"], field), f"trace.{field}")
+    for k in ref["fused"]:
+        bits(one.fused[k], ref["fused"][k], k)
+    for k in ops.FLASHGS_MAPS:
+        bits(one.maps[k], ref["maps"][k], k)
+    return one
+
+
+@pytest.mark.parametrize("traced", [False, True])
+def test_flashgs_view_matches_the_steps(traced):
+    run_flashgs_view(SMALL, scenes.generic_camera(SMALL, 1), traced=traced)
+
+
+def test_flashgs_view_on_a_torch_stream():
+    run_flashgs_view(SMALL, scenes.generic_camera(SMALL, 3), traced=True, torch_stream=torch.cuda.Stream())
+
+
+def test_flashgs_view_with_no_reflective_gaussians():
+    one = run_flashgs_view(SMALL, scenes.generic_camera(SMALL, 2), traced=False, empty_reflection=True)
+    assert one.reflection_rays.shape == (0, 36) and int(one.reflection.rendered[0]) == 0
+
+
+def test_flashgs_view_benchmark_frame():
+    """The FlashGS benchmark frame (1M + 200k, 1292x839, orbit view 7),
+    reflection colours traced."""
+    run_flashgs_view("flashgs_1m", scenes.orbit_camera("flashgs_1m", 7), traced=True)

@@ -24,10 +24,11 @@ EXT_HEADER = REPO / "include" / "hybridsplat_b200_ext.h"
 C_TYPES = {
     "HsRasterizerHandle": ctypes.c_void_p, "uint64_t": ctypes.c_uint64, "int32_t": ctypes.c_int32,
     "uint32_t": ctypes.c_uint32, "float": ctypes.c_float, "double": ctypes.c_double,
-    "HsB200StandardGroupV2": nr.StandardGroupV2,
+    "HsB200StandardGroupV2": nr.StandardGroupV2, "HsB200FlashgsCallV2": nr.FlashgsCallV2,
 }
 MIRRORS = [("HsB200FlashgsCallV2", nr.FlashgsCallV2), ("HsB200RasterizerCallV2", nr.RasterizerCallV2),
-           ("HsB200StandardGroupV2", nr.StandardGroupV2), ("HsB200StandardViewV2", nr.StandardViewV2)]
+           ("HsB200StandardGroupV2", nr.StandardGroupV2), ("HsB200StandardViewV2", nr.StandardViewV2),
+           ("HsB200FlashgsViewV2", nr.FlashgsViewV2)]
 
 
 def header_struct(name: str) -> list[tuple[str, object]]:
@@ -196,3 +197,50 @@ def test_view_checks_every_argument_before_the_handles(lib, over, expected):
 
 def test_view_null(lib):
     assert _view(lib, None) == (1, "standard view is null or its struct_size is too small")
+
+
+def _flashgs_view_struct(keep, **over):
+    base, hold_b = _flashgs_struct(use_sh=1)
+    refl, hold_r = _flashgs_struct(handle=32, use_sh=0)
+    keep += [hold_b, hold_r]
+    dummy = 16
+    v = nr.FlashgsViewV2(struct_size=ctypes.sizeof(nr.FlashgsViewV2), base=base, reflection=refl,
+                         camera_center3=dummy, fused_rgb3=dummy, diffuse_rgb3=dummy, reflection_rgb_map3=dummy)
+    for k, val in over.items():
+        if "." in k:
+            outer, inner = k.split(".")
+            setattr(getattr(v, outer), inner, val)
+        else:
+            setattr(v, k, val)
+    return v
+
+
+def _flashgs_view(lib, v):
+    err = ctypes.create_string_buffer(512)
+    status = lib.hs_b200_flashgs_view_v2(None if v is None else ctypes.byref(v), err, len(err))
+    return status, err.value.decode()
+
+
+@pytest.mark.parametrize("over,expected", [
+    (dict(struct_size=8), (1, "FlashGS view is null or its struct_size is too small")),
+    (dict(**{"base.handle": None}), (1, "FlashGS received a null required handle or buffer")),
+    (dict(**{"reflection.width": 0}), (3, "FlashGS dimensions or scalar arguments are invalid")),
+    (dict(**{"reflection.handle": 16}), (1, "FlashGS view needs two distinct handles")),
+    (dict(**{"base.use_sh": 0}), (1, "FlashGS view takes the base call with SH, the reflection call with colours")),
+    (dict(**{"reflection.width": 32}), (3, "FlashGS view calls must render the same whole frame")),
+    (dict(**{"base.tile_row_end": 2}), (3, "FlashGS view calls must render the same whole frame")),
+    (dict(camera_center3=None), (1, "FlashGS view received a null required buffer")),
+    (dict(trace=3), (3, "FlashGS view trace must be 0 or 1")),
+    (dict(trace=1, trace_coefficients=9, trace_degree=3), (3, "OptiX trace dimensions or scalars are invalid")),
+    (dict(trace=1, trace_coefficients=16, trace_degree=3, **{"reflection.colors3": 16}),
+     (1, "OptiX trace received a null non-empty buffer")),
+    (dict(postprocess=2), (3, "FlashGS view postprocess must be 0 or 1")),
+    (dict(postprocess=1), (1, "FlashGS view postprocess received a null buffer")),
+])
+def test_flashgs_view_checks_every_argument_before_the_handles(lib, over, expected):
+    keep = []
+    assert _flashgs_view(lib, _flashgs_view_struct(keep, **over)) == expected
+
+
+def test_flashgs_view_null(lib):
+    assert _flashgs_view(lib, None) == (1, "FlashGS view is null or its struct_size is too small")
