@@ -116,8 +116,9 @@ def parse_args():
     p.add_argument("--no-reference-gpu", action="store_true", help="skip timing the reference CUDA rebuild")
     p.add_argument("--no-blocks", action="store_true",
                    help="skip the flashgs / large_6m / stress_4k blocks of the default run")
-    p.add_argument("--readback", choices=("after-call", "before-call"), default="after-call",
-                   help="e2e: queue frame s-1's map read-back before or after frame s's raster calls")
+    p.add_argument("--readback", choices=("at-raster", "after-call", "before-call"), default="after-call",
+                   help="e2e: queue frame s-1's map read-back before or after frame s's raster calls, or after "
+                        "them to start when frame s's renderers may start (one-call views)")
     p.add_argument("--scale", type=float, default=1.0, help="Gaussian-count scale (profiling runs only)")
     p.add_argument("--profile-frames", type=int, default=0,
                    help="render this many frames untimed and exit (a short, fixed launch sequence for ncu)")
@@ -311,6 +312,7 @@ class Frame:
         # hs_b200_flashgs_view_v2) unless instrumented, rendered in strips or
         # run sequentially.
         self.view_entry = hasattr(lib, f"hs_b200_{backend}_view_v2")
+        self.raster_event = None  # one-call views record it when their renderers may start
 
     def enable_trace(self) -> float:
         """Builds the reflection trace scene of the session (the disks of the
@@ -492,7 +494,8 @@ class Frame:
             out = self.ops.flashgs_view(dict(zip(names, self.b_in), **common), dict(zip(names, self.r_in), **common),
                                         group, self.view, self.proj, self.center, base_context=self.ctx,
                                         reflection_context=self.ctx_r, trace=trace, postprocess=self.with_post,
-                                        stream=torch.cuda.current_stream(self.device).cuda_stream)
+                                        stream=torch.cuda.current_stream(self.device).cuda_stream,
+                                        raster_begin_event=self.raster_event)
             return out.base, out.reflection, out.fused, out.reflection_rays, out.maps
         base = dict(means3d=self.b_xyz, opacities=self.b_op, scales=self.b_scale, rotations=self.b_rot,
                     specular=self.b_spec, roughness=self.b_rough, sh=self.b_sh)
@@ -508,7 +511,8 @@ class Frame:
                                      height=cam.height, tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy, sh_degree=3,
                                      base_context=self.ctx, reflection_context=self.ctx_r, trace=trace,
                                      postprocess=post,
-                                     stream=torch.cuda.current_stream(self.device).cuda_stream)
+                                     stream=torch.cuda.current_stream(self.device).cuda_stream,
+                                     raster_begin_event=self.raster_event)
         return out.base, out.reflection, out.fused, out.reflection_rays, out.maps
 
     def maps_for_host(self, result):
@@ -1010,8 +1014,13 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
     h2d = pinned_cam[0].numel() * 4  # the camera row: view, projection, centre
     copy_stream = torch.cuda.Stream(device=frame.device)
 
+    at_raster = args.readback == "at-raster" and frame.one_call()
+    raster_events = [torch.cuda.Event() for _ in range(2)] if at_raster else None
+
     def read_back(s, out, done):
         copy_stream.wait_event(done)
+        if at_raster:  # frame s + 1's binning is done: its renderers take the link's traffic best
+            copy_stream.wait_event(raster_events[(s + 1) % 2])
         with torch.cuda.stream(copy_stream):
             for dst, src in zip(host_maps[s % 2], frame.maps_for_host(out)):
                 dst.copy_(src, non_blocking=True)
@@ -1024,6 +1033,8 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
                 read_back(*pending)
                 pending = None
             frame.set_camera(cams[s], upload_from=pinned_cam[s])
+            if at_raster:
+                frame.raster_event = raster_events[s % 2]
             out = frame.render()
             done = torch.cuda.Event()
             done.record(stream)
@@ -1048,6 +1059,7 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
         e1.record(stream)
         torch.cuda.synchronize()
         loops.append(e0.elapsed_time(e1) / args.steps)
+    frame.raster_event = None
     job.barrier()
     e2e_ms = job.max(float(statistics.median(loops)))[0]
     # The host-link ceiling: the same read-back alone (last frame's maps, same
@@ -1070,6 +1082,8 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
     return {"value": value, "unit": "frames/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "overlap": ("maps of frame s-1 copied to pinned host memory on a copy stream queued before frame s's "
                         "raster calls" if args.readback == "before-call" else
+                        "maps of frame s-1 copied on a copy stream once frame s's binning is done and its "
+                        "renderers may start" if at_raster else
                         "maps of frame s-1 copied on a copy stream queued after frame s's raster calls return"),
             "statistic": "median of 5 loops of exactly --steps steps, max over ranks",
             "d2h_ms_alone": d2h_worst, "d2h_gbs_alone_per_gpu": d2h / (d2h_worst * 1e6),

@@ -2070,7 +2070,7 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
             if (e != cudaSuccess) return cuda_failure(e, "standard view colours", error_text, error_capacity);
         }
         // both raster calls, concurrently
-        e = hs::standard_forward_many(contexts, calls, 2, s);
+        e = hs::standard_forward_many(contexts, calls, 2, s, static_cast<cudaEvent_t>(v->raster_begin_event));
         if (e != cudaSuccess) return cuda_failure(e, "concurrent five-channel rasterizer forward", error_text,
                                                   error_capacity);
         // fusion from the colour planes (renderer.py:326, math.py:301-311)
@@ -2186,7 +2186,7 @@ int32_t hs_b200_flashgs_view_v2(const HsB200FlashgsViewV2* v, char* error_text,
             if (e != cudaSuccess) return cuda_failure(e, "reflection trace", error_text, error_capacity);
         }
         // both raster calls, concurrently
-        e = hs::flashgs_forward_many(contexts, calls, 2, s);
+        e = hs::flashgs_forward_many(contexts, calls, 2, s, static_cast<cudaEvent_t>(v->raster_begin_event));
         if (e != cudaSuccess) return cuda_failure(e, "concurrent FlashGS forward", error_text, error_capacity);
         // fusion from the colour planes; specular is the base call's other[0]
         // (renderer.py:420-427)
@@ -2215,7 +2215,10 @@ int32_t hs_b200_flashgs_forward_many_v2(const HsB200FlashgsCallV2* calls, uint32
                                         uint64_t error_capacity) noexcept {
     return many_entry<HsB200FlashgsCallV2, hs::FlashgsCall>(
         calls, call_count, stream, "concurrent FlashGS forward", check_flashgs,
-        hs::flashgs_forward_many, error_text, error_capacity);
+        [](HsRasterizerContext* const* c, const hs::FlashgsCall* k, uint32_t n, cudaStream_t st) {
+            return hs::flashgs_forward_many(c, k, n, st);
+        },
+        error_text, error_capacity);
 }
 
 int32_t hs_b200_rasterizer_forward_many_v2(const HsB200RasterizerCallV2* calls,
@@ -2223,7 +2226,10 @@ int32_t hs_b200_rasterizer_forward_many_v2(const HsB200RasterizerCallV2* calls,
                                            uint64_t error_capacity) noexcept {
     return many_entry<HsB200RasterizerCallV2, hs::StandardCall>(
         calls, call_count, stream, "concurrent five-channel rasterizer forward", check_rasterizer,
-        hs::standard_forward_many, error_text, error_capacity);
+        [](HsRasterizerContext* const* c, const hs::StandardCall* k, uint32_t n, cudaStream_t st) {
+            return hs::standard_forward_many(c, k, n, st);
+        },
+        error_text, error_capacity);
 }
 
 }  // extern "C"

@@ -23,9 +23,11 @@
 
 namespace hs {
 
+// raster_begin (optional) is recorded when every call's binning is done and
+// the renderers may start, for callers that time other traffic around them.
 template <class Pass, class Call>
 cudaError_t run_many(HsRasterizerContext* const* contexts, const Call* calls, uint32_t count,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, cudaEvent_t raster_begin = nullptr) {
     if (count == 0) return cudaSuccess;
     for (uint32_t i = 0; i < count; ++i) {
         const cudaError_t st = ensure_side_stream(contexts[i]);
@@ -57,6 +59,9 @@ cudaError_t run_many(HsRasterizerContext* const* contexts, const Call* calls, ui
             }
         }
     }
+    // contexts[0]'s side stream has waited for every call's binning
+    if (st == cudaSuccess && raster_begin != nullptr)
+        st = cudaEventRecord(raster_begin, contexts[0]->side_stream);
     for (auto& p : passes)
         if (st == cudaSuccess) st = p->render();
     for (auto& p : passes)

@@ -259,8 +259,10 @@ cudaError_t flashgs_forward(HsRasterizerContext* context, const FlashgsCall& cal
 // stages are queued before any tile renderer, and `stream` (the caller's)
 // is ordered before and after all of them. Each call's stream field is
 // ignored. Outputs are identical to flashgs_forward of each call.
+// raster_begin, when given, is recorded once all binning is done, before the
+// tile renderers.
 cudaError_t flashgs_forward_many(HsRasterizerContext* const* contexts, const FlashgsCall* calls,
-                                 uint32_t count, cudaStream_t stream);
+                                 uint32_t count, cudaStream_t stream, cudaEvent_t raster_begin = nullptr);
 
 cudaError_t flashgs_debug_copy(HsRasterizerContext* context, uint64_t point_capacity,
                                uint64_t pair_capacity, uint64_t tile_capacity,
@@ -281,7 +283,7 @@ cudaError_t standard_forward(HsRasterizerContext* context, const StandardCall& c
 // Independent standard calls run as flashgs_forward_many runs FlashGS calls.
 cudaError_t standard_forward_many(HsRasterizerContext* const* contexts,
                                   const StandardCall* calls, uint32_t count,
-                                  cudaStream_t stream);
+                                  cudaStream_t stream, cudaEvent_t raster_begin = nullptr);
 
 // Arguments of one hs_optix_trace_f32_v1 call (device pointers; checked by
 // the entry point).

@@ -389,8 +389,8 @@ cudaError_t flashgs_forward(HsRasterizerContext* ctx, const FlashgsCall& call) {
 }
 
 cudaError_t flashgs_forward_many(HsRasterizerContext* const* contexts, const FlashgsCall* calls,
-                                 uint32_t count, cudaStream_t stream) {
-    return run_many<fg::FlashgsPass>(contexts, calls, count, stream);
+                                 uint32_t count, cudaStream_t stream, cudaEvent_t raster_begin) {
+    return run_many<fg::FlashgsPass>(contexts, calls, count, stream, raster_begin);
 }
 
 cudaError_t flashgs_debug_copy(HsRasterizerContext* ctx, uint64_t point_capacity,

@@ -382,8 +382,8 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, const StandardCall& call)
 }
 
 cudaError_t standard_forward_many(HsRasterizerContext* const* contexts, const StandardCall* calls,
-                                  uint32_t count, cudaStream_t stream) {
-    return run_many<st::StandardPass>(contexts, calls, count, stream);
+                                  uint32_t count, cudaStream_t stream, cudaEvent_t raster_begin) {
+    return run_many<st::StandardPass>(contexts, calls, count, stream, raster_begin);
 }
 
 }  // namespace hs

@@ -243,7 +243,8 @@ class StandardViewV2(ctypes.Structure):
         ("depth_ratio", ctypes.c_double), ("camera30", ctypes.c_void_p), ("pixel_rays3", ctypes.c_void_p),
         ("rgb_map3", ctypes.c_void_p), ("acc_map", ctypes.c_void_p), ("dpt_map", ctypes.c_void_p),
         ("norm_map3", ctypes.c_void_p), ("surf_norm_map3", ctypes.c_void_p), ("dist_map", ctypes.c_void_p),
-        ("spec_map", ctypes.c_void_p), ("rough_map", ctypes.c_void_p), ("stream", ctypes.c_void_p),
+        ("spec_map", ctypes.c_void_p), ("rough_map", ctypes.c_void_p), ("raster_begin_event", ctypes.c_void_p),
+        ("stream", ctypes.c_void_p),
     ]
 
 
@@ -266,7 +267,8 @@ class FlashgsViewV2(ctypes.Structure):
         ("fused_rgb3", ctypes.c_void_p), ("diffuse_rgb3", ctypes.c_void_p), ("reflection_rgb_map3", ctypes.c_void_p),
         ("postprocess", ctypes.c_int32), ("rgb_map3", ctypes.c_void_p), ("acc_map", ctypes.c_void_p),
         ("dpt_map", ctypes.c_void_p), ("norm_map3", ctypes.c_void_p), ("surf_norm_map3", ctypes.c_void_p),
-        ("dist_map", ctypes.c_void_p), ("spec_map", ctypes.c_void_p), ("stream", ctypes.c_void_p),
+        ("dist_map", ctypes.c_void_p), ("spec_map", ctypes.c_void_p), ("raster_begin_event", ctypes.c_void_p),
+        ("stream", ctypes.c_void_p),
     ]
 
 

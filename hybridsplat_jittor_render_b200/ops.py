@@ -861,7 +861,14 @@ class StandardViewOutputs(NamedTuple):
     maps: dict[str, torch.Tensor] | None
 
 
-_GROUP_KEYS = ("means3d", "opacities", "scales", "rotations", "specular", "roughness")
+def _event_handle(event: torch.cuda.Event | None) -> int | None:
+    """The cudaEvent_t of a torch event (created by a first record if torch
+    has not created it yet)."""
+    if event is None:
+        return None
+    if not event.cuda_event:
+        event.record()
+    return int(event.cuda_event)
 
 
 def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Tensor], viewmatrix: torch.Tensor,
@@ -869,7 +876,8 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
                   width: int, height: int, tan_fovx: float, tan_fovy: float, sh_degree: int,
                   base_context: NativeRendererContext, reflection_context: NativeRendererContext,
                   trace: dict[str, Any] | None = None, postprocess: dict[str, float] | None = None,
-                  stream: int | None = None) -> StandardViewOutputs:
+                  stream: int | None = None, raster_begin_event: torch.cuda.Event | None = None
+                  ) -> StandardViewOutputs:
     """One view of the standard session (render_hybridsplat_view,
     renderer.py:232-341, and postprocess_raster, math.py:426-463) in one call
     (hs_b200_standard_view_v2).
@@ -884,8 +892,9 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
     ``max_trace_depth`` (0), ``specular_threshold`` (0.0), as trace_reflection.
     ``postprocess`` (optional) adds the raw-map postprocess: ``fov_x``,
     ``fov_y`` and ``depth_ratio`` (0.0). ``background`` is the raster calls'
-    [5]. ``stream`` as in rasterize_forward_many. Every output equals that of
-    the same steps called one by one.
+    [5]. ``stream`` as in rasterize_forward_many. ``raster_begin_event``
+    (optional) is recorded when both calls' binning is done, before the tile
+    renderers. Every output equals that of the same steps called one by one.
     """
     if base_context is reflection_context:
         raise ValueError("standard_view needs two distinct contexts")
@@ -980,6 +989,7 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
             setattr(view, field, _ptr(maps[name]))
         camera = {"inverse_intrinsics": camera_buf[0:9].view(3, 3), "rotation": camera_buf[9:18].view(3, 3),
                   "origin": camera_buf[18:21], "normal_rotation": camera_buf[21:30].view(3, 3), "rays": pixel_rays}
+    view.raster_begin_event = _event_handle(raster_begin_event)
     error = error_buffer()
     status = base_context.library.hs_b200_standard_view_v2(ctypes.byref(view), error, len(error))
     check_status(status, "hs_b200_standard_view_v2", error)
@@ -1011,7 +1021,8 @@ def flashgs_view(base: dict[str, Any], reflection: dict[str, Any], trace_group: 
                  world_view: torch.Tensor, full_proj: torch.Tensor, camera_center: torch.Tensor, *,
                  base_context: NativeRendererContext, reflection_context: NativeRendererContext,
                  trace: dict[str, Any] | None = None, postprocess: bool = False,
-                 stream: int | None = None) -> FlashgsViewOutputs:
+                 stream: int | None = None, raster_begin_event: torch.cuda.Event | None = None
+                 ) -> FlashgsViewOutputs:
     """One view of the FlashGS session (render_hybridsplat_flashgs_view,
     renderer.py:344-446, with _flashgs_postprocess) in one call
     (hs_b200_flashgs_view_v2).
@@ -1025,8 +1036,8 @@ def flashgs_view(base: dict[str, Any], reflection: dict[str, Any], trace_group: 
     ``others``, ``degree``, optional ``use_others``, ``max_trace_depth``,
     ``specular_threshold``); ``world_view``, ``full_proj`` and
     ``camera_center`` are the view's device camera. ``postprocess`` adds the
-    FlashGS raw maps. Every output equals that of the same steps called one by
-    one.
+    FlashGS raw maps; ``raster_begin_event`` as in standard_view. Every output
+    equals that of the same steps called one by one.
     """
     if base_context is reflection_context:
         raise ValueError("flashgs_view needs two distinct contexts")
@@ -1101,6 +1112,7 @@ def flashgs_view(base: dict[str, Any], reflection: dict[str, Any], trace_group: 
         for field, name in zip(("rgb_map3", "acc_map", "dpt_map", "norm_map3", "surf_norm_map3", "dist_map",
                                 "spec_map"), FLASHGS_MAPS):
             setattr(view, field, _ptr(maps[name]))
+    view.raster_begin_event = _event_handle(raster_begin_event)
     error = error_buffer()
     status = base_context.library.hs_b200_flashgs_view_v2(ctypes.byref(view), error, len(error))
     del hold_b, hold_r

@@ -298,6 +298,8 @@ typedef struct HsB200StandardViewV2 {
     float* dist_map;
     float* spec_map;
     float* rough_map;
+    void* raster_begin_event;              /* optional cudaEvent_t, recorded when both calls' binning
+                                            * is done and the tile renderers may start */
     void* stream;
 } HsB200StandardViewV2;
 
@@ -374,6 +376,7 @@ typedef struct HsB200FlashgsViewV2 {
     float* surf_norm_map3;
     float* dist_map;
     float* spec_map;
+    void* raster_begin_event;              /* optional cudaEvent_t, as in HsB200StandardViewV2 */
     void* stream;
 } HsB200FlashgsViewV2;
 

@@ -282,3 +282,23 @@ def test_flashgs_view_benchmark_frame():
     """The FlashGS benchmark frame (1M + 200k, 1292x839, orbit view 7),
     reflection colours traced."""
     run_flashgs_view("flashgs_1m", scenes.orbit_camera("flashgs_1m", 7), traced=True)
+
+
+def test_view_records_the_raster_begin_event():
+    """The optional event of the one-view entries is recorded between the
+    binning and the renderers: after the view's first kernel and before its
+    last."""
+    cam = scenes.generic_camera(SMALL, 1)
+    base, refl, trace, camera = make_view(SMALL, cam)
+    with NativeRendererContext(0) as ctx, NativeRendererContext(0) as ctx_r:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        raster = torch.cuda.Event(enable_timing=True)
+        start.record()
+        ops.standard_view(base, refl, camera["viewmatrix"], camera["projmatrix"], camera["camera_position"],
+                          camera["background"], width=cam.width, height=cam.height, tan_fovx=cam.tan_fovx,
+                          tan_fovy=cam.tan_fovy, sh_degree=3, base_context=ctx, reflection_context=ctx_r,
+                          raster_begin_event=raster)
+        end.record()
+        torch.cuda.synchronize()
+        assert raster.query()
+        assert 0.0 <= start.elapsed_time(raster) <= start.elapsed_time(end)
