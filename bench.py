@@ -532,13 +532,30 @@ class Frame:
 
     def launches_per_step(self, width: int, height: int) -> int:
         """Kernels of this library launched by one render() call (memsets and
-        copies excluded): per raster call preprocess, totals publication,
-        depth-sort histogram + 4 passes, pair offsets, emission, tile-sort
-        histogram + passes, ranges, tile order, wait-status publication and the
-        rasteriser; plus the elementwise kernels of the view."""
+        copies excluded): per raster call preprocess, totals publication, the
+        depth sort, pair offsets, emission, the tile sort, ranges, tile order
+        (which also publishes the wait status) and the rasteriser; plus the
+        elementwise kernels of the view. A sort of n items in p 8-bit passes
+        launches 1 histogram + p one-sweep passes, or 3 kernels per pass
+        (count, scan, scatter) from 2^21 items. The tile sorts' pair counts
+        are the groups' `rendered` counts of the last view, an upper bound of
+        the pairs emitted after culling (the same side of 2^21 on the
+        benchmark frame: 4.5M / 3.66M base, under 1M reflection)."""
+        torch = self.torch
+        if getattr(self, "pair_counts", None) is None:
+            base, refl = self.render()[:2]
+            torch.cuda.synchronize()
+            self.pair_counts = (int(base.rendered.reshape(-1)[0]), int(refl.rendered.reshape(-1)[0]))
+
+        def sort_launches(n: int, bits: int) -> int:
+            passes = math.ceil(bits / 8)
+            return 0 if n == 0 else (3 * passes if n >= 1 << 21 else 1 + passes)
+
         tiles = ((width + 15) // 16) * ((height + 15) // 16)
-        tile_passes = math.ceil(max(1, int(tiles).bit_length()) / 8)
-        per_raster = 1 + 1 + (1 + 4) + 1 + 1 + (1 + tile_passes) + 1 + 1 + 1 + 1
+        tile_bits = max(1, int(tiles).bit_length())
+        per_raster = 0
+        for points, pairs in zip((self.nb, self.nr), self.pair_counts):
+            per_raster += 1 + 1 + sort_launches(points, 32) + 1 + 1 + sort_launches(pairs, tile_bits) + 1 + 1 + 1
         if self.fused_glue:
             extra = 1 if self.backend == "standard" else 0  # direction + SH + concatenation
         else:
@@ -553,7 +570,7 @@ class Frame:
             # normal column, suffix and the standard colours); a traced
             # standard view concatenates its colours after the trace
             extra -= 0 if (self.traced and self.backend == "standard") else 1
-        return 2 * per_raster + extra + 3  # + reflection prefix, suffix, fusion
+        return per_raster + extra + 3  # + reflection prefix, suffix, fusion
 
 
 def camera_row(cam, scenes) -> np.ndarray:
@@ -771,6 +788,13 @@ def stage_split(frame: Frame, cam, steps: int) -> dict:
     sums = np.zeros(n)
     for c in {id(c): c for c in (frame.ctx, frame.ctx_r)}.values():
         c.stage_timing(True)
+        c.read_stage_timing()
+    # one untimed pass first: the one-call frames before it never launched some
+    # of the separate steps' kernels, and a first launch loads its module
+    frame.set_camera(cam)
+    frame.render([torch.cuda.Event(enable_timing=True) for _ in range(n + 1)])
+    torch.cuda.synchronize()
+    for c in {id(c): c for c in (frame.ctx, frame.ctx_r)}.values():
         c.read_stage_timing()
     frame.split = []
     for _ in range(steps):

@@ -41,16 +41,6 @@ static __global__ void publish_totals_kernel(const uint32_t* __restrict__ totals
     __threadfence_system();
 }
 
-// Publishes a call's look-back error word (set when a bounded wait of its
-// depth sort, pair-offset scan or tile sort gave up) to mapped pinned host
-// memory, after the last of those kernels: the host reads it once binning is
-// done and fails the same call.
-static __global__ void publish_error_kernel(const uint32_t* __restrict__ error,
-                                            volatile uint32_t* host) {
-    if (threadIdx.x == 0) host[0] = *reinterpret_cast<const volatile uint32_t*>(error);
-    __threadfence_system();
-}
-
 // Allocates the mapped pinned totals block of a context: *host for the host,
 // *device for kernels.
 inline cudaError_t alloc_mapped_totals(uint32_t** host, uint32_t** device) {
@@ -254,16 +244,24 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
 // below the leading one; any order inside a bucket), so that the persistent
 // rasterisers take the expensive tiles before the cheap ones.
 // One block of kOrderThreads threads over tiles [tile_first, tile_first +
-// tile_count); `counter` (the rasteriser's work counter) is reset here.
+// tile_count); `counter` (the rasteriser's work counter) is reset here. When
+// host_error (mapped pinned memory) is given, the call's look-back error word
+// (set when a bounded wait of its depth sort, pair-offset scan or tile sort
+// gave up) is published to it: this is the last kernel of binning, the host
+// reads the word once binning is done and fails the same call.
 constexpr int kOrderThreads = 1024;
 
 template <class Range>
 __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
     uint32_t tile_first, uint32_t tile_count, const Range* __restrict__ ranges,
-    uint32_t* __restrict__ order, uint32_t* __restrict__ counter) {
+    uint32_t* __restrict__ order, uint32_t* __restrict__ counter, const uint32_t* __restrict__ error,
+    volatile uint32_t* host_error) {
     constexpr uint32_t kBuckets = 33u * 8u;
+    constexpr uint32_t kScanWarps = (kBuckets + 31u) / 32u;
+    static_assert(kScanWarps <= 32u && kScanWarps * 32u <= static_cast<uint32_t>(kOrderThreads), "scan");
     __shared__ uint32_t hist[kBuckets];
     __shared__ uint32_t next[kBuckets];
+    __shared__ uint32_t warp_base[kScanWarps];
     // bucket 8 * clz + (7 - next three bits): ascending buckets, descending lengths
     auto bucket = [](uint32_t len) -> uint32_t {
         if (len == 0u) return kBuckets - 1u;
@@ -278,17 +276,42 @@ __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(
         atomicAdd(&hist[bucket(len)], 1u);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        uint32_t run = 0;
-        for (uint32_t b = 0; b < kBuckets; ++b) {
-            next[b] = run;
-            run += hist[b];
+    // exclusive scan of the bucket counts: one warp-level scan per 32 buckets,
+    // then a scan of the warps' totals
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    uint32_t count = 0, incl = 0;
+    if (warp < kScanWarps) {
+        count = threadIdx.x < kBuckets ? hist[threadIdx.x] : 0u;
+        incl = count;
+#pragma unroll
+        for (uint32_t off = 1; off < 32u; off <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += t;
         }
+        if (lane == 31u) warp_base[warp] = incl;
     }
+    __syncthreads();
+    if (warp == 0) {
+        const uint32_t total = lane < kScanWarps ? warp_base[lane] : 0u;
+        uint32_t run = total;
+#pragma unroll
+        for (uint32_t off = 1; off < 32u; off <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, run, off);
+            if (lane >= off) run += t;
+        }
+        __syncwarp();
+        if (lane < kScanWarps) warp_base[lane] = run - total;
+    }
+    __syncthreads();
+    if (warp < kScanWarps && threadIdx.x < kBuckets) next[threadIdx.x] = warp_base[warp] + incl - count;
     __syncthreads();
     for (uint32_t t = tile_first + threadIdx.x; t < tile_first + tile_count; t += kOrderThreads) {
         const uint32_t len = static_cast<uint32_t>(ranges[t].y - ranges[t].x);
         order[atomicAdd(&next[bucket(len)], 1u)] = t;
+    }
+    if (host_error != nullptr && threadIdx.x == 0) {
+        host_error[0] = *reinterpret_cast<const volatile uint32_t*>(error);
+        __threadfence_system();
     }
 }
 

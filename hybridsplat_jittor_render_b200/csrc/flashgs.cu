@@ -306,16 +306,15 @@ cudaError_t FlashgsPass::bin() {
         }
     }
     const uint32_t strip_tiles = (c_.row_end - c_.row_begin) * static_cast<uint32_t>(grid_x_);
+    // The waits of the depth sort, offset scan and tile sort are over: the
+    // tile order kernel also sends their error word to the host (non-empty
+    // calls), read by finish().
     bin::tile_order_kernel<int2><<<1, bin::kOrderThreads, 0, stream>>>(
         c_.row_begin * static_cast<uint32_t>(grid_x_), strip_tiles, ranges_, tile_order_,
-        work_counter_);
+        work_counter_, ctx_->device_error, c_.point_count > 0 ? ctx_->fg_total_mapped + 1 : nullptr);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
     if (c_.point_count > 0) {
-        // The waits of the depth sort, offset scan and tile sort are over:
-        // their error word goes to the host, read by finish().
-        bin::publish_error_kernel<<<1, 32, 0, stream>>>(ctx_->device_error, ctx_->fg_total_mapped + 1);
-        st = cudaGetLastError();
         if (st == cudaSuccess) st = cudaEventRecord(ctx_->fg_count_event, stream);
         if (st != cudaSuccess) return st;
         published_ = true;

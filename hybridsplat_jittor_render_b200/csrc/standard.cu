@@ -314,13 +314,12 @@ cudaError_t StandardPass::bin() {
         if (st != cudaSuccess) return st;
     }
     const uint32_t strip_tiles = (c_.row_end - c_.row_begin) * grid_x_;
+    // The waits of the depth sort, offset scan and tile sort are over: the tile
+    // order kernel also sends their error word to the host, read by finish()
+    // once the renderer is queued.
     bin::tile_order_kernel<uint2><<<1, bin::kOrderThreads, 0, stream>>>(
-        c_.row_begin * grid_x_, strip_tiles, ranges_, tile_order_, work_counter_);
-    st = cudaGetLastError();
-    if (st != cudaSuccess) return st;
-    // The waits of the depth sort, offset scan and tile sort are over: their
-    // error word goes to the host, read by finish() once the renderer is queued.
-    bin::publish_error_kernel<<<1, 32, 0, stream>>>(ctx_->device_error, ctx_->std_total_mapped + 3);
+        c_.row_begin * grid_x_, strip_tiles, ranges_, tile_order_, work_counter_, ctx_->device_error,
+        ctx_->std_total_mapped + 3);
     st = cudaGetLastError();
     if (st == cudaSuccess) st = cudaEventRecord(ctx_->std_count_event, stream);
     if (st != cudaSuccess) return st;

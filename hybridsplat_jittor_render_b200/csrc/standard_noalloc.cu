@@ -207,7 +207,7 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
     }
     bin::tile_order_kernel<uint2><<<1, bin::kOrderThreads, 0, stream>>>(
-        0u, static_cast<uint32_t>(tiles), l.ranges, l.tile_order, l.work_counter);
+        0u, static_cast<uint32_t>(tiles), l.ranges, l.tile_order, l.work_counter, l.error, nullptr);
     st = cudaGetLastError();
     if (st != cudaSuccess) return {st, nullptr, 0, 0};
     const uint32_t items = static_cast<uint32_t>(tiles) * 4u;
