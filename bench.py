@@ -567,9 +567,13 @@ class Frame:
             extra += 6 if self.backend == "standard" else 1
         if self.one_call():
             # the one-call entries prepare the reflection in one kernel (prefix,
-            # normal column, suffix and the standard colours); a traced
-            # standard view concatenates its colours after the trace
-            extra -= 0 if (self.traced and self.backend == "standard") else 1
+            # normal column, suffix and the standard colours), which the
+            # standard entry runs in the same grid as the base colours; a
+            # traced standard view concatenates its colours after the trace
+            if self.backend == "standard":
+                extra -= 1 if self.traced else 2
+            else:
+                extra -= 1
         return per_raster + extra + 3  # + reflection prefix, suffix, fusion
 
 

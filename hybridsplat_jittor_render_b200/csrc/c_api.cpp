@@ -2044,19 +2044,15 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
         }
         // base colours, reflection preparation, trace, reflection colours
         const bool traced = v->trace == 1;
-        e = hs::precise::sh_colors5(v->base_sh, v->sh_coefficients, v->sh_degree, v->base.means3d,
-                                    v->camera_position3, v->base.specular, v->base.roughness, nb,
-                                    v->base.colors5, s);
-        // prefix, normal column, suffix and (traced) the ray split or
-        // (untraced) the reflection colours, in one pass
-        if (e == cudaSuccess) {
-            e = hs::precise::reflection_view(
-                v->reflection_rotation_raw4, v->reflection.means3d, v->camera_position3, nr,
-                v->reflection_rotation9, v->reflection_normal3, v->reflection_rays36,
-                traced ? v->reflection_ray_origins3 : nullptr, traced ? v->reflection_ray_directions3 : nullptr,
-                v->reflection_rgb3, v->reflection.specular, v->reflection.roughness,
-                traced ? nullptr : v->reflection.colors5, s);
-        }
+        // base colours, and the reflection's prefix, normal column, suffix and
+        // (traced) ray split or (untraced) colours, side by side in one grid
+        e = hs::precise::view_prologue(
+            v->base_sh, v->sh_coefficients, v->sh_degree, v->base.means3d, v->camera_position3, v->base.specular,
+            v->base.roughness, nb, v->base.colors5, v->reflection_rotation_raw4, v->reflection.means3d, nr,
+            v->reflection_rotation9, v->reflection_normal3, v->reflection_rays36,
+            traced ? v->reflection_ray_origins3 : nullptr, traced ? v->reflection_ray_directions3 : nullptr,
+            v->reflection_rgb3, v->reflection.specular, v->reflection.roughness,
+            traced ? nullptr : v->reflection.colors5, s);
         if (e != cudaSuccess) return cuda_failure(e, "standard view preparation", error_text, error_capacity);
         if (traced && nr != 0) {
             const hs::TraceCall t = view_trace_call(*v, nr, v->reflection.means3d, v->reflection_shs,

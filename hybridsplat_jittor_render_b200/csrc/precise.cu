@@ -239,18 +239,25 @@ __global__ void sh_colors5_kernel(const float* __restrict__ sh, uint32_t coeffic
 }
 
 // sh_colors5_kernel for 16 coefficients per channel in 16-byte aligned rows,
-// staged through shared memory as in sh16_to_rgb_kernel.
+// staged through shared memory as in sh16_to_rgb_kernel: the work of one
+// block (`block`, `rows` its kShThreads * kShStride shared floats).
+struct ShColorsArgs {
+    const float4* sh;
+    const float* points;
+    const float* center;
+    const float* specular;
+    const float* roughness;
+    uint64_t count;
+    float* out5;
+};
+
 template <uint32_t kDegree>
-__global__ void __launch_bounds__(kShThreads) sh16_colors5_kernel(
-    const float4* __restrict__ sh, const float* __restrict__ points,
-    const float* __restrict__ center, const float* __restrict__ specular,
-    const float* __restrict__ roughness, uint64_t count, float* __restrict__ out5) {
-    __shared__ float rows[kShThreads * kShStride];
-    const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kShThreads;
-    const uint64_t left = count - first;
+__device__ __forceinline__ void sh16_colors5_block(const ShColorsArgs& a, uint32_t block, float* rows) {
+    const uint64_t first = static_cast<uint64_t>(block) * kShThreads;
+    const uint64_t left = a.count - first;
     const uint32_t n = left < kShThreads ? static_cast<uint32_t>(left) : kShThreads;
     for (uint32_t f = threadIdx.x; f < n * 12; f += kShThreads) {
-        const float4 v = sh[first * 12 + f];
+        const float4 v = a.sh[first * 12 + f];
         float* d = rows + (f / 12) * kShStride + (f % 12) * 4;
         d[0] = v.x;
         d[1] = v.y;
@@ -262,15 +269,21 @@ __global__ void __launch_bounds__(kShThreads) sh16_colors5_kernel(
     const uint64_t i = first + threadIdx.x;
     const float* c = rows + threadIdx.x * kShStride;
     float x, y, z;
-    view_direction(points + 3 * i, center[0], center[1], center[2], x, y, z);
+    view_direction(a.points + 3 * i, a.center[0], a.center[1], a.center[2], x, y, z);
     const float xx = mul(x, x), yy = mul(y, y), zz = mul(z, z);
     const float xy = mul(x, y), yz = mul(y, z), xz = mul(x, z);
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch) {
-        out5[5 * i + ch] = sh_channel(c + 16 * ch, x, y, z, xx, yy, zz, xy, yz, xz, kDegree);
+        a.out5[5 * i + ch] = sh_channel(c + 16 * ch, x, y, z, xx, yy, zz, xy, yz, xz, kDegree);
     }
-    out5[5 * i + 3] = specular[i];
-    out5[5 * i + 4] = roughness[i];
+    a.out5[5 * i + 3] = a.specular[i];
+    a.out5[5 * i + 4] = a.roughness[i];
+}
+
+template <uint32_t kDegree>
+__global__ void __launch_bounds__(kShThreads) sh16_colors5_kernel(ShColorsArgs a) {
+    __shared__ float rows[kShThreads * kShStride];
+    sh16_colors5_block<kDegree>(a, blockIdx.x, rows);
 }
 
 // fuse_maps_kernel with channel-first inputs: base and reflection colours as
@@ -434,46 +447,81 @@ __global__ void __launch_bounds__(kSuffixThreads) reflection_suffix_kernel(
 // (row columns 12..14) and directions (9..11) and the raster colours
 // colors5 = [rgb3, specular, roughness]. Each value is computed by the same
 // functions as the separate kernels, so they are bit-identical to them.
-__global__ void __launch_bounds__(kSuffixThreads) reflection_view_kernel(
-    const float* __restrict__ rot_raw, const float* __restrict__ xyz, const float* __restrict__ center,
-    uint64_t count, float* __restrict__ rot9, float* __restrict__ normal3, float* __restrict__ out36,
-    float* __restrict__ origins3, float* __restrict__ directions3, const float* __restrict__ rgb3,
-    const float* __restrict__ specular, const float* __restrict__ roughness, float* __restrict__ colors5) {
-    __shared__ float rows[kSuffixThreads * kSuffixStride];
-    const uint64_t first = static_cast<uint64_t>(blockIdx.x) * kSuffixThreads;
-    const uint64_t left = count - first;
+struct ReflectionViewArgs {
+    const float* rot_raw;
+    const float* xyz;
+    const float* center;
+    uint64_t count;
+    float* rot9;
+    float* normal3;
+    float* out36;
+    float* origins3;
+    float* directions3;
+    const float* rgb3;
+    const float* specular;
+    const float* roughness;
+    float* colors5;
+};
+
+// The work of one block (`rows`: kSuffixThreads * kSuffixStride shared floats).
+__device__ __forceinline__ void reflection_view_block(const ReflectionViewArgs& a, uint32_t block, float* rows) {
+    const uint64_t first = static_cast<uint64_t>(block) * kSuffixThreads;
+    const uint64_t left = a.count - first;
     const uint32_t n = left < kSuffixThreads ? static_cast<uint32_t>(left) : kSuffixThreads;
     if (threadIdx.x < n) {
         const uint64_t i = first + threadIdx.x;
         float o[9];
-        prefix_matrix(rot_raw + 4 * i, o);
+        prefix_matrix(a.rot_raw + 4 * i, o);
 #pragma unroll
-        for (int k = 0; k < 9; ++k) rot9[9 * i + k] = o[k];
-        normal3[3 * i] = o[2];
-        normal3[3 * i + 1] = o[5];
-        normal3[3 * i + 2] = o[8];
+        for (int k = 0; k < 9; ++k) a.rot9[9 * i + k] = o[k];
+        a.normal3[3 * i] = o[2];
+        a.normal3[3 * i + 1] = o[5];
+        a.normal3[3 * i + 2] = o[8];
         float values[36];
-        suffix_row(xyz[3 * i], xyz[3 * i + 1], xyz[3 * i + 2], center[0], center[1], center[2], o[2], o[5],
-                   o[8], values);
-        if (origins3 != nullptr) {
+        suffix_row(a.xyz[3 * i], a.xyz[3 * i + 1], a.xyz[3 * i + 2], a.center[0], a.center[1], a.center[2], o[2],
+                   o[5], o[8], values);
+        if (a.origins3 != nullptr) {
             for (int c = 0; c < 3; ++c) {
-                origins3[3 * i + c] = values[12 + c];
-                directions3[3 * i + c] = values[9 + c];
+                a.origins3[3 * i + c] = values[12 + c];
+                a.directions3[3 * i + c] = values[9 + c];
             }
         }
-        if (colors5 != nullptr) {
-            colors5[5 * i] = rgb3[3 * i];
-            colors5[5 * i + 1] = rgb3[3 * i + 1];
-            colors5[5 * i + 2] = rgb3[3 * i + 2];
-            colors5[5 * i + 3] = specular[i];
-            colors5[5 * i + 4] = roughness[i];
+        if (a.colors5 != nullptr) {
+            a.colors5[5 * i] = a.rgb3[3 * i];
+            a.colors5[5 * i + 1] = a.rgb3[3 * i + 1];
+            a.colors5[5 * i + 2] = a.rgb3[3 * i + 2];
+            a.colors5[5 * i + 3] = a.specular[i];
+            a.colors5[5 * i + 4] = a.roughness[i];
         }
         float* row = rows + threadIdx.x * kSuffixStride;
 #pragma unroll
         for (int k = 0; k < 36; ++k) row[k] = values[k];
     }
     __syncthreads();
-    store_rows(rows, first, n, out36);
+    store_rows(rows, first, n, a.out36);
+}
+
+__global__ void __launch_bounds__(kSuffixThreads) reflection_view_kernel(ReflectionViewArgs a) {
+    __shared__ float rows[kSuffixThreads * kSuffixStride];
+    reflection_view_block(a, blockIdx.x, rows);
+}
+
+// A view's prologue in one grid: blocks [0, sh_blocks) compute the base
+// colours (sh16_colors5_block), the rest the reflection preparation
+// (reflection_view_block); the two are independent and run side by side.
+static_assert(kShThreads == kSuffixThreads, "one block size for both parts of the prologue");
+constexpr int kPrologueRows =
+    kShThreads * kShStride > kSuffixThreads * kSuffixStride ? kShThreads * kShStride : kSuffixThreads * kSuffixStride;
+
+template <uint32_t kDegree>
+__global__ void __launch_bounds__(kShThreads) view_prologue_kernel(ShColorsArgs a, ReflectionViewArgs b,
+                                                                   uint32_t sh_blocks) {
+    __shared__ float rows[kPrologueRows];
+    if (blockIdx.x < sh_blocks) {
+        sh16_colors5_block<kDegree>(a, blockIdx.x, rows);
+    } else {
+        reflection_view_block(b, blockIdx.x - sh_blocks, rows);
+    }
 }
 
 unsigned grid_for(uint64_t count) {
@@ -542,12 +590,12 @@ cudaError_t sh_colors5(const float* sh, uint32_t coefficients, uint32_t degree,
     if (count == 0) return cudaSuccess;
     if (coefficients == 16 && (reinterpret_cast<uintptr_t>(sh) & 15u) == 0 && degree <= 3) {
         const unsigned blocks = static_cast<unsigned>((count + kShThreads - 1) / kShThreads);
-        const float4* sh4 = reinterpret_cast<const float4*>(sh);
+        const ShColorsArgs a{reinterpret_cast<const float4*>(sh), points, center, specular, roughness, count, out5};
         switch (degree) {
-            case 0: sh16_colors5_kernel<0><<<blocks, kShThreads, 0, s>>>(sh4, points, center, specular, roughness, count, out5); break;
-            case 1: sh16_colors5_kernel<1><<<blocks, kShThreads, 0, s>>>(sh4, points, center, specular, roughness, count, out5); break;
-            case 2: sh16_colors5_kernel<2><<<blocks, kShThreads, 0, s>>>(sh4, points, center, specular, roughness, count, out5); break;
-            default: sh16_colors5_kernel<3><<<blocks, kShThreads, 0, s>>>(sh4, points, center, specular, roughness, count, out5); break;
+            case 0: sh16_colors5_kernel<0><<<blocks, kShThreads, 0, s>>>(a); break;
+            case 1: sh16_colors5_kernel<1><<<blocks, kShThreads, 0, s>>>(a); break;
+            case 2: sh16_colors5_kernel<2><<<blocks, kShThreads, 0, s>>>(a); break;
+            default: sh16_colors5_kernel<3><<<blocks, kShThreads, 0, s>>>(a); break;
         }
         return cudaGetLastError();
     }
@@ -591,9 +639,43 @@ cudaError_t reflection_view(const float* rot_raw, const float* xyz, const float*
                             const float* rgb3, const float* specular, const float* roughness, float* colors5,
                             cudaStream_t s) {
     if (count == 0) return cudaSuccess;
+    const ReflectionViewArgs a{rot_raw, xyz,         center, count,    rot9,      normal3, out36,
+                               origins3, directions3, rgb3,  specular, roughness, colors5};
     reflection_view_kernel<<<static_cast<unsigned>((count + kSuffixThreads - 1) / kSuffixThreads),
-                             kSuffixThreads, 0, s>>>(rot_raw, xyz, center, count, rot9, normal3, out36, origins3,
-                                                     directions3, rgb3, specular, roughness, colors5);
+                             kSuffixThreads, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t view_prologue(const float* sh, uint32_t coefficients, uint32_t degree, const float* points,
+                          const float* center, const float* specular, const float* roughness, uint64_t count,
+                          float* out5, const float* rot_raw, const float* xyz, uint64_t reflection_count,
+                          float* rot9, float* normal3, float* out36, float* origins3, float* directions3,
+                          const float* rgb3, const float* reflection_specular, const float* reflection_roughness,
+                          float* colors5, cudaStream_t s) {
+    const uint64_t sh_blocks = (count + kShThreads - 1) / kShThreads;
+    const uint64_t refl_blocks = (reflection_count + kSuffixThreads - 1) / kSuffixThreads;
+    const bool fused = coefficients == 16 && (reinterpret_cast<uintptr_t>(sh) & 15u) == 0 && degree <= 3 &&
+                       count != 0 && reflection_count != 0 && sh_blocks + refl_blocks <= 0x7fffffffu;
+    if (!fused) {
+        cudaError_t e = sh_colors5(sh, coefficients, degree, points, center, specular, roughness, count, out5, s);
+        if (e == cudaSuccess) {
+            e = reflection_view(rot_raw, xyz, center, reflection_count, rot9, normal3, out36, origins3,
+                                directions3, rgb3, reflection_specular, reflection_roughness, colors5, s);
+        }
+        return e;
+    }
+    const ShColorsArgs a{reinterpret_cast<const float4*>(sh), points, center, specular, roughness, count, out5};
+    const ReflectionViewArgs b{rot_raw,  xyz,         center, reflection_count,    rot9,
+                               normal3,  out36,       origins3, directions3,       rgb3,
+                               reflection_specular, reflection_roughness, colors5};
+    const unsigned blocks = static_cast<unsigned>(sh_blocks + refl_blocks);
+    const uint32_t split = static_cast<uint32_t>(sh_blocks);
+    switch (degree) {
+        case 0: view_prologue_kernel<0><<<blocks, kShThreads, 0, s>>>(a, b, split); break;
+        case 1: view_prologue_kernel<1><<<blocks, kShThreads, 0, s>>>(a, b, split); break;
+        case 2: view_prologue_kernel<2><<<blocks, kShThreads, 0, s>>>(a, b, split); break;
+        default: view_prologue_kernel<3><<<blocks, kShThreads, 0, s>>>(a, b, split); break;
+    }
     return cudaGetLastError();
 }
 

@@ -38,6 +38,16 @@ cudaError_t reflection_view(const float* rot_raw, const float* xyz, const float*
                             float* rot9, float* normal3, float* out36, float* origins3, float* directions3,
                             const float* rgb3, const float* specular, const float* roughness, float* colors5,
                             cudaStream_t s);
+// sh_colors5 of the base group and reflection_view of the reflection group in
+// one launch (side by side in one grid when the SH rows are 16 aligned
+// coefficients and both groups are non-empty, else the two launches);
+// bit-identical to them.
+cudaError_t view_prologue(const float* sh, uint32_t coefficients, uint32_t degree, const float* points,
+                          const float* center, const float* specular, const float* roughness, uint64_t count,
+                          float* out5, const float* rot_raw, const float* xyz, uint64_t reflection_count,
+                          float* rot9, float* normal3, float* out36, float* origins3, float* directions3,
+                          const float* rgb3, const float* reflection_specular, const float* reflection_roughness,
+                          float* colors5, cudaStream_t s);
 
 // Tiny kernels used around the cuBLAS / cuSOLVER camera helpers.
 cudaError_t negate9(const float* in, float* out, cudaStream_t s);
