@@ -2069,11 +2069,8 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
         e = hs::standard_forward_many(contexts, calls, 2, s, static_cast<cudaEvent_t>(v->raster_begin_event));
         if (e != cudaSuccess) return cuda_failure(e, "concurrent five-channel rasterizer forward", error_text,
                                                   error_capacity);
-        // fusion from the colour planes (renderer.py:326, math.py:301-311)
-        e = hs::precise::fuse_maps_planar(v->base.output_color5, v->reflection.output_color5,
-                                          v->base.output_color5 + 3 * pixels, v->diffuse_rgb3, v->fused_rgb3,
-                                          v->reflection_rgb_map3, pixels, s);
-        if (e != cudaSuccess) return cuda_failure(e, "standard view fusion", error_text, error_capacity);
+        // fusion from the colour planes (renderer.py:326, math.py:301-311) and,
+        // with the postprocess, the maps in the same pass
         if (post) {
             e = cudaStreamWaitEvent(s, base->post_done_event, 0);
             if (e != cudaSuccess) return cuda_failure(e, "standard view join", error_text, error_capacity);
@@ -2082,9 +2079,16 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
             const float ratio = static_cast<float>(v->depth_ratio);
             const hs::post::StandardMaps maps{v->rgb_map3, v->acc_map, v->dpt_map, v->norm_map3,
                                              v->surf_norm_map3, v->dist_map, v->spec_map, v->rough_map};
-            e = hs::post::standard(v->width, v->height, v->base.output_color5, v->base.output_aux7, v->pixel_rays3,
-                                   v->camera30 + 18, v->camera30 + 21, keep, ratio, maps, s);
+            e = hs::post::standard_with_fusion(v->width, v->height, v->base.output_color5, v->base.output_aux7,
+                                               v->pixel_rays3, v->camera30 + 18, v->camera30 + 21, keep, ratio,
+                                               maps, v->reflection.output_color5, v->diffuse_rgb3, v->fused_rgb3,
+                                               v->reflection_rgb_map3, s);
             if (e != cudaSuccess) return cuda_failure(e, "standard view postprocess", error_text, error_capacity);
+        } else {
+            e = hs::precise::fuse_maps_planar(v->base.output_color5, v->reflection.output_color5,
+                                              v->base.output_color5 + 3 * pixels, v->diffuse_rgb3, v->fused_rgb3,
+                                              v->reflection_rgb_map3, pixels, s);
+            if (e != cudaSuccess) return cuda_failure(e, "standard view fusion", error_text, error_capacity);
         }
         const cudaError_t trailing = cudaGetLastError();
         if (trailing != cudaSuccess)

@@ -31,6 +31,7 @@
 #include <cstdint>
 
 #include "fp.cuh"
+#include "fuse.cuh"
 #include "postprocess.h"
 
 namespace hs {
@@ -88,10 +89,63 @@ __global__ void __launch_bounds__(kThreads) pixel_grid_kernel(int width, int hei
     }
 }
 
+// One pixel of the standard maps (see the file comment).
+__device__ __forceinline__ void standard_pixel(int width, int height, size_t plane, size_t p,
+                                               const float* __restrict__ color, const float* __restrict__ aux,
+                                               const float* __restrict__ rays, const float* o, const float* b,
+                                               float keep, float ratio, const StandardMaps& maps) {
+    const int x = static_cast<int>(p % width), y = static_cast<int>(p / width);
+    const float alpha = aux[plane + p];
+    const float depth = surface_depth(aux, plane, p, keep, ratio);
+    const float n[3] = {aux[2 * plane + p], aux[3 * plane + p], aux[4 * plane + p]};
+    float nr[3];
+    rotate(n, b, nr);
+    float s[3] = {0.0f, 0.0f, 0.0f};
+    if (x > 0 && y > 0 && x < width - 1 && y < height - 1) {
+        // xyz of the four neighbours, then the central differences
+        float up[3], down[3], left[3], right[3];
+        world_point(aux, rays, plane, p - width, keep, ratio, o, up);
+        world_point(aux, rays, plane, p + width, keep, ratio, o, down);
+        world_point(aux, rays, plane, p - 1, keep, ratio, o, left);
+        world_point(aux, rays, plane, p + 1, keep, ratio, o, right);
+        float dx[3], dy[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            dx[c] = sub(down[c], up[c]);
+            dy[c] = sub(right[c], left[c]);
+        }
+        const float cr[3] = {sub(mul(dx[1], dy[2]), mul(dx[2], dy[1])),
+                             sub(mul(dx[2], dy[0]), mul(dx[0], dy[2])),
+                             sub(mul(dx[0], dy[1]), mul(dx[1], dy[0]))};
+        // norm.maximum(eps) with PyTorch's NaN propagation (fmaxf would drop a NaN)
+        const float length = __fsqrt_rn(add(add(mul(cr[0], cr[0]), mul(cr[1], cr[1])), mul(cr[2], cr[2])));
+        const float norm = isnan(length) ? length : fmaxf(length, 1e-12f);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) s[c] = div(cr[c], norm);
+    }
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        maps.rgb3[3 * p + c] = color[c * plane + p];
+        maps.norm3[3 * p + c] = nr[c];
+        maps.surf_norm3[3 * p + c] = mul(s[c], alpha);
+    }
+    maps.acc[p] = alpha;
+    maps.dpt[p] = depth;
+    maps.dist[p] = aux[6 * plane + p];
+    maps.spec[p] = color[3 * plane + p];
+    maps.rough[p] = color[4 * plane + p];
+}
+
+// The maps alone (kFuse false) or, for the one-view entry, with the colour
+// fusion of the same pixel from the base call's colour planes 0..3 and the
+// reflection call's planes 0..2 (fuse_planar_pixel), in one pass.
+template <bool kFuse>
 __global__ void __launch_bounds__(kThreads) standard_kernel(
     int width, int height, const float* __restrict__ color, const float* __restrict__ aux,
     const float* __restrict__ rays, const float* __restrict__ origin3,
-    const float* __restrict__ rotation9, float keep, float ratio, StandardMaps maps) {
+    const float* __restrict__ rotation9, float keep, float ratio, StandardMaps maps,
+    const float* __restrict__ refl_color, float* __restrict__ diffuse, float* __restrict__ final_rgb,
+    float* __restrict__ stored) {
     const size_t plane = static_cast<size_t>(width) * height;
     float b[9], o[3];
 #pragma unroll
@@ -100,47 +154,8 @@ __global__ void __launch_bounds__(kThreads) standard_kernel(
     for (int k = 0; k < 3; ++k) o[k] = origin3[k];
     for (size_t p = blockIdx.x * size_t(kThreads) + threadIdx.x; p < plane;
          p += size_t(gridDim.x) * kThreads) {
-        const int x = static_cast<int>(p % width), y = static_cast<int>(p / width);
-        const float alpha = aux[plane + p];
-        const float depth = surface_depth(aux, plane, p, keep, ratio);
-        const float n[3] = {aux[2 * plane + p], aux[3 * plane + p], aux[4 * plane + p]};
-        float nr[3];
-        rotate(n, b, nr);
-        float s[3] = {0.0f, 0.0f, 0.0f};
-        if (x > 0 && y > 0 && x < width - 1 && y < height - 1) {
-            // xyz of the four neighbours, then the central differences
-            float up[3], down[3], left[3], right[3];
-            world_point(aux, rays, plane, p - width, keep, ratio, o, up);
-            world_point(aux, rays, plane, p + width, keep, ratio, o, down);
-            world_point(aux, rays, plane, p - 1, keep, ratio, o, left);
-            world_point(aux, rays, plane, p + 1, keep, ratio, o, right);
-            float dx[3], dy[3];
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                dx[c] = sub(down[c], up[c]);
-                dy[c] = sub(right[c], left[c]);
-            }
-            const float cr[3] = {sub(mul(dx[1], dy[2]), mul(dx[2], dy[1])),
-                                 sub(mul(dx[2], dy[0]), mul(dx[0], dy[2])),
-                                 sub(mul(dx[0], dy[1]), mul(dx[1], dy[0]))};
-            // norm.maximum(eps) with PyTorch's NaN propagation (fmaxf would drop a NaN)
-            const float length =
-                __fsqrt_rn(add(add(mul(cr[0], cr[0]), mul(cr[1], cr[1])), mul(cr[2], cr[2])));
-            const float norm = isnan(length) ? length : fmaxf(length, 1e-12f);
-#pragma unroll
-            for (int c = 0; c < 3; ++c) s[c] = div(cr[c], norm);
-        }
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            maps.rgb3[3 * p + c] = color[c * plane + p];
-            maps.norm3[3 * p + c] = nr[c];
-            maps.surf_norm3[3 * p + c] = mul(s[c], alpha);
-        }
-        maps.acc[p] = alpha;
-        maps.dpt[p] = depth;
-        maps.dist[p] = aux[6 * plane + p];
-        maps.spec[p] = color[3 * plane + p];
-        maps.rough[p] = color[4 * plane + p];
+        standard_pixel(width, height, plane, p, color, aux, rays, o, b, keep, ratio, maps);
+        if (kFuse) fuse_planar_pixel(color, refl_color, color[3 * plane + p], plane, p, diffuse, final_rgb, stored);
     }
 }
 
@@ -353,8 +368,21 @@ cudaError_t standard(int width, int height, const float* color5, const float* au
                      float ratio, const StandardMaps& maps, cudaStream_t s) {
     const uint64_t pixels = static_cast<uint64_t>(width) * height;
     if (pixels == 0) return cudaSuccess;
-    standard_kernel<<<grid_for(pixels), kThreads, 0, s>>>(width, height, color5, aux7, rays3,
-                                                          origin3, rotation9, keep, ratio, maps);
+    standard_kernel<false><<<grid_for(pixels), kThreads, 0, s>>>(width, height, color5, aux7, rays3, origin3,
+                                                                 rotation9, keep, ratio, maps, nullptr, nullptr,
+                                                                 nullptr, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t standard_with_fusion(int width, int height, const float* color5, const float* aux7, const float* rays3,
+                                 const float* origin3, const float* rotation9, float keep, float ratio,
+                                 const StandardMaps& maps, const float* reflection_color5, float* diffuse3,
+                                 float* final_rgb3, float* stored3, cudaStream_t s) {
+    const uint64_t pixels = static_cast<uint64_t>(width) * height;
+    if (pixels == 0) return cudaSuccess;
+    standard_kernel<true><<<grid_for(pixels), kThreads, 0, s>>>(width, height, color5, aux7, rays3, origin3,
+                                                                rotation9, keep, ratio, maps, reflection_color5,
+                                                                diffuse3, final_rgb3, stored3);
     return cudaGetLastError();
 }
 

@@ -65,6 +65,14 @@ cudaError_t standard(int width, int height, const float* color5, const float* au
                      const float* rays3, const float* origin3, const float* rotation9, float keep,
                      float ratio, const StandardMaps& maps, cudaStream_t s);
 
+// standard() and, in the same pass, the colour fusion of the view
+// (fuse_maps_planar of color5 planes 0..2, reflection_color5 planes 0..2 and
+// color5 plane 3); bit-identical to the two launches.
+cudaError_t standard_with_fusion(int width, int height, const float* color5, const float* aux7, const float* rays3,
+                                 const float* origin3, const float* rotation9, float keep, float ratio,
+                                 const StandardMaps& maps, const float* reflection_color5, float* diffuse3,
+                                 float* final_rgb3, float* stored3, cudaStream_t s);
+
 cudaError_t flashgs(int width, int height, const float* color3, const float* other2,
                     const float* depth1, const float* alpha1, const float* normal3,
                     const float* rotation9, const FlashgsMaps& maps, cudaStream_t s);

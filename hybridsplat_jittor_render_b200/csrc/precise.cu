@@ -13,6 +13,7 @@
 #include <cstdint>
 
 #include "fp.cuh"
+#include "fuse.cuh"
 #include "precise.h"
 
 namespace hs {
@@ -298,15 +299,7 @@ __global__ void fuse_maps_planar_kernel(const float* __restrict__ base,
                                         float* __restrict__ stored, uint64_t pixels) {
     for (uint64_t p = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; p < pixels;
          p += uint64_t(gridDim.x) * blockDim.x) {
-        const float s = specular[p];
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            const float dv = mul(base[c * pixels + p], sub(1.0f, s));
-            const float rv = mul(mul(refl[c * pixels + p], s), 2.0f);
-            diffuse[3 * p + c] = dv;
-            stored[3 * p + c] = rv;
-            final_rgb[3 * p + c] = add(dv, mul(0.5f, rv));
-        }
+        fuse_planar_pixel(base, refl, specular[p], pixels, p, diffuse, final_rgb, stored);
     }
 }
 
