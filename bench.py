@@ -572,10 +572,10 @@ class Frame:
             # traced standard view concatenates its colours after the trace
             if self.backend == "standard":
                 extra -= 1 if self.traced else 2
-                if self.with_post:
-                    extra -= 1  # the maps kernel also does the fusion
             else:
                 extra -= 1
+            if self.with_post:
+                extra -= 1  # the maps kernel also does the fusion
         return per_raster + extra + 3  # + reflection prefix, suffix, fusion
 
 

@@ -2189,19 +2189,22 @@ int32_t hs_b200_flashgs_view_v2(const HsB200FlashgsViewV2* v, char* error_text,
         e = hs::flashgs_forward_many(contexts, calls, 2, s, static_cast<cudaEvent_t>(v->raster_begin_event));
         if (e != cudaSuccess) return cuda_failure(e, "concurrent FlashGS forward", error_text, error_capacity);
         // fusion from the colour planes; specular is the base call's other[0]
-        // (renderer.py:420-427)
+        // (renderer.py:420-427); with the postprocess, in the maps pass
         const uint64_t pixels = static_cast<uint64_t>(v->base.width) * static_cast<uint64_t>(v->base.height);
-        e = hs::precise::fuse_maps_planar(v->base.output_color3, v->reflection.output_color3,
-                                          v->base.output_other2, v->diffuse_rgb3, v->fused_rgb3,
-                                          v->reflection_rgb_map3, pixels, s);
-        if (e != cudaSuccess) return cuda_failure(e, "FlashGS view fusion", error_text, error_capacity);
         if (v->postprocess == 1) {
             const hs::post::FlashgsMaps maps{v->rgb_map3, v->acc_map, v->dpt_map, v->norm_map3,
                                              v->surf_norm_map3, v->dist_map, v->spec_map};
             e = hs::post::flashgs_from_view(v->base.width, v->base.height, v->base.output_color3,
                                             v->base.output_other2, v->base.output_depth1, v->base.output_alpha1,
-                                            v->base.output_normal3, v->world_view4x4, maps, s);
+                                            v->base.output_normal3, v->world_view4x4, maps,
+                                            v->reflection.output_color3, v->diffuse_rgb3, v->fused_rgb3,
+                                            v->reflection_rgb_map3, s);
             if (e != cudaSuccess) return cuda_failure(e, "FlashGS view postprocess", error_text, error_capacity);
+        } else {
+            e = hs::precise::fuse_maps_planar(v->base.output_color3, v->reflection.output_color3,
+                                              v->base.output_other2, v->diffuse_rgb3, v->fused_rgb3,
+                                              v->reflection_rgb_map3, pixels, s);
+            if (e != cudaSuccess) return cuda_failure(e, "FlashGS view fusion", error_text, error_capacity);
         }
         const cudaError_t trailing = cudaGetLastError();
         if (trailing != cudaSuccess)

@@ -161,11 +161,15 @@ __global__ void __launch_bounds__(kThreads) standard_kernel(
 
 // kFromView: `rotation` is the row-major world_view_transform (4 x 4) and the
 // normal rotation world_view[:3,:3]^T is read from it in place.
-template <bool kFromView>
+// kFuse: also the colour fusion of the pixel from color3, refl_color3 and the
+// specular plane other2[0] (fuse_planar_pixel), for the one-view entry.
+template <bool kFromView, bool kFuse>
 __global__ void __launch_bounds__(kThreads) flashgs_kernel(
     int width, int height, const float* __restrict__ color3, const float* __restrict__ other2,
     const float* __restrict__ depth1, const float* __restrict__ alpha1,
-    const float* __restrict__ normal3, const float* __restrict__ rotation, FlashgsMaps maps) {
+    const float* __restrict__ normal3, const float* __restrict__ rotation, FlashgsMaps maps,
+    const float* __restrict__ refl_color3, float* __restrict__ diffuse, float* __restrict__ final_rgb,
+    float* __restrict__ stored) {
     const size_t plane = static_cast<size_t>(width) * height;
     float b[9];
 #pragma unroll
@@ -186,6 +190,7 @@ __global__ void __launch_bounds__(kThreads) flashgs_kernel(
         maps.dpt[p] = depth_divide(depth1[p], alpha);
         maps.spec[p] = other2[p];
         if (maps.dist != nullptr) maps.dist[p] = 0.0f;
+        if (kFuse) fuse_planar_pixel(color3, refl_color3, other2[p], plane, p, diffuse, final_rgb, stored);
     }
 }
 
@@ -391,18 +396,26 @@ cudaError_t flashgs(int width, int height, const float* color3, const float* oth
                     const float* rotation9, const FlashgsMaps& maps, cudaStream_t s) {
     const uint64_t pixels = static_cast<uint64_t>(width) * height;
     if (pixels == 0) return cudaSuccess;
-    flashgs_kernel<false><<<grid_for(pixels), kThreads, 0, s>>>(width, height, color3, other2, depth1,
-                                                                alpha1, normal3, rotation9, maps);
+    flashgs_kernel<false, false><<<grid_for(pixels), kThreads, 0, s>>>(
+        width, height, color3, other2, depth1, alpha1, normal3, rotation9, maps, nullptr, nullptr, nullptr, nullptr);
     return cudaGetLastError();
 }
 
 cudaError_t flashgs_from_view(int width, int height, const float* color3, const float* other2,
                               const float* depth1, const float* alpha1, const float* normal3,
-                              const float* world_view4x4, const FlashgsMaps& maps, cudaStream_t s) {
+                              const float* world_view4x4, const FlashgsMaps& maps, const float* reflection_color3,
+                              float* diffuse3, float* final_rgb3, float* stored3, cudaStream_t s) {
     const uint64_t pixels = static_cast<uint64_t>(width) * height;
     if (pixels == 0) return cudaSuccess;
-    flashgs_kernel<true><<<grid_for(pixels), kThreads, 0, s>>>(width, height, color3, other2, depth1,
-                                                               alpha1, normal3, world_view4x4, maps);
+    if (reflection_color3 != nullptr) {
+        flashgs_kernel<true, true><<<grid_for(pixels), kThreads, 0, s>>>(
+            width, height, color3, other2, depth1, alpha1, normal3, world_view4x4, maps, reflection_color3, diffuse3,
+            final_rgb3, stored3);
+    } else {
+        flashgs_kernel<true, false><<<grid_for(pixels), kThreads, 0, s>>>(
+            width, height, color3, other2, depth1, alpha1, normal3, world_view4x4, maps, nullptr, nullptr, nullptr,
+            nullptr);
+    }
     return cudaGetLastError();
 }
 

@@ -77,10 +77,14 @@ cudaError_t flashgs(int width, int height, const float* color3, const float* oth
                     const float* depth1, const float* alpha1, const float* normal3,
                     const float* rotation9, const FlashgsMaps& maps, cudaStream_t s);
 // flashgs() with the normal rotation world_view[:3,:3]^T read from the
-// row-major world_view_transform (_flashgs_postprocess, renderer.py:188).
+// row-major world_view_transform (_flashgs_postprocess, renderer.py:188)
+// and, when reflection_color3 is not null, the colour fusion of the view
+// (fuse_maps_planar of color3, reflection_color3 and other2 plane 0) in the
+// same pass.
 cudaError_t flashgs_from_view(int width, int height, const float* color3, const float* other2,
                               const float* depth1, const float* alpha1, const float* normal3,
-                              const float* world_view4x4, const FlashgsMaps& maps, cudaStream_t s);
+                              const float* world_view4x4, const FlashgsMaps& maps, const float* reflection_color3,
+                              float* diffuse3, float* final_rgb3, float* stored3, cudaStream_t s);
 
 }  // namespace post
 }  // namespace hs
