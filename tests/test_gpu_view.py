@@ -26,11 +26,13 @@ def dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
 
-def make_view(spec, cam, *, empty_reflection=False, sh_degree=3):
+def make_view(spec, cam, *, empty_reflection=False, sh_degree=3, empty_base=False):
     scene = scenes.make_scene(spec)
     b, r = scene["base"], scene["reflection"]
     if empty_reflection:
         r = {k: v[:0] for k, v in r.items()}
+    if empty_base:
+        b = {k: v[:0] for k, v in b.items()}
     base = {"means3d": dev(b["xyz"]), "opacities": ops.precise_sigmoid(dev(b["opacity"])),
             "scales": ops.precise_exp(dev(b["scaling"])), "rotations": ops.precise_normalize4(dev(b["rotation"])),
             "specular": ops.precise_sigmoid(dev(b["specular"])), "roughness": ops.precise_sigmoid(dev(b["roughness"])),
@@ -113,8 +115,10 @@ def check(one, ref):
         bits(one.maps[k], ref["maps"][k], k)
 
 
-def run_view(spec, cam, *, traced, depth_ratio=0.0, empty_reflection=False, torch_stream=None, sh_degree=3):
-    base, refl, trace, camera = make_view(spec, cam, empty_reflection=empty_reflection, sh_degree=sh_degree)
+def run_view(spec, cam, *, traced, depth_ratio=0.0, empty_reflection=False, torch_stream=None, sh_degree=3,
+             empty_base=False):
+    base, refl, trace, camera = make_view(spec, cam, empty_reflection=empty_reflection, sh_degree=sh_degree,
+                                          empty_base=empty_base)
     with NativeRendererContext(0) as ctx, NativeRendererContext(0) as ctx_r:
         if traced and refl["means3d"].shape[0] != 0:
             v, t = ops.gaussian_disks(refl["means3d"], refl["rotations_raw"], refl["scales"])
@@ -160,6 +164,15 @@ def test_view_with_no_reflective_gaussians():
     one = run_view(SMALL, scenes.generic_camera(SMALL, 2), traced=False, empty_reflection=True)
     assert one.trace is None and one.reflection_rays.shape == (0, 36)
     assert int(one.reflection.rendered[0]) == 0
+
+
+@pytest.mark.parametrize("empty_reflection", [False, True])
+def test_view_with_no_base_gaussians(empty_reflection):
+    """An empty base group (and both groups empty): the rasters write the
+    background, the prologue takes its two-launch form, the maps follow."""
+    one = run_view(SMALL, scenes.generic_camera(SMALL, 5), traced=False, empty_base=True,
+                   empty_reflection=empty_reflection)
+    assert one.base_colors.shape == (0, 5) and int(one.base.rendered[0]) == 0
 
 
 def test_view_benchmark_frame():
