@@ -279,9 +279,10 @@ __global__ void __launch_bounds__(kThreads) tf32_rows3_kernel(
             if (row < rows && t < 3) {
                 float v;
                 if (kPixels) {
-                    v = t == 0 ? static_cast<float>(row % static_cast<uint64_t>(width))
-                               : (t == 1 ? static_cast<float>(row / static_cast<uint64_t>(width))
-                                         : 1.0f);
+                    // pixel images hold fewer than 2^32 pixels (pixel_rays), so
+                    // the column and row come from a 32-bit division
+                    const uint32_t r32 = static_cast<uint32_t>(row), w32 = static_cast<uint32_t>(width);
+                    v = t == 0 ? static_cast<float>(r32 % w32) : (t == 1 ? static_cast<float>(r32 / w32) : 1.0f);
                 } else {
                     v = left3[3 * row + t];
                 }
@@ -344,6 +345,7 @@ cudaError_t pixel_rays(int width, int height, const float* inverse_intrinsics3x3
                        const float* rotation3x3, float* rays3, cudaStream_t s) {
     const uint64_t pixels = static_cast<uint64_t>(width) * height;
     if (pixels == 0) return cudaSuccess;
+    if (pixels > UINT32_MAX) return cudaErrorInvalidValue;
     tf32_rows3_kernel<true><<<mma_grid_for(pixels), kThreads, 0, s>>>(
         pixels, width, nullptr, inverse_intrinsics3x3, rotation3x3, rays3);
     return cudaGetLastError();
