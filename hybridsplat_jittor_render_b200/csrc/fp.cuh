@@ -69,6 +69,32 @@ __device__ __forceinline__ float diff2(int v, float a, float b, float c, float d
     if (v == 1) return fma(-c, d, mul(a, b));
     return sub(mul(a, b), mul(c, d));
 }
+// Packed pairs: the FP32x2 instructions of sm_100 (__ffma2_rn, __fmul2_rn,
+// __fadd2_rn) round each component exactly as the scalar instruction does, so
+// two independent evaluations of the same expression can issue as one
+// instruction per operation. The helpers below mirror mad / msub / dot2 /
+// diff2 with the same variant numbers; subtraction is addition of the
+// negation, which IEEE arithmetic defines to be the same operation.
+__device__ __forceinline__ float2 pair(float x) { return make_float2(x, x); }
+__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __fadd2_rn(a, neg2(b)); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 msub_x2(int v, float2 a, float2 b, float2 c) {
+    return v == 0 ? fma2(a, b, neg2(c)) : sub2(mul2(a, b), c);
+}
+__device__ __forceinline__ float2 dot2_x2(int v, float2 a, float2 b, float2 c, float2 d) {
+    if (v == 0) return fma2(a, b, mul2(c, d));
+    if (v == 1) return fma2(c, d, mul2(a, b));
+    return add2(mul2(a, b), mul2(c, d));
+}
+__device__ __forceinline__ float2 diff2_x2(int v, float2 a, float2 b, float2 c, float2 d) {
+    if (v == 0) return fma2(a, b, neg2(mul2(c, d)));
+    if (v == 1) return fma2(neg2(c), d, mul2(a, b));
+    return sub2(mul2(a, b), mul2(c, d));
+}
+
 // (a*b + c*d) + e*f: pair choice as dot2, tail 0 fused, 1 rounded.
 __device__ __forceinline__ float dot3(int vp, int vt, float a, float b, float c, float d,
                                       float e, float f) {

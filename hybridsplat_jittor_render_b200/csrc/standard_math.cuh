@@ -239,6 +239,42 @@ __device__ __forceinline__ float alpha_of(const R& r, const PixelState& s, const
     return alpha;
 }
 
+// alpha_of for a lane's two pixels (rows py0 and py1 of one column), with
+// every operation the two pixels share issued once as a packed pair (fp.cuh:
+// each component rounds as the scalar instruction of alpha_of); the
+// divisions, expf and the minima stay per pixel. Outputs as alpha_of's, for
+// pixel 0 and pixel 1.
+template <class R>
+__device__ __forceinline__ void alpha_of2(const R& r, const PixelState& s0, const PixelState& s1,
+                                          const ColumnTerms& col, float py0, float py1, const BlendRecord& g,
+                                          float& a0, float& a1, float& d0, float& d1, bool& live0, bool& live1) {
+    const float2 py = make_float2(py0, py1);
+    const int vk = r(S_K);
+    const float2 lx = msub_x2(vk, py, pair(g.twx), pair(g.tvx));
+    const float2 ly = msub_x2(vk, py, pair(g.twy), pair(g.tvy));
+    const float2 lz = msub_x2(vk, py, pair(g.twz), pair(g.tvz));
+    const int vc = r(S_CROSS);
+    const float2 kx = pair(col.kx), ky = pair(col.ky), kz = pair(col.kz);
+    const float2 pzv = diff2_x2(vc, kx, ly, ky, lx);
+    const float2 pxv = diff2_x2(vc, ky, lz, kz, ly);
+    const float2 pyv = diff2_x2(vc, kz, lx, kx, lz);
+    const float2 sx = make_float2(div(pxv.x, pzv.x), div(pxv.y, pzv.y));
+    const float2 sy = make_float2(div(pyv.x, pzv.x), div(pyv.y, pzv.y));
+    const float2 rho3d = dot2_x2(r(S_RHO3), sx, sx, sy, sy);
+    const float2 dy = sub2(pair(g.y), py);
+    const float2 rho2d = mul2(pair(2.0f), dot2_x2(r(S_RHO2), pair(col.dx), pair(col.dx), dy, dy));
+    const float2 rho = make_float2(fminf(rho3d.x, rho2d.x), fminf(rho3d.y, rho2d.y));
+    const float2 on_plane = add2(dot2_x2(r(S_DEPTH), sx, pair(g.twx), sy, pair(g.twy)), pair(g.twz));
+    d0 = rho3d.x <= rho2d.x ? on_plane.x : g.twz;
+    d1 = rho3d.y <= rho2d.y ? on_plane.y : g.twz;
+    const float2 power = mul2(pair(-0.5f), rho);
+    const float2 scaled = mul2(pair(g.op), make_float2(expf(power.x), expf(power.y)));
+    a0 = fminf(0.99f, scaled.x);
+    a1 = fminf(0.99f, scaled.y);
+    live0 = !s0.done && pzv.x != 0.0f && !(d0 < kNear) && !(power.x > 0.0f) && !(a0 < 1.0f / 255.0f);
+    live1 = !s1.done && pzv.y != 0.0f && !(d1 < kNear) && !(power.y > 0.0f) && !(a1 < 1.0f / 255.0f);
+}
+
 // The state update of blend() after its alpha test. Returns w.
 template <class R>
 __device__ __forceinline__ float apply(const R& r, PixelState& s, float alpha, float depth, const BlendRecord& g) {
@@ -274,10 +310,9 @@ __device__ __forceinline__ float apply(const R& r, PixelState& s, float alpha, f
 template <class R>
 __device__ __forceinline__ float blend2(const R& r, PixelState& s0, PixelState& s1, const ColumnTerms& col,
                                         float py0, float py1, const BlendRecord& g) {
-    float d0, d1;
+    float a0, a1, d0, d1;
     bool live0, live1;
-    const float a0 = alpha_of(r, s0, col, py0, g, d0, live0);
-    const float a1 = alpha_of(r, s1, col, py1, g, d1, live1);
+    alpha_of2(r, s0, s1, col, py0, py1, g, a0, a1, d0, d1, live0, live1);
     float w = 0.0f;
     if (live0) w = apply(r, s0, a0, d0, g);
     if (live1) w += apply(r, s1, a1, d1, g);
