@@ -295,9 +295,9 @@ __global__ void __launch_bounds__(kRenderThreads) render_kernel(
         }
         const float fx = static_cast<float>(px);
         const float fy0 = static_cast<float>(py0), fy1 = static_cast<float>(py1);
-        PixelState s0, s1;
-        pixel_init(s0);
-        pixel_init(s1);
+        const float2 fy = make_float2(fy0, fy1);
+        PixelPair sp;
+        pair_init(sp);
         const int n = range.y - range.x;
         bool warp_done = false;
         int warp_done_at = 0;
@@ -316,9 +316,8 @@ __global__ void __launch_bounds__(kRenderThreads) render_kernel(
                 for (int j = 0; j < nb; ++j) {
                     const BlendRecord g = load_record(batch + j * 5);
                     const ColumnTerms col = column_terms(r, fx, g);
-                    blend(r, s0, col, fy0, g);
-                    blend(r, s1, col, fy1, g);
-                    if (__all_sync(0xffffffffu, s0.t < 0.0001f && s1.t < 0.0001f)) {
+                    blend_pair(r, sp, col, fy, g);
+                    if (__all_sync(0xffffffffu, sp.t.x < 0.0001f && sp.t.y < 0.0001f)) {
                         warp_done = true;
                         warp_done_at = base + j;
                         cursor = j + 1;
@@ -335,13 +334,12 @@ __global__ void __launch_bounds__(kRenderThreads) render_kernel(
             for (int j = cursor; j < stop; ++j) {
                 const BlendRecord g = load_record(batch + j * 5);
                 const ColumnTerms col = column_terms(r, fx, g);
-                blend(r, s0, col, fy0, g);
-                blend(r, s1, col, fy1, g);
+                blend_pair(r, sp, col, fy, g);
             }
             if (tile_end != INT_MAX) break;
         }
-        if (in0) store_pixel(r, s0, bg, out, plane, static_cast<size_t>(py0) * width + px);
-        if (in1) store_pixel(r, s1, bg, out, plane, static_cast<size_t>(py1) * width + px);
+        if (in0) store_pixel(r, pixel_of(sp, 0), bg, out, plane, static_cast<size_t>(py0) * width + px);
+        if (in1) store_pixel(r, pixel_of(sp, 1), bg, out, plane, static_cast<size_t>(py1) * width + px);
     }
 }
 

@@ -373,6 +373,94 @@ __device__ __forceinline__ void blend(const R& r, PixelState& s, const ColumnTer
     s.nz = mad(va, g.nz, w, s.nz);
 }
 
+// The states of a lane's two pixels (rows py0 and py1 of one column), member
+// by member as pairs (.x: py0, .y: py1), so that blend_pair can update both
+// with packed FP32x2 instructions.
+struct PixelPair {
+    float2 cr, cg, cb, o0, o1, t, d, m1, m2, dist, median, nx, ny, nz;
+};
+
+__device__ __forceinline__ void pair_init(PixelPair& s) {
+    s.cr = s.cg = s.cb = s.o0 = s.o1 = pair(0.0f);
+    s.t = pair(1.0f);
+    s.d = s.m1 = s.m2 = s.dist = s.median = pair(0.0f);
+    s.nx = s.ny = s.nz = pair(0.0f);
+}
+
+// The state of pixel `which` (0: .x, 1: .y) of a pair.
+__device__ __forceinline__ PixelState pixel_of(const PixelPair& p, int which) {
+    auto c = [which](float2 v) { return which == 0 ? v.x : v.y; };
+    PixelState s;
+    s.cr = c(p.cr);
+    s.cg = c(p.cg);
+    s.cb = c(p.cb);
+    s.o0 = c(p.o0);
+    s.o1 = c(p.o1);
+    s.t = c(p.t);
+    s.d = c(p.d);
+    s.m1 = c(p.m1);
+    s.m2 = c(p.m2);
+    s.dist = c(p.dist);
+    s.median = c(p.median);
+    s.nx = c(p.nx);
+    s.ny = c(p.ny);
+    s.nz = c(p.nz);
+    return s;
+}
+
+// blend() of one Gaussian at both pixels of a pair: every operation of
+// blend() issued once as a packed pair (fp.cuh: each component rounds as the
+// scalar instruction), except the divisions, expf, the minima and the median
+// selection, which stay per pixel. Each component equals blend() of that
+// pixel.
+template <class R>
+__device__ __forceinline__ void blend_pair(const R& r, PixelPair& s, const ColumnTerms& col, float2 py,
+                                           const BlendRecord& g) {
+    const int vk = r(S_K);
+    const float2 kx = pair(col.kx), ky = pair(col.ky), kz = pair(col.kz);
+    const float2 lx = msub_x2(vk, py, pair(g.twx), pair(g.tvx));
+    const float2 ly = msub_x2(vk, py, pair(g.twy), pair(g.tvy));
+    const float2 lz = msub_x2(vk, py, pair(g.twz), pair(g.tvz));
+    const int vc = r(S_CROSS);
+    const float2 pxv = diff2_x2(vc, ky, lz, kz, ly);
+    const float2 pyv = diff2_x2(vc, kz, lx, kx, lz);
+    const float2 pzv = diff2_x2(vc, kx, ly, ky, lx);
+    const float2 sx = make_float2(div(pxv.x, pzv.x), div(pxv.y, pzv.y));
+    const float2 sy = make_float2(div(pyv.x, pzv.x), div(pyv.y, pzv.y));
+    const float2 rho3d = dot2_x2(r(S_RHO3), sx, sx, sy, sy);
+    const float2 dx = pair(col.dx);
+    const float2 dy = sub2(pair(g.y), py);
+    const float2 rho2d = mul2(pair(2.0f), dot2_x2(r(S_RHO2), dx, dx, dy, dy));
+    const float2 rho = make_float2(fminf(rho3d.x, rho2d.x), fminf(rho3d.y, rho2d.y));
+    const float2 on_plane = add2(dot2_x2(r(S_DEPTH), sx, pair(g.twx), sy, pair(g.twy)), pair(g.twz));
+    const float2 depth = make_float2(rho3d.x <= rho2d.x ? on_plane.x : g.twz, rho3d.y <= rho2d.y ? on_plane.y : g.twz);
+    const float2 power = mul2(pair(-0.5f), rho);
+    const float2 scaled = mul2(pair(g.op), make_float2(expf(power.x), expf(power.y)));
+    const float2 alpha = make_float2(fminf(0.99f, scaled.x), fminf(0.99f, scaled.y));
+    const float2 w = mul2(alpha, s.t);
+    const int va = r(S_ACC);
+    s.cr = mad_x2(va, pair(g.r), w, s.cr);
+    s.cg = mad_x2(va, pair(g.g), w, s.cg);
+    s.cb = mad_x2(va, pair(g.b), w, s.cb);
+    s.t = r(S_T) == 0 ? fma2(neg2(alpha), s.t, s.t) : sub2(s.t, w);
+    s.o0 = mad_x2(va, pair(g.spec), w, s.o0);
+    s.o1 = mad_x2(va, pair(g.rough), w, s.o1);
+    const float2 a = sub2(pair(1.0f), s.t);
+    const float2 m = mul2(pair(kFar / (kFar - kNear)),
+                          sub2(pair(1.0f), make_float2(div(kNear, depth.x), div(kNear, depth.y))));
+    const float2 mm = mul2(m, m);
+    const float2 dd = nmad_x2(r(S_D2), mad_x2(r(S_D1), mm, a, s.m2), mul2(pair(2.0f), m), s.m1);
+    s.dist = mad_x2(va, dd, w, s.dist);
+    s.m1 = mad_x2(va, m, w, s.m1);
+    s.m2 = mad_x2(va, mm, w, s.m2);
+    if (s.t.x > 0.5f) s.median.x = depth.x;
+    if (s.t.y > 0.5f) s.median.y = depth.y;
+    s.d = mad_x2(va, depth, w, s.d);
+    s.nx = mad_x2(va, pair(g.nx), w, s.nx);
+    s.ny = mad_x2(va, pair(g.ny), w, s.ny);
+    s.nz = mad_x2(va, pair(g.nz), w, s.nz);
+}
+
 // write_output (render.cu:143-183) for one pixel: returns the 12 output
 // values in the channel order color3, other2, depth, alpha, normal3,
 // median, distortion.

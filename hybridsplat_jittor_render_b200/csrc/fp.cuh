@@ -81,6 +81,12 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __fadd2_rn(a, neg2(b)); }
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mad_x2(int v, float2 a, float2 b, float2 c) {
+    return v == 0 ? fma2(a, b, c) : add2(mul2(a, b), c);
+}
+__device__ __forceinline__ float2 nmad_x2(int v, float2 x, float2 a, float2 b) {
+    return v == 0 ? fma2(neg2(a), b, x) : sub2(x, mul2(a, b));
+}
 __device__ __forceinline__ float2 msub_x2(int v, float2 a, float2 b, float2 c) {
     return v == 0 ? fma2(a, b, neg2(c)) : sub2(mul2(a, b), c);
 }
