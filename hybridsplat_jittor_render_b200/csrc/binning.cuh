@@ -60,6 +60,24 @@ inline uint64_t scan_scratch_bytes(uint32_t count) {
     return (static_cast<uint64_t>(scan_tiles(count > 0 ? count : 1)) + 64) * sizeof(uint32_t);
 }
 
+// The next pair slot of Gaussian `owner` for the calling lane. The lanes of
+// the warp that take a slot of the same Gaussian at this call share one
+// shared-memory atomic (the leader fetches the base for all of them, each adds
+// its rank among them) instead of issuing one atomic each on the same address,
+// which the hardware serialises. Slots of one Gaussian are handed out in some
+// order either way: its pairs name different tiles, and the stable tile sort
+// that follows makes their order irrelevant.
+__device__ __forceinline__ uint32_t take_slot(uint32_t* cursor, uint32_t owner) {
+    const uint32_t active = __activemask();
+    const uint32_t peers = __match_any_sync(active, owner);
+    const int lane = threadIdx.x & 31;
+    const int leader = __ffs(peers) - 1;
+    uint32_t first = 0;
+    if (lane == leader) first = atomicAdd(&cursor[owner], static_cast<uint32_t>(__popc(peers)));
+    first = __shfl_sync(peers, first, leader);
+    return first + static_cast<uint32_t>(__popc(peers & ((1u << lane) - 1u)));
+}
+
 __device__ __forceinline__ uint32_t warp_sum(uint32_t v) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -230,7 +248,7 @@ __global__ void __launch_bounds__(kEmitThreads) emit_flat_compact_kernel(
         const uint32_t k = f - (j == 0 ? 0u : inclusive[owner - 1]);
         uint32_t tile, tag = 0;
         if (em.pair_at(shapes[owner], owner, k, tile, tag, cache)) {
-            const uint32_t slot = atomicAdd(&cursor[owner], 1u);
+            const uint32_t slot = take_slot(cursor, owner);
             if (slot < counted[owner]) {
                 tile_ids[offsets[owner] + slot] = tile;
                 values[offsets[owner] + slot] = (blockIdx.x * kEmitThreads + owner) | tag;

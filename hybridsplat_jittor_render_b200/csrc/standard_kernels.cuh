@@ -314,7 +314,7 @@ static __global__ void __launch_bounds__(kEmitRowThreads) emit_rows_kernel(
             uint32_t tag = 0;
             if (masked) tag = (w.never ? 0xfu : quadrant_mask(w.top, w.bottom, tx)) << kIndexBits;
             const uint32_t owner = w.owner;
-            const uint32_t slot = atomicAdd(&cursor[owner], 1u);
+            const uint32_t slot = bin::take_slot(cursor, owner);
             if (slot < counted[owner]) {
                 const uint32_t at = offsets[owner] + slot;
                 tile_ids[at] = static_cast<uint32_t>(w.ty) * grid_x + static_cast<uint32_t>(tx);
