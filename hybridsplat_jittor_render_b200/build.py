@@ -65,6 +65,7 @@ SOURCES = [
     ("sort.cu", "cuda", []),
     ("trace.cu", "cuda", []),
     ("view.cu", "cuda", []),
+    ("pair_check.cu", "cuda", []),
     ("precise.cu", "cuda", ["--fmad=false"]),
     ("precise_exp.cu", "cuda", []),
     ("postprocess.cu", "cuda", []),

@@ -26,6 +26,7 @@
 #include "context.h"
 #include "postprocess.h"
 #include "view.h"
+#include "pair_check.h"
 #include "precise.h"
 
 namespace hs {
@@ -2209,6 +2210,18 @@ int32_t hs_b200_flashgs_view_v2(const HsB200FlashgsViewV2* v, char* error_text,
         const cudaError_t trailing = cudaGetLastError();
         if (trailing != cudaSuccess)
             return cuda_failure(trailing, "FlashGS view execution", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_b200_test_pair_ops_v1(const float* a, const float* b, const float* c, const float* d, uint64_t count,
+                                 uint32_t* mismatches16, char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (mismatches16 == nullptr || (count >= 2 && (a == nullptr || b == nullptr || c == nullptr || d == nullptr))) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "pair check received a null buffer", error_text, error_capacity);
+        }
+        const cudaError_t e = hs::pair_check(a, b, c, d, count, mismatches16, nullptr);
+        if (e != cudaSuccess) return cuda_failure(e, "pair check", error_text, error_capacity);
         return ok(error_text, error_capacity);
     });
 }

@@ -383,6 +383,19 @@ typedef struct HsB200FlashgsViewV2 {
 HS_API int32_t hs_b200_flashgs_view_v2(
     const HsB200FlashgsViewV2* view, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
 
+/* Self-check of the packed FP32x2 arithmetic the rasterisers use (each lane
+ * evaluates two pixels with sm_100 pair instructions whose components must
+ * round exactly as the scalar instructions): for the count / 2 input pairs
+ * (a, b, c, d at 2i and 2i + 1), every packed helper variant is compared bit
+ * for bit, per component, with the scalar helper; mismatches16[k] receives
+ * the number of differing pairs of operation k (mul, add, sub, fma, the two
+ * mad, the two msub and the two nmad forms, the three dot2 and the three
+ * diff2 forms). Device pointers; legacy default stream. A test entry; no
+ * counterpart in the reference library. */
+HS_API int32_t hs_b200_test_pair_ops_v1(
+    const float* a, const float* b, const float* c, const float* d, uint64_t count,
+    uint32_t* mismatches16, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
+
 /* The standard branch's colours in one pass: hs_rasterizer_precise_direction_f32_v1
  * of points[count,3] from center3, hs_rasterizer_precise_sh_to_rgb_f32_v1 of
  * sh[count,3,coefficient_count] (channel-major, as the reference passes its
