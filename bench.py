@@ -20,7 +20,12 @@ reference's hs_optix_* entry points).
 
 A step is one library call per view (hs_b200_standard_view_v2 or
 hs_b200_flashgs_view_v2, the same steps in the same order); --no-view-entry
-issues them as the session's separate calls instead.
+issues them as the session's separate calls instead. The frames run on a
+stream of their own, with the camera written into one device buffer and the
+standard view's outputs written into three sets used in turn, so that the
+standard view entry replays each set's captured graph
+(hs_b200_view_graph_stats_v1, `view_graphs` in the line); --no-view-graphs
+queues every view directly.
 
 Both steps end with the session's raw-map postprocess of the base raster
 (standard: camera matrices and TF32 pixel rays on a side stream beside the
@@ -100,6 +105,7 @@ FLOP_FLASHGS = 75
 HEADLINE_MIN_SECONDS, HEADLINE_MIN_REPEATS = 3.0, 10
 BLOCK_MIN_SECONDS, BLOCK_MIN_REPEATS = 1.0, 5
 MAX_REPEATS = 2000
+VIEW_OUTPUT_SETS = 3
 
 
 def parse_args():
@@ -128,6 +134,8 @@ def parse_args():
                    help="with --profile-frames: trace the reflection colours of every frame")
     p.add_argument("--no-view-entry", action="store_true",
                    help="standard views as the session's separate calls instead of hs_b200_standard_view_v2")
+    p.add_argument("--no-view-graphs", action="store_true",
+                   help="queue every standard view directly (HS_B200_VIEW_GRAPHS=0): no captured graph replays")
     return p.parse_args()
 
 
@@ -313,6 +321,13 @@ class Frame:
         # run sequentially.
         self.view_entry = hasattr(lib, f"hs_b200_{backend}_view_v2")
         self.raster_event = None  # one-call views record it when their renderers may start
+        # the standard view's outputs and its camera row on the device: three
+        # sets used in turn (next_slot: the set of the next view); a set is
+        # rewritten only after its read-back is queued
+        self.view_outs = [None] * VIEW_OUTPUT_SETS
+        self.cam_slots = [None] * VIEW_OUTPUT_SETS
+        self.cam_dev = None
+        self.next_slot = 0
 
     def enable_trace(self) -> float:
         """Builds the reflection trace scene of the session (the disks of the
@@ -354,15 +369,26 @@ class Frame:
         if self.ctx_r is not self.ctx:
             self.ctx_r.close()
 
-    def set_camera(self, cam, upload_from=None):
-        """Per-view camera state. For the standard backend the matrices are
-        device tensors (uploaded from pinned host memory when given)."""
+    def camera_buffer(self, slot: int, like):
+        """The device camera row of output set `slot` (allocated like `like`)."""
+        buf = self.cam_slots[slot]
+        if buf is None or buf.shape != like.shape:
+            buf = self.cam_slots[slot] = self.torch.empty(like.shape, dtype=like.dtype, device=self.device)
+        return buf
+
+    def set_camera(self, cam, upload_from=None, uploaded=False):
+        """Per-view camera state: the row (view and projection matrices,
+        centre) in the camera buffer of the next view's output set, copied
+        from `upload_from` (pinned host or device memory) or from the camera
+        on the current stream, or (uploaded) already written there."""
         torch = self.torch
         self.cam = cam
         host = upload_from if upload_from is not None else torch.from_numpy(camera_row(cam, self.scenes))
-        self.cam_dev = host.to(self.device, non_blocking=True)
-        self.view, self.proj, self.center = self.cam_dev[:16].view(4, 4), self.cam_dev[16:32].view(4, 4), \
-            self.cam_dev[32:35]
+        buf = self.camera_buffer(self.next_slot, host)
+        if not uploaded:
+            buf.copy_(host, non_blocking=True)
+        self.cam_dev = buf
+        self.view, self.proj, self.center = buf[:16].view(4, 4), buf[16:32].view(4, 4), buf[32:35]
         # FlashGS takes the camera as host values; the device row gives the
         # ray centre and the postprocess's normal rotation
 
@@ -507,12 +533,18 @@ class Frame:
         if self.with_post:
             post = {"fov_x": 2.0 * math.atan(cam.tan_fovx), "fov_y": 2.0 * math.atan(cam.tan_fovy),
                     "depth_ratio": 0.0}
+        slot = self.next_slot
+        self.next_slot = (slot + 1) % VIEW_OUTPUT_SETS
+        reuse = self.view_outs[slot]
+        if reuse is not None and (reuse.trace is None) != (trace is None):
+            reuse = None
         out = self.ops.standard_view(base, refl, self.view, self.proj, self.center, self.bg5, width=cam.width,
                                      height=cam.height, tan_fovx=cam.tan_fovx, tan_fovy=cam.tan_fovy, sh_degree=3,
                                      base_context=self.ctx, reflection_context=self.ctx_r, trace=trace,
                                      postprocess=post,
                                      stream=torch.cuda.current_stream(self.device).cuda_stream,
-                                     raster_begin_event=self.raster_event)
+                                     raster_begin_event=self.raster_event, out=reuse)
+        self.view_outs[slot] = out
         return out.base, out.reflection, out.fused, out.reflection_rays, out.maps
 
     def maps_for_host(self, result):
@@ -895,9 +927,19 @@ def run_block(job: Job, args, scene: DeviceScene, workload: Workload, backend: s
 
 def run_ours(args, workload: Workload) -> int:
     import torch
+    if args.no_view_graphs:
+        os.environ["HS_B200_VIEW_GRAPHS"] = "0"
+    job = Job()
+    # the frames on a stream of their own (a graph capture needs a stream
+    # other than the legacy default stream)
+    with torch.cuda.stream(torch.cuda.Stream(device=job.device)):
+        return run_ours_on_stream(job, args, workload)
+
+
+def run_ours_on_stream(job, args, workload: Workload) -> int:
+    import torch
     from hybridsplat_jittor_render_b200 import multigpu, scenes
 
-    job = Job()
     device = job.device
     world = job.world
     spec = scenes.SCENES[workload.scene]
@@ -967,6 +1009,10 @@ def run_ours(args, workload: Workload) -> int:
                                           "reference rebuild's frame has none (its postprocess is Jittor code)"},
                 "stages_ms": stages, "clocks": clocks.summary(), "e2e": e2e,
                 "gpu_launches": frame.launches_per_step(spec.width, spec.height) * args.steps * t["repeats"]}
+        if frame.one_call() and args.backend == "standard":
+            line["view_graphs"] = dict(frame.ops.view_graph_stats(frame.ctx), enabled=not args.no_view_graphs,
+                                       what="standard views replayed as captured graphs "
+                                            "(hs_b200_view_graph_stats_v1 on the base context, whole run)")
     if world == 1 and line is not None:
         # single GPU: render-kernel roofline, CPU baseline, reference CUDA rebuild
         line.update(roofline_and_baselines(args, workload, frame, cams, scene, stages, line["clocks"], ms))
@@ -1046,6 +1092,25 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
 
     at_raster = args.readback == "at-raster" and frame.one_call()
     raster_events = [torch.cuda.Event() for _ in range(2)] if at_raster else None
+    # frame s writes output set s % 3 (standard view entry): after the
+    # read-back of the frame that last wrote it
+    copied = [torch.cuda.Event() for _ in range(VIEW_OUTPUT_SETS)]
+    copy_queued = [False] * VIEW_OUTPUT_SETS
+    # frame s's camera row goes to camera set s % 3 on an upload stream,
+    # queued before frame s - 1 is rendered (after the frame that last read
+    # that set): the upload does not wait in the frame stream's queue
+    upload_stream = torch.cuda.Stream(device=frame.device)
+    uploaded = [torch.cuda.Event() for _ in range(VIEW_OUTPUT_SETS)]
+    rendered = [None] * VIEW_OUTPUT_SETS
+
+    def upload(s):
+        slot = s % VIEW_OUTPUT_SETS
+        buf = frame.camera_buffer(slot, pinned_cam[s])
+        if rendered[slot] is not None:
+            upload_stream.wait_event(rendered[slot])
+        with torch.cuda.stream(upload_stream):
+            buf.copy_(pinned_cam[s], non_blocking=True)
+        uploaded[slot].record(upload_stream)
 
     def read_back(s, out, done):
         copy_stream.wait_event(done)
@@ -1055,19 +1120,29 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
             for dst, src in zip(host_maps[s % 2], frame.maps_for_host(out)):
                 dst.copy_(src, non_blocking=True)
                 src.record_stream(copy_stream)
+            copied[s % VIEW_OUTPUT_SETS].record(copy_stream)
+            copy_queued[s % VIEW_OUTPUT_SETS] = True
 
     def run(first, count):
         pending = None
+        upload(first)
         for s in range(first, first + count):
             if args.readback == "before-call" and pending is not None:
                 read_back(*pending)
                 pending = None
-            frame.set_camera(cams[s], upload_from=pinned_cam[s])
+            frame.next_slot = s % VIEW_OUTPUT_SETS
+            stream.wait_event(uploaded[s % VIEW_OUTPUT_SETS])
+            frame.set_camera(cams[s], upload_from=pinned_cam[s], uploaded=True)
+            if s + 1 < first + count:
+                upload(s + 1)
             if at_raster:
                 frame.raster_event = raster_events[s % 2]
+            if copy_queued[s % VIEW_OUTPUT_SETS]:
+                stream.wait_event(copied[s % VIEW_OUTPUT_SETS])
             out = frame.render()
             done = torch.cuda.Event()
             done.record(stream)
+            rendered[s % VIEW_OUTPUT_SETS] = done
             if pending is not None:
                 read_back(*pending)
             pending = (s, out, done)

@@ -41,6 +41,26 @@ static __global__ void publish_totals_kernel(const uint32_t* __restrict__ totals
     __threadfence_system();
 }
 
+// The status of the raster calls of one graph replay, for the host: per call
+// (blockIdx.x) its first three totals words (rendered, prefiltered
+// violation, emitted pairs) and its wait-status word, to the call's mapped
+// totals block. Launched on a branch of the graph that follows every call's
+// binning, so that no renderer waits for these stores to reach the host.
+struct ViewStatusCall {
+    const uint32_t* totals;
+    const uint32_t* error;
+    volatile uint32_t* host;
+};
+struct ViewStatusArgs {
+    ViewStatusCall call[2];
+};
+static __global__ void view_status_kernel(ViewStatusArgs a) {
+    const ViewStatusCall c = a.call[blockIdx.x];
+    if (threadIdx.x < 3) c.host[threadIdx.x] = c.totals[threadIdx.x];
+    if (threadIdx.x == 3) c.host[3] = *reinterpret_cast<const volatile uint32_t*>(c.error);
+    __threadfence_system();
+}
+
 // Allocates the mapped pinned totals block of a context: *host for the host,
 // *device for kernels.
 inline cudaError_t alloc_mapped_totals(uint32_t** host, uint32_t** device) {
@@ -159,11 +179,14 @@ inline unsigned ranges_grid(uint32_t pair_count) {
     return static_cast<unsigned>(blocks < 148 * 8 ? (blocks > 0 ? blocks : 1) : 148 * 8);
 }
 
+// bound (device word, may be null): only the first min(*bound, pair_count)
+// pairs are read, for a grid sized by a capacity.
 template <class Range>
 __global__ void __launch_bounds__(kRangeThreads) ranges_kernel(
     uint32_t pair_count, uint32_t tile_count, const uint32_t* __restrict__ tile_ids,
-    Range* __restrict__ ranges) {
+    Range* __restrict__ ranges, const uint32_t* __restrict__ bound = nullptr) {
     using Index = decltype(ranges[0].x);
+    if (bound != nullptr) pair_count = min(*bound, pair_count);
     const uint32_t quads = (pair_count + 3u) / 4u;
     for (uint32_t q = blockIdx.x * kRangeThreads + threadIdx.x; q < quads;
          q += gridDim.x * kRangeThreads) {

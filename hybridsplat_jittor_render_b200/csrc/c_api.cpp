@@ -16,7 +16,9 @@
 #include <climits>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <exception>
 #include <mutex>
 #include <new>
@@ -653,6 +655,108 @@ hs::TraceCall view_trace_call(const View& v, uint64_t rays, const float* means3d
     t.output_wet1 = v.trace_wet1;
     t.stream = stream;
     return t;
+}
+
+// ---- graph replays of the one-view entries ----
+
+constexpr size_t kMaxViewGraphs = 4;
+
+// HS_B200_VIEW_GRAPHS=0 turns the replays off (every view queued directly).
+bool view_graphs_enabled() {
+    const char* flag = std::getenv("HS_B200_VIEW_GRAPHS");
+    return flag == nullptr || std::strcmp(flag, "0") != 0;
+}
+
+template <class T>
+void key_put(std::vector<unsigned char>& key, const T& value) {
+    const unsigned char* p = reinterpret_cast<const unsigned char*>(&value);
+    key.insert(key.end(), p, p + sizeof(T));
+}
+
+// What a captured view depends on: the entry's argument block (every pointer,
+// size, scalar and the stream) and, per context, the buffers the graph reads
+// and writes (their addresses and sizes).
+std::vector<unsigned char> view_graph_key(const void* args, size_t bytes, HsRasterizerContext* const* contexts,
+                                          uint32_t count) {
+    const unsigned char* a = static_cast<const unsigned char*>(args);
+    std::vector<unsigned char> key(a, a + bytes);
+    for (uint32_t i = 0; i < count; ++i) {
+        const HsRasterizerContext* c = contexts[i];
+        key_put(key, c);
+        for (const hs::DeviceBuffer* b : {&c->std_geometry, &c->std_image, &c->std_binning, &c->fg_gaussian,
+                                          &c->fg_pairs, &c->fg_sort, &c->fg_ranges}) {
+            key_put(key, b->ptr);
+            key_put(key, b->bytes);
+        }
+        key_put(key, c->std_total_mapped);
+        key_put(key, c->fg_total_mapped);
+        key_put(key, c->device_error);
+        key_put(key, c->side_stream);
+        key_put(key, c->math_workspace);
+        key_put(key, c->math_workspace_bytes);
+    }
+    return key;
+}
+
+HsRasterizerContext::ViewGraph* find_view_graph(HsRasterizerContext* c, const std::vector<unsigned char>& key) {
+    for (HsRasterizerContext::ViewGraph& g : c->view_graphs) {
+        if (g.key == key) return &g;
+    }
+    return nullptr;
+}
+
+// Keeps at most kMaxViewGraphs, dropping the least recently used (an
+// executable still in flight is freed when it completes).
+HsRasterizerContext::ViewGraph* insert_view_graph(HsRasterizerContext* c, std::vector<unsigned char> key,
+                                                  cudaGraphExec_t exec, const uint32_t* capacity) {
+    if (c->view_graphs.size() >= kMaxViewGraphs) {
+        auto oldest = std::min_element(c->view_graphs.begin(), c->view_graphs.end(),
+                                       [](const auto& x, const auto& y) { return x.last_use < y.last_use; });
+        if (oldest->exec != nullptr) cudaGraphExecDestroy(oldest->exec);
+        c->view_graphs.erase(oldest);
+    }
+    HsRasterizerContext::ViewGraph g;
+    g.key = std::move(key);
+    g.exec = exec;
+    g.capacity[0] = capacity[0];
+    g.capacity[1] = capacity[1];
+    g.last_use = ++c->view_graph_clock;
+    c->view_graphs.push_back(std::move(g));
+    return &c->view_graphs.back();
+}
+
+// Captures queue(true) on `stream` into an uploaded executable graph; null
+// when the capture or the instantiation fails (the view then runs directly).
+// After a failed queue every branch stream is joined back so that the
+// capture can end.
+template <class Queue>
+cudaGraphExec_t capture_view(cudaStream_t stream, const Queue& queue, std::initializer_list<cudaStream_t> branches,
+                             cudaEvent_t join_event) {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    if (cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    const bool queued = queue();
+    if (!queued) {
+        for (cudaStream_t b : branches) {
+            if (b != nullptr && cudaEventRecord(join_event, b) == cudaSuccess)
+                (void)cudaStreamWaitEvent(stream, join_event, 0);
+        }
+    }
+    const cudaError_t end = cudaStreamEndCapture(stream, &graph);
+    if (queued && end == cudaSuccess && graph != nullptr) {
+        if (cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
+            exec = nullptr;
+        } else if (cudaGraphUpload(exec, stream) != cudaSuccess) {
+            cudaGraphExecDestroy(exec);
+            exec = nullptr;
+        }
+    }
+    if (graph != nullptr) cudaGraphDestroy(graph);
+    (void)cudaGetLastError();
+    return exec;
 }
 
 }  // namespace
@@ -1534,9 +1638,12 @@ namespace {
 // The view's camera terms of the standard postprocess on `stream`
 // (hs_b200_postprocess_camera_f32_v1 after its argument checks; the caller
 // holds h's mutex on h's device).
+// captured: queued inside a stream capture, whose caller orders the graph's
+// launches after view_camera_event and records it after them (an event
+// recorded outside a capture cannot be waited on inside it).
 int32_t camera_terms(HsRasterizerContext* h, int32_t width, int32_t height, double fov_x, double fov_y,
                      const float* world_view4x4, float* camera30, float* rays_n3, cudaStream_t stream,
-                     char* error_text, uint64_t error_capacity) {
+                     char* error_text, uint64_t error_capacity, bool captured = false) {
     const uint64_t count = static_cast<uint64_t>(width) * static_cast<uint64_t>(height);
     // The intrinsics as depth_to_normal builds them (math.py:338-389):
     // focal = float32(length) / float32(2 tan(float32(fov) / 2)) with the
@@ -1556,7 +1663,7 @@ int32_t camera_terms(HsRasterizerContext* h, int32_t width, int32_t height, doub
     cudaError_t ce = cudaSuccess;
     if (h->view_camera_event == nullptr) {
         ce = cudaEventCreateWithFlags(&h->view_camera_event, cudaEventDisableTiming);
-    } else {
+    } else if (!captured) {
         ce = cudaStreamWaitEvent(s, h->view_camera_event, 0);
     }
     if (ce == cudaSuccess) ce = hs::post::camera_inputs(fx, cx, fy, cy, world_view4x4, k9, wt16, s);
@@ -1606,8 +1713,10 @@ int32_t camera_terms(HsRasterizerContext* h, int32_t width, int32_t height, doub
         if (ce == cudaSuccess) ce = hs::post::pixel_rays(width, height, camera30, camera30 + 9, rays_n3, s);
         if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera rays", error_text, error_capacity);
     }
-    ce = cudaEventRecord(h->view_camera_event, s);
-    if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera event", error_text, error_capacity);
+    if (!captured) {
+        ce = cudaEventRecord(h->view_camera_event, s);
+        if (ce != cudaSuccess) return cuda_failure(ce, "postprocess_camera event", error_text, error_capacity);
+    }
     h->math_matmul_calls += 2;
     return HS_STATUS_OK;
 }
@@ -2029,71 +2138,175 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
             return fail(HS_STATUS_INVALID_ARGUMENT, "OptiX scene is not built", error_text, error_capacity);
         }
         const cudaStream_t s = static_cast<cudaStream_t>(v->stream);
-        cudaError_t e = cudaSuccess;
-        // postprocess camera terms: only the camera, so beside everything else
-        if (post) {
-            e = hs::ensure_post_stream(base);
-            if (e == cudaSuccess) e = cudaEventRecord(base->post_fork_event, s);
-            if (e == cudaSuccess) e = cudaStreamWaitEvent(base->post_stream, base->post_fork_event, 0);
-            if (e != cudaSuccess) return cuda_failure(e, "standard view fork", error_text, error_capacity);
-            const int32_t ps = camera_terms(base, v->width, v->height, v->fov_x, v->fov_y, v->viewmatrix4x4,
-                                            v->camera30, v->pixel_rays3, base->post_stream, error_text,
-                                            error_capacity);
-            if (ps != HS_STATUS_OK) return ps;
-            e = cudaEventRecord(base->post_done_event, base->post_stream);
-            if (e != cudaSuccess) return cuda_failure(e, "standard view join", error_text, error_capacity);
-        }
-        // base colours, reflection preparation, trace, reflection colours
         const bool traced = v->trace == 1;
-        // base colours, and the reflection's prefix, normal column, suffix and
-        // (traced) ray split or (untraced) colours, side by side in one grid
-        e = hs::precise::view_prologue(
-            v->base_sh, v->sh_coefficients, v->sh_degree, v->base.means3d, v->camera_position3, v->base.specular,
-            v->base.roughness, nb, v->base.colors5, v->reflection_rotation_raw4, v->reflection.means3d, nr,
-            v->reflection_rotation9, v->reflection_normal3, v->reflection_rays36,
-            traced ? v->reflection_ray_origins3 : nullptr, traced ? v->reflection_ray_directions3 : nullptr,
-            v->reflection_rgb3, v->reflection.specular, v->reflection.roughness,
-            traced ? nullptr : v->reflection.colors5, s);
-        if (e != cudaSuccess) return cuda_failure(e, "standard view preparation", error_text, error_capacity);
-        if (traced && nr != 0) {
-            const hs::TraceCall t = view_trace_call(*v, nr, v->reflection.means3d, v->reflection_shs,
-                                                    v->reflection_others2, v->reflection.opacities,
-                                                    v->reflection.scales2, v->reflection.rotations4,
-                                                    v->viewmatrix4x4, v->projmatrix4x4, v->camera_position3, s);
-            e = hs::trace_rays(refl, t);
-            if (e != cudaSuccess) return cuda_failure(e, "reflection trace", error_text, error_capacity);
-            e = hs::view::colors5(v->trace_rgb3, v->reflection.specular, v->reflection.roughness, nr,
-                                  v->reflection.colors5, s);
-            if (e != cudaSuccess) return cuda_failure(e, "standard view colours", error_text, error_capacity);
+        // Queues the whole view on s. captured: inside a stream capture of s,
+        // with the raster calls sized for their pair capacities: nothing
+        // waits on the host, and a branch after both calls' binning publishes
+        // their status for the host (signal_event).
+        auto queue_view = [&](const hs::StandardCall* view_calls, bool captured) -> int32_t {
+            cudaError_t e = cudaSuccess;
+            // postprocess camera terms: only the camera, so beside everything else
+            if (post) {
+                e = hs::ensure_post_stream(base);
+                if (e == cudaSuccess) e = cudaEventRecord(base->post_fork_event, s);
+                if (e == cudaSuccess) e = cudaStreamWaitEvent(base->post_stream, base->post_fork_event, 0);
+                if (e != cudaSuccess) return cuda_failure(e, "standard view fork", error_text, error_capacity);
+                const int32_t ps = camera_terms(base, v->width, v->height, v->fov_x, v->fov_y, v->viewmatrix4x4,
+                                                v->camera30, v->pixel_rays3, base->post_stream, error_text,
+                                                error_capacity, captured);
+                if (ps != HS_STATUS_OK) return ps;
+                e = cudaEventRecord(base->post_done_event, base->post_stream);
+                if (e != cudaSuccess) return cuda_failure(e, "standard view join", error_text, error_capacity);
+            }
+            // base colours, and the reflection's prefix, normal column, suffix and
+            // (traced) ray split or (untraced) colours, side by side in one grid
+            e = hs::precise::view_prologue(
+                v->base_sh, v->sh_coefficients, v->sh_degree, v->base.means3d, v->camera_position3, v->base.specular,
+                v->base.roughness, nb, v->base.colors5, v->reflection_rotation_raw4, v->reflection.means3d, nr,
+                v->reflection_rotation9, v->reflection_normal3, v->reflection_rays36,
+                traced ? v->reflection_ray_origins3 : nullptr, traced ? v->reflection_ray_directions3 : nullptr,
+                v->reflection_rgb3, v->reflection.specular, v->reflection.roughness,
+                traced ? nullptr : v->reflection.colors5, s);
+            if (e != cudaSuccess) return cuda_failure(e, "standard view preparation", error_text, error_capacity);
+            if (traced && nr != 0) {
+                const hs::TraceCall t = view_trace_call(*v, nr, v->reflection.means3d, v->reflection_shs,
+                                                        v->reflection_others2, v->reflection.opacities,
+                                                        v->reflection.scales2, v->reflection.rotations4,
+                                                        v->viewmatrix4x4, v->projmatrix4x4, v->camera_position3, s);
+                e = hs::trace_rays(refl, t);
+                if (e != cudaSuccess) return cuda_failure(e, "reflection trace", error_text, error_capacity);
+                e = hs::view::colors5(v->trace_rgb3, v->reflection.specular, v->reflection.roughness, nr,
+                                      v->reflection.colors5, s);
+                if (e != cudaSuccess) return cuda_failure(e, "standard view colours", error_text, error_capacity);
+            }
+            // both raster calls, concurrently
+            if (captured) {
+                e = hs::standard_forward_many(contexts, view_calls, 2, s, base->graph_fork_event, false);
+                const uint64_t counts[2] = {nb, nr};
+                if (e == cudaSuccess) e = cudaStreamWaitEvent(base->signal_stream, base->graph_fork_event, 0);
+                if (e == cudaSuccess) e = hs::standard_view_status(contexts, counts, 2, base->signal_stream);
+                if (e == cudaSuccess)
+                    e = cudaEventRecordWithFlags(base->signal_event, base->signal_stream, cudaEventRecordExternal);
+                if (e == cudaSuccess) e = cudaEventRecord(base->graph_join_event, base->signal_stream);
+                if (e == cudaSuccess) e = cudaStreamWaitEvent(s, base->graph_join_event, 0);
+            } else {
+                e = hs::standard_forward_many(contexts, view_calls, 2, s,
+                                              static_cast<cudaEvent_t>(v->raster_begin_event));
+            }
+            if (e != cudaSuccess)
+                return cuda_failure(e, "concurrent five-channel rasterizer forward", error_text, error_capacity);
+            // fusion from the colour planes (renderer.py:326, math.py:301-311) and,
+            // with the postprocess, the maps in the same pass
+            if (post) {
+                e = cudaStreamWaitEvent(s, base->post_done_event, 0);
+                if (e != cudaSuccess) return cuda_failure(e, "standard view join", error_text, error_capacity);
+                // (1 - ratio) and ratio as float32 scalars of a double ratio (math.py:440-442)
+                const float keep = static_cast<float>(1.0 - v->depth_ratio);
+                const float ratio = static_cast<float>(v->depth_ratio);
+                const hs::post::StandardMaps maps{v->rgb_map3, v->acc_map, v->dpt_map, v->norm_map3,
+                                                 v->surf_norm_map3, v->dist_map, v->spec_map, v->rough_map};
+                e = hs::post::standard_with_fusion(v->width, v->height, v->base.output_color5, v->base.output_aux7,
+                                                   v->pixel_rays3, v->camera30 + 18, v->camera30 + 21, keep, ratio,
+                                                   maps, v->reflection.output_color5, v->diffuse_rgb3, v->fused_rgb3,
+                                                   v->reflection_rgb_map3, s);
+                if (e != cudaSuccess) return cuda_failure(e, "standard view postprocess", error_text, error_capacity);
+            } else {
+                e = hs::precise::fuse_maps_planar(v->base.output_color5, v->reflection.output_color5,
+                                                  v->base.output_color5 + 3 * pixels, v->diffuse_rgb3, v->fused_rgb3,
+                                                  v->reflection_rgb_map3, pixels, s);
+                if (e != cudaSuccess) return cuda_failure(e, "standard view fusion", error_text, error_capacity);
+            }
+            const cudaError_t trailing = cudaGetLastError();
+            if (trailing != cudaSuccess)
+                return cuda_failure(trailing, "standard view execution", error_text, error_capacity);
+            return HS_STATUS_OK;
+        };
+        auto direct = [&]() -> int32_t {
+            const int32_t qs = queue_view(calls, false);
+            return qs != HS_STATUS_OK ? qs : ok(error_text, error_capacity);
+        };
+        // Graph replays: a view whose arguments and buffers repeat those of
+        // the previous call is captured once and then replayed as one graph
+        // launch (no launch of its own per kernel, no host wait before the
+        // renderers). Each raster call is captured for a pair capacity a
+        // quarter above its last pair count; a replay whose count exceeds it
+        // (or that breaks a limit the direct path checks) is rendered again
+        // directly, which grows the buffers and reports what the direct path
+        // reports.
+        const bool replayable = !traced && v->raster_begin_event == nullptr && nb != 0 && nr != 0 &&
+                                view_graphs_enabled() && !base->timer.enabled && !refl->timer.enabled &&
+                                base->test_stall_tile == UINT32_MAX && refl->test_stall_tile == UINT32_MAX &&
+                                base->std_last_emitted != 0 && refl->std_last_emitted != 0;
+        if (!replayable) return direct();
+        std::vector<unsigned char> key = view_graph_key(v, sizeof(HsB200StandardViewV2), contexts, 2);
+        HsRasterizerContext::ViewGraph* g = find_view_graph(base, key);
+        if (g == nullptr) {
+            // seen once: remember the key (the last few, so that views cycling
+            // through a few output buffers replay too) and render directly
+            auto& recent = base->view_recent_keys;
+            const auto seen = std::find(recent.begin(), recent.end(), key);
+            if (seen == recent.end()) {
+                if (recent.size() >= 2 * kMaxViewGraphs) recent.erase(recent.begin());
+                recent.push_back(std::move(key));
+                return direct();
+            }
+            recent.erase(seen);
+            cudaError_t e = hs::ensure_graph_streams(base);
+            for (HsRasterizerContext* c : contexts) {
+                if (e == cudaSuccess) e = hs::ensure_side_stream(c);
+                const uint64_t want = std::min<uint64_t>(c->std_last_emitted + c->std_last_emitted / 4 + 65536,
+                                                         hs::kMaxStandardPairs);
+                if (e == cudaSuccess && hs::standard_pair_capacity(c) < want) e = hs::standard_reserve_pairs(c, want);
+            }
+            if (e == cudaSuccess && post) e = hs::ensure_post_stream(base);
+            if (e != cudaSuccess) return cuda_failure(e, "standard view graph setup", error_text, error_capacity);
+            hs::StandardCall graph_calls[2] = {calls[0], calls[1]};
+            uint32_t capacity[2];
+            for (int i = 0; i < 2; ++i) {
+                capacity[i] = std::min<uint32_t>(hs::standard_pair_capacity(contexts[i]), hs::kMaxStandardPairs);
+                graph_calls[i].pair_capacity = capacity[i];
+            }
+            const cudaGraphExec_t exec = capture_view(
+                s, [&]() { return queue_view(graph_calls, true) == HS_STATUS_OK; },
+                {base->post_stream, base->signal_stream, base->side_stream, refl->side_stream},
+                base->graph_join_event);
+            ++base->view_graph_captures;
+            // the key of the buffers as captured (the reservation may have grown them)
+            g = insert_view_graph(base, view_graph_key(v, sizeof(HsB200StandardViewV2), contexts, 2), exec,
+                                  capacity);
         }
-        // both raster calls, concurrently
-        e = hs::standard_forward_many(contexts, calls, 2, s, static_cast<cudaEvent_t>(v->raster_begin_event));
-        if (e != cudaSuccess) return cuda_failure(e, "concurrent five-channel rasterizer forward", error_text,
-                                                  error_capacity);
-        // fusion from the colour planes (renderer.py:326, math.py:301-311) and,
-        // with the postprocess, the maps in the same pass
+        if (g->exec == nullptr) return direct();
+        g->last_use = ++base->view_graph_clock;
+        cudaError_t e = cudaSuccess;
+        // the camera terms' workspace: after its previous user, as the direct path orders it
+        if (post) e = cudaStreamWaitEvent(s, base->view_camera_event, 0);
+        if (e == cudaSuccess) e = cudaGraphLaunch(g->exec, s);
+        if (e == cudaSuccess && post) e = cudaEventRecord(base->view_camera_event, s);
+        if (e != cudaSuccess) return cuda_failure(e, "standard view graph launch", error_text, error_capacity);
+        ++base->view_graph_replays;
         if (post) {
-            e = cudaStreamWaitEvent(s, base->post_done_event, 0);
-            if (e != cudaSuccess) return cuda_failure(e, "standard view join", error_text, error_capacity);
-            // (1 - ratio) and ratio as float32 scalars of a double ratio (math.py:440-442)
-            const float keep = static_cast<float>(1.0 - v->depth_ratio);
-            const float ratio = static_cast<float>(v->depth_ratio);
-            const hs::post::StandardMaps maps{v->rgb_map3, v->acc_map, v->dpt_map, v->norm_map3,
-                                             v->surf_norm_map3, v->dist_map, v->spec_map, v->rough_map};
-            e = hs::post::standard_with_fusion(v->width, v->height, v->base.output_color5, v->base.output_aux7,
-                                               v->pixel_rays3, v->camera30 + 18, v->camera30 + 21, keep, ratio,
-                                               maps, v->reflection.output_color5, v->diffuse_rgb3, v->fused_rgb3,
-                                               v->reflection_rgb_map3, s);
-            if (e != cudaSuccess) return cuda_failure(e, "standard view postprocess", error_text, error_capacity);
-        } else {
-            e = hs::precise::fuse_maps_planar(v->base.output_color5, v->reflection.output_color5,
-                                              v->base.output_color5 + 3 * pixels, v->diffuse_rgb3, v->fused_rgb3,
-                                              v->reflection_rgb_map3, pixels, s);
-            if (e != cudaSuccess) return cuda_failure(e, "standard view fusion", error_text, error_capacity);
+            base->math_matmul_calls += 2;
+            base->math_general_inverse_calls += 2;
         }
-        const cudaError_t trailing = cudaGetLastError();
-        if (trailing != cudaSuccess)
-            return cuda_failure(trailing, "standard view execution", error_text, error_capacity);
+        // The end of both calls' binning, with the renderers queued (the
+        // direct path's finish()).
+        e = cudaEventSynchronize(base->signal_event);
+        if (e != cudaSuccess) return cuda_failure(e, "standard view graph status", error_text, error_capacity);
+        bool gave_up = false, again = false;
+        for (int i = 0; i < 2; ++i) {
+            const uint32_t* t = contexts[i]->std_total_host;
+            gave_up = gave_up || t[3] != 0;
+            again = again || t[1] != 0 || t[0] > static_cast<uint32_t>(INT_MAX) || t[2] > g->capacity[i];
+            contexts[i]->std_last_emitted = t[2];
+        }
+        if (gave_up) {
+            return cuda_failure(hs::kWaitGaveUp, "concurrent five-channel rasterizer forward", error_text,
+                                error_capacity);
+        }
+        if (again) {
+            ++base->view_graph_reruns;
+            return direct();
+        }
         return ok(error_text, error_capacity);
     });
 }
@@ -2210,6 +2423,21 @@ int32_t hs_b200_flashgs_view_v2(const HsB200FlashgsViewV2* v, char* error_text,
         const cudaError_t trailing = cudaGetLastError();
         if (trailing != cudaSuccess)
             return cuda_failure(trailing, "FlashGS view execution", error_text, error_capacity);
+        return ok(error_text, error_capacity);
+    });
+}
+
+int32_t hs_b200_view_graph_stats_v1(HsRasterizerHandle base_handle, uint64_t* captures, uint64_t* replays,
+                                    uint64_t* reruns, char* error_text, uint64_t error_capacity) noexcept {
+    return guard(error_text, error_capacity, [&]() -> int32_t {
+        if (base_handle == nullptr || captures == nullptr || replays == nullptr || reruns == nullptr) {
+            return fail(HS_STATUS_INVALID_ARGUMENT, "view graph stats received a null pointer", error_text,
+                        error_capacity);
+        }
+        std::lock_guard<std::mutex> lock(base_handle->mutex);
+        *captures = base_handle->view_graph_captures;
+        *replays = base_handle->view_graph_replays;
+        *reruns = base_handle->view_graph_reruns;
         return ok(error_text, error_capacity);
     });
 }

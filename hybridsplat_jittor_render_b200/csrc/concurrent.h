@@ -25,9 +25,11 @@ namespace hs {
 
 // raster_begin (optional) is recorded when every call's binning is done and
 // the renderers may start, for callers that time other traffic around them.
+// finish false leaves out the finish() phases (calls captured into a graph,
+// whose status the capturer reads after each replay).
 template <class Pass, class Call>
 cudaError_t run_many(HsRasterizerContext* const* contexts, const Call* calls, uint32_t count,
-                     cudaStream_t stream, cudaEvent_t raster_begin = nullptr) {
+                     cudaStream_t stream, cudaEvent_t raster_begin = nullptr, bool finish = true) {
     if (count == 0) return cudaSuccess;
     for (uint32_t i = 0; i < count; ++i) {
         const cudaError_t st = ensure_side_stream(contexts[i]);
@@ -65,7 +67,7 @@ cudaError_t run_many(HsRasterizerContext* const* contexts, const Call* calls, ui
     for (auto& p : passes)
         if (st == cudaSuccess) st = p->render();
     for (auto& p : passes)
-        if (st == cudaSuccess) st = p->finish();
+        if (st == cudaSuccess && finish) st = p->finish();
     // Join also after an error: the caller's stream stays ordered after
     // everything that was queued.
     for (uint32_t i = 0; i < count; ++i) {

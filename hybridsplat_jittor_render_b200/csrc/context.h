@@ -87,6 +87,11 @@ cudaError_t ensure_device_error(HsRasterizerContext* context);
 cudaError_t ensure_side_stream(HsRasterizerContext* context);
 // The stream and events of the per-view entry's postprocess camera terms.
 cudaError_t ensure_post_stream(HsRasterizerContext* context);
+// The stream and events of the per-view entry's graph replays.
+cudaError_t ensure_graph_streams(HsRasterizerContext* context);
+// Destroys the context's captured view graphs (waits for nothing: a launched
+// graph completes after its executable is destroyed).
+void destroy_view_graphs(HsRasterizerContext* context);
 void destroy_side_stream(HsRasterizerContext* context);
 void stage_timing_destroy(StageTimer& timer);
 
@@ -177,6 +182,28 @@ struct HsRasterizerContext {
     cudaEvent_t post_fork_event = nullptr;   // recorded on the view's stream before them
     cudaEvent_t post_done_event = nullptr;   // recorded on post_stream after them
     cudaEvent_t fork_event = nullptr;  // recorded on the caller's stream
+
+    // Per-view entry replays (hs_b200_standard_view_v2 on the base handle): a
+    // view whose arguments and buffers match an earlier call's runs as one
+    // captured CUDA graph, sized for pair_capacity pairs per raster call,
+    // with no host wait before its renderers are queued.
+    struct ViewGraph {
+        std::vector<unsigned char> key;    // the call's arguments and both contexts' buffer generations
+        cudaGraphExec_t exec = nullptr;     // null: capture failed for this key, run the call directly
+        uint32_t capacity[2] = {0, 0};      // pairs each raster call was captured for
+        uint64_t last_use = 0;
+    };
+    std::vector<ViewGraph> view_graphs;    // at most kMaxViewGraphs
+    std::vector<std::vector<unsigned char>> view_recent_keys;  // keys seen once (captured when seen again)
+    uint64_t view_graph_clock = 0;
+    uint64_t view_graph_captures = 0;
+    uint64_t view_graph_replays = 0;
+    uint64_t view_graph_reruns = 0;        // replays whose pair count overflowed, rendered again directly
+    uint64_t std_last_emitted = 0;         // pairs of the last standard call that read its totals
+    cudaStream_t signal_stream = nullptr;  // a replay's host publication branch
+    cudaEvent_t signal_event = nullptr;    // recorded (external) after that publication
+    cudaEvent_t graph_fork_event = nullptr;
+    cudaEvent_t graph_join_event = nullptr;
 };
 
 namespace hs {
@@ -249,6 +276,14 @@ struct StandardCall {
     int32_t* output_rendered = nullptr;
     cudaStream_t stream = nullptr;
     uint32_t row_begin = 0, row_end = UINT32_MAX;
+    // Non-zero: the call is being captured into a graph and never waits on
+    // the host. Its binning is sized for pair_capacity pairs (the context's
+    // pair buffers must hold them: standard_reserve_pairs); emission, tile
+    // sort and ranges read the pair count from device memory and stop at the
+    // capacity. Nothing is published to the host and finish() is not run:
+    // the capturer publishes the totals (view_status_kernel) and checks them
+    // after every replay.
+    uint32_t pair_capacity = 0;
 };
 
 // FlashGS forward (flashgs.cu) on call.stream.
@@ -281,9 +316,26 @@ cudaError_t standard_debug_copy(HsRasterizerContext* context, uint64_t point_cap
 cudaError_t standard_forward(HsRasterizerContext* context, const StandardCall& call);
 
 // Independent standard calls run as flashgs_forward_many runs FlashGS calls.
+// With finish false (captured calls, pair_capacity set) the calls are queued
+// and joined to `stream` without the host reading their wait status.
 cudaError_t standard_forward_many(HsRasterizerContext* const* contexts,
                                   const StandardCall* calls, uint32_t count,
-                                  cudaStream_t stream, cudaEvent_t raster_begin = nullptr);
+                                  cudaStream_t stream, cudaEvent_t raster_begin = nullptr,
+                                  bool finish = true);
+
+// Publishes the totals and wait status of captured standard calls (one per
+// context, 1 or 2, each of point_counts[i] > 0 Gaussians) to the contexts'
+// mapped totals blocks, on `stream`: the host reads them after a replay.
+cudaError_t standard_view_status(HsRasterizerContext* const* contexts, const uint64_t* point_counts,
+                                 uint32_t count, cudaStream_t stream);
+
+// The most pairs one standard call sorts (the radix sort's 30-bit counts).
+constexpr uint32_t kMaxStandardPairs = (1u << 30) - 1u;
+
+// Pairs the context's standard pair buffers hold (0 before the first call).
+uint32_t standard_pair_capacity(const HsRasterizerContext* context);
+// Grows the standard pair buffers to hold at least `pairs` pairs.
+cudaError_t standard_reserve_pairs(HsRasterizerContext* context, uint64_t pairs);
 
 // Arguments of one hs_optix_trace_f32_v1 call (device pointers; checked by
 // the entry point).

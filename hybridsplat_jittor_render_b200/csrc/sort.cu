@@ -84,8 +84,10 @@ __device__ __forceinline__ uint32_t digit_of(uint32_t key, int shift, uint32_t m
 __global__ void __launch_bounds__(kThreads) histogram_kernel(const uint32_t* __restrict__ keys,
                                                              uint32_t count, int begin_bit,
                                                              int end_bit, int drop,
-                                                             uint32_t* __restrict__ hist) {
+                                                             uint32_t* __restrict__ hist,
+                                                             const uint32_t* __restrict__ bound) {
     __shared__ uint32_t bins[kMaxPasses][kBins];
+    if (bound != nullptr) count = min(*bound, count);
     const int passes = (end_bit - begin_bit + kRadixBits - 1) / kRadixBits;
     for (int p = 0; p < passes; ++p) bins[p][threadIdx.x] = 0;
     __syncthreads();
@@ -348,9 +350,10 @@ __device__ __forceinline__ void tile_scatter(PassTile<kItems>& t, uint32_t n, in
     }
 }
 
-// Items of a pass: *live_count after a dropping first pass, else count.
+// Items of a pass: *live_count (the survivors after a dropping first pass, or
+// the bound of a sort sized for a capacity), at most count; else count.
 __device__ __forceinline__ uint32_t pass_items(uint32_t count, const uint32_t* live_count) {
-    return live_count != nullptr ? *live_count : count;
+    return live_count != nullptr ? min(*live_count, count) : count;
 }
 
 // ---- onesweep pass: one kernel, cross-tile prefix by decoupled look-back ----
@@ -510,7 +513,7 @@ namespace {
 // Reduce-then-scan passes (count, scan, scatter kernels per pass).
 cudaError_t sort_split(uint32_t*& src_k, uint32_t*& src_v, uint32_t*& dst_k, uint32_t*& dst_v,
                        uint32_t count, int begin_bit, int end_bit, void* scratch, cudaStream_t stream,
-                       uint32_t* error, const uint32_t* kept, int drop, bool ballot) {
+                       uint32_t* error, const uint32_t* kept, int drop, bool ballot, const uint32_t* bound) {
     const uint32_t tiles =
         static_cast<uint32_t>((static_cast<uint64_t>(count) + kThreads * kLargeItems - 1) / (kThreads * kLargeItems));
     uint32_t* counts = static_cast<uint32_t*>(scratch);
@@ -518,7 +521,7 @@ cudaError_t sort_split(uint32_t*& src_k, uint32_t*& src_v, uint32_t*& dst_k, uin
     int pass = 0;
     for (int shift = begin_bit; shift < end_bit; shift += kRadixBits, ++pass) {
         const int bits = min(kRadixBits, end_bit - shift);
-        const uint32_t* live = pass > 0 ? kept : nullptr;
+        const uint32_t* live = pass > 0 && kept != nullptr ? kept : bound;
         const int pass_drop = pass == 0 ? drop : 0;
         count_kernel<kLargeItems><<<tiles, kThreads, 0, stream>>>(src_k, count, live, pass_drop, shift, bits,
                                                                   tiles, counts, error);
@@ -545,7 +548,8 @@ cudaError_t sort_split(uint32_t*& src_k, uint32_t*& src_v, uint32_t*& dst_k, uin
 // Onesweep passes (histogram of every pass, then one kernel per pass).
 cudaError_t sort_onesweep(uint32_t*& src_k, uint32_t*& src_v, uint32_t*& dst_k, uint32_t*& dst_v,
                           uint32_t count, int begin_bit, int end_bit, void* scratch, cudaStream_t stream,
-                          uint32_t* error, uint32_t stall_tile, const uint32_t* kept, int drop, bool ballot) {
+                          uint32_t* error, uint32_t stall_tile, const uint32_t* kept, int drop, bool ballot,
+                          const uint32_t* bound) {
     const uint32_t tiles = tiles_for(count);
     const bool large = count >= kLargeTileItems;
     const uint32_t large_tiles =
@@ -562,7 +566,8 @@ cudaError_t sort_onesweep(uint32_t*& src_k, uint32_t*& src_v, uint32_t*& dst_k, 
     }
     const uint32_t hist_cap = static_cast<uint32_t>(sms) * 8u;
     const uint32_t hist_blocks = tiles < hist_cap ? tiles : hist_cap;
-    histogram_kernel<<<hist_blocks, kThreads, 0, stream>>>(src_k, count, begin_bit, end_bit, drop, s.hist);
+    histogram_kernel<<<hist_blocks, kThreads, 0, stream>>>(src_k, count, begin_bit, end_bit, drop, s.hist,
+                                                           bound);
     int pass = 0;
     for (int shift = begin_bit; shift < end_bit; shift += kRadixBits, ++pass) {
         const int bits = min(kRadixBits, end_bit - shift);
@@ -570,7 +575,7 @@ cudaError_t sort_onesweep(uint32_t*& src_k, uint32_t*& src_v, uint32_t*& dst_k, 
         uint32_t* pass_status = s.status + static_cast<uint64_t>(pass) * tiles * kBins;
         // the first pass of a dropping sort reads every item and drops; the
         // later ones sort the *kept survivors
-        const uint32_t* live = pass > 0 ? kept : nullptr;
+        const uint32_t* live = pass > 0 && kept != nullptr ? kept : bound;
         const int pass_drop = pass == 0 ? drop : 0;
         if (large && ballot) {
             onesweep_kernel<kLargeItems, kLargeWindow, true><<<large_tiles, kThreads, 0, stream>>>(
@@ -597,8 +602,9 @@ cudaError_t sort_onesweep(uint32_t*& src_k, uint32_t*& src_v, uint32_t*& dst_k, 
 cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals,
                        uint32_t count, int begin_bit, int end_bit, void* scratch,
                        cudaStream_t stream, uint32_t* error, uint32_t stall_tile,
-                       const uint32_t* kept) {
+                       const uint32_t* kept, const uint32_t* bound) {
     if (count == 0 || end_bit <= begin_bit) return cudaSuccess;
+    if (kept != nullptr && bound != nullptr) return cudaErrorInvalidValue;
     if (count > kMaxItems || end_bit - begin_bit > kMaxPasses * kRadixBits) {
         return cudaErrorInvalidValue;
     }
@@ -615,9 +621,9 @@ cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint3
     const cudaError_t st =
         count >= kSplitItems
             ? sort_split(src_k, src_v, dst_k, dst_v, count, begin_bit, end_bit, scratch, stream, error, kept,
-                         drop, ballot)
+                         drop, ballot, bound)
             : sort_onesweep(src_k, src_v, dst_k, dst_v, count, begin_bit, end_bit, scratch, stream, error,
-                            stall_tile, kept, drop, ballot);
+                            stall_tile, kept, drop, ballot, bound);
     if (st != cudaSuccess) return st;
     if (passes & 1) {
         cudaError_t cs = cudaMemcpyAsync(keys, src_k, static_cast<size_t>(count) * sizeof(uint32_t),

@@ -70,12 +70,18 @@ constexpr uint32_t kDropKey = 0xffffffffu;
 // keys/vals[0, *kept) in the same stable order, and the passes after the
 // first only touch those. The depth sorts use it to skip the Gaussians that
 // emit no pair.
+// bound (device word, may be null; not with kept): every pass sorts only the
+// first min(*bound, count) items, so `count` may be a capacity that sizes the
+// grids and *bound the number of items an earlier kernel of the stream
+// wrote. The launches then depend on the capacity alone (a captured graph
+// replays them for any item count up to it).
 // Launches: one memset, one histogram kernel, one kernel per 8-bit pass
 // (plus two copies when the pass count is odd).
 cudaError_t sort_pairs(uint32_t* keys, uint32_t* vals, uint32_t* alt_keys, uint32_t* alt_vals,
                        uint32_t count, int begin_bit, int end_bit, void* scratch,
                        cudaStream_t stream, uint32_t* error = nullptr,
-                       uint32_t stall_tile = kNoStall, const uint32_t* kept = nullptr);
+                       uint32_t stall_tile = kNoStall, const uint32_t* kept = nullptr,
+                       const uint32_t* bound = nullptr);
 
 // Number of bits needed to hold values in [0, n): the reference's
 // getHigherMsb(n) for the tile count (sort.cu:141-156).

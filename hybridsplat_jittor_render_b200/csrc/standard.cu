@@ -248,10 +248,12 @@ cudaError_t StandardPass::begin() {
         c_.prefiltered ? 1 : 0, c_.row_begin, c_.row_end, po);
     st = cudaGetLastError();
     if (st != cudaSuccess) return st;
-    bin::publish_totals_kernel<<<1, 32, 0, stream>>>(gv_.totals, ctx_->std_total_mapped);
-    st = cudaGetLastError();
-    if (st == cudaSuccess) st = cudaEventRecord(ctx_->std_count_event, stream);
-    if (st != cudaSuccess) return st;
+    if (c_.pair_capacity == 0) {
+        bin::publish_totals_kernel<<<1, 32, 0, stream>>>(gv_.totals, ctx_->std_total_mapped);
+        st = cudaGetLastError();
+        if (st == cudaSuccess) st = cudaEventRecord(ctx_->std_count_event, stream);
+        if (st != cudaSuccess) return st;
+    }
     marks_.mark(1);
     // The depth sort does not depend on the totals: queue it before waiting.
     // It leaves out the Gaussians that emit no pair (totals[4] counts the
@@ -265,13 +267,24 @@ cudaError_t StandardPass::begin() {
 cudaError_t StandardPass::bin() {
     if (done_) return cudaSuccess;
     const cudaStream_t stream = c_.stream;
-    cudaError_t st = cudaEventSynchronize(ctx_->std_count_event);
-    if (st != cudaSuccess) return st;
-    const uint32_t rendered = ctx_->std_total_host[0];
-    const uint32_t emitted = ctx_->std_total_host[2];
-    if (ctx_->std_total_host[1] != 0) return kPrefilteredViolation;
-    if (rendered > static_cast<uint32_t>(INT_MAX) || emitted > sort::kMaxItems) {
-        return cudaErrorInvalidValue;
+    const bool captured = c_.pair_capacity != 0;
+    cudaError_t st = cudaSuccess;
+    uint32_t emitted = c_.pair_capacity;
+    // captured: the pair count stays on the device and bounds the tile sort
+    // and the ranges; the buffers are sized for the capacity
+    const uint32_t* bound = captured ? gv_.totals + 2 : nullptr;
+    if (!captured) {
+        st = cudaEventSynchronize(ctx_->std_count_event);
+        if (st != cudaSuccess) return st;
+        const uint32_t rendered = ctx_->std_total_host[0];
+        emitted = ctx_->std_total_host[2];
+        if (ctx_->std_total_host[1] != 0) return kPrefilteredViolation;
+        if (rendered > static_cast<uint32_t>(INT_MAX) || emitted > sort::kMaxItems) {
+            return cudaErrorInvalidValue;
+        }
+        ctx_->std_last_emitted = emitted;
+    } else if (ctx_->std_binning.bytes < binning_bytes(emitted)) {
+        return cudaErrorInvalidValue;  // standard_reserve_pairs first
     }
     st = cudaMemcpyAsync(c_.output_rendered, gv_.totals, sizeof(int32_t), cudaMemcpyDeviceToDevice,
                          stream);
@@ -301,15 +314,15 @@ cudaError_t StandardPass::bin() {
         emit_rows_kernel<<<(c_.point_count + kEmitRowThreads - 1) / kEmitRowThreads,
                            kEmitRowThreads, 0, stream>>>(
             static_cast<uint32_t>(c_.point_count), gv_.counts, first_pair, gv_.cull, grid_x_,
-            masked_ ? 1 : 0, tile_ids, values_, ctx_->device_error);
+            masked_ ? 1 : 0, tile_ids, values_, ctx_->device_error, emitted);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
         st = sort::sort_pairs(tile_ids, values_, alt_tiles, alt_values, emitted, 0,
                               sort::bits_for_tiles(static_cast<uint32_t>(tiles_)), scratch, stream,
-                              ctx_->device_error);
+                              ctx_->device_error, sort::kNoStall, nullptr, bound);
         if (st != cudaSuccess) return st;
         bin::ranges_kernel<uint2><<<bin::ranges_grid(emitted), bin::kRangeThreads, 0, stream>>>(
-            emitted, static_cast<uint32_t>(tiles_), tile_ids, ranges_);
+            emitted, static_cast<uint32_t>(tiles_), tile_ids, ranges_, bound);
         st = cudaGetLastError();
         if (st != cudaSuccess) return st;
     }
@@ -319,11 +332,11 @@ cudaError_t StandardPass::bin() {
     // once the renderer is queued.
     bin::tile_order_kernel<uint2><<<1, bin::kOrderThreads, 0, stream>>>(
         c_.row_begin * grid_x_, strip_tiles, ranges_, tile_order_, work_counter_, ctx_->device_error,
-        ctx_->std_total_mapped + 3);
+        captured ? nullptr : ctx_->std_total_mapped + 3);
     st = cudaGetLastError();
-    if (st == cudaSuccess) st = cudaEventRecord(ctx_->std_count_event, stream);
+    if (st == cudaSuccess && !captured) st = cudaEventRecord(ctx_->std_count_event, stream);
     if (st != cudaSuccess) return st;
-    published_ = true;
+    published_ = !captured;
     marks_.mark(2);
     return cudaSuccess;
 }
@@ -381,8 +394,43 @@ cudaError_t standard_forward(HsRasterizerContext* ctx, const StandardCall& call)
 }
 
 cudaError_t standard_forward_many(HsRasterizerContext* const* contexts, const StandardCall* calls,
-                                  uint32_t count, cudaStream_t stream, cudaEvent_t raster_begin) {
-    return run_many<st::StandardPass>(contexts, calls, count, stream, raster_begin);
+                                  uint32_t count, cudaStream_t stream, cudaEvent_t raster_begin,
+                                  bool finish) {
+    return run_many<st::StandardPass>(contexts, calls, count, stream, raster_begin, finish);
+}
+
+cudaError_t standard_view_status(HsRasterizerContext* const* contexts, const uint64_t* point_counts,
+                                 uint32_t count, cudaStream_t stream) {
+    if (count == 0 || count > 2) return cudaErrorInvalidValue;
+    bin::ViewStatusArgs a{};
+    for (uint32_t i = 0; i < count; ++i) {
+        HsRasterizerContext* ctx = contexts[i];
+        if (ctx->std_total_mapped == nullptr || ctx->device_error == nullptr || point_counts[i] == 0)
+            return cudaErrorInvalidValue;
+        a.call[i].totals = st::geometry_views(ctx->std_geometry.ptr, point_counts[i]).totals;
+        a.call[i].error = ctx->device_error;
+        a.call[i].host = ctx->std_total_mapped;
+    }
+    bin::view_status_kernel<<<count, 32, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+static_assert(kMaxStandardPairs == sort::kMaxItems, "the pair limit is the sort's");
+
+uint32_t standard_pair_capacity(const HsRasterizerContext* ctx) {
+    // the largest pair count whose binning layout fits the buffer
+    uint64_t lo = 0, hi = sort::kMaxItems;
+    if (ctx->std_binning.bytes < st::binning_bytes(1)) return 0;
+    while (lo < hi) {
+        const uint64_t mid = lo + (hi - lo + 1) / 2;
+        if (st::binning_bytes(mid) <= ctx->std_binning.bytes) lo = mid; else hi = mid - 1;
+    }
+    return static_cast<uint32_t>(lo);
+}
+
+cudaError_t standard_reserve_pairs(HsRasterizerContext* ctx, uint64_t pairs) {
+    if (pairs > sort::kMaxItems) return cudaErrorInvalidValue;
+    return ensure_buffer(ctx->std_binning, st::binning_bytes(pairs), &ctx->std_growth_count, true);
 }
 
 }  // namespace hs

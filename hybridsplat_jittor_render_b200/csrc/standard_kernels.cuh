@@ -235,7 +235,7 @@ constexpr int kEmitRowThreads = 128;
 static __global__ void __launch_bounds__(kEmitRowThreads) emit_rows_kernel(
     uint32_t count, const uint32_t* __restrict__ counts, const uint32_t* __restrict__ first_pair,
     const float4* __restrict__ cull, uint32_t grid_x, int masked, uint32_t* __restrict__ tile_ids,
-    uint32_t* __restrict__ values, const uint32_t* __restrict__ error) {
+    uint32_t* __restrict__ values, const uint32_t* __restrict__ error, uint32_t capacity) {
     if (sort::wait_failed(error)) return;  // first_pair is not a valid offset table
     __shared__ RowUnit units[kEmitRowThreads];
     __shared__ uint32_t cursor[kEmitRowThreads], counted[kEmitRowThreads],
@@ -247,8 +247,13 @@ static __global__ void __launch_bounds__(kEmitRowThreads) emit_rows_kernel(
     int bx0 = 0, by0 = 0, bx1 = 0, by1 = 0;
     if (cnt != 0u) load_cull_shape(cull, gid, bx0, by0, bx1, by1);
     cursor[threadIdx.x] = 0;
-    counted[threadIdx.x] = cnt;
-    offsets[threadIdx.x] = cnt != 0u ? first_pair[gid] : 0u;
+    const uint32_t first = cnt != 0u ? first_pair[gid] : 0u;
+    // Slots from `capacity` on are not written: a call whose buffers were
+    // sized before its pair count was known (a graph replay) checks the count
+    // afterwards and renders again when it did not fit.
+    const uint32_t room = first < capacity ? capacity - first : 0u;
+    counted[threadIdx.x] = cnt < room ? cnt : room;
+    offsets[threadIdx.x] = first;
     uint32_t incl = cnt != 0u ? static_cast<uint32_t>(by1 - by0) : 0u;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {

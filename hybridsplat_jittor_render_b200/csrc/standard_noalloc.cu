@@ -194,7 +194,8 @@ Result forward(int device, int32_t point_count, const float* background5, int32_
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
         emit_rows_kernel<<<(point_count + kEmitRowThreads - 1) / kEmitRowThreads, kEmitRowThreads, 0,
                            stream>>>(static_cast<uint32_t>(point_count), l.counts, first_pair,
-                                     l.cull, grid_x, 1, l.tile_ids, l.values, l.error);
+                                     l.cull, grid_x, 1, l.tile_ids, l.values, l.error,
+                                     emitted);
         st = cudaGetLastError();
         if (st != cudaSuccess) return {st, nullptr, 0, 0};
         st = sort::sort_pairs(l.tile_ids, l.values, l.alt_tiles, l.alt_values, emitted, 0,

@@ -132,7 +132,33 @@ cudaError_t ensure_post_stream(HsRasterizerContext* context) {
     return st;
 }
 
+cudaError_t ensure_graph_streams(HsRasterizerContext* context) {
+    cudaError_t st = cudaSuccess;
+    if (context->signal_stream == nullptr)
+        st = cudaStreamCreateWithFlags(&context->signal_stream, cudaStreamNonBlocking);
+    for (cudaEvent_t* e : {&context->signal_event, &context->graph_fork_event, &context->graph_join_event}) {
+        if (st == cudaSuccess && *e == nullptr) st = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
+    }
+    return st;
+}
+
+void destroy_view_graphs(HsRasterizerContext* context) {
+    // an executable still in flight is freed when it completes
+    for (HsRasterizerContext::ViewGraph& g : context->view_graphs) {
+        if (g.exec != nullptr) cudaGraphExecDestroy(g.exec);
+    }
+    context->view_graphs.clear();
+    context->view_recent_keys.clear();
+}
+
 void destroy_side_stream(HsRasterizerContext* context) {
+    destroy_view_graphs(context);
+    if (context->signal_stream != nullptr) cudaStreamDestroy(context->signal_stream);
+    for (cudaEvent_t* e : {&context->signal_event, &context->graph_fork_event, &context->graph_join_event}) {
+        if (*e != nullptr) cudaEventDestroy(*e);
+        *e = nullptr;
+    }
+    context->signal_stream = nullptr;
     if (context->side_stream != nullptr) cudaStreamDestroy(context->side_stream);
     if (context->side_event != nullptr) cudaEventDestroy(context->side_event);
     if (context->fork_event != nullptr) cudaEventDestroy(context->fork_event);

@@ -289,6 +289,7 @@ EXTENSION_SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "hs_b200_flashgs_view_v2": (_I32, [ctypes.POINTER(FlashgsViewV2), *_ERR]),
     "hs_b200_test_stall_lookback_v1": (_I32, [_V, _U32, *_ERR]),
     "hs_b200_test_pair_ops_v1": (_I32, [_V, _V, _V, _V, _U64, _V, *_ERR]),
+    "hs_b200_view_graph_stats_v1": (_I32, [_V, _V, _V, _V, *_ERR]),
     "hs_b200_comm_unique_id_v1": (_I32, [_V, *_ERR]),
     "hs_b200_comm_create_v1": (_I32, [_I32, _I32, _I32, _V, ctypes.c_double, ctypes.POINTER(ctypes.c_void_p),
                                       *_ERR]),

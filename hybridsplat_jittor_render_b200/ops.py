@@ -876,8 +876,8 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
                   width: int, height: int, tan_fovx: float, tan_fovy: float, sh_degree: int,
                   base_context: NativeRendererContext, reflection_context: NativeRendererContext,
                   trace: dict[str, Any] | None = None, postprocess: dict[str, float] | None = None,
-                  stream: int | None = None, raster_begin_event: torch.cuda.Event | None = None
-                  ) -> StandardViewOutputs:
+                  stream: int | None = None, raster_begin_event: torch.cuda.Event | None = None,
+                  out: StandardViewOutputs | None = None) -> StandardViewOutputs:
     """One view of the standard session (render_hybridsplat_view,
     renderer.py:232-341, and postprocess_raster, math.py:426-463) in one call
     (hs_b200_standard_view_v2).
@@ -894,29 +894,45 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
     ``fov_y`` and ``depth_ratio`` (0.0). ``background`` is the raster calls'
     [5]. ``stream`` as in rasterize_forward_many. ``raster_begin_event``
     (optional) is recorded when both calls' binning is done, before the tile
-    renderers. Every output equals that of the same steps called one by one.
+    renderers. ``out`` (optional) is the result of an earlier call with the
+    same sizes, trace and postprocess choice, whose tensors receive the
+    outputs: an untraced view whose arguments and buffers repeat those of one
+    of the context's last calls replays as one captured graph on a
+    non-default ``stream`` (hs_b200_view_graph_stats_v1), so reusing a few
+    output sets lets a sequence of views replay. Every output equals that of
+    the same steps called one by one.
     """
     if base_context is reflection_context:
         raise ValueError("standard_view needs two distinct contexts")
     device = viewmatrix.device
     f = dict(dtype=torch.float32, device=device)
+
+    def take(name, existing, shape):
+        if out is None:
+            return torch.empty(shape, **f)
+        if existing is None:
+            raise ValueError(f"out has no {name}")
+        _check_tensor(f"out {name}", existing, shape)
+        return existing
+
     sh = base["sh"].contiguous()
     nb, nr = int(base["means3d"].shape[0]), int(reflection["means3d"].shape[0])
     _check_tensor("base sh", sh, (nb, 3, int(sh.shape[-1])))
     _check_tensor("reflection rotations_raw", reflection["rotations_raw"], (nr, 4))
     if isinstance(sh_degree, bool) or not isinstance(sh_degree, int) or sh_degree not in range(4):
         raise ValueError("sh_degree must be an integer in [0, 3]")
-    base_colors, refl_colors = torch.empty((nb, 5), **f), torch.empty((nr, 5), **f)
+    base_colors = take("base_colors", out and out.base_colors, (nb, 5))
+    refl_colors = take("reflection_colors", out and out.reflection_colors, (nr, 5))
     for name, group, n in (("base", base, nb), ("reflection", reflection, nr)):
         _check_tensor(f"{name} specular", group["specular"], (n, 1))
         _check_tensor(f"{name} roughness", group["roughness"], (n, 1))
     common = dict(width=width, height=height, scale_modifier=1.0, tan_fovx=tan_fovx, tan_fovy=tan_fovy)
     named_b, out_b = _rasterizer_arguments(background, base["means3d"], base_colors, base["opacities"],
                                            base["scales"], base["rotations"], viewmatrix, projmatrix,
-                                           camera_position, **common)
+                                           camera_position, out=out and out.base, **common)
     named_r, out_r = _rasterizer_arguments(background, reflection["means3d"], refl_colors, reflection["opacities"],
                                            reflection["scales"], reflection["rotations"], viewmatrix, projmatrix,
-                                           camera_position, **common)
+                                           camera_position, out=out and out.reflection, **common)
 
     def group(named, g):
         return native_runtime.StandardGroupV2(
@@ -927,10 +943,12 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
             output_weight=named["output_weight"], output_radii=named["output_radii"],
             output_rendered=named["output_rendered"])
 
-    rotation, normal, rays = torch.empty((nr, 3, 3), **f), torch.empty((nr, 3), **f), torch.empty((nr, 36), **f)
+    rotation = take("reflection_rotation", out and out.reflection_rotation, (nr, 3, 3))
+    normal = take("reflection_normal", out and out.reflection_normal, (nr, 3))
+    rays = take("reflection_rays", out and out.reflection_rays, (nr, 36))
     origins = directions = None
     pixels = width * height
-    fused = {k: torch.empty((height, width, 3), **f) for k in ("rgb_map", "dif_rgb_map", "ref_rgb_map")}
+    fused = {k: take(k, out and out.fused.get(k), (height, width, 3)) for k in ("rgb_map", "dif_rgb_map", "ref_rgb_map")}
     view = native_runtime.StandardViewV2(
         struct_size=ctypes.sizeof(native_runtime.StandardViewV2), base_handle=base_context.handle,
         reflection_handle=reflection_context.handle, width=width, height=height, tan_fovx=named_b["tan_fovx"],
@@ -957,10 +975,11 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
         depth = trace.get("max_trace_depth", 0)
         if depth not in (0, 1) or isinstance(depth, bool):
             raise ValueError("max_trace_depth must be 0 or 1")
-        traced = TraceOutputs(torch.empty((nr, 3), **f), torch.empty((nr, 1), **f), torch.empty((nr, 1), **f),
-                              torch.empty((nr, 3), **f), torch.empty((nr, 1), **f), torch.empty((nr, 2), **f),
-                              torch.empty((nr, 32), **f), torch.empty((nr, 1), **f))
-        origins, directions = torch.empty((nr, 3), **f), torch.empty((nr, 3), **f)
+        widths = (3, 1, 1, 3, 1, 2, 32, 1)
+        traced = TraceOutputs(*(take(f"trace.{k}", out and out.trace and getattr(out.trace, k), (nr, c))
+                                for k, c in zip(TraceOutputs._fields, widths)))
+        origins = take("ray_origins", out and out.ray_origins, (nr, 3))
+        directions = take("ray_directions", out and out.ray_directions, (nr, 3))
         view.trace = 1
         view.reflection_ray_origins3 = _ptr(origins)
         view.reflection_ray_directions3 = _ptr(directions)
@@ -977,8 +996,11 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
             setattr(view, field, _ptr(t))
     camera = maps = None
     if postprocess is not None:
-        camera_buf, pixel_rays = torch.empty(30, **f), torch.empty((pixels, 3), **f)
-        maps = {name: torch.empty((1, pixels, c), **f) for name, c in zip(STANDARD_MAPS, STANDARD_MAP_CHANNELS)}
+        old_camera = out and out.camera
+        camera_buf = take("camera", old_camera and old_camera["inverse_intrinsics"].view(-1)._base, (30,))
+        pixel_rays = take("camera rays", old_camera and old_camera["rays"], (pixels, 3))
+        maps = {name: take(name, out and out.maps and out.maps.get(name), (1, pixels, c))
+                for name, c in zip(STANDARD_MAPS, STANDARD_MAP_CHANNELS)}
         view.fov_x = _finite("fov_x", postprocess["fov_x"])
         view.fov_y = _finite("fov_y", postprocess["fov_y"])
         view.depth_ratio = _finite("depth_ratio", postprocess.get("depth_ratio", 0.0))
@@ -995,6 +1017,19 @@ def standard_view(base: dict[str, torch.Tensor], reflection: dict[str, torch.Ten
     check_status(status, "hs_b200_standard_view_v2", error)
     return StandardViewOutputs(out_b, out_r, base_colors, refl_colors, rotation, normal, rays, origins, directions,
                                traced, fused, camera, maps)
+
+
+def view_graph_stats(base_context: NativeRendererContext) -> dict[str, int]:
+    """Graph replays of standard_view with ``base_context`` as its base
+    context (hs_b200_view_graph_stats_v1): views captured, replayed, and
+    replays rendered again directly because their pair count outgrew the
+    capture."""
+    values = [ctypes.c_uint64() for _ in range(3)]
+    error = error_buffer()
+    status = base_context.library.hs_b200_view_graph_stats_v1(base_context.handle,
+                                                              *(ctypes.byref(v) for v in values), error, len(error))
+    check_status(status, "hs_b200_view_graph_stats_v1", error)
+    return dict(zip(("captures", "replays", "reruns"), (v.value for v in values)))
 
 
 class FlashgsViewOutputs(NamedTuple):

@@ -383,6 +383,23 @@ typedef struct HsB200FlashgsViewV2 {
 HS_API int32_t hs_b200_flashgs_view_v2(
     const HsB200FlashgsViewV2* view, char* error_text, uint64_t error_capacity) HS_NOEXCEPT;
 
+/* Graph replays of hs_b200_standard_view_v2, counted on its base handle.
+ * An untraced view on a non-default stream, without raster_begin_event,
+ * whose argument block and buffers repeat those of one of the last eight
+ * such calls on the same base handle is captured as one CUDA graph (captures;
+ * at most four are kept, the least recently used dropped); later calls with
+ * that argument block replay it (replays: one graph launch, no host wait
+ * before the renderers, the call returning after both raster calls' binning
+ * as the direct path does). A replay whose pair count exceeds the capacity
+ * it was captured for (a quarter above the previous count), or that breaks a
+ * limit the direct path checks, is rendered again directly (reruns), with
+ * the direct path's outputs and status. The environment variable
+ * HS_B200_VIEW_GRAPHS=0 turns the replays off. No counterpart in the
+ * reference library. */
+HS_API int32_t hs_b200_view_graph_stats_v1(
+    HsRasterizerHandle base_handle, uint64_t* captures, uint64_t* replays, uint64_t* reruns, char* error_text,
+    uint64_t error_capacity) HS_NOEXCEPT;
+
 /* Self-check of the packed FP32x2 arithmetic the rasterisers use (each lane
  * evaluates two pixels with sm_100 pair instructions whose components must
  * round exactly as the scalar instructions): for the count / 2 input pairs
