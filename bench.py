@@ -1123,7 +1123,7 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
             copied[s % VIEW_OUTPUT_SETS].record(copy_stream)
             copy_queued[s % VIEW_OUTPUT_SETS] = True
 
-    def run(first, count):
+    def run(first, count, marks=None):
         pending = None
         upload(first)
         for s in range(first, first + count):
@@ -1139,7 +1139,12 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
                 frame.raster_event = raster_events[s % 2]
             if copy_queued[s % VIEW_OUTPUT_SETS]:
                 stream.wait_event(copied[s % VIEW_OUTPUT_SETS])
+            if marks is not None:
+                marks.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+                marks[-1][0].record(stream)
             out = frame.render()
+            if marks is not None:
+                marks[-1][1].record(stream)
             done = torch.cuda.Event()
             done.record(stream)
             rendered[s % VIEW_OUTPUT_SETS] = done
@@ -1164,6 +1169,14 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
         e1.record(stream)
         torch.cuda.synchronize()
         loops.append(e0.elapsed_time(e1) / args.steps)
+    # one more loop, outside the statistic, with an event pair around every
+    # frame: how long the frames take on the device under the read-back, and
+    # the device time between them
+    marks = []
+    run(args.warmup, args.steps, marks)
+    torch.cuda.synchronize()
+    frame_ms = [a.elapsed_time(b) for a, b in marks]
+    gap_ms = [marks[i][1].elapsed_time(marks[i + 1][0]) for i in range(len(marks) - 1)]
     frame.raster_event = None
     job.barrier()
     e2e_ms = job.max(float(statistics.median(loops)))[0]
@@ -1192,7 +1205,9 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
                         "maps of frame s-1 copied on a copy stream queued after frame s's raster calls return"),
             "statistic": "median of 5 loops of exactly --steps steps, max over ranks",
             "d2h_ms_alone": d2h_worst, "d2h_gbs_alone_per_gpu": d2h / (d2h_worst * 1e6),
-            "host_link_ceiling_fps": ceiling, "fraction_of_host_link_ceiling": value / ceiling}
+            "host_link_ceiling_fps": ceiling, "fraction_of_host_link_ceiling": value / ceiling,
+            "frame_ms_under_readback": float(statistics.median(frame_ms)),
+            "gap_ms_between_frames": float(statistics.median(gap_ms)) if gap_ms else 0.0}
 
 
 def cpu_stages_block() -> dict:
