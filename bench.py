@@ -562,9 +562,11 @@ class Frame:
             acc, depth, normal, spec = base.alpha[0], base.depth[0], base.normal, base.other[0]
         return [fused["rgb_map"], acc, depth, normal, spec, fused["dif_rgb_map"], fused["ref_rgb_map"]]
 
-    def launches_per_step(self, width: int, height: int) -> int:
+    def launches_per_step(self, width: int, height: int, replayed: bool = False) -> int:
         """Kernels of this library launched by one render() call (memsets and
-        copies excluded): per raster call preprocess, totals publication, the
+        copies excluded; `replayed`: the standard view replayed as a captured
+        graph, whose two totals publications are one status kernel): per raster
+        call preprocess, totals publication, the
         depth sort, pair offsets, emission, the tile sort, ranges, tile order
         (which also publishes the wait status) and the rasteriser; plus the
         elementwise kernels of the view. A sort of n items in p 8-bit passes
@@ -608,6 +610,8 @@ class Frame:
                 extra -= 1
             if self.with_post:
                 extra -= 1  # the maps kernel also does the fusion
+        if replayed:
+            per_raster -= 1
         return per_raster + extra + 3  # + reflection prefix, suffix, fusion
 
 
@@ -1016,7 +1020,10 @@ def run_headline(job, args, workload: Workload) -> int:
                            "postprocess": "in the frame (session raw-map postprocess of the base raster); the "
                                           "reference rebuild's frame has none (its postprocess is Jittor code)"},
                 "stages_ms": stages, "clocks": clocks.summary(), "e2e": e2e,
-                "gpu_launches": frame.launches_per_step(spec.width, spec.height) * args.steps * t["repeats"]}
+                "gpu_launches": frame.launches_per_step(
+                    spec.width, spec.height,
+                    replayed=frame.one_call() and args.backend == "standard" and not args.no_view_graphs)
+                * args.steps * t["repeats"]}
         if frame.one_call() and args.backend == "standard":
             line["view_graphs"] = dict(frame.ops.view_graph_stats(frame.ctx), enabled=not args.no_view_graphs,
                                        what="standard views replayed as captured graphs "
@@ -1150,8 +1157,10 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
             if marks is not None:
                 marks.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
                 marks[-1][0].record(stream)
+                host_t0 = time.perf_counter()
             out = frame.render()
             if marks is not None:
+                host_ms.append((time.perf_counter() - host_t0) * 1000.0)
                 marks[-1][1].record(stream)
             done = torch.cuda.Event()
             done.record(stream)
@@ -1181,6 +1190,7 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
     # frame: how long the frames take on the device under the read-back, and
     # the device time between them
     marks = []
+    host_ms = []
     run(args.warmup, args.steps, marks)
     torch.cuda.synchronize()
     frame_ms = [a.elapsed_time(b) for a, b in marks]
@@ -1215,7 +1225,8 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
             "d2h_ms_alone": d2h_worst, "d2h_gbs_alone_per_gpu": d2h / (d2h_worst * 1e6),
             "host_link_ceiling_fps": ceiling, "fraction_of_host_link_ceiling": value / ceiling,
             "frame_ms_under_readback": float(statistics.median(frame_ms)),
-            "gap_ms_between_frames": float(statistics.median(gap_ms)) if gap_ms else 0.0}
+            "gap_ms_between_frames": float(statistics.median(gap_ms)) if gap_ms else 0.0,
+            "host_ms_per_view_call": float(statistics.median(host_ms)) if host_ms else 0.0}
 
 
 def cpu_stages_block() -> dict:

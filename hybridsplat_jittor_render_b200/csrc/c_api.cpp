@@ -2240,6 +2240,7 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
         if (!replayable) return direct();
         std::vector<unsigned char> key = view_graph_key(v, sizeof(HsB200StandardViewV2), contexts, 2);
         HsRasterizerContext::ViewGraph* g = find_view_graph(base, key);
+        bool captured_now = false;  // the capture itself counted the camera terms' library calls
         if (g == nullptr) {
             // seen once: remember the key (the last few, so that views cycling
             // through a few output buffers replay too) and render directly
@@ -2271,6 +2272,7 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
                 {base->post_stream, base->signal_stream, base->side_stream, refl->side_stream},
                 base->graph_join_event);
             ++base->view_graph_captures;
+            captured_now = true;
             // the key of the buffers as captured (the reservation may have grown them)
             g = insert_view_graph(base, view_graph_key(v, sizeof(HsB200StandardViewV2), contexts, 2), exec,
                                   capacity);
@@ -2284,7 +2286,7 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
         if (e == cudaSuccess && post) e = cudaEventRecord(base->view_camera_event, s);
         if (e != cudaSuccess) return cuda_failure(e, "standard view graph launch", error_text, error_capacity);
         ++base->view_graph_replays;
-        if (post) {
+        if (post && !captured_now) {
             base->math_matmul_calls += 2;
             base->math_general_inverse_calls += 2;
         }
