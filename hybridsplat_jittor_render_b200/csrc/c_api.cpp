@@ -2226,13 +2226,13 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
             return qs != HS_STATUS_OK ? qs : ok(error_text, error_capacity);
         };
         // Graph replays: a view whose arguments and buffers repeat those of
-        // the previous call is captured once and then replayed as one graph
+        // a recent call is captured once and then replayed as one graph
         // launch (no launch of its own per kernel, no host wait before the
-        // renderers). Each raster call is captured for a pair capacity a
-        // quarter above its last pair count; a replay whose count exceeds it
-        // (or that breaks a limit the direct path checks) is rendered again
-        // directly, which grows the buffers and reports what the direct path
-        // reports.
+        // renderers). Each raster call is captured for a pair capacity an
+        // eighth (plus 16384) above the largest of its context's last 16
+        // pair counts; a replay whose count exceeds it (or that breaks a
+        // limit the direct path checks) is rendered again directly, which
+        // grows the buffers and reports what the direct path reports.
         const bool replayable = !traced && v->raster_begin_event == nullptr && nb != 0 && nr != 0 &&
                                 view_graphs_enabled() && !base->timer.enabled && !refl->timer.enabled &&
                                 base->test_stall_tile == UINT32_MAX && refl->test_stall_tile == UINT32_MAX &&
@@ -2253,20 +2253,21 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
             }
             recent.erase(seen);
             cudaError_t e = hs::ensure_graph_streams(base);
-            for (HsRasterizerContext* c : contexts) {
+            uint32_t capacity[2];
+            for (int i = 0; i < 2; ++i) {
+                HsRasterizerContext* c = contexts[i];
                 if (e == cudaSuccess) e = hs::ensure_side_stream(c);
-                const uint64_t want = std::min<uint64_t>(c->std_last_emitted + c->std_last_emitted / 4 + 65536,
-                                                         hs::kMaxStandardPairs);
-                if (e == cudaSuccess && hs::standard_pair_capacity(c) < want) e = hs::standard_reserve_pairs(c, want);
+                const uint64_t recent = hs::recent_standard_pairs(c);
+                capacity[i] = static_cast<uint32_t>(
+                    std::min<uint64_t>(recent + recent / 8 + 16384, hs::kMaxStandardPairs));
+                if (e == cudaSuccess && hs::standard_pair_capacity(c) < capacity[i])
+                    e = hs::standard_reserve_pairs(c, capacity[i]);
             }
             if (e == cudaSuccess && post) e = hs::ensure_post_stream(base);
             if (e != cudaSuccess) return cuda_failure(e, "standard view graph setup", error_text, error_capacity);
+            // the grids are sized for the capacity, not for the (larger) buffers
             hs::StandardCall graph_calls[2] = {calls[0], calls[1]};
-            uint32_t capacity[2];
-            for (int i = 0; i < 2; ++i) {
-                capacity[i] = std::min<uint32_t>(hs::standard_pair_capacity(contexts[i]), hs::kMaxStandardPairs);
-                graph_calls[i].pair_capacity = capacity[i];
-            }
+            for (int i = 0; i < 2; ++i) graph_calls[i].pair_capacity = capacity[i];
             const cudaGraphExec_t exec = capture_view(
                 s, [&]() { return queue_view(graph_calls, true) == HS_STATUS_OK; },
                 {base->post_stream, base->signal_stream, base->side_stream, refl->side_stream},
@@ -2299,7 +2300,7 @@ int32_t hs_b200_standard_view_v2(const HsB200StandardViewV2* v, char* error_text
             const uint32_t* t = contexts[i]->std_total_host;
             gave_up = gave_up || t[3] != 0;
             again = again || t[1] != 0 || t[0] > static_cast<uint32_t>(INT_MAX) || t[2] > g->capacity[i];
-            contexts[i]->std_last_emitted = t[2];
+            hs::note_standard_pairs(contexts[i], t[2]);
         }
         if (gave_up) {
             return cuda_failure(hs::kWaitGaveUp, "concurrent five-channel rasterizer forward", error_text,

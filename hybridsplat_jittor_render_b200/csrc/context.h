@@ -200,6 +200,8 @@ struct HsRasterizerContext {
     uint64_t view_graph_replays = 0;
     uint64_t view_graph_reruns = 0;        // replays whose pair count overflowed, rendered again directly
     uint64_t std_last_emitted = 0;         // pairs of the last standard call that read its totals
+    uint32_t std_recent_emitted[16] = {};  // pair counts of the last 16 such calls (ring)
+    uint32_t std_recent_next = 0;
     cudaStream_t signal_stream = nullptr;  // a replay's host publication branch
     cudaEvent_t signal_event = nullptr;    // recorded (external) after that publication
     cudaEvent_t graph_fork_event = nullptr;
@@ -331,6 +333,19 @@ cudaError_t standard_view_status(HsRasterizerContext* const* contexts, const uin
 
 // The most pairs one standard call sorts (the radix sort's 30-bit counts).
 constexpr uint32_t kMaxStandardPairs = (1u << 30) - 1u;
+
+// Records a standard call's pair count (last and recent counts).
+inline void note_standard_pairs(HsRasterizerContext* ctx, uint32_t pairs) {
+    ctx->std_last_emitted = pairs;
+    ctx->std_recent_emitted[ctx->std_recent_next++ % 16] = pairs;
+}
+
+// The largest pair count of the context's last 16 standard calls.
+inline uint32_t recent_standard_pairs(const HsRasterizerContext* ctx) {
+    uint32_t most = 0;
+    for (uint32_t v : ctx->std_recent_emitted) most = v > most ? v : most;
+    return most;
+}
 
 // Pairs the context's standard pair buffers hold (0 before the first call).
 uint32_t standard_pair_capacity(const HsRasterizerContext* context);

@@ -282,7 +282,7 @@ cudaError_t StandardPass::bin() {
         if (rendered > static_cast<uint32_t>(INT_MAX) || emitted > sort::kMaxItems) {
             return cudaErrorInvalidValue;
         }
-        ctx_->std_last_emitted = emitted;
+        note_standard_pairs(ctx_, emitted);
     } else if (ctx_->std_binning.bytes < binning_bytes(emitted)) {
         return cudaErrorInvalidValue;  // standard_reserve_pairs first
     }

@@ -391,7 +391,7 @@ HS_API int32_t hs_b200_flashgs_view_v2(
  * that argument block replay it (replays: one graph launch, no host wait
  * before the renderers, the call returning after both raster calls' binning
  * as the direct path does). A replay whose pair count exceeds the capacity
- * it was captured for (a quarter above the previous count), or that breaks a
+ * it was captured for (an eighth plus 16384 above the largest of the last 16 counts), or that breaks a
  * limit the direct path checks, is rendered again directly (reruns), with
  * the direct path's outputs and status. The environment variable
  * HS_B200_VIEW_GRAPHS=0 turns the replays off. No counterpart in the

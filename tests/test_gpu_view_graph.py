@@ -2,8 +2,8 @@
 
 A view whose argument block and buffers repeat those of one of the last calls
 on the same base context is captured once as a CUDA graph and then replayed
-as one launch: the raster calls are sized for a pair capacity a quarter above
-their last pair count, read the count from device memory, and the host reads
+as one launch: the raster calls are sized for a pair capacity above their
+recent pair counts, read the count from device memory, and the host reads
 their status after the replay. Every replayed output must equal the direct
 call's bit for bit (the per-Gaussian weights, float atomic sums, to rounding):
 for the same view, for a new camera written into the same buffers, and after
