@@ -1221,6 +1221,9 @@ def end_to_end(job: Job, frame: Frame, cams, cam_rows, args) -> dict:
                         "maps of frame s-1 copied on a copy stream once frame s's binning is done and its "
                         "renderers may start" if at_raster else
                         "maps of frame s-1 copied on a copy stream queued after frame s's raster calls return"),
+            "pipeline": (f"frames on their own stream, each writing output set s % {VIEW_OUTPUT_SETS} after that "
+                         "set's previous read-back; each camera row uploaded from pinned memory on an upload stream "
+                         "one frame ahead; standard views replayed as captured graphs unless --no-view-graphs"),
             "statistic": "median of 5 loops of exactly --steps steps, max over ranks",
             "d2h_ms_alone": d2h_worst, "d2h_gbs_alone_per_gpu": d2h / (d2h_worst * 1e6),
             "host_link_ceiling_fps": ceiling, "fraction_of_host_link_ceiling": value / ceiling,
