@@ -199,6 +199,18 @@ def test_view_null(lib):
     assert _view(lib, None) == (1, "standard view is null or its struct_size is too small")
 
 
+def test_view_graph_stats_checks_its_pointers(lib):
+    """hs_b200_view_graph_stats_v1 checks every pointer before reading the
+    handle (a null or foreign handle is never dereferenced here)."""
+    err = ctypes.create_string_buffer(256)
+    counters = [ctypes.c_uint64(7) for _ in range(3)]
+    refs = [ctypes.byref(c) for c in counters]
+    for args in ((None, *refs), (16, None, refs[1], refs[2]), (16, refs[0], None, refs[2]), (16, refs[0], refs[1], None)):
+        status = lib.hs_b200_view_graph_stats_v1(*args, err, len(err))
+        assert (status, err.value.decode()) == (1, "view graph stats received a null pointer")
+    assert [c.value for c in counters] == [7, 7, 7]
+
+
 def _flashgs_view_struct(keep, **over):
     base, hold_b = _flashgs_struct(use_sh=1)
     refl, hold_r = _flashgs_struct(handle=32, use_sh=0)
