@@ -132,6 +132,9 @@ def parse_args():
                    help="with --profile-frames: render with the reference CUDA rebuild (oracle/_ref)")
     p.add_argument("--trace", action="store_true",
                    help="with --profile-frames: trace the reflection colours of every frame")
+    p.add_argument("--profile-replays", action="store_true",
+                   help="with --profile-frames: render the frames on a stream of their own with the output sets in "
+                        "turn, as the headline loop does (standard views replayed from their third use of a set on)")
     p.add_argument("--no-view-entry", action="store_true",
                    help="standard views as the session's separate calls instead of hs_b200_standard_view_v2")
     p.add_argument("--no-view-graphs", action="store_true",
@@ -961,10 +964,15 @@ def run_headline(job, args, workload: Workload) -> int:
     if args.profile_frames > 0:
         if args.trace:
             frame.enable_trace()
-        for s in range(args.profile_frames):
-            frame.set_camera(cams[s % len(cams)])
-            frame.render()
         torch.cuda.synchronize()
+        with torch.cuda.stream(torch.cuda.Stream(device=device) if args.profile_replays
+                               else torch.cuda.current_stream(device)):
+            for s in range(args.profile_frames):
+                frame.set_camera(cams[s % len(cams)])
+                frame.render()
+        torch.cuda.synchronize()
+        if args.profile_replays and frame.one_call() and args.backend == "standard":
+            print(json.dumps({"view_graphs": frame.ops.view_graph_stats(frame.ctx)}), flush=True)
         job.close()
         return 0
 
